@@ -1,0 +1,146 @@
+/*
+ * moearc.h — the C ABI of libmoearc_b200.so, a B200 (sm_100a) implementation of MoEArc's
+ * mixture-of-experts decode hot path.
+ *
+ * The first half is the reference's own operator ABI, symbol for symbol: every function
+ * declared in crates/moearc-kernels/src/ffi.rs:19-263 (defined in kernels.cpp:734-1922) with
+ * the same name, the same argument meaning and the same return codes, so the reference's Rust
+ * crate links against this library unchanged. Each declaration cites the ffi.rs lines it
+ * replaces. The second half (moearc_x_*) holds extensions the reference does not have.
+ *
+ * Return codes (ffi.rs:8-10): 0 success; -1 a device failure or a null argument; -2 an
+ * argument out of range (unsupported type, a shape that is not whole blocks, k or n_mat above
+ * 32, an empty key span, n_heads not a multiple of n_kv_heads, head_dim above 1024).
+ *
+ * Ordering (kernels.cpp:804-828): every context owns one in-order CUDA stream. Kernels return
+ * 0 for "accepted", not "completed"; a device fault surfaces at moearc_sync or at the next
+ * device-to-host copy. `unsigned long` is 64 bits (LP64), as in the reference's c_ulong.
+ *
+ * Type ids are GGUF's (reference.rs:21-40): F32 0, F16 1, Q4_0 2, Q8_0 8, BF16 30, MXFP4 39.
+ * This library expands F32, F16, BF16, Q4_0, Q8_0 and MXFP4 (the K-quants 12/13/14 answer
+ * -2). KV caches may be F32, F16 or BF16.
+ */
+#ifndef MOEARC_H
+#define MOEARC_H
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct moearc_ctx moearc_ctx; /* ffi.rs:14-17 MoearcCtx, opaque */
+
+/* ---- lifecycle, profiling, memory (ffi.rs:20-66) --------------------------------------- */
+moearc_ctx *moearc_ctx_create(void);                                        /* ffi.rs:20 */
+void moearc_ctx_destroy(moearc_ctx *c);                                     /* ffi.rs:21 */
+int moearc_profile_events_enabled(moearc_ctx *c);                           /* ffi.rs:22 */
+int moearc_profile_events_reset(moearc_ctx *c);                             /* ffi.rs:23 */
+int moearc_profile_events_report(moearc_ctx *c, char *out, unsigned long cap); /* ffi.rs:24-28 */
+int moearc_sync(moearc_ctx *c);                                             /* ffi.rs:29 */
+int moearc_zero(moearc_ctx *c, float *dst, unsigned long n);                /* ffi.rs:30 */
+int moearc_device_name(moearc_ctx *c, char *out, unsigned long cap);        /* ffi.rs:31 */
+void *moearc_alloc_device(moearc_ctx *c, unsigned long bytes);              /* ffi.rs:32 */
+void moearc_free_device(moearc_ctx *c, void *p);                            /* ffi.rs:33 */
+int moearc_copy_h2d(moearc_ctx *c, void *dst, const void *src, unsigned long bytes);       /* :34-39 */
+int moearc_copy_h2d_async(moearc_ctx *c, void *dst, const void *src, unsigned long bytes); /* :40-45 */
+int moearc_copy_d2h(moearc_ctx *c, void *dst, const void *src, unsigned long bytes);       /* :46-51 */
+/* ffi.rs:52-59: dst[i] = pool[idx[i]] for count slots of slot_bytes; idx is a HOST array. */
+int moearc_gather_experts(moearc_ctx *c, void *dst, const void *pool, const unsigned int *idx,
+                          unsigned int count, unsigned long slot_bytes);
+
+/* ---- dequantisation and matvecs (ffi.rs:61-117) ---------------------------------------- */
+/* ffi.rs:61-67: nblocks blocks of type_id -> nblocks*block_elems floats. */
+int moearc_dequant(moearc_ctx *c, unsigned int type_id, float *dst, const void *src,
+                   unsigned long nblocks);
+/* ffi.rs:68-76: out[r] = sum_c W[r,c] x[c], W rows in GGUF block layout. */
+int moearc_matvec_q(moearc_ctx *c, unsigned int type_id, float *out, const void *w,
+                    const float *x, unsigned long n_rows, unsigned long n_cols);
+/* ffi.rs:77-88: n_mat <= 32 matrices of one shape; matrix m writes out[m*n_rows ...] and
+ * reads x + m*x_stride (x_stride 0 shares one x). w is a HOST array of device pointers,
+ * copied into the launch by value. */
+int moearc_matvec_q_batched(moearc_ctx *c, unsigned int type_id, float *out,
+                            const void *const *w, unsigned int n_mat, const float *x,
+                            unsigned long x_stride, unsigned long n_rows, unsigned long n_cols);
+/* ffi.rs:89-96: out[i] = sum over m ascending of weights[m]*parts[m*n+i] (weights on device). */
+int moearc_moe_combine(moearc_ctx *c, float *out, const float *parts, const float *weights,
+                       unsigned int n_mat, unsigned long n);
+/* ffi.rs:97-104: f32 rows. Fixed order: lane l of a warp folds columns 4l+128i..+3 with fma,
+ * then an xor butterfly 16,8,4,2,1 — reproducible bit for bit on the host. */
+int moearc_matvec_f32(moearc_ctx *c, float *out, const float *w, const float *x,
+                      unsigned long n_rows, unsigned long n_cols);
+
+/* ---- normalisation and activations (ffi.rs:105-181) ------------------------------------ */
+int moearc_rmsnorm(moearc_ctx *c, float *out, const float *x, const float *weight,
+                   unsigned long n_rows, unsigned long n_cols, float eps);  /* ffi.rs:105-113 */
+int moearc_silu(moearc_ctx *c, float *out, const float *x, unsigned long n); /* ffi.rs:114-119 */
+int moearc_swiglu(moearc_ctx *c, float *out, const float *gate, const float *up,
+                  unsigned long n);                                          /* ffi.rs:120-126 */
+int moearc_swiglu_halves(moearc_ctx *c, float *out, const float *gu, unsigned long n); /* :127-132 */
+int moearc_swiglu_oai(moearc_ctx *c, float *out, const float *gate, const float *up,
+                      unsigned long n, float alpha, float limit);            /* ffi.rs:133-141 */
+int moearc_swiglu_oai_halves(moearc_ctx *c, float *out, const float *gu, unsigned long n,
+                             float alpha, float limit);                      /* ffi.rs:142-149 */
+/* ffi.rs:150-157: out[m*n_rows+r] += bias[idx[m]*n_rows+r]; idx is a HOST array (<= 32). */
+int moearc_add_bias_id(moearc_ctx *c, float *out, const float *bias, const unsigned int *idx,
+                       unsigned int n_mat, unsigned long n_rows);
+int moearc_softmax(moearc_ctx *c, float *out, const float *x, const float *mask,
+                   unsigned long n_rows, unsigned long n_cols, float scale); /* ffi.rs:158-166 */
+int moearc_add(moearc_ctx *c, float *out, const float *a, const float *b, unsigned long n); /* :167-173 */
+int moearc_mul(moearc_ctx *c, float *out, const float *a, const float *b, unsigned long n); /* :174-180 */
+int moearc_axpy(moearc_ctx *c, float *out, const float *x, float alpha, unsigned long n);   /* :181-187 */
+int moearc_quantize_f16(moearc_ctx *c, void *dst, const float *src, unsigned long n);      /* :188-193 */
+/* ffi.rs:194-202: gather + dequantise n_tokens rows; token_ids on the device. */
+int moearc_embed_rows(moearc_ctx *c, unsigned int type_id, float *out, const void *table,
+                      const unsigned int *token_ids, unsigned long n_tokens,
+                      unsigned long n_embd);
+
+/* ---- paged KV cache and decode attention (ffi.rs:203-238) ------------------------------ */
+/* ffi.rs:203-216: write one token's K and V at (page_id, slot); layout
+ * [page][slot][kv_head][head_dim]; kv_type F32, F16 or BF16 (30, an extension). */
+int moearc_kv_append(moearc_ctx *c, void *k_pages, void *v_pages, const float *k,
+                     const float *v, unsigned int page_id, unsigned int slot,
+                     unsigned long n_kv_heads, unsigned long head_dim, unsigned long page_tokens,
+                     unsigned int kv_type);
+/* ffi.rs:217-238: single-query attention over logical keys [kv_begin, n_kv) through
+ * block_table (device), GQA, optional per-head sinks (device, may be NULL). Split-K over the
+ * span; bf16/f16 caches with group <= 8 and head_dim 64/128 run on tensor cores. */
+int moearc_attn_decode(moearc_ctx *c, float *out, const float *q, const void *k_pages,
+                       const void *v_pages, const unsigned int *block_table, const float *sinks,
+                       unsigned long n_heads, unsigned long n_kv_heads, unsigned long head_dim,
+                       unsigned long kv_begin, unsigned long n_kv, unsigned long page_tokens,
+                       float scale, unsigned int kv_type);
+/* ffi.rs:239-254: RoPE over [n_tokens][n_heads][head_dim] with the YaRN ramp; pos on the
+ * device; neox selects (i, i+n_dims/2) pairs. */
+int moearc_rope(moearc_ctx *c, float *dst, const float *src, const int *pos,
+                unsigned long n_tokens, unsigned long n_heads, unsigned long head_dim,
+                unsigned long n_dims, float freq_base, float freq_scale, float ext_factor,
+                float attn_factor, float corr_lo, float corr_hi, int neox);
+/* ffi.rs:255-264: k rounds of argmax over logits (lower id wins a tie); gating 0 softmax,
+ * 1 softmax renormalised over k (sum clamped to 2^-14), 2 softmax of the k selected. */
+int moearc_topk_router(moearc_ctx *c, unsigned int *idx, float *weights, const float *logits,
+                       unsigned long n_tokens, unsigned long n_expert, unsigned int k,
+                       unsigned int gating);
+
+/* ======================================================================================= */
+/* Extensions (no counterpart in ffi.rs)                                                    */
+/* ======================================================================================= */
+
+/* The context's compute stream (a cudaStream_t), for callers that order their own work. */
+void *moearc_x_stream(moearc_ctx *c);
+/* Device timing on the context's stream: start records an event, stop records a second one,
+ * waits for it and writes the elapsed milliseconds. */
+int moearc_x_timer_start(moearc_ctx *c);
+int moearc_x_timer_stop(moearc_ctx *c, float *ms);
+/* Number of streaming multiprocessors of the context's device. */
+int moearc_x_sm_count(moearc_ctx *c);
+/* f32 -> bf16, round to nearest even. */
+int moearc_x_quantize_bf16(moearc_ctx *c, void *dst, const float *src, unsigned long n);
+/* Fill dst with n deterministic synthetic values (SplitMix64 stream `seed`, counter-based):
+ * kind 0 = normal(0, sigma) as f32, 1 = normal(0, sigma) as bf16, 2 = MXFP4 blocks (n blocks,
+ * e8m0 exponent uniform in [lo, hi]), 3 = Q4_0 blocks (n blocks, |normal(0, sigma)| scales). */
+int moearc_x_synth(moearc_ctx *c, void *dst, unsigned long n, unsigned int kind,
+                   unsigned long long seed, float sigma, int lo, int hi);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

@@ -1,0 +1,94 @@
+"""ctypes binding to libmoearc_b200.so — every symbol include/moearc.h declares.
+
+The library is the product: there is no Python or CPU fallback. If the shared object is
+missing this module raises, so a machine without the CUDA build fails loudly instead of
+quietly running something else.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+
+PKG = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(PKG, "libmoearc_b200.so")
+
+P = C.c_void_p
+UL = C.c_ulong
+U = C.c_uint
+I = C.c_int
+F = C.c_float
+
+# name -> (restype, argtypes). Kept in the order of include/moearc.h.
+SIGNATURES: dict[str, tuple] = {
+    "moearc_ctx_create": (P, []),
+    "moearc_ctx_destroy": (None, [P]),
+    "moearc_profile_events_enabled": (I, [P]),
+    "moearc_profile_events_reset": (I, [P]),
+    "moearc_profile_events_report": (I, [P, C.c_char_p, UL]),
+    "moearc_sync": (I, [P]),
+    "moearc_zero": (I, [P, P, UL]),
+    "moearc_device_name": (I, [P, C.c_char_p, UL]),
+    "moearc_alloc_device": (P, [P, UL]),
+    "moearc_free_device": (None, [P, P]),
+    "moearc_copy_h2d": (I, [P, P, P, UL]),
+    "moearc_copy_h2d_async": (I, [P, P, P, UL]),
+    "moearc_copy_d2h": (I, [P, P, P, UL]),
+    "moearc_gather_experts": (I, [P, P, P, P, U, UL]),
+    "moearc_dequant": (I, [P, U, P, P, UL]),
+    "moearc_matvec_q": (I, [P, U, P, P, P, UL, UL]),
+    "moearc_matvec_q_batched": (I, [P, U, P, P, U, P, UL, UL, UL]),
+    "moearc_moe_combine": (I, [P, P, P, P, U, UL]),
+    "moearc_matvec_f32": (I, [P, P, P, P, UL, UL]),
+    "moearc_rmsnorm": (I, [P, P, P, P, UL, UL, F]),
+    "moearc_silu": (I, [P, P, P, UL]),
+    "moearc_swiglu": (I, [P, P, P, P, UL]),
+    "moearc_swiglu_halves": (I, [P, P, P, UL]),
+    "moearc_swiglu_oai": (I, [P, P, P, P, UL, F, F]),
+    "moearc_swiglu_oai_halves": (I, [P, P, P, UL, F, F]),
+    "moearc_add_bias_id": (I, [P, P, P, P, U, UL]),
+    "moearc_softmax": (I, [P, P, P, P, UL, UL, F]),
+    "moearc_add": (I, [P, P, P, P, UL]),
+    "moearc_mul": (I, [P, P, P, P, UL]),
+    "moearc_axpy": (I, [P, P, P, F, UL]),
+    "moearc_quantize_f16": (I, [P, P, P, UL]),
+    "moearc_embed_rows": (I, [P, U, P, P, P, UL, UL]),
+    "moearc_kv_append": (I, [P, P, P, P, P, U, U, UL, UL, UL, U]),
+    "moearc_attn_decode": (I, [P, P, P, P, P, P, P, UL, UL, UL, UL, UL, UL, F, U]),
+    "moearc_rope": (I, [P, P, P, P, UL, UL, UL, UL, F, F, F, F, F, F, I]),
+    "moearc_topk_router": (I, [P, P, P, P, UL, UL, U, U]),
+    "moearc_x_stream": (P, [P]),
+    "moearc_x_timer_start": (I, [P]),
+    "moearc_x_timer_stop": (I, [P, C.POINTER(F)]),
+    "moearc_x_sm_count": (I, [P]),
+    "moearc_x_quantize_bf16": (I, [P, P, P, UL]),
+    "moearc_x_synth": (I, [P, P, UL, U, C.c_ulonglong, F, I, I]),
+}
+
+_lib: C.CDLL | None = None
+
+
+def load() -> C.CDLL:
+    """Load the shared library once and declare every signature."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not os.path.exists(LIB_PATH):
+        raise RuntimeError(
+            f"{LIB_PATH} is missing: build it with `python -m moearc_b200.build` "
+            "(there is no fallback implementation)")
+    lib = C.CDLL(LIB_PATH)
+    for name, (res, args) in SIGNATURES.items():
+        fn = getattr(lib, name)
+        fn.restype = res
+        fn.argtypes = args
+    _lib = lib
+    return lib
+
+
+def declare(name: str, restype, argtypes) -> None:
+    """Register one more signature (used by modules that add extension entry points)."""
+    SIGNATURES[name] = (restype, argtypes)
+    if _lib is not None:
+        fn = getattr(_lib, name)
+        fn.restype = restype
+        fn.argtypes = argtypes

@@ -1,0 +1,154 @@
+// common.cuh — shared definitions of libmoearc_b200: the context, return codes, the block
+// formats' element rules, and the launch bookkeeping every entry point uses.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <string>
+#include <vector>
+
+#include "../../include/moearc.h"
+
+namespace moearc {
+
+// Return codes (crates/moearc-kernels/src/ffi.rs:8-10, kernels.cpp:470-476).
+constexpr int OK = 0;
+constexpr int ERR = -1;
+constexpr int ERR_ARG = -2;
+
+// GGUF type ids (reference.rs:21-40; crates/moearc-model/src/quant.rs:51-107).
+constexpr unsigned T_F32 = 0, T_F16 = 1, T_Q4_0 = 2, T_Q8_0 = 8, T_BF16 = 30, T_MXFP4 = 39;
+
+// Largest k the router selects and largest matrix count one batched launch takes
+// (kernels.cpp:451, 651): both bound by-value kernel arguments, not allocations.
+constexpr int MAX_TOPK = 32;
+constexpr int MAX_BATCHED_MATS = 32;
+
+inline int block_bytes(unsigned t) {
+    switch (t) {
+    case T_F32: return 4;
+    case T_F16: return 2;
+    case T_BF16: return 2;
+    case T_Q4_0: return 18;
+    case T_Q8_0: return 34;
+    case T_MXFP4: return 17;
+    default: return 0;
+    }
+}
+inline int block_elems(unsigned t) {
+    switch (t) {
+    case T_F32:
+    case T_F16:
+    case T_BF16: return 1;
+    case T_Q4_0:
+    case T_Q8_0:
+    case T_MXFP4: return 32;
+    default: return 0;
+    }
+}
+
+struct kernel_time {
+    std::string key;
+    unsigned long long ns;
+    unsigned long long calls;
+};
+
+struct pending_event {
+    std::string key;
+    cudaEvent_t start, stop;
+};
+
+}  // namespace moearc
+
+// The context: one device, one in-order stream (kernels.cpp:804-828), a second stream for
+// host-to-device expert staging, event profiling (kernels.cpp:736-872) and a scratch arena
+// for kernels that need temporary device memory (split-K partials).
+struct moearc_ctx {
+    int device = 0;
+    int sm_count = 148;
+    cudaStream_t stream = nullptr;
+    cudaStream_t copy_stream = nullptr;
+    bool profiling = false;  // MOEARC_PROFILE_EVENTS=1
+    bool sync_each = false;  // MOEARC_SYNC_EACH=1
+    std::vector<moearc::pending_event> pending;
+    std::vector<moearc::kernel_time> totals;
+    void *scratch = nullptr;
+    size_t scratch_bytes = 0;
+    cudaEvent_t t0 = nullptr, t1 = nullptr;
+};
+
+namespace moearc {
+
+// Bookkeeping around one launch: an event pair when profiling, a wait when MOEARC_SYNC_EACH
+// is set, and the launch error (a bad configuration) turned into ERR.
+struct launch_scope {
+    moearc_ctx *c;
+    const char *what;
+    unsigned long rows;
+    unsigned mats;
+    cudaEvent_t e0 = nullptr;
+    launch_scope(moearc_ctx *c_, const char *what_, unsigned long rows_, unsigned mats_)
+        : c(c_), what(what_), rows(rows_), mats(mats_) {
+        if (c->profiling) {
+            cudaEventCreate(&e0);
+            cudaEventRecord(e0, c->stream);
+        }
+    }
+    int finish();
+};
+
+// A scratch buffer of at least `bytes`, owned by the context. Growing it waits for the
+// stream (the old buffer may still be in use) and is not allowed during stream capture.
+void *ctx_scratch(moearc_ctx *c, size_t bytes);
+
+// ---- device-side element rules ----------------------------------------------------------
+
+// ggml_e8m0_to_fp32_half: 2^(x-128); x < 2 is the subnormal arm (reference.rs:66-70).
+__device__ __forceinline__ float e8m0_half(uint32_t x) {
+    const uint32_t bits = (x < 2u) ? (0x00200000u << x) : ((x - 1u) << 23);
+    return __uint_as_float(bits);
+}
+
+// The doubled E2M1 table (reference.rs:56) as a function: magnitudes {0,1,2,3,4,6,8,12} packed
+// one per nibble, sign in bit 3 of the code. Index 8 is negative zero and decodes to 0.
+__device__ __forceinline__ float kv_mxfp4(uint32_t code) {
+    const int mag = (int)((0xC8643210u >> (4u * (code & 7u))) & 0xFu);
+    return (float)((code & 8u) ? -mag : mag);
+}
+
+__device__ __forceinline__ float f16_bits_to_f32(uint16_t h) {
+    return __half2float(__ushort_as_half(h));
+}
+__device__ __forceinline__ float bf16_bits_to_f32(uint16_t h) {
+    return __uint_as_float(static_cast<uint32_t>(h) << 16);
+}
+// f32 -> bf16 bits, round to nearest even; a NaN stays a (quiet) NaN.
+__device__ __forceinline__ uint16_t f32_to_bf16_bits(float f) {
+    return __bfloat16_as_ushort(__float2bfloat16_rn(f));
+}
+
+// Two E2M1 codes (one byte: low nibble first) -> f16x2 of their true values, exactly.
+__device__ __forceinline__ uint32_t e2m1x2_to_f16x2(uint32_t byte) {
+    uint32_t r;
+    asm("{\n .reg .b8 b0, b1, b2, b3;\n mov.b32 {b0, b1, b2, b3}, %1;\n"
+        " cvt.rn.f16x2.e2m1x2 %0, b0;\n}" : "=r"(r) : "r"(byte));
+    return r;
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+
+inline unsigned cdiv(unsigned long a, unsigned long b) { return (unsigned)((a + b - 1) / b); }
+
+}  // namespace moearc
