@@ -140,6 +140,48 @@ int moearc_x_quantize_bf16(moearc_ctx *c, void *dst, const float *src, unsigned 
 int moearc_x_synth(moearc_ctx *c, void *dst, unsigned long n, unsigned int kind,
                    unsigned long long seed, float sigma, int lo, int hi);
 
+/* ---- fused MoE decode (moe.cu) ----------------------------------------------------------- */
+/* The MoE block of crates/moearc-engine/src/moe.rs:2074-2427 (router -> top-k -> gate/up ->
+ * activation -> down -> weighted combine -> residual) as three kernels with no host readback:
+ * the router's choice stays on the device. Replaces the host-driven sequence moe.rs issues
+ * through moearc_matvec_f32, moearc_topk_router, moearc_matvec_q_batched (x2),
+ * moearc_swiglu*_halves and moearc_moe_combine. Expert banks are first repacked
+ * (moearc_x_moe_pack) into tensor-core fragment order; bytes per block are unchanged. */
+typedef struct moearc_x_moe moearc_x_moe;
+typedef struct {
+    unsigned int n_embd;     /* H, a multiple of 64 */
+    unsigned int n_ff;       /* I, expert intermediate, a multiple of 64 */
+    unsigned int n_expert;   /* E <= 1024 */
+    unsigned int k;          /* experts per token <= 32 */
+    unsigned int gating;     /* 0 softmax, 1 softmax renormalised, 2 softmax after top-k */
+    unsigned int act;        /* 0 SwiGLU, 1 SwiGLU-OAI(alpha, limit) */
+    float alpha, limit;
+    unsigned int wtype;      /* 39 MXFP4 or 2 Q4_0 */
+    unsigned int max_tokens; /* tokens per forward call */
+} moearc_x_moe_desc;
+/* NULL on an unsupported shape or a failed allocation. */
+moearc_x_moe *moearc_x_moe_create(moearc_ctx *c, const moearc_x_moe_desc *d);
+void moearc_x_moe_destroy(moearc_x_moe *m);
+/* Bytes of one expert's packed gate-up (which = 0) or down (which = 1) bank. */
+unsigned long moearc_x_moe_packed_bytes(const moearc_x_moe_desc *d, int which);
+/* Repack n_expert experts from GGUF layout (gate/up: n_expert x [n_ff x n_embd], down:
+ * n_expert x [n_embd x n_ff], each expert contiguous, device memory) into the two packed banks
+ * (16-byte aligned device memory). */
+int moearc_x_moe_pack(moearc_x_moe *m, const void *gate, const void *up, const void *down,
+                      unsigned int n_expert, void *gateup_packed, void *down_packed);
+/* out[t] = residual[t] (if not NULL) + MoE(x[t]) for t < n_tokens; x, router_w (E x H f32),
+ * router_b (E, may be NULL), residual and out are device pointers; x and router_w 16-byte
+ * aligned. The router GEMV folds in the fixed order of moearc_matvec_f32. */
+int moearc_x_moe_forward(moearc_x_moe *m, const float *x, unsigned int n_tokens,
+                         const float *router_w, const float *router_b, const void *gateup_packed,
+                         const void *down_packed, const float *residual, float *out);
+/* Device pointers to the last call's internals: 0 expert ids [T x k] (u32), 1 router weights
+ * [T x k], 2 activations [column x n_ff] (column order: experts ascending, tokens ascending
+ * within an expert), 3 router logits [T x E], 4 the int slot tables. */
+void *moearc_x_moe_buffer(moearc_x_moe *m, int which);
+/* Reads and clears the device status word: 0, or bit 1 = a bounded wait gave up. */
+int moearc_x_moe_status(moearc_x_moe *m);
+
 #ifdef __cplusplus
 }
 #endif

@@ -62,7 +62,20 @@ SIGNATURES: dict[str, tuple] = {
     "moearc_x_sm_count": (I, [P]),
     "moearc_x_quantize_bf16": (I, [P, P, P, UL]),
     "moearc_x_synth": (I, [P, P, UL, U, C.c_ulonglong, F, I, I]),
+    "moearc_x_moe_create": (P, [P, P]),
+    "moearc_x_moe_destroy": (None, [P]),
+    "moearc_x_moe_packed_bytes": (UL, [P, I]),
+    "moearc_x_moe_pack": (I, [P, P, P, P, U, P, P]),
+    "moearc_x_moe_forward": (I, [P, P, U, P, P, P, P, P, P]),
+    "moearc_x_moe_buffer": (P, [P, I]),
+    "moearc_x_moe_status": (I, [P]),
 }
+
+
+class MoeDesc(C.Structure):
+    """moearc_x_moe_desc (include/moearc.h)."""
+    _fields_ = [("n_embd", U), ("n_ff", U), ("n_expert", U), ("k", U), ("gating", U), ("act", U),
+                ("alpha", F), ("limit", F), ("wtype", U), ("max_tokens", U)]
 
 _lib: C.CDLL | None = None
 

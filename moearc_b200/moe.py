@@ -1,0 +1,66 @@
+"""The fused MoE decode path (include/moearc.h, moearc_x_moe_*), host side.
+
+``MoeLayer`` owns the device state of one MoE FFN shape and the packed expert banks of one
+layer; ``forward`` runs route -> gate/up + activation -> down + combine (+ residual) on the
+device with no host round trip, the sequence of crates/moearc-engine/src/moe.rs:2074-2427.
+"""
+from __future__ import annotations
+
+import ctypes as C
+
+import numpy as np
+
+from . import _lib
+from .kernels import BadArgument, Context, DeviceBuffer, Failed
+
+
+class MoeLayer:
+    def __init__(self, ctx: Context, n_embd: int, n_ff: int, n_expert: int, k: int, gating: int,
+                 act: int, wtype: int, max_tokens: int = 1, alpha: float = 1.702, limit: float = 7.0):
+        self.ctx = ctx
+        self.desc = _lib.MoeDesc(n_embd, n_ff, n_expert, k, gating, act, alpha, limit, wtype, max_tokens)
+        self.h = ctx.lib.moearc_x_moe_create(ctx.raw, C.byref(self.desc))
+        if not self.h:
+            raise BadArgument("moearc_x_moe_create refused the shape")
+        self.gu_bytes = ctx.lib.moearc_x_moe_packed_bytes(C.byref(self.desc), 0)
+        self.dn_bytes = ctx.lib.moearc_x_moe_packed_bytes(C.byref(self.desc), 1)
+        self.gateup: DeviceBuffer | None = None
+        self.down: DeviceBuffer | None = None
+
+    def close(self) -> None:
+        if self.h:
+            self.ctx.lib.moearc_x_moe_destroy(self.h)
+            self.h = None
+
+    def pack(self, gate: DeviceBuffer, up: DeviceBuffer, down: DeviceBuffer) -> None:
+        """Repack GGUF-layout banks (device) into this layer's packed banks."""
+        E = self.desc.n_expert
+        self.gateup = self.ctx.alloc(E * self.gu_bytes)
+        self.down = self.ctx.alloc(E * self.dn_bytes)
+        rc = self.ctx.lib.moearc_x_moe_pack(self.h, gate.ptr, up.ptr, down.ptr, E, self.gateup.ptr,
+                                            self.down.ptr)
+        self.ctx._finish(rc, "moe_pack")
+
+    def forward(self, x: DeviceBuffer, n_tokens: int, router_w: DeviceBuffer, out: DeviceBuffer,
+                router_b: DeviceBuffer | None = None, residual: DeviceBuffer | None = None) -> None:
+        H = self.desc.n_embd
+        x.require("moe input", 4 * n_tokens * H)
+        out.require("moe output", 4 * n_tokens * H)
+        router_w.require("router weights", 4 * self.desc.n_expert * H)
+        rc = self.ctx.lib.moearc_x_moe_forward(self.h, x.ptr, n_tokens, router_w.ptr,
+                                               None if router_b is None else router_b.ptr,
+                                               self.gateup.ptr, self.down.ptr,
+                                               None if residual is None else residual.ptr, out.ptr)
+        self.ctx._finish(rc, "moe_forward")
+
+    def status(self) -> int:
+        st = self.ctx.lib.moearc_x_moe_status(self.h)
+        if st < 0:
+            raise Failed("reading the MoE status word")
+        return st
+
+    def buffer(self, which: int, dtype, n: int) -> np.ndarray:
+        p = self.ctx.lib.moearc_x_moe_buffer(self.h, which)
+        out = np.empty(n, dtype)
+        self.ctx._finish(self.ctx.lib.moearc_copy_d2h(self.ctx.raw, out.ctypes.data, p, out.nbytes), "download")
+        return out

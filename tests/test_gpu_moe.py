@@ -1,0 +1,141 @@
+"""The fused MoE decode path on the B200 against the oracle's MoE block.
+
+configs[0] of the benchmark description at full size: hidden 2880, 32 experts, top-4,
+intermediate 2880, MXFP4 experts (nibbles uniform, e8m0 exponent in [-8, -4]), router weights
+f32 N(0, 0.02), 16 tokens of N(0, 1) activations. Routing is checked bit-exact: the device
+router GEMV folds in a fixed, documented order and the oracle reproduces that order
+(or_matvec_f32_gpu_order), so both select from identical logits. Outputs are checked at the
+f32 check-mode bound, max |a - b| / max(|b|, 1) <= 1e-4.
+"""
+import numpy as np
+import pytest
+
+import oracle as O
+from moearc_b200 import Context
+from moearc_b200.moe import MoeLayer
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def ctx():
+    c = Context()
+    yield c
+    c.close()
+
+
+def rel_err(got, want):
+    return float(np.max(np.abs(got.astype(np.float64) - want) / np.maximum(np.abs(want), 1.0)))
+
+
+def make_layer(ctx, H, I, E, k, gating, act, wtype, T, seed):
+    nb_gate = E * I * H // 32
+    nb_down = E * H * I // 32
+    if wtype == O.MXFP4:
+        gate, up, down = (O.synth_mxfp4(seed + i, n) for i, n in enumerate((nb_gate, nb_gate, nb_down)))
+    else:
+        gate, up, down = (O.synth_q4_0(seed + i, n, 0.01) for i, n in enumerate((nb_gate, nb_gate, nb_down)))
+    router = O.synth_normal_f32(seed + 7, E * H, 0.02)
+    layer = MoeLayer(ctx, H, I, E, k, gating, act, wtype, max_tokens=T)
+    layer.pack(ctx.upload_new(gate), ctx.upload_new(up), ctx.upload_new(down))
+    return layer, (gate, up, down, router)
+
+
+def oracle_token(H, I, E, k, gating, act, wtype, host, x):
+    gate, up, down, router = host
+    cfg = O.MoeCfg(H, I, E, k, gating, act, 1.702, 7.0, wtype, 1)
+    out = np.zeros(H, np.float32)
+    idx = np.zeros(k, np.uint32)
+    w = np.zeros(k, np.float32)
+    rc = O.lib().or_moe_ffn_token(cfg, O.ptr(x), O.ptr(router), None, O.ptr(gate), O.ptr(up), O.ptr(down),
+                                  None, None, None, O.ptr(out), O.ptr(idx), O.ptr(w))
+    assert rc == 0
+    return out, idx, w
+
+
+@pytest.mark.parametrize("act", [0, 1])
+def test_config0_moe_layer_matches_the_oracle(ctx, act):
+    H = I = 2880
+    E, k, T, gating = 32, 4, 16, 2
+    layer, host = make_layer(ctx, H, I, E, k, gating, act, O.MXFP4, T, 0x5EED0)
+    x = O.synth_normal_f32(0x5EED9, T * H, 1.0)
+    dx = ctx.upload_new(x)
+    out = ctx.alloc_n(np.float32, T * H)
+    layer.forward(dx, T, ctx.upload_new(host[3]), out)
+    got = ctx.download(out, np.float32, T * H).reshape(T, H)
+    assert layer.status() == 0
+    idx = layer.buffer(0, np.uint32, T * k).reshape(T, k)
+    wts = layer.buffer(1, np.float32, T * k).reshape(T, k)
+    logits = layer.buffer(3, np.float32, T * E).reshape(T, E)
+    worst = 0.0
+    for t in range(T):
+        xt = x[t * H:(t + 1) * H].copy()
+        assert np.array_equal(logits[t], O.matvec_f32(host[3].reshape(E, H), xt, gpu_order=True))
+        if t % 4 == 0:  # the oracle's MoE block on a quarter of the tokens keeps this bounded
+            want, widx, ww = oracle_token(H, I, E, k, gating, act, O.MXFP4, host, xt)
+            assert np.array_equal(idx[t], widx), (t, idx[t], widx)
+            assert np.allclose(wts[t], ww, rtol=1e-6, atol=1e-7)
+            worst = max(worst, rel_err(got[t], want))
+    print(f"config0 act={act}: max rel err {worst:.3e} over 4 tokens (bound 1e-4)")
+    assert worst <= 1e-4
+
+
+def test_batch_invariance_and_the_residual(ctx):
+    """A token's output does not depend on which other tokens share the call, and the
+    residual lands on top of the MoE output."""
+    H = I = 2880
+    E, k, gating = 32, 4, 2
+    layer, host = make_layer(ctx, H, I, E, k, gating, 1, O.MXFP4, 16, 0xBA7C4)
+    rw = ctx.upload_new(host[3])
+    x = O.synth_normal_f32(0xBA7C5, 16 * H, 1.0)
+    res = O.synth_normal_f32(0xBA7C6, 16 * H, 1.0)
+    out16 = ctx.alloc_n(np.float32, 16 * H)
+    layer.forward(ctx.upload_new(x), 16, rw, out16)
+    all16 = ctx.download(out16, np.float32, 16 * H)
+    for t in (0, 5, 15):
+        o1 = ctx.alloc_n(np.float32, H)
+        layer.forward(ctx.upload_new(x[t * H:(t + 1) * H].copy()), 1, rw, o1)
+        assert np.array_equal(ctx.download(o1, np.float32, H), all16[t * H:(t + 1) * H])
+    outr = ctx.alloc_n(np.float32, 16 * H)
+    layer.forward(ctx.upload_new(x), 16, rw, outr, residual=ctx.upload_new(res))
+    assert np.array_equal(ctx.download(outr, np.float32, 16 * H), (res + all16).astype(np.float32))
+
+
+def test_activation_buffer_matches_the_oracle(ctx):
+    """The intermediate SwiGLU-OAI activations of one token, column by column."""
+    H = I = 2880
+    E, k = 32, 4
+    layer, (gate, up, down, router) = make_layer(ctx, H, I, E, k, 2, 1, O.MXFP4, 1, 0xAC7)
+    x = O.synth_normal_f32(0xAC8, H, 1.0)
+    out = ctx.alloc_n(np.float32, H)
+    layer.forward(ctx.upload_new(x), 1, ctx.upload_new(router), out)
+    idx = layer.buffer(0, np.uint32, k)
+    act = layer.buffer(2, np.float32, k * I).reshape(k, I)
+    gb = I * H // 32 * 17
+    for col, e in enumerate(sorted(idx.tolist())):  # columns: experts ascending
+        g = O.matvec_q(O.MXFP4, gate[e * gb:(e + 1) * gb], x, I, H)
+        u = O.matvec_q(O.MXFP4, up[e * gb:(e + 1) * gb], x, I, H)
+        want = np.zeros(I, np.float32)
+        O.lib().or_swiglu_oai(O.ptr(g), O.ptr(u), I, 1.702, 7.0, O.ptr(want))
+        err = rel_err(act[col], want)
+        print(f"expert {e}: activation max rel err {err:.3e}")
+        assert err <= 1e-4
+
+
+def test_qwen3_shaped_q4_0_layer(ctx):
+    """Hidden 2048, 128 experts, top-8, intermediate 768, Q4_0 (f16 deltas |N(0, 0.01)|),
+    renormalised softmax gating, SwiGLU, 4 tokens."""
+    H, I, E, k, T = 2048, 768, 128, 8, 4
+    layer, host = make_layer(ctx, H, I, E, k, 1, 0, O.Q4_0, T, 0x0E3)
+    x = O.synth_normal_f32(0x0E4, T * H, 1.0)
+    out = ctx.alloc_n(np.float32, T * H)
+    layer.forward(ctx.upload_new(x), T, ctx.upload_new(host[3]), out)
+    got = ctx.download(out, np.float32, T * H).reshape(T, H)
+    idx = layer.buffer(0, np.uint32, T * k).reshape(T, k)
+    worst = 0.0
+    for t in range(T):
+        want, widx, _ = oracle_token(H, I, E, k, 1, 0, O.Q4_0, host, x[t * H:(t + 1) * H].copy())
+        assert np.array_equal(idx[t], widx)
+        worst = max(worst, rel_err(got[t], want))
+    print(f"qwen3 Q4_0: max rel err {worst:.3e} (bound 1e-4)")
+    assert worst <= 1e-4
