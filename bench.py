@@ -1,0 +1,346 @@
+"""Benchmark: MoE decode tok/s at gpt-oss-120b shape (configs[2], experts resident in HBM).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--depth D] [--config 120b|20b]
+    python bench.py --impl reference ...   # the reference's CPU path, timed on the host cores
+
+A step is one batch-1 decode token through the whole synthetic decoder (36 blocks: RMSNorm,
+Q/K/V, RoPE, paged-KV append, attention with sinks over a full or 128-key window, O
+projection, and the fused MoE FFN with 128 MXFP4 experts, top-4). Weights are random (seeded)
+and generated on the device; inputs are synthetic. The weights (≈63 GB) are far larger than
+the 126 MB L2, so consecutive steps never hit in L2 for them; no flush is needed.
+
+value     tokens/s with the input already on the device, timed with CUDA events over K steps
+e2e       the same through the public API with host buffers: per step the input embedding is
+          copied from pinned host memory and the output read back, wall-clock timed
+roofline  the MoE gate-up grouped GEMV (the path's dominant kernel): algorithmic bytes per
+          launch (4 experts x 2 matrices x 2880 x 2880 MXFP4 = 35.25 MB) over its average
+          device time, against the measured HBM copy bandwidth in MEASURED_PEAKS.json
+Multi-GPU: batch-1 decode does not shard; with N GPUs each rank runs an independent replica
+(weak scaling) and `value` sums their tokens/s, timed as the max over ranks.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+# One process per GPU: pin this rank's device before anything initialises CUDA.
+if "LOCAL_RANK" in os.environ and "CUDA_VISIBLE_DEVICES" not in os.environ:
+    os.environ["CUDA_VISIBLE_DEVICES"] = os.environ["LOCAL_RANK"]
+
+METRIC = "MoE decode tok/s at gpt-oss-120b shape; expert-GEMM HBM GB/s vs 8 TB/s"
+UNIT = "tok/s"
+
+
+def load_peaks() -> tuple[float, str]:
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            return float(json.load(f)["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+# ---- clocks during the timed region --------------------------------------------------------
+
+class ClockSampler:
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self):
+        self.proc = None
+        self.path = tempfile.mktemp(prefix="clocks_", suffix=".csv")
+
+    def start(self):
+        try:
+            self.f = open(self.path, "w")
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
+                                          "-lms", "200"], stdout=self.f, stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+
+    def stop(self) -> dict:
+        if not self.proc:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        self.proc.wait(timeout=10)
+        self.f.close()
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        vis = os.environ.get("CUDA_VISIBLE_DEVICES", "0").split(",")[0]
+        for line in open(self.path):
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9 or (vis.isdigit() and parts[0] != vis):
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx.append(float(parts[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        os.unlink(self.path)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ---- the CPU baseline (the reference's CPU path, restated) ---------------------------------
+
+def cpu_decode_sample(cfg, layers: int = 2, budget_s: float = 12.0, threads: int = 0) -> dict:
+    """Time the restated CPU decode path (host_experts.rs's pinned pool for the experts, the
+    same-style threaded matvec for the dense projections, reference.rs attention) on `layers`
+    blocks of the configuration, and extrapolate to the whole model: tokens/s =
+    1 / (n_layer x seconds per block-token)."""
+    import ctypes as C
+
+    import numpy as np
+
+    import oracle as O
+
+    H, Dq, Dkv = cfg.n_embd, cfg.n_head * cfg.head_dim, cfg.n_head_kv * cfg.head_dim
+    nb = cfg.n_expert * cfg.n_ff * H // 32
+    keep, arr = [], []
+    t0 = time.time()
+    for l in range(layers):
+        t = {
+            "attn_norm": np.ones(H, np.float32), "ffn_norm": np.ones(H, np.float32),
+            "wq": O.synth_normal_bf16(100 + l, Dq * H, 0.02), "wk": O.synth_normal_bf16(200 + l, Dkv * H, 0.02),
+            "wv": O.synth_normal_bf16(300 + l, Dkv * H, 0.02), "wo": O.synth_normal_bf16(400 + l, H * Dq, 0.02),
+            "sinks": np.zeros(cfg.n_head, np.float32),
+            "router": O.synth_normal_f32(500 + l, cfg.n_expert * H, 0.02),
+            "gate": O.synth_mxfp4(600 + l, nb), "up": O.synth_mxfp4(700 + l, nb), "down": O.synth_mxfp4(800 + l, nb),
+        }
+        pool = 4096 * Dkv
+        t["k"] = np.zeros(pool, np.uint16)
+        t["v"] = np.zeros(pool, np.uint16)
+        t["table"] = np.arange(4096 // 32, dtype=np.uint32)
+        keep.append(t)
+        arr.append(O.CdLayer(*[O.ptr(t[n]) for n in ("attn_norm", "ffn_norm", "wq", "wk", "wv", "wo", "sinks",
+                                                     "router", "gate", "up", "down", "k", "v", "table")]))
+    gen_s = time.time() - t0
+    layers_arr = (O.CdLayer * layers)(*arr)
+    c = O.CdCfg(layers, H, cfg.n_head, cfg.n_head_kv, cfg.head_dim, cfg.n_expert, cfg.n_ff, cfg.n_expert_used,
+                cfg.gating, cfg.act, O.MXFP4, O.BF16, cfg.alpha, cfg.limit, cfg.rms_eps, cfg.n_swa,
+                cfg.swa_pattern, 32, cfg.rope_base, cfg.rope_freq_scale, cfg.rope_ext_factor,
+                cfg.rope_attn_factor, cfg.rope_corr_lo, cfg.rope_corr_hi)
+    pool = O.lib().hx_create(threads)
+    n_threads = O.lib().hx_threads(pool)
+    h = O.synth_normal_f32(9, H, 1.0)
+    # warm: touch every weight once
+    O.lib().cd_layers(C.byref(c), layers_arr, 0, layers, O.ptr(h), 0, pool, None)
+    tokens, t0 = 0, time.time()
+    while True:
+        h = O.synth_normal_f32(10 + tokens, H, 1.0)
+        rc = O.lib().cd_layers(C.byref(c), layers_arr, 0, layers, O.ptr(h), tokens + 1, pool, None)
+        assert rc == 0, rc
+        tokens += 1
+        el = time.time() - t0
+        if (el > budget_s and tokens >= 3) or tokens >= 4000:
+            break
+    O.lib().hx_destroy(pool)
+    per_block_token = el / (tokens * layers)
+    tps = 1.0 / (per_block_token * cfg.n_layer)
+    load = os.getloadavg()[0] if hasattr(os, "getloadavg") else None
+    return {"value": tps, "unit": UNIT, "cores": n_threads, "kind": "port",
+            "sample": f"{tokens} tokens x {layers} of {cfg.n_layer} blocks ({el:.1f} s; weights generated in "
+                      f"{gen_s:.1f} s), extrapolated to {cfg.n_layer} blocks; restated host_experts.rs pool, "
+                      f"{n_threads} threads, nproc {os.cpu_count()}, load {load}"}
+
+
+# ---- the GPU run ----------------------------------------------------------------------------
+
+def gpu_run(args, cfg, rank: int, world: int, dist) -> dict:
+    import ctypes as C
+
+    import numpy as np
+
+    from moearc_b200 import Context
+    from moearc_b200.decoder import Decoder
+
+    ctx = Context()
+    cfg.n_ctx = args.depth + args.warmup + 2 * args.steps + 64
+    t0 = time.time()
+    dec = Decoder(ctx, cfg)
+    ctx.sync()
+    build_s = time.time() - t0
+    if args.depth:
+        dec.fill_kv(args.depth)
+    else:
+        dec.set_pos(0)
+    lib = ctx.lib
+    H = cfg.n_embd
+    host_in = lib.moearc_x_host_alloc(4 * H)
+    host_out = lib.moearc_x_host_alloc(4 * H)
+    C.memmove(host_in, np.random.default_rng(rank).standard_normal(H).astype(np.float32).ctypes.data, 4 * H)
+    lib.moearc_copy_h2d(ctx.raw, dec.in_ptr, host_in, 4 * H)
+
+    for _ in range(args.warmup):
+        dec.step()
+    ctx.sync()
+
+    # per-kernel device times (one un-graphed step; events between launches)
+    ms = (C.c_float * 8)()
+    cnt = (C.c_int * 8)()
+    ctx._finish(lib.moearc_x_decoder_profile(dec.h, ms, cnt, 8), "profile")
+    kernel_ms = {k: ms[i] for i, k in enumerate(["qkv", "attention", "o_proj", "moe_route", "moe_gate_up",
+                                                  "moe_down", "final_norm"])}
+    launches_per_step = sum(cnt[i] for i in range(7))
+
+    sampler = ClockSampler() if rank == 0 else None
+    if sampler:
+        sampler.start()
+        time.sleep(0.5)
+    if dist:
+        dist.barrier()
+    ctx.sync()
+    ctx.timer_start()
+    for _ in range(args.steps):
+        dec.step()
+    ms_total = ctx.timer_stop()
+
+    # end to end through the public API: host input in, host output out, every step
+    ctx.sync()
+    t1 = time.perf_counter()
+    for _ in range(args.steps):
+        lib.moearc_copy_h2d_async(ctx.raw, dec.in_ptr, host_in, 4 * H)
+        dec.step()
+        lib.moearc_x_copy_d2h_async(ctx.raw, host_out, dec.out_ptr, 4 * H)
+        ctx.sync()
+    e2e_s = time.perf_counter() - t1
+    clocks = sampler.stop() if sampler else None
+    out = np.ctypeslib.as_array(C.cast(host_out, C.POINTER(C.c_float)), (H,)).copy()
+    assert np.all(np.isfinite(out)), "non-finite decoder output"
+    lib.moearc_x_host_free(host_in)
+    lib.moearc_x_host_free(host_out)
+    dec.close()
+    ctx.close()
+    return {"ms_total": ms_total, "e2e_s": e2e_s, "kernel_ms": kernel_ms, "counts": [cnt[i] for i in range(7)],
+            "launches_per_step": launches_per_step, "clocks": clocks, "build_s": build_s}
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--depth", type=int, default=0)
+    ap.add_argument("--config", default="120b", choices=["120b", "20b"])
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--layers", type=int, default=0,
+                    help="blocks to build (default: the configuration's); a smaller model for profiling")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+
+    from moearc_b200.decoder import DecoderConfig
+
+    cfg = DecoderConfig.gpt_oss_120b() if args.config == "120b" else DecoderConfig.gpt_oss_20b()
+    if args.layers:
+        cfg.n_layer = args.layers
+    workload = (f"configs[{2 if args.config == '120b' else 1}] gpt-oss-{args.config} shape, batch-1 decode, "
+                f"depth {args.depth}, experts resident in HBM")
+    config = {"workload": workload, "n_layer": cfg.n_layer, "n_embd": cfg.n_embd, "n_expert": cfg.n_expert,
+              "top_k": cfg.n_expert_used, "n_ff": cfg.n_ff, "expert_type": "MXFP4", "kv": "bf16, pages of 32",
+              "attention": "64 q / 8 kv heads x 64, sinks, alternating full / 128-key window",
+              "depth": args.depth, "batch": 1,
+              "l2": "weights (~63 GB) far exceed the 126 MB L2; no flush"}
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+
+    if args.impl == "reference":
+        if rank != 0:
+            return
+        cpu = cpu_decode_sample(cfg, budget_s=12.0)
+        line = {"impl": "reference", "metric": METRIC, "value": cpu["value"], "unit": UNIT, "n_gpus": args.gpus,
+                "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000.0 / cpu["value"],
+                "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+                "data": "synthetic", "config": config,
+                "cpu_baseline": {"value": cpu["value"], "unit": UNIT, "cores": cpu["cores"], "kind": "port",
+                                 "sample": cpu["sample"]},
+                "e2e": {"value": cpu["value"], "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+        print(json.dumps(line))
+        return
+
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as tdist
+
+        tdist.init_process_group("gloo", timeout=datetime.timedelta(seconds=300))
+        dist = tdist
+    r = gpu_run(args, cfg, rank, world, dist)
+    ms_total = r["ms_total"]
+    if dist:
+        import torch
+
+        t = torch.tensor([ms_total, r["e2e_s"]], dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms_total, e2e_s = float(t[0]), float(t[1])
+        dist.barrier()
+        dist.destroy_process_group()
+    else:
+        e2e_s = r["e2e_s"]
+    if rank != 0:
+        return
+    ms_step = ms_total / args.steps
+    value = world * args.steps / (ms_total / 1000.0)
+    e2e = world * args.steps / e2e_s
+
+    peak, peak_kind = load_peaks()
+    H, I, k = cfg.n_embd, cfg.n_ff, cfg.n_expert_used
+    gu_bytes = k * 2 * I * H // 32 * 17
+    n_gu = max(1, r["counts"][4])
+    gu_ms = r["kernel_ms"]["moe_gate_up"] / n_gu
+    achieved = gu_bytes / (gu_ms / 1000.0) / 1e9
+    # the whole step's algorithmic bytes: dense bf16 projections, routers, the 4 chosen experts'
+    # three matrices, the KV span each block reads
+    Dq, Dkv = cfg.n_head * cfg.head_dim, cfg.n_head_kv * cfg.head_dim
+    dense_b = (H * (Dq + 2 * Dkv) + H * Dq) * 2
+    expert_b = 3 * k * I * H // 32 * 17
+    router_b = cfg.n_expert * H * 4
+    kv_b = 0
+    for l in range(cfg.n_layer):
+        span = args.depth + 1
+        if cfg.n_swa and (l % cfg.swa_pattern) < cfg.swa_pattern - 1:
+            span = min(span, cfg.n_swa)
+        kv_b += span * Dkv * 2 * 2
+    step_bytes = cfg.n_layer * (dense_b + expert_b + router_b) + kv_b
+    step_gbs = step_bytes / (ms_step / 1000.0) / 1e9
+
+    line = {
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded random weights, N(0,1) inputs)",
+        "config": config,
+        "roofline": {"bound": "hbm", "kernel": "moe gate-up grouped GEMV (MXFP4, tensor cores)",
+                     "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                     "peak_kind": peak_kind, "traffic": None,
+                     "bytes_per_launch": gu_bytes, "avg_launch_ms": gu_ms,
+                     "frac_of_8tbs": achieved / 8000.0},
+        "step_hbm": {"algorithmic_bytes": step_bytes, "achieved_gbs": step_gbs, "frac": step_gbs / peak,
+                     "frac_of_8tbs": step_gbs / 8000.0},
+        "kernel_ms_per_step": r["kernel_ms"],
+        "e2e": {"value": e2e, "unit": UNIT, "h2d_bytes_per_step": 4 * H, "d2h_bytes_per_step": 4 * H},
+        "gpu_launches": r["launches_per_step"] * args.steps,
+        "clocks": r["clocks"],
+        "build_s": r["build_s"],
+    }
+    if world == 1 and not args.no_cpu:
+        line["cpu_baseline"] = cpu_decode_sample(cfg, budget_s=12.0)
+    print(json.dumps(line))
+
+
+if __name__ == "__main__":
+    main()

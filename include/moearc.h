@@ -130,13 +130,19 @@ void *moearc_x_stream(moearc_ctx *c);
  * waits for it and writes the elapsed milliseconds. */
 int moearc_x_timer_start(moearc_ctx *c);
 int moearc_x_timer_stop(moearc_ctx *c, float *ms);
+/* Page-locked host memory (for full-rate, overlappable copies) and its release. */
+void *moearc_x_host_alloc(unsigned long bytes);
+void moearc_x_host_free(void *p);
+/* Device-to-host copy enqueued on the context's stream without waiting. */
+int moearc_x_copy_d2h_async(moearc_ctx *c, void *dst, const void *src, unsigned long bytes);
 /* Number of streaming multiprocessors of the context's device. */
 int moearc_x_sm_count(moearc_ctx *c);
 /* f32 -> bf16, round to nearest even. */
 int moearc_x_quantize_bf16(moearc_ctx *c, void *dst, const float *src, unsigned long n);
 /* Fill dst with n deterministic synthetic values (SplitMix64 stream `seed`, counter-based):
  * kind 0 = normal(0, sigma) as f32, 1 = normal(0, sigma) as bf16, 2 = MXFP4 blocks (n blocks,
- * e8m0 exponent uniform in [lo, hi]), 3 = Q4_0 blocks (n blocks, |normal(0, sigma)| scales). */
+ * e8m0 exponent uniform in [lo, hi]), 3 = Q4_0 blocks (n blocks, |normal(0, sigma)| scales),
+ * 4 = 1 + normal(0, sigma) as f32 (norm weights). */
 int moearc_x_synth(moearc_ctx *c, void *dst, unsigned long n, unsigned int kind,
                    unsigned long long seed, float sigma, int lo, int hi);
 
@@ -181,6 +187,52 @@ int moearc_x_moe_forward(moearc_x_moe *m, const float *x, unsigned int n_tokens,
 void *moearc_x_moe_buffer(moearc_x_moe *m, int which);
 /* Reads and clears the device status word: 0, or bit 1 = a bounded wait gave up. */
 int moearc_x_moe_status(moearc_x_moe *m);
+
+/* ---- synthetic decoder (decoder.cu) ----------------------------------------------------- */
+/* One decode step of a routed-MoE transformer (crates/moearc-engine/src/moe.rs:1862-2443,
+ * Model::decode) with random, seeded weights generated on the device: per block RMSNorm,
+ * Q/K/V (bf16), NeoX RoPE with the YaRN ramp, paged bf16 KV (pages of 32 tokens; blocks with
+ * l % swa_pattern < swa_pattern - 1 use a window of n_swa keys in a cyclic ring), decode
+ * attention with optional sinks, O projection, and the fused MoE FFN; then a final RMSNorm.
+ * There is no token embedding or output head: the step reads an n_embd vector from
+ * moearc_x_decoder_input and writes the normalised final state to moearc_x_decoder_output. */
+typedef struct moearc_x_decoder moearc_x_decoder;
+typedef struct {
+    unsigned int n_layer, n_embd, n_head, n_head_kv, head_dim; /* head_dim 64 or 128 */
+    unsigned int n_expert, n_expert_used, n_ff;
+    unsigned int expert_type;                 /* 39 MXFP4 or 2 Q4_0 */
+    unsigned int gating, act;                 /* as moearc_x_moe_desc */
+    float alpha, limit;
+    unsigned int n_swa, swa_pattern;          /* window (0: none) and pattern */
+    float rope_base, rope_freq_scale, rope_ext_factor, rope_attn_factor, rope_corr_lo, rope_corr_hi;
+    float rms_eps;
+    unsigned int has_sinks;
+    unsigned int n_ctx;                       /* positions the KV cache holds */
+    unsigned long long seed;
+} moearc_x_decoder_cfg;
+moearc_x_decoder *moearc_x_decoder_create(moearc_ctx *c, const moearc_x_decoder_cfg *cfg);
+void moearc_x_decoder_destroy(moearc_x_decoder *d);
+void *moearc_x_decoder_input(moearc_x_decoder *d);   /* device, n_embd f32 */
+void *moearc_x_decoder_output(moearc_x_decoder *d);  /* device, n_embd f32 */
+int moearc_x_decoder_pos(moearc_x_decoder *d);       /* the next position to decode */
+int moearc_x_decoder_set_pos(moearc_x_decoder *d, unsigned int pos);
+/* Fill every KV page with synthetic bf16 N(0, 0.02) and set the position to depth. */
+int moearc_x_decoder_fill_kv(moearc_x_decoder *d, unsigned int depth, unsigned long long seed);
+/* Decode one token at the current position, enqueued on the context's stream; the first call
+ * captures the step as a CUDA graph (unless disabled) and later calls replay it. */
+int moearc_x_decoder_step(moearc_x_decoder *d);
+int moearc_x_decoder_use_graph(moearc_x_decoder *d, int on);
+/* One step without the graph and with an event after every kernel: ms[k] gets the device time
+ * of kernel kind k (0 Q/K/V, 1 attention, 2 O projection, 3 MoE route, 4 MoE gate-up, 5 MoE
+ * down, 6 final norm) summed over the blocks, counts[k] the launches; n >= 7. */
+int moearc_x_decoder_profile(moearc_x_decoder *d, float *ms, int *counts, int n);
+/* Device pointer (and size) of one block's tensor: 0 attn_norm, 1 ffn_norm, 2 sinks,
+ * 3 router, 4 K pool, 5 V pool, 6 page table, 7 packed Q/K/V, 8 packed O, 9 packed gate-up,
+ * 10 packed down, 11 output norm. */
+void *moearc_x_decoder_tensor(moearc_x_decoder *d, int which, unsigned int layer, unsigned long *bytes);
+/* The seed tensor `kind` of block `layer` was generated from, given the model seed. */
+unsigned long long moearc_x_decoder_seed(moearc_x_decoder *d, int kind, unsigned int layer,
+                                         unsigned long long base);
 
 #ifdef __cplusplus
 }

@@ -10,7 +10,8 @@ import ctypes as C
 import os
 
 PKG = os.path.dirname(os.path.abspath(__file__))
-LIB_PATH = os.path.join(PKG, "libmoearc_b200.so")
+# MOEARC_LIB selects another build of the same library (e.g. one compiled with timestamps).
+LIB_PATH = os.environ.get("MOEARC_LIB") or os.path.join(PKG, "libmoearc_b200.so")
 
 P = C.c_void_p
 UL = C.c_ulong
@@ -62,6 +63,9 @@ SIGNATURES: dict[str, tuple] = {
     "moearc_x_sm_count": (I, [P]),
     "moearc_x_quantize_bf16": (I, [P, P, P, UL]),
     "moearc_x_synth": (I, [P, P, UL, U, C.c_ulonglong, F, I, I]),
+    "moearc_x_host_alloc": (P, [UL]),
+    "moearc_x_host_free": (None, [P]),
+    "moearc_x_copy_d2h_async": (I, [P, P, P, UL]),
     "moearc_x_moe_create": (P, [P, P]),
     "moearc_x_moe_destroy": (None, [P]),
     "moearc_x_moe_packed_bytes": (UL, [P, I]),
@@ -69,7 +73,29 @@ SIGNATURES: dict[str, tuple] = {
     "moearc_x_moe_forward": (I, [P, P, U, P, P, P, P, P, P]),
     "moearc_x_moe_buffer": (P, [P, I]),
     "moearc_x_moe_status": (I, [P]),
+    "moearc_x_decoder_create": (P, [P, P]),
+    "moearc_x_decoder_destroy": (None, [P]),
+    "moearc_x_decoder_input": (P, [P]),
+    "moearc_x_decoder_output": (P, [P]),
+    "moearc_x_decoder_pos": (I, [P]),
+    "moearc_x_decoder_set_pos": (I, [P, U]),
+    "moearc_x_decoder_fill_kv": (I, [P, U, C.c_ulonglong]),
+    "moearc_x_decoder_step": (I, [P]),
+    "moearc_x_decoder_use_graph": (I, [P, I]),
+    "moearc_x_decoder_profile": (I, [P, C.POINTER(F), C.POINTER(I), I]),
+    "moearc_x_decoder_tensor": (P, [P, I, U, C.POINTER(UL)]),
+    "moearc_x_decoder_seed": (C.c_ulonglong, [P, I, U, C.c_ulonglong]),
 }
+
+
+class DecoderCfg(C.Structure):
+    """moearc_x_decoder_cfg (include/moearc.h)."""
+    _fields_ = [("n_layer", U), ("n_embd", U), ("n_head", U), ("n_head_kv", U), ("head_dim", U),
+                ("n_expert", U), ("n_expert_used", U), ("n_ff", U), ("expert_type", U), ("gating", U),
+                ("act", U), ("alpha", F), ("limit", F), ("n_swa", U), ("swa_pattern", U),
+                ("rope_base", F), ("rope_freq_scale", F), ("rope_ext_factor", F), ("rope_attn_factor", F),
+                ("rope_corr_lo", F), ("rope_corr_hi", F), ("rms_eps", F), ("has_sinks", U), ("n_ctx", U),
+                ("seed", C.c_ulonglong)]
 
 
 class MoeDesc(C.Structure):

@@ -48,6 +48,58 @@ __device__ __forceinline__ float kv_get(const void *base, size_t i, unsigned t) 
 
 constexpr float LOG2E = 1.4426950408889634f;
 
+// The key span of a decode step whose position lives in device memory: n_kv = pos + 1, a
+// window of `window` keys (0 = full causal), split over at most max_splits CTAs in runs of a
+// multiple of 64 keys. Returns false for a CTA past the last split.
+__device__ __forceinline__ bool device_span(const int *dpos, int window, int max_splits, size_t &kv_begin,
+                                            size_t &n_kv, size_t &kps, int &n_splits) {
+    n_kv = (size_t)(*dpos) + 1;
+    kv_begin = (window > 0 && n_kv > (size_t)window) ? n_kv - (size_t)window : 0;
+    const size_t span = n_kv - kv_begin;
+    kps = (span + max_splits - 1) / max_splits;
+    kps = ((kps + 63) / 64) * 64;
+    n_splits = (int)((span + kps - 1) / kps);
+    return (int)blockIdx.y < n_splits;
+}
+
+// Merge the n_splits partial (max, sum, acc) triples of heads [h0, h0 + nh) into out, with
+// the sink as one extra logit (kernels.cpp:1856-1880). Run by one whole CTA.
+__device__ void merge_heads(float *out, const float *part_ml, const float *part_acc, const float *sinks,
+                            int h0, int nh, int hd, int n_splits) {
+    for (int e = threadIdx.x; e < nh * hd; e += blockDim.x) {
+        const int h = h0 + e / hd, d = e % hd;
+        const float *ml = part_ml + (size_t)h * n_splits * 2;
+        float M = sinks ? sinks[h] : -INFINITY;
+        for (int s = 0; s < n_splits; ++s) M = fmaxf(M, __ldcg(ml + 2 * s));
+        float L = sinks ? exp2f((sinks[h] - M) * LOG2E) : 0.f;
+        float v = 0.f;
+        for (int s = 0; s < n_splits; ++s) {
+            const float ms = __ldcg(ml + 2 * s);
+            if (ms == -INFINITY) continue;
+            const float f = exp2f((ms - M) * LOG2E);
+            L += __ldcg(ml + 2 * s + 1) * f;
+            v += __ldcg(part_acc + ((size_t)h * n_splits + s) * hd + d) * f;
+        }
+        out[(size_t)h * hd + d] = v / L;
+    }
+}
+
+// After a CTA wrote its partials: count it in; the last CTA of `unit` merges the unit's heads
+// and resets the counter for the next call.
+__device__ __forceinline__ void arrive_and_merge(unsigned *ctr, int unit, int n_splits, float *out,
+                                                 const float *part_ml, const float *part_acc,
+                                                 const float *sinks, int h0, int nh, int hd) {
+    __shared__ unsigned last;
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0) last = (atomicAdd(ctr + unit, 1u) == (unsigned)n_splits - 1);
+    __syncthreads();
+    if (!last) return;
+    __threadfence();
+    merge_heads(out, part_ml, part_acc, sinks, h0, nh, hd, n_splits);
+    if (threadIdx.x == 0) ctr[unit] = 0;
+}
+
 // ---- the generic split-K kernel (any cache type, group, head_dim <= 1024) ----------------
 //
 // CTA (query head, split), 4 warps; warp w walks keys s0+w, s0+w+4, ...; lanes hold NPL
@@ -57,9 +109,12 @@ __global__ void __launch_bounds__(128)
     k_attn_generic(float *part_ml, float *part_acc, float *out, const float *q, const void *kp,
                    const void *vp, const unsigned *table, const float *sinks, int n_heads,
                    int n_kv_heads, int hd, size_t kv_begin, size_t n_kv, size_t pt, float scale,
-                   unsigned kv_type, size_t kps, int n_splits) {
+                   unsigned kv_type, size_t kps, int n_splits, const int *dpos, int window, unsigned *ctr) {
     extern __shared__ float sm[];  // [4][2] m,l then [4][hd] acc
     const int h = blockIdx.x, split = blockIdx.y;
+    pdl_trigger();
+    pdl_wait();
+    if (dpos && !device_span(dpos, window, gridDim.y, kv_begin, n_kv, kps, n_splits)) return;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int group = n_heads / n_kv_heads, kvh = h / group;
     const size_t s0 = kv_begin + (size_t)split * kps;
@@ -134,13 +189,19 @@ __global__ void __launch_bounds__(128)
             for (int w = 0; w < 4; ++w) v += wacc[w * hd + d] * fw[w];
             part_acc[((size_t)h * n_splits + split) * hd + d] = v;
         }
+        if (ctr) arrive_and_merge(ctr, h, n_splits, out, part_ml, part_acc, sinks, h, 1, hd);
     }
 }
 
 // Merge the splits of every query head, with the sink as one extra logit.
 __global__ void k_attn_combine(float *out, const float *part_ml, const float *part_acc,
-                               const float *sinks, int hd, int n_splits) {
+                               const float *sinks, int hd, int n_splits, const int *dpos, int window,
+                               int max_splits) {
     const int h = blockIdx.x;
+    if (dpos) {
+        size_t b = 0, n = 0, kps = 0;
+        if (!device_span(dpos, window, max_splits, b, n, kps, n_splits) || n_splits == 1) return;
+    }
     const float *ml = part_ml + (size_t)h * n_splits * 2;
     float M = sinks ? sinks[h] : -INFINITY;
     for (int s = 0; s < n_splits; ++s) M = fmaxf(M, ml[2 * s]);
@@ -222,10 +283,13 @@ __global__ void __launch_bounds__(128)
     k_attn_mma(float *part_ml, float *part_acc, float *out, const float *q, const uint16_t *kp,
                const uint16_t *vp, const unsigned *table, const float *sinks, int n_heads,
                int n_kv_heads, int group, size_t kv_begin, size_t n_kv, size_t pt, float scale,
-               size_t kps, int n_splits) {
+               size_t kps, int n_splits, const int *dpos, int window, unsigned *ctr) {
     extern __shared__ __align__(16) uint16_t smem[];
     constexpr int CH = D / 8;  // 16-byte chunks per row
     const int kvh = blockIdx.x, split = blockIdx.y;
+    pdl_trigger();
+    pdl_wait();
+    if (dpos && !device_span(dpos, window, gridDim.y, kv_begin, n_kv, kps, n_splits)) return;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int qd = lane & 3, hr = lane >> 2;  // quad position, head row
     const size_t s0 = kv_begin + (size_t)split * kps;
@@ -384,6 +448,7 @@ __global__ void __launch_bounds__(128)
             part_acc[((size_t)hq * n_splits + split) * D + d] = v;
         }
     }
+    if (n_splits > 1 && ctr) arrive_and_merge(ctr, kvh, n_splits, out, part_ml, part_acc, sinks, kvh * group, group, D);
 }
 
 template <int D, bool BF>
@@ -427,10 +492,14 @@ bool attn_mma_ok(size_t n_heads, size_t n_kv_heads, size_t head_dim, unsigned kv
 int attn_launch(moearc_ctx *c, float *out, const float *q, const void *kp, const void *vp,
                 const unsigned *table, const float *sinks, size_t n_heads, size_t n_kv_heads,
                 size_t hd, size_t kv_begin, size_t n_kv, size_t pt, float scale, unsigned kv_type,
-                float *scratch, size_t scratch_bytes) {
+                float *scratch, size_t scratch_bytes, const int *dpos, int window, int max_splits,
+                unsigned *ctr) {
     const bool mma = attn_mma_ok(n_heads, n_kv_heads, hd, kv_type, kp, vp);
+    cudaError_t err = cudaSuccess;
     size_t kps = 0;
-    const int n_splits = attn_splits(c, n_kv_heads, n_heads, n_kv - kv_begin, mma, &kps);
+    // With the position on the device the split count is decided there; the grid is sized
+    // for the most splits the caller allows.
+    const int n_splits = dpos ? max_splits : attn_splits(c, n_kv_heads, n_heads, n_kv - kv_begin, mma, &kps);
     float *ml = nullptr, *acc = nullptr;
     if (n_splits > 1) {
         if (!scratch || scratch_bytes < attn_scratch_bytes(n_heads, hd, n_splits)) return ERR;
@@ -446,26 +515,26 @@ int attn_launch(moearc_ctx *c, float *out, const float *q, const void *kp, const
             constexpr size_t sm = 4 * warp_smem_elems<64>() * 2;
             if (kv_type == T_BF16) {
                 set_mma_smem<64, true>();
-                k_attn_mma<64, true><<<grid, 128, sm, c->stream>>>(ml, acc, out, q, k16, v16, table, sinks, (int)n_heads, (int)n_kv_heads, group, kv_begin, n_kv, pt, scale, kps, n_splits);
+                err = launch_pdl(k_attn_mma<64, true>, grid, dim3(128), sm, c->stream, ml, acc, out, q, k16, v16, table, sinks, (int)n_heads, (int)n_kv_heads, group, kv_begin, n_kv, pt, scale, kps, n_splits, dpos, window, ctr);
             } else {
                 set_mma_smem<64, false>();
-                k_attn_mma<64, false><<<grid, 128, sm, c->stream>>>(ml, acc, out, q, k16, v16, table, sinks, (int)n_heads, (int)n_kv_heads, group, kv_begin, n_kv, pt, scale, kps, n_splits);
+                err = launch_pdl(k_attn_mma<64, false>, grid, dim3(128), sm, c->stream, ml, acc, out, q, k16, v16, table, sinks, (int)n_heads, (int)n_kv_heads, group, kv_begin, n_kv, pt, scale, kps, n_splits, dpos, window, ctr);
             }
         } else {
             constexpr size_t sm = 4 * warp_smem_elems<128>() * 2;
             if (kv_type == T_BF16) {
                 set_mma_smem<128, true>();
-                k_attn_mma<128, true><<<grid, 128, sm, c->stream>>>(ml, acc, out, q, k16, v16, table, sinks, (int)n_heads, (int)n_kv_heads, group, kv_begin, n_kv, pt, scale, kps, n_splits);
+                err = launch_pdl(k_attn_mma<128, true>, grid, dim3(128), sm, c->stream, ml, acc, out, q, k16, v16, table, sinks, (int)n_heads, (int)n_kv_heads, group, kv_begin, n_kv, pt, scale, kps, n_splits, dpos, window, ctr);
             } else {
                 set_mma_smem<128, false>();
-                k_attn_mma<128, false><<<grid, 128, sm, c->stream>>>(ml, acc, out, q, k16, v16, table, sinks, (int)n_heads, (int)n_kv_heads, group, kv_begin, n_kv, pt, scale, kps, n_splits);
+                err = launch_pdl(k_attn_mma<128, false>, grid, dim3(128), sm, c->stream, ml, acc, out, q, k16, v16, table, sinks, (int)n_heads, (int)n_kv_heads, group, kv_begin, n_kv, pt, scale, kps, n_splits, dpos, window, ctr);
             }
         }
     } else {
         const dim3 grid((unsigned)n_heads, (unsigned)n_splits);
         const size_t sm = (8 + 4 * hd) * sizeof(float);
         const int npl = (int)((hd + 31) / 32);
-#define GEN(N) k_attn_generic<N><<<grid, 128, sm, c->stream>>>(ml, acc, out, q, kp, vp, table, sinks, (int)n_heads, (int)n_kv_heads, (int)hd, kv_begin, n_kv, pt, scale, kv_type, kps, n_splits)
+#define GEN(N) err = launch_pdl(k_attn_generic<N>, grid, dim3(128), sm, c->stream, ml, acc, out, q, kp, vp, table, sinks, (int)n_heads, (int)n_kv_heads, (int)hd, kv_begin, n_kv, pt, scale, kv_type, kps, n_splits, dpos, window, ctr)
         if (npl <= 2) GEN(2);
         else if (npl <= 4) GEN(4);
         else if (npl <= 8) GEN(8);
@@ -475,8 +544,12 @@ int attn_launch(moearc_ctx *c, float *out, const float *q, const void *kp, const
         }
 #undef GEN
     }
-    if (n_splits > 1)
-        k_attn_combine<<<(unsigned)n_heads, 128, 0, c->stream>>>(out, ml, acc, sinks, (int)hd, n_splits);
+    if (err != cudaSuccess) return ERR;
+    // with counters the last split of each head group merges in the kernel; without, a
+    // second kernel merges
+    if (n_splits > 1 && !ctr)
+        k_attn_combine<<<(unsigned)n_heads, 128, 0, c->stream>>>(out, ml, acc, sinks, (int)hd, n_splits, dpos,
+                                                                window, n_splits);
     return OK;
 }
 
@@ -522,7 +595,8 @@ int moearc_attn_decode(moearc_ctx *c, float *out, const float *q, const void *k_
     }
     launch_scope ls(c, "attn_decode", n_heads, (unsigned)head_dim);
     const int rc = attn_launch(c, out, q, k_pages, v_pages, block_table, sinks, n_heads, n_kv_heads,
-                               head_dim, kv_begin, n_kv, page_tokens, scale, kv_type, scratch, sb);
+                               head_dim, kv_begin, n_kv, page_tokens, scale, kv_type, scratch, sb,
+                               nullptr, 0, 0, nullptr);
     const int rc2 = ls.finish();
     return rc ? rc : rc2;
 }

@@ -8,6 +8,7 @@
 
 #include <cstdint>
 #include <string>
+#include <utility>
 #include <vector>
 
 #include "../../include/moearc.h"
@@ -150,5 +151,56 @@ __device__ __forceinline__ float warp_max(float v) {
 }
 
 inline unsigned cdiv(unsigned long a, unsigned long b) { return (unsigned)((a + b - 1) / b); }
+
+// ---- phase timestamps (compiled in only with -DMOEARC_TRACE) --------------------------------
+// TRACE(slot) stores %globaltimer for thread 0 of each CTA at trace[trace_row * 32 + slot]
+// (trace_row: the CTA's row, defined by the kernel as its block index plus a per-kernel base); the
+// buffer is set per translation unit with moearc_trace_set_<unit>. A normal build has none.
+#ifdef MOEARC_TRACE
+static __device__ unsigned long long *g_trace;
+#define TRACE(slot)                                                                      \
+    do {                                                                                 \
+        if (threadIdx.x == 0 && g_trace) {                                               \
+            unsigned long long t_;                                                       \
+            asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t_));                      \
+            g_trace[(size_t)(trace_row) * 32 + (slot)] = t_;                             \
+        }                                                                                \
+    } while (0)
+#define TRACE_SETTER(unit)                                                               \
+    extern "C" int moearc_trace_set_##unit(void *p) {                                    \
+        unsigned long long *v = static_cast<unsigned long long *>(p);                     \
+        return cudaMemcpyToSymbol(g_trace, &v, sizeof(v)) == cudaSuccess ? 0 : -1;         \
+    }
+#else
+#define TRACE(slot) \
+    do {            \
+    } while (0)
+#define TRACE_SETTER(unit)
+#endif
+
+// ---- programmatic dependent launch ---------------------------------------------------------
+// A kernel launched with launch_pdl may begin while the kernel before it in the stream is
+// still running. Everything it does before pdl_wait() must not read that kernel's outputs nor
+// write anything another kernel reads (only static data: weights); pdl_wait() returns once the
+// preceding kernel has completed and its writes are visible. pdl_trigger() lets the next
+// kernel launch early. Both are no-ops in a kernel launched without the attribute.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;\n" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory"); }
+
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
+                              Args &&...args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
 
 }  // namespace moearc

@@ -211,6 +211,26 @@ int moearc_copy_h2d_async(moearc_ctx *c, void *dst, const void *src, unsigned lo
 
 // ---- extensions ------------------------------------------------------------------------
 
+// Page-locked host memory, so host<->device copies run at full PCIe rate and can overlap.
+void *moearc_x_host_alloc(unsigned long bytes) {
+    void *p = nullptr;
+    if (cudaMallocHost(&p, bytes ? bytes : 1) != cudaSuccess) {
+        cudaGetLastError();
+        return nullptr;
+    }
+    return p;
+}
+
+void moearc_x_host_free(void *p) {
+    if (p) cudaFreeHost(p);
+}
+
+int moearc_x_copy_d2h_async(moearc_ctx *c, void *dst, const void *src, unsigned long bytes) {
+    if (!c || !dst || !src) return ERR;
+    if (!bytes) return OK;
+    return cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDeviceToHost, c->stream) == cudaSuccess ? OK : ERR;
+}
+
 void *moearc_x_stream(moearc_ctx *c) { return c ? (void *)c->stream : nullptr; }
 
 int moearc_x_sm_count(moearc_ctx *c) { return c ? c->sm_count : 0; }

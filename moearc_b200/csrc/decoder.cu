@@ -1,0 +1,450 @@
+// decoder.cu — a synthetic routed-MoE decoder (gpt-oss / Qwen3-MoE shaped) decoding one token
+// per step on the device, the per-block sequence of crates/moearc-engine/src/moe.rs:1862-2443:
+//
+//   h = input embedding
+//   for each block: x = rmsnorm(h) ; q,k,v = W x ; rope(q), rope(k) ; append K,V at (page,slot)
+//                   attn = attention over [kv_begin, n_kv) (+ sinks) ; h += Wo attn
+//                   h += MoE(rmsnorm(h))
+//   out = rmsnorm(h)
+//
+// Blocks with l % swa_pattern < swa_pattern - 1 attend through a window of n_swa keys
+// (moe.rs:687-699) kept in a ring of ceil(n_swa / page) pages addressed through a cyclic page
+// table (moe.rs:1420-1438, 1506-1513); the others through the sequence's page table.
+//
+// Weights are random (seeded) and generated on the device; nothing is read from a model file.
+// The position lives in device memory and is advanced by the step's last kernel, so the whole
+// step — 7 kernels per block — is captured once as a CUDA graph and replayed.
+#include <algorithm>
+#include <cmath>
+#include <vector>
+
+#include "common.cuh"
+#include "dense.cuh"
+
+namespace moearc {
+int moe_forward_impl(moearc_x_moe *m, const float *x, unsigned n_tokens, const float *norm_w, float eps,
+                     const float *router_w, const float *router_b, const void *gateup_packed,
+                     const void *down_packed, const float *residual, float *out,
+                     std::vector<cudaEvent_t> *marks = nullptr, std::vector<int> *kinds = nullptr);
+size_t attn_scratch_bytes(size_t n_heads, size_t head_dim, int n_splits);
+int attn_launch(moearc_ctx *c, float *out, const float *q, const void *kp, const void *vp,
+                const unsigned *table, const float *sinks, size_t n_heads, size_t n_kv_heads,
+                size_t hd, size_t kv_begin, size_t n_kv, size_t pt, float scale, unsigned kv_type,
+                float *scratch, size_t scratch_bytes, const int *dpos, int window, int max_splits,
+                unsigned *ctr);
+}  // namespace moearc
+
+using namespace moearc;
+
+namespace {
+
+constexpr int PAGE_TOKENS = 32;  // moe.rs:153
+
+// Seed of one tensor: the model seed, the tensor kind and the layer, mixed.
+uint64_t tensor_seed(uint64_t seed, int kind, int layer) {
+    uint64_t z = seed ^ ((uint64_t)(kind + 1) << 40) ^ ((uint64_t)(layer + 1) * 0x9E3779B97F4A7C15ull);
+    z = (z ^ (z >> 31)) * 0xBF58476D1CE4E5B9ull;
+    return z ^ (z >> 29);
+}
+
+__global__ void k_step_end(float *out, const float *h, const float *w, int n, float eps, int *pos) {
+    __shared__ float red[32];
+    pdl_wait();
+    float ss = 0.f;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) ss = fmaf(h[i], h[i], ss);
+    ss = warp_sum(ss);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+    __syncthreads();
+    float t = 0.f;
+    for (int i = 0; i < (int)(blockDim.x >> 5); ++i) t += red[i];
+    const float scale = 1.0f / sqrtf(t / (float)n + eps);
+    for (int i = threadIdx.x; i < n; i += blockDim.x) out[i] = (h[i] * scale) * w[i];
+    __syncthreads();
+    if (threadIdx.x == 0) *pos += 1;
+}
+
+__global__ void k_set_pos(int *pos, int v) { *pos = v; }
+
+}  // namespace
+
+struct moearc_x_decoder {
+    moearc_ctx *c;
+    moearc_x_decoder_cfg cfg;
+    int Dq, Dkv, n_qkv;
+    struct layer {
+        float *attn_norm, *ffn_norm, *sinks, *router;
+        void *wqkv, *wo, *gateup, *down;
+        uint16_t *k_pages, *v_pages;
+        const unsigned *table;
+        int window;
+        size_t pool_tokens;
+    };
+    std::vector<layer> L;
+    float *output_norm = nullptr;
+    dense_gemv *qkv = nullptr, *wo = nullptr;
+    moearc_x_moe *moe = nullptr;
+    int *dpos = nullptr;
+    unsigned *table_full = nullptr, *table_swa = nullptr;
+    float *in = nullptr, *h = nullptr, *q = nullptr, *att = nullptr, *out = nullptr;
+    float *attn_scratch = nullptr;
+    size_t attn_scratch_b = 0;
+    unsigned *attn_ctr = nullptr;  // one split counter per KV head, zero between steps
+    int max_splits = 1;
+    int pos = 0;
+    std::vector<void *> allocs;
+    cudaGraph_t graph = nullptr;
+    cudaGraphExec_t exec = nullptr;
+    bool use_graph = true;
+
+    void *alloc(size_t bytes) {
+        void *p = nullptr;
+        if (cudaMalloc(&p, bytes ? bytes : 16) != cudaSuccess) {
+            cudaGetLastError();
+            return nullptr;
+        }
+        allocs.push_back(p);
+        return p;
+    }
+};
+
+namespace {
+
+bool is_swa(const moearc_x_decoder_cfg &c, unsigned l) {
+    return c.n_swa > 0 && c.swa_pattern > 0 && (l % c.swa_pattern) < c.swa_pattern - 1;
+}
+
+// Profiling: an event after each launch, tagged with the launch's kind.
+struct step_marks {
+    std::vector<cudaEvent_t> ev;
+    std::vector<int> kind;
+    void mark(cudaStream_t s, int k) {
+        cudaEvent_t e;
+        cudaEventCreate(&e);
+        cudaEventRecord(e, s);
+        ev.push_back(e);
+        kind.push_back(k);
+    }
+};
+
+// Everything one step enqueues, in order (captured into a graph on first use). With `pm`,
+// an event follows every kernel: kinds 0 qkv, 1 attention (+ combine), 2 o-proj, 3 MoE route,
+// 4 MoE gate-up, 5 MoE down, 6 final norm.
+int enqueue_step(moearc_x_decoder *d, step_marks *pm = nullptr) {
+    moearc_ctx *c = d->c;
+    const auto &cfg = d->cfg;
+    if (cudaMemcpyAsync(d->h, d->in, sizeof(float) * cfg.n_embd, cudaMemcpyDeviceToDevice, c->stream) != cudaSuccess)
+        return ERR;
+    if (pm) pm->mark(c->stream, -1);
+    dense_rope rope;
+    rope.n_q_heads = (int)cfg.n_head;
+    rope.n_kv_heads = (int)cfg.n_head_kv;
+    rope.head_dim = (int)cfg.head_dim;
+    rope.n_rot = (int)cfg.head_dim;
+    rope.theta_scale = std::pow((double)cfg.rope_base, -2.0 / (double)cfg.head_dim);
+    rope.freq_scale = cfg.rope_freq_scale;
+    rope.ext_factor = cfg.rope_ext_factor;
+    rope.attn_factor = cfg.rope_attn_factor;
+    rope.corr_lo = cfg.rope_corr_lo;
+    rope.corr_hi = cfg.rope_corr_hi;
+    const float scale = 1.0f / std::sqrt((float)cfg.head_dim);
+    for (unsigned l = 0; l < cfg.n_layer; ++l) {
+        auto &b = d->L[l];
+        dense_kv kv{b.k_pages, b.v_pages, b.table, PAGE_TOKENS};
+        int rc = dense_run(d->qkv, b.wqkv, d->h, b.attn_norm, cfg.rms_eps, d->q, nullptr, d->dpos, &rope, &kv);
+        if (rc) return rc;
+        if (pm) pm->mark(c->stream, 0);
+        rc = attn_launch(c, d->att, d->q, b.k_pages, b.v_pages, b.table, b.sinks, cfg.n_head, cfg.n_head_kv,
+                         cfg.head_dim, 0, 1, PAGE_TOKENS, scale, T_BF16, d->attn_scratch, d->attn_scratch_b,
+                         d->dpos, b.window, d->max_splits, d->attn_ctr);
+        if (rc) return rc;
+        if (pm) pm->mark(c->stream, 1);
+        rc = dense_run(d->wo, b.wo, d->att, nullptr, 0.f, d->h, d->h, d->dpos, nullptr, nullptr);
+        if (rc) return rc;
+        if (pm) pm->mark(c->stream, 2);
+        rc = moe_forward_impl(d->moe, d->h, 1, b.ffn_norm, cfg.rms_eps, b.router, nullptr, b.gateup, b.down,
+                              d->h, d->h, pm ? &pm->ev : nullptr, pm ? &pm->kind : nullptr);
+        if (rc) return rc;
+    }
+    if (launch_pdl(k_step_end, dim3(1), dim3(512), 0, c->stream, d->out, (const float *)d->h,
+                   (const float *)d->output_norm, (int)cfg.n_embd, cfg.rms_eps, d->dpos) != cudaSuccess)
+        return ERR;
+    if (pm) pm->mark(c->stream, 6);
+    return cudaGetLastError() == cudaSuccess ? OK : ERR;
+}
+
+int synth(moearc_ctx *c, void *dst, size_t n, unsigned kind, uint64_t seed, float sigma, int lo = -8, int hi = -4) {
+    return moearc_x_synth(c, dst, n, kind, seed, sigma, lo, hi);
+}
+
+}  // namespace
+
+extern "C" {
+
+moearc_x_decoder *moearc_x_decoder_create(moearc_ctx *c, const moearc_x_decoder_cfg *cfg) {
+    if (!c || !cfg) return nullptr;
+    const auto &g = *cfg;
+    if (g.n_layer == 0 || g.n_head % std::max(1u, g.n_head_kv) || (g.head_dim != 64 && g.head_dim != 128))
+        return nullptr;
+    if (g.n_head / g.n_head_kv > 8 || g.n_ctx == 0) return nullptr;
+    auto *d = new moearc_x_decoder();
+    d->c = c;
+    d->cfg = g;
+    d->Dq = (int)(g.n_head * g.head_dim);
+    d->Dkv = (int)(g.n_head_kv * g.head_dim);
+    d->n_qkv = d->Dq + 2 * d->Dkv;
+    const int H = (int)g.n_embd;
+    bool ok = true;
+    auto fail = [&]() {
+        moearc_x_decoder_destroy(d);
+        return (moearc_x_decoder *)nullptr;
+    };
+    moearc_x_moe_desc md{g.n_embd, g.n_ff, g.n_expert, g.n_expert_used, g.gating, g.act, g.alpha, g.limit,
+                         g.expert_type, 1};
+    d->moe = moearc_x_moe_create(c, &md);
+    d->qkv = dense_create(c, d->n_qkv, H, 0);
+    d->wo = dense_create(c, H, d->Dq, 1);
+    if (!d->moe || !d->qkv || !d->wo) return fail();
+
+    // page tables: the sequence's (a seeded permutation, so pages are scattered as a pool that
+    // has served other sequences would hand them out) and the windowed blocks' ring
+    const int pages = (int)((g.n_ctx + PAGE_TOKENS - 1) / PAGE_TOKENS);
+    const int swa_pages = g.n_swa ? std::min(pages, (int)((g.n_swa + PAGE_TOKENS - 1) / PAGE_TOKENS)) : pages;
+    std::vector<unsigned> tf(pages), ts(pages);
+    for (int i = 0; i < pages; ++i) tf[i] = (unsigned)i;
+    uint64_t st = g.seed ^ 0x7AB1Eull;
+    for (int i = pages - 1; i > 0; --i) {
+        st = st * 6364136223846793005ull + 1442695040888963407ull;
+        std::swap(tf[i], tf[(int)((st >> 33) % (uint64_t)(i + 1))]);
+    }
+    for (int i = 0; i < pages; ++i) ts[i] = (unsigned)(i % swa_pages);
+    d->table_full = static_cast<unsigned *>(d->alloc(sizeof(unsigned) * pages));
+    d->table_swa = static_cast<unsigned *>(d->alloc(sizeof(unsigned) * pages));
+    d->dpos = static_cast<int *>(d->alloc(sizeof(int)));
+    d->in = static_cast<float *>(d->alloc(sizeof(float) * H));
+    d->h = static_cast<float *>(d->alloc(sizeof(float) * H));
+    d->out = static_cast<float *>(d->alloc(sizeof(float) * H));
+    d->q = static_cast<float *>(d->alloc(sizeof(float) * d->Dq));
+    d->att = static_cast<float *>(d->alloc(sizeof(float) * d->Dq));
+    d->output_norm = static_cast<float *>(d->alloc(sizeof(float) * H));
+    d->max_splits = std::max(1, (2 * c->sm_count + (int)g.n_head_kv - 1) / (int)g.n_head_kv);
+    d->attn_scratch_b = attn_scratch_bytes(g.n_head, g.head_dim, d->max_splits);
+    d->attn_scratch = static_cast<float *>(d->alloc(d->attn_scratch_b));
+    d->attn_ctr = static_cast<unsigned *>(d->alloc(sizeof(unsigned) * g.n_head));
+    if (!d->table_full || !d->table_swa || !d->dpos || !d->in || !d->h || !d->out || !d->q || !d->att ||
+        !d->output_norm || !d->attn_scratch)
+        return fail();
+    ok &= cudaMemcpy(d->table_full, tf.data(), sizeof(unsigned) * pages, cudaMemcpyHostToDevice) == cudaSuccess;
+    ok &= cudaMemcpy(d->table_swa, ts.data(), sizeof(unsigned) * pages, cudaMemcpyHostToDevice) == cudaSuccess;
+    ok &= cudaMemset(d->dpos, 0, sizeof(int)) == cudaSuccess;
+    ok &= d->attn_ctr && cudaMemset(d->attn_ctr, 0, sizeof(unsigned) * g.n_head) == cudaSuccess;
+    ok &= cudaMemset(d->in, 0, sizeof(float) * H) == cudaSuccess;
+    ok &= synth(c, d->output_norm, H, 4, tensor_seed(g.seed, 11, 0), 0.1f) == OK;
+
+    // per-layer weights: generated in GGUF/row-major layout into a staging buffer, then packed
+    const size_t bb = (g.expert_type == T_MXFP4) ? 17 : 18;
+    const size_t blocks = (size_t)g.n_expert * g.n_ff * g.n_embd / 32;
+    const size_t bank_bytes = blocks * bb;
+    const size_t qkv_elems = (size_t)d->n_qkv * H, wo_elems = (size_t)H * d->Dq;
+    const size_t stage_bytes = std::max({3 * bank_bytes, qkv_elems * 2, wo_elems * 2});
+    void *staging = nullptr;
+    if (cudaMalloc(&staging, stage_bytes) != cudaSuccess) {
+        cudaGetLastError();
+        return fail();
+    }
+    const unsigned ekind = (g.expert_type == T_MXFP4) ? 2 : 3;
+    const float esig = 0.01f;
+    d->L.resize(g.n_layer);
+    for (unsigned l = 0; l < g.n_layer && ok; ++l) {
+        auto &b = d->L[l];
+        const int window = is_swa(g, l) ? (int)g.n_swa : 0;
+        b.window = window;
+        b.table = window ? d->table_swa : d->table_full;
+        b.pool_tokens = (size_t)(window ? swa_pages : pages) * PAGE_TOKENS;
+        b.attn_norm = static_cast<float *>(d->alloc(sizeof(float) * H));
+        b.ffn_norm = static_cast<float *>(d->alloc(sizeof(float) * H));
+        b.sinks = g.has_sinks ? static_cast<float *>(d->alloc(sizeof(float) * g.n_head)) : nullptr;
+        b.router = static_cast<float *>(d->alloc(sizeof(float) * g.n_expert * H));
+        b.wqkv = d->alloc(qkv_elems * 2);
+        b.wo = d->alloc(wo_elems * 2);
+        b.gateup = d->alloc(2 * bank_bytes);
+        b.down = d->alloc(bank_bytes);
+        b.k_pages = static_cast<uint16_t *>(d->alloc(b.pool_tokens * d->Dkv * 2));
+        b.v_pages = static_cast<uint16_t *>(d->alloc(b.pool_tokens * d->Dkv * 2));
+        if (!b.attn_norm || !b.ffn_norm || (g.has_sinks && !b.sinks) || !b.router || !b.wqkv || !b.wo ||
+            !b.gateup || !b.down || !b.k_pages || !b.v_pages) {
+            ok = false;
+            break;
+        }
+        ok &= synth(c, b.attn_norm, H, 4, tensor_seed(g.seed, 0, l), 0.1f) == OK;
+        ok &= synth(c, b.ffn_norm, H, 4, tensor_seed(g.seed, 1, l), 0.1f) == OK;
+        if (b.sinks) ok &= synth(c, b.sinks, g.n_head, 0, tensor_seed(g.seed, 6, l), 1.0f) == OK;
+        ok &= synth(c, b.router, (size_t)g.n_expert * H, 0, tensor_seed(g.seed, 7, l), 0.02f) == OK;
+        // Q, K, V rows concatenated into one [Dq + 2 Dkv] x H matrix
+        uint16_t *s16 = static_cast<uint16_t *>(staging);
+        ok &= synth(c, s16, (size_t)d->Dq * H, 1, tensor_seed(g.seed, 2, l), 0.02f) == OK;
+        ok &= synth(c, s16 + (size_t)d->Dq * H, (size_t)d->Dkv * H, 1, tensor_seed(g.seed, 3, l), 0.02f) == OK;
+        ok &= synth(c, s16 + (size_t)(d->Dq + d->Dkv) * H, (size_t)d->Dkv * H, 1, tensor_seed(g.seed, 4, l), 0.02f) == OK;
+        ok &= dense_pack(c, b.wqkv, staging, d->n_qkv, H) == OK;
+        ok &= synth(c, s16, wo_elems, 1, tensor_seed(g.seed, 5, l), 0.02f) == OK;
+        ok &= dense_pack(c, b.wo, staging, H, d->Dq) == OK;
+        uint8_t *s8 = static_cast<uint8_t *>(staging);
+        ok &= synth(c, s8, blocks, ekind, tensor_seed(g.seed, 8, l), esig) == OK;
+        ok &= synth(c, s8 + bank_bytes, blocks, ekind, tensor_seed(g.seed, 9, l), esig) == OK;
+        ok &= synth(c, s8 + 2 * bank_bytes, blocks, ekind, tensor_seed(g.seed, 10, l), esig) == OK;
+        ok &= moearc_x_moe_pack(d->moe, s8, s8 + bank_bytes, s8 + 2 * bank_bytes, g.n_expert, b.gateup, b.down) == OK;
+        // an empty cache reads as zeros; fill_kv writes synthetic contents
+        ok &= cudaMemsetAsync(b.k_pages, 0, b.pool_tokens * d->Dkv * 2, c->stream) == cudaSuccess;
+        ok &= cudaMemsetAsync(b.v_pages, 0, b.pool_tokens * d->Dkv * 2, c->stream) == cudaSuccess;
+    }
+    ok &= cudaStreamSynchronize(c->stream) == cudaSuccess;
+    cudaFree(staging);
+    if (!ok) return fail();
+    return d;
+}
+
+void moearc_x_decoder_destroy(moearc_x_decoder *d) {
+    if (!d) return;
+    cudaStreamSynchronize(d->c->stream);
+    if (d->exec) cudaGraphExecDestroy(d->exec);
+    if (d->graph) cudaGraphDestroy(d->graph);
+    if (d->moe) moearc_x_moe_destroy(d->moe);
+    if (d->qkv) dense_destroy(d->qkv);
+    if (d->wo) dense_destroy(d->wo);
+    for (void *p : d->allocs) cudaFree(p);
+    delete d;
+}
+
+void *moearc_x_decoder_input(moearc_x_decoder *d) { return d ? d->in : nullptr; }
+void *moearc_x_decoder_output(moearc_x_decoder *d) { return d ? d->out : nullptr; }
+
+int moearc_x_decoder_pos(moearc_x_decoder *d) { return d ? d->pos : -1; }
+
+int moearc_x_decoder_set_pos(moearc_x_decoder *d, unsigned pos) {
+    if (!d) return ERR;
+    if (pos >= d->cfg.n_ctx) return ERR_ARG;
+    k_set_pos<<<1, 1, 0, d->c->stream>>>(d->dpos, (int)pos);
+    d->pos = (int)pos;
+    return cudaGetLastError() == cudaSuccess ? OK : ERR;
+}
+
+// Synthetic K/V bf16 N(0, 0.02) in every page of every block, and the position set to depth:
+// the state of a sequence that has already decoded `depth` tokens.
+int moearc_x_decoder_fill_kv(moearc_x_decoder *d, unsigned depth, unsigned long long seed) {
+    if (!d) return ERR;
+    if (depth >= d->cfg.n_ctx) return ERR_ARG;
+    for (unsigned l = 0; l < d->cfg.n_layer; ++l) {
+        auto &b = d->L[l];
+        const size_t n = b.pool_tokens * d->Dkv;
+        if (synth(d->c, b.k_pages, n, 1, tensor_seed(seed, 12, l), 0.02f) != OK) return ERR;
+        if (synth(d->c, b.v_pages, n, 1, tensor_seed(seed, 13, l), 0.02f) != OK) return ERR;
+    }
+    return moearc_x_decoder_set_pos(d, depth);
+}
+
+int moearc_x_decoder_use_graph(moearc_x_decoder *d, int on) {
+    if (!d) return ERR;
+    d->use_graph = on != 0;
+    return OK;
+}
+
+int moearc_x_decoder_step(moearc_x_decoder *d) {
+    if (!d) return ERR;
+    if ((unsigned)d->pos >= d->cfg.n_ctx) return ERR_ARG;
+    moearc_ctx *c = d->c;
+    int rc = OK;
+    if (!d->use_graph) {
+        rc = enqueue_step(d);
+    } else {
+        if (!d->exec) {
+            if (cudaStreamBeginCapture(c->stream, cudaStreamCaptureModeThreadLocal) != cudaSuccess) return ERR;
+            rc = enqueue_step(d);
+            cudaGraph_t g = nullptr;
+            const cudaError_t e = cudaStreamEndCapture(c->stream, &g);
+            if (rc || e != cudaSuccess) {
+                if (g) cudaGraphDestroy(g);
+                cudaGetLastError();
+                return rc ? rc : ERR;
+            }
+            d->graph = g;
+            if (cudaGraphInstantiate(&d->exec, g, 0) != cudaSuccess) {
+                cudaGetLastError();
+                return ERR;
+            }
+        }
+        rc = cudaGraphLaunch(d->exec, c->stream) == cudaSuccess ? OK : ERR;
+    }
+    if (rc == OK) d->pos += 1;
+    return rc;
+}
+
+// One step, not graphed, with an event after every kernel; ms[k] receives the total device
+// time of kernel kind k (0 qkv, 1 attention, 2 o-proj, 3 MoE route, 4 MoE gate-up, 5 MoE down,
+// 6 final norm) and counts[k] how many launches of that kind ran.
+int moearc_x_decoder_profile(moearc_x_decoder *d, float *ms, int *counts, int n) {
+    if (!d || !ms || n < 7) return ERR;
+    if ((unsigned)d->pos >= d->cfg.n_ctx) return ERR_ARG;
+    step_marks pm;
+    int rc = enqueue_step(d, &pm);
+    if (cudaStreamSynchronize(d->c->stream) != cudaSuccess) rc = ERR;
+    for (int k = 0; k < n; ++k) {
+        ms[k] = 0.f;
+        if (counts) counts[k] = 0;
+    }
+    for (size_t i = 1; i < pm.ev.size(); ++i) {
+        float t = 0.f;
+        cudaEventElapsedTime(&t, pm.ev[i - 1], pm.ev[i]);
+        const int k = pm.kind[i];
+        if (k >= 0 && k < n) {
+            ms[k] += t;
+            if (counts) counts[k] += 1;
+        }
+    }
+    for (auto e : pm.ev) cudaEventDestroy(e);
+    if (rc == OK) d->pos += 1;
+    return rc;
+}
+
+// Device pointers of one block's tensors, for inspection: 0 attn_norm, 1 ffn_norm, 2 sinks,
+// 3 router, 4 K pool, 5 V pool, 6 page table, 7 packed Q/K/V, 8 packed O, 9 packed gate-up,
+// 10 packed down; 11 output norm (layer ignored). `bytes` receives the size.
+void *moearc_x_decoder_tensor(moearc_x_decoder *d, int which, unsigned layer, unsigned long *bytes) {
+    if (!d || (which != 11 && layer >= d->cfg.n_layer)) return nullptr;
+    const auto &g = d->cfg;
+    const size_t H = g.n_embd;
+    const size_t bb = (g.expert_type == T_MXFP4) ? 17 : 18;
+    const size_t bank = (size_t)g.n_expert * g.n_ff * g.n_embd / 32 * bb;
+    unsigned long n = 0;
+    void *p = nullptr;
+    if (which == 11) {
+        p = d->output_norm;
+        n = H * 4;
+    } else {
+        auto &b = d->L[layer];
+        switch (which) {
+        case 0: p = b.attn_norm; n = H * 4; break;
+        case 1: p = b.ffn_norm; n = H * 4; break;
+        case 2: p = b.sinks; n = b.sinks ? g.n_head * 4 : 0; break;
+        case 3: p = b.router; n = (unsigned long)g.n_expert * H * 4; break;
+        case 4: p = b.k_pages; n = b.pool_tokens * d->Dkv * 2; break;
+        case 5: p = b.v_pages; n = b.pool_tokens * d->Dkv * 2; break;
+        case 6: p = (void *)b.table; n = (g.n_ctx + PAGE_TOKENS - 1) / PAGE_TOKENS * 4; break;
+        case 7: p = b.wqkv; n = (unsigned long)d->n_qkv * H * 2; break;
+        case 8: p = b.wo; n = H * d->Dq * 2; break;
+        case 9: p = b.gateup; n = 2 * bank; break;
+        case 10: p = b.down; n = bank; break;
+        default: return nullptr;
+        }
+    }
+    if (bytes) *bytes = n;
+    return p;
+}
+
+// The seed the decoder generated tensor `kind` of block `layer` from (kinds: 0 attn_norm,
+// 1 ffn_norm, 2 wq, 3 wk, 4 wv, 5 wo, 6 sinks, 7 router, 8 gate, 9 up, 10 down,
+// 11 output_norm, 12/13 K/V fill), so a checker can regenerate the GGUF-layout tensors.
+unsigned long long moearc_x_decoder_seed(moearc_x_decoder *d, int kind, unsigned layer, unsigned long long base) {
+    (void)d;
+    return tensor_seed(base, kind, (int)layer);
+}
+
+}  // extern "C"

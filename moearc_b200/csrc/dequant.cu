@@ -155,6 +155,8 @@ __global__ void k_synth(uint8_t *dst, size_t n, unsigned kind, uint64_t seed, fl
     for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
         if (kind == 0) {
             reinterpret_cast<float *>(dst)[i] = (float)(normal_at(seed, i) * (double)sigma);
+        } else if (kind == 4) {
+            reinterpret_cast<float *>(dst)[i] = (float)(1.0 + normal_at(seed, i) * (double)sigma);
         } else if (kind == 1) {
             reinterpret_cast<uint16_t *>(dst)[i] = f32_to_bf16_bits((float)(normal_at(seed, i) * (double)sigma));
         } else if (kind == 2) {
@@ -245,7 +247,7 @@ int moearc_gather_experts(moearc_ctx *c, void *dst, const void *pool, const unsi
 int moearc_x_synth(moearc_ctx *c, void *dst, unsigned long n, unsigned int kind,
                    unsigned long long seed, float sigma, int lo, int hi) {
     if (!c || !dst) return ERR;
-    if (kind > 3 || (kind == 2 && hi < lo)) return ERR_ARG;
+    if (kind > 4 || (kind == 2 && hi < lo)) return ERR_ARG;
     if (n == 0) return OK;
     launch_scope ls(c, "synth", n, kind);
     k_synth<<<grid_for(c, n, 256), 256, 0, c->stream>>>(static_cast<uint8_t *>(dst), n, kind, seed,

@@ -47,9 +47,9 @@ struct moearc_x_moe {
     // derived
     int tile_bytes;  // one packed tile (16 rows x 64 cols)
     int nkt_h, nkt_i, ntr_h, ntr_i;
-    int kc_gu, nch_gu, kc_dn, nch_dn;
-    int stage_gu, stage_dn;  // bytes per warp per stage
-    int grid_gu, grid_dn;
+    // gate-up (mode 0) and down (mode 1) kernel plans
+    int warps_gu, ranges_gu, tpr_gu, stages_gu, stage_gu, smem_gu, grid_gu;
+    int warps_dn, ranges_dn, tpr_dn, stages_dn, stage_dn, smem_dn, grid_dn;
     // device scratch (one allocation)
     void *mem;
     size_t mem_bytes;
@@ -60,16 +60,12 @@ struct moearc_x_moe {
     uint32_t *xfrag;   // [T_max][H/32][2][4][4] u32
     uint32_t *actfrag; // [T_max*K][I/32][2][4][4] u32
     float *act_f32;    // [T_max*K][I], the activation, kept for inspection
-    float *part_gu;    // [nch_gu][T_max*K][I][2]
-    float *part_dn;    // [nch_dn][T_max*K][H]
     unsigned *ctr;     // route done counter, gate-up unit counters, down unit counters
     int *status;
 };
 
 namespace {
 
-constexpr int WARPS = 4;   // per CTA of the expert kernels
-constexpr int STAGES = 2;
 constexpr int GROUP = 4;   // tokens per column group (2 MMA columns each)
 
 // Layout of the int tables written by k_route (offsets in ints):
@@ -87,7 +83,7 @@ struct tab_view {
     __host__ __device__ int *slot_expert() const { return grp_ntok() + G; }
     __host__ __device__ int *col_tok() const { return slot_expert() + S; }
     __host__ __device__ int *col_of() const { return col_tok() + C; }
-    static size_t ints(int G, int S, int C, int TK) { return 4 + 3 * (size_t)G + S + C + TK; }
+    __host__ __device__ static size_t ints(int G, int S, int C, int TK) { return 4 + 3 * (size_t)G + S + C + TK; }
 };
 
 // ---- packing ------------------------------------------------------------------------------
@@ -268,6 +264,8 @@ __device__ __forceinline__ float act_fn(int act, float g, float u, float alpha, 
 
 struct route_args {
     const float *x;       // [T][H]
+    const float *norm_w;  // [H]: route rmsnorm(x) * norm_w instead of x (null: x as is)
+    float eps;
     const float *router;  // [E][H]
     const float *rbias;   // [E] or null
     int T, H, E, K, gating;
@@ -333,55 +331,119 @@ __device__ void topk_token(const route_args &a, int t, int lane) {
     if (mine) a.wts[(size_t)t * a.K + lane] = w;
 }
 
-__global__ void __launch_bounds__(256) k_route(route_args a) {
+constexpr int ROUTE_NORM_TOKENS = 64;
+
+constexpr int ROUTE_WARPS = 4;
+
+__global__ void __launch_bounds__(ROUTE_WARPS * 32) k_route(route_args a) {
+    const int trace_row = (int)blockIdx.x;
+    (void)trace_row;
+    TRACE(0);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int gw = blockIdx.x * 8 + warp, nw = gridDim.x * 8;
-    // (a) router logits, the fixed order of moearc_matvec_f32 (reproducible on the host)
+    const int gw = blockIdx.x * ROUTE_WARPS + warp, nw = gridDim.x * ROUTE_WARPS;
+    // The router weights are static: have L2 fetch this warp's rows while the previous kernel
+    // finishes.
+    if (lane == 0)
+        for (int row = gw; row < a.T * a.E; row += nw)
+            bulk_prefetch_l2(a.router + (size_t)(row % a.E) * a.H, (unsigned)(a.H * 4));
+    pdl_trigger();
+    pdl_wait();
+    TRACE(1);
+    // (0) the RMSNorm scale of every token, when routing the normalised residual stream
+    // (moe.rs:2074-2076): f32 sum of squares, 1/sqrt(mean + eps)
+    __shared__ float nscale[ROUTE_NORM_TOKENS];
+    if (a.norm_w) {
+        for (int t = warp; t < a.T; t += ROUTE_WARPS) {
+            const float4 *xr = reinterpret_cast<const float4 *>(a.x + (size_t)t * a.H);
+            float ss = 0.f;
+#pragma unroll 8
+            for (int c = lane; c < a.H / 4; c += 32) {
+                const float4 v = __ldcg(xr + c);
+                ss = fmaf(v.x, v.x, fmaf(v.y, v.y, fmaf(v.z, v.z, fmaf(v.w, v.w, ss))));
+            }
+            ss = warp_sum(ss);
+            if (lane == 0) nscale[t] = 1.0f / sqrtf(ss / (float)a.H + a.eps);
+        }
+        __syncthreads();
+    }
+    // (a) router logits, the fixed order of moearc_matvec_f32 (reproducible on the host):
+    // lane l folds float4 columns l, l + 32, l + 64, ... in that order; loads are batched
+    // eight deep ahead of the multiply-adds, which keeps the order
+    const int n4 = a.H / 4;
     for (int row = gw; row < a.T * a.E; row += nw) {
         const int t = row / a.E, e = row % a.E;
-        const float *wr = a.router + (size_t)e * a.H;
-        const float *xr = a.x + (size_t)t * a.H;
+        const float4 *wr = reinterpret_cast<const float4 *>(a.router + (size_t)e * a.H);
+        const float4 *xr = reinterpret_cast<const float4 *>(a.x + (size_t)t * a.H);
+        const float4 *nr = reinterpret_cast<const float4 *>(a.norm_w);
         float acc = 0.f;
-        for (int c4 = lane; c4 < a.H / 4; c4 += 32) {
-            const float4 w4 = __ldg(reinterpret_cast<const float4 *>(wr) + c4);
-            const float4 x4 = __ldg(reinterpret_cast<const float4 *>(xr) + c4);
-            acc = fmaf(w4.x, x4.x, acc);
-            acc = fmaf(w4.y, x4.y, acc);
-            acc = fmaf(w4.z, x4.z, acc);
-            acc = fmaf(w4.w, x4.w, acc);
+        for (int c0 = lane; c0 < n4; c0 += 32 * 8) {
+            float4 wv[8], xv[8];
+#pragma unroll
+            for (int u = 0; u < 8; ++u) {
+                const int c4 = c0 + 32 * u;
+                if (c4 < n4) {
+                    wv[u] = __ldg(wr + c4);
+                    xv[u] = __ldcg(xr + c4);
+                    if (a.norm_w) {
+                        const float s = nscale[t];
+                        const float4 n = __ldg(nr + c4);
+                        xv[u] = make_float4((xv[u].x * s) * n.x, (xv[u].y * s) * n.y, (xv[u].z * s) * n.z,
+                                            (xv[u].w * s) * n.w);
+                    }
+                }
+            }
+#pragma unroll
+            for (int u = 0; u < 8; ++u) {
+                if (c0 + 32 * u < n4) {
+                    acc = fmaf(wv[u].x, xv[u].x, acc);
+                    acc = fmaf(wv[u].y, xv[u].y, acc);
+                    acc = fmaf(wv[u].z, xv[u].z, acc);
+                    acc = fmaf(wv[u].w, xv[u].w, acc);
+                }
+            }
         }
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
         if (lane == 0) a.logits[row] = a.rbias ? acc + a.rbias[e] : acc;
     }
+    TRACE(2);
     // (b) x -> B fragments: [t][block][part][q][j] = pair (x[32b+4q+j], x[32b+4q+16+j])
     const int nblk = a.H / 32;
-    for (int i = blockIdx.x * 256 + threadIdx.x; i < a.T * nblk * 16; i += gridDim.x * 256) {
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < a.T * nblk * 16; i += gridDim.x * blockDim.x) {
         const int j = i & 3, q = (i >> 2) & 3;
         const int tb = i >> 4, t = tb / nblk, b = tb % nblk;
         const float *xr = a.x + (size_t)t * a.H + 32 * b;
+        float v0 = xr[4 * q + j], v1 = xr[4 * q + 16 + j];
+        if (a.norm_w) {
+            const float s = nscale[t];
+            v0 = (v0 * s) * a.norm_w[32 * b + 4 * q + j];
+            v1 = (v1 * s) * a.norm_w[32 * b + 4 * q + 16 + j];
+        }
         uint32_t hi, lo;
-        split_f16x2(xr[4 * q + j], xr[4 * q + 16 + j], hi, lo);
+        split_f16x2(v0, v1, hi, lo);
         a.xfrag[((((size_t)t * nblk + b) * 2 + 0) * 4 + q) * 4 + j] = hi;
         a.xfrag[((((size_t)t * nblk + b) * 2 + 1) * 4 + q) * 4 + j] = lo;
     }
     // the last CTA to finish does the top-k and builds the slot tables
+    TRACE(3);
     __shared__ unsigned last;
     __threadfence();
     __syncthreads();
     if (threadIdx.x == 0) last = (atomicAdd(a.done, 1u) == gridDim.x - 1);
     __syncthreads();
+    TRACE(4);
     if (!last) return;
     __threadfence();
-    for (int t = warp; t < a.T; t += 8) topk_token(a, t, lane);
+    for (int t = warp; t < a.T; t += ROUTE_WARPS) topk_token(a, t, lane);
+    TRACE(5);
     __threadfence_block();
     __syncthreads();
     // slots: distinct experts ascending; a slot's columns are its tokens in token order
     __shared__ int cnt[1024];
-    for (int e = threadIdx.x; e < a.E; e += 256) cnt[e] = 0;
+    for (int e = threadIdx.x; e < a.E; e += blockDim.x) cnt[e] = 0;
     __syncthreads();
     const int TK = a.T * a.K;
-    for (int e = threadIdx.x; e < a.E; e += 256) {
+    for (int e = threadIdx.x; e < a.E; e += blockDim.x) {
         int c = 0;
         for (int i = 0; i < TK; ++i) c += (a.idx[i] == (unsigned)e);
         cnt[e] = c;
@@ -403,6 +465,7 @@ __global__ void __launch_bounds__(256) k_route(route_args a) {
             col += n;
             ++s;
         }
+        TRACE(6);
         *a.tab.n_slots() = s;
         *a.tab.n_groups() = g;
         *a.tab.n_cols() = col;
@@ -418,170 +481,244 @@ __global__ void __launch_bounds__(256) k_route(route_args a) {
 }
 
 // ---- kernels 2 and 3: the grouped expert GEMVs ---------------------------------------------
+//
+// A CTA owns a unit of output rows and nothing else touches them:
+//   gate-up  unit (column group, tile-row): 16 rows of gate and up for <= 4 tokens
+//   down     unit tile-row: 16 output rows for every token
+// The unit's K extent is cut into `ranges` contiguous runs of k-tiles; an item is one run of
+// one column group. The CTA's warps take the unit's items round-robin, each warp streaming
+// its items' weight runs (and activation fragments) through its own ring of `stages`
+// shared-memory buffers, filled by TMA bulk copies and tracked by mbarriers. The ring runs
+// ahead across unit boundaries, so a warp's next unit is already in flight while the CTA
+// reduces the current one. Partial sums go to shared memory; after a CTA barrier the unit is
+// reduced in a fixed order (range ascending) and finished: SwiGLU into the down kernel's
+// fragments, or the router-weighted combine in router order plus the residual.
 
-struct gemv_args {
+struct rows_args {
     const uint8_t *bank;      // packed gate-up (2 tiles per k-tile) or down bank
     size_t bank_stride;       // bytes per expert
     int mats;                 // 2 for gate-up, 1 for down
-    int ntr, nkt, kc, nch;    // tile-rows, k-tiles per row, k-tiles per chunk, chunks
+    int ntr, nkt;             // tile-rows, k-tiles (64 columns) per row
+    int ranges, tpr;          // K runs per item row, most k-tiles in one run
     int tile_bytes;
-    int stage_bytes;
+    int stages, stage_bytes;  // per-warp ring
+    int n_units_hint;         // units the grid was sized for
     const uint32_t *bsrc;     // B fragments, indexed by token (gate-up) or column (down)
-    int b_by_column;          // 0: bsrc row = token of the column, 1: row = the column itself
-    int nblk_b;               // blocks per B row
-    tab_view tab;
+    int b_by_column;
+    int nblk_b;
+    tab_view tab;             // in global memory; copied to shared memory at start
     // gate-up epilogue
     int act;
     float alpha, limit;
     uint32_t *actfrag;        // [col][I/32][2][4][4]
-    float *act_out;           // [col][I] f32, optional
+    float *act_out;           // [col][I] f32
     int I;
     // down epilogue
     const float *wts;         // [T][K]
     const float *residual;    // [T][H] or null
     float *out;               // [T][H]
     int T, K, H;
-    float *part;
-    unsigned *ctr;
     int *status;
 };
 
-// Item i -> (group, tile-row, chunk).
-__device__ __forceinline__ void item_of(const gemv_args &a, int i, int &g, int &tr, int &ch) {
-    ch = i % a.nch;
-    const int r = i / a.nch;
-    tr = r % a.ntr;
-    g = r / a.ntr;
-}
+__device__ __forceinline__ int range_lo(int r, int nkt, int ranges) { return (int)(((long)r * nkt) / ranges); }
 
-__device__ __forceinline__ void issue_item(const gemv_args &a, int item, uint8_t *stage, uint64_t *bar,
-                                           int lane) {
-    int g, tr, ch;
-    item_of(a, item, g, tr, ch);
-    const int slot = a.tab.grp_slot()[g];
-    const int expert = a.tab.slot_expert()[slot];
-    const int col0 = a.tab.grp_col0()[g], ntok = a.tab.grp_ntok()[g];
-    const int k0 = ch * a.kc;
-    const int kn = min(a.kc, a.nkt - k0);
-    const unsigned wbytes = (unsigned)(kn * a.mats * a.tile_bytes);
-    const unsigned bbytes_tok = (unsigned)(2 * kn * 128);
-    if (lane == 0) {
-        fence_proxy_async();
-        mbar_expect_tx(bar, wbytes + bbytes_tok * ntok);
-        const uint8_t *w = a.bank + (size_t)expert * a.bank_stride +
-                           ((size_t)tr * a.nkt + k0) * a.mats * a.tile_bytes;
-        bulk_g2s(stage, w, wbytes, bar);
-        uint8_t *bs = stage + a.kc * a.mats * a.tile_bytes;
-        for (int t = 0; t < ntok; ++t) {
-            const int col = col0 + t;
-            const int row = a.b_by_column ? col : a.tab.col_tok()[col];
-            const uint32_t *src = a.bsrc + ((size_t)row * a.nblk_b + 2 * k0) * 32;
-            bulk_g2s(bs + (size_t)t * a.kc * 2 * 128, src, bbytes_tok, bar);
-        }
-    }
-}
+struct item_pos {
+    int u, i;
+};
 
 template <int WT>
-__global__ void __launch_bounds__(WARPS * 32) k_expert_gemv(gemv_args a) {
+__global__ void __launch_bounds__(256) k_moe_rows(rows_args a) {
     extern __shared__ __align__(128) uint8_t smem[];
-    __shared__ __align__(8) uint64_t bars[WARPS][STAGES];
+    __shared__ __align__(8) uint64_t bars[8][4];
+    const int trace_row = (int)blockIdx.x + (a.mats == 2 ? 1024 : 2048);
+    (void)trace_row;
+    TRACE(0);
+    const int nwarps = blockDim.x >> 5;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int gw = blockIdx.x * WARPS + warp, nw = gridDim.x * WARPS;
-    uint8_t *my = smem + (size_t)warp * STAGES * a.stage_bytes;
+    const bool down = a.mats == 1;
+
+    // gate-up consumes the routing tables of the kernel before it: wait, then release the
+    // down kernel, which may then read the same tables before its own wait.
+    if (!down) {
+        pdl_wait();
+        pdl_trigger();
+    }
+    // routing tables into shared memory
+    const int n_tab = (int)tab_view::ints(a.tab.G, a.tab.S, a.tab.C, a.tab.TK);
+    int *tabs = reinterpret_cast<int *>(smem);
+    for (int i = threadIdx.x; i < n_tab; i += blockDim.x) tabs[i] = __ldcg(a.tab.base + i);
+    __syncthreads();
+    tab_view tb = a.tab;
+    tb.base = tabs;
+    const int G = *tb.n_groups(), ncol = *tb.n_cols();
+    const size_t tab_bytes = ((size_t)n_tab * 4 + 127) / 128 * 128;
+    float *part = reinterpret_cast<float *>(smem + tab_bytes);
+    const size_t part_floats = down ? (size_t)a.tab.G * a.ranges * 16 * GROUP : (size_t)a.ranges * 2 * 16 * GROUP;
+    float *osum = part + part_floats;  // down: [col][16]
+    const size_t part_bytes = ((part_floats + (down ? (size_t)a.tab.C * 16 : 0)) * 4 + 127) / 128 * 128;
+    uint8_t *ring = smem + tab_bytes + part_bytes + (size_t)warp * a.stages * a.stage_bytes;
+
+    const int n_units = down ? a.ntr : G * a.ntr;
+    const int items_per_unit = down ? G * a.ranges : a.ranges;
     if (lane == 0) {
-        for (int s = 0; s < STAGES; ++s) mbar_init(&bars[warp][s], 1);
+        for (int s = 0; s < a.stages; ++s) mbar_init(&bars[warp][s], 1);
         fence_mbar_init();
     }
     __syncwarp();
-    const int n_items = *a.tab.n_groups() * a.ntr * a.nch;
-    unsigned phase[STAGES] = {0u, 0u};
-    bool pending[STAGES] = {false, false};
-    // prologue: the first two items
-    for (int s = 0; s < STAGES; ++s) {
-        const int it = gw + s * nw;
-        if (it < n_items) {
-            issue_item(a, it, my + s * a.stage_bytes, &bars[warp][s], lane);
-            pending[s] = true;
-        }
-    }
-    int stage = 0;
-    for (int it = gw; it < n_items; it += nw) {
-        uint8_t *st = my + stage * a.stage_bytes;
-        const bool ok = mbar_wait(&bars[warp][stage], phase[stage], a.status);
-        phase[stage] ^= 1u;
-        pending[stage] = false;
-        if (!ok) break;  // status raised; the host reports it
-        int g, tr, ch;
-        item_of(a, it, g, tr, ch);
-        const int ntok = a.tab.grp_ntok()[g], col0 = a.tab.grp_col0()[g];
-        const int k0 = ch * a.kc, kn = min(a.kc, a.nkt - k0);
-        const uint32_t *bsm = reinterpret_cast<const uint32_t *>(st + a.kc * a.mats * a.tile_bytes);
-        float acc0[4] = {0.f, 0.f, 0.f, 0.f}, acc1[4] = {0.f, 0.f, 0.f, 0.f};
-        for (int kt = 0; kt < kn; ++kt) {
-            uint32_t bfr[2][2][2];
-            load_b(bsm, 2 * a.kc, kt, lane, ntok, bfr);
-            const uint8_t *tile = st + (size_t)kt * a.mats * a.tile_bytes;
-            tile_mma<WT>(tile, lane, bfr, acc0);
-            if (a.mats == 2) tile_mma<WT>(tile + a.tile_bytes, lane, bfr, acc1);
-        }
-        __syncwarp();
-        // the stage is free: start the item after next into it
-        const int nxt = it + STAGES * nw;
-        if (nxt < n_items) {
-            issue_item(a, nxt, st, &bars[warp][stage], lane);
-            pending[stage] = true;
-        }
-        stage = (stage + 1) % STAGES;
 
-        // partial: lane (r, q) holds column pair (2q, 2q+1) = (f16 part, residual part) of
-        // group member q, rows r and r+8.
-        const int r = lane >> 2, q = lane & 3;
-        const int row0 = tr * 16 + r;
-        const int ncol = *a.tab.n_cols();
-        if (q < ntok) {
-            const int col = col0 + q;
-            if (a.mats == 2) {
-                float *p = a.part + (((size_t)ch * ncol + col) * a.I) * 2;
-                p[(size_t)row0 * 2] = acc0[0] + acc0[1];
-                p[(size_t)row0 * 2 + 1] = acc1[0] + acc1[1];
-                p[(size_t)(row0 + 8) * 2] = acc0[2] + acc0[3];
-                p[(size_t)(row0 + 8) * 2 + 1] = acc1[2] + acc1[3];
-            } else {
-                float *p = a.part + ((size_t)ch * ncol + col) * a.H;
-                p[row0] = acc0[0] + acc0[1];
-                p[row0 + 8] = acc0[2] + acc0[3];
+    auto valid = [&](const item_pos &p) { return p.u < n_units; };
+    auto advance = [&](item_pos &p) {
+        p.i += nwarps;
+        while (p.u < n_units && p.i >= items_per_unit) {
+            p.u += gridDim.x;
+            p.i = warp;
+        }
+    };
+    auto first = [&]() {
+        item_pos p{(int)blockIdx.x, warp};
+        if (p.i >= items_per_unit) p.u = n_units;  // this warp has no item in any unit
+        return p;
+    };
+    // (unit, item) -> group, tile-row, K run
+    auto decode = [&](const item_pos &p, int &g, int &tr, int &rg) {
+        if (down) {
+            tr = p.u;
+            g = p.i / a.ranges;
+            rg = p.i % a.ranges;
+        } else {
+            g = p.u / a.ntr;
+            tr = p.u % a.ntr;
+            rg = p.i;
+        }
+    };
+    auto issue = [&](const item_pos &p, int stage, bool weights, bool acts) {
+        if (lane != 0) return;
+        int g, tr, rg;
+        decode(p, g, tr, rg);
+        const int slot = tb.grp_slot()[g];
+        const int expert = tb.slot_expert()[slot];
+        const int col0 = tb.grp_col0()[g], ntok = tb.grp_ntok()[g];
+        const int k0 = range_lo(rg, a.nkt, a.ranges), kn = range_lo(rg + 1, a.nkt, a.ranges) - k0;
+        const unsigned wbytes = (unsigned)(kn * a.mats * a.tile_bytes);
+        const unsigned bbytes = (unsigned)(2 * kn * 128);
+        uint8_t *st = ring + (size_t)stage * a.stage_bytes;
+        uint64_t *bar = &bars[warp][stage];
+        if (weights) {
+            fence_proxy_async();
+            mbar_expect_tx(bar, wbytes + bbytes * ntok);
+            bulk_g2s(st, a.bank + (size_t)expert * a.bank_stride + ((size_t)tr * a.nkt + k0) * a.mats * a.tile_bytes,
+                     wbytes, bar);
+        }
+        if (acts) {
+            uint8_t *bs = st + (size_t)a.tpr * a.mats * a.tile_bytes;
+            for (int t = 0; t < ntok; ++t) {
+                const int col = col0 + t;
+                const int row = a.b_by_column ? col : tb.col_tok()[col];
+                bulk_g2s(bs + (size_t)t * a.tpr * 2 * 128, a.bsrc + ((size_t)row * a.nblk_b + 2 * k0) * 32, bbytes, bar);
             }
         }
-        __threadfence();
-        __syncwarp();
-        // the unit: (group, tile-row) for gate-up, tile-row for down
-        unsigned prev = 0;
-        const int unit = (a.mats == 2) ? g * a.ntr + tr : tr;
-        const unsigned target = (a.mats == 2) ? (unsigned)a.nch : (unsigned)(*a.tab.n_groups() * a.nch);
-        if (lane == 0) prev = atomicAdd(a.ctr + unit, 1u);
-        prev = __shfl_sync(0xffffffffu, prev, 0);
-        if (prev != target - 1) continue;
-        __threadfence();
-        if (lane == 0) a.ctr[unit] = 0;  // ready for the next call
-        if (a.mats == 2) {
-            // gate-up unit complete: reduce the chunks in order, apply the activation, write
-            // the activation both as f32 and as the down GEMV's B fragments.
-            const int nblk_i = a.I / 32;
-            for (int e = lane; e < ntok * 16; e += 32) {
-                const int t = e / 16, rr = e % 16;
-                const int col = col0 + t, row = tr * 16 + rr;
-                float gsum = 0.f, usum = 0.f;
-                for (int c = 0; c < a.nch; ++c) {
-                    const float *p = a.part + (((size_t)c * ncol + col) * a.I + row) * 2;
-                    gsum += __ldcg(p);
-                    usum += __ldcg(p + 1);
+    };
+
+    // prologue: the first `stages` items of this warp (down: weights now, fragments after the wait)
+    item_pos iss = first();
+    const item_pos start = iss;
+    int issued = 0, n_issued = 0;
+    for (int s = 0; s < a.stages && valid(iss); ++s) {
+        issue(iss, s, true, !down);
+        advance(iss);
+        ++issued;
+        ++n_issued;
+    }
+    TRACE(1);
+    if (down) {
+        pdl_trigger();
+        pdl_wait();
+        TRACE(2);
+        item_pos p = start;
+        for (int s = 0; s < issued; ++s) {
+            issue(p, s, false, true);
+            advance(p);
+        }
+    }
+
+    // Item j of this warp's sequence lives in stage j % stages and completes that stage's
+    // barrier phase number j / stages, parity (j / stages) & 1.
+    int k = 0;        // items this warp has consumed
+    int kf = -1;      // the first item whose wait gave up (-1: none)
+    bool failed = false;
+    const int r = lane >> 2, q = lane & 3;
+    int un = 0;
+    for (int u = blockIdx.x; u < n_units; u += gridDim.x, ++un) {
+        if (un < 12) TRACE(4 + 2 * un);
+        for (int i = warp; i < items_per_unit; i += nwarps) {
+            const int stage = k % a.stages;
+            if (!failed && !mbar_wait(&bars[warp][stage], (unsigned)(k / a.stages) & 1u, a.status)) {
+                failed = true;
+                kf = k;
+            }
+            ++k;
+            int g, tr, rg;
+            decode(item_pos{u, i}, g, tr, rg);
+            const int ntok = tb.grp_ntok()[g];
+            const int kn = range_lo(rg + 1, a.nkt, a.ranges) - range_lo(rg, a.nkt, a.ranges);
+            const uint8_t *st = ring + (size_t)stage * a.stage_bytes;
+            const uint32_t *bsm = reinterpret_cast<const uint32_t *>(st + (size_t)a.tpr * a.mats * a.tile_bytes);
+            float acc0[4] = {0.f, 0.f, 0.f, 0.f}, acc1[4] = {0.f, 0.f, 0.f, 0.f};
+            if (!failed) {
+                for (int kt = 0; kt < kn; ++kt) {
+                    uint32_t bfr[2][2][2];
+                    load_b(bsm, 2 * a.tpr, kt, lane, ntok, bfr);
+                    const uint8_t *tile = st + (size_t)kt * a.mats * a.tile_bytes;
+                    tile_mma<WT>(tile, lane, bfr, acc0);
+                    if (a.mats == 2) tile_mma<WT>(tile + a.tile_bytes, lane, bfr, acc1);
                 }
-                const float v = act_fn(a.act, gsum, usum, a.alpha, a.limit);
-                if (a.act_out) a.act_out[(size_t)col * a.I + row] = v;
+            }
+            __syncwarp();
+            if (valid(iss) && !failed) {
+                issue(iss, stage, true, true);
+                advance(iss);
+                ++n_issued;
+            }
+            // lane (r, q) holds column pair (2q, 2q+1) = (f16 part, residual part) of group
+            // member q for rows r and r+8
+            if (q < ntok) {
+                if (down) {
+                    float *p = part + (size_t)i * 16 * GROUP;
+                    p[r * GROUP + q] = acc0[0] + acc0[1];
+                    p[(r + 8) * GROUP + q] = acc0[2] + acc0[3];
+                } else {
+                    float *pg = part + ((size_t)rg * 2 + 0) * 16 * GROUP;
+                    float *pu = part + ((size_t)rg * 2 + 1) * 16 * GROUP;
+                    pg[r * GROUP + q] = acc0[0] + acc0[1];
+                    pg[(r + 8) * GROUP + q] = acc0[2] + acc0[3];
+                    pu[r * GROUP + q] = acc1[0] + acc1[1];
+                    pu[(r + 8) * GROUP + q] = acc1[2] + acc1[3];
+                }
+            }
+        }
+        __syncthreads();
+        if (un < 12) TRACE(5 + 2 * un);
+        if (!down) {
+            // gate-up unit: sum the K runs in order, apply the activation, write the f32
+            // activation and the down kernel's B fragments (f16 rounding + residual halves)
+            const int g = u / a.ntr, tr = u % a.ntr;
+            const int ntok = tb.grp_ntok()[g], col0 = tb.grp_col0()[g];
+            const int nblk_i = a.I / 32;
+            for (int e = threadIdx.x; e < ntok * 16; e += blockDim.x) {
+                const int t = e / 16, rr = e % 16;
+                float gs = 0.f, us = 0.f;
+                for (int rg = 0; rg < a.ranges; ++rg) {
+                    gs += part[((size_t)rg * 2 + 0) * 16 * GROUP + rr * GROUP + t];
+                    us += part[((size_t)rg * 2 + 1) * 16 * GROUP + rr * GROUP + t];
+                }
+                const int col = col0 + t, row = tr * 16 + rr;
+                const float v = act_fn(a.act, gs, us, a.alpha, a.limit);
+                a.act_out[(size_t)col * a.I + row] = v;
                 const __half hh = __float2half_rn(v);
                 const __half hl = __float2half_rn(v - __half2float(hh));
-                // element el of block blk sits in pair j = el & 3 of lane q = (el & 15) >> 2,
-                // in the low half for el < 16 and the high half for el >= 16
+                // element el of block blk sits in pair j = el & 3 of lane q = (el & 15) >> 2, in
+                // the low half for el < 16 and the high half for el >= 16
                 const int blk = row / 32, el = row % 32;
                 const int qq = (el & 15) >> 2, jj = el & 3, half = el >> 4;
                 const size_t ihi = ((((size_t)col * nblk_i + blk) * 2 + 0) * 4 + qq) * 4 + jj;
@@ -590,47 +727,41 @@ __global__ void __launch_bounds__(WARPS * 32) k_expert_gemv(gemv_args a) {
                 reinterpret_cast<uint16_t *>(a.actfrag + ilo)[half] = __half_as_ushort(hl);
             }
         } else {
-            // down tile-row complete: out[t][row] = residual + sum_m w[t][m] * o_(t,m)[row],
-            // m ascending (router order), each o the chunks summed in order.
-            for (int e = lane; e < a.T * 16; e += 32) {
-                const int t = e / 16, row = tr * 16 + e % 16;
-                float acc = 0.f;
-                for (int m = 0; m < a.K; ++m) {
-                    const int col = a.tab.col_of()[t * a.K + m];
-                    float o = 0.f;
-                    for (int c = 0; c < a.nch; ++c) o += __ldcg(a.part + ((size_t)c * ncol + col) * a.H + row);
-                    acc = fmaf(a.wts[t * a.K + m], o, acc);
-                }
-                a.out[(size_t)t * a.H + row] = a.residual ? a.residual[(size_t)t * a.H + row] + acc : acc;
+            // down unit: each column's output = its K runs in order; then per token the
+            // router-weighted sum over its k experts in router order, plus the residual
+            const int tr = u;
+            for (int e = threadIdx.x; e < G * 16 * GROUP; e += blockDim.x) {
+                const int g = e / (16 * GROUP), rr = (e / GROUP) % 16, t = e % GROUP;
+                if (t >= tb.grp_ntok()[g]) continue;
+                float o = 0.f;
+                for (int rg = 0; rg < a.ranges; ++rg) o += part[((size_t)g * a.ranges + rg) * 16 * GROUP + rr * GROUP + t];
+                osum[(size_t)(tb.grp_col0()[g] + t) * 16 + rr] = o;
             }
+            __syncthreads();
+            for (int e = threadIdx.x; e < a.T * 16; e += blockDim.x) {
+                const int t = e / 16, rr = e % 16;
+                float acc = 0.f;
+                for (int m = 0; m < a.K; ++m)
+                    acc = fmaf(a.wts[t * a.K + m], osum[(size_t)tb.col_of()[t * a.K + m] * 16 + rr], acc);
+                const size_t o = (size_t)t * a.H + tr * 16 + rr;
+                a.out[o] = a.residual ? a.residual[o] + acc : acc;
+            }
+            (void)ncol;
         }
+        __syncthreads();
     }
-    // no bulk copy may still be landing in this warp's shared memory when the CTA exits
-    for (int s = 0; s < STAGES; ++s)
-        if (pending[s]) mbar_wait(&bars[warp][s], phase[s], a.status);
-}
-
-// Choose the chunk length (k-tiles per item) that best balances `units` rows of `nkt` k-tiles
-// over `nw` warps: the makespan in k-tiles plus a fixed per-item cost, minimised.
-int pick_kc(long units, int nkt, long nw, int kc_max) {
-    int best = 1;
-    double best_cost = 1e30;
-    for (int kc = 1; kc <= std::min(kc_max, nkt); ++kc) {
-        const long nch = (nkt + kc - 1) / kc;
-        const long items = units * nch;
-        const long per_warp = (items + nw - 1) / nw;
-        const double cost = (double)per_warp * (kc + 1.5);
-        if (cost < best_cost - 1e-9) {
-            best_cost = cost;
-            best = kc;
-        }
-    }
-    return best;
+    // no bulk copy may still be landing in this warp's ring when the CTA exits: wait (bounded)
+    // for any that were issued and not consumed (only after a failed wait)
+    if (failed)
+        for (int j = kf; j < n_issued; ++j) mbar_wait(&bars[warp][j % a.stages], (unsigned)(j / a.stages) & 1u, a.status);
+    TRACE(31);
 }
 
 }  // namespace
 
 // ---- host side ----------------------------------------------------------------------------
+
+TRACE_SETTER(moe)
 
 namespace {
 
@@ -681,21 +812,40 @@ moearc_x_moe *moearc_x_moe_create(moearc_ctx *c, const moearc_x_moe_desc *d) {
     m->ntr_i = m->I / 16;
     const int TK = m->T_max * m->K;
     const int tok_group = std::min(GROUP, m->T_max);
-    // Balance the chunking for the expected number of column groups (k at batch 1).
+    const size_t n_tab = tab_view::ints(TK, std::min(TK, m->E), TK, TK);
+    const int tab_bytes = (int)((n_tab * 4 + 127) / 128 * 128);
+    auto round128 = [](long b) { return (int)((b + 127) & ~127L); };
+    // gate-up: 8 warps, one K run each; down: 4 warps, 4 K runs per column group
+    m->warps_gu = 8;
+    m->ranges_gu = 8;
+    m->tpr_gu = (m->nkt_h + m->ranges_gu - 1) / m->ranges_gu;
+    m->stage_gu = round128((long)m->tpr_gu * 2 * m->tile_bytes + (long)tok_group * 2 * m->tpr_gu * 128);
+    const int part_gu = round128((long)m->ranges_gu * 2 * 16 * GROUP * 4);
+    m->warps_dn = 4;
+    m->ranges_dn = 4;
+    m->tpr_dn = (m->nkt_i + m->ranges_dn - 1) / m->ranges_dn;
+    m->stage_dn = round128((long)m->tpr_dn * m->tile_bytes + (long)tok_group * 2 * m->tpr_dn * 128);
+    const int part_dn = round128(((long)TK * m->ranges_dn * 16 * GROUP + (long)TK * 16) * 4);
+    const int budget = 220 * 1024;
+    m->stages_gu = std::max(1, std::min(3, (budget - tab_bytes - part_gu) / (m->warps_gu * m->stage_gu)));
+    m->stages_dn = std::max(1, std::min(3, (budget - tab_bytes - part_dn) / (m->warps_dn * m->stage_dn)));
+    m->smem_gu = tab_bytes + part_gu + m->warps_gu * m->stages_gu * m->stage_gu;
+    m->smem_dn = tab_bytes + part_dn + m->warps_dn * m->stages_dn * m->stage_dn;
+    // grids: as many CTAs as fit, then shrunk so every CTA gets the same number of units
     const long groups = std::min<long>(TK, std::max<long>(m->K, std::min(m->E, TK)));
-    const long nw = (long)c->sm_count * 2 * WARPS;
-    m->kc_gu = pick_kc(groups * m->ntr_i, m->nkt_h, nw, 8);
-    m->kc_dn = pick_kc(groups * m->ntr_h, m->nkt_i, nw, 16);
-    m->nch_gu = (m->nkt_h + m->kc_gu - 1) / m->kc_gu;
-    m->nch_dn = (m->nkt_i + m->kc_dn - 1) / m->kc_dn;
-    auto round128 = [](int b) { return (b + 127) & ~127; };
-    m->stage_gu = round128(m->kc_gu * 2 * m->tile_bytes + tok_group * 2 * m->kc_gu * 128);
-    m->stage_dn = round128(m->kc_dn * 1 * m->tile_bytes + tok_group * 2 * m->kc_dn * 128);
-    m->grid_gu = occupancy_grid(c, WARPS * STAGES * m->stage_gu);
-    m->grid_dn = occupancy_grid(c, WARPS * STAGES * m->stage_dn);
+    auto balanced = [&](long units, int smem) {
+        const long cap = occupancy_grid(c, smem);
+        const long rounds = (units + cap - 1) / cap;
+        return (int)std::max<long>(1, (units + rounds - 1) / rounds);
+    };
+    m->grid_gu = balanced(groups * m->ntr_i, m->smem_gu);
+    m->grid_dn = balanced(m->ntr_h, m->smem_dn);
+    if (m->smem_gu > 226 * 1024 || m->smem_dn > 226 * 1024 || m->stages_gu < 1 || m->stages_dn < 1) {
+        delete m;
+        return nullptr;
+    }
 
     // one scratch allocation
-    const size_t n_tab = tab_view::ints(TK, std::min(TK, m->E), TK, TK);
     size_t off = 0;
     auto take = [&](size_t bytes) {
         const size_t o = off;
@@ -709,8 +859,6 @@ moearc_x_moe *moearc_x_moe_create(moearc_ctx *c, const moearc_x_moe_desc *d) {
     const size_t o_xf = take((size_t)m->T_max * (m->H / 32) * 128);
     const size_t o_af = take((size_t)TK * (m->I / 32) * 128);
     const size_t o_act = take(sizeof(float) * (size_t)TK * m->I);
-    const size_t o_pgu = take(sizeof(float) * (size_t)m->nch_gu * TK * m->I * 2);
-    const size_t o_pdn = take(sizeof(float) * (size_t)m->nch_dn * TK * m->H);
     const size_t n_ctr = 1 + (size_t)TK * m->ntr_i + m->ntr_h;
     const size_t o_ctr = take(sizeof(unsigned) * n_ctr);
     const size_t o_st = take(sizeof(int));
@@ -727,15 +875,14 @@ moearc_x_moe *moearc_x_moe_create(moearc_ctx *c, const moearc_x_moe_desc *d) {
     m->tables = reinterpret_cast<int *>(b + o_tab);
     m->xfrag = reinterpret_cast<uint32_t *>(b + o_xf);
     m->actfrag = reinterpret_cast<uint32_t *>(b + o_af);
-    m->part_gu = reinterpret_cast<float *>(b + o_pgu);
-    m->part_dn = reinterpret_cast<float *>(b + o_pdn);
     m->ctr = reinterpret_cast<unsigned *>(b + o_ctr);
     m->status = reinterpret_cast<int *>(b + o_st);
     m->act_f32 = reinterpret_cast<float *>(b + o_act);
     cudaMemsetAsync(m->mem, 0, off, c->stream);
-    const int smem_max = WARPS * STAGES * std::max(m->stage_gu, m->stage_dn);
-    if (cudaFuncSetAttribute(k_expert_gemv<39>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_max) != cudaSuccess ||
-        cudaFuncSetAttribute(k_expert_gemv<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_max) != cudaSuccess ||
+    // per-kernel attribute shared by every layer object: the most any of them may use
+    const int smem_attr = 226 * 1024;
+    if (cudaFuncSetAttribute(k_moe_rows<39>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_attr) != cudaSuccess ||
+        cudaFuncSetAttribute(k_moe_rows<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_attr) != cudaSuccess ||
         cudaStreamSynchronize(c->stream) != cudaSuccess) {
         cudaGetLastError();
         cudaFree(m->mem);
@@ -776,12 +923,27 @@ int moearc_x_moe_pack(moearc_x_moe *m, const void *gate, const void *up, const v
     return ls.finish();
 }
 
-int moearc_x_moe_forward(moearc_x_moe *m, const float *x, unsigned n_tokens, const float *router_w,
-                         const float *router_b, const void *gateup_packed, const void *down_packed,
-                         const float *residual, float *out) {
+}  // extern "C"
+
+namespace moearc {
+
+// The forward pass; norm_w (may be null) routes rmsnorm(x) * norm_w instead of x.
+int moe_forward_impl(moearc_x_moe *m, const float *x, unsigned n_tokens, const float *norm_w, float eps,
+                     const float *router_w, const float *router_b, const void *gateup_packed,
+                     const void *down_packed, const float *residual, float *out,
+                     std::vector<cudaEvent_t> *marks, std::vector<int> *kinds) {
+    auto mark = [&](int k) {
+        if (!marks) return;
+        cudaEvent_t e;
+        cudaEventCreate(&e);
+        cudaEventRecord(e, m->ctx->stream);
+        marks->push_back(e);
+        kinds->push_back(k);
+    };
     if (!m || !x || !router_w || !gateup_packed || !down_packed || !out) return ERR;
     if (n_tokens == 0) return OK;
     if ((int)n_tokens > m->T_max) return ERR_ARG;
+    if (norm_w && n_tokens > (unsigned)ROUTE_NORM_TOKENS) return ERR_ARG;
     if ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(router_w) |
          reinterpret_cast<uintptr_t>(gateup_packed) | reinterpret_cast<uintptr_t>(down_packed)) & 15)
         return ERR_ARG;
@@ -790,22 +952,25 @@ int moearc_x_moe_forward(moearc_x_moe *m, const float *x, unsigned n_tokens, con
     const tab_view tab = make_tab(m);
     launch_scope ls(c, "moe_forward", (unsigned long)m->H, (unsigned)T);
 
-    route_args ra{x, router_w, router_b, T, m->H, m->E, m->K, m->gating, m->logits, m->idx, m->wts,
-                  m->xfrag, tab, m->ctr};
-    const int rows_ctas = (T * m->E + 7) / 8;
-    const int conv_ctas = (T * (m->H / 32) * 16 + 255) / 256;
-    const int grid_r = std::max(1, std::min(std::max(rows_ctas, conv_ctas), c->sm_count * 2));
-    k_route<<<grid_r, 256, 0, c->stream>>>(ra);
+    route_args ra{x, norm_w, eps, router_w, router_b, T, m->H, m->E, m->K, m->gating, m->logits, m->idx,
+                  m->wts, m->xfrag, tab, m->ctr};
+    // one router row per warp, one pass of the fragment conversion
+    const int rows_ctas = (T * m->E + ROUTE_WARPS - 1) / ROUTE_WARPS;
+    const int conv_ctas = (T * (m->H / 32) * 16 + ROUTE_WARPS * 32 - 1) / (ROUTE_WARPS * 32);
+    const int grid_r = std::max(1, std::min(std::max(rows_ctas, conv_ctas), c->sm_count * 4));
+    if (launch_pdl(k_route, dim3(grid_r), dim3(ROUTE_WARPS * 32), 0, c->stream, ra) != cudaSuccess) return ERR;
+    mark(3);
 
-    gemv_args ga{};
+    rows_args ga{};
     ga.bank = static_cast<const uint8_t *>(gateup_packed);
     ga.bank_stride = (size_t)2 * m->ntr_i * m->nkt_h * m->tile_bytes;
     ga.mats = 2;
     ga.ntr = m->ntr_i;
     ga.nkt = m->nkt_h;
-    ga.kc = m->kc_gu;
-    ga.nch = m->nch_gu;
+    ga.ranges = m->ranges_gu;
+    ga.tpr = m->tpr_gu;
     ga.tile_bytes = m->tile_bytes;
+    ga.stages = m->stages_gu;
     ga.stage_bytes = m->stage_gu;
     ga.bsrc = m->xfrag;
     ga.b_by_column = 0;
@@ -820,21 +985,21 @@ int moearc_x_moe_forward(moearc_x_moe *m, const float *x, unsigned n_tokens, con
     ga.T = T;
     ga.K = m->K;
     ga.H = m->H;
-    ga.part = m->part_gu;
-    ga.ctr = m->ctr + 1;
     ga.status = m->status;
-    const size_t smem_gu = (size_t)WARPS * STAGES * m->stage_gu;
-    if (m->wtype == T_MXFP4) k_expert_gemv<39><<<m->grid_gu, WARPS * 32, smem_gu, c->stream>>>(ga);
-    else k_expert_gemv<2><<<m->grid_gu, WARPS * 32, smem_gu, c->stream>>>(ga);
+    if (launch_pdl(m->wtype == T_MXFP4 ? k_moe_rows<39> : k_moe_rows<2>, dim3(m->grid_gu), dim3(m->warps_gu * 32),
+                   (size_t)m->smem_gu, c->stream, ga) != cudaSuccess)
+        return ERR;
+    mark(4);
 
-    gemv_args da = ga;
+    rows_args da = ga;
     da.bank = static_cast<const uint8_t *>(down_packed);
     da.bank_stride = (size_t)m->ntr_h * m->nkt_i * m->tile_bytes;
     da.mats = 1;
     da.ntr = m->ntr_h;
     da.nkt = m->nkt_i;
-    da.kc = m->kc_dn;
-    da.nch = m->nch_dn;
+    da.ranges = m->ranges_dn;
+    da.tpr = m->tpr_dn;
+    da.stages = m->stages_dn;
     da.stage_bytes = m->stage_dn;
     da.bsrc = m->actfrag;
     da.b_by_column = 1;
@@ -842,12 +1007,22 @@ int moearc_x_moe_forward(moearc_x_moe *m, const float *x, unsigned n_tokens, con
     da.wts = m->wts;
     da.residual = residual;
     da.out = out;
-    da.part = m->part_dn;
-    da.ctr = m->ctr + 1 + (size_t)m->T_max * m->K * m->ntr_i;
-    const size_t smem_dn = (size_t)WARPS * STAGES * m->stage_dn;
-    if (m->wtype == T_MXFP4) k_expert_gemv<39><<<m->grid_dn, WARPS * 32, smem_dn, c->stream>>>(da);
-    else k_expert_gemv<2><<<m->grid_dn, WARPS * 32, smem_dn, c->stream>>>(da);
+    if (launch_pdl(m->wtype == T_MXFP4 ? k_moe_rows<39> : k_moe_rows<2>, dim3(m->grid_dn), dim3(m->warps_dn * 32),
+                   (size_t)m->smem_dn, c->stream, da) != cudaSuccess)
+        return ERR;
+    mark(5);
     return ls.finish();
+}
+
+}  // namespace moearc
+
+extern "C" {
+
+int moearc_x_moe_forward(moearc_x_moe *m, const float *x, unsigned n_tokens, const float *router_w,
+                         const float *router_b, const void *gateup_packed, const void *down_packed,
+                         const float *residual, float *out) {
+    return moe_forward_impl(m, x, n_tokens, nullptr, 0.f, router_w, router_b, gateup_packed, down_packed,
+                            residual, out, nullptr, nullptr);
 }
 
 void *moearc_x_moe_buffer(moearc_x_moe *m, int which) {

@@ -46,6 +46,11 @@ __device__ __forceinline__ void bulk_g2s(void *dst, const void *src, unsigned by
         : "memory");
 }
 
+// Hint the L2 to fetch [src, src + bytes) (16-byte aligned, a multiple of 16).
+__device__ __forceinline__ void bulk_prefetch_l2(const void *src, unsigned bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;\n" ::"l"(src), "r"(bytes) : "memory");
+}
+
 __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, unsigned parity) {
     unsigned ok;
     asm volatile(

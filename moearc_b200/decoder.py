@@ -1,0 +1,179 @@
+"""The synthetic decoder (include/moearc.h, moearc_x_decoder_*), host side.
+
+``Decoder`` builds a gpt-oss- or Qwen3-MoE-shaped model with seeded random weights on the
+device and decodes one token per ``step()``: the per-block sequence of
+crates/moearc-engine/src/moe.rs:1862-2443 (Model::decode), captured once as a CUDA graph.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import math
+from dataclasses import dataclass, fields
+
+import numpy as np
+
+from . import _lib
+from .kernels import BadArgument, Context, Failed
+
+MXFP4, Q4_0 = 39, 2
+
+
+@dataclass
+class DecoderConfig:
+    n_layer: int
+    n_embd: int
+    n_head: int
+    n_head_kv: int
+    head_dim: int
+    n_expert: int
+    n_expert_used: int
+    n_ff: int
+    expert_type: int = MXFP4
+    gating: int = 2
+    act: int = 1
+    alpha: float = 1.702
+    limit: float = 7.0
+    n_swa: int = 128
+    swa_pattern: int = 2
+    rope_base: float = 150000.0
+    rope_freq_scale: float = 1.0
+    rope_ext_factor: float = 0.0
+    rope_attn_factor: float = 1.0
+    rope_corr_lo: float = 0.0
+    rope_corr_hi: float = 0.0
+    rms_eps: float = 1e-5
+    has_sinks: int = 1
+    n_ctx: int = 4096
+    seed: int = 0x5EED
+
+    def yarn(self, factor: float, n_ctx_orig: int, beta_fast: float = 32.0, beta_slow: float = 1.0):
+        """YaRN parameters the way reference.rs:572-591 derives them (RopeScaling::yarn)."""
+        n_dims = self.head_dim
+
+        def corr(beta):
+            return n_dims * math.log(n_ctx_orig / (beta * 2 * math.pi)) / (2 * math.log(self.rope_base))
+
+        self.rope_freq_scale = 1.0 / factor
+        self.rope_ext_factor = 1.0
+        self.rope_attn_factor = 1.0
+        self.rope_corr_lo = max(0.0, math.floor(corr(beta_fast)))
+        self.rope_corr_hi = min(n_dims - 1.0, math.ceil(corr(beta_slow)))
+        return self
+
+    def to_c(self) -> _lib.DecoderCfg:
+        return _lib.DecoderCfg(*[getattr(self, f.name) for f in fields(self)])
+
+    # ---- the BASELINE configurations ---------------------------------------------------------
+    @staticmethod
+    def gpt_oss_20b(**kw) -> "DecoderConfig":
+        """24 layers, hidden 2880, 64 q / 8 kv heads of 64, 32 experts top-4, I 2880."""
+        c = DecoderConfig(24, 2880, 64, 8, 64, 32, 4, 2880, **kw)
+        return c.yarn(32.0, 4096)
+
+    @staticmethod
+    def gpt_oss_120b(**kw) -> "DecoderConfig":
+        """as configs[1] with 36 layers and 128 experts."""
+        c = DecoderConfig(36, 2880, 64, 8, 64, 128, 4, 2880, **kw)
+        return c.yarn(32.0, 4096)
+
+    @staticmethod
+    def qwen3_moe(**kw) -> "DecoderConfig":
+        """48 layers, hidden 2048, 32 q / 4 kv heads of 128, 128 experts top-8,
+        I 768, Q4_0 experts, renormalised softmax gating, SwiGLU, no window, no sinks."""
+        kw.setdefault("expert_type", Q4_0)
+        kw.setdefault("gating", 1)
+        kw.setdefault("act", 0)
+        kw.setdefault("n_swa", 0)
+        kw.setdefault("has_sinks", 0)
+        kw.setdefault("rope_base", 1000000.0)
+        kw.setdefault("rms_eps", 1e-6)
+        return DecoderConfig(48, 2048, 32, 4, 128, 128, 8, 768, **kw)
+
+
+class Decoder:
+    def __init__(self, ctx: Context, cfg: DecoderConfig):
+        self.ctx, self.cfg = ctx, cfg
+        self._c = cfg.to_c()
+        self.h = ctx.lib.moearc_x_decoder_create(ctx.raw, C.byref(self._c))
+        if not self.h:
+            raise BadArgument("moearc_x_decoder_create refused the configuration or ran out of memory")
+        self.in_ptr = ctx.lib.moearc_x_decoder_input(self.h)
+        self.out_ptr = ctx.lib.moearc_x_decoder_output(self.h)
+
+    def close(self) -> None:
+        if self.h:
+            self.ctx.lib.moearc_x_decoder_destroy(self.h)
+            self.h = None
+
+    @property
+    def pos(self) -> int:
+        return self.ctx.lib.moearc_x_decoder_pos(self.h)
+
+    def fill_kv(self, depth: int, seed: int = 0xC0DE) -> None:
+        self.ctx._finish(self.ctx.lib.moearc_x_decoder_fill_kv(self.h, depth, seed), "fill_kv")
+
+    def set_pos(self, pos: int) -> None:
+        self.ctx._finish(self.ctx.lib.moearc_x_decoder_set_pos(self.h, pos), "set_pos")
+
+    def use_graph(self, on: bool) -> None:
+        self.ctx._finish(self.ctx.lib.moearc_x_decoder_use_graph(self.h, 1 if on else 0), "use_graph")
+
+    def step(self) -> None:
+        """Enqueue one decode step (the caller synchronises when it needs the output)."""
+        self.ctx._finish(self.ctx.lib.moearc_x_decoder_step(self.h), "decoder step")
+
+    def set_input(self, x: np.ndarray) -> None:
+        x = np.ascontiguousarray(x, np.float32)
+        assert x.size == self.cfg.n_embd
+        self.ctx._finish(self.ctx.lib.moearc_copy_h2d(self.ctx.raw, self.in_ptr, x.ctypes.data, x.nbytes), "input")
+
+    def output(self) -> np.ndarray:
+        out = np.empty(self.cfg.n_embd, np.float32)
+        self.ctx._finish(self.ctx.lib.moearc_copy_d2h(self.ctx.raw, out.ctypes.data, self.out_ptr, out.nbytes), "output")
+        return out
+
+    def tensor(self, which: int, layer: int, dtype) -> np.ndarray:
+        n = C.c_ulong()
+        p = self.ctx.lib.moearc_x_decoder_tensor(self.h, which, layer, C.byref(n))
+        if not p and n.value:
+            raise Failed("no such tensor")
+        out = np.empty(n.value // np.dtype(dtype).itemsize, dtype)
+        if n.value:
+            self.ctx._finish(self.ctx.lib.moearc_copy_d2h(self.ctx.raw, out.ctypes.data, p, n.value), "tensor")
+        return out
+
+    def seed(self, kind: int, layer: int) -> int:
+        return self.ctx.lib.moearc_x_decoder_seed(self.h, kind, layer, self.cfg.seed)
+
+
+def unpack_dense(packed: np.ndarray, n_rows: int, n_cols: int) -> np.ndarray:
+    """Invert the packed bf16 tile layout (dense.cuh) back to a row-major [n_rows][n_cols] bf16
+    matrix: tile (tr, tk) = 16 rows x 64 cols; lane l = 4r + q; for each 16-column sub-block s
+    four u32: (row r, cols 16s+2q..+1), (row r+8, same), (row r, 16s+2q+8..+9), (row r+8, same)."""
+    ntr, nkt = n_rows // 16, n_cols // 64
+    p = packed.view(np.uint16).reshape(ntr, nkt, 8, 4, 4, 4, 2)  # tr, tk, r, q, s, reg, half
+    w = np.empty((ntr, 16, nkt, 64), np.uint16)
+    offs = ((0, 0), (8, 0), (0, 8), (8, 8))  # (row, col) offset of register reg
+    for r in range(8):
+        for q in range(4):
+            for s in range(4):
+                for reg, (ro, co) in enumerate(offs):
+                    for half in range(2):
+                        w[:, r + ro, :, 16 * s + 2 * q + co + half] = p[:, :, r, q, s, reg, half]
+    return w.reshape(n_rows, n_cols)
+
+
+def pack_dense(w: np.ndarray) -> np.ndarray:
+    """The packed bf16 tile layout, built on the host (the inverse of unpack_dense)."""
+    n_rows, n_cols = w.shape
+    ntr, nkt = n_rows // 16, n_cols // 64
+    v = w.reshape(ntr, 16, nkt, 64)
+    p = np.empty((ntr, nkt, 8, 4, 4, 4, 2), np.uint16)
+    offs = ((0, 0), (8, 0), (0, 8), (8, 8))
+    for r in range(8):
+        for q in range(4):
+            for s in range(4):
+                for reg, (ro, co) in enumerate(offs):
+                    for half in range(2):
+                        p[:, :, r, q, s, reg, half] = v[:, r + ro, :, 16 * s + 2 * q + co + half]
+    return p.ravel()

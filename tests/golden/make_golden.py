@@ -108,7 +108,9 @@ def extract(ref_root: str) -> dict:
 
 
 def main() -> None:
-    ref = sys.argv[1] if len(sys.argv) > 1 else "/root/reference"
+    if len(sys.argv) != 2:
+        sys.exit("usage: python tests/golden/make_golden.py <path to the MoEArc source tree>")
+    ref = sys.argv[1]
     data = extract(ref)
     dst = os.path.join(os.path.dirname(os.path.abspath(__file__)), "reference_kats.json")
     with open(dst, "w") as f:

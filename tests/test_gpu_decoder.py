@@ -1,0 +1,121 @@
+"""The synthetic decoder on the B200 against the oracle's decode step (cd_step, double
+accumulation, reference.rs semantics), token by token, over windowed and full blocks, with
+sinks, YaRN RoPE and scattered KV pages.
+
+The weights are generated on the device; the checker rebuilds them on the host — the expert
+banks bit for bit from the same seeds (the integer generator is identical on both sides), the
+bf16 projections by unpacking the packed tiles, the f32 tensors by download — and keeps its own
+KV pools.
+"""
+import ctypes as C
+
+import numpy as np
+import pytest
+
+import oracle as O
+from moearc_b200 import Context
+from moearc_b200.decoder import Decoder, DecoderConfig, unpack_dense
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def ctx():
+    c = Context()
+    yield c
+    c.close()
+
+
+def host_model(dec: Decoder):
+    cfg = dec.cfg
+    H, Dq, Dkv = cfg.n_embd, cfg.n_head * cfg.head_dim, cfg.n_head_kv * cfg.head_dim
+    nb = cfg.n_expert * cfg.n_ff * H // 32
+    layers, keep = [], []
+    for l in range(cfg.n_layer):
+        t = {}
+        t["attn_norm"] = dec.tensor(0, l, np.float32)
+        t["ffn_norm"] = dec.tensor(1, l, np.float32)
+        t["sinks"] = dec.tensor(2, l, np.float32) if cfg.has_sinks else None
+        t["router"] = dec.tensor(3, l, np.float32)
+        wqkv = unpack_dense(dec.tensor(7, l, np.uint16), Dq + 2 * Dkv, H)
+        t["wq"] = np.ascontiguousarray(wqkv[:Dq])
+        t["wk"] = np.ascontiguousarray(wqkv[Dq:Dq + Dkv])
+        t["wv"] = np.ascontiguousarray(wqkv[Dq + Dkv:])
+        t["wo"] = np.ascontiguousarray(unpack_dense(dec.tensor(8, l, np.uint16), H, Dq))
+        synth = O.synth_mxfp4 if cfg.expert_type == O.MXFP4 else (lambda s, n: O.synth_q4_0(s, n, 0.01))
+        t["gate"], t["up"], t["down"] = (synth(dec.seed(k, l), nb) for k in (8, 9, 10))
+        kp = dec.tensor(4, l, np.uint16)
+        t["k"], t["v"] = np.zeros_like(kp), np.zeros_like(kp)
+        t["table"] = dec.tensor(6, l, np.uint32)
+        keep.append(t)
+        layers.append(O.CdLayer(*[O.ptr(t[n]) if t[n] is not None else None for n in
+                                  ("attn_norm", "ffn_norm", "wq", "wk", "wv", "wo", "sinks", "router",
+                                   "gate", "up", "down", "k", "v", "table")]))
+    arr = (O.CdLayer * cfg.n_layer)(*layers)
+    c = O.CdCfg(cfg.n_layer, H, cfg.n_head, cfg.n_head_kv, cfg.head_dim, cfg.n_expert, cfg.n_ff,
+                cfg.n_expert_used, cfg.gating, cfg.act, cfg.expert_type, O.BF16, cfg.alpha, cfg.limit,
+                cfg.rms_eps, cfg.n_swa, cfg.swa_pattern, 32, cfg.rope_base, cfg.rope_freq_scale,
+                cfg.rope_ext_factor, cfg.rope_attn_factor, cfg.rope_corr_lo, cfg.rope_corr_hi)
+    return c, arr, keep, dec.tensor(11, 0, np.float32)
+
+
+@pytest.mark.parametrize("graph", [False, True])
+def test_small_gpt_oss_shaped_decoder_matches_the_oracle(ctx, graph):
+    cfg = DecoderConfig(n_layer=3, n_embd=256, n_head=8, n_head_kv=2, head_dim=64, n_expert=8,
+                        n_expert_used=2, n_ff=128, n_swa=40, swa_pattern=2, n_ctx=256, seed=0xDEC0DE)
+    cfg.yarn(32.0, 4096)
+    dec = Decoder(ctx, cfg)
+    dec.use_graph(graph)
+    c, arr, keep, out_norm = host_model(dec)
+    worst = 0.0
+    for pos in range(70):  # past the 40-key window and across page boundaries
+        x = O.synth_normal_f32(0x1000 + pos, cfg.n_embd, 1.0)
+        dec.set_input(x)
+        dec.step()
+        got = dec.output()
+        want = np.zeros(cfg.n_embd, np.float32)
+        assert O.lib().cd_step(C.byref(c), arr, O.ptr(out_norm), O.ptr(x), pos, None, O.ptr(want), None) == 0
+        err = float(np.max(np.abs(got.astype(np.float64) - want) / np.maximum(np.abs(want), 1.0)))
+        worst = max(worst, err)
+    print(f"decoder graph={graph}: 70 tokens, max rel err {worst:.3e}")
+    assert dec.pos == 70
+    # bf16 K/V rounding amplifies last-bit differences of k and v into 2^-9 relative steps, so the
+    # composed output is held to 1e-3; every component kernel is held to 1e-4 on its own.
+    assert worst <= 1e-3
+    dec.close()
+
+
+def test_the_kv_cache_holds_the_roped_keys(ctx):
+    cfg = DecoderConfig(n_layer=2, n_embd=256, n_head=8, n_head_kv=2, head_dim=64, n_expert=8,
+                        n_expert_used=2, n_ff=128, n_swa=0, n_ctx=128, seed=0xCAC4E)
+    dec = Decoder(ctx, cfg)
+    c, arr, keep, out_norm = host_model(dec)
+    for pos in range(5):
+        x = O.synth_normal_f32(0x2000 + pos, cfg.n_embd, 1.0)
+        dec.set_input(x)
+        dec.step()
+        want = np.zeros(cfg.n_embd, np.float32)
+        assert O.lib().cd_step(C.byref(c), arr, O.ptr(out_norm), O.ptr(x), pos, None, O.ptr(want), None) == 0
+    for l in range(2):
+        gk = O.bf16_to_f32(dec.tensor(4, l, np.uint16))
+        wk = O.bf16_to_f32(keep[l]["k"])
+        gv = O.bf16_to_f32(dec.tensor(5, l, np.uint16))
+        wv = O.bf16_to_f32(keep[l]["v"])
+        # bf16 storage: equal, or one bf16 step apart where the f32 values straddle a rounding edge
+        assert np.max(np.abs(gk - wk)) <= 2 ** -7 * max(1.0, float(np.abs(wk).max()))
+        assert np.max(np.abs(gv - wv)) <= 2 ** -7 * max(1.0, float(np.abs(wv).max()))
+        assert np.mean(gk == wk) > 0.95 and np.mean(gv == wv) > 0.95
+    dec.close()
+
+
+def test_fill_kv_sets_the_depth_and_decoding_continues(ctx):
+    cfg = DecoderConfig(n_layer=2, n_embd=256, n_head=8, n_head_kv=2, head_dim=64, n_expert=8,
+                        n_expert_used=2, n_ff=128, n_swa=64, n_ctx=2048, seed=0xF111)
+    dec = Decoder(ctx, cfg)
+    dec.fill_kv(1500)
+    assert dec.pos == 1500
+    dec.set_input(O.synth_normal_f32(3, 256, 1.0))
+    dec.step()
+    out = dec.output()
+    assert np.all(np.isfinite(out)) and dec.pos == 1501
+    dec.close()
