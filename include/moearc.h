@@ -234,6 +234,25 @@ void *moearc_x_decoder_tensor(moearc_x_decoder *d, int which, unsigned int layer
 unsigned long long moearc_x_decoder_seed(moearc_x_decoder *d, int kind, unsigned int layer,
                                          unsigned long long base);
 
+/* ---- decode attention without allocation (no counterpart in the reference) ----------------
+ * Same arguments, result and return codes as moearc_attn_decode, but the split-K partials live
+ * in a fixed per-device array of MOEARC_X_ATTN_STATIC_SCRATCH_BYTES compiled into the library,
+ * so no call allocates device or host memory. It serves hosts that may not allocate while they
+ * decode (a fixed memory budget, or a neighbouring thread capturing a CUDA graph).
+ * - Returns -2 when the partials for the split count the call picks,
+ *   n_heads x n_splits x (head_dim + 2) x 4 bytes, exceed that size (2 MiB: e.g. 64 heads of
+ *   128 over 8 KV heads needs 1.2 MiB on a 148-SM B200); nothing is enqueued then.
+ * - The first call on a device looks the array's address up (cudaGetSymbolAddress, with that
+ *   device made current for the lookup); make that first call before any stream capture.
+ * - There is one array per device: calls that may overlap on a device (two streams, two
+ *   contexts, two threads) race on it. Serialise them. Nothing in it needs to start at zero. */
+#define MOEARC_X_ATTN_STATIC_SCRATCH_BYTES (2ul << 20)
+int moearc_x_attn_decode_static(moearc_ctx *c, float *out, const float *q, const void *k_pages,
+                                const void *v_pages, const unsigned int *block_table, const float *sinks,
+                                unsigned long n_heads, unsigned long n_kv_heads, unsigned long head_dim,
+                                unsigned long kv_begin, unsigned long n_kv, unsigned long page_tokens,
+                                float scale, unsigned int kv_type);
+
 #ifdef __cplusplus
 }
 #endif

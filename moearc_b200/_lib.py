@@ -85,6 +85,7 @@ SIGNATURES: dict[str, tuple] = {
     "moearc_x_decoder_profile": (I, [P, C.POINTER(F), C.POINTER(I), I]),
     "moearc_x_decoder_tensor": (P, [P, I, U, C.POINTER(UL)]),
     "moearc_x_decoder_seed": (C.c_ulonglong, [P, I, U, C.c_ulonglong]),
+    "moearc_x_attn_decode_static": (I, [P, P, P, P, P, P, P, UL, UL, UL, UL, UL, UL, F, U]),
 }
 
 
