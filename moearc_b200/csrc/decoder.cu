@@ -89,6 +89,8 @@ struct moearc_x_decoder {
     float *attn_scratch = nullptr;
     size_t attn_scratch_b = 0;
     unsigned *attn_ctr = nullptr;  // one split counter per KV head, zero between steps
+    double *rope_freq = nullptr;   // head_dim / 2 angle multipliers (see dense_rope)
+    double rope_mscale = 1.0;
     int max_splits = 1;
     int pos = 0;
     std::vector<void *> allocs;
@@ -139,13 +141,8 @@ int enqueue_step(moearc_x_decoder *d, step_marks *pm = nullptr) {
     rope.n_q_heads = (int)cfg.n_head;
     rope.n_kv_heads = (int)cfg.n_head_kv;
     rope.head_dim = (int)cfg.head_dim;
-    rope.n_rot = (int)cfg.head_dim;
-    rope.theta_scale = std::pow((double)cfg.rope_base, -2.0 / (double)cfg.head_dim);
-    rope.freq_scale = cfg.rope_freq_scale;
-    rope.ext_factor = cfg.rope_ext_factor;
-    rope.attn_factor = cfg.rope_attn_factor;
-    rope.corr_lo = cfg.rope_corr_lo;
-    rope.corr_hi = cfg.rope_corr_hi;
+    rope.freq = d->rope_freq;
+    rope.mscale = d->rope_mscale;
     const float scale = 1.0f / std::sqrt((float)cfg.head_dim);
     for (unsigned l = 0; l < cfg.n_layer; ++l) {
         auto &b = d->L[l];
@@ -230,6 +227,29 @@ moearc_x_decoder *moearc_x_decoder_create(moearc_ctx *c, const moearc_x_decoder_
     d->attn_scratch_b = attn_scratch_bytes(g.n_head, g.head_dim, d->max_splits);
     d->attn_scratch = static_cast<float *>(d->alloc(d->attn_scratch_b));
     d->attn_ctr = static_cast<unsigned *>(d->alloc(sizeof(unsigned) * g.n_head));
+    // RoPE angle of pair p at position pos = pos * freq[p]: base^(-2p/head_dim), blended per
+    // pair by the YaRN ramp (the closed form of reference.rs rope_ext, folded per pair)
+    {
+        const int half = (int)g.head_dim / 2;
+        std::vector<double> fr(half);
+        const double ts = std::pow((double)g.rope_base, -2.0 / (double)g.head_dim);
+        double ms = g.rope_attn_factor;
+        for (int p = 0; p < half; ++p) {
+            double f = (double)g.rope_freq_scale;
+            if (g.rope_ext_factor != 0.0f) {
+                const double den = std::fmax(0.001, (double)g.rope_corr_hi - (double)g.rope_corr_lo);
+                const double y = ((double)p - (double)g.rope_corr_lo) / den;
+                const double ramp = 1.0 - std::fmin(1.0, std::fmax(0.0, y));
+                const double mix = ramp * (double)g.rope_ext_factor;
+                f = f * (1.0 - mix) + mix;
+            }
+            fr[p] = std::pow(ts, (double)p) * f;
+        }
+        if (g.rope_ext_factor != 0.0f) ms *= 1.0 + 0.1 * std::log(1.0 / (double)g.rope_freq_scale);
+        d->rope_mscale = ms;
+        d->rope_freq = static_cast<double *>(d->alloc(sizeof(double) * half));
+        ok &= d->rope_freq && cudaMemcpy(d->rope_freq, fr.data(), sizeof(double) * half, cudaMemcpyHostToDevice) == cudaSuccess;
+    }
     if (!d->table_full || !d->table_swa || !d->dpos || !d->in || !d->h || !d->out || !d->q || !d->att ||
         !d->output_norm || !d->attn_scratch)
         return fail();

@@ -1,5 +1,5 @@
 // dense.cu — packed bf16 tensor-core GEMVs for the decoder's attention projections.
-// See dense.cuh for the structure; the persistent/TMA/last-arriver scheme is moe.cu's.
+// See dense.cuh for the structure.
 #include <algorithm>
 #include <cmath>
 
@@ -10,29 +10,31 @@ namespace moearc {
 
 namespace {
 
-constexpr int WARPS = 4;
-constexpr int STAGES = 2;
-constexpr int PARTS = 3;  // bf16 rounding + two residuals
+constexpr int WARPS = 8;
+constexpr int CH = 2;          // tiles per ring stage (4 KB bulk copies)
+constexpr int STAGES = 3;      // ring stages per warp
+constexpr int PARTS = 3;       // bf16 rounding + two residuals
+constexpr int MAX_LOCAL = 8;   // tile-rows (hence units) one CTA may touch; <= WARPS
+constexpr int MAX_ITEMS = 8;   // B-fragment items per thread: n_cols / 2 <= 8 x 256
+constexpr int MAX_COLS = 2 * MAX_ITEMS * WARPS * 32;
+constexpr int RING_BYTES = WARPS * STAGES * CH * DENSE_TILE;
 
 __global__ void k_dense_pack(uint8_t *dst, const uint16_t *src, int n_rows, int n_cols) {
     const int nkt = n_cols / 64;
-    const size_t total = (size_t)(n_rows / 16) * nkt * 32;
+    const size_t total = (size_t)(n_rows / 16) * nkt * 128;  // (tile, sub-block, lane)
     for (size_t g = blockIdx.x * (size_t)blockDim.x + threadIdx.x; g < total; g += (size_t)gridDim.x * blockDim.x) {
-        const int lane = (int)(g & 31);
-        const size_t tile = g >> 5;
+        const int lane = (int)(g & 31), s = (int)((g >> 5) & 3);
+        const size_t tile = g >> 7;
         const int tr = (int)(tile / nkt), tk = (int)(tile % nkt);
         const int r = lane >> 2, q = lane & 3;
-        uint32_t *o = reinterpret_cast<uint32_t *>(dst + tile * DENSE_TILE + lane * 64);
+        uint32_t *o = reinterpret_cast<uint32_t *>(dst + tile * DENSE_TILE + s * 512 + lane * 16);
         const uint16_t *rowA = src + (size_t)(tr * 16 + r) * n_cols + tk * 64;
         const uint16_t *rowB = rowA + (size_t)8 * n_cols;
-#pragma unroll
-        for (int s = 0; s < 4; ++s) {
-            const int c0 = 16 * s + 2 * q, c1 = c0 + 8;
-            o[4 * s + 0] = (uint32_t)rowA[c0] | ((uint32_t)rowA[c0 + 1] << 16);
-            o[4 * s + 1] = (uint32_t)rowB[c0] | ((uint32_t)rowB[c0 + 1] << 16);
-            o[4 * s + 2] = (uint32_t)rowA[c1] | ((uint32_t)rowA[c1 + 1] << 16);
-            o[4 * s + 3] = (uint32_t)rowB[c1] | ((uint32_t)rowB[c1 + 1] << 16);
-        }
+        const int c0 = 16 * s + 2 * q, c1 = c0 + 8;
+        o[0] = (uint32_t)rowA[c0] | ((uint32_t)rowA[c0 + 1] << 16);
+        o[1] = (uint32_t)rowB[c0] | ((uint32_t)rowB[c0 + 1] << 16);
+        o[2] = (uint32_t)rowA[c1] | ((uint32_t)rowA[c1 + 1] << 16);
+        o[3] = (uint32_t)rowB[c1] | ((uint32_t)rowB[c1 + 1] << 16);
     }
 }
 
@@ -46,9 +48,11 @@ __device__ __forceinline__ uint16_t bf(float v) { return f32_to_bf16_bits(v); }
 
 struct dense_args {
     const uint8_t *w;
-    int n_rows, n_cols, ntr, nkt, kc, nch;
-    int stage_bytes;
+    int n_rows, n_cols, ntr, nkt;
+    long T;         // tiles
     int mode;
+    int unit_trs;   // tile-rows per unit
+    int maxc;       // partial slots per tile-row (the most CTAs that touch one tile-row)
     const float *in;
     const float *norm_w;
     float eps;
@@ -57,226 +61,272 @@ struct dense_args {
     const int *pos;
     dense_rope rope;
     dense_kv kv;
-    float *part;     // [nch][n_rows]
-    unsigned *ctr;   // per unit
+    float *part;    // [ntr][maxc][16]
+    unsigned *ctr;  // per unit
     int *status;
 };
 
-__device__ __forceinline__ void issue(const dense_args &a, int item, uint8_t *stage, uint64_t *bar, int lane) {
-    const int ch = item % a.nch, tr = item / a.nch;
-    const int k0 = ch * a.kc, kn = min(a.kc, a.nkt - k0);
-    if (lane == 0) {
-        fence_proxy_async();
-        mbar_expect_tx(bar, (unsigned)(kn * DENSE_TILE));
-        bulk_g2s(stage, a.w + ((size_t)tr * a.nkt + k0) * DENSE_TILE, (unsigned)(kn * DENSE_TILE), bar);
-    }
-}
+// First tile of CTA c's range (ranges are [T c / G, T (c + 1) / G)), and the CTA whose range
+// holds tile t.
+__host__ __device__ __forceinline__ long tile_lo(long T, int G, int c) { return T * c / G; }
+__host__ __device__ __forceinline__ int cta_of(long T, int G, long t) { return (int)(((t + 1) * G - 1) / T); }
 
-__global__ void __launch_bounds__(WARPS * 32) k_dense(dense_args a) {
+__global__ void __launch_bounds__(WARPS * 32, 1) k_dense(dense_args a) {
     extern __shared__ __align__(128) uint8_t smem[];
+    __shared__ __align__(8) uint64_t bars[WARPS][STAGES];
+    __shared__ float red[WARPS];
+    __shared__ int fin[MAX_LOCAL];
+    __shared__ double rfreq[64];
     const int trace_row = (int)blockIdx.x + (a.mode == 0 ? 0 : 1024);
     (void)trace_row;
     TRACE(0);
-    __shared__ __align__(8) uint64_t bars[WARPS][STAGES];
-    __shared__ float red[WARPS];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int gw = blockIdx.x * WARPS + warp, nw = gridDim.x * WARPS;
+    const int G = gridDim.x, cta = blockIdx.x;
+    const long ta = tile_lo(a.T, G, cta), tb = tile_lo(a.T, G, cta + 1);
+    const long wa = ta + (tb - ta) * warp / WARPS, wb = ta + (tb - ta) * (warp + 1) / WARPS;
     const int nkb = a.n_cols / 16;
-    uint32_t *bsm = reinterpret_cast<uint32_t *>(smem);                   // [nkb][3][4][2]
-    const size_t bsm_bytes = ((size_t)nkb * PARTS * 4 * 8 + 127) / 128 * 128;
-    float *xs = reinterpret_cast<float *>(smem + bsm_bytes);              // [n_cols]
-    const size_t xs_bytes = ((size_t)a.n_cols * 8 + 127) / 128 * 128;  // activation + norm weights
-    uint8_t *my = smem + bsm_bytes + xs_bytes + (size_t)warp * STAGES * a.stage_bytes;
-    const int n_items = a.ntr * a.nch;
+    uint8_t *ring = smem + (size_t)warp * STAGES * CH * DENSE_TILE;
+    uint32_t *bsm = reinterpret_cast<uint32_t *>(smem + RING_BYTES);  // [nkb][3][4][2]
+    float *psm = reinterpret_cast<float *>(smem + RING_BYTES + (size_t)nkb * PARTS * 32);  // [WARPS][MAX_LOCAL][16]
+    const int tr0 = (int)(ta / a.nkt), tr1 = (int)((tb - 1) / a.nkt);  // tile-rows this CTA touches
+
     if (lane == 0) {
         for (int s = 0; s < STAGES; ++s) mbar_init(&bars[warp][s], 1);
         fence_mbar_init();
     }
     __syncwarp();
-    unsigned phase[STAGES] = {0u, 0u};
-    bool pending[STAGES] = {false, false};
-    // The weights do not depend on the previous kernel: start streaming them before waiting.
-    for (int s = 0; s < STAGES; ++s) {
-        const int it = gw + s * nw;
-        if (it < n_items) {
-            issue(a, it, my + s * a.stage_bytes, &bars[warp][s], lane);
-            pending[s] = true;
+    const long nch = (wb - wa + CH - 1) / CH;
+    auto issue = [&](long j, int s) {
+        const long t0 = wa + j * CH;
+        const long n = (wb - t0 < CH) ? wb - t0 : CH;
+        const unsigned bytes = (unsigned)(n * DENSE_TILE);
+        fence_proxy_async();
+        mbar_expect_tx(&bars[warp][s], bytes);
+        bulk_g2s(ring + (size_t)s * CH * DENSE_TILE, a.w + t0 * DENSE_TILE, bytes, &bars[warp][s]);
+    };
+    // the weights do not depend on the previous kernel: stream the first stages now
+    long issued = nch < STAGES ? nch : STAGES;
+    if (lane == 0)
+        for (long j = 0; j < issued; ++j) issue(j, (int)j);
+    for (int i = threadIdx.x; i < WARPS * MAX_LOCAL * 16; i += WARPS * 32) psm[i] = 0.f;
+    // B-fragment item i of this thread: (k16 block kb, q, register reg) -> columns c, c + 1
+    // with c = 16 kb + 2q + 8 reg. The norm weights are static and load before the wait too.
+    const int n_items = nkb * 8;
+    float2 nw[MAX_ITEMS];
+#pragma unroll
+    for (int m = 0; m < MAX_ITEMS; ++m) {
+        const int i = threadIdx.x + m * WARPS * 32;
+        nw[m] = make_float2(1.f, 1.f);
+        if (a.norm_w && i < n_items) {
+            const int reg = i & 1, q = (i >> 1) & 3, kb = i >> 3;
+            nw[m] = __ldg(reinterpret_cast<const float2 *>(a.norm_w + 16 * kb + 2 * q + 8 * reg));
         }
     }
+    if (a.mode == 0)
+        for (int p = threadIdx.x; p < a.rope.head_dim / 2; p += WARPS * 32) rfreq[p] = __ldg(a.rope.freq + p);
     pdl_trigger();
     pdl_wait();
     TRACE(1);
-    // The activation (and the norm weights) into shared memory, all loads in flight at once.
-    const int n4 = a.n_cols / 4;
-    float ss = 0.f;
-    float *ns = xs + a.n_cols;  // norm weights, when present
-    {
-        constexpr int U = 8;  // float4 per thread per batch; 128 threads x 8 x 4 = 4096 values
-        for (int base = threadIdx.x; base < n4; base += WARPS * 32 * U) {
-            float4 v[U], w[U];
+    float2 xv[MAX_ITEMS];
 #pragma unroll
-            for (int u = 0; u < U; ++u) {
-                const int i = base + u * WARPS * 32;
-                if (i < n4) {
-                    v[u] = __ldcg(reinterpret_cast<const float4 *>(a.in) + i);
-                    if (a.norm_w) w[u] = __ldg(reinterpret_cast<const float4 *>(a.norm_w) + i);
-                }
-            }
-#pragma unroll
-            for (int u = 0; u < U; ++u) {
-                const int i = base + u * WARPS * 32;
-                if (i < n4) {
-                    reinterpret_cast<float4 *>(xs)[i] = v[u];
-                    if (a.norm_w) reinterpret_cast<float4 *>(ns)[i] = w[u];
-                    ss = fmaf(v[u].x, v[u].x, fmaf(v[u].y, v[u].y, fmaf(v[u].z, v[u].z, fmaf(v[u].w, v[u].w, ss))));
-                }
-            }
+    for (int m = 0; m < MAX_ITEMS; ++m) {
+        const int i = threadIdx.x + m * WARPS * 32;
+        xv[m] = make_float2(0.f, 0.f);
+        if (i < n_items) {
+            const int reg = i & 1, q = (i >> 1) & 3, kb = i >> 3;
+            xv[m] = __ldcg(reinterpret_cast<const float2 *>(a.in + 16 * kb + 2 * q + 8 * reg));
         }
     }
     float scale = 1.f;
     if (a.norm_w) {
+        // RMSNorm (moe.rs:1936-1940): f32 sum of squares, 1 / sqrt(mean + eps)
+        float ss = 0.f;
+#pragma unroll
+        for (int m = 0; m < MAX_ITEMS; ++m) ss = fmaf(xv[m].x, xv[m].x, fmaf(xv[m].y, xv[m].y, ss));
         ss = warp_sum(ss);
         if (lane == 0) red[warp] = ss;
-    }
-    __syncthreads();
-    if (a.norm_w) {
+        __syncthreads();
         float t = 0.f;
         for (int w = 0; w < WARPS; ++w) t += red[w];
         scale = 1.0f / sqrtf(t / (float)a.n_cols + a.eps);
     }
-    // B fragments: (k16 block, q, register) -> the pair (x[16kb + 2q + 8reg], x[... + 1]),
-    // RMSNorm applied for the Q/K/V projection, split into three bf16 parts
-    for (int i = threadIdx.x; i < nkb * 4 * 2; i += WARPS * 32) {
-        const int reg = i & 1, q = (i >> 1) & 3, kb = i >> 3;
-        const int c = 16 * kb + 2 * q + 8 * reg;
-        float v0 = xs[c], v1 = xs[c + 1];
-        if (a.norm_w) {
-            v0 = (v0 * scale) * ns[c];
-            v1 = (v1 * scale) * ns[c + 1];
+#pragma unroll
+    for (int m = 0; m < MAX_ITEMS; ++m) {
+        const int i = threadIdx.x + m * WARPS * 32;
+        if (i < n_items) {
+            const int reg = i & 1, q = (i >> 1) & 3, kb = i >> 3;
+            float v0 = xv[m].x, v1 = xv[m].y;
+            if (a.norm_w) {
+                v0 = (v0 * scale) * nw[m].x;
+                v1 = (v1 * scale) * nw[m].y;
+            }
+            const uint16_t h0 = bf(v0), h1 = bf(v1);
+            float r0 = v0 - bf16_bits_to_f32(h0), r1 = v1 - bf16_bits_to_f32(h1);
+            const uint16_t m0 = bf(r0), m1 = bf(r1);
+            r0 -= bf16_bits_to_f32(m0);
+            r1 -= bf16_bits_to_f32(m1);
+            const uint16_t l0 = bf(r0), l1 = bf(r1);
+            bsm[(((size_t)kb * PARTS + 0) * 4 + q) * 2 + reg] = (uint32_t)h0 | ((uint32_t)h1 << 16);
+            bsm[(((size_t)kb * PARTS + 1) * 4 + q) * 2 + reg] = (uint32_t)m0 | ((uint32_t)m1 << 16);
+            bsm[(((size_t)kb * PARTS + 2) * 4 + q) * 2 + reg] = (uint32_t)l0 | ((uint32_t)l1 << 16);
         }
-        uint16_t h0 = bf(v0), h1 = bf(v1);
-        float r0 = v0 - bf16_bits_to_f32(h0), r1 = v1 - bf16_bits_to_f32(h1);
-        uint16_t m0 = bf(r0), m1 = bf(r1);
-        r0 -= bf16_bits_to_f32(m0);
-        r1 -= bf16_bits_to_f32(m1);
-        uint16_t l0 = bf(r0), l1 = bf(r1);
-        bsm[(((size_t)kb * PARTS + 0) * 4 + q) * 2 + reg] = (uint32_t)h0 | ((uint32_t)h1 << 16);
-        bsm[(((size_t)kb * PARTS + 1) * 4 + q) * 2 + reg] = (uint32_t)m0 | ((uint32_t)m1 << 16);
-        bsm[(((size_t)kb * PARTS + 2) * 4 + q) * 2 + reg] = (uint32_t)l0 | ((uint32_t)l1 << 16);
     }
     __syncthreads();
-
     TRACE(2);
-    const int n = lane >> 2, qd = lane & 3, r = lane >> 2;
-    int stage = 0;
-    int itn = 0;
-    for (int it = gw; it < n_items; it += nw, ++itn) {
-        uint8_t *st = my + stage * a.stage_bytes;
-        const bool ok = mbar_wait(&bars[warp][stage], phase[stage], a.status);
-        phase[stage] ^= 1u;
-        pending[stage] = false;
-        if (!ok) break;
-        if (itn < 6) TRACE(3 + 4 * itn);
-        const int ch = it % a.nch, tr = it / a.nch;
-        const int k0 = ch * a.kc, kn = min(a.kc, a.nkt - k0);
-        float acc[4] = {0.f, 0.f, 0.f, 0.f};
-        for (int kt = 0; kt < kn; ++kt) {
-            const uint8_t *tile = st + (size_t)kt * DENSE_TILE + lane * 64;
-#pragma unroll
-            for (int s = 0; s < 4; ++s) {
-                const uint4 av = *reinterpret_cast<const uint4 *>(tile + 16 * s);
-                const int kb = (k0 + kt) * 4 + s;
-                uint2 bv = make_uint2(0u, 0u);
-                if (n < PARTS) bv = *reinterpret_cast<const uint2 *>(bsm + (((size_t)kb * PARTS + n) * 4 + qd) * 2);
-                mma_bf16(acc, av, bv.x, bv.y);
-            }
-        }
-        __syncwarp();
-        const int nxt = it + STAGES * nw;
-        if (nxt < n_items) {
-            issue(a, nxt, st, &bars[warp][stage], lane);
-            pending[stage] = true;
-        }
-        stage ^= 1;
-        // columns 0,1 (lane q = 0) and 2 (lane q = 1, c0) are the three parts
-        const float lo_r = __shfl_xor_sync(0xffffffffu, acc[0], 1);
-        const float lo_r8 = __shfl_xor_sync(0xffffffffu, acc[2], 1);
+
+    // body: lane (n = lane / 4, q = lane % 4) feeds B column n (part n; zero past the three);
+    // sub-blocks alternate between two accumulators to halve the MMA dependency chain
+    const int n8 = lane >> 2, qd = lane & 3;
+    float acc0[4] = {0.f, 0.f, 0.f, 0.f}, acc1[4] = {0.f, 0.f, 0.f, 0.f};
+    int cur = -1;
+    long kf = -1;
+    // (tile-row, k-tile) of the warp's next tile, advanced per tile (a 64-bit division per
+    // tile would cost more than the tile's multiply)
+    int wtr = (int)(wa / a.nkt), wkt = (int)(wa % a.nkt);
+    // row r of the tile-row = columns 0 + 1 (lane q = 0) + column 2 (lane q = 1)
+    auto flush = [&](int ltr) {
+        const float a0 = acc0[0] + acc1[0], a1 = acc0[1] + acc1[1];
+        const float a2 = acc0[2] + acc1[2], a3 = acc0[3] + acc1[3];
+        const float p0 = __shfl_xor_sync(0xffffffffu, a0, 1);
+        const float p2 = __shfl_xor_sync(0xffffffffu, a2, 1);
         if (qd == 0) {
-            a.part[(size_t)ch * a.n_rows + tr * 16 + r] = (acc[0] + acc[1]) + lo_r;
-            a.part[(size_t)ch * a.n_rows + tr * 16 + r + 8] = (acc[2] + acc[3]) + lo_r8;
+            float *ps = psm + ((size_t)warp * MAX_LOCAL + ltr) * 16;
+            ps[n8] = (a0 + a1) + p0;
+            ps[n8 + 8] = (a2 + a3) + p2;
         }
-        if (itn < 6) TRACE(4 + 4 * itn);
-        __threadfence();
+    };
+    for (long j = 0; j < nch; ++j) {
+        const int s = (int)(j % STAGES);
+        if (!mbar_wait(&bars[warp][s], (unsigned)((j / STAGES) & 1), a.status)) {
+            kf = j;
+            break;
+        }
+        if (j < 4) TRACE(3 + j);
+        const long t0 = wa + j * CH;
+        const int n = (int)((wb - t0 < CH) ? wb - t0 : CH);
+        const uint8_t *st = ring + (size_t)s * CH * DENSE_TILE + lane * 16;
+        for (int i = 0; i < n; ++i) {
+            const int ltr = wtr - tr0, kt = wkt;
+            if (++wkt == a.nkt) {
+                wkt = 0;
+                ++wtr;
+            }
+            if (ltr != cur) {
+                if (cur >= 0) flush(cur);
+                cur = ltr;
+#pragma unroll
+                for (int e = 0; e < 4; ++e) acc0[e] = acc1[e] = 0.f;
+            }
+            const uint8_t *tile = st + (size_t)i * DENSE_TILE;
+            uint4 av[4];
+            uint2 bv[4];
+#pragma unroll
+            for (int sb = 0; sb < 4; ++sb) {
+                av[sb] = *reinterpret_cast<const uint4 *>(tile + sb * 512);
+                bv[sb] = make_uint2(0u, 0u);
+                if (n8 < PARTS)
+                    bv[sb] = *reinterpret_cast<const uint2 *>(bsm + (((size_t)(kt * 4 + sb) * PARTS + n8) * 4 + qd) * 2);
+            }
+            mma_bf16(acc0, av[0], bv[0].x, bv[0].y);
+            mma_bf16(acc1, av[1], bv[1].x, bv[1].y);
+            mma_bf16(acc0, av[2], bv[2].x, bv[2].y);
+            mma_bf16(acc1, av[3], bv[3].x, bv[3].y);
+        }
         __syncwarp();
-        if (itn < 6) TRACE(5 + 4 * itn);
-        const int rows_per_unit = (a.mode == 0) ? a.rope.head_dim : 16;
-        const int tr_per_unit = rows_per_unit / 16;
-        const int unit = tr / tr_per_unit;
-        unsigned prev = 0;
-        if (lane == 0) prev = atomicAdd(a.ctr + unit, 1u);
-        prev = __shfl_sync(0xffffffffu, prev, 0);
-        if (prev != (unsigned)(tr_per_unit * a.nch) - 1) continue;
-        if (itn < 6) TRACE(6 + 4 * itn);
-        __threadfence();
-        if (lane == 0) a.ctr[unit] = 0;
-        const int row0 = unit * rows_per_unit;
-        if (a.mode == 1) {
-            if (lane < 16) {
-                const int row = row0 + lane;
-                float s = 0.f;
-                for (int c = 0; c < a.nch; ++c) s += __ldcg(a.part + (size_t)c * a.n_rows + row);
-                a.out[row] = a.residual ? a.residual[row] + s : s;
-            }
-            continue;
-        }
-        // Q/K/V head complete: unit < n_q_heads is a query head, then the K heads, then V.
-        const int D = a.rope.head_dim, half = D / 2;
-        float v[4];
-        const int per = D / 32;  // values per lane: d = lane + 32 i
-        for (int i = 0; i < per; ++i) {
-            const int row = row0 + lane + 32 * i;
-            float s = 0.f;
-            for (int c = 0; c < a.nch; ++c) s += __ldcg(a.part + (size_t)c * a.n_rows + row);
-            v[i] = s;
-        }
-        const int hq = a.rope.n_q_heads, hk = a.rope.n_kv_heads;
-        const int pos = *a.pos;
-        if (unit < hq + hk) {
-            // NeoX RoPE: pairs (d, d + half); this lane holds d = lane + 32 i.
-            for (int i = 0; i < per / 2; ++i) {
-                const int p = lane + 32 * i;  // pair index < half
-                const double te = (double)pos * pow(a.rope.theta_scale, (double)p);
-                double th = (double)a.rope.freq_scale * te, ms = a.rope.attn_factor;
-                if (a.rope.ext_factor != 0.0f) {
-                    const double y = ((double)p - a.rope.corr_lo) / fmax(0.001, (double)a.rope.corr_hi - a.rope.corr_lo);
-                    const double ramp = 1.0 - fmin(1.0, fmax(0.0, y));
-                    const double mix = ramp * a.rope.ext_factor;
-                    th = th * (1.0 - mix) + te * mix;
-                    ms *= 1.0 + 0.1 * log(1.0 / (double)a.rope.freq_scale);
-                }
-                double sn, cs;
-                sincos(th, &sn, &cs);
-                cs *= ms;
-                sn *= ms;
-                const double x0 = v[i], x1 = v[i + per / 2];
-                v[i] = (float)(x0 * cs - x1 * sn);
-                v[i + per / 2] = (float)(x0 * sn + x1 * cs);
-            }
-            (void)half;
-        }
-        if (unit < hq) {
-            for (int i = 0; i < per; ++i) a.out[(size_t)unit * D + lane + 32 * i] = v[i];
-        } else {
-            const int kvh = (unit < hq + hk) ? unit - hq : unit - hq - hk;
-            uint16_t *pool = (unit < hq + hk) ? a.kv.k_pages : a.kv.v_pages;
-            const int pt = a.kv.page_tokens;
-            const size_t page = a.kv.table[pos / pt], slot = pos % pt;
-            uint16_t *dst = pool + ((page * pt + slot) * hk + kvh) * D;
-            for (int i = 0; i < per; ++i) dst[lane + 32 * i] = bf(v[i]);
+        if (issued < nch) {
+            if (lane == 0) issue(issued, s);
+            ++issued;
         }
     }
-    for (int s = 0; s < STAGES; ++s)
-        if (pending[s]) mbar_wait(&bars[warp][s], phase[s], a.status);
+    if (kf >= 0) {
+        // a copy did not complete in time: no bulk copy may still land in this warp's ring
+        // when the CTA exits, so wait (bounded) for every one issued, then skip the epilogue
+        for (long j = kf; j < issued; ++j) mbar_wait(&bars[warp][j % STAGES], (unsigned)((j / STAGES) & 1), a.status);
+    } else if (cur >= 0) {
+        flush(cur);
+    }
+    if (__syncthreads_or(kf >= 0)) return;
+    TRACE(8);
+
+    // the CTA's partial of every tile-row it touched: its warps summed in order
+    const int n_local = tr1 - tr0 + 1;
+    for (int e = threadIdx.x; e < n_local * 16; e += WARPS * 32) {
+        const int ltr = e >> 4, row = e & 15;
+        float s = 0.f;
+        for (int w = 0; w < WARPS; ++w) s += psm[((size_t)w * MAX_LOCAL + ltr) * 16 + row];
+        const int tr = tr0 + ltr;
+        const int slot = cta - cta_of(a.T, G, (long)tr * a.nkt);
+        a.part[((size_t)tr * a.maxc + slot) * 16 + row] = s;
+    }
+    __threadfence();
+    __syncthreads();
+    // one arrival per unit touched; the CTAs that touch a unit are a contiguous run
+    const int u0 = tr0 / a.unit_trs, u1 = tr1 / a.unit_trs;
+    if ((int)threadIdx.x <= u1 - u0) {
+        const int u = u0 + threadIdx.x;
+        const long first = (long)u * a.unit_trs * a.nkt, last = (long)(u + 1) * a.unit_trs * a.nkt - 1;
+        const unsigned target = (unsigned)(cta_of(a.T, G, last) - cta_of(a.T, G, first) + 1);
+        fin[threadIdx.x] = atomicAdd(a.ctr + u, 1u) == target - 1;
+    }
+    __syncthreads();
+    TRACE(9);
+    // finish the units this CTA completed last: warp i takes the i-th unit touched
+    if (warp > u1 - u0 || !fin[warp]) return;
+    __threadfence();
+    const int unit = u0 + warp;
+    if (lane == 0) a.ctr[unit] = 0;
+    auto row_value = [&](int row) {
+        const int tr = row >> 4;
+        const int c0 = cta_of(a.T, G, (long)tr * a.nkt), c1 = cta_of(a.T, G, (long)(tr + 1) * a.nkt - 1);
+        float s = 0.f;
+        for (int k = 0; k <= c1 - c0; ++k) s += __ldcg(a.part + ((size_t)tr * a.maxc + k) * 16 + (row & 15));
+        return s;
+    };
+    if (a.mode == 1) {
+        for (int rr = lane; rr < a.unit_trs * 16; rr += 32) {
+            const int row = unit * a.unit_trs * 16 + rr;
+            const float s = row_value(row);
+            a.out[row] = a.residual ? a.residual[row] + s : s;
+        }
+        return;
+    }
+    // Q/K/V head complete: unit < n_q_heads is a query head, then the K heads, then V.
+    const int D = a.rope.head_dim;
+    const int per = D / 32;  // values per lane: d = lane + 32 i
+    const int row0 = unit * D;
+    float v[4];
+    for (int i = 0; i < per; ++i) v[i] = row_value(row0 + lane + 32 * i);
+    const int hq = a.rope.n_q_heads, hk = a.rope.n_kv_heads;
+    const int pos = *a.pos;
+    if (unit < hq + hk) {
+        // NeoX RoPE: pairs (d, d + D/2); this lane holds d = lane + 32 i. The angle of pair p
+        // is pos * freq[p] (the YaRN blend folded into freq on the host), reduced by 2 pi in
+        // two steps before the sine and cosine so large positions keep full precision.
+        for (int i = 0; i < per / 2; ++i) {
+            const int p = lane + 32 * i;  // pair index < D/2
+            const double th = (double)pos * rfreq[p];
+            const double k = rint(th * 0.15915494309189535);
+            double r = fma(-k, 6.283185307179586, th);
+            r = fma(-k, 2.4492935982947064e-16, r);
+            double sn, cs;
+            sincos(r, &sn, &cs);
+            cs *= a.rope.mscale;
+            sn *= a.rope.mscale;
+            const double x0 = v[i], x1 = v[i + per / 2];
+            v[i] = (float)(x0 * cs - x1 * sn);
+            v[i + per / 2] = (float)(x0 * sn + x1 * cs);
+        }
+    }
+    if (unit < hq) {
+        for (int i = 0; i < per; ++i) a.out[(size_t)unit * D + lane + 32 * i] = v[i];
+    } else {
+        const int kvh = (unit < hq + hk) ? unit - hq : unit - hq - hk;
+        uint16_t *pool = (unit < hq + hk) ? a.kv.k_pages : a.kv.v_pages;
+        const int pt = a.kv.page_tokens;
+        const size_t page = a.kv.table[pos / pt], slot = pos % pt;
+        uint16_t *dst = pool + ((page * pt + slot) * hk + kvh) * D;
+        for (int i = 0; i < per; ++i) dst[lane + 32 * i] = bf(v[i]);
+    }
     TRACE(31);
 }
 
@@ -287,7 +337,8 @@ TRACE_SETTER(dense)
 struct dense_gemv {
     moearc_ctx *c;
     int n_rows, n_cols, mode;
-    int ntr, nkt, kc, nch, stage_bytes, grid, smem;
+    int ntr, nkt, grid, smem, maxc;
+    long T;
     float *part;
     unsigned *ctr;
     int *status;
@@ -296,14 +347,16 @@ struct dense_gemv {
 
 int dense_pack(moearc_ctx *c, void *dst, const void *src, int n_rows, int n_cols) {
     if (n_rows % 16 || n_cols % 64) return ERR_ARG;
-    const size_t work = (size_t)(n_rows / 16) * (n_cols / 64) * 32;
+    const size_t work = (size_t)(n_rows / 16) * (n_cols / 64) * 128;
     const unsigned g = (unsigned)std::min<size_t>((work + 255) / 256, (size_t)c->sm_count * 64);
     k_dense_pack<<<g, 256, 0, c->stream>>>(static_cast<uint8_t *>(dst), static_cast<const uint16_t *>(src), n_rows, n_cols);
     return cudaGetLastError() == cudaSuccess ? OK : ERR;
 }
 
+// Units: mode 0 heads of head_dim rows (head_dim a multiple of 64, at most 128, from
+// dense_run's rope), mode 1 single tile-rows.
 dense_gemv *dense_create(moearc_ctx *c, int n_rows, int n_cols, int mode) {
-    if (n_rows % 16 || n_cols % 64) return nullptr;
+    if (n_rows % 16 || n_cols % 64 || n_cols > MAX_COLS) return nullptr;
     auto *g = new dense_gemv();
     g->c = c;
     g->n_rows = n_rows;
@@ -311,29 +364,29 @@ dense_gemv *dense_create(moearc_ctx *c, int n_rows, int n_cols, int mode) {
     g->mode = mode;
     g->ntr = n_rows / 16;
     g->nkt = n_cols / 64;
-    // chunking: balance ntr * nch items over the grid's warps
-    const int bsm = ((n_cols / 16) * PARTS * 4 * 8 + 127) / 128 * 128 + (n_cols * 8 + 127) / 128 * 128;
-    int best = 1;
-    double best_cost = 1e30;
-    for (int kc = 1; kc <= std::min(8, g->nkt); ++kc) {
-        const int stage = kc * DENSE_TILE;
-        const int smem = bsm + WARPS * STAGES * stage;
-        const int per_sm = std::max(1, std::min(4, (228 * 1024) / (smem + 1024 + 128)));
-        const long nw = (long)c->sm_count * per_sm * WARPS;
-        const long items = (long)g->ntr * ((g->nkt + kc - 1) / kc);
-        const double cost = (double)((items + nw - 1) / nw) * (kc + 1.0);
-        if (cost < best_cost - 1e-9) {
-            best_cost = cost;
-            best = kc;
+    g->T = (long)g->ntr * g->nkt;
+    // one CTA per SM with a few stages of tiles per warp; more CTAs only when a CTA's range
+    // would touch more than MAX_LOCAL tile-rows (short rows)
+    auto fits = [&](int grid) {
+        for (int cta = 0; cta < grid; ++cta) {
+            const long ta = tile_lo(g->T, grid, cta), tb = tile_lo(g->T, grid, cta + 1);
+            if (tb <= ta || (tb - 1) / g->nkt - ta / g->nkt + 1 > MAX_LOCAL) return false;
         }
+        return true;
+    };
+    int grid = (int)std::max(1L, std::min<long>(c->sm_count, g->T / (WARPS * CH)));
+    while (!fits(grid) && grid < g->T) ++grid;
+    if (!fits(grid)) {
+        delete g;
+        return nullptr;
     }
-    g->kc = best;
-    g->nch = (g->nkt + best - 1) / best;
-    g->stage_bytes = best * DENSE_TILE;
-    g->smem = bsm + WARPS * STAGES * g->stage_bytes;
-    const int per_sm = std::max(1, std::min(4, (228 * 1024) / (g->smem + 1024 + 128)));
-    g->grid = c->sm_count * per_sm;
-    const size_t part_b = sizeof(float) * (size_t)g->nch * n_rows;
+    g->grid = grid;
+    int maxc = 1;
+    for (int tr = 0; tr < g->ntr; ++tr)
+        maxc = std::max(maxc, cta_of(g->T, grid, (long)(tr + 1) * g->nkt - 1) - cta_of(g->T, grid, (long)tr * g->nkt) + 1);
+    g->maxc = maxc;
+    g->smem = RING_BYTES + (n_cols / 16) * PARTS * 32 + WARPS * MAX_LOCAL * 16 * 4;
+    const size_t part_b = sizeof(float) * (size_t)g->ntr * maxc * 16;
     const size_t ctr_b = sizeof(unsigned) * (size_t)g->ntr;
     if (cudaMalloc(&g->mem, part_b + ctr_b + 256) != cudaSuccess) {
         cudaGetLastError();
@@ -344,10 +397,10 @@ dense_gemv *dense_create(moearc_ctx *c, int n_rows, int n_cols, int mode) {
     g->ctr = reinterpret_cast<unsigned *>(static_cast<uint8_t *>(g->mem) + part_b);
     g->status = reinterpret_cast<int *>(static_cast<uint8_t *>(g->mem) + part_b + ctr_b);
     cudaMemsetAsync(g->mem, 0, part_b + ctr_b + 256, c->stream);
-    // The attribute is per kernel, shared by every plan: set it to the most any plan may use
-    // (227 KB less the kernel's static shared memory), not to this plan's need.
-    if (g->smem > 226 * 1024 ||
-        cudaFuncSetAttribute(k_dense, cudaFuncAttributeMaxDynamicSharedMemorySize, 226 * 1024) != cudaSuccess) {
+    // The attribute is per kernel, shared by every plan: set it to the most any plan may use,
+    // not to this plan's need.
+    if (g->smem > 200 * 1024 ||
+        cudaFuncSetAttribute(k_dense, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024) != cudaSuccess) {
         cudaGetLastError();
         cudaFree(g->mem);
         delete g;
@@ -371,10 +424,16 @@ int dense_run(dense_gemv *g, const void *w_packed, const float *in, const float 
     a.n_cols = g->n_cols;
     a.ntr = g->ntr;
     a.nkt = g->nkt;
-    a.kc = g->kc;
-    a.nch = g->nch;
-    a.stage_bytes = g->stage_bytes;
+    a.T = g->T;
     a.mode = g->mode;
+    a.maxc = g->maxc;
+    a.unit_trs = 1;
+    if (g->mode == 0) {
+        if (!rope || !kv || rope->head_dim % 64 != 0 || rope->head_dim > 128 ||
+            g->n_rows != (rope->n_q_heads + 2 * rope->n_kv_heads) * rope->head_dim)
+            return ERR_ARG;
+        a.unit_trs = rope->head_dim / 16;
+    }
     a.in = in;
     a.norm_w = norm_w;
     a.eps = eps;

@@ -2,31 +2,41 @@
 //
 // The reference issues these as four matvecs plus separate RMSNorm, RoPE, KV-append and
 // residual-add launches per block (crates/moearc-engine/src/moe.rs:1936-2072). Here one
-// persistent kernel per projection does all of it:
-//   prologue  each CTA issues its first weight copies, then builds the activation's B
-//             fragments in shared memory — RMSNorm of the residual stream applied on the way
-//             for Q/K/V — while those copies land;
-//   body      warps stream packed 16x64 bf16 tiles with TMA bulk copies and multiply on the
-//             tensor cores; the activation enters as three bf16 columns (its rounding and two
-//             rounding residuals), ~24 bits of the f32 value;
-//   epilogue  the last warp to finish a unit reduces the split-K partials in a fixed order
-//             and either applies RoPE and writes q (f32) and K/V (bf16, into the paged cache
-//             at this step's page and slot), or adds the residual.
+// kernel per projection does all of it, one CTA per SM:
+//   split     the packed tiles, in memory order, are cut into one equal contiguous range per
+//             CTA and that range into one per warp, so every SM streams the same number of
+//             bytes whatever the matrix shape;
+//   prologue  each warp issues the bulk copies of its first tiles before waiting for the
+//             previous kernel (the weights do not depend on it), so they stream while that
+//             kernel finishes; after the wait the activation becomes B fragments in one pass,
+//             RMSNorm of the residual stream applied on the way for Q/K/V;
+//   body      warps multiply 16x64 bf16 tiles on the tensor cores; the activation enters as
+//             three bf16 columns (its rounding and two rounding residuals), ~24 bits of the
+//             f32 value;
+//   epilogue  per-tile-row sums of the CTA's warps go to a partial buffer; the last CTA to
+//             finish a unit (a head for Q/K/V, a tile-row for O) sums its partials in a fixed
+//             order and either applies RoPE and writes q (f32) and K/V (bf16, into the paged
+//             cache at this step's page and slot), or adds the residual.
 #pragma once
 
 #include "common.cuh"
 
 namespace moearc {
 
-// Packed bf16 tile: 16 rows x 64 columns = 2 KB; lane l = 4r + q holds 64 contiguous bytes,
-// for each 16-column sub-block s: (row r, cols 16s+2q..+1), (row r+8, same), (row r,
-// 16s+2q+8..+9), (row r+8, same) — the m16n8k16 A fragment.
+// Packed bf16 tile: 16 rows x 64 columns = 2 KB, tiles in tile-row-major order. Inside a tile,
+// 16-column sub-block s holds 32 lanes x 16 bytes at 512 s + 16 l; lane l = 4r + q holds
+// (row r, cols 16s+2q..+1), (row r+8, same), (row r, 16s+2q+8..+9), (row r+8, same) — the
+// m16n8k16 A fragment — so a warp's 16-byte shared-memory reads of one sub-block touch every
+// bank once.
 constexpr int DENSE_TILE = 2048;
 
+// NeoX RoPE of the Q and K heads: pair p of a head at position pos turns by pos * freq[p]
+// (device, head_dim / 2 doubles: base^(-2p/head_dim) times the YaRN blend of the pair) and both
+// outputs scale by mscale.
 struct dense_rope {
-    int n_q_heads, n_kv_heads, head_dim, n_rot;
-    double theta_scale;
-    float freq_scale, ext_factor, attn_factor, corr_lo, corr_hi;
+    int n_q_heads, n_kv_heads, head_dim;
+    const double *freq;
+    double mscale;
 };
 
 struct dense_kv {

@@ -50,6 +50,11 @@ struct moearc_x_moe {
     // gate-up (mode 0) and down (mode 1) kernel plans
     int warps_gu, ranges_gu, tpr_gu, stages_gu, stage_gu, smem_gu, grid_gu;
     int warps_dn, ranges_dn, tpr_dn, stages_dn, stage_dn, smem_dn, grid_dn;
+    // decode path (T_max * K <= MAX_TK columns): k_xroute + k_xexpert
+    bool xpath;
+    int x_grid, x_route_grid, x_route_smem, x_ch_gu, x_ch_dn, x_stage_gu, x_stage_dn, x_ntok, x_maxc;
+    float *x_part_gu, *x_part_dn;
+    unsigned *x_ctr_gu, *x_ctr_dn;
     // device scratch (one allocation)
     void *mem;
     size_t mem_bytes;
@@ -173,14 +178,19 @@ __device__ __forceinline__ void decode4(uint32_t w, uint32_t (&r)[4]) {
 }
 
 // The scale of (row r or r+8, block b0 or b0+1) from the lane's scale word(s), as the factor
-// the block's MMA sum is multiplied by: MXFP4 2 * 2^(e-128) (the E2M1 values decoded are
-// the true ones, half the reference's doubled table, reference.rs:51-70); Q4_0 the delta.
+// the block's MMA sum is multiplied by: MXFP4 2 * 2^(e-128) = 2^(e-127) (the E2M1 values
+// decoded are the true ones, half the reference's doubled table, reference.rs:51-70), built
+// by moving the byte into the f32 exponent field — exact for e >= 1; e = 0 (2^-127, a
+// subnormal) becomes 0, an absolute difference below 6 * 2^-127 * sum|x| per block. Q4_0:
+// the f16 delta.
 template <int WT>
 __device__ __forceinline__ void scales4(const uint8_t *tile, int r, float (&s)[4]) {
     if constexpr (WT == 39) {
         const uint32_t e = *reinterpret_cast<const uint32_t *>(tile + 512 + 4 * r);
-#pragma unroll
-        for (int i = 0; i < 4; ++i) s[i] = 2.0f * e8m0_half((e >> (8 * i)) & 0xFFu);
+        s[0] = __uint_as_float((e << 23) & 0x7F800000u);
+        s[1] = __uint_as_float((e << 15) & 0x7F800000u);
+        s[2] = __uint_as_float((e << 7) & 0x7F800000u);
+        s[3] = __uint_as_float((e >> 1) & 0x7F800000u);
     } else {
         const uint2 d = *reinterpret_cast<const uint2 *>(tile + 512 + 8 * r);
         s[0] = f16_bits_to_f32((uint16_t)(d.x & 0xFFFF));
@@ -650,13 +660,15 @@ __global__ void __launch_bounds__(256) k_moe_rows(rows_args a) {
     const int r = lane >> 2, q = lane & 3;
     int un = 0;
     for (int u = blockIdx.x; u < n_units; u += gridDim.x, ++un) {
-        if (un < 12) TRACE(4 + 2 * un);
+        if (un < 5) TRACE(4 + 2 * un);
         for (int i = warp; i < items_per_unit; i += nwarps) {
             const int stage = k % a.stages;
+            if (k < 8) TRACE(14 + 2 * k);
             if (!failed && !mbar_wait(&bars[warp][stage], (unsigned)(k / a.stages) & 1u, a.status)) {
                 failed = true;
                 kf = k;
             }
+            if (k < 8) TRACE(15 + 2 * k);
             ++k;
             int g, tr, rg;
             decode(item_pos{u, i}, g, tr, rg);
@@ -698,7 +710,7 @@ __global__ void __launch_bounds__(256) k_moe_rows(rows_args a) {
             }
         }
         __syncthreads();
-        if (un < 12) TRACE(5 + 2 * un);
+        if (un < 5) TRACE(5 + 2 * un);
         if (!down) {
             // gate-up unit: sum the K runs in order, apply the activation, write the f32
             // activation and the down kernel's B fragments (f16 rounding + residual halves)
@@ -754,6 +766,558 @@ __global__ void __launch_bounds__(256) k_moe_rows(rows_args a) {
     // for any that were issued and not consumed (only after a failed wait)
     if (failed)
         for (int j = kf; j < n_issued; ++j) mbar_wait(&bars[warp][j % a.stages], (unsigned)(j / a.stages) & 1u, a.status);
+    TRACE(31);
+}
+
+// ---- the decode path: T x K <= 32 columns --------------------------------------------------
+//
+// Three kernels per layer, each one CTA per SM at most, each sized to share an SM with its
+// neighbours so a kernel's CTAs become resident (and start their weight copies) while the
+// kernel before it still runs:
+//   x_route   router logits (+ bias) and the activation's B fragments; the router rows are
+//             bulk-copied to shared memory before the wait, so after it only the activation
+//             is read
+//   x_expert  gate-up (mode 0) or down (mode 1). Every CTA derives the top-k and the slot
+//             tables itself from the logits (warp-parallel, in shared memory) instead of one
+//             CTA building them for all. The work is one flattened sequence — gate-up
+//             (group, tile-row, k-tile) pairs of gate and up tiles, down (tile-row, group,
+//             k-tile) tiles — cut into equal contiguous ranges, one per warp, streamed through
+//             a per-warp ring of bulk copies (down issues its first stages before the wait).
+//             A warp writes one partial per segment (nkt consecutive elements: one k-extent)
+//             it touches, then fences once and arrives on the segment's counter (gate-up) or
+//             the tile-row's (down); the last warp to arrive finishes: the activation into the
+//             down kernel's fragments, or the router-weighted combine plus the residual.
+
+constexpr int XW = 8;          // warps per expert CTA
+constexpr int XSTAGES = 3;     // ring stages per warp
+constexpr int MAX_TK = 32;     // columns (token, expert choices) of the decode path
+constexpr int XREC_GU = 2 * 16 * GROUP;  // floats in one gate-up partial (gate, up x 16 rows x 4 cols)
+constexpr int XREC_DN = 16 * GROUP;      // floats in one down partial
+constexpr int XROUTE_WARPS = 4;
+constexpr int XMAX_PIECES = 24;          // pieces per segment (k-extent / piece length)
+
+struct xroute_args {
+    const float *x;       // [T][H]
+    const float *norm_w;  // [H] or null
+    float eps;
+    const float *router;  // [E][H]
+    const float *rbias;   // [E] or null
+    int T, H, E;
+    float *logits;        // [T][E]
+    uint32_t *xfrag;      // [T][H/32][2][4][4]
+    int *status;
+};
+
+// One router row per warp, staged in shared memory by a bulk copy issued before the wait; the
+// activation row is read once per CTA after it. The dot product keeps the fixed order of
+// moearc_matvec_f32 (lane l folds float4 columns l, l + 32, ... in order, then a butterfly).
+__global__ void __launch_bounds__(XROUTE_WARPS * 32) k_xroute(xroute_args a) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    __shared__ __align__(8) uint64_t bar[XROUTE_WARPS];
+    __shared__ float red[XROUTE_WARPS];
+    const int trace_row = (int)blockIdx.x;
+    (void)trace_row;
+    TRACE(0);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int H = a.H, n4 = H / 4;
+    float *wrow = reinterpret_cast<float *>(smem) + (size_t)warp * H;
+    float *xs = reinterpret_cast<float *>(smem) + (size_t)XROUTE_WARPS * H;
+    const int e0 = blockIdx.x * XROUTE_WARPS + warp;
+    const int nw = gridDim.x * XROUTE_WARPS;
+    if (lane == 0) {
+        mbar_init(&bar[warp], 1);
+        fence_mbar_init();
+        if (e0 < a.E) {
+            mbar_expect_tx(&bar[warp], (unsigned)(H * 4));
+            bulk_g2s(wrow, a.router + (size_t)e0 * H, (unsigned)(H * 4), &bar[warp]);
+        }
+    }
+    __syncwarp();
+    pdl_trigger();
+    pdl_wait();
+    TRACE(1);
+    bool have_row = true;
+    for (int t = 0; t < a.T; ++t) {
+        // the token's activation (normalised when routing rmsnorm(x) * norm_w)
+        const float4 *xr = reinterpret_cast<const float4 *>(a.x + (size_t)t * H);
+        float ss = 0.f;
+        for (int c = threadIdx.x; c < n4; c += XROUTE_WARPS * 32) {
+            const float4 v = __ldcg(xr + c);
+            reinterpret_cast<float4 *>(xs)[c] = v;
+            ss = fmaf(v.x, v.x, fmaf(v.y, v.y, fmaf(v.z, v.z, fmaf(v.w, v.w, ss))));
+        }
+        if (a.norm_w) {
+            ss = warp_sum(ss);
+            if (lane == 0) red[warp] = ss;
+            __syncthreads();
+            float tot = 0.f;
+            for (int w = 0; w < XROUTE_WARPS; ++w) tot += red[w];
+            const float s = 1.0f / sqrtf(tot / (float)H + a.eps);
+            for (int c = threadIdx.x; c < n4; c += XROUTE_WARPS * 32) {
+                float4 v = reinterpret_cast<float4 *>(xs)[c];
+                const float4 n = __ldg(reinterpret_cast<const float4 *>(a.norm_w) + c);
+                v = make_float4((v.x * s) * n.x, (v.y * s) * n.y, (v.z * s) * n.z, (v.w * s) * n.w);
+                reinterpret_cast<float4 *>(xs)[c] = v;
+            }
+        }
+        __syncthreads();
+        for (int e = e0; e < a.E; e += nw) {
+            const float *w = wrow;
+            if (e != e0) {
+                // more experts than warps: the row comes straight from global memory
+                w = a.router + (size_t)e * H;
+            } else if (t == 0) {
+                have_row = mbar_wait(&bar[warp], 0, a.status);
+            }
+            if (!have_row && e == e0) continue;
+            float acc = 0.f;
+            for (int c = lane; c < n4; c += 32) {
+                const float4 wv = (e == e0) ? reinterpret_cast<const float4 *>(w)[c] : __ldg(reinterpret_cast<const float4 *>(w) + c);
+                const float4 xv = reinterpret_cast<const float4 *>(xs)[c];
+                acc = fmaf(wv.x, xv.x, acc);
+                acc = fmaf(wv.y, xv.y, acc);
+                acc = fmaf(wv.z, xv.z, acc);
+                acc = fmaf(wv.w, xv.w, acc);
+            }
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+            if (lane == 0) a.logits[(size_t)t * a.E + e] = a.rbias ? acc + a.rbias[e] : acc;
+        }
+        // B fragments of this token: [block][part][q][j] = pair (x[32b+4q+j], x[32b+4q+16+j])
+        const int nblk = H / 32;
+        for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < nblk * 16; i += gridDim.x * blockDim.x) {
+            const int j = i & 3, q = (i >> 2) & 3, b = i >> 4;
+            uint32_t hi, lo;
+            split_f16x2(xs[32 * b + 4 * q + j], xs[32 * b + 4 * q + 16 + j], hi, lo);
+            a.xfrag[((((size_t)t * nblk + b) * 2 + 0) * 4 + q) * 4 + j] = hi;
+            a.xfrag[((((size_t)t * nblk + b) * 2 + 1) * 4 + q) * 4 + j] = lo;
+        }
+        __syncthreads();
+    }
+    // a row copy that was issued and never waited for (no tokens) must land before exit
+    if (a.T == 0 && lane == 0 && e0 < a.E) mbar_wait(&bar[warp], 0, a.status);
+    TRACE(2);
+}
+
+// Routing tables of the decode path, in shared memory.
+struct xtab {
+    int G, C;                         // groups, columns (= T * K)
+    int grp_expert[MAX_TK], grp_col0[MAX_TK], grp_ntok[MAX_TK];
+    int col_tok[MAX_TK], col_grp[MAX_TK];
+    int col_of[MAX_TK];               // column of choice i = t * K + m
+    float wts[MAX_TK];                // gating weight of choice i
+    unsigned idx[MAX_TK];             // expert of choice i
+};
+
+// Top-k of one token by one warp (reference.rs:613-640 semantics, as topk_token): k rounds of
+// argmax over the logits held in registers (lower id wins a tie), then the gating weights.
+template <int MAXP>  // logits per lane: E <= 32 MAXP
+__device__ void xtopk_n(const float *logits, int E, int K, int gating, int lane, unsigned *idx, float *wts) {
+    float v[MAXP];
+#pragma unroll
+    for (int i = 0; i < MAXP; ++i) {
+        const int j = lane + 32 * i;
+        v[i] = (j < E) ? __ldcg(logits + j) : -INFINITY;
+    }
+    uint32_t taken = 0;
+    float my_v = -INFINITY;
+    int my_i = 0;
+    for (int r = 0; r < K; ++r) {
+        float bv = -INFINITY;
+        int bi = 0x7FFFFFFF;
+#pragma unroll
+        for (int i = 0; i < MAXP; ++i) {
+            const int j = lane + 32 * i;
+            if (j < E && !(taken & (1u << i)) && (bi == 0x7FFFFFFF || v[i] > bv)) {
+                bv = v[i];
+                bi = j;
+            }
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+            const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+            if (oi != 0x7FFFFFFF && (bi == 0x7FFFFFFF || ov > bv || (ov == bv && oi < bi))) {
+                bv = ov;
+                bi = oi;
+            }
+        }
+        if ((bi & 31) == lane) taken |= 1u << (bi >> 5);
+        if (lane == r) {
+            my_v = bv;
+            my_i = bi;
+        }
+    }
+    const bool mine = lane < K;
+    float w;
+    if (gating == 2) {
+        const float smax = warp_max(mine ? my_v : -INFINITY);
+        const float e = mine ? expf(my_v - smax) : 0.f;
+        w = e / warp_sum(e);
+    } else {
+        float mx = -INFINITY;
+#pragma unroll
+        for (int i = 0; i < MAXP; ++i) mx = fmaxf(mx, v[i]);
+        mx = warp_max(mx);
+        float part = 0.f;
+#pragma unroll
+        for (int i = 0; i < MAXP; ++i)
+            if (lane + 32 * i < E) part += expf(v[i] - mx);
+        const float denom = warp_sum(part);
+        w = mine ? expf(my_v - mx) / denom : 0.f;
+        if (gating == 1) w /= fmaxf(warp_sum(w), 6.103515625e-5f);
+    }
+    if (mine) {
+        idx[lane] = (unsigned)my_i;
+        wts[lane] = w;
+    }
+}
+
+__device__ __forceinline__ void xtopk(const float *logits, int E, int K, int gating, int lane, unsigned *idx, float *wts) {
+    if (E <= 64) xtopk_n<2>(logits, E, K, gating, lane, idx, wts);
+    else if (E <= 128) xtopk_n<4>(logits, E, K, gating, lane, idx, wts);
+    else if (E <= 256) xtopk_n<8>(logits, E, K, gating, lane, idx, wts);
+    else xtopk_n<32>(logits, E, K, gating, lane, idx, wts);
+}
+
+// Every token's top-k (warp t takes tokens t, t + XW, ...), then the tables by warp 0: the
+// columns are the choices sorted by (expert, token) — distinct experts ascending, a slot's
+// tokens in token order — cut into groups of at most GROUP columns of one expert.
+__device__ void xbuild(xtab &tb, const float *logits, int T, int E, int K, int gating, int warp, int lane) {
+    for (int t = warp; t < T; t += XW) xtopk(logits + (size_t)t * E, E, K, gating, lane, tb.idx + t * K, tb.wts + t * K);
+    __syncthreads();
+    if (warp == 0) {
+        const int C = T * K;
+        const bool live = lane < C;
+        const int key = live ? (int)tb.idx[lane] * 64 + lane / K : 0x7FFFFFFF;
+        int rank = 0;
+        for (int j = 0; j < 32; ++j) {
+            const int kj = __shfl_sync(0xffffffffu, key, j);
+            rank += (kj < key);
+        }
+        if (live) {
+            tb.col_of[lane] = rank;
+            tb.col_tok[rank] = lane / K;
+            tb.grp_expert[rank] = (int)tb.idx[lane];  // expert of column `rank`, for now
+        }
+        __syncwarp();
+        const int ex = live ? tb.grp_expert[lane] : -1;
+        const int prev = __shfl_up_sync(0xffffffffu, ex, 1);
+        const bool start = live && (lane == 0 || prev != ex);
+        const unsigned starts = __ballot_sync(0xffffffffu, start);
+        const unsigned le = (lane == 31) ? 0xffffffffu : ((2u << lane) - 1u);
+        const int first = live ? 31 - __clz(starts & le) : 0;  // first column of this expert
+        const bool gstart = live && ((lane - first) % GROUP == 0);
+        const unsigned gs = __ballot_sync(0xffffffffu, gstart);
+        const int g = __popc(gs & le) - 1;
+        __syncwarp();
+        if (live) tb.col_grp[lane] = g;
+        if (gstart) {
+            const unsigned after = gs & ~le;
+            const int nxt = after ? __ffs(after) - 1 : C;
+            // a group ends at the next group start or at the expert's end, whichever is first
+            const unsigned next_exp = starts & ~le;
+            const int exp_end = next_exp ? __ffs(next_exp) - 1 : C;
+            tb.grp_expert[g] = ex;
+            tb.grp_col0[g] = lane;
+            tb.grp_ntok[g] = min(nxt, exp_end) - lane;
+        }
+        if (lane == 0) {
+            tb.G = __popc(gs);
+            tb.C = C;
+        }
+    }
+    __syncthreads();
+}
+
+struct xexp_args {
+    const uint8_t *bank;      // packed gate-up (pairs) or down (tiles)
+    size_t bank_stride;       // bytes per expert
+    int ntr, nkt;             // tile-rows and k-tiles per row of one expert matrix
+    int tile_bytes, elem_bytes;
+    int ch, stage_bytes, ntok_max;
+    int nblk_b;               // B fragment blocks per row (H/32 gate-up, I/32 down)
+    const uint32_t *bsrc;     // xfrag (gate-up, by token) or actfrag (down, by column)
+    const float *logits;
+    int T, E, K, gating;
+    // gate-up epilogue
+    int act;
+    float alpha, limit;
+    uint32_t *actfrag;
+    float *act_out;
+    int I;
+    unsigned *idx_out;
+    float *wts_out;
+    // down epilogue
+    const float *residual;
+    float *out;
+    int H;
+    float *part;
+    unsigned *ctr;
+    int maxc;
+    int *status;
+};
+
+__device__ __forceinline__ int xcta(long P, long NW, long p) { return (int)(((p + 1) * NW - 1) / P); }
+
+template <int WT, int MODE>
+__global__ void __launch_bounds__(XW * 32, 1) k_xexpert(xexp_args a) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    __shared__ __align__(8) uint64_t bars[XW][XSTAGES];
+    __shared__ xtab tb;
+    const int trace_row = (int)blockIdx.x + (MODE == 0 ? 1024 : 2048);
+    (void)trace_row;
+    TRACE(0);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    constexpr int MATS = MODE == 0 ? 2 : 1;
+    if (MODE == 0) {
+        // the logits are the previous kernel's output; release the down kernel, which reads
+        // them before its own wait
+        pdl_wait();
+        pdl_trigger();
+        TRACE(12);
+    }
+    xbuild(tb, a.logits, a.T, a.E, a.K, a.gating, warp, lane);
+    TRACE(1);
+    if (MODE == 0 && blockIdx.x == 0)
+        for (int i = threadIdx.x; i < tb.C; i += blockDim.x) {
+            a.idx_out[i] = tb.idx[i];
+            a.wts_out[i] = tb.wts[i];
+        }
+    // Work: segments (gate-up: group * ntr + tile-row; down: tile-row * G + group), each one
+    // k-extent of nkt elements cut into np pieces of a.ch elements at fixed places. A warp
+    // takes a contiguous run of pieces; every piece leaves its own partial, so the sums do not
+    // depend on how pieces fall to warps (the batch, the grid).
+    const int G = tb.G, nkt = a.nkt, ntr = a.ntr, ch = a.ch;
+    const int np = (nkt + ch - 1) / ch;
+    const long Q = (long)G * ntr * np;
+    const long NW = (long)gridDim.x * XW, gw = (long)blockIdx.x * XW + warp;
+    const long qa = Q * gw / NW, qb = Q * (gw + 1) / NW;
+    uint8_t *ring = smem + (size_t)warp * XSTAGES * a.stage_bytes;
+    const int wmax = ch * a.elem_bytes;  // B region offset inside a stage
+    if (lane == 0) {
+        for (int s = 0; s < XSTAGES; ++s) mbar_init(&bars[warp][s], 1);
+        fence_mbar_init();
+    }
+    __syncwarp();
+    auto piece_len = [&](int j) { return min(ch, nkt - j * ch); };
+    // piece cursor: piece q is index j of segment (group g, tile-row tr); it advances without
+    // division (the issuing lane runs it once per piece while the warp's other lanes wait)
+    struct cur {
+        long q;
+        int j, g, tr;
+    };
+    auto at = [&](long q) {
+        cur c;
+        c.q = q;
+        const long seg = q / np;
+        c.j = (int)(q - seg * np);
+        if (MODE == 0) {
+            c.g = (int)(seg / ntr);
+            c.tr = (int)(seg - (long)c.g * ntr);
+        } else {
+            c.tr = (int)(seg / G);
+            c.g = (int)(seg - (long)c.tr * G);
+        }
+        return c;
+    };
+    auto step = [&](cur &c) {
+        ++c.q;
+        if (++c.j == np) {
+            c.j = 0;
+            if (MODE == 0) {
+                if (++c.tr == ntr) {
+                    c.tr = 0;
+                    ++c.g;
+                }
+            } else if (++c.g == G) {
+                c.g = 0;
+                ++c.tr;
+            }
+        }
+    };
+    auto issue = [&](const cur &c, int stage, bool weights, bool acts) {
+        const int n = piece_len(c.j), kt = c.j * ch;
+        const int ntok = tb.grp_ntok[c.g];
+        uint8_t *st = ring + (size_t)stage * a.stage_bytes;
+        uint64_t *bar = &bars[warp][stage];
+        if (weights) {
+            fence_proxy_async();
+            mbar_expect_tx(bar, (unsigned)(n * a.elem_bytes + ntok * n * 256));
+            bulk_g2s(st, a.bank + (size_t)tb.grp_expert[c.g] * a.bank_stride + (size_t)((c.tr * nkt + kt) * a.elem_bytes),
+                     (unsigned)(n * a.elem_bytes), bar);
+        }
+        if (acts)
+            for (int t = 0; t < ntok; ++t) {
+                const int col = tb.grp_col0[c.g] + t;
+                const int row = MODE == 0 ? tb.col_tok[col] : col;
+                bulk_g2s(st + wmax + t * ch * 256, a.bsrc + (size_t)((row * a.nblk_b + 2 * kt) * 32), (unsigned)(n * 256), bar);
+            }
+    };
+    const cur start = at(qa);
+    cur ic = start;
+    long n_issued = 0;  // lane 0's count
+    if (lane == 0)
+        for (int s = 0; s < XSTAGES && ic.q < qb; ++s) {
+            issue(ic, s, true, MODE == 0);
+            step(ic);
+            ++n_issued;
+        }
+    if (MODE == 1) {
+        // the weights are static and stream now; the activation fragments are the gate-up
+        // kernel's output and follow the wait
+        pdl_trigger();
+        pdl_wait();
+        TRACE(2);
+        if (lane == 0) {
+            cur c = start;
+            for (long s = 0; s < n_issued; ++s) {
+                issue(c, (int)s, false, true);
+                step(c);
+            }
+        }
+    }
+    // consume: lane (r = lane / 4, q = lane % 4) holds rows r, r + 8 of column q; B column
+    // n = lane / 4 is token n / 2, part n % 2
+    const int r = lane >> 2, qd = lane & 3;
+    const int rec = MODE == 0 ? XREC_GU : XREC_DN;
+    cur cc = start;
+    long k = 0, kf = -1;
+    while (cc.q < qb) {
+        const int stage = (int)(k % XSTAGES);
+        if (!mbar_wait(&bars[warp][stage], (unsigned)((k / XSTAGES) & 1), a.status)) {
+            kf = k;
+            break;
+        }
+        if (k < 6) TRACE(3 + k);
+        const int n = piece_len(cc.j);
+        const int ntok = tb.grp_ntok[cc.g];
+        const uint8_t *st = ring + (size_t)stage * a.stage_bytes;
+        const uint32_t *bsm = reinterpret_cast<const uint32_t *>(st + wmax);
+        float acc0[4] = {0.f, 0.f, 0.f, 0.f}, acc1[4] = {0.f, 0.f, 0.f, 0.f};
+        for (int i = 0; i < n; ++i) {
+            uint32_t bfr[2][2][2];
+            load_b(bsm, 2 * ch, i, lane, ntok, bfr);
+            const uint8_t *tile = st + i * a.elem_bytes;
+            tile_mma<WT>(tile, lane, bfr, acc0);
+            if (MATS == 2) tile_mma<WT>(tile + a.tile_bytes, lane, bfr, acc1);
+        }
+        __syncwarp();
+        ++k;
+        if (lane == 0 && ic.q < qb) {
+            issue(ic, stage, true, true);
+            step(ic);
+            ++n_issued;
+        }
+        // the piece's partial: column q = (f16 part + residual part) of rows r and r + 8
+        float *pr = a.part + (size_t)cc.q * rec;  // piece q = segment * np + j
+        if (qd < ntok) {
+            pr[r * GROUP + qd] = acc0[0] + acc0[1];
+            pr[(r + 8) * GROUP + qd] = acc0[2] + acc0[3];
+            if (MATS == 2) {
+                pr[64 + r * GROUP + qd] = acc1[0] + acc1[1];
+                pr[64 + (r + 8) * GROUP + qd] = acc1[2] + acc1[3];
+            }
+        }
+        step(cc);
+    }
+    if (kf >= 0) {
+        // a copy did not complete in time: wait (bounded) for every copy issued, so none lands
+        // after the CTA exits, and finish nothing
+        n_issued = __shfl_sync(0xffffffffu, n_issued, 0);
+        for (long j = kf; j < n_issued; ++j) mbar_wait(&bars[warp][j % XSTAGES], (unsigned)((j / XSTAGES) & 1), a.status);
+        return;
+    }
+    if (qb <= qa) return;
+    TRACE(10);
+    __threadfence();
+    __syncwarp();
+    // arrivals: gate-up one per segment touched; down one per tile-row, counting the segments
+    // of that tile-row this warp touched. The warps on a segment are a contiguous run.
+    auto seg_warps = [&](long s) {
+        return (unsigned)(xcta(Q, NW, (s + 1) * np - 1) - xcta(Q, NW, s * np) + 1);
+    };
+    const int seg_first = (int)(qa / np), seg_last = (int)((qb - 1) / np);
+    const int u_first = MODE == 0 ? seg_first : seg_first / G, u_last = MODE == 0 ? seg_last : seg_last / G;
+    bool mine = false;
+    if (lane <= u_last - u_first) {
+        const int u = u_first + lane;
+        unsigned target = 0, inc = 0;
+        if (MODE == 0) {
+            target = seg_warps(u);
+            inc = 1;
+        } else {
+            for (int gg = 0; gg < G; ++gg) {
+                const int s = u * G + gg;
+                target += seg_warps(s);
+                if (s >= seg_first && s <= seg_last) ++inc;
+            }
+        }
+        const unsigned old = atomicAdd(a.ctr + u, inc);
+        if (old + inc == target) {
+            mine = true;
+            a.ctr[u] = 0;
+        }
+    }
+    unsigned done_mask = __ballot_sync(0xffffffffu, mine);
+    if (!done_mask) return;
+    __threadfence();
+    TRACE(11);
+    // a segment's pieces summed in piece order; the loads are all issued before the adds
+    auto sum_seg = [&](int s, int off) {
+        const float *pp = a.part + (size_t)s * np * rec + off;
+        float t[XMAX_PIECES];
+#pragma unroll
+        for (int j = 0; j < XMAX_PIECES; ++j) t[j] = (j < np) ? __ldcg(pp + (size_t)j * rec) : 0.f;
+        float v = 0.f;
+#pragma unroll
+        for (int j = 0; j < XMAX_PIECES; ++j)
+            if (j < np) v += t[j];
+        return v;
+    };
+    while (done_mask) {
+        const int u = u_first + __ffs(done_mask) - 1;
+        done_mask &= done_mask - 1;
+        if (MODE == 0) {
+            // gate-up segment (group g, tile-row tr): the activation of 16 rows x ntok columns
+            const int g = u / ntr, tr = u % ntr;
+            const int ntok = tb.grp_ntok[g], col0 = tb.grp_col0[g];
+            const int nblk_i = a.I / 32;
+            for (int e = lane; e < 16 * ntok; e += 32) {
+                const int rr = e & 15, t = e >> 4;
+                const float gs = sum_seg(u, rr * GROUP + t), us = sum_seg(u, 64 + rr * GROUP + t);
+                const int col = col0 + t, row = tr * 16 + rr;
+                const float v = act_fn(a.act, gs, us, a.alpha, a.limit);
+                a.act_out[(size_t)col * a.I + row] = v;
+                const __half hh = __float2half_rn(v);
+                const __half hl = __float2half_rn(v - __half2float(hh));
+                // element el of block blk sits in pair j = el & 3 of lane q = (el & 15) >> 2, in
+                // the low half for el < 16 and the high half for el >= 16
+                const int blk = row / 32, el = row % 32;
+                const int qq = (el & 15) >> 2, jj = el & 3, half = el >> 4;
+                const size_t ihi = ((((size_t)col * nblk_i + blk) * 2 + 0) * 4 + qq) * 4 + jj;
+                const size_t ilo = ((((size_t)col * nblk_i + blk) * 2 + 1) * 4 + qq) * 4 + jj;
+                reinterpret_cast<uint16_t *>(a.actfrag + ihi)[half] = __half_as_ushort(hh);
+                reinterpret_cast<uint16_t *>(a.actfrag + ilo)[half] = __half_as_ushort(hl);
+            }
+        } else {
+            // down tile-row tr: per token, the router-weighted sum over its k experts in router
+            // order (moe.rs:2395-2421), plus the residual
+            const int tr = u;
+            for (int e = lane; e < a.T * 16; e += 32) {
+                const int t = e >> 4, rr = e & 15;
+                float acc = 0.f;
+                for (int m = 0; m < a.K; ++m) {
+                    const int col = tb.col_of[t * a.K + m];
+                    const int g = tb.col_grp[col];
+                    const float o = sum_seg(tr * G + g, rr * GROUP + (col - tb.grp_col0[g]));
+                    acc = fmaf(tb.wts[t * a.K + m], o, acc);
+                }
+                const size_t o = (size_t)t * a.H + tr * 16 + rr;
+                a.out[o] = a.residual ? a.residual[o] + acc : acc;
+            }
+        }
+    }
     TRACE(31);
 }
 
@@ -845,6 +1409,24 @@ moearc_x_moe *moearc_x_moe_create(moearc_ctx *c, const moearc_x_moe_desc *d) {
         return nullptr;
     }
 
+    // decode path plan: one CTA per SM (fewer when a warp would get under two elements), a
+    // ring of XSTAGES stages per warp, each ch elements and their B fragments
+    m->xpath = TK <= MAX_TK && m->T_max <= 32;
+    const long x_pmin = (long)m->K * m->ntr_i * m->nkt_h;  // fewest elements of a launch (both modes)
+    m->x_grid = (int)std::max(1L, std::min<long>(c->sm_count, x_pmin / (XW * 2 * 5)));
+    m->x_ntok = tok_group;
+    m->x_ch_gu = 3;
+    m->x_ch_dn = 5;
+    m->x_stage_gu = round128((long)m->x_ch_gu * 2 * m->tile_bytes + (long)m->x_ntok * m->x_ch_gu * 256);
+    m->x_stage_dn = round128((long)m->x_ch_dn * m->tile_bytes + (long)m->x_ntok * m->x_ch_dn * 256);
+    m->x_maxc = 0;  // unused: partials are per piece
+    m->x_route_grid = (m->E + XROUTE_WARPS - 1) / XROUTE_WARPS;
+    m->x_route_smem = (XROUTE_WARPS + 1) * m->H * 4;
+    if (m->xpath && (XW * XSTAGES * std::max(m->x_stage_gu, m->x_stage_dn) > 200 * 1024 || m->x_route_smem > 200 * 1024 ||
+                     (m->nkt_h + m->x_ch_gu - 1) / m->x_ch_gu > XMAX_PIECES ||
+                     (m->nkt_i + m->x_ch_dn - 1) / m->x_ch_dn > XMAX_PIECES))
+        m->xpath = false;
+
     // one scratch allocation
     size_t off = 0;
     auto take = [&](size_t bytes) {
@@ -862,6 +1444,12 @@ moearc_x_moe *moearc_x_moe_create(moearc_ctx *c, const moearc_x_moe_desc *d) {
     const size_t n_ctr = 1 + (size_t)TK * m->ntr_i + m->ntr_h;
     const size_t o_ctr = take(sizeof(unsigned) * n_ctr);
     const size_t o_st = take(sizeof(int));
+    const size_t x_segs_gu = (size_t)TK * m->ntr_i, x_segs_dn = (size_t)m->ntr_h * TK;
+    const size_t np_gu = (m->nkt_h + m->x_ch_gu - 1) / m->x_ch_gu, np_dn = (m->nkt_i + m->x_ch_dn - 1) / m->x_ch_dn;
+    const size_t o_xpg = take(m->xpath ? sizeof(float) * x_segs_gu * np_gu * XREC_GU : 0);
+    const size_t o_xpd = take(m->xpath ? sizeof(float) * x_segs_dn * np_dn * XREC_DN : 0);
+    const size_t o_xcg = take(m->xpath ? sizeof(unsigned) * x_segs_gu : 0);
+    const size_t o_xcd = take(m->xpath ? sizeof(unsigned) * m->ntr_h : 0);
     m->mem_bytes = off;
     if (cudaMalloc(&m->mem, off) != cudaSuccess) {
         cudaGetLastError();
@@ -878,11 +1466,20 @@ moearc_x_moe *moearc_x_moe_create(moearc_ctx *c, const moearc_x_moe_desc *d) {
     m->ctr = reinterpret_cast<unsigned *>(b + o_ctr);
     m->status = reinterpret_cast<int *>(b + o_st);
     m->act_f32 = reinterpret_cast<float *>(b + o_act);
+    m->x_part_gu = reinterpret_cast<float *>(b + o_xpg);
+    m->x_part_dn = reinterpret_cast<float *>(b + o_xpd);
+    m->x_ctr_gu = reinterpret_cast<unsigned *>(b + o_xcg);
+    m->x_ctr_dn = reinterpret_cast<unsigned *>(b + o_xcd);
     cudaMemsetAsync(m->mem, 0, off, c->stream);
     // per-kernel attribute shared by every layer object: the most any of them may use
     const int smem_attr = 226 * 1024;
     if (cudaFuncSetAttribute(k_moe_rows<39>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_attr) != cudaSuccess ||
         cudaFuncSetAttribute(k_moe_rows<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_attr) != cudaSuccess ||
+        cudaFuncSetAttribute(k_xexpert<39, 0>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024) != cudaSuccess ||
+        cudaFuncSetAttribute(k_xexpert<39, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024) != cudaSuccess ||
+        cudaFuncSetAttribute(k_xexpert<2, 0>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024) != cudaSuccess ||
+        cudaFuncSetAttribute(k_xexpert<2, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024) != cudaSuccess ||
+        cudaFuncSetAttribute(k_xroute, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024) != cudaSuccess ||
         cudaStreamSynchronize(c->stream) != cudaSuccess) {
         cudaGetLastError();
         cudaFree(m->mem);
@@ -951,6 +1548,68 @@ int moe_forward_impl(moearc_x_moe *m, const float *x, unsigned n_tokens, const f
     const int T = (int)n_tokens;
     const tab_view tab = make_tab(m);
     launch_scope ls(c, "moe_forward", (unsigned long)m->H, (unsigned)T);
+
+    if (m->xpath) {
+        xroute_args xr{x, norm_w, eps, router_w, router_b, T, m->H, m->E, m->logits, m->xfrag, m->status};
+        if (launch_pdl(k_xroute, dim3(m->x_route_grid), dim3(XROUTE_WARPS * 32), (size_t)m->x_route_smem, c->stream,
+                       xr) != cudaSuccess)
+            return ERR;
+        mark(3);
+        xexp_args xa{};
+        xa.bank = static_cast<const uint8_t *>(gateup_packed);
+        xa.bank_stride = (size_t)2 * m->ntr_i * m->nkt_h * m->tile_bytes;
+        xa.ntr = m->ntr_i;
+        xa.nkt = m->nkt_h;
+        xa.tile_bytes = m->tile_bytes;
+        xa.elem_bytes = 2 * m->tile_bytes;
+        xa.ch = m->x_ch_gu;
+        xa.stage_bytes = m->x_stage_gu;
+        xa.ntok_max = m->x_ntok;
+        xa.nblk_b = m->H / 32;
+        xa.bsrc = m->xfrag;
+        xa.logits = m->logits;
+        xa.T = T;
+        xa.E = m->E;
+        xa.K = m->K;
+        xa.gating = m->gating;
+        xa.act = m->act;
+        xa.alpha = m->alpha;
+        xa.limit = m->limit;
+        xa.actfrag = m->actfrag;
+        xa.act_out = m->act_f32;
+        xa.I = m->I;
+        xa.idx_out = m->idx;
+        xa.wts_out = m->wts;
+        xa.H = m->H;
+        xa.part = m->x_part_gu;
+        xa.ctr = m->x_ctr_gu;
+        xa.maxc = m->x_maxc;
+        xa.status = m->status;
+        const bool mx = m->wtype == T_MXFP4;
+        if (launch_pdl(mx ? k_xexpert<39, 0> : k_xexpert<2, 0>, dim3(m->x_grid), dim3(XW * 32),
+                       (size_t)XW * XSTAGES * m->x_stage_gu, c->stream, xa) != cudaSuccess)
+            return ERR;
+        mark(4);
+        xexp_args xd = xa;
+        xd.bank = static_cast<const uint8_t *>(down_packed);
+        xd.bank_stride = (size_t)m->ntr_h * m->nkt_i * m->tile_bytes;
+        xd.ntr = m->ntr_h;
+        xd.nkt = m->nkt_i;
+        xd.elem_bytes = m->tile_bytes;
+        xd.ch = m->x_ch_dn;
+        xd.stage_bytes = m->x_stage_dn;
+        xd.nblk_b = m->I / 32;
+        xd.bsrc = m->actfrag;
+        xd.residual = residual;
+        xd.out = out;
+        xd.part = m->x_part_dn;
+        xd.ctr = m->x_ctr_dn;
+        if (launch_pdl(mx ? k_xexpert<39, 1> : k_xexpert<2, 1>, dim3(m->x_grid), dim3(XW * 32),
+                       (size_t)XW * XSTAGES * m->x_stage_dn, c->stream, xd) != cudaSuccess)
+            return ERR;
+        mark(5);
+        return ls.finish();
+    }
 
     route_args ra{x, norm_w, eps, router_w, router_b, T, m->H, m->E, m->K, m->gating, m->logits, m->idx,
                   m->wts, m->xfrag, tab, m->ctr};

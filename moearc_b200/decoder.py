@@ -148,10 +148,11 @@ class Decoder:
 
 def unpack_dense(packed: np.ndarray, n_rows: int, n_cols: int) -> np.ndarray:
     """Invert the packed bf16 tile layout (dense.cuh) back to a row-major [n_rows][n_cols] bf16
-    matrix: tile (tr, tk) = 16 rows x 64 cols; lane l = 4r + q; for each 16-column sub-block s
-    four u32: (row r, cols 16s+2q..+1), (row r+8, same), (row r, 16s+2q+8..+9), (row r+8, same)."""
+    matrix: tile (tr, tk) = 16 rows x 64 cols; inside it, for each 16-column sub-block s, lane
+    l = 4r + q holds four u32: (row r, cols 16s+2q..+1), (row r+8, same), (row r,
+    16s+2q+8..+9), (row r+8, same)."""
     ntr, nkt = n_rows // 16, n_cols // 64
-    p = packed.view(np.uint16).reshape(ntr, nkt, 8, 4, 4, 4, 2)  # tr, tk, r, q, s, reg, half
+    p = packed.view(np.uint16).reshape(ntr, nkt, 4, 8, 4, 4, 2)  # tr, tk, s, r, q, reg, half
     w = np.empty((ntr, 16, nkt, 64), np.uint16)
     offs = ((0, 0), (8, 0), (0, 8), (8, 8))  # (row, col) offset of register reg
     for r in range(8):
@@ -159,7 +160,7 @@ def unpack_dense(packed: np.ndarray, n_rows: int, n_cols: int) -> np.ndarray:
             for s in range(4):
                 for reg, (ro, co) in enumerate(offs):
                     for half in range(2):
-                        w[:, r + ro, :, 16 * s + 2 * q + co + half] = p[:, :, r, q, s, reg, half]
+                        w[:, r + ro, :, 16 * s + 2 * q + co + half] = p[:, :, s, r, q, reg, half]
     return w.reshape(n_rows, n_cols)
 
 
@@ -168,12 +169,12 @@ def pack_dense(w: np.ndarray) -> np.ndarray:
     n_rows, n_cols = w.shape
     ntr, nkt = n_rows // 16, n_cols // 64
     v = w.reshape(ntr, 16, nkt, 64)
-    p = np.empty((ntr, nkt, 8, 4, 4, 4, 2), np.uint16)
+    p = np.empty((ntr, nkt, 4, 8, 4, 4, 2), np.uint16)
     offs = ((0, 0), (8, 0), (0, 8), (8, 8))
     for r in range(8):
         for q in range(4):
             for s in range(4):
                 for reg, (ro, co) in enumerate(offs):
                     for half in range(2):
-                        p[:, :, r, q, s, reg, half] = v[:, r + ro, :, 16 * s + 2 * q + co + half]
+                        p[:, :, s, r, q, reg, half] = v[:, r + ro, :, 16 * s + 2 * q + co + half]
     return p.ravel()

@@ -139,3 +139,31 @@ def test_qwen3_shaped_q4_0_layer(ctx):
         worst = max(worst, rel_err(got[t], want))
     print(f"qwen3 Q4_0: max rel err {worst:.3e} (bound 1e-4)")
     assert worst <= 1e-4
+
+
+@pytest.mark.parametrize("wtype", [O.MXFP4, O.Q4_0])
+def test_decode_path_is_batch_invariant_and_matches_the_oracle(ctx, wtype):
+    """Up to 32 (token, expert) columns take the decode path (per-CTA routing tables, pieces
+    of fixed k-extent): a token's output is bit-identical whether it is decoded alone or among
+    eight, every token matches the oracle, and the residual lands on top."""
+    H, I, E, k, T = 2880, 1024, 64, 4, 8
+    layer, host = make_layer(ctx, H, I, E, k, 0, 1, wtype, T, 0xDEC0DE)
+    rw = ctx.upload_new(host[3])
+    x = O.synth_normal_f32(0xDEC1, T * H, 1.0)
+    res = O.synth_normal_f32(0xDEC2, T * H, 1.0)
+    out = ctx.alloc_n(np.float32, T * H)
+    layer.forward(ctx.upload_new(x), T, rw, out, residual=ctx.upload_new(res))
+    got = ctx.download(out, np.float32, T * H).reshape(T, H)
+    assert layer.status() == 0
+    idx = layer.buffer(0, np.uint32, T * k).reshape(T, k)
+    worst = 0.0
+    for t in range(T):
+        xt = x[t * H:(t + 1) * H].copy()
+        o1 = ctx.alloc_n(np.float32, H)
+        layer.forward(ctx.upload_new(xt), 1, rw, o1, residual=ctx.upload_new(res[t * H:(t + 1) * H].copy()))
+        assert np.array_equal(ctx.download(o1, np.float32, H), got[t]), t
+        want, widx, _ = oracle_token(H, I, E, k, 0, 1, wtype, host, xt)
+        assert np.array_equal(idx[t], widx)
+        worst = max(worst, rel_err(got[t] - res[t * H:(t + 1) * H], want))
+    print(f"decode path wtype={wtype}: max rel err {worst:.3e} over {T} tokens (bound 1e-4)")
+    assert worst <= 1e-4
