@@ -41,6 +41,21 @@ METRIC = "MoE decode tok/s at gpt-oss-120b shape; expert-GEMM HBM GB/s vs 8 TB/s
 UNIT = "tok/s"
 
 
+def gate_up_traffic() -> float | None:
+    """DRAM read + write bytes of one gate-up launch, from the committed ncu capture summary
+    (profiles/moe_and_dense_kernels_gpt_oss_120b_1layer.md, the gate-up row); None if absent."""
+    import re
+    p = os.path.join(ROOT, "profiles", "moe_and_dense_kernels_gpt_oss_120b_1layer.md")
+    if not os.path.exists(p):
+        return None
+    for line in open(p):
+        if line.startswith("| `k_xexpert<39,0>`"):
+            m = re.search(r"\| ([\d.]+) MB / ([\d.]+) MB \|", line)
+            if m:
+                return (float(m.group(1)) + float(m.group(2))) * 1e6
+    return None
+
+
 def load_peaks() -> tuple[float, str]:
     p = os.path.join(ROOT, "MEASURED_PEAKS.json")
     if os.path.exists(p):
@@ -326,7 +341,8 @@ def main() -> None:
         "config": config,
         "roofline": {"bound": "hbm", "kernel": "moe gate-up grouped GEMV (MXFP4, tensor cores)",
                      "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
-                     "peak_kind": peak_kind, "traffic": None,
+                     "peak_kind": peak_kind, "traffic": gate_up_traffic(),
+                     "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum, profiles/",
                      "bytes_per_launch": gu_bytes, "avg_launch_ms": gu_ms,
                      "frac_of_8tbs": achieved / 8000.0},
         "step_hbm": {"algorithmic_bytes": step_bytes, "achieved_gbs": step_gbs, "frac": step_gbs / peak,

@@ -55,6 +55,10 @@ struct moearc_x_moe {
     int x_grid, x_route_grid, x_route_smem, x_ch_gu, x_ch_dn, x_stage_gu, x_stage_dn, x_ntok, x_maxc;
     float *x_part_gu, *x_part_dn;
     unsigned *x_ctr_gu, *x_ctr_dn;
+    // the fused decode kernel (k_moe_fused): one cooperative launch per layer
+    bool fused;
+    int f_grid, f_stage, f_smem, f_bsmem;
+    unsigned *f_ready, *f_bar;
     // device scratch (one allocation)
     void *mem;
     size_t mem_bytes;
@@ -1235,6 +1239,7 @@ __global__ void __launch_bounds__(XW * 32, 1) k_xexpert(xexp_args a) {
     // arrivals: gate-up one per segment touched; down one per tile-row, counting the segments
     // of that tile-row this warp touched. The warps on a segment are a contiguous run.
     auto seg_warps = [&](long s) {
+        if (Q < NW) return (unsigned)np;  // fewer pieces than warps: one warp per piece
         return (unsigned)(xcta(Q, NW, (s + 1) * np - 1) - xcta(Q, NW, s * np) + 1);
     };
     const int seg_first = (int)(qa / np), seg_last = (int)((qb - 1) / np);
@@ -1318,6 +1323,509 @@ __global__ void __launch_bounds__(XW * 32, 1) k_xexpert(xexp_args a) {
             }
         }
     }
+    TRACE(31);
+}
+
+// ---- the decode path, fused: route, gate-up and down in one cooperative launch -------------
+//
+// One CTA per SM, all resident at once (cooperative launch), so CTAs may wait on one another:
+//   route    router rows spread one per warp over the grid (the lane order of moearc_matvec_f32,
+//            so the logits match the oracle bit for bit); the activation's gate-up B fragments
+//            are built in every CTA's shared memory (or, past two tokens, in global memory);
+//            then a grid barrier
+//   tables   every CTA derives the top-k and the slot tables from the logits (xbuild)
+//   stream   every warp takes an equal run of gate-up pieces and then of down pieces and
+//            streams both through one ring of bulk copies, so down weights are in flight while
+//            gate-up finishes. Gate-up pieces leave partials; the last warp on a segment
+//            applies the activation, writes the down kernel's fragments and bumps the ready
+//            count of the down k-range those rows feed. A down piece waits (bounded) for its
+//            k-range's count, copies its fragments from global memory and multiplies; the last
+//            warp on a tile-row combines in router order and adds the residual.
+
+struct xfused_args {
+    const float *x;        // [T][H]
+    const float *norm_w;   // [H] or null
+    float eps;
+    const float *router;   // [E][H]
+    const float *rbias;    // [E] or null
+    int T, H, E, K, gating, I;
+    float *logits;         // [T][E]
+    const uint8_t *gu_bank, *dn_bank;
+    size_t gu_stride, dn_stride;
+    int ntr_i, nkt_h, ntr_h, nkt_i, tile_bytes;
+    int ch_gu, ch_dn, stage_bytes, ntok_max, b_smem;
+    uint32_t *xfrag;       // [T][H/32][2][4][4], used when !b_smem
+    int act;
+    float alpha, limit;
+    uint32_t *actfrag;     // [col][I/32][2][4][4]
+    float *act_out;        // [col][I]
+    unsigned *idx_out;
+    float *wts_out;
+    const float *residual;
+    float *out;
+    float *part_gu, *part_dn;
+    unsigned *ctr_gu, *ctr_dn, *ready, *bar;
+    int *status;
+};
+
+__device__ __forceinline__ unsigned ld_acquire_u32(const unsigned *p) {
+    unsigned v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+__device__ __forceinline__ unsigned long long gtimer() {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+constexpr unsigned long long XWAIT_NS = 200000000ull;  // a wait on other CTAs gives up after 0.2 s
+
+// Grid barrier of a cooperative launch (arrivals counter + generation word, reusable across
+// launches): every CTA's writes before it are visible to every CTA after it. A CTA that waits
+// longer than XWAIT_NS sets STATUS_WAIT_TIMEOUT and goes on.
+__device__ void grid_barrier(unsigned *bar, int *status) {
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        const unsigned gen = ld_acquire_u32(bar + 1);
+        __threadfence();
+        if (atomicAdd(bar, 1u) == gridDim.x - 1) {
+            atomicExch(bar, 0u);
+            __threadfence();
+            atomicAdd(bar + 1, 1u);
+        } else {
+            const unsigned long long t0 = gtimer();
+            while (ld_acquire_u32(bar + 1) == gen) {
+                if (gtimer() - t0 > XWAIT_NS) {
+                    atomicOr(status, STATUS_WAIT_TIMEOUT);
+                    break;
+                }
+                __nanosleep(32);
+            }
+        }
+        __threadfence();
+    }
+    __syncthreads();
+}
+
+// Wait (one lane) until *p >= target; false (and STATUS_WAIT_TIMEOUT) after XWAIT_NS.
+__device__ bool wait_count(const unsigned *p, unsigned target, int *status) {
+    if (ld_acquire_u32(p) >= target) return true;
+    const unsigned long long t0 = gtimer();
+    while (ld_acquire_u32(p) < target) {
+        if (gtimer() - t0 > XWAIT_NS) {
+            atomicOr(status, STATUS_WAIT_TIMEOUT);
+            return false;
+        }
+        __nanosleep(64);
+    }
+    return true;
+}
+
+// B fragments of one k-tile for lane (n = lane / 4, q = lane % 4) from a fragment row
+// [block][part][q][4 x u32] (null: a column past the group, zeros)
+__device__ __forceinline__ void load_b_row(const uint32_t *brow, int kt, int lane, uint32_t (&bfr)[2][2][2]) {
+    const int part = (lane >> 2) & 1, q = lane & 3;
+    if (brow) {
+#pragma unroll
+        for (int blk = 0; blk < 2; ++blk) {
+            const uint4 v = *reinterpret_cast<const uint4 *>(brow + ((2 * kt + blk) * 2 + part) * 16 + q * 4);
+            bfr[blk][0][0] = v.x;
+            bfr[blk][0][1] = v.y;
+            bfr[blk][1][0] = v.z;
+            bfr[blk][1][1] = v.w;
+        }
+    } else {
+#pragma unroll
+        for (int blk = 0; blk < 2; ++blk) bfr[blk][0][0] = bfr[blk][0][1] = bfr[blk][1][0] = bfr[blk][1][1] = 0u;
+    }
+}
+
+template <int WT>
+__global__ void __launch_bounds__(XW * 32, 1) k_moe_fused(xfused_args a) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    __shared__ __align__(8) uint64_t bars[XW][XSTAGES];
+    __shared__ xtab tb;
+    __shared__ float red[XW];
+    const int trace_row = (int)blockIdx.x + 1024;
+    (void)trace_row;
+    TRACE(0);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int H = a.H, n4 = H / 4, nblk_h = H / 32, nblk_i = a.I / 32;
+    const long NW = (long)gridDim.x * XW, gw = (long)blockIdx.x * XW + warp;
+    const int chmax = max(a.ch_gu, a.ch_dn);
+    uint8_t *ring = smem + (size_t)warp * XSTAGES * a.stage_bytes;
+    const size_t ring_all = (size_t)XW * XSTAGES * a.stage_bytes;
+    uint32_t *bbuf = reinterpret_cast<uint32_t *>(smem + ring_all) + (size_t)warp * a.ntok_max * chmax * 64;
+    uint32_t *xf = reinterpret_cast<uint32_t *>(smem + ring_all + (size_t)XW * a.ntok_max * chmax * 256);
+    float *xs = reinterpret_cast<float *>(smem);  // the route phase only: aliases the ring
+    if (lane == 0) {
+        for (int s = 0; s < XSTAGES; ++s) mbar_init(&bars[warp][s], 1);
+        fence_mbar_init();
+    }
+    // router rows of this warp: e with floor(e * NW / E) == gw; fetch them to L2 now (static)
+    const int e_lo = (int)((gw * a.E + NW - 1) / NW), e_hi = (int)(((gw + 1) * a.E + NW - 1) / NW);
+    if (lane == 0)
+        for (int e = e_lo; e < e_hi; ++e) bulk_prefetch_l2(a.router + (size_t)e * H, (unsigned)(H * 4));
+    const int np_dn = (a.nkt_i + a.ch_dn - 1) / a.ch_dn;
+    if (blockIdx.x == 0)
+        for (int i = threadIdx.x; i < a.K * a.T * np_dn; i += blockDim.x) a.ready[i] = 0u;
+    pdl_wait();
+    TRACE(1);
+
+    // ---- route ----
+    for (int t = 0; t < a.T; ++t) {
+        const float4 *xr = reinterpret_cast<const float4 *>(a.x + (size_t)t * H);
+        float ss = 0.f;
+        for (int c = threadIdx.x; c < n4; c += XW * 32) {
+            const float4 v = __ldcg(xr + c);
+            reinterpret_cast<float4 *>(xs)[c] = v;
+            ss = fmaf(v.x, v.x, fmaf(v.y, v.y, fmaf(v.z, v.z, fmaf(v.w, v.w, ss))));
+        }
+        if (a.norm_w) {
+            ss = warp_sum(ss);
+            if (lane == 0) red[warp] = ss;
+            __syncthreads();
+            float tot = 0.f;
+            for (int w = 0; w < XW; ++w) tot += red[w];
+            const float s = 1.0f / sqrtf(tot / (float)H + a.eps);
+            for (int c = threadIdx.x; c < n4; c += XW * 32) {
+                float4 v = reinterpret_cast<float4 *>(xs)[c];
+                const float4 n = __ldg(reinterpret_cast<const float4 *>(a.norm_w) + c);
+                v = make_float4((v.x * s) * n.x, (v.y * s) * n.y, (v.z * s) * n.z, (v.w * s) * n.w);
+                reinterpret_cast<float4 *>(xs)[c] = v;
+            }
+        }
+        __syncthreads();
+        for (int e = e_lo; e < e_hi; ++e) {
+            const float4 *wr = reinterpret_cast<const float4 *>(a.router + (size_t)e * H);
+            float acc = 0.f;
+            for (int c = lane; c < n4; c += 32) {
+                const float4 wv = __ldg(wr + c);
+                const float4 xv = reinterpret_cast<const float4 *>(xs)[c];
+                acc = fmaf(wv.x, xv.x, acc);
+                acc = fmaf(wv.y, xv.y, acc);
+                acc = fmaf(wv.z, xv.z, acc);
+                acc = fmaf(wv.w, xv.w, acc);
+            }
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+            if (lane == 0) a.logits[(size_t)t * a.E + e] = a.rbias ? acc + a.rbias[e] : acc;
+        }
+        // gate-up B fragments: [block][part][q][j] = pair (x[32b+4q+j], x[32b+4q+16+j])
+        if (a.b_smem) {
+            for (int i = threadIdx.x; i < nblk_h * 16; i += blockDim.x) {
+                const int j = i & 3, q = (i >> 2) & 3, b = i >> 4;
+                uint32_t hi, lo;
+                split_f16x2(xs[32 * b + 4 * q + j], xs[32 * b + 4 * q + 16 + j], hi, lo);
+                xf[(((size_t)t * nblk_h + b) * 2 + 0) * 16 + q * 4 + j] = hi;
+                xf[(((size_t)t * nblk_h + b) * 2 + 1) * 16 + q * 4 + j] = lo;
+            }
+        } else {
+            for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < nblk_h * 16; i += gridDim.x * blockDim.x) {
+                const int j = i & 3, q = (i >> 2) & 3, b = i >> 4;
+                uint32_t hi, lo;
+                split_f16x2(xs[32 * b + 4 * q + j], xs[32 * b + 4 * q + 16 + j], hi, lo);
+                a.xfrag[(((size_t)t * nblk_h + b) * 2 + 0) * 16 + q * 4 + j] = hi;
+                a.xfrag[(((size_t)t * nblk_h + b) * 2 + 1) * 16 + q * 4 + j] = lo;
+            }
+        }
+        __syncthreads();
+    }
+    grid_barrier(a.bar, a.status);
+    // every CTA is resident and past the route: the next kernel may launch
+    pdl_trigger();
+    TRACE(2);
+
+    // ---- tables ----
+    xbuild(tb, a.logits, a.T, a.E, a.K, a.gating, warp, lane);
+    TRACE(3);
+    if (blockIdx.x == 0)
+        for (int i = threadIdx.x; i < tb.C; i += blockDim.x) {
+            a.idx_out[i] = tb.idx[i];
+            a.wts_out[i] = tb.wts[i];
+        }
+    const int G = tb.G;
+    const int np_gu = (a.nkt_h + a.ch_gu - 1) / a.ch_gu;
+    const long Qg = (long)G * a.ntr_i * np_gu, Qd = (long)a.ntr_h * G * np_dn;
+    const long ga = Qg * gw / NW, gb = Qg * (gw + 1) / NW;  // this warp's gate-up pieces
+    const long da = Qd * gw / NW, db = Qd * (gw + 1) / NW;  // and down pieces
+    const long n_gu = gb - ga, n_all = n_gu + (db - da);
+
+    // piece cursor over the warp's gate-up run, then its down run: piece q of a run is index j
+    // of segment (g, tr) — gate-up segments (group, tile-row of I), down (tile-row of H, group)
+    struct cur {
+        long q;      // position in the warp's sequence
+        int j, g, tr;
+        bool dn;
+    };
+    auto locate = [&](long k) {
+        cur c;
+        c.q = k;
+        c.dn = k >= n_gu;
+        const long p = c.dn ? da + (k - n_gu) : ga + k;
+        const int np = c.dn ? np_dn : np_gu;
+        const long seg = p / np;
+        c.j = (int)(p - seg * np);
+        if (!c.dn) {
+            c.g = (int)(seg / a.ntr_i);
+            c.tr = (int)(seg - (long)c.g * a.ntr_i);
+        } else {
+            c.tr = (int)(seg / G);
+            c.g = (int)(seg - (long)c.tr * G);
+        }
+        return c;
+    };
+    auto step = [&](cur &c) {
+        ++c.q;
+        if (c.q == n_gu) {
+            c = locate(c.q);  // from the gate-up run to the down run
+            return;
+        }
+        const int np = c.dn ? np_dn : np_gu;
+        if (++c.j == np) {
+            c.j = 0;
+            if (!c.dn) {
+                if (++c.tr == a.ntr_i) {
+                    c.tr = 0;
+                    ++c.g;
+                }
+            } else if (++c.g == G) {
+                c.g = 0;
+                ++c.tr;
+            }
+        }
+    };
+    auto plen = [&](const cur &c) {
+        return c.dn ? min(a.ch_dn, a.nkt_i - c.j * a.ch_dn) : min(a.ch_gu, a.nkt_h - c.j * a.ch_gu);
+    };
+    auto issue = [&](const cur &c, int stage) {
+        const int n = plen(c);
+        const int elem = c.dn ? a.tile_bytes : 2 * a.tile_bytes;
+        const int nkt = c.dn ? a.nkt_i : a.nkt_h;
+        const int kt = c.j * (c.dn ? a.ch_dn : a.ch_gu);
+        const uint8_t *src = (c.dn ? a.dn_bank + (size_t)tb.grp_expert[c.g] * a.dn_stride
+                                   : a.gu_bank + (size_t)tb.grp_expert[c.g] * a.gu_stride) +
+                             (size_t)(c.tr * nkt + kt) * elem;
+        uint64_t *bar = &bars[warp][stage];
+        fence_proxy_async();
+        mbar_expect_tx(bar, (unsigned)(n * elem));
+        bulk_g2s(ring + (size_t)stage * a.stage_bytes, src, (unsigned)(n * elem), bar);
+    };
+    cur ic = locate(0);
+    long n_issued = 0;
+    if (lane == 0)
+        for (int s = 0; s < XSTAGES && ic.q < n_all; ++s) {
+            issue(ic, s);
+            step(ic);
+            ++n_issued;
+        }
+    const int r = lane >> 2, qd = lane & 3, tt = (lane >> 3);  // tt: group member of B column lane / 4
+    cur cc = locate(0);
+    long kf = -1;
+    bool gu_done = n_gu == 0;
+    // finishing steps shared by both runs: fence the warp's partials, arrive on its counters and
+    // finish the units it completed last
+    // warps holding pieces of segment s: with at least one piece per warp, the run from the
+    // first piece's owner to the last's; with fewer pieces than warps every piece has its own
+    auto seg_warps = [&](long Q, int np, long s) {
+        if (Q < NW) return (unsigned)np;
+        return (unsigned)(xcta(Q, NW, (s + 1) * np - 1) - xcta(Q, NW, s * np) + 1);
+    };
+    auto sum_seg = [&](const float *base, int rec, int np, int s, int off) {
+        const float *pp = base + (size_t)s * np * rec + off;
+        float t[XMAX_PIECES];
+#pragma unroll
+        for (int j = 0; j < XMAX_PIECES; ++j) t[j] = (j < np) ? __ldcg(pp + (size_t)j * rec) : 0.f;
+        float v = 0.f;
+#pragma unroll
+        for (int j = 0; j < XMAX_PIECES; ++j)
+            if (j < np) v += t[j];
+        return v;
+    };
+    auto finish_gu = [&]() {
+        if (gb <= ga) return;
+        __threadfence();
+        __syncwarp();
+        const int s_first = (int)(ga / np_gu), s_last = (int)((gb - 1) / np_gu);
+        bool mine = false;
+        if (lane <= s_last - s_first) {
+            const int u = s_first + lane;
+            const unsigned target = seg_warps(Qg, np_gu, u);
+            if (atomicAdd(a.ctr_gu + u, 1u) + 1 == target) {
+                mine = true;
+                a.ctr_gu[u] = 0;
+            }
+        }
+        unsigned done = __ballot_sync(0xffffffffu, mine);
+        if (!done) return;
+        __threadfence();
+        while (done) {
+            const int u = s_first + __ffs(done) - 1;
+            done &= done - 1;
+            const int g = u / a.ntr_i, tr = u % a.ntr_i;
+            const int ntok = tb.grp_ntok[g], col0 = tb.grp_col0[g];
+            for (int e = lane; e < 16 * ntok; e += 32) {
+                const int rr = e & 15, t = e >> 4;
+                const float gs = sum_seg(a.part_gu, XREC_GU, np_gu, u, rr * GROUP + t);
+                const float us = sum_seg(a.part_gu, XREC_GU, np_gu, u, 64 + rr * GROUP + t);
+                const int col = col0 + t, row = tr * 16 + rr;
+                const float v = act_fn(a.act, gs, us, a.alpha, a.limit);
+                a.act_out[(size_t)col * a.I + row] = v;
+                const __half hh = __float2half_rn(v);
+                const __half hl = __float2half_rn(v - __half2float(hh));
+                const int blk = row / 32, el = row % 32;
+                const int qq = (el & 15) >> 2, jj = el & 3, half = el >> 4;
+                const size_t ihi = ((((size_t)col * nblk_i + blk) * 2 + 0) * 4 + qq) * 4 + jj;
+                const size_t ilo = ((((size_t)col * nblk_i + blk) * 2 + 1) * 4 + qq) * 4 + jj;
+                reinterpret_cast<uint16_t *>(a.actfrag + ihi)[half] = __half_as_ushort(hh);
+                reinterpret_cast<uint16_t *>(a.actfrag + ilo)[half] = __half_as_ushort(hl);
+            }
+            // publish: these 16 rows feed down k-tile tr / 4, i.e. down piece (tr / 4) / ch_dn
+            __threadfence();
+            __syncwarp();
+            if (lane == 0) atomicAdd(a.ready + g * np_dn + (tr / 4) / a.ch_dn, 1u);
+        }
+    };
+    auto finish_dn = [&]() {
+        if (db <= da) return;
+        __threadfence();
+        __syncwarp();
+        const int s_first = (int)(da / np_dn), s_last = (int)((db - 1) / np_dn);
+        const int u_first = s_first / G, u_last = s_last / G;
+        bool mine = false;
+        if (lane <= u_last - u_first) {
+            const int u = u_first + lane;
+            unsigned target = 0, inc = 0;
+            for (int gg = 0; gg < G; ++gg) {
+                const int s = u * G + gg;
+                target += seg_warps(Qd, np_dn, s);
+                if (s >= s_first && s <= s_last) ++inc;
+            }
+            if (atomicAdd(a.ctr_dn + u, inc) + inc == target) {
+                mine = true;
+                a.ctr_dn[u] = 0;
+            }
+        }
+        unsigned done = __ballot_sync(0xffffffffu, mine);
+        if (!done) return;
+        __threadfence();
+        while (done) {
+            const int tr = u_first + __ffs(done) - 1;
+            done &= done - 1;
+            // the router-weighted sum over the token's k experts in router order
+            // (moe.rs:2395-2421), plus the residual
+            for (int e = lane; e < a.T * 16; e += 32) {
+                const int t = e >> 4, rr = e & 15;
+                float acc = 0.f;
+                for (int m = 0; m < a.K; ++m) {
+                    const int col = tb.col_of[t * a.K + m];
+                    const int g = tb.col_grp[col];
+                    const float o = sum_seg(a.part_dn, XREC_DN, np_dn, tr * G + g, rr * GROUP + (col - tb.grp_col0[g]));
+                    acc = fmaf(tb.wts[t * a.K + m], o, acc);
+                }
+                const size_t o = (size_t)t * H + tr * 16 + rr;
+                a.out[o] = a.residual ? a.residual[o] + acc : acc;
+            }
+        }
+    };
+
+    float acc0[4], acc1[4];
+    while (cc.q < n_all) {
+        if (cc.dn && !gu_done) {
+            finish_gu();
+            gu_done = true;
+            TRACE(8);
+        }
+        const int n = plen(cc);
+        const int ntok = tb.grp_ntok[cc.g], col0 = tb.grp_col0[cc.g];
+        const uint32_t *brow = nullptr;
+        if (!cc.dn && a.b_smem) {
+            if (tt < ntok) brow = xf + (size_t)tb.col_tok[col0 + tt] * nblk_h * 32 + (size_t)cc.j * a.ch_gu * 64;
+        } else {
+            // fragments of this piece from global memory: down waits for its k-range first
+            const int kt0 = cc.j * (cc.dn ? a.ch_dn : a.ch_gu);
+            if (cc.dn) {
+                const unsigned target = 4u * (unsigned)n;
+                bool ok = true;
+                if (lane == 0) ok = wait_count(a.ready + cc.g * np_dn + cc.j, target, a.status);
+                ok = __shfl_sync(0xffffffffu, ok, 0);
+                if (!ok) {
+                    kf = cc.q;
+                    break;
+                }
+            }
+            __syncwarp();
+            const int nb = cc.dn ? nblk_i : nblk_h;
+            const uint32_t *src_base = cc.dn ? a.actfrag : a.xfrag;
+            for (int t = 0; t < ntok; ++t) {
+                const int row = cc.dn ? col0 + t : tb.col_tok[col0 + t];
+                const uint4 *src = reinterpret_cast<const uint4 *>(src_base + ((size_t)row * nb + 2 * kt0) * 32);
+                uint4 *dst = reinterpret_cast<uint4 *>(bbuf + (size_t)t * chmax * 64);
+                for (int i = lane; i < n * 16; i += 32) dst[i] = __ldcg(src + i);
+            }
+            __syncwarp();
+            if (tt < ntok) brow = bbuf + (size_t)tt * chmax * 64;
+        }
+        const int stage = (int)(cc.q % XSTAGES);
+        if (!mbar_wait(&bars[warp][stage], (unsigned)((cc.q / XSTAGES) & 1), a.status)) {
+            kf = cc.q;
+            break;
+        }
+        if (cc.q < 4) TRACE(4 + cc.q);
+        const uint8_t *st = ring + (size_t)stage * a.stage_bytes;
+#pragma unroll
+        for (int e = 0; e < 4; ++e) acc0[e] = acc1[e] = 0.f;
+        if (!cc.dn) {
+            for (int i = 0; i < n; ++i) {
+                uint32_t bfr[2][2][2];
+                load_b_row(brow, i, lane, bfr);
+                const uint8_t *tile = st + i * 2 * a.tile_bytes;
+                tile_mma<WT>(tile, lane, bfr, acc0);
+                tile_mma<WT>(tile + a.tile_bytes, lane, bfr, acc1);
+            }
+        } else {
+            for (int i = 0; i < n; ++i) {
+                uint32_t bfr[2][2][2];
+                load_b_row(brow, i, lane, bfr);
+                tile_mma<WT>(st + i * a.tile_bytes, lane, bfr, acc0);
+            }
+        }
+        __syncwarp();
+        if (lane == 0 && ic.q < n_all) {
+            issue(ic, stage);
+            step(ic);
+            ++n_issued;
+        }
+        // the piece's partial: column q = (f16 part + residual part) of rows r and r + 8
+        if (!cc.dn) {
+            float *pr = a.part_gu + (size_t)(ga + cc.q) * XREC_GU;
+            if (qd < ntok) {
+                pr[r * GROUP + qd] = acc0[0] + acc0[1];
+                pr[(r + 8) * GROUP + qd] = acc0[2] + acc0[3];
+                pr[64 + r * GROUP + qd] = acc1[0] + acc1[1];
+                pr[64 + (r + 8) * GROUP + qd] = acc1[2] + acc1[3];
+            }
+        } else {
+            float *pr = a.part_dn + (size_t)(da + cc.q - n_gu) * XREC_DN;
+            if (qd < ntok) {
+                pr[r * GROUP + qd] = acc0[0] + acc0[1];
+                pr[(r + 8) * GROUP + qd] = acc0[2] + acc0[3];
+            }
+        }
+        step(cc);
+    }
+    if (kf >= 0) {
+        // a wait gave up: let every issued copy land before the CTA exits, finish nothing
+        n_issued = __shfl_sync(0xffffffffu, n_issued, 0);
+        for (long j = kf; j < n_issued; ++j) mbar_wait(&bars[warp][j % XSTAGES], (unsigned)((j / XSTAGES) & 1), a.status);
+        if (!gu_done) finish_gu();  // down warps elsewhere may be waiting on these rows
+        return;
+    }
+    if (!gu_done) finish_gu();
+    TRACE(9);
+    finish_dn();
     TRACE(31);
 }
 
@@ -1427,6 +1935,30 @@ moearc_x_moe *moearc_x_moe_create(moearc_ctx *c, const moearc_x_moe_desc *d) {
                      (m->nkt_i + m->x_ch_dn - 1) / m->x_ch_dn > XMAX_PIECES))
         m->xpath = false;
 
+    // fused decode kernel: one CTA per SM, all resident; a ring stage holds one piece of either
+    // kind; the gate-up B fragments of up to 24 KB of tokens stay in shared memory
+    {
+        const int chmax = std::max(m->x_ch_gu, m->x_ch_dn);
+        m->f_stage = round128(std::max((long)m->x_ch_gu * 2 * m->tile_bytes, (long)m->x_ch_dn * m->tile_bytes));
+        m->f_bsmem = (long)m->T_max * (m->H / 32) * 128 <= 24 * 1024;
+        m->f_smem = XW * XSTAGES * m->f_stage + XW * m->x_ntok * chmax * 256 +
+                    (m->f_bsmem ? m->T_max * (m->H / 32) * 128 : 0);
+        int occ = 0;
+        const bool ok = m->xpath && m->f_smem <= 200 * 1024 && XW * XSTAGES * m->f_stage >= m->H * 4 &&
+                        cudaOccupancyMaxActiveBlocksPerMultiprocessor(
+                            &occ, m->wtype == T_MXFP4 ? k_moe_fused<39> : k_moe_fused<2>, XW * 32, 0) == cudaSuccess;
+        cudaGetLastError();
+        // one CTA per SM, fewer when even the smallest launch (one group per chosen expert)
+        // would leave warps without a piece
+        const long qmin = std::min((long)m->K * m->ntr_i * ((m->nkt_h + m->x_ch_gu - 1) / m->x_ch_gu),
+                                   (long)m->K * m->ntr_h * ((m->nkt_i + m->x_ch_dn - 1) / m->x_ch_dn));
+        m->f_grid = (int)std::max(1L, std::min<long>(c->sm_count, qmin / XW));
+        // opt-in: correct (the same tests pass) but, as a cooperative launch, it cannot start
+        // while the kernel before it finishes, and it measured slower than the three kernels
+        const char *fz = std::getenv("MOEARC_FUSED_MOE");
+        m->fused = ok && occ >= 1 && fz && fz[0] == '1';
+    }
+
     // one scratch allocation
     size_t off = 0;
     auto take = [&](size_t bytes) {
@@ -1450,6 +1982,8 @@ moearc_x_moe *moearc_x_moe_create(moearc_ctx *c, const moearc_x_moe_desc *d) {
     const size_t o_xpd = take(m->xpath ? sizeof(float) * x_segs_dn * np_dn * XREC_DN : 0);
     const size_t o_xcg = take(m->xpath ? sizeof(unsigned) * x_segs_gu : 0);
     const size_t o_xcd = take(m->xpath ? sizeof(unsigned) * m->ntr_h : 0);
+    const size_t o_frd = take(m->xpath ? sizeof(unsigned) * (size_t)TK * np_dn : 0);
+    const size_t o_fbar = take(sizeof(unsigned) * 2);
     m->mem_bytes = off;
     if (cudaMalloc(&m->mem, off) != cudaSuccess) {
         cudaGetLastError();
@@ -1470,6 +2004,8 @@ moearc_x_moe *moearc_x_moe_create(moearc_ctx *c, const moearc_x_moe_desc *d) {
     m->x_part_dn = reinterpret_cast<float *>(b + o_xpd);
     m->x_ctr_gu = reinterpret_cast<unsigned *>(b + o_xcg);
     m->x_ctr_dn = reinterpret_cast<unsigned *>(b + o_xcd);
+    m->f_ready = reinterpret_cast<unsigned *>(b + o_frd);
+    m->f_bar = reinterpret_cast<unsigned *>(b + o_fbar);
     cudaMemsetAsync(m->mem, 0, off, c->stream);
     // per-kernel attribute shared by every layer object: the most any of them may use
     const int smem_attr = 226 * 1024;
@@ -1480,6 +2016,8 @@ moearc_x_moe *moearc_x_moe_create(moearc_ctx *c, const moearc_x_moe_desc *d) {
         cudaFuncSetAttribute(k_xexpert<2, 0>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024) != cudaSuccess ||
         cudaFuncSetAttribute(k_xexpert<2, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024) != cudaSuccess ||
         cudaFuncSetAttribute(k_xroute, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024) != cudaSuccess ||
+        cudaFuncSetAttribute(k_moe_fused<39>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024) != cudaSuccess ||
+        cudaFuncSetAttribute(k_moe_fused<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024) != cudaSuccess ||
         cudaStreamSynchronize(c->stream) != cudaSuccess) {
         cudaGetLastError();
         cudaFree(m->mem);
@@ -1549,6 +2087,57 @@ int moe_forward_impl(moearc_x_moe *m, const float *x, unsigned n_tokens, const f
     const tab_view tab = make_tab(m);
     launch_scope ls(c, "moe_forward", (unsigned long)m->H, (unsigned)T);
 
+    if (m->fused) {
+        xfused_args f{};
+        f.x = x;
+        f.norm_w = norm_w;
+        f.eps = eps;
+        f.router = router_w;
+        f.rbias = router_b;
+        f.T = T;
+        f.H = m->H;
+        f.E = m->E;
+        f.K = m->K;
+        f.gating = m->gating;
+        f.I = m->I;
+        f.logits = m->logits;
+        f.gu_bank = static_cast<const uint8_t *>(gateup_packed);
+        f.dn_bank = static_cast<const uint8_t *>(down_packed);
+        f.gu_stride = (size_t)2 * m->ntr_i * m->nkt_h * m->tile_bytes;
+        f.dn_stride = (size_t)m->ntr_h * m->nkt_i * m->tile_bytes;
+        f.ntr_i = m->ntr_i;
+        f.nkt_h = m->nkt_h;
+        f.ntr_h = m->ntr_h;
+        f.nkt_i = m->nkt_i;
+        f.tile_bytes = m->tile_bytes;
+        f.ch_gu = m->x_ch_gu;
+        f.ch_dn = m->x_ch_dn;
+        f.stage_bytes = m->f_stage;
+        f.ntok_max = m->x_ntok;
+        f.b_smem = m->f_bsmem;
+        f.xfrag = m->xfrag;
+        f.act = m->act;
+        f.alpha = m->alpha;
+        f.limit = m->limit;
+        f.actfrag = m->actfrag;
+        f.act_out = m->act_f32;
+        f.idx_out = m->idx;
+        f.wts_out = m->wts;
+        f.residual = residual;
+        f.out = out;
+        f.part_gu = m->x_part_gu;
+        f.part_dn = m->x_part_dn;
+        f.ctr_gu = m->x_ctr_gu;
+        f.ctr_dn = m->x_ctr_dn;
+        f.ready = m->f_ready;
+        f.bar = m->f_bar;
+        f.status = m->status;
+        if (launch_coop(m->wtype == T_MXFP4 ? k_moe_fused<39> : k_moe_fused<2>, dim3(m->f_grid), dim3(XW * 32),
+                        (size_t)m->f_smem, c->stream, f) != cudaSuccess)
+            return ERR;
+        mark(4);
+        return ls.finish();
+    }
     if (m->xpath) {
         xroute_args xr{x, norm_w, eps, router_w, router_b, T, m->H, m->E, m->logits, m->xfrag, m->status};
         if (launch_pdl(k_xroute, dim3(m->x_route_grid), dim3(XROUTE_WARPS * 32), (size_t)m->x_route_smem, c->stream,
