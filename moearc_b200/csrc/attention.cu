@@ -63,22 +63,63 @@ __device__ __forceinline__ bool device_span(const int *dpos, int window, int max
 }
 
 // Merge the n_splits partial (max, sum, acc) triples of heads [h0, h0 + nh) into out, with
-// the sink as one extra logit (kernels.cpp:1856-1880). Run by one whole CTA.
+// the sink as one extra logit (kernels.cpp:1856-1880). Run by one whole CTA. The splits'
+// (max, sum) pairs are staged in shared memory and turned into per-split weights first, so the
+// accumulator loads (independent of one another) are issued in batches, not one round trip
+// per split.
+constexpr int MERGE_MAX = 8 * 64;  // heads x splits the staged weights cover
 __device__ void merge_heads(float *out, const float *part_ml, const float *part_acc, const float *sinks,
                             int h0, int nh, int hd, int n_splits) {
+    __shared__ float wgt[MERGE_MAX];  // [head][split] exp(m_s - M)
+    __shared__ float inv_l[8];
+    const bool staged = nh <= 8 && nh * n_splits <= MERGE_MAX;
+    if (staged) {
+        for (int i = threadIdx.x; i < nh * n_splits; i += blockDim.x)
+            wgt[i] = __ldcg(part_ml + ((size_t)(h0 + i / n_splits) * n_splits + i % n_splits) * 2);
+        __syncthreads();
+        // one warp per head: the max, the weights and 1 / (sum of weighted l + sink)
+        const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+        for (int h = warp; h < nh; h += blockDim.x >> 5) {
+            float M = sinks ? sinks[h0 + h] : -INFINITY;
+            for (int sp = lane; sp < n_splits; sp += 32) M = fmaxf(M, wgt[h * n_splits + sp]);
+            M = warp_max(M);
+            float L = 0.f;
+            for (int sp = lane; sp < n_splits; sp += 32) {
+                const float ms = wgt[h * n_splits + sp];
+                const float f = (ms == -INFINITY) ? 0.f : exp2f((ms - M) * LOG2E);
+                L += __ldcg(part_ml + ((size_t)(h0 + h) * n_splits + sp) * 2 + 1) * f;
+                wgt[h * n_splits + sp] = f;
+            }
+            L = warp_sum(L);
+            if (lane == 0) inv_l[h] = 1.f / (L + (sinks ? exp2f((sinks[h0 + h] - M) * LOG2E) : 0.f));
+        }
+        __syncthreads();
+        for (int e = threadIdx.x; e < nh * hd; e += blockDim.x) {
+            const int h = e / hd, d = e % hd;
+            const float *pa = part_acc + (size_t)(h0 + h) * n_splits * hd + d;
+            float v = 0.f;
+#pragma unroll 8
+            for (int sp = 0; sp < n_splits; ++sp) {
+                const float w = wgt[h * n_splits + sp];
+                if (w != 0.f) v += __ldcg(pa + (size_t)sp * hd) * w;  // a split with no keys adds nothing
+            }
+            out[(size_t)(h0 + h) * hd + d] = v * inv_l[h];
+        }
+        return;
+    }
     for (int e = threadIdx.x; e < nh * hd; e += blockDim.x) {
         const int h = h0 + e / hd, d = e % hd;
         const float *ml = part_ml + (size_t)h * n_splits * 2;
         float M = sinks ? sinks[h] : -INFINITY;
-        for (int s = 0; s < n_splits; ++s) M = fmaxf(M, __ldcg(ml + 2 * s));
+        for (int sp = 0; sp < n_splits; ++sp) M = fmaxf(M, __ldcg(ml + 2 * sp));
         float L = sinks ? exp2f((sinks[h] - M) * LOG2E) : 0.f;
         float v = 0.f;
-        for (int s = 0; s < n_splits; ++s) {
-            const float ms = __ldcg(ml + 2 * s);
+        for (int sp = 0; sp < n_splits; ++sp) {
+            const float ms = __ldcg(ml + 2 * sp);
             if (ms == -INFINITY) continue;
             const float f = exp2f((ms - M) * LOG2E);
-            L += __ldcg(ml + 2 * s + 1) * f;
-            v += __ldcg(part_acc + ((size_t)h * n_splits + s) * hd + d) * f;
+            L += __ldcg(ml + 2 * sp + 1) * f;
+            v += __ldcg(part_acc + ((size_t)h * n_splits + sp) * hd + d) * f;
         }
         out[(size_t)h * hd + d] = v / L;
     }
@@ -90,12 +131,12 @@ __device__ __forceinline__ void arrive_and_merge(unsigned *ctr, int unit, int n_
                                                  const float *part_ml, const float *part_acc,
                                                  const float *sinks, int h0, int nh, int hd) {
     __shared__ unsigned last;
-    __threadfence();
+    fence_acq_rel_gpu();
     __syncthreads();
     if (threadIdx.x == 0) last = (atomicAdd(ctr + unit, 1u) == (unsigned)n_splits - 1);
     __syncthreads();
     if (!last) return;
-    __threadfence();
+    fence_acq_rel_gpu();
     merge_heads(out, part_ml, part_acc, sinks, h0, nh, hd, n_splits);
     if (threadIdx.x == 0) ctr[unit] = 0;
 }
@@ -287,9 +328,20 @@ __global__ void __launch_bounds__(128)
     extern __shared__ __align__(16) uint16_t smem[];
     constexpr int CH = D / 8;  // 16-byte chunks per row
     const int kvh = blockIdx.x, split = blockIdx.y;
+    const int trace_row = (int)(blockIdx.y * gridDim.x + blockIdx.x);
+    (void)trace_row;
+    TRACE(0);
+    // Before the wait only what the kernel before this one (the Q/K/V projection) does not
+    // write: the sinks (weights) and the key span (the position advances only at the end of a
+    // step).
+    __shared__ float s_sink[8];
+    if (threadIdx.x < group) s_sink[threadIdx.x] = sinks ? sinks[kvh * group + threadIdx.x] : 0.f;
+    const bool live = !dpos || device_span(dpos, window, gridDim.y, kv_begin, n_kv, kps, n_splits);
     pdl_trigger();
+    if (!live) return;
     pdl_wait();
-    if (dpos && !device_span(dpos, window, gridDim.y, kv_begin, n_kv, kps, n_splits)) return;
+    TRACE(1);
+    TRACE(2);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int qd = lane & 3, hr = lane >> 2;  // quad position, head row
     const size_t s0 = kv_begin + (size_t)split * kps;
@@ -400,6 +452,7 @@ __global__ void __launch_bounds__(128)
         stage ^= 1;
     }
     cp_async_wait<0>();
+    TRACE(3);
     lsum += __shfl_xor_sync(0xffffffffu, lsum, 1);
     lsum += __shfl_xor_sync(0xffffffffu, lsum, 2);
 
@@ -434,7 +487,7 @@ __global__ void __launch_bounds__(128)
         if (n_splits == 1) {
             float fs = 1.f;
             if (sinks) {
-                const float sk = sinks[hq];
+                const float sk = s_sink[h];
                 const float Mf = fmaxf(M, sk);
                 fs = (M == -INFINITY) ? 0.f : exp2f((M - Mf) * LOG2E);
                 L = L * fs + exp2f((sk - Mf) * LOG2E);
@@ -448,20 +501,23 @@ __global__ void __launch_bounds__(128)
             part_acc[((size_t)hq * n_splits + split) * D + d] = v;
         }
     }
+    TRACE(4);
     if (n_splits > 1 && ctr) arrive_and_merge(ctr, kvh, n_splits, out, part_ml, part_acc, sinks, kvh * group, group, D);
+    TRACE(5);
 }
 
 template <int D, bool BF>
 void set_mma_smem() {
     static bool done = false;
     if (!done) {
-        cudaFuncSetAttribute(k_attn_mma<D, BF>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             4 * warp_smem_elems<D>() * 2);
+        set_smem(k_attn_mma<D, BF>, 4 * warp_smem_elems<D>() * 2);
         done = true;
     }
 }
 
 }  // namespace
+
+TRACE_SETTER(attn)
 
 namespace moearc {
 

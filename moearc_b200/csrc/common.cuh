@@ -178,6 +178,11 @@ static __device__ unsigned long long *g_trace;
 #define TRACE_SETTER(unit)
 #endif
 
+// Release / acquire fence at GPU scope, for the last-arriver reductions: each thread that
+// wrote partials fences before its warp's arrival (an atomic), and the last arriver fences
+// after seeing the count, before it reads them. Cheaper than __threadfence (fence.sc).
+__device__ __forceinline__ void fence_acq_rel_gpu() { asm volatile("fence.acq_rel.gpu;\n" ::: "memory"); }
+
 // ---- programmatic dependent launch ---------------------------------------------------------
 // A kernel launched with launch_pdl may begin while the kernel before it in the stream is
 // still running. Everything it does before pdl_wait() must not read that kernel's outputs nor
@@ -201,6 +206,16 @@ inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, s
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
+
+// Shared-memory limit of a kernel, with the SM's unified L1 / shared storage configured for
+// the most shared memory. The carveout is per kernel: a kernel launched with a smaller one
+// leaves its SMs unable to take a neighbouring kernel's CTA (PDL overlap needs both resident).
+template <typename... KArgs>
+inline cudaError_t set_smem(void (*kernel)(KArgs...), int max_dynamic) {
+    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, max_dynamic);
+    if (e != cudaSuccess) return e;
+    return cudaFuncSetAttribute(kernel, cudaFuncAttributePreferredSharedMemoryCarveout, cudaSharedmemCarveoutMaxShared);
 }
 
 // A cooperative launch (every CTA resident at once, so CTAs may wait on one another), with

@@ -198,6 +198,8 @@ moearc_x_decoder *moearc_x_decoder_create(moearc_ctx *c, const moearc_x_decoder_
     moearc_x_moe_desc md{g.n_embd, g.n_ff, g.n_expert, g.n_expert_used, g.gating, g.act, g.alpha, g.limit,
                          g.expert_type, 1};
     d->moe = moearc_x_moe_create(c, &md);
+    set_smem(k_step_end, 0);
+    cudaGetLastError();
     d->qkv = dense_create(c, d->n_qkv, H, 0);
     d->wo = dense_create(c, H, d->Dq, 1);
     if (!d->moe || !d->qkv || !d->wo) return fail();

@@ -18,6 +18,7 @@ constexpr int MAX_LOCAL = 8;   // tile-rows (hence units) one CTA may touch; <= 
 constexpr int MAX_ITEMS = 8;   // B-fragment items per thread: n_cols / 2 <= 8 x 256
 constexpr int MAX_COLS = 2 * MAX_ITEMS * WARPS * 32;
 constexpr int RING_BYTES = WARPS * STAGES * CH * DENSE_TILE;
+constexpr int MAX_CONTRIB = 4;  // CTAs that may share one tile-row (checked at plan time)
 
 __global__ void k_dense_pack(uint8_t *dst, const uint16_t *src, int n_rows, int n_cols) {
     const int nkt = n_cols / 64;
@@ -124,6 +125,14 @@ __global__ void __launch_bounds__(WARPS * 32, 1) k_dense(dense_args a) {
     }
     if (a.mode == 0)
         for (int p = threadIdx.x; p < a.rope.head_dim / 2; p += WARPS * 32) rfreq[p] = __ldg(a.rope.freq + p);
+    // the position and this step's K/V page: the position advances only at the end of a step,
+    // after the last kernel of the step, so both can be read before the wait
+    int pos = 0;
+    size_t page = 0;
+    if (a.mode == 0) {
+        pos = *a.pos;
+        page = a.kv.table[pos / a.kv.page_tokens];
+    }
     pdl_trigger();
     pdl_wait();
     TRACE(1);
@@ -258,7 +267,7 @@ __global__ void __launch_bounds__(WARPS * 32, 1) k_dense(dense_args a) {
         const int slot = cta - cta_of(a.T, G, (long)tr * a.nkt);
         a.part[((size_t)tr * a.maxc + slot) * 16 + row] = s;
     }
-    __threadfence();
+    fence_acq_rel_gpu();
     __syncthreads();
     // one arrival per unit touched; the CTAs that touch a unit are a contiguous run
     const int u0 = tr0 / a.unit_trs, u1 = tr1 / a.unit_trs;
@@ -272,14 +281,22 @@ __global__ void __launch_bounds__(WARPS * 32, 1) k_dense(dense_args a) {
     TRACE(9);
     // finish the units this CTA completed last: warp i takes the i-th unit touched
     if (warp > u1 - u0 || !fin[warp]) return;
-    __threadfence();
+    fence_acq_rel_gpu();
     const int unit = u0 + warp;
     if (lane == 0) a.ctr[unit] = 0;
+    // a row's contributors summed in CTA order; their loads are issued together first
     auto row_value = [&](int row) {
         const int tr = row >> 4;
         const int c0 = cta_of(a.T, G, (long)tr * a.nkt), c1 = cta_of(a.T, G, (long)(tr + 1) * a.nkt - 1);
+        const int nc = c1 - c0 + 1;
+        const float *pp = a.part + (size_t)tr * a.maxc * 16 + (row & 15);
+        float t[MAX_CONTRIB];
+#pragma unroll
+        for (int k = 0; k < MAX_CONTRIB; ++k) t[k] = (k < nc) ? __ldcg(pp + k * 16) : 0.f;
         float s = 0.f;
-        for (int k = 0; k <= c1 - c0; ++k) s += __ldcg(a.part + ((size_t)tr * a.maxc + k) * 16 + (row & 15));
+#pragma unroll
+        for (int k = 0; k < MAX_CONTRIB; ++k)
+            if (k < nc) s += t[k];
         return s;
     };
     if (a.mode == 1) {
@@ -295,9 +312,9 @@ __global__ void __launch_bounds__(WARPS * 32, 1) k_dense(dense_args a) {
     const int per = D / 32;  // values per lane: d = lane + 32 i
     const int row0 = unit * D;
     float v[4];
-    for (int i = 0; i < per; ++i) v[i] = row_value(row0 + lane + 32 * i);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) v[i] = (i < per) ? row_value(row0 + lane + 32 * i) : 0.f;
     const int hq = a.rope.n_q_heads, hk = a.rope.n_kv_heads;
-    const int pos = *a.pos;
     if (unit < hq + hk) {
         // NeoX RoPE: pairs (d, d + D/2); this lane holds d = lane + 32 i. The angle of pair p
         // is pos * freq[p] (the YaRN blend folded into freq on the host), reduced by 2 pi in
@@ -323,7 +340,7 @@ __global__ void __launch_bounds__(WARPS * 32, 1) k_dense(dense_args a) {
         const int kvh = (unit < hq + hk) ? unit - hq : unit - hq - hk;
         uint16_t *pool = (unit < hq + hk) ? a.kv.k_pages : a.kv.v_pages;
         const int pt = a.kv.page_tokens;
-        const size_t page = a.kv.table[pos / pt], slot = pos % pt;
+        const size_t slot = pos % pt;
         uint16_t *dst = pool + ((page * pt + slot) * hk + kvh) * D;
         for (int i = 0; i < per; ++i) dst[lane + 32 * i] = bf(v[i]);
     }
@@ -384,6 +401,10 @@ dense_gemv *dense_create(moearc_ctx *c, int n_rows, int n_cols, int mode) {
     int maxc = 1;
     for (int tr = 0; tr < g->ntr; ++tr)
         maxc = std::max(maxc, cta_of(g->T, grid, (long)(tr + 1) * g->nkt - 1) - cta_of(g->T, grid, (long)tr * g->nkt) + 1);
+    if (maxc > MAX_CONTRIB) {
+        delete g;
+        return nullptr;
+    }
     g->maxc = maxc;
     g->smem = RING_BYTES + (n_cols / 16) * PARTS * 32 + WARPS * MAX_LOCAL * 16 * 4;
     const size_t part_b = sizeof(float) * (size_t)g->ntr * maxc * 16;
@@ -400,7 +421,7 @@ dense_gemv *dense_create(moearc_ctx *c, int n_rows, int n_cols, int mode) {
     // The attribute is per kernel, shared by every plan: set it to the most any plan may use,
     // not to this plan's need.
     if (g->smem > 200 * 1024 ||
-        cudaFuncSetAttribute(k_dense, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024) != cudaSuccess) {
+        set_smem(k_dense, 200 * 1024) != cudaSuccess) {
         cudaGetLastError();
         cudaFree(g->mem);
         delete g;

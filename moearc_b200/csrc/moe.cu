@@ -799,6 +799,8 @@ constexpr int XREC_GU = 2 * 16 * GROUP;  // floats in one gate-up partial (gate,
 constexpr int XREC_DN = 16 * GROUP;      // floats in one down partial
 constexpr int XROUTE_WARPS = 4;
 constexpr int XMAX_PIECES = 24;          // pieces per segment (k-extent / piece length)
+constexpr int XMAX_K = 8;                // experts per token the decode path's combine unrolls
+constexpr int XEXCLUSIVE_SMEM = 116 * 1024;  // > half of the 228 KB an SM has: one CTA per SM
 
 struct xroute_args {
     const float *x;       // [T][H]
@@ -1234,7 +1236,7 @@ __global__ void __launch_bounds__(XW * 32, 1) k_xexpert(xexp_args a) {
     }
     if (qb <= qa) return;
     TRACE(10);
-    __threadfence();
+    fence_acq_rel_gpu();
     __syncwarp();
     // arrivals: gate-up one per segment touched; down one per tile-row, counting the segments
     // of that tile-row this warp touched. The warps on a segment are a contiguous run.
@@ -1266,7 +1268,7 @@ __global__ void __launch_bounds__(XW * 32, 1) k_xexpert(xexp_args a) {
     }
     unsigned done_mask = __ballot_sync(0xffffffffu, mine);
     if (!done_mask) return;
-    __threadfence();
+    fence_acq_rel_gpu();
     TRACE(11);
     // a segment's pieces summed in piece order; the loads are all issued before the adds
     auto sum_seg = [&](int s, int off) {
@@ -1280,6 +1282,24 @@ __global__ void __launch_bounds__(XW * 32, 1) k_xexpert(xexp_args a) {
             if (j < np) v += t[j];
         return v;
     };
+    // two sums of one segment (gate and up) with all loads issued before any add
+    auto sum_seg2 = [&](int s, int off0, int off1, float &v0, float &v1) {
+        const float *pp = a.part + (size_t)s * np * rec;
+        float t0[XMAX_PIECES], t1[XMAX_PIECES];
+#pragma unroll
+        for (int j = 0; j < XMAX_PIECES; ++j) {
+            t0[j] = (j < np) ? __ldcg(pp + (size_t)j * rec + off0) : 0.f;
+            t1[j] = (j < np) ? __ldcg(pp + (size_t)j * rec + off1) : 0.f;
+        }
+        v0 = 0.f;
+        v1 = 0.f;
+#pragma unroll
+        for (int j = 0; j < XMAX_PIECES; ++j)
+            if (j < np) {
+                v0 += t0[j];
+                v1 += t1[j];
+            }
+    };
     while (done_mask) {
         const int u = u_first + __ffs(done_mask) - 1;
         done_mask &= done_mask - 1;
@@ -1290,7 +1310,8 @@ __global__ void __launch_bounds__(XW * 32, 1) k_xexpert(xexp_args a) {
             const int nblk_i = a.I / 32;
             for (int e = lane; e < 16 * ntok; e += 32) {
                 const int rr = e & 15, t = e >> 4;
-                const float gs = sum_seg(u, rr * GROUP + t), us = sum_seg(u, 64 + rr * GROUP + t);
+                float gs, us;
+                sum_seg2(u, rr * GROUP + t, 64 + rr * GROUP + t, gs, us);
                 const int col = col0 + t, row = tr * 16 + rr;
                 const float v = act_fn(a.act, gs, us, a.alpha, a.limit);
                 a.act_out[(size_t)col * a.I + row] = v;
@@ -1309,18 +1330,27 @@ __global__ void __launch_bounds__(XW * 32, 1) k_xexpert(xexp_args a) {
             // down tile-row tr: per token, the router-weighted sum over its k experts in router
             // order (moe.rs:2395-2421), plus the residual
             const int tr = u;
+            // every (token, row, expert) output of the tile-row on its own lane (one batch of
+            // piece loads each), staged in this warp's ring (all its copies have landed), then
+            // per (token, row) the fmaf chain in router order
+            float *os = reinterpret_cast<float *>(ring);  // [T][16][K]
+            const int n_o = a.T * 16 * a.K;
+            for (int e = lane; e < n_o; e += 32) {
+                const int m = e % a.K, rr = (e / a.K) & 15, t = e / (16 * a.K);
+                const int col = tb.col_of[t * a.K + m];
+                const int g = tb.col_grp[col];
+                os[e] = sum_seg(tr * G + g, rr * GROUP + (col - tb.grp_col0[g]));
+            }
+            __syncwarp();
             for (int e = lane; e < a.T * 16; e += 32) {
                 const int t = e >> 4, rr = e & 15;
+                const size_t oi = (size_t)t * a.H + tr * 16 + rr;
+                const float res = a.residual ? a.residual[oi] : 0.f;
                 float acc = 0.f;
-                for (int m = 0; m < a.K; ++m) {
-                    const int col = tb.col_of[t * a.K + m];
-                    const int g = tb.col_grp[col];
-                    const float o = sum_seg(tr * G + g, rr * GROUP + (col - tb.grp_col0[g]));
-                    acc = fmaf(tb.wts[t * a.K + m], o, acc);
-                }
-                const size_t o = (size_t)t * a.H + tr * 16 + rr;
-                a.out[o] = a.residual ? a.residual[o] + acc : acc;
+                for (int m = 0; m < a.K; ++m) acc = fmaf(tb.wts[t * a.K + m], os[e * a.K + m], acc);
+                a.out[oi] = a.residual ? res + acc : acc;
             }
+            __syncwarp();
         }
     }
     TRACE(31);
@@ -1919,7 +1949,7 @@ moearc_x_moe *moearc_x_moe_create(moearc_ctx *c, const moearc_x_moe_desc *d) {
 
     // decode path plan: one CTA per SM (fewer when a warp would get under two elements), a
     // ring of XSTAGES stages per warp, each ch elements and their B fragments
-    m->xpath = TK <= MAX_TK && m->T_max <= 32;
+    m->xpath = TK <= MAX_TK && m->T_max <= 32 && m->K <= XMAX_K;
     const long x_pmin = (long)m->K * m->ntr_i * m->nkt_h;  // fewest elements of a launch (both modes)
     m->x_grid = (int)std::max(1L, std::min<long>(c->sm_count, x_pmin / (XW * 2 * 5)));
     m->x_ntok = tok_group;
@@ -2009,15 +2039,15 @@ moearc_x_moe *moearc_x_moe_create(moearc_ctx *c, const moearc_x_moe_desc *d) {
     cudaMemsetAsync(m->mem, 0, off, c->stream);
     // per-kernel attribute shared by every layer object: the most any of them may use
     const int smem_attr = 226 * 1024;
-    if (cudaFuncSetAttribute(k_moe_rows<39>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_attr) != cudaSuccess ||
-        cudaFuncSetAttribute(k_moe_rows<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_attr) != cudaSuccess ||
-        cudaFuncSetAttribute(k_xexpert<39, 0>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024) != cudaSuccess ||
-        cudaFuncSetAttribute(k_xexpert<39, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024) != cudaSuccess ||
-        cudaFuncSetAttribute(k_xexpert<2, 0>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024) != cudaSuccess ||
-        cudaFuncSetAttribute(k_xexpert<2, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024) != cudaSuccess ||
-        cudaFuncSetAttribute(k_xroute, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024) != cudaSuccess ||
-        cudaFuncSetAttribute(k_moe_fused<39>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024) != cudaSuccess ||
-        cudaFuncSetAttribute(k_moe_fused<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024) != cudaSuccess ||
+    if (set_smem(k_moe_rows<39>, smem_attr) != cudaSuccess ||
+        set_smem(k_moe_rows<2>, smem_attr) != cudaSuccess ||
+        set_smem(k_xexpert<39, 0>, 200 * 1024) != cudaSuccess ||
+        set_smem(k_xexpert<39, 1>, 200 * 1024) != cudaSuccess ||
+        set_smem(k_xexpert<2, 0>, 200 * 1024) != cudaSuccess ||
+        set_smem(k_xexpert<2, 1>, 200 * 1024) != cudaSuccess ||
+        set_smem(k_xroute, 200 * 1024) != cudaSuccess ||
+        set_smem(k_moe_fused<39>, 200 * 1024) != cudaSuccess ||
+        set_smem(k_moe_fused<2>, 200 * 1024) != cudaSuccess ||
         cudaStreamSynchronize(c->stream) != cudaSuccess) {
         cudaGetLastError();
         cudaFree(m->mem);
@@ -2175,8 +2205,13 @@ int moe_forward_impl(moearc_x_moe *m, const float *x, unsigned n_tokens, const f
         xa.maxc = m->x_maxc;
         xa.status = m->status;
         const bool mx = m->wtype == T_MXFP4;
-        if (launch_pdl(mx ? k_xexpert<39, 0> : k_xexpert<2, 0>, dim3(m->x_grid), dim3(XW * 32),
-                       (size_t)XW * XSTAGES * m->x_stage_gu, c->stream, xa) != cudaSuccess)
+        // More than half an SM's shared memory, so no SM takes two gate-up CTAs: at launch the
+        // router's CTAs still hold some SMs, and a CTA that fits beside another gate-up CTA
+        // would start there, leaving its SM's share of the stream to be split with a neighbour
+        // while other SMs go without. One down CTA still fits beside it.
+        const size_t smem_gu = std::max((size_t)XW * XSTAGES * m->x_stage_gu, (size_t)XEXCLUSIVE_SMEM);
+        if (launch_pdl(mx ? k_xexpert<39, 0> : k_xexpert<2, 0>, dim3(m->x_grid), dim3(XW * 32), smem_gu,
+                       c->stream, xa) != cudaSuccess)
             return ERR;
         mark(4);
         xexp_args xd = xa;
