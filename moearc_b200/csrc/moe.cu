@@ -52,7 +52,7 @@ struct moearc_x_moe {
     int warps_dn, ranges_dn, tpr_dn, stages_dn, stage_dn, smem_dn, grid_dn;
     // decode path (T_max * K <= MAX_TK columns): k_xroute + k_xexpert
     bool xpath;
-    int x_grid, x_route_grid, x_route_smem, x_ch_gu, x_ch_dn, x_stage_gu, x_stage_dn, x_ntok, x_maxc;
+    int x_grid, x_warps, x_route_grid, x_route_smem, x_ch_gu, x_ch_dn, x_stage_gu, x_stage_dn, x_ntok, x_maxc;
     float *x_part_gu, *x_part_dn;
     unsigned *x_ctr_gu, *x_ctr_dn;
     // the fused decode kernel (k_moe_fused): one cooperative launch per layer
@@ -291,6 +291,23 @@ struct route_args {
     unsigned *done;
 };
 
+// Argmax across the warp of each lane's candidate (bv at index bi; bi = 0x7FFFFFFF for none),
+// the lower index winning a tie, in two integer reductions: the largest order-preserving key of
+// the value (-0 counts as +0, so equal logits tie), then the lowest index holding it. Every
+// lane gets the winner. NaN logits are outside the contract (reference.rs:616 rejects them).
+__device__ __forceinline__ void warp_argmax(float &bv, int &bi) {
+    unsigned kb = 0;  // no candidate in this lane
+    if (bi != 0x7FFFFFFF) {
+        unsigned b = __float_as_uint(bv);
+        if (b == 0x80000000u) b = 0;
+        kb = max((b & 0x80000000u) ? ~b : (b | 0x80000000u), 1u);
+    }
+    const unsigned km = __reduce_max_sync(0xffffffffu, kb);
+    const unsigned gi = __reduce_min_sync(0xffffffffu, (kb == km && kb != 0) ? (unsigned)bi : 0xFFFFFFFFu);
+    bi = (gi == 0xFFFFFFFFu) ? 0x7FFFFFFF : (int)gi;
+    bv = __shfl_sync(0xffffffffu, bv, gi & 31);
+}
+
 __device__ void topk_token(const route_args &a, int t, int lane) {
     const float *l = a.logits + (size_t)t * a.E;
     const unsigned nper = (a.E + 31) / 32;
@@ -310,15 +327,7 @@ __device__ void topk_token(const route_args &a, int t, int lane) {
                 }
             }
         }
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) {
-            const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-            const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-            if (oi != 0x7FFFFFFF && (bi == 0x7FFFFFFF || ov > bv || (ov == bv && oi < bi))) {
-                bv = ov;
-                bi = oi;
-            }
-        }
+        warp_argmax(bv, bi);
         if ((bi & 31) == lane) taken |= 1u << (bi >> 5);
         if (lane == r) {
             my_v = bv;
@@ -792,7 +801,7 @@ __global__ void __launch_bounds__(256) k_moe_rows(rows_args a) {
 //             the tile-row's (down); the last warp to arrive finishes: the activation into the
 //             down kernel's fragments, or the router-weighted combine plus the residual.
 
-constexpr int XW = 8;          // warps per expert CTA
+constexpr int XW = 16;         // most warps per expert CTA (the plan takes 8 when 16 rings do not fit)
 constexpr int XSTAGES = 3;     // ring stages per warp
 constexpr int MAX_TK = 32;     // columns (token, expert choices) of the decode path
 constexpr int XREC_GU = 2 * 16 * GROUP;  // floats in one gate-up partial (gate, up x 16 rows x 4 cols)
@@ -913,6 +922,7 @@ struct xtab {
     int col_of[MAX_TK];               // column of choice i = t * K + m
     float wts[MAX_TK];                // gating weight of choice i
     unsigned idx[MAX_TK];             // expert of choice i
+    int key[32];                      // sort keys of the rank step (expert * 64 + token)
 };
 
 // Top-k of one token by one warp (reference.rs:613-640 semantics, as topk_token): k rounds of
@@ -939,15 +949,7 @@ __device__ void xtopk_n(const float *logits, int E, int K, int gating, int lane,
                 bi = j;
             }
         }
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) {
-            const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-            const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-            if (oi != 0x7FFFFFFF && (bi == 0x7FFFFFFF || ov > bv || (ov == bv && oi < bi))) {
-                bv = ov;
-                bi = oi;
-            }
-        }
+        warp_argmax(bv, bi);
         if ((bi & 31) == lane) taken |= 1u << (bi >> 5);
         if (lane == r) {
             my_v = bv;
@@ -986,21 +988,24 @@ __device__ __forceinline__ void xtopk(const float *logits, int E, int K, int gat
     else xtopk_n<32>(logits, E, K, gating, lane, idx, wts);
 }
 
-// Every token's top-k (warp t takes tokens t, t + XW, ...), then the tables by warp 0: the
+// Every token's top-k (warp t of nw takes tokens t, t + nw, ...), then the tables by warp 0: the
 // columns are the choices sorted by (expert, token) — distinct experts ascending, a slot's
 // tokens in token order — cut into groups of at most GROUP columns of one expert.
 __device__ void xbuild(xtab &tb, const float *logits, int T, int E, int K, int gating, int warp, int lane) {
-    for (int t = warp; t < T; t += XW) xtopk(logits + (size_t)t * E, E, K, gating, lane, tb.idx + t * K, tb.wts + t * K);
+    const int nw = (int)(blockDim.x >> 5);
+    for (int t = warp; t < T; t += nw) xtopk(logits + (size_t)t * E, E, K, gating, lane, tb.idx + t * K, tb.wts + t * K);
     __syncthreads();
     if (warp == 0) {
         const int C = T * K;
         const bool live = lane < C;
         const int key = live ? (int)tb.idx[lane] * 64 + lane / K : 0x7FFFFFFF;
+        // rank = number of smaller keys; the keys go through shared memory, which the unrolled
+        // compares read as broadcasts (a loop of 32 shuffles took several times as long)
+        tb.key[lane] = key;
+        __syncwarp();
         int rank = 0;
-        for (int j = 0; j < 32; ++j) {
-            const int kj = __shfl_sync(0xffffffffu, key, j);
-            rank += (kj < key);
-        }
+#pragma unroll
+        for (int j = 0; j < 32; ++j) rank += (tb.key[j] < key);
         if (live) {
             tb.col_of[lane] = rank;
             tb.col_tok[rank] = lane / K;
@@ -1097,7 +1102,8 @@ __global__ void __launch_bounds__(XW * 32, 1) k_xexpert(xexp_args a) {
     const int G = tb.G, nkt = a.nkt, ntr = a.ntr, ch = a.ch;
     const int np = (nkt + ch - 1) / ch;
     const long Q = (long)G * ntr * np;
-    const long NW = (long)gridDim.x * XW, gw = (long)blockIdx.x * XW + warp;
+    const int nw = (int)(blockDim.x >> 5);
+    const long NW = (long)gridDim.x * nw, gw = (long)blockIdx.x * nw + warp;
     const long qa = Q * gw / NW, qb = Q * (gw + 1) / NW;
     uint8_t *ring = smem + (size_t)warp * XSTAGES * a.stage_bytes;
     const int wmax = ch * a.elem_bytes;  // B region offset inside a stage
@@ -1951,7 +1957,6 @@ moearc_x_moe *moearc_x_moe_create(moearc_ctx *c, const moearc_x_moe_desc *d) {
     // ring of XSTAGES stages per warp, each ch elements and their B fragments
     m->xpath = TK <= MAX_TK && m->T_max <= 32 && m->K <= XMAX_K;
     const long x_pmin = (long)m->K * m->ntr_i * m->nkt_h;  // fewest elements of a launch (both modes)
-    m->x_grid = (int)std::max(1L, std::min<long>(c->sm_count, x_pmin / (XW * 2 * 5)));
     m->x_ntok = tok_group;
     m->x_ch_gu = 3;
     m->x_ch_dn = 5;
@@ -1960,7 +1965,10 @@ moearc_x_moe *moearc_x_moe_create(moearc_ctx *c, const moearc_x_moe_desc *d) {
     m->x_maxc = 0;  // unused: partials are per piece
     m->x_route_grid = (m->E + XROUTE_WARPS - 1) / XROUTE_WARPS;
     m->x_route_smem = (XROUTE_WARPS + 1) * m->H * 4;
-    if (m->xpath && (XW * XSTAGES * std::max(m->x_stage_gu, m->x_stage_dn) > 200 * 1024 || m->x_route_smem > 200 * 1024 ||
+    // 16 warps per CTA when their rings fit (one token: 192 KB for gpt-oss-120b), else 8
+    m->x_warps = XW * XSTAGES * std::max(m->x_stage_gu, m->x_stage_dn) <= 200 * 1024 ? XW : XW / 2;
+    m->x_grid = (int)std::max(1L, std::min<long>(c->sm_count, x_pmin / (m->x_warps * 2 * 5)));
+    if (m->xpath && (m->x_warps * XSTAGES * std::max(m->x_stage_gu, m->x_stage_dn) > 200 * 1024 || m->x_route_smem > 200 * 1024 ||
                      (m->nkt_h + m->x_ch_gu - 1) / m->x_ch_gu > XMAX_PIECES ||
                      (m->nkt_i + m->x_ch_dn - 1) / m->x_ch_dn > XMAX_PIECES))
         m->xpath = false;
@@ -2209,8 +2217,8 @@ int moe_forward_impl(moearc_x_moe *m, const float *x, unsigned n_tokens, const f
         // router's CTAs still hold some SMs, and a CTA that fits beside another gate-up CTA
         // would start there, leaving its SM's share of the stream to be split with a neighbour
         // while other SMs go without. One down CTA still fits beside it.
-        const size_t smem_gu = std::max((size_t)XW * XSTAGES * m->x_stage_gu, (size_t)XEXCLUSIVE_SMEM);
-        if (launch_pdl(mx ? k_xexpert<39, 0> : k_xexpert<2, 0>, dim3(m->x_grid), dim3(XW * 32), smem_gu,
+        const size_t smem_gu = std::max((size_t)m->x_warps * XSTAGES * m->x_stage_gu, (size_t)XEXCLUSIVE_SMEM);
+        if (launch_pdl(mx ? k_xexpert<39, 0> : k_xexpert<2, 0>, dim3(m->x_grid), dim3(m->x_warps * 32), smem_gu,
                        c->stream, xa) != cudaSuccess)
             return ERR;
         mark(4);
@@ -2228,8 +2236,8 @@ int moe_forward_impl(moearc_x_moe *m, const float *x, unsigned n_tokens, const f
         xd.out = out;
         xd.part = m->x_part_dn;
         xd.ctr = m->x_ctr_dn;
-        if (launch_pdl(mx ? k_xexpert<39, 1> : k_xexpert<2, 1>, dim3(m->x_grid), dim3(XW * 32),
-                       (size_t)XW * XSTAGES * m->x_stage_dn, c->stream, xd) != cudaSuccess)
+        if (launch_pdl(mx ? k_xexpert<39, 1> : k_xexpert<2, 1>, dim3(m->x_grid), dim3(m->x_warps * 32),
+                       (size_t)m->x_warps * XSTAGES * m->x_stage_dn, c->stream, xd) != cudaSuccess)
             return ERR;
         mark(5);
         return ls.finish();
