@@ -2,6 +2,8 @@
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--depth D] [--config 120b|20b]
     python bench.py --impl reference ...   # the reference's CPU path, timed on the host cores
+    python bench.py --offload 30 ...       # configs[2] mode (b): experts of blocks 0-29 in
+                                           # pinned host memory, fetched over PCIe every step
 
 A step is one batch-1 decode token through the whole synthetic decoder (36 blocks: RMSNorm,
 Q/K/V, RoPE, paged-KV append, attention with sinks over a full or 128-key window, O
@@ -15,6 +17,8 @@ e2e       the same through the public API with host buffers: per step the input 
 roofline  the MoE gate-up grouped GEMV (the path's dominant kernel): algorithmic bytes per
           launch (4 experts x 2 matrices x 2880 x 2880 MXFP4 = 35.25 MB) over its average
           device time, against the measured HBM copy bandwidth in MEASURED_PEAKS.json
+          (with --offload: the PCIe bytes of the offloaded blocks' routed experts per step over the
+          step time, against a pinned host-to-device copy measured in the same run)
 Multi-GPU: batch-1 decode does not shard; with N GPUs each rank runs an independent replica
 (weak scaling) and `value` sums their tokens/s, timed as the max over ranks.
 """
@@ -174,6 +178,24 @@ def cpu_decode_sample(cfg, layers: int = 2, budget_s: float = 12.0, threads: int
 
 # ---- the GPU run ----------------------------------------------------------------------------
 
+def pcie_h2d_gbs(ctx, nbytes: int = 256 << 20, reps: int = 5) -> float:
+    """Pinned host-to-device copy bandwidth (one copy engine, CUDA events): the PCIe peak the
+    offload roofline is quoted against (the BULK method of the reference's stream_bench)."""
+    lib = ctx.lib
+    hb = lib.moearc_x_host_alloc(nbytes)
+    db = lib.moearc_alloc_device(ctx.raw, nbytes)
+    assert hb and db, "pcie probe: allocation failed"
+    lib.moearc_copy_h2d_async(ctx.raw, db, hb, nbytes)
+    ctx.sync()
+    ctx.timer_start()
+    for _ in range(reps):
+        lib.moearc_copy_h2d_async(ctx.raw, db, hb, nbytes)
+    ms = ctx.timer_stop()
+    lib.moearc_free_device(ctx.raw, db)
+    lib.moearc_x_host_free(hb)
+    return nbytes * reps / (ms / 1000.0) / 1e9
+
+
 def gpu_run(args, cfg, rank: int, world: int, dist) -> dict:
     import ctypes as C
 
@@ -208,8 +230,8 @@ def gpu_run(args, cfg, rank: int, world: int, dist) -> dict:
     cnt = (C.c_int * 8)()
     ctx._finish(lib.moearc_x_decoder_profile(dec.h, ms, cnt, 8), "profile")
     kernel_ms = {k: ms[i] for i, k in enumerate(["qkv", "attention", "o_proj", "moe_route", "moe_gate_up",
-                                                  "moe_down", "final_norm"])}
-    launches_per_step = sum(cnt[i] for i in range(7))
+                                                  "moe_down", "final_norm", "expert_fetch"])}
+    launches_per_step = sum(cnt[i] for i in range(8))
 
     sampler = ClockSampler() if rank == 0 else None
     if sampler:
@@ -233,14 +255,15 @@ def gpu_run(args, cfg, rank: int, world: int, dist) -> dict:
         ctx.sync()
     e2e_s = time.perf_counter() - t1
     clocks = sampler.stop() if sampler else None
+    pcie = pcie_h2d_gbs(ctx) if cfg.n_offload else None
     out = np.ctypeslib.as_array(C.cast(host_out, C.POINTER(C.c_float)), (H,)).copy()
     assert np.all(np.isfinite(out)), "non-finite decoder output"
     lib.moearc_x_host_free(host_in)
     lib.moearc_x_host_free(host_out)
     dec.close()
     ctx.close()
-    return {"ms_total": ms_total, "e2e_s": e2e_s, "kernel_ms": kernel_ms, "counts": [cnt[i] for i in range(7)],
-            "launches_per_step": launches_per_step, "clocks": clocks, "build_s": build_s}
+    return {"ms_total": ms_total, "e2e_s": e2e_s, "kernel_ms": kernel_ms, "counts": [cnt[i] for i in range(8)],
+            "launches_per_step": launches_per_step, "clocks": clocks, "build_s": build_s, "pcie_gbs": pcie}
 
 
 def main() -> None:
@@ -254,6 +277,8 @@ def main() -> None:
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--layers", type=int, default=0,
                     help="blocks to build (default: the configuration's); a smaller model for profiling")
+    ap.add_argument("--offload", type=int, default=0,
+                    help="blocks whose experts stay in pinned host memory (configs[2] mode (b): 30)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -262,12 +287,16 @@ def main() -> None:
     cfg = DecoderConfig.gpt_oss_120b() if args.config == "120b" else DecoderConfig.gpt_oss_20b()
     if args.layers:
         cfg.n_layer = args.layers
+    cfg.n_offload = min(args.offload, cfg.n_layer)
+    residency = ("experts resident in HBM" if not cfg.n_offload else
+                 f"mode (b): experts of blocks 0-{cfg.n_offload - 1} in pinned host memory, the routed ones "
+                 f"fetched over PCIe every step")
     workload = (f"configs[{2 if args.config == '120b' else 1}] gpt-oss-{args.config} shape, batch-1 decode, "
-                f"depth {args.depth}, experts resident in HBM")
+                f"depth {args.depth}, {residency}")
     config = {"workload": workload, "n_layer": cfg.n_layer, "n_embd": cfg.n_embd, "n_expert": cfg.n_expert,
               "top_k": cfg.n_expert_used, "n_ff": cfg.n_ff, "expert_type": "MXFP4", "kv": "bf16, pages of 32",
               "attention": "64 q / 8 kv heads x 64, sinks, alternating full / 128-key window",
-              "depth": args.depth, "batch": 1,
+              "depth": args.depth, "batch": 1, "offloaded_blocks": cfg.n_offload,
               "l2": "weights (~63 GB) far exceed the 126 MB L2; no flush"}
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -353,6 +382,15 @@ def main() -> None:
         "clocks": r["clocks"],
         "build_s": r["build_s"],
     }
+    if cfg.n_offload:
+        # mode (b) is bound by PCIe: the offloaded blocks' routed experts cross it every step
+        pcie_b = cfg.n_offload * expert_b
+        pcie_gbs = pcie_b / (ms_step / 1000.0) / 1e9
+        line["roofline_hbm_gate_up"] = line["roofline"]
+        line["roofline"] = {"bound": "pcie", "kernel": "expert fetch of the offloaded blocks (whole step)",
+                            "achieved": pcie_gbs, "peak": r["pcie_gbs"], "unit": "GB/s",
+                            "frac": pcie_gbs / r["pcie_gbs"], "peak_kind": "measured in this run (pinned H2D copy)",
+                            "traffic": None, "bytes_per_step": pcie_b}
     if world == 1 and not args.no_cpu:
         line["cpu_baseline"] = cpu_decode_sample(cfg, budget_s=12.0)
     print(json.dumps(line))

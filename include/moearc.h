@@ -209,6 +209,10 @@ typedef struct {
     unsigned int has_sinks;
     unsigned int n_ctx;                       /* positions the KV cache holds */
     unsigned long long seed;
+    /* Blocks 0 .. n_offload-1 keep their packed expert banks in pinned, device-mapped host
+     * memory (the -ncmoe mirror, moe.rs:1179-1299); each step fetches the routed experts of
+     * such a block over PCIe into device slots, with no host round trip. 0: all resident. */
+    unsigned int n_offload;
 } moearc_x_decoder_cfg;
 moearc_x_decoder *moearc_x_decoder_create(moearc_ctx *c, const moearc_x_decoder_cfg *cfg);
 void moearc_x_decoder_destroy(moearc_x_decoder *d);
@@ -224,11 +228,13 @@ int moearc_x_decoder_step(moearc_x_decoder *d);
 int moearc_x_decoder_use_graph(moearc_x_decoder *d, int on);
 /* One step without the graph and with an event after every kernel: ms[k] gets the device time
  * of kernel kind k (0 Q/K/V, 1 attention, 2 O projection, 3 MoE route, 4 MoE gate-up, 5 MoE
- * down, 6 final norm) summed over the blocks, counts[k] the launches; n >= 7. */
+ * down, 6 final norm, 7 expert fetch of an offloaded block) summed over the blocks, counts[k]
+ * the launches; n >= 7 (kinds >= n are not reported). */
 int moearc_x_decoder_profile(moearc_x_decoder *d, float *ms, int *counts, int n);
 /* Device pointer (and size) of one block's tensor: 0 attn_norm, 1 ffn_norm, 2 sinks,
  * 3 router, 4 K pool, 5 V pool, 6 page table, 7 packed Q/K/V, 8 packed O, 9 packed gate-up,
- * 10 packed down, 11 output norm. */
+ * 10 packed down, 11 output norm. For an offloaded block, 9 and 10 are device-visible
+ * pointers of the pinned host banks. */
 void *moearc_x_decoder_tensor(moearc_x_decoder *d, int which, unsigned int layer, unsigned long *bytes);
 /* The seed tensor `kind` of block `layer` was generated from, given the model seed. */
 unsigned long long moearc_x_decoder_seed(moearc_x_decoder *d, int kind, unsigned int layer,

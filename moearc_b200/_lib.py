@@ -96,7 +96,7 @@ class DecoderCfg(C.Structure):
                 ("act", U), ("alpha", F), ("limit", F), ("n_swa", U), ("swa_pattern", U),
                 ("rope_base", F), ("rope_freq_scale", F), ("rope_ext_factor", F), ("rope_attn_factor", F),
                 ("rope_corr_lo", F), ("rope_corr_hi", F), ("rms_eps", F), ("has_sinks", U), ("n_ctx", U),
-                ("seed", C.c_ulonglong)]
+                ("seed", C.c_ulonglong), ("n_offload", U)]
 
 
 class MoeDesc(C.Structure):

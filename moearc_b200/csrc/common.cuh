@@ -192,6 +192,12 @@ __device__ __forceinline__ void fence_acq_rel_gpu() { asm volatile("fence.acq_re
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;\n" ::: "memory"); }
 __device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory"); }
 
+// Device slots of an offloaded MoE block: the routed experts' packed gate-up and down banks,
+// one slot per distinct routed expert, filled from pinned host memory each step.
+struct moe_offload {
+    uint8_t *gu_stage, *dn_stage;
+};
+
 template <typename... KArgs, typename... Args>
 inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
                               Args &&...args) {

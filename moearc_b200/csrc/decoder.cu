@@ -14,6 +14,11 @@
 // Weights are random (seeded) and generated on the device; nothing is read from a model file.
 // The position lives in device memory and is advanced by the step's last kernel, so the whole
 // step — 7 kernels per block — is captured once as a CUDA graph and replayed.
+//
+// Blocks below cfg.n_offload keep their packed expert banks in pinned, device-mapped host memory
+// (the -ncmoe mirror, moe.rs:1179-1299 StaticSplit with every expert of the block streamed);
+// their MoE adds two fetch kernels that copy the routed experts over PCIe into device slots, so
+// the step stays one graph with no host round trip.
 #include <algorithm>
 #include <cmath>
 #include <vector>
@@ -25,7 +30,8 @@ namespace moearc {
 int moe_forward_impl(moearc_x_moe *m, const float *x, unsigned n_tokens, const float *norm_w, float eps,
                      const float *router_w, const float *router_b, const void *gateup_packed,
                      const void *down_packed, const float *residual, float *out,
-                     std::vector<cudaEvent_t> *marks = nullptr, std::vector<int> *kinds = nullptr);
+                     std::vector<cudaEvent_t> *marks = nullptr, std::vector<int> *kinds = nullptr,
+                     const moe_offload *off = nullptr);
 size_t attn_scratch_bytes(size_t n_heads, size_t head_dim, int n_splits);
 int attn_launch(moearc_ctx *c, float *out, const float *q, const void *kp, const void *vp,
                 const unsigned *table, const float *sinks, size_t n_heads, size_t n_kv_heads,
@@ -73,7 +79,8 @@ struct moearc_x_decoder {
     int Dq, Dkv, n_qkv;
     struct layer {
         float *attn_norm, *ffn_norm, *sinks, *router;
-        void *wqkv, *wo, *gateup, *down;
+        void *wqkv, *wo, *gateup, *down;  // gateup/down: device-visible host banks when offloaded
+        void *gu_host, *dn_host;           // pinned host allocations of an offloaded block
         uint16_t *k_pages, *v_pages;
         const unsigned *table;
         int window;
@@ -94,6 +101,8 @@ struct moearc_x_decoder {
     int max_splits = 1;
     int pos = 0;
     std::vector<void *> allocs;
+    std::vector<void *> host_allocs;  // pinned (cudaHostAlloc) banks of offloaded blocks
+    moe_offload off{};                // device slots the offloaded blocks' experts are fetched into
     cudaGraph_t graph = nullptr;
     cudaGraphExec_t exec = nullptr;
     bool use_graph = true;
@@ -130,7 +139,7 @@ struct step_marks {
 
 // Everything one step enqueues, in order (captured into a graph on first use). With `pm`,
 // an event follows every kernel: kinds 0 qkv, 1 attention (+ combine), 2 o-proj, 3 MoE route,
-// 4 MoE gate-up, 5 MoE down, 6 final norm.
+// 4 MoE gate-up, 5 MoE down, 6 final norm, 7 expert fetch (offloaded blocks).
 int enqueue_step(moearc_x_decoder *d, step_marks *pm = nullptr) {
     moearc_ctx *c = d->c;
     const auto &cfg = d->cfg;
@@ -159,7 +168,8 @@ int enqueue_step(moearc_x_decoder *d, step_marks *pm = nullptr) {
         if (rc) return rc;
         if (pm) pm->mark(c->stream, 2);
         rc = moe_forward_impl(d->moe, d->h, 1, b.ffn_norm, cfg.rms_eps, b.router, nullptr, b.gateup, b.down,
-                              d->h, d->h, pm ? &pm->ev : nullptr, pm ? &pm->kind : nullptr);
+                              d->h, d->h, pm ? &pm->ev : nullptr, pm ? &pm->kind : nullptr,
+                              l < cfg.n_offload ? &d->off : nullptr);
         if (rc) return rc;
     }
     if (launch_pdl(k_step_end, dim3(1), dim3(512), 0, c->stream, d->out, (const float *)d->h,
@@ -182,7 +192,7 @@ moearc_x_decoder *moearc_x_decoder_create(moearc_ctx *c, const moearc_x_decoder_
     const auto &g = *cfg;
     if (g.n_layer == 0 || g.n_head % std::max(1u, g.n_head_kv) || (g.head_dim != 64 && g.head_dim != 128))
         return nullptr;
-    if (g.n_head / g.n_head_kv > 8 || g.n_ctx == 0) return nullptr;
+    if (g.n_head / g.n_head_kv > 8 || g.n_ctx == 0 || g.n_offload > g.n_layer) return nullptr;
     auto *d = new moearc_x_decoder();
     d->c = c;
     d->cfg = g;
@@ -273,6 +283,19 @@ moearc_x_decoder *moearc_x_decoder_create(moearc_ctx *c, const moearc_x_decoder_
         cudaGetLastError();
         return fail();
     }
+    // offloaded blocks: packed on the device into pack_tmp, then copied to pinned host banks;
+    // one device slot per expert a token routes to
+    const size_t gu_stride = moearc_x_moe_packed_bytes(&md, 0), dn_stride = moearc_x_moe_packed_bytes(&md, 1);
+    void *pack_tmp = nullptr;
+    if (g.n_offload) {
+        d->off.gu_stage = static_cast<uint8_t *>(d->alloc(g.n_expert_used * gu_stride));
+        d->off.dn_stage = static_cast<uint8_t *>(d->alloc(g.n_expert_used * dn_stride));
+        if (!d->off.gu_stage || !d->off.dn_stage || cudaMalloc(&pack_tmp, g.n_expert * (gu_stride + dn_stride)) != cudaSuccess) {
+            cudaGetLastError();
+            cudaFree(staging);
+            return fail();
+        }
+    }
     const unsigned ekind = (g.expert_type == T_MXFP4) ? 2 : 3;
     const float esig = 0.01f;
     d->L.resize(g.n_layer);
@@ -288,8 +311,15 @@ moearc_x_decoder *moearc_x_decoder_create(moearc_ctx *c, const moearc_x_decoder_
         b.router = static_cast<float *>(d->alloc(sizeof(float) * g.n_expert * H));
         b.wqkv = d->alloc(qkv_elems * 2);
         b.wo = d->alloc(wo_elems * 2);
-        b.gateup = d->alloc(2 * bank_bytes);
-        b.down = d->alloc(bank_bytes);
+        const bool offl = l < g.n_offload;
+        b.gu_host = b.dn_host = nullptr;
+        if (offl) {
+            b.gateup = static_cast<uint8_t *>(pack_tmp);
+            b.down = static_cast<uint8_t *>(pack_tmp) + g.n_expert * gu_stride;
+        } else {
+            b.gateup = d->alloc(2 * bank_bytes);
+            b.down = d->alloc(bank_bytes);
+        }
         b.k_pages = static_cast<uint16_t *>(d->alloc(b.pool_tokens * d->Dkv * 2));
         b.v_pages = static_cast<uint16_t *>(d->alloc(b.pool_tokens * d->Dkv * 2));
         if (!b.attn_norm || !b.ffn_norm || (g.has_sinks && !b.sinks) || !b.router || !b.wqkv || !b.wo ||
@@ -314,12 +344,29 @@ moearc_x_decoder *moearc_x_decoder_create(moearc_ctx *c, const moearc_x_decoder_
         ok &= synth(c, s8 + bank_bytes, blocks, ekind, tensor_seed(g.seed, 9, l), esig) == OK;
         ok &= synth(c, s8 + 2 * bank_bytes, blocks, ekind, tensor_seed(g.seed, 10, l), esig) == OK;
         ok &= moearc_x_moe_pack(d->moe, s8, s8 + bank_bytes, s8 + 2 * bank_bytes, g.n_expert, b.gateup, b.down) == OK;
+        if (offl && ok) {
+            const size_t gb = g.n_expert * gu_stride, db = g.n_expert * dn_stride;
+            void *gdev = nullptr, *ddev = nullptr;
+            if (cudaHostAlloc(&b.gu_host, gb, cudaHostAllocMapped | cudaHostAllocPortable) != cudaSuccess) b.gu_host = nullptr;
+            else d->host_allocs.push_back(b.gu_host);
+            if (cudaHostAlloc(&b.dn_host, db, cudaHostAllocMapped | cudaHostAllocPortable) != cudaSuccess) b.dn_host = nullptr;
+            else d->host_allocs.push_back(b.dn_host);
+            ok = b.gu_host && b.dn_host && cudaStreamSynchronize(c->stream) == cudaSuccess &&
+                 cudaMemcpy(b.gu_host, b.gateup, gb, cudaMemcpyDeviceToHost) == cudaSuccess &&
+                 cudaMemcpy(b.dn_host, b.down, db, cudaMemcpyDeviceToHost) == cudaSuccess &&
+                 cudaHostGetDevicePointer(&gdev, b.gu_host, 0) == cudaSuccess &&
+                 cudaHostGetDevicePointer(&ddev, b.dn_host, 0) == cudaSuccess;
+            cudaGetLastError();
+            b.gateup = gdev;
+            b.down = ddev;
+        }
         // an empty cache reads as zeros; fill_kv writes synthetic contents
         ok &= cudaMemsetAsync(b.k_pages, 0, b.pool_tokens * d->Dkv * 2, c->stream) == cudaSuccess;
         ok &= cudaMemsetAsync(b.v_pages, 0, b.pool_tokens * d->Dkv * 2, c->stream) == cudaSuccess;
     }
     ok &= cudaStreamSynchronize(c->stream) == cudaSuccess;
     cudaFree(staging);
+    if (pack_tmp) cudaFree(pack_tmp);
     if (!ok) return fail();
     return d;
 }
@@ -333,6 +380,7 @@ void moearc_x_decoder_destroy(moearc_x_decoder *d) {
     if (d->qkv) dense_destroy(d->qkv);
     if (d->wo) dense_destroy(d->wo);
     for (void *p : d->allocs) cudaFree(p);
+    for (void *p : d->host_allocs) cudaFreeHost(p);
     delete d;
 }
 
@@ -401,7 +449,8 @@ int moearc_x_decoder_step(moearc_x_decoder *d) {
 
 // One step, not graphed, with an event after every kernel; ms[k] receives the total device
 // time of kernel kind k (0 qkv, 1 attention, 2 o-proj, 3 MoE route, 4 MoE gate-up, 5 MoE down,
-// 6 final norm) and counts[k] how many launches of that kind ran.
+// 6 final norm, 7 expert fetch) and counts[k] how many launches of that kind ran (kinds >= n
+// are left out).
 int moearc_x_decoder_profile(moearc_x_decoder *d, float *ms, int *counts, int n) {
     if (!d || !ms || n < 7) return ERR;
     if ((unsigned)d->pos >= d->cfg.n_ctx) return ERR_ARG;

@@ -917,6 +917,8 @@ __global__ void __launch_bounds__(XROUTE_WARPS * 32) k_xroute(xroute_args a) {
 // Routing tables of the decode path, in shared memory.
 struct xtab {
     int G, C;                         // groups, columns (= T * K)
+    int n_slots;                      // distinct experts, ascending
+    int grp_slot[MAX_TK], slot_expert[MAX_TK];
     int grp_expert[MAX_TK], grp_col0[MAX_TK], grp_ntok[MAX_TK];
     int col_tok[MAX_TK], col_grp[MAX_TK];
     int col_of[MAX_TK];               // column of choice i = t * K + m
@@ -1037,6 +1039,16 @@ __device__ void xbuild(xtab &tb, const float *logits, int T, int E, int K, int g
             tb.G = __popc(gs);
             tb.C = C;
         }
+        __syncwarp();
+        // slots: the distinct experts in ascending order (groups of one expert are adjacent)
+        const int G = __popc(gs);
+        const int ge = lane < G ? tb.grp_expert[lane] : -1;
+        const int gprev = __shfl_up_sync(0xffffffffu, ge, 1);
+        const bool new_slot = lane < G && (lane == 0 || gprev != ge);
+        const unsigned ns = __ballot_sync(0xffffffffu, new_slot);
+        if (lane < G) tb.grp_slot[lane] = __popc(ns & le) - 1;
+        if (new_slot) tb.slot_expert[__popc(ns & le) - 1] = ge;
+        if (lane == 0) tb.n_slots = __popc(ns);
     }
     __syncthreads();
 }
@@ -1066,6 +1078,7 @@ struct xexp_args {
     float *part;
     unsigned *ctr;
     int maxc;
+    int by_slot;              // bank holds one expert per slot (staged offload), not all experts
     int *status;
 };
 
@@ -1156,7 +1169,8 @@ __global__ void __launch_bounds__(XW * 32, 1) k_xexpert(xexp_args a) {
         if (weights) {
             fence_proxy_async();
             mbar_expect_tx(bar, (unsigned)(n * a.elem_bytes + ntok * n * 256));
-            bulk_g2s(st, a.bank + (size_t)tb.grp_expert[c.g] * a.bank_stride + (size_t)((c.tr * nkt + kt) * a.elem_bytes),
+            const int bank_ix = a.by_slot ? tb.grp_slot[c.g] : tb.grp_expert[c.g];
+            bulk_g2s(st, a.bank + (size_t)bank_ix * a.bank_stride + (size_t)((c.tr * nkt + kt) * a.elem_bytes),
                      (unsigned)(n * a.elem_bytes), bar);
         }
         if (acts)
@@ -1169,6 +1183,11 @@ __global__ void __launch_bounds__(XW * 32, 1) k_xexpert(xexp_args a) {
     const cur start = at(qa);
     cur ic = start;
     long n_issued = 0;  // lane 0's count
+    if (MODE == 1 && a.by_slot) {
+        // staged down banks are the previous kernel's output: nothing streams before the wait
+        pdl_trigger();
+        pdl_wait();
+    }
     if (lane == 0)
         for (int s = 0; s < XSTAGES && ic.q < qb; ++s) {
             issue(ic, s, true, MODE == 0);
@@ -1414,6 +1433,66 @@ __device__ __forceinline__ unsigned long long gtimer() {
     unsigned long long t;
     asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
     return t;
+}
+
+// ---- expert offload: the routed experts of a block fetched from pinned host memory ------
+//
+// The -ncmoe mirror (moe.rs:1179-1299 StaticSplit, stage() 2521-2564): the packed banks of an
+// offloaded block live in pinned, device-mapped host memory. Instead of reading the routing back
+// to the host and issuing copies (moe.rs:2121-2149), each fetch kernel builds the block's
+// routing tables itself and copies the distinct routed experts' banks over PCIe into device
+// slots (slot s = the s-th distinct expert, ascending), so an offloaded block is still a chain
+// of kernels with no host round trip. Gate-up banks are fetched before the gate-up kernel; the
+// down banks are fetched while the gate-up kernel computes.
+
+constexpr int XFETCH_THREADS = 256;
+
+struct xfetch_args {
+    const float *logits;  // [T][E], the router kernel's output
+    int T, E, K, gating;
+    const uint8_t *host;  // device-visible pointer of the pinned bank (all experts)
+    size_t stride;        // packed bytes per expert (a multiple of 16)
+    uint8_t *stage;       // device slots, one per distinct routed expert
+};
+
+// Copy n16 16-byte words, the grid's threads striding, eight loads in flight per thread (host
+// memory answers over PCIe with a latency of microseconds).
+__device__ __forceinline__ void copy16(const uint4 *src, uint4 *dst, size_t n16) {
+    const size_t nt = (size_t)gridDim.x * blockDim.x;
+    size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
+    for (; i + 7 * nt < n16; i += 8 * nt) {
+        uint4 v[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) v[u] = __ldcs(src + i + u * nt);
+#pragma unroll
+        for (int u = 0; u < 8; ++u) dst[i + u * nt] = v[u];
+    }
+    for (; i < n16; i += nt) dst[i] = __ldcs(src + i);
+}
+
+// MODE 0 (gate-up banks) follows the router kernel; MODE 1 (down banks) follows the gate-up
+// kernel and needs nothing from it: the logits it reads were final before the gate-up kernel
+// got past its own wait. MODE 1 waits for the gate-up kernel at its end, so the down kernel's
+// wait on this one covers both.
+// At most 48 registers a thread, so that a down-fetch CTA fits on an SM beside a gate-up CTA
+// (512 threads x 96 registers) and the two run together.
+template <int MODE>
+__global__ void __launch_bounds__(XFETCH_THREADS, 5) k_xfetch(xfetch_args a) {
+    __shared__ xtab tb;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (MODE == 0) {
+        pdl_wait();
+        pdl_trigger();
+    }
+    xbuild(tb, a.logits, a.T, a.E, a.K, a.gating, warp, lane);
+    const size_t n16 = a.stride / 16;
+    for (int s = 0; s < tb.n_slots; ++s)
+        copy16(reinterpret_cast<const uint4 *>(a.host + (size_t)tb.slot_expert[s] * a.stride),
+               reinterpret_cast<uint4 *>(a.stage + (size_t)s * a.stride), n16);
+    if (MODE == 1) {
+        pdl_trigger();
+        pdl_wait();
+    }
 }
 
 constexpr unsigned long long XWAIT_NS = 200000000ull;  // a wait on other CTAs gives up after 0.2 s
@@ -2104,7 +2183,7 @@ namespace moearc {
 int moe_forward_impl(moearc_x_moe *m, const float *x, unsigned n_tokens, const float *norm_w, float eps,
                      const float *router_w, const float *router_b, const void *gateup_packed,
                      const void *down_packed, const float *residual, float *out,
-                     std::vector<cudaEvent_t> *marks, std::vector<int> *kinds) {
+                     std::vector<cudaEvent_t> *marks, std::vector<int> *kinds, const moe_offload *off) {
     auto mark = [&](int k) {
         if (!marks) return;
         cudaEvent_t e;
@@ -2125,7 +2204,10 @@ int moe_forward_impl(moearc_x_moe *m, const float *x, unsigned n_tokens, const f
     const tab_view tab = make_tab(m);
     launch_scope ls(c, "moe_forward", (unsigned long)m->H, (unsigned)T);
 
-    if (m->fused) {
+    // an offloaded block runs the decode path with the fetch kernels (gateup_packed and
+    // down_packed are then device-visible pointers of pinned host banks)
+    if (off && (!m->xpath || !off->gu_stage || !off->dn_stage)) return ERR_ARG;
+    if (m->fused && !off) {
         xfused_args f{};
         f.x = x;
         f.norm_w = norm_w;
@@ -2182,9 +2264,21 @@ int moe_forward_impl(moearc_x_moe *m, const float *x, unsigned n_tokens, const f
                        xr) != cudaSuccess)
             return ERR;
         mark(3);
+        const size_t gu_stride = (size_t)2 * m->ntr_i * m->nkt_h * m->tile_bytes;
+        const size_t dn_stride = (size_t)m->ntr_h * m->nkt_i * m->tile_bytes;
+        xfetch_args fa{m->logits, T, m->E, m->K, m->gating, nullptr, 0, nullptr};
+        if (off) {
+            fa.host = static_cast<const uint8_t *>(gateup_packed);
+            fa.stride = gu_stride;
+            fa.stage = off->gu_stage;
+            if (launch_pdl(k_xfetch<0>, dim3(c->sm_count), dim3(XFETCH_THREADS), 0, c->stream, fa) != cudaSuccess)
+                return ERR;
+            mark(7);
+        }
         xexp_args xa{};
-        xa.bank = static_cast<const uint8_t *>(gateup_packed);
-        xa.bank_stride = (size_t)2 * m->ntr_i * m->nkt_h * m->tile_bytes;
+        xa.bank = off ? off->gu_stage : static_cast<const uint8_t *>(gateup_packed);
+        xa.bank_stride = gu_stride;
+        xa.by_slot = off ? 1 : 0;
         xa.ntr = m->ntr_i;
         xa.nkt = m->nkt_h;
         xa.tile_bytes = m->tile_bytes;
@@ -2222,9 +2316,17 @@ int moe_forward_impl(moearc_x_moe *m, const float *x, unsigned n_tokens, const f
                        c->stream, xa) != cudaSuccess)
             return ERR;
         mark(4);
+        if (off) {
+            fa.host = static_cast<const uint8_t *>(down_packed);
+            fa.stride = dn_stride;
+            fa.stage = off->dn_stage;
+            if (launch_pdl(k_xfetch<1>, dim3(c->sm_count), dim3(XFETCH_THREADS), 0, c->stream, fa) != cudaSuccess)
+                return ERR;
+            mark(7);
+        }
         xexp_args xd = xa;
-        xd.bank = static_cast<const uint8_t *>(down_packed);
-        xd.bank_stride = (size_t)m->ntr_h * m->nkt_i * m->tile_bytes;
+        xd.bank = off ? off->dn_stage : static_cast<const uint8_t *>(down_packed);
+        xd.bank_stride = dn_stride;
         xd.ntr = m->ntr_h;
         xd.nkt = m->nkt_i;
         xd.elem_bytes = m->tile_bytes;
@@ -2313,7 +2415,7 @@ int moearc_x_moe_forward(moearc_x_moe *m, const float *x, unsigned n_tokens, con
                          const float *router_b, const void *gateup_packed, const void *down_packed,
                          const float *residual, float *out) {
     return moe_forward_impl(m, x, n_tokens, nullptr, 0.f, router_w, router_b, gateup_packed, down_packed,
-                            residual, out, nullptr, nullptr);
+                            residual, out, nullptr, nullptr, nullptr);
 }
 
 void *moearc_x_moe_buffer(moearc_x_moe *m, int which) {

@@ -45,6 +45,9 @@ class DecoderConfig:
     has_sinks: int = 1
     n_ctx: int = 4096
     seed: int = 0x5EED
+    # blocks 0 .. n_offload-1 keep their experts in pinned host memory, fetched over PCIe each
+    # step (the -ncmoe mirror, moe.rs:1179-1299); 0 = all resident
+    n_offload: int = 0
 
     def yarn(self, factor: float, n_ctx_orig: int, beta_fast: float = 32.0, beta_slow: float = 1.0):
         """YaRN parameters the way reference.rs:572-591 derives them (RopeScaling::yarn)."""

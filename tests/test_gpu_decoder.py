@@ -119,3 +119,24 @@ def test_fill_kv_sets_the_depth_and_decoding_continues(ctx):
     out = dec.output()
     assert np.all(np.isfinite(out)) and dec.pos == 1501
     dec.close()
+
+
+@pytest.mark.parametrize("etype,n_expert,k", [(O.MXFP4, 8, 2), (O.Q4_0, 16, 4)])
+def test_expert_offload_matches_the_resident_decoder(ctx, etype, n_expert, k):
+    """Blocks whose experts live in pinned host memory (fetched over PCIe into device slots each
+    step) give the same bits as the all-resident decoder: the fetch changes where the banks are
+    read from, not the arithmetic."""
+    kw = dict(n_layer=3, n_embd=256, n_head=8, n_head_kv=2, head_dim=64, n_expert=n_expert,
+              n_expert_used=k, n_ff=128, expert_type=etype, n_swa=40, swa_pattern=2, n_ctx=128,
+              seed=0x0FF1)
+    res = Decoder(ctx, DecoderConfig(**kw))
+    off = Decoder(ctx, DecoderConfig(**kw, n_offload=2))
+    for pos in range(12):
+        x = O.synth_normal_f32(0x2000 + pos, kw["n_embd"], 1.0)
+        for d in (res, off):
+            d.set_input(x)
+            d.step()
+        a, b = res.output(), off.output()
+        assert np.array_equal(a.view(np.uint32), b.view(np.uint32)), f"token {pos}"
+    off.close()
+    res.close()
