@@ -14,9 +14,10 @@ the 126 MB L2, so consecutive steps never hit in L2 for them; no flush is needed
 value     tokens/s with the input already on the device, timed with CUDA events over K steps
 e2e       the same through the public API with host buffers: per step the input embedding is
           copied from pinned host memory and the output read back, wall-clock timed
-roofline  the MoE gate-up grouped GEMV (the path's dominant kernel): algorithmic bytes per
-          launch (4 experts x 2 matrices x 2880 x 2880 MXFP4 = 35.25 MB) over its average
-          device time, against the measured HBM copy bandwidth in MEASURED_PEAKS.json
+roofline  the MoE expert kernel (the path's dominant kernel: gate-up, SwiGLU, down and the
+          combine in one launch): algorithmic bytes per launch (4 experts x 3 matrices x 2880 x
+          2880 MXFP4 = 52.88 MB) over its average device time, against the measured HBM copy
+          bandwidth in MEASURED_PEAKS.json
           (with --offload: the PCIe bytes of the offloaded blocks' routed experts per step over the
           step time, against a pinned host-to-device copy measured in the same run)
 Multi-GPU: batch-1 decode does not shard; with N GPUs each rank runs an independent replica
@@ -45,15 +46,17 @@ METRIC = "MoE decode tok/s at gpt-oss-120b shape; expert-GEMM HBM GB/s vs 8 TB/s
 UNIT = "tok/s"
 
 
-def gate_up_traffic() -> float | None:
-    """DRAM read + write bytes of one gate-up launch, from the committed ncu capture summary
-    (profiles/moe_and_dense_kernels_gpt_oss_120b_1layer.md, the gate-up row); None if absent."""
+def expert_traffic(fused: bool) -> float | None:
+    """DRAM read + write bytes of one launch of the roofline kernel, from the committed ncu
+    capture summary (profiles/moe_and_dense_kernels_gpt_oss_120b_1layer.md: the fused gate-up +
+    down row, or the gate-up row of the split kernels); None if absent."""
     import re
     p = os.path.join(ROOT, "profiles", "moe_and_dense_kernels_gpt_oss_120b_1layer.md")
     if not os.path.exists(p):
         return None
+    row = "| `k_moe_fused<39,false>`" if fused else "| `k_xexpert<39,0>`"
     for line in open(p):
-        if line.startswith("| `k_xexpert<39,0>`"):
+        if line.startswith(row):
             m = re.search(r"\| ([\d.]+) MB / ([\d.]+) MB \|", line)
             if m:
                 return (float(m.group(1)) + float(m.group(2))) * 1e6
@@ -344,7 +347,8 @@ def main() -> None:
 
     peak, peak_kind = load_peaks()
     H, I, k = cfg.n_embd, cfg.n_ff, cfg.n_expert_used
-    gu_bytes = k * 2 * I * H // 32 * 17
+    fused = r["counts"][5] == 0  # gate-up and down in one launch (the default decode path)
+    gu_bytes = k * (3 if fused else 2) * I * H // 32 * 17
     n_gu = max(1, r["counts"][4])
     gu_ms = r["kernel_ms"]["moe_gate_up"] / n_gu
     achieved = gu_bytes / (gu_ms / 1000.0) / 1e9
@@ -368,9 +372,11 @@ def main() -> None:
         "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded random weights, N(0,1) inputs)",
         "config": config,
-        "roofline": {"bound": "hbm", "kernel": "moe gate-up grouped GEMV (MXFP4, tensor cores)",
+        "roofline": {"bound": "hbm",
+                     "kernel": ("moe gate-up + SwiGLU + down + combine, one launch (k_moe_fused, MXFP4, tensor cores)"
+                                if fused else "moe gate-up grouped GEMV (MXFP4, tensor cores)"),
                      "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
-                     "peak_kind": peak_kind, "traffic": gate_up_traffic(),
+                     "peak_kind": peak_kind, "traffic": expert_traffic(fused),
                      "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum, profiles/",
                      "bytes_per_launch": gu_bytes, "avg_launch_ms": gu_ms,
                      "frac_of_8tbs": achieved / 8000.0},

@@ -57,6 +57,7 @@ struct moearc_x_moe {
     unsigned *x_ctr_gu, *x_ctr_dn;
     // the fused decode kernel (k_moe_fused): one cooperative launch per layer
     bool fused;
+    bool fused_gd;  // gate-up + down in one launch after k_xroute (opt-in)
     int f_grid, f_stage, f_smem, f_bsmem;
     unsigned *f_ready, *f_bar;
     // device scratch (one allocation)
@@ -1557,7 +1558,14 @@ __device__ __forceinline__ void load_b_row(const uint32_t *brow, int kt, int lan
     }
 }
 
-template <int WT>
+// ROUTE = false: the gate-up and down phases only, after k_xroute (logits and the gate-up B
+// fragments are its output). That launch is not cooperative but PDL-chained, so it starts under
+// the router kernel; its CTAs still wait on one another (down pieces on ready counts), which
+// needs them all resident: the grid is at most one CTA per SM, each CTA takes more than half an
+// SM's shared memory, and a CTA lets the next kernel launch only once it runs, so the next
+// kernel cannot take an SM before every CTA of this one has one. Every wait is bounded. With no
+// grid barrier, the ready counts are reset by the last warp to leave, for the next launch.
+template <int WT, bool ROUTE>
 __global__ void __launch_bounds__(XW * 32, 1) k_moe_fused(xfused_args a) {
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ __align__(8) uint64_t bars[XW][XSTAGES];
@@ -1581,16 +1589,26 @@ __global__ void __launch_bounds__(XW * 32, 1) k_moe_fused(xfused_args a) {
     }
     // router rows of this warp: e with floor(e * NW / E) == gw; fetch them to L2 now (static)
     const int e_lo = (int)((gw * a.E + NW - 1) / NW), e_hi = (int)(((gw + 1) * a.E + NW - 1) / NW);
-    if (lane == 0)
+    if (ROUTE && lane == 0)
         for (int e = e_lo; e < e_hi; ++e) bulk_prefetch_l2(a.router + (size_t)e * H, (unsigned)(H * 4));
     const int np_dn = (a.nkt_i + a.ch_dn - 1) / a.ch_dn;
-    if (blockIdx.x == 0)
+    if (ROUTE && blockIdx.x == 0)
         for (int i = threadIdx.x; i < a.K * a.T * np_dn; i += blockDim.x) a.ready[i] = 0u;
     pdl_wait();
     TRACE(1);
+    if (!ROUTE) {
+        pdl_trigger();
+        // the router kernel's gate-up B fragments of every token, into shared memory (xbuild's
+        // barrier orders the copy before the first use)
+        if (a.b_smem) {
+            const uint4 *src = reinterpret_cast<const uint4 *>(a.xfrag);
+            uint4 *dst = reinterpret_cast<uint4 *>(xf);
+            for (int i = threadIdx.x; i < a.T * nblk_h * 8; i += blockDim.x) dst[i] = __ldcg(src + i);
+        }
+    }
 
     // ---- route ----
-    for (int t = 0; t < a.T; ++t) {
+    for (int t = 0; ROUTE && t < a.T; ++t) {
         const float4 *xr = reinterpret_cast<const float4 *>(a.x + (size_t)t * H);
         float ss = 0.f;
         for (int c = threadIdx.x; c < n4; c += XW * 32) {
@@ -1648,9 +1666,11 @@ __global__ void __launch_bounds__(XW * 32, 1) k_moe_fused(xfused_args a) {
         }
         __syncthreads();
     }
-    grid_barrier(a.bar, a.status);
-    // every CTA is resident and past the route: the next kernel may launch
-    pdl_trigger();
+    if (ROUTE) {
+        grid_barrier(a.bar, a.status);
+        // every CTA is resident and past the route: the next kernel may launch
+        pdl_trigger();
+    }
     TRACE(2);
 
     // ---- tables ----
@@ -1740,6 +1760,7 @@ __global__ void __launch_bounds__(XW * 32, 1) k_moe_fused(xfused_args a) {
     cur cc = locate(0);
     long kf = -1;
     bool gu_done = n_gu == 0;
+    bool leave_last = false;
     // finishing steps shared by both runs: fence the warp's partials, arrive on its counters and
     // finish the units it completed last
     // warps holding pieces of segment s: with at least one piece per warp, the run from the
@@ -1846,6 +1867,20 @@ __global__ void __launch_bounds__(XW * 32, 1) k_moe_fused(xfused_args a) {
         }
     };
 
+    // the last warp of the grid to leave resets the ready counts (launches without a barrier)
+    auto leave = [&]() {
+        if (ROUTE) return;
+        __syncwarp();
+        if (lane == 0) {
+            __threadfence();
+            leave_last = atomicAdd(a.bar, 1u) == (unsigned)NW - 1;
+        }
+        if (__shfl_sync(0xffffffffu, leave_last ? 1 : 0, 0)) {
+            for (int i = lane; i < G * np_dn; i += 32) a.ready[i] = 0u;
+            if (lane == 0) a.bar[0] = 0u;
+        }
+    };
+
     float acc0[4], acc1[4];
     while (cc.q < n_all) {
         if (cc.dn && !gu_done) {
@@ -1936,11 +1971,13 @@ __global__ void __launch_bounds__(XW * 32, 1) k_moe_fused(xfused_args a) {
         n_issued = __shfl_sync(0xffffffffu, n_issued, 0);
         for (long j = kf; j < n_issued; ++j) mbar_wait(&bars[warp][j % XSTAGES], (unsigned)((j / XSTAGES) & 1), a.status);
         if (!gu_done) finish_gu();  // down warps elsewhere may be waiting on these rows
+        leave();
         return;
     }
     if (!gu_done) finish_gu();
     TRACE(9);
     finish_dn();
+    leave();
     TRACE(31);
 }
 
@@ -2063,7 +2100,8 @@ moearc_x_moe *moearc_x_moe_create(moearc_ctx *c, const moearc_x_moe_desc *d) {
         int occ = 0;
         const bool ok = m->xpath && m->f_smem <= 200 * 1024 && XW * XSTAGES * m->f_stage >= m->H * 4 &&
                         cudaOccupancyMaxActiveBlocksPerMultiprocessor(
-                            &occ, m->wtype == T_MXFP4 ? k_moe_fused<39> : k_moe_fused<2>, XW * 32, 0) == cudaSuccess;
+                            &occ, m->wtype == T_MXFP4 ? k_moe_fused<39, true> : k_moe_fused<2, true>, XW * 32,
+                            0) == cudaSuccess;
         cudaGetLastError();
         // one CTA per SM, fewer when even the smallest launch (one group per chosen expert)
         // would leave warps without a piece
@@ -2074,6 +2112,15 @@ moearc_x_moe *moearc_x_moe_create(moearc_ctx *c, const moearc_x_moe_desc *d) {
         // while the kernel before it finishes, and it measured slower than the three kernels
         const char *fz = std::getenv("MOEARC_FUSED_MOE");
         m->fused = ok && occ >= 1 && fz && fz[0] == '1';
+        // opt-in (MOEARC_MOE_FUSED_GD=1): k_xroute, then gate-up and down as one PDL-chained
+        // launch (its CTAs wait on one another, so it needs every CTA resident: one per SM, and
+        // more than half an SM's shared memory each, so no SM takes two). Correct (the same
+        // tests pass) but measured slower than separate gate-up and down kernels: each warp
+        // runs its gate-up and its down pieces in series, and the down pieces wait for the
+        // slowest gate-up segment of their k-range.
+        const char *gd = std::getenv("MOEARC_MOE_FUSED_GD");
+        m->fused_gd = m->xpath && m->f_smem <= 200 * 1024 && m->f_smem > 114 * 1024 && m->f_bsmem &&
+                      m->f_grid <= c->sm_count && gd && gd[0] == '1';
     }
 
     // one scratch allocation
@@ -2133,8 +2180,10 @@ moearc_x_moe *moearc_x_moe_create(moearc_ctx *c, const moearc_x_moe_desc *d) {
         set_smem(k_xexpert<2, 0>, 200 * 1024) != cudaSuccess ||
         set_smem(k_xexpert<2, 1>, 200 * 1024) != cudaSuccess ||
         set_smem(k_xroute, 200 * 1024) != cudaSuccess ||
-        set_smem(k_moe_fused<39>, 200 * 1024) != cudaSuccess ||
-        set_smem(k_moe_fused<2>, 200 * 1024) != cudaSuccess ||
+        set_smem(k_moe_fused<39, true>, 200 * 1024) != cudaSuccess ||
+        set_smem(k_moe_fused<2, true>, 200 * 1024) != cudaSuccess ||
+        set_smem(k_moe_fused<39, false>, 200 * 1024) != cudaSuccess ||
+        set_smem(k_moe_fused<2, false>, 200 * 1024) != cudaSuccess ||
         cudaStreamSynchronize(c->stream) != cudaSuccess) {
         cudaGetLastError();
         cudaFree(m->mem);
@@ -2207,7 +2256,7 @@ int moe_forward_impl(moearc_x_moe *m, const float *x, unsigned n_tokens, const f
     // an offloaded block runs the decode path with the fetch kernels (gateup_packed and
     // down_packed are then device-visible pointers of pinned host banks)
     if (off && (!m->xpath || !off->gu_stage || !off->dn_stage)) return ERR_ARG;
-    if (m->fused && !off) {
+    auto fused_args = [&]() {
         xfused_args f{};
         f.x = x;
         f.norm_w = norm_w;
@@ -2252,8 +2301,11 @@ int moe_forward_impl(moearc_x_moe *m, const float *x, unsigned n_tokens, const f
         f.ready = m->f_ready;
         f.bar = m->f_bar;
         f.status = m->status;
-        if (launch_coop(m->wtype == T_MXFP4 ? k_moe_fused<39> : k_moe_fused<2>, dim3(m->f_grid), dim3(XW * 32),
-                        (size_t)m->f_smem, c->stream, f) != cudaSuccess)
+        return f;
+    };
+    if (m->fused && !off) {
+        if (launch_coop(m->wtype == T_MXFP4 ? k_moe_fused<39, true> : k_moe_fused<2, true>, dim3(m->f_grid),
+                        dim3(XW * 32), (size_t)m->f_smem, c->stream, fused_args()) != cudaSuccess)
             return ERR;
         mark(4);
         return ls.finish();
@@ -2264,6 +2316,14 @@ int moe_forward_impl(moearc_x_moe *m, const float *x, unsigned n_tokens, const f
                        xr) != cudaSuccess)
             return ERR;
         mark(3);
+        if (m->fused_gd && !off) {
+            // gate-up and down in one launch: down weights stream while gate-up finishes
+            if (launch_pdl(m->wtype == T_MXFP4 ? k_moe_fused<39, false> : k_moe_fused<2, false>, dim3(m->f_grid),
+                           dim3(XW * 32), (size_t)m->f_smem, c->stream, fused_args()) != cudaSuccess)
+                return ERR;
+            mark(4);
+            return ls.finish();
+        }
         const size_t gu_stride = (size_t)2 * m->ntr_i * m->nkt_h * m->tile_bytes;
         const size_t dn_stride = (size_t)m->ntr_h * m->nkt_i * m->tile_bytes;
         xfetch_args fa{m->logits, T, m->E, m->K, m->gating, nullptr, 0, nullptr};

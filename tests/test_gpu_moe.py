@@ -167,3 +167,24 @@ def test_decode_path_is_batch_invariant_and_matches_the_oracle(ctx, wtype):
         worst = max(worst, rel_err(got[t] - res[t * H:(t + 1) * H], want))
     print(f"decode path wtype={wtype}: max rel err {worst:.3e} over {T} tokens (bound 1e-4)")
     assert worst <= 1e-4
+
+
+@pytest.mark.parametrize("env", ["MOEARC_MOE_FUSED_GD", "MOEARC_FUSED_MOE"])
+def test_opt_in_single_launch_paths_give_the_same_bits(ctx, env, monkeypatch):
+    """The opt-in launches of the decode path (gate-up and down in one PDL-chained launch; route,
+    gate-up and down in one cooperative launch) run the same pieces in the same order, so their
+    outputs equal the default kernels' bit for bit, for one token and for eight."""
+    H, I, E, k, T = 2880, 1024, 64, 4, 8
+    base, host = make_layer(ctx, H, I, E, k, 2, 1, O.MXFP4, T, 0xF05E)
+    monkeypatch.setenv(env, "1")
+    alt, _ = make_layer(ctx, H, I, E, k, 2, 1, O.MXFP4, T, 0xF05E)
+    rw = ctx.upload_new(host[3])
+    for n in (1, T):
+        x = ctx.upload_new(O.synth_normal_f32(0xF05F + n, n * H, 1.0))
+        res = ctx.upload_new(O.synth_normal_f32(0xF060 + n, n * H, 1.0))
+        a, b = ctx.alloc_n(np.float32, n * H), ctx.alloc_n(np.float32, n * H)
+        base.forward(x, n, rw, a, residual=res)
+        alt.forward(x, n, rw, b, residual=res)
+        ga, gb = ctx.download(a, np.float32, n * H), ctx.download(b, np.float32, n * H)
+        assert base.status() == 0 and alt.status() == 0
+        assert np.array_equal(ga.view(np.uint32), gb.view(np.uint32)), (env, n)
