@@ -188,6 +188,34 @@ void *moearc_x_moe_buffer(moearc_x_moe *m, int which);
 /* Reads and clears the device status word: 0, or bit 1 = a bounded wait gave up. */
 int moearc_x_moe_status(moearc_x_moe *m);
 
+/* ---- MoE prefill on tcgen05 (prefill.cu; no counterpart in the reference, whose engine
+ * decodes one token at a time through matvec kernels, crates/moearc-engine/src/moe.rs:2074-2427)
+ * The same MoE block for many tokens per call: router logits in the fixed fold order of
+ * moearc_matvec_f32 (bit-exact routing), top-k as moearc_topk_router, then the expert FFN as
+ * grouped GEMMs on the fifth-generation tensor cores (TMA operands, TMEM accumulators) with bf16
+ * activations and f32 accumulation, SwiGLU fused into the gate-up epilogue, and the combine in
+ * router order. d->max_tokens bounds n_tokens per call; scratch for that many tokens and the
+ * bf16 expansion of one block's experts is allocated at create. */
+typedef struct moearc_x_prefill moearc_x_prefill;
+moearc_x_prefill *moearc_x_prefill_create(moearc_ctx *c, const moearc_x_moe_desc *d);
+void moearc_x_prefill_destroy(moearc_x_prefill *p);
+/* Expand one block's packed banks (moearc_x_moe_pack layout, device) into the object's bf16
+ * weight matrices; later forward calls use them until the next load. */
+int moearc_x_prefill_load(moearc_x_prefill *p, const void *gateup_packed, const void *down_packed);
+/* out[t] = residual[t] (if not NULL) + MoE(x[t]) for t < n_tokens; x is bf16 [n_tokens][n_embd]
+ * (16-byte aligned), router_w f32 [E][n_embd] (16-byte aligned), router_b [E] or NULL; out f32. */
+int moearc_x_prefill_forward(moearc_x_prefill *p, const unsigned short *x, unsigned int n_tokens,
+                             const float *router_w, const float *router_b, const float *residual,
+                             float *out);
+/* Device pointers to the last call's internals: 0 expert ids [T x k] (u32), 1 gating weights
+ * [T x k], 2 logits [T x E], 3 per-expert counts [E] (int), 4 expanded gate-up weights
+ * [E][2][n_ff][n_embd] (bf16), 5 expanded down weights [E][n_embd][n_ff] (bf16), 6 activations
+ * in expert order [T k][n_embd] (bf16), 7 SwiGLU outputs [T k][n_ff] (bf16), 8 down rows
+ * [T k][n_embd] (f32), 9 row of each (token, choice) [T k] (int), 10 segment offsets [E + 1]. */
+void *moearc_x_prefill_buffer(moearc_x_prefill *p, int which);
+/* Reads and clears the device status word: 0, or bit 0 = a pipeline wait gave up. */
+int moearc_x_prefill_status(moearc_x_prefill *p);
+
 /* ---- synthetic decoder (decoder.cu) ----------------------------------------------------- */
 /* One decode step of a routed-MoE transformer (crates/moearc-engine/src/moe.rs:1862-2443,
  * Model::decode) with random, seeded weights generated on the device: per block RMSNorm,

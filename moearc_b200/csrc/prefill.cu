@@ -1,0 +1,608 @@
+// prefill.cu — the MoE FFN for prefill (many tokens per call) on the fifth-generation tensor
+// cores: route every token, group the (token, expert) pairs by expert, and run the expert FFN as
+// two grouped GEMMs on tcgen05 with operands loaded by TMA and accumulators in TMEM.
+//
+// The reference has no prefill path (its decode loop, crates/moearc-engine/src/moe.rs:2074-2427,
+// runs one token at a time through matvec kernels); this is the same MoE block, token for token:
+//   logits = router . x (+ bias)                         (the decode router's fixed fold order)
+//   top-k, gating weights                                (reference.rs:599-639, shared route.cuh)
+//   a[t,m] = act(W_gate[e] x, W_up[e] x)                 (SwiGLU / SwiGLU-OAI, reference.rs:369-396)
+//   out[t] = residual[t] + sum_m w[t,m] (W_down[e] a[t,m])   (router order, moe.rs:2395-2421)
+//
+// Kernels, in stream order (no host round trip; the GEMMs read their tile counts on the device):
+//   k_pf_logits   8 tokens per CTA, every expert; bf16 x -> f32, fixed lane order
+//   k_pf_topk     one warp per token; expert counts
+//   k_pf_scan     row offsets and 128-token tile counts per expert
+//   k_pf_scatter  each (token, choice) gets a row of its expert's segment; x copied there (bf16)
+//   k_pf_gemm<0>  gate-up: W_gate and W_up tiles of the same 128 features against 128 rows,
+//                 two TMEM accumulators, SwiGLU in the epilogue, bf16 activations out
+//   k_pf_gemm<1>  down: W_down tiles against the activations, f32 rows out
+//   k_pf_combine  per token the router-weighted sum of its k rows, plus the residual
+//
+// Precision: expert weights are MXFP4 (E2M1 x e8m0: exact in bf16) or Q4_0 ((n - 8) d: rounded
+// to bf16); activations are bf16 (the inputs as given; SwiGLU outputs rounded once); products
+// accumulate in f32 in TMEM. The bound is the reference's bf16-activation tolerance.
+//
+// Weights: moearc_x_prefill_load expands a block's packed banks (moearc_x_moe_pack layout) into
+// bf16 K-major matrices [E][2][n_ff][n_embd] (gate block, up block) and [E][n_embd][n_ff].
+#include <cuda_bf16.h>
+
+#include <algorithm>
+#include <cmath>
+#include <vector>
+
+#include "common.cuh"
+#include "route.cuh"
+#include "tc.cuh"
+
+using namespace moearc;
+
+namespace {
+
+constexpr int PF_BM = 128, PF_BN = 128, PF_BK = 64;
+constexpr int PF_TILE_BYTES = PF_BM * PF_BK * 2;  // one 128 x 64 bf16 operand tile (16 KB)
+constexpr int PF_LOGIT_TOK = 8;                   // tokens per router CTA
+constexpr int PF_STATUS_WAIT = 1;                 // a pipeline wait gave up
+
+__device__ __forceinline__ uint16_t f32_to_bf16_rn(float f) {
+    return __bfloat16_as_ushort(__float2bfloat16_rn(f));
+}
+
+// ---- routing -------------------------------------------------------------------------------
+
+struct pf_route_args {
+    const uint16_t *x;  // [T][H] bf16
+    const float *router, *rbias;
+    int T, H, E, K, gating;
+    float *logits;      // [T][E]
+    unsigned *idx;      // [T][K]
+    float *wts;         // [T][K]
+    int *cnt;           // [E], zeroed before
+};
+
+// Logits of PF_LOGIT_TOK tokens against every expert. Per (token, expert) the fold is that of
+// moearc_matvec_f32 / the decode router: lane l accumulates float4 columns l, l + 32, ... with
+// fmaf over x, y, z, w in turn, then an xor-shuffle tree.
+__global__ void __launch_bounds__(256) k_pf_logits(pf_route_args a) {
+    extern __shared__ __align__(16) float xs[];  // [PF_LOGIT_TOK][H]
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int t0 = blockIdx.x * PF_LOGIT_TOK, nt = min(PF_LOGIT_TOK, a.T - t0);
+    const int H = a.H, n4 = H / 4;
+    for (int i = threadIdx.x; i < nt * H / 2; i += blockDim.x) {
+        const uint32_t v = reinterpret_cast<const uint32_t *>(a.x + (size_t)t0 * H)[i];
+        xs[2 * i] = __uint_as_float(v << 16);
+        xs[2 * i + 1] = __uint_as_float(v & 0xFFFF0000u);
+    }
+    __syncthreads();
+    for (int e = warp; e < a.E; e += blockDim.x >> 5) {
+        const float4 *wr = reinterpret_cast<const float4 *>(a.router + (size_t)e * H);
+        float acc[PF_LOGIT_TOK];
+#pragma unroll
+        for (int t = 0; t < PF_LOGIT_TOK; ++t) acc[t] = 0.f;
+        for (int c = lane; c < n4; c += 32) {
+            const float4 wv = __ldg(wr + c);
+#pragma unroll
+            for (int t = 0; t < PF_LOGIT_TOK; ++t) {
+                const float4 xv = reinterpret_cast<const float4 *>(xs + (size_t)t * H)[c];
+                acc[t] = fmaf(wv.x, xv.x, acc[t]);
+                acc[t] = fmaf(wv.y, xv.y, acc[t]);
+                acc[t] = fmaf(wv.z, xv.z, acc[t]);
+                acc[t] = fmaf(wv.w, xv.w, acc[t]);
+            }
+        }
+#pragma unroll
+        for (int t = 0; t < PF_LOGIT_TOK; ++t) {
+            float v = acc[t];
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+            if (lane == 0 && t < nt) a.logits[(size_t)(t0 + t) * a.E + e] = a.rbias ? v + a.rbias[e] : v;
+        }
+    }
+}
+
+// Top-k of each token (one warp per token) and the per-expert counts.
+__global__ void __launch_bounds__(256) k_pf_topk(pf_route_args a) {
+    const int lane = threadIdx.x & 31;
+    const int t = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    if (t >= a.T) return;
+    xtopk(a.logits + (size_t)t * a.E, a.E, a.K, a.gating, lane, a.idx + (size_t)t * a.K, a.wts + (size_t)t * a.K);
+    __syncwarp();
+    if (lane < a.K) atomicAdd(a.cnt + __ldcg(a.idx + (size_t)t * a.K + lane), 1);
+}
+
+// Row offsets (off[e], off[E] = T K), 128-row tile offsets (toff[e], toff[E] = all tiles) and
+// zeroed cursors. One CTA; E <= 1024.
+__global__ void k_pf_scan(const int *cnt, int E, int *off, int *toff, int *cursor) {
+    __shared__ int s_c[1024], s_t[1024];
+    const int e = threadIdx.x;
+    const int c = e < E ? cnt[e] : 0;
+    s_c[e] = c;
+    s_t[e] = (c + PF_BN - 1) / PF_BN;
+    __syncthreads();
+    // inclusive scans (Hillis-Steele; E is small)
+    for (int d = 1; d < (int)blockDim.x; d <<= 1) {
+        const int vc = e >= d ? s_c[e - d] : 0, vt = e >= d ? s_t[e - d] : 0;
+        __syncthreads();
+        s_c[e] += vc;
+        s_t[e] += vt;
+        __syncthreads();
+    }
+    if (e < E) {
+        off[e + 1] = s_c[e];
+        toff[e + 1] = s_t[e];
+        cursor[e] = 0;
+    }
+    if (e == 0) {
+        off[0] = 0;
+        toff[0] = 0;
+    }
+}
+
+// One warp per (token, choice): its row in the expert's segment, and the token's bf16 activation
+// copied there. Rows within a segment are in arrival order; every row's results depend only on
+// its own activation, so the order does not reach the output.
+__global__ void __launch_bounds__(256) k_pf_scatter(const uint16_t *x, const unsigned *idx, int T, int K, int H,
+                                                    const int *off, int *cursor, int *perm, uint16_t *xp) {
+    const int lane = threadIdx.x & 31;
+    const long p = (long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    if (p >= (long)T * K) return;
+    int row = 0;
+    if (lane == 0) {
+        const int e = (int)idx[p];
+        row = off[e] + atomicAdd(cursor + e, 1);
+        perm[p] = row;
+    }
+    row = __shfl_sync(0xffffffffu, row, 0);
+    const uint4 *src = reinterpret_cast<const uint4 *>(x + (size_t)(p / K) * H);
+    uint4 *dst = reinterpret_cast<uint4 *>(xp + (size_t)row * H);
+    for (int i = lane; i < H / 8; i += 32) dst[i] = __ldg(src + i);
+}
+
+// out[t] = residual[t] + sum_m w[t,m] y[perm[t,m]] (fmaf chain, m ascending).
+__global__ void __launch_bounds__(256) k_pf_combine(const float *y, const int *perm, const float *wts, const float *residual,
+                                                    float *out, int T, int K, int H) {
+    const long i = (long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= (long)T * H) return;
+    const int t = (int)(i / H), h = (int)(i - (long)t * H);
+    float acc = 0.f;
+    for (int m = 0; m < K; ++m) acc = fmaf(wts[t * K + m], y[(size_t)perm[t * K + m] * H + h], acc);
+    out[i] = residual ? residual[i] + acc : acc;
+}
+
+// ---- weights: packed tiles -> bf16 K-major -----------------------------------------------
+
+// One warp per packed tile (16 rows x 64 columns). mats = 2: gate-up pairs (gate tile, up
+// tile) -> dst [E][2][R][Kc]; mats = 1: down tiles -> dst [E][R][Kc]. R rows, Kc columns per
+// matrix; tiles run tile-row-major per expert.
+template <int WT>
+__global__ void __launch_bounds__(256) k_pf_unpack(const uint8_t *bank, int E, int R, int Kc, int mats, int tile_bytes,
+                                                   uint16_t *dst) {
+    const int lane = threadIdx.x & 31, r = lane >> 2, q = lane & 3;
+    const long ntr = R / 16, nkt = Kc / 64;
+    const long per_e = ntr * nkt * mats;
+    const long g = (long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    if (g >= (long)E * per_e) return;
+    const int e = (int)(g / per_e);
+    const long rem = g - e * per_e;
+    const long pair = rem / mats;
+    const int mat = (int)(rem - pair * mats);
+    const int tr = (int)(pair / nkt), kt = (int)(pair - (long)tr * nkt);
+    const uint8_t *tile = bank + (size_t)g * tile_bytes;
+    const uint4 w = *reinterpret_cast<const uint4 *>(tile + lane * 16);
+    float s[4];
+    scales4<WT>(tile, r, s);
+    uint16_t *m = dst + ((size_t)e * mats + mat) * (size_t)R * Kc;
+    const uint32_t words[4] = {w.x, w.y, w.z, w.w};  // (row r, blk 0), (r+8, 0), (r, 1), (r+8, 1)
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        uint32_t pr[4];
+        decode4<WT>(words[i], pr);
+        const int row = tr * 16 + r + ((i & 1) ? 8 : 0), blk = i >> 1;
+        const float sc = s[blk * 2 + (i & 1)];
+        uint16_t *dr = m + (size_t)row * Kc + kt * 64 + blk * 32;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const __half2 h = *reinterpret_cast<const __half2 *>(&pr[j]);
+            dr[4 * q + j] = f32_to_bf16_rn(__low2float(h) * sc);
+            dr[4 * q + j + 16] = f32_to_bf16_rn(__high2float(h) * sc);
+        }
+    }
+}
+
+// ---- the grouped GEMM on tcgen05 ------------------------------------------------------------
+
+struct pf_gemm_args {
+    int Mrows;        // feature rows of one matrix per expert (gate-up: n_ff; down: n_embd)
+    int K;            // reduction length (gate-up: n_embd; down: n_ff)
+    int E;
+    const int *off;   // [E + 1] row offsets of the expert segments
+    const int *toff;  // [E + 1] 128-row tile offsets
+    int act;          // gate-up epilogue
+    float alpha, limit;
+    uint16_t *act_out;  // gate-up: [rows][n_ff] bf16
+    float *y_out;       // down: [rows][n_embd] f32
+    int *status;
+};
+
+template <int MODE>
+struct pf_cfg {
+    static constexpr int NA = MODE == 0 ? 2 : 1;  // A tiles per stage (gate and up, or down)
+    static constexpr int STAGE = (NA + 1) * PF_TILE_BYTES;
+    static constexpr int STAGES = MODE == 0 ? 4 : 6;
+    static constexpr int SMEM = STAGES * STAGE + 1024;
+    static constexpr int TMEM_COLS = 256;
+};
+
+// Persistent: CTA b takes tiles b, b + grid, ...; tile = (n-tile over all experts' segments,
+// m-tile of features), features fastest so CTAs running together share a row block in L2.
+// Warp 0: TMA producer (and TMEM owner); warp 1: MMA issuer; warps 2-5: epilogue (warp w reads
+// TMEM lanes 32 (w % 4) ..). Stages cycle across tiles; one accumulator, handed between the MMA
+// issuer and the epilogue by acc_full (tcgen05.commit) and acc_empty (4 epilogue warps).
+template <int MODE>
+__global__ void __launch_bounds__(192, 1) k_pf_gemm(const __grid_constant__ CUtensorMap wmap,
+                                                    const __grid_constant__ CUtensorMap xmap, pf_gemm_args a) {
+    using C = pf_cfg<MODE>;
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+    __shared__ __align__(8) uint64_t full[C::STAGES], empty[C::STAGES], acc_full, acc_empty, done;
+    __shared__ uint32_t tmem_slot;
+    __shared__ volatile int abort_;
+    __shared__ int s_toff[1025];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    for (int i = threadIdx.x; i <= a.E; i += blockDim.x) s_toff[i] = a.toff[i];
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < C::STAGES; ++s) {
+            tc::bar_init(&full[s], 1);
+            tc::bar_init(&empty[s], 1);
+        }
+        tc::bar_init(&acc_full, 1);
+        tc::bar_init(&acc_empty, 4);
+        tc::bar_init(&done, 1);
+        abort_ = 0;
+        tc::bar_init_fence();
+    }
+    if (warp == 0) tc::tmem_alloc(&tmem_slot, C::TMEM_COLS);
+    tc::fence_before_sync();
+    __syncthreads();
+    tc::fence_after_sync();
+    const uint32_t tmem = tmem_slot;
+    const int MT = (a.Mrows + PF_BM - 1) / PF_BM, KB = a.K / PF_BK;
+    const long total = (long)s_toff[a.E] * MT;
+    // tile -> expert, n-tile within the expert, m-tile
+    auto locate = [&](long tile, int &e, int &nt, int &mt) {
+        const int ntg = (int)(tile / MT);
+        mt = (int)(tile - (long)ntg * MT);
+        int lo = 0, hi = a.E;  // largest e with s_toff[e] <= ntg (empty experts skipped)
+        while (hi - lo > 1) {
+            const int mid = (lo + hi) >> 1;
+            if (s_toff[mid] <= ntg) lo = mid;
+            else hi = mid;
+        }
+        e = lo;
+        nt = ntg - s_toff[e];
+    };
+
+    if (warp == 0) {
+        long g = 0;  // k-blocks issued (lane 0)
+        if (lane == 0) {
+            for (long tile = blockIdx.x; tile < total && !abort_; tile += gridDim.x) {
+                int e, nt, mt;
+                locate(tile, e, nt, mt);
+                const int rowA = MODE == 0 ? e * 2 * a.Mrows + mt * PF_BM : e * a.Mrows + mt * PF_BM;
+                const int rowB = a.off[e] + nt * PF_BN;
+                for (int kb = 0; kb < KB; ++kb, ++g) {
+                    const int s = (int)(g % C::STAGES);
+                    if (g >= C::STAGES && !tc::bar_wait(&empty[s], (unsigned)(((g / C::STAGES) - 1) & 1), &abort_, a.status, PF_STATUS_WAIT))
+                        break;
+                    uint8_t *st = smem + (size_t)s * C::STAGE;
+                    tc::bar_expect_tx(&full[s], C::STAGE);
+                    tc::tma_load_2d(st, &wmap, kb * PF_BK, rowA, &full[s]);
+                    if (MODE == 0) tc::tma_load_2d(st + PF_TILE_BYTES, &wmap, kb * PF_BK, rowA + a.Mrows, &full[s]);
+                    tc::tma_load_2d(st + C::NA * PF_TILE_BYTES, &xmap, kb * PF_BK, rowB, &full[s]);
+                }
+            }
+            if (abort_)  // let every issued copy land (bounded) before the CTA exits
+                for (long j = std::max(0L, g - C::STAGES); j < g; ++j)
+                    tc::bar_drain(&full[j % C::STAGES], (unsigned)((j / C::STAGES) & 1));
+        }
+        __syncwarp();
+    } else if (warp == 1) {
+        if (lane == 0) {
+            constexpr uint32_t idesc = tc::idesc_bf16_f32(PF_BM, PF_BN);
+            long g = 0, i = 0;
+            for (long tile = blockIdx.x; tile < total && !abort_; tile += gridDim.x, ++i) {
+                if (i > 0 && !tc::bar_wait(&acc_empty, (unsigned)((i - 1) & 1), &abort_, a.status, PF_STATUS_WAIT)) break;
+                tc::fence_after_sync();
+                bool ok = true;
+                for (int kb = 0; kb < KB; ++kb, ++g) {
+                    const int s = (int)(g % C::STAGES);
+                    if (!tc::bar_wait(&full[s], (unsigned)((g / C::STAGES) & 1), &abort_, a.status, PF_STATUS_WAIT)) {
+                        ok = false;
+                        break;
+                    }
+                    tc::fence_after_sync();
+                    const uint32_t a0 = tc::sa(smem + (size_t)s * C::STAGE);
+                    const uint32_t b0 = a0 + C::NA * PF_TILE_BYTES;
+#pragma unroll
+                    for (int k = 0; k < PF_BK / 16; ++k) {
+                        const uint32_t acc = (kb > 0 || k > 0) ? 1u : 0u;
+                        tc::mma_bf16(tmem, tc::desc_k_sw128(a0 + k * 32), tc::desc_k_sw128(b0 + k * 32), idesc, acc);
+                        if (MODE == 0)
+                            tc::mma_bf16(tmem + PF_BN, tc::desc_k_sw128(a0 + PF_TILE_BYTES + k * 32),
+                                         tc::desc_k_sw128(b0 + k * 32), idesc, acc);
+                    }
+                    tc::mma_commit(&empty[s]);  // the stage is free once these MMAs have read it
+                }
+                if (!ok) break;
+                tc::mma_commit(&acc_full);
+            }
+            // every MMA issued has completed before the columns can be freed
+            tc::mma_commit(&done);
+            tc::bar_drain(&done, 0);
+        }
+        __syncwarp();
+    } else {
+        const int qd = warp & 3;  // TMEM lane quarter
+        const uint32_t lane_base = tmem + ((uint32_t)(32 * qd) << 16);
+        long i = 0;
+        for (long tile = blockIdx.x; tile < total; tile += gridDim.x, ++i) {
+            if (!tc::bar_wait(&acc_full, (unsigned)(i & 1), &abort_, a.status, PF_STATUS_WAIT)) break;
+            tc::fence_after_sync();
+            int e, nt, mt;
+            locate(tile, e, nt, mt);
+            const int seg = a.off[e], n_rows = a.off[e + 1] - seg;
+            const int f = mt * PF_BM + 32 * qd + lane;  // this thread's feature row
+            const bool fok = f < a.Mrows;
+            for (int c0 = 0; c0 < PF_BN; c0 += 16) {
+                float d[16];
+                tc::tmem_ld16(lane_base + c0, d);
+                if (MODE == 0) {
+                    float u[16];
+                    tc::tmem_ld16(lane_base + PF_BN + c0, u);
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) {
+                        const int n = nt * PF_BN + c0 + j;
+                        if (fok && n < n_rows)
+                            a.act_out[(size_t)(seg + n) * a.Mrows + f] = f32_to_bf16_rn(act_fn(a.act, d[j], u[j], a.alpha, a.limit));
+                    }
+                } else {
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) {
+                        const int n = nt * PF_BN + c0 + j;
+                        if (fok && n < n_rows) a.y_out[(size_t)(seg + n) * a.Mrows + f] = d[j];
+                    }
+                }
+            }
+            tc::fence_before_sync();
+            __syncwarp();
+            if (lane == 0) tc::bar_arrive(&acc_empty);
+        }
+    }
+    tc::fence_before_sync();
+    __syncthreads();
+    if (warp == 0) {
+        tc::fence_after_sync();
+        tc::tmem_dealloc(tmem, C::TMEM_COLS);
+    }
+}
+
+// ---- host ---------------------------------------------------------------------------------
+
+typedef CUresult (*encode_tiled_fn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
+                                    const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
+                                    CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+encode_tiled_fn encoder() {
+    static encode_tiled_fn fn = nullptr;
+    if (!fn) {
+        cudaDriverEntryPointQueryResult q;
+        void *p = nullptr;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<encode_tiled_fn>(p);
+        cudaGetLastError();
+    }
+    return fn;
+}
+
+// A bf16 row-major [rows][cols] matrix read as 128-row x 64-column boxes, 128-byte swizzle
+// (the UMMA K-major canonical layout); rows past the end read as zeros.
+bool make_map(CUtensorMap *map, const void *base, long rows, int cols) {
+    encode_tiled_fn enc = encoder();
+    if (!enc) return false;
+    const cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+    const cuuint64_t strides[1] = {(cuuint64_t)cols * 2};
+    const cuuint32_t box[2] = {PF_BK, PF_BM};
+    const cuuint32_t es[2] = {1, 1};
+    return enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void *>(base), dims, strides, box, es,
+               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+}  // namespace
+
+struct moearc_x_prefill {
+    moearc_ctx *c;
+    int H, I, E, K, wtype, gating, act;
+    float alpha, limit;
+    int T_max, tile_bytes;
+    void *mem = nullptr;
+    float *logits, *y, *wts;
+    unsigned *idx;
+    int *cnt, *off, *toff, *cursor, *perm, *status;
+    uint16_t *xp, *actb, *wgu, *wdn;
+    CUtensorMap map_wgu, map_xp, map_wdn, map_act;
+};
+
+extern "C" {
+
+moearc_x_prefill *moearc_x_prefill_create(moearc_ctx *c, const moearc_x_moe_desc *d) {
+    if (!c || !d) return nullptr;
+    if (d->wtype != T_MXFP4 && d->wtype != T_Q4_0) return nullptr;
+    if (d->n_embd % 64 || d->n_ff % 64 || d->n_expert == 0 || d->n_expert > 1024 || d->k == 0 || d->k > 32 ||
+        d->k > d->n_expert || d->max_tokens == 0)
+        return nullptr;
+    auto *p = new moearc_x_prefill();
+    p->c = c;
+    p->H = (int)d->n_embd;
+    p->I = (int)d->n_ff;
+    p->E = (int)d->n_expert;
+    p->K = (int)d->k;
+    p->wtype = (int)d->wtype;
+    p->gating = (int)d->gating;
+    p->act = (int)d->act;
+    p->alpha = d->alpha;
+    p->limit = d->limit;
+    p->T_max = (int)d->max_tokens;
+    p->tile_bytes = d->wtype == T_MXFP4 ? 544 : 576;
+    const size_t rows = (size_t)p->T_max * p->K;
+    size_t off = 0;
+    auto take = [&](size_t bytes) {
+        const size_t o = off;
+        off += (bytes + 1023) & ~(size_t)1023;
+        return o;
+    };
+    const size_t o_lg = take(sizeof(float) * p->T_max * p->E), o_y = take(sizeof(float) * rows * p->H);
+    const size_t o_w = take(sizeof(float) * rows), o_i = take(sizeof(unsigned) * rows);
+    const size_t o_cnt = take(sizeof(int) * (p->E + 1)), o_off = take(sizeof(int) * (p->E + 1));
+    const size_t o_toff = take(sizeof(int) * (p->E + 1)), o_cur = take(sizeof(int) * (p->E + 1));
+    const size_t o_perm = take(sizeof(int) * rows), o_st = take(sizeof(int));
+    const size_t o_xp = take(2 * rows * p->H), o_act = take(2 * rows * p->I);
+    const size_t o_wgu = take(2 * (size_t)p->E * 2 * p->I * p->H), o_wdn = take(2 * (size_t)p->E * p->H * p->I);
+    if (cudaMalloc(&p->mem, off) != cudaSuccess) {
+        cudaGetLastError();
+        delete p;
+        return nullptr;
+    }
+    uint8_t *b = static_cast<uint8_t *>(p->mem);
+    p->logits = reinterpret_cast<float *>(b + o_lg);
+    p->y = reinterpret_cast<float *>(b + o_y);
+    p->wts = reinterpret_cast<float *>(b + o_w);
+    p->idx = reinterpret_cast<unsigned *>(b + o_i);
+    p->cnt = reinterpret_cast<int *>(b + o_cnt);
+    p->off = reinterpret_cast<int *>(b + o_off);
+    p->toff = reinterpret_cast<int *>(b + o_toff);
+    p->cursor = reinterpret_cast<int *>(b + o_cur);
+    p->perm = reinterpret_cast<int *>(b + o_perm);
+    p->status = reinterpret_cast<int *>(b + o_st);
+    p->xp = reinterpret_cast<uint16_t *>(b + o_xp);
+    p->actb = reinterpret_cast<uint16_t *>(b + o_act);
+    p->wgu = reinterpret_cast<uint16_t *>(b + o_wgu);
+    p->wdn = reinterpret_cast<uint16_t *>(b + o_wdn);
+    const bool ok = make_map(&p->map_wgu, p->wgu, (long)p->E * 2 * p->I, p->H) &&
+                    make_map(&p->map_xp, p->xp, (long)rows, p->H) &&
+                    make_map(&p->map_wdn, p->wdn, (long)p->E * p->H, p->I) &&
+                    make_map(&p->map_act, p->actb, (long)rows, p->I) &&
+                    set_smem(k_pf_gemm<0>, pf_cfg<0>::SMEM) == cudaSuccess &&
+                    set_smem(k_pf_gemm<1>, pf_cfg<1>::SMEM) == cudaSuccess &&
+                    set_smem(k_pf_logits, PF_LOGIT_TOK * p->H * 4) == cudaSuccess &&
+                    cudaMemsetAsync(p->mem, 0, off, c->stream) == cudaSuccess &&
+                    cudaStreamSynchronize(c->stream) == cudaSuccess;
+    if (!ok) {
+        cudaGetLastError();
+        cudaFree(p->mem);
+        delete p;
+        return nullptr;
+    }
+    return p;
+}
+
+void moearc_x_prefill_destroy(moearc_x_prefill *p) {
+    if (!p) return;
+    cudaStreamSynchronize(p->c->stream);
+    cudaFree(p->mem);
+    delete p;
+}
+
+int moearc_x_prefill_load(moearc_x_prefill *p, const void *gateup_packed, const void *down_packed) {
+    if (!p || !gateup_packed || !down_packed) return ERR;
+    moearc_ctx *c = p->c;
+    const long gu_tiles = (long)p->E * (p->I / 16) * (p->H / 64) * 2, dn_tiles = (long)p->E * (p->H / 16) * (p->I / 64);
+    const bool mx = p->wtype == T_MXFP4;
+    auto grid = [](long warps) { return dim3((unsigned)((warps + 7) / 8)); };
+    if (mx) {
+        k_pf_unpack<39><<<grid(gu_tiles), 256, 0, c->stream>>>(static_cast<const uint8_t *>(gateup_packed), p->E, p->I,
+                                                               p->H, 2, p->tile_bytes, p->wgu);
+        k_pf_unpack<39><<<grid(dn_tiles), 256, 0, c->stream>>>(static_cast<const uint8_t *>(down_packed), p->E, p->H,
+                                                               p->I, 1, p->tile_bytes, p->wdn);
+    } else {
+        k_pf_unpack<2><<<grid(gu_tiles), 256, 0, c->stream>>>(static_cast<const uint8_t *>(gateup_packed), p->E, p->I,
+                                                              p->H, 2, p->tile_bytes, p->wgu);
+        k_pf_unpack<2><<<grid(dn_tiles), 256, 0, c->stream>>>(static_cast<const uint8_t *>(down_packed), p->E, p->H,
+                                                              p->I, 1, p->tile_bytes, p->wdn);
+    }
+    return cudaGetLastError() == cudaSuccess ? OK : ERR;
+}
+
+int moearc_x_prefill_forward(moearc_x_prefill *p, const uint16_t *x, unsigned n_tokens, const float *router_w,
+                             const float *router_b, const float *residual, float *out) {
+    if (!p || !x || !router_w || !out) return ERR;
+    if (n_tokens == 0) return OK;
+    if ((int)n_tokens > p->T_max) return ERR_ARG;
+    if ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(router_w)) & 15) return ERR_ARG;
+    moearc_ctx *c = p->c;
+    cudaStream_t st = c->stream;
+    const int T = (int)n_tokens;
+    launch_scope ls(c, "moe_prefill", (unsigned long)p->H, (unsigned)T);
+    if (cudaMemsetAsync(p->cnt, 0, sizeof(int) * (p->E + 1), st) != cudaSuccess) return ERR;
+    pf_route_args ra{x, router_w, router_b, T, p->H, p->E, p->K, p->gating, p->logits, p->idx, p->wts, p->cnt};
+    k_pf_logits<<<(T + PF_LOGIT_TOK - 1) / PF_LOGIT_TOK, 256, PF_LOGIT_TOK * p->H * 4, st>>>(ra);
+    k_pf_topk<<<(T + 7) / 8, 256, 0, st>>>(ra);
+    k_pf_scan<<<1, 1024, 0, st>>>(p->cnt, p->E, p->off, p->toff, p->cursor);
+    const long pairs = (long)T * p->K;
+    k_pf_scatter<<<(unsigned)((pairs + 7) / 8), 256, 0, st>>>(x, p->idx, T, p->K, p->H, p->off, p->cursor, p->perm, p->xp);
+    pf_gemm_args g{};
+    g.E = p->E;
+    g.off = p->off;
+    g.toff = p->toff;
+    g.act = p->act;
+    g.alpha = p->alpha;
+    g.limit = p->limit;
+    g.act_out = p->actb;
+    g.y_out = p->y;
+    g.status = p->status;
+    g.Mrows = p->I;
+    g.K = p->H;
+    k_pf_gemm<0><<<c->sm_count, 192, pf_cfg<0>::SMEM, st>>>(p->map_wgu, p->map_xp, g);
+    g.Mrows = p->H;
+    g.K = p->I;
+    k_pf_gemm<1><<<c->sm_count, 192, pf_cfg<1>::SMEM, st>>>(p->map_wdn, p->map_act, g);
+    const long n = (long)T * p->H;
+    k_pf_combine<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(p->y, p->perm, p->wts, residual, out, T, p->K, p->H);
+    return ls.finish();
+}
+
+// 0 expert ids [T x k] (u32), 1 gating weights [T x k], 2 logits [T x E], 3 per-expert counts
+// [E] (int), 4 expanded gate-up weights [E][2][n_ff][n_embd] (bf16), 5 expanded down weights,
+// 6 the activations in expert order [T k][n_embd] (bf16), 7 the SwiGLU outputs [T k][n_ff]
+// (bf16), 8 the down rows [T k][n_embd] (f32), 9 the row of each (token, choice) [T k] (int),
+// 10 the expert segment offsets [E + 1] (int).
+void *moearc_x_prefill_buffer(moearc_x_prefill *p, int which) {
+    if (!p) return nullptr;
+    switch (which) {
+    case 0: return p->idx;
+    case 1: return p->wts;
+    case 2: return p->logits;
+    case 3: return p->cnt;
+    case 4: return p->wgu;
+    case 5: return p->wdn;
+    case 6: return p->xp;
+    case 7: return p->actb;
+    case 8: return p->y;
+    case 9: return p->perm;
+    case 10: return p->off;
+    default: return nullptr;
+    }
+}
+
+int moearc_x_prefill_status(moearc_x_prefill *p) {
+    if (!p) return ERR;
+    int s = 0;
+    if (cudaMemcpyAsync(&s, p->status, sizeof(int), cudaMemcpyDeviceToHost, p->c->stream) != cudaSuccess ||
+        cudaMemsetAsync(p->status, 0, sizeof(int), p->c->stream) != cudaSuccess ||
+        cudaStreamSynchronize(p->c->stream) != cudaSuccess)
+        return ERR;
+    return s;
+}
+
+}  // extern "C"

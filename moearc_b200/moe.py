@@ -64,3 +64,49 @@ class MoeLayer:
         out = np.empty(n, dtype)
         self.ctx._finish(self.ctx.lib.moearc_copy_d2h(self.ctx.raw, out.ctypes.data, p, out.nbytes), "download")
         return out
+
+
+class MoePrefill:
+    """The MoE block for many tokens per call on the tcgen05 tensor cores
+    (``moearc_x_prefill_*``): bf16 activations in, f32 out, routing bit-exact with the decode
+    path's router."""
+
+    def __init__(self, ctx: Context, n_embd: int, n_ff: int, n_expert: int, k: int, gating: int,
+                 act: int, wtype: int, max_tokens: int, alpha: float = 1.702, limit: float = 7.0):
+        self.ctx = ctx
+        self.desc = _lib.MoeDesc(n_embd, n_ff, n_expert, k, gating, act, alpha, limit, wtype, max_tokens)
+        self.h = ctx.lib.moearc_x_prefill_create(ctx.raw, C.byref(self.desc))
+        if not self.h:
+            raise BadArgument("moearc_x_prefill_create refused the shape")
+
+    def close(self) -> None:
+        if self.h:
+            self.ctx.lib.moearc_x_prefill_destroy(self.h)
+            self.h = None
+
+    def load(self, gateup: DeviceBuffer, down: DeviceBuffer) -> None:
+        """Expand packed banks (MoeLayer.pack's output) into the bf16 weights the GEMMs read."""
+        self.ctx._finish(self.ctx.lib.moearc_x_prefill_load(self.h, gateup.ptr, down.ptr), "prefill_load")
+
+    def forward(self, x_bf16: DeviceBuffer, n_tokens: int, router_w: DeviceBuffer, out: DeviceBuffer,
+                router_b: DeviceBuffer | None = None, residual: DeviceBuffer | None = None) -> None:
+        H = self.desc.n_embd
+        x_bf16.require("prefill input", 2 * n_tokens * H)
+        out.require("prefill output", 4 * n_tokens * H)
+        router_w.require("router weights", 4 * self.desc.n_expert * H)
+        rc = self.ctx.lib.moearc_x_prefill_forward(self.h, x_bf16.ptr, n_tokens, router_w.ptr,
+                                                   None if router_b is None else router_b.ptr,
+                                                   None if residual is None else residual.ptr, out.ptr)
+        self.ctx._finish(rc, "prefill_forward")
+
+    def status(self) -> int:
+        st = self.ctx.lib.moearc_x_prefill_status(self.h)
+        if st < 0:
+            raise Failed("reading the prefill status word")
+        return st
+
+    def buffer(self, which: int, dtype, n: int) -> np.ndarray:
+        p = self.ctx.lib.moearc_x_prefill_buffer(self.h, which)
+        out = np.empty(n, dtype)
+        self.ctx._finish(self.ctx.lib.moearc_copy_d2h(self.ctx.raw, out.ctypes.data, p, out.nbytes), "download")
+        return out
