@@ -215,6 +215,12 @@ int moearc_x_prefill_forward(moearc_x_prefill *p, const unsigned short *x, unsig
 void *moearc_x_prefill_buffer(moearc_x_prefill *p, int which);
 /* Reads and clears the device status word: 0, or bit 0 = a pipeline wait gave up. */
 int moearc_x_prefill_status(moearc_x_prefill *p);
+/* moearc_x_prefill_forward with an event between its kernels, waited for: ms[i] = device time of
+ * kernel i (0 router logits, 1 top-k, 2 scan, 3 scatter, 4 gate-up GEMM, 5 down GEMM, 6 combine);
+ * n >= 7. */
+int moearc_x_prefill_profile(moearc_x_prefill *p, const unsigned short *x, unsigned int n_tokens,
+                             const float *router_w, const float *router_b, const float *residual,
+                             float *out, float *ms, int n);
 
 /* ---- synthetic decoder (decoder.cu) ----------------------------------------------------- */
 /* One decode step of a routed-MoE transformer (crates/moearc-engine/src/moe.rs:1862-2443,

@@ -79,6 +79,7 @@ SIGNATURES: dict[str, tuple] = {
     "moearc_x_prefill_forward": (I, [P, P, U, P, P, P, P]),
     "moearc_x_prefill_buffer": (P, [P, I]),
     "moearc_x_prefill_status": (I, [P]),
+    "moearc_x_prefill_profile": (I, [P, P, U, P, P, P, P, P, I]),
     "moearc_x_decoder_create": (P, [P, P]),
     "moearc_x_decoder_destroy": (None, [P]),
     "moearc_x_decoder_input": (P, [P]),

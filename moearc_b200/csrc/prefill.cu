@@ -173,11 +173,14 @@ __global__ void __launch_bounds__(256) k_pf_combine(const float *y, const int *p
 
 // One warp per packed tile (16 rows x 64 columns). mats = 2: gate-up pairs (gate tile, up
 // tile) -> dst [E][2][R][Kc]; mats = 1: down tiles -> dst [E][R][Kc]. R rows, Kc columns per
-// matrix; tiles run tile-row-major per expert.
+// matrix; tiles run tile-row-major per expert. The warp decodes its tile into shared memory and
+// writes it out as 16 rows of 128 contiguous bytes (16-byte stores).
 template <int WT>
 __global__ void __launch_bounds__(256) k_pf_unpack(const uint8_t *bank, int E, int R, int Kc, int mats, int tile_bytes,
                                                    uint16_t *dst) {
+    __shared__ __align__(16) uint16_t stage[8][16 * 64];
     const int lane = threadIdx.x & 31, r = lane >> 2, q = lane & 3;
+    uint16_t *tl = stage[threadIdx.x >> 5];
     const long ntr = R / 16, nkt = Kc / 64;
     const long per_e = ntr * nkt * mats;
     const long g = (long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
@@ -197,15 +200,23 @@ __global__ void __launch_bounds__(256) k_pf_unpack(const uint8_t *bank, int E, i
     for (int i = 0; i < 4; ++i) {
         uint32_t pr[4];
         decode4<WT>(words[i], pr);
-        const int row = tr * 16 + r + ((i & 1) ? 8 : 0), blk = i >> 1;
+        const int lrow = r + ((i & 1) ? 8 : 0), blk = i >> 1;
         const float sc = s[blk * 2 + (i & 1)];
-        uint16_t *dr = m + (size_t)row * Kc + kt * 64 + blk * 32;
+        uint16_t *dr = tl + lrow * 64 + blk * 32;
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
             const __half2 h = *reinterpret_cast<const __half2 *>(&pr[j]);
             dr[4 * q + j] = f32_to_bf16_rn(__low2float(h) * sc);
             dr[4 * q + j + 16] = f32_to_bf16_rn(__high2float(h) * sc);
         }
+    }
+    __syncwarp();
+    // 16 rows x 8 chunks of 16 bytes: lane takes chunks lane, lane + 32, ...
+#pragma unroll
+    for (int c = lane; c < 128; c += 32) {
+        const int row = c >> 3, ch = c & 7;
+        *reinterpret_cast<uint4 *>(m + (size_t)(tr * 16 + row) * Kc + kt * 64 + ch * 8) =
+            *reinterpret_cast<const uint4 *>(tl + row * 64 + ch * 8);
     }
 }
 
@@ -230,21 +241,24 @@ struct pf_cfg {
     static constexpr int STAGE = (NA + 1) * PF_TILE_BYTES;
     static constexpr int STAGES = MODE == 0 ? 4 : 6;
     static constexpr int SMEM = STAGES * STAGE + 1024;
-    static constexpr int TMEM_COLS = 256;
+    static constexpr int ACC_COLS = NA * PF_BN;      // one accumulator set (gate + up, or down)
+    static constexpr int TMEM_COLS = 2 * ACC_COLS;   // two sets: the epilogue of tile i overlaps
+                                                     // the MMAs of tile i + 1
 };
 
 // Persistent: CTA b takes tiles b, b + grid, ...; tile = (n-tile over all experts' segments,
 // m-tile of features), features fastest so CTAs running together share a row block in L2.
 // Warp 0: TMA producer (and TMEM owner); warp 1: MMA issuer; warps 2-5: epilogue (warp w reads
-// TMEM lanes 32 (w % 4) ..). Stages cycle across tiles; one accumulator, handed between the MMA
-// issuer and the epilogue by acc_full (tcgen05.commit) and acc_empty (4 epilogue warps).
+// TMEM lanes 32 (w % 4) ..). Stages cycle across tiles; two accumulator sets (tile i uses set
+// i % 2), each handed between the MMA issuer and the epilogue by acc_full (tcgen05.commit) and
+// acc_empty (4 epilogue warps).
 template <int MODE>
 __global__ void __launch_bounds__(192, 1) k_pf_gemm(const __grid_constant__ CUtensorMap wmap,
                                                     const __grid_constant__ CUtensorMap xmap, pf_gemm_args a) {
     using C = pf_cfg<MODE>;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
-    __shared__ __align__(8) uint64_t full[C::STAGES], empty[C::STAGES], acc_full, acc_empty, done;
+    __shared__ __align__(8) uint64_t full[C::STAGES], empty[C::STAGES], acc_full[2], acc_empty[2], done;
     __shared__ uint32_t tmem_slot;
     __shared__ volatile int abort_;
     __shared__ int s_toff[1025];
@@ -255,8 +269,10 @@ __global__ void __launch_bounds__(192, 1) k_pf_gemm(const __grid_constant__ CUte
             tc::bar_init(&full[s], 1);
             tc::bar_init(&empty[s], 1);
         }
-        tc::bar_init(&acc_full, 1);
-        tc::bar_init(&acc_empty, 4);
+        for (int b = 0; b < 2; ++b) {
+            tc::bar_init(&acc_full[b], 1);
+            tc::bar_init(&acc_empty[b], 4);
+        }
         tc::bar_init(&done, 1);
         abort_ = 0;
         tc::bar_init_fence();
@@ -311,7 +327,10 @@ __global__ void __launch_bounds__(192, 1) k_pf_gemm(const __grid_constant__ CUte
             constexpr uint32_t idesc = tc::idesc_bf16_f32(PF_BM, PF_BN);
             long g = 0, i = 0;
             for (long tile = blockIdx.x; tile < total && !abort_; tile += gridDim.x, ++i) {
-                if (i > 0 && !tc::bar_wait(&acc_empty, (unsigned)((i - 1) & 1), &abort_, a.status, PF_STATUS_WAIT)) break;
+                const int ab = (int)(i & 1);
+                const uint32_t dcol = tmem + (uint32_t)(ab * C::ACC_COLS);
+                if (i >= 2 && !tc::bar_wait(&acc_empty[ab], (unsigned)(((i >> 1) - 1) & 1), &abort_, a.status, PF_STATUS_WAIT))
+                    break;
                 tc::fence_after_sync();
                 bool ok = true;
                 for (int kb = 0; kb < KB; ++kb, ++g) {
@@ -326,15 +345,15 @@ __global__ void __launch_bounds__(192, 1) k_pf_gemm(const __grid_constant__ CUte
 #pragma unroll
                     for (int k = 0; k < PF_BK / 16; ++k) {
                         const uint32_t acc = (kb > 0 || k > 0) ? 1u : 0u;
-                        tc::mma_bf16(tmem, tc::desc_k_sw128(a0 + k * 32), tc::desc_k_sw128(b0 + k * 32), idesc, acc);
+                        tc::mma_bf16(dcol, tc::desc_k_sw128(a0 + k * 32), tc::desc_k_sw128(b0 + k * 32), idesc, acc);
                         if (MODE == 0)
-                            tc::mma_bf16(tmem + PF_BN, tc::desc_k_sw128(a0 + PF_TILE_BYTES + k * 32),
+                            tc::mma_bf16(dcol + PF_BN, tc::desc_k_sw128(a0 + PF_TILE_BYTES + k * 32),
                                          tc::desc_k_sw128(b0 + k * 32), idesc, acc);
                     }
                     tc::mma_commit(&empty[s]);  // the stage is free once these MMAs have read it
                 }
                 if (!ok) break;
-                tc::mma_commit(&acc_full);
+                tc::mma_commit(&acc_full[ab]);
             }
             // every MMA issued has completed before the columns can be freed
             tc::mma_commit(&done);
@@ -346,19 +365,21 @@ __global__ void __launch_bounds__(192, 1) k_pf_gemm(const __grid_constant__ CUte
         const uint32_t lane_base = tmem + ((uint32_t)(32 * qd) << 16);
         long i = 0;
         for (long tile = blockIdx.x; tile < total; tile += gridDim.x, ++i) {
-            if (!tc::bar_wait(&acc_full, (unsigned)(i & 1), &abort_, a.status, PF_STATUS_WAIT)) break;
+            const int ab = (int)(i & 1);
+            if (!tc::bar_wait(&acc_full[ab], (unsigned)((i >> 1) & 1), &abort_, a.status, PF_STATUS_WAIT)) break;
             tc::fence_after_sync();
             int e, nt, mt;
             locate(tile, e, nt, mt);
             const int seg = a.off[e], n_rows = a.off[e + 1] - seg;
             const int f = mt * PF_BM + 32 * qd + lane;  // this thread's feature row
             const bool fok = f < a.Mrows;
+            const uint32_t acc_base = lane_base + (uint32_t)(ab * C::ACC_COLS);
             for (int c0 = 0; c0 < PF_BN; c0 += 16) {
                 float d[16];
-                tc::tmem_ld16(lane_base + c0, d);
+                tc::tmem_ld16(acc_base + c0, d);
                 if (MODE == 0) {
                     float u[16];
-                    tc::tmem_ld16(lane_base + PF_BN + c0, u);
+                    tc::tmem_ld16(acc_base + PF_BN + c0, u);
 #pragma unroll
                     for (int j = 0; j < 16; ++j) {
                         const int n = nt * PF_BN + c0 + j;
@@ -375,7 +396,7 @@ __global__ void __launch_bounds__(192, 1) k_pf_gemm(const __grid_constant__ CUte
             }
             tc::fence_before_sync();
             __syncwarp();
-            if (lane == 0) tc::bar_arrive(&acc_empty);
+            if (lane == 0) tc::bar_arrive(&acc_empty[ab]);
         }
     }
     tc::fence_before_sync();
@@ -534,8 +555,14 @@ int moearc_x_prefill_load(moearc_x_prefill *p, const void *gateup_packed, const 
     return cudaGetLastError() == cudaSuccess ? OK : ERR;
 }
 
-int moearc_x_prefill_forward(moearc_x_prefill *p, const uint16_t *x, unsigned n_tokens, const float *router_w,
-                             const float *router_b, const float *residual, float *out) {
+}  // extern "C"
+
+namespace {
+
+// The forward sequence; with `ev`, an event is recorded before the first kernel and after each
+// of the 7 kernels (routing, top-k, scan, scatter, gate-up GEMM, down GEMM, combine).
+int prefill_forward(moearc_x_prefill *p, const uint16_t *x, unsigned n_tokens, const float *router_w,
+                    const float *router_b, const float *residual, float *out, cudaEvent_t *ev) {
     if (!p || !x || !router_w || !out) return ERR;
     if (n_tokens == 0) return OK;
     if ((int)n_tokens > p->T_max) return ERR_ARG;
@@ -544,13 +571,21 @@ int moearc_x_prefill_forward(moearc_x_prefill *p, const uint16_t *x, unsigned n_
     cudaStream_t st = c->stream;
     const int T = (int)n_tokens;
     launch_scope ls(c, "moe_prefill", (unsigned long)p->H, (unsigned)T);
+    auto mark = [&](int i) {
+        if (ev) cudaEventRecord(ev[i], st);
+    };
     if (cudaMemsetAsync(p->cnt, 0, sizeof(int) * (p->E + 1), st) != cudaSuccess) return ERR;
+    mark(0);
     pf_route_args ra{x, router_w, router_b, T, p->H, p->E, p->K, p->gating, p->logits, p->idx, p->wts, p->cnt};
     k_pf_logits<<<(T + PF_LOGIT_TOK - 1) / PF_LOGIT_TOK, 256, PF_LOGIT_TOK * p->H * 4, st>>>(ra);
+    mark(1);
     k_pf_topk<<<(T + 7) / 8, 256, 0, st>>>(ra);
+    mark(2);
     k_pf_scan<<<1, 1024, 0, st>>>(p->cnt, p->E, p->off, p->toff, p->cursor);
+    mark(3);
     const long pairs = (long)T * p->K;
     k_pf_scatter<<<(unsigned)((pairs + 7) / 8), 256, 0, st>>>(x, p->idx, T, p->K, p->H, p->off, p->cursor, p->perm, p->xp);
+    mark(4);
     pf_gemm_args g{};
     g.E = p->E;
     g.off = p->off;
@@ -564,12 +599,41 @@ int moearc_x_prefill_forward(moearc_x_prefill *p, const uint16_t *x, unsigned n_
     g.Mrows = p->I;
     g.K = p->H;
     k_pf_gemm<0><<<c->sm_count, 192, pf_cfg<0>::SMEM, st>>>(p->map_wgu, p->map_xp, g);
+    mark(5);
     g.Mrows = p->H;
     g.K = p->I;
     k_pf_gemm<1><<<c->sm_count, 192, pf_cfg<1>::SMEM, st>>>(p->map_wdn, p->map_act, g);
+    mark(6);
     const long n = (long)T * p->H;
     k_pf_combine<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(p->y, p->perm, p->wts, residual, out, T, p->K, p->H);
+    mark(7);
     return ls.finish();
+}
+
+}  // namespace
+
+extern "C" {
+
+int moearc_x_prefill_forward(moearc_x_prefill *p, const uint16_t *x, unsigned n_tokens, const float *router_w,
+                             const float *router_b, const float *residual, float *out) {
+    return prefill_forward(p, x, n_tokens, router_w, router_b, residual, out, nullptr);
+}
+
+// One forward with an event between kernels; ms[i] = device time of kernel i (0 routing logits,
+// 1 top-k, 2 scan, 3 scatter, 4 gate-up GEMM, 5 down GEMM, 6 combine); n >= 7. Waits for it.
+int moearc_x_prefill_profile(moearc_x_prefill *p, const uint16_t *x, unsigned n_tokens, const float *router_w,
+                             const float *router_b, const float *residual, float *out, float *ms, int n) {
+    if (!p || !ms || n < 7) return ERR;
+    cudaEvent_t ev[8];
+    for (auto &e : ev) cudaEventCreate(&e);
+    int rc = prefill_forward(p, x, n_tokens, router_w, router_b, residual, out, ev);
+    if (cudaStreamSynchronize(p->c->stream) != cudaSuccess) rc = ERR;
+    for (int i = 0; i < 7; ++i) {
+        ms[i] = 0.f;
+        if (rc == OK) cudaEventElapsedTime(&ms[i], ev[i], ev[i + 1]);
+    }
+    for (auto &e : ev) cudaEventDestroy(e);
+    return rc;
 }
 
 // 0 expert ids [T x k] (u32), 1 gating weights [T x k], 2 logits [T x E], 3 per-expert counts
