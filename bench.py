@@ -286,7 +286,7 @@ def prefill_bench(args) -> dict:
     ctx = Context()
     lib = ctx.lib
     H = I = 2880
-    E, k, T = 128, 4, 8 * 4096
+    E, k, T = args.experts, 4, args.tokens
     nb = E * I * H // 32
     banks = [ctx.alloc(nb * 17) for _ in range(3)]
     for i, b in enumerate(banks):
@@ -364,7 +364,7 @@ def prefill_main(args) -> None:
         "ms_per_step": r["ms_step"], "tokens_per_s": T / (r["ms_step"] / 1000.0), "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "bf16 operands, f32 accumulate (MXFP4 weights expanded to bf16)",
         "data": "synthetic (seeded MXFP4 experts, bf16 N(0,1) activations, Zipf(1.1) router bias)",
-        "config": {"workload": "configs[3] MoE block: 8 sequences x 4096 tokens, 128 experts top-4, 2880 x 2880",
+        "config": {"workload": f"configs[3] MoE block: {T} tokens (8 x 4096 at full size), {r['E']} experts top-4, 2880 x 2880",
                    "tokens": T, "expert_load_max": int(cnt.max()), "expert_load_mean": float(cnt.mean()),
                    "l2": "operands (1.5 GB activations, 6.4 GB bf16 weights) far exceed the 126 MB L2"},
         "roofline": {"bound": "tensor", "kernel": "gate-up grouped GEMM (tcgen05 kind::f16, SwiGLU epilogue)",
@@ -389,6 +389,8 @@ def main() -> None:
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--layers", type=int, default=0,
                     help="blocks to build (default: the configuration's); a smaller model for profiling")
+    ap.add_argument("--tokens", type=int, default=8 * 4096, help="prefill: tokens per step (configs[3]: 8 x 4096)")
+    ap.add_argument("--experts", type=int, default=128, help="prefill: experts (configs[3]: 128)")
     ap.add_argument("--offload", type=int, default=0,
                     help="blocks whose experts stay in pinned host memory (configs[2] mode (b): 30)")
     args = ap.parse_args()

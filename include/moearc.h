@@ -195,7 +195,8 @@ int moearc_x_moe_status(moearc_x_moe *m);
  * grouped GEMMs on the fifth-generation tensor cores (TMA operands, TMEM accumulators) with bf16
  * activations and f32 accumulation, SwiGLU fused into the gate-up epilogue, and the combine in
  * router order. d->max_tokens bounds n_tokens per call; scratch for that many tokens and the
- * bf16 expansion of one block's experts is allocated at create. */
+ * bf16 expansion of one block's experts is allocated at create. NULL for n_embd > 3584 or
+ * shapes the decode path also refuses. */
 typedef struct moearc_x_prefill moearc_x_prefill;
 moearc_x_prefill *moearc_x_prefill_create(moearc_ctx *c, const moearc_x_moe_desc *d);
 void moearc_x_prefill_destroy(moearc_x_prefill *p);

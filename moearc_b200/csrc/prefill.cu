@@ -41,7 +41,8 @@ namespace {
 
 constexpr int PF_BM = 128, PF_BN = 128, PF_BK = 64;
 constexpr int PF_TILE_BYTES = PF_BM * PF_BK * 2;  // one 128 x 64 bf16 operand tile (16 KB)
-constexpr int PF_LOGIT_TOK = 8;                   // tokens per router CTA
+constexpr int PF_LOGIT_TOK = 16;                  // tokens per router CTA
+constexpr int PF_LOGIT_EXP = 4;                   // experts a warp folds at once
 constexpr int PF_STATUS_WAIT = 1;                 // a pipeline wait gave up
 
 __device__ __forceinline__ uint16_t f32_to_bf16_rn(float f) {
@@ -62,7 +63,9 @@ struct pf_route_args {
 
 // Logits of PF_LOGIT_TOK tokens against every expert. Per (token, expert) the fold is that of
 // moearc_matvec_f32 / the decode router: lane l accumulates float4 columns l, l + 32, ... with
-// fmaf over x, y, z, w in turn, then an xor-shuffle tree.
+// fmaf over x, y, z, w in turn, then an xor-shuffle tree. A warp folds PF_LOGIT_EXP experts
+// against all PF_LOGIT_TOK tokens at once (64 accumulators a lane), so each router load from
+// L2 and each activation load from shared memory feeds 16 and 4 folds.
 __global__ void __launch_bounds__(256) k_pf_logits(pf_route_args a) {
     extern __shared__ __align__(16) float xs[];  // [PF_LOGIT_TOK][H]
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -74,29 +77,50 @@ __global__ void __launch_bounds__(256) k_pf_logits(pf_route_args a) {
         xs[2 * i + 1] = __uint_as_float(v & 0xFFFF0000u);
     }
     __syncthreads();
-    for (int e = warp; e < a.E; e += blockDim.x >> 5) {
-        const float4 *wr = reinterpret_cast<const float4 *>(a.router + (size_t)e * H);
-        float acc[PF_LOGIT_TOK];
+    const int nwarps = blockDim.x >> 5;
+    for (int e0 = warp * PF_LOGIT_EXP; e0 < a.E; e0 += nwarps * PF_LOGIT_EXP) {
+        float acc[PF_LOGIT_EXP][PF_LOGIT_TOK];
 #pragma unroll
-        for (int t = 0; t < PF_LOGIT_TOK; ++t) acc[t] = 0.f;
+        for (int j = 0; j < PF_LOGIT_EXP; ++j)
+#pragma unroll
+            for (int t = 0; t < PF_LOGIT_TOK; ++t) acc[j][t] = 0.f;
+        // the router columns of the next step are loaded one step ahead (L2 latency is long and
+        // few warps share an SM)
+        auto load_w = [&](int c, float4 (&w)[PF_LOGIT_EXP]) {
+#pragma unroll
+            for (int j = 0; j < PF_LOGIT_EXP; ++j)
+                w[j] = (c < n4 && e0 + j < a.E) ? __ldg(reinterpret_cast<const float4 *>(a.router + (size_t)(e0 + j) * H) + c)
+                                                : make_float4(0.f, 0.f, 0.f, 0.f);
+        };
+        float4 wn[PF_LOGIT_EXP];
+        load_w(lane, wn);
         for (int c = lane; c < n4; c += 32) {
-            const float4 wv = __ldg(wr + c);
+            float4 wv[PF_LOGIT_EXP];
+#pragma unroll
+            for (int j = 0; j < PF_LOGIT_EXP; ++j) wv[j] = wn[j];
+            load_w(c + 32, wn);
 #pragma unroll
             for (int t = 0; t < PF_LOGIT_TOK; ++t) {
                 const float4 xv = reinterpret_cast<const float4 *>(xs + (size_t)t * H)[c];
-                acc[t] = fmaf(wv.x, xv.x, acc[t]);
-                acc[t] = fmaf(wv.y, xv.y, acc[t]);
-                acc[t] = fmaf(wv.z, xv.z, acc[t]);
-                acc[t] = fmaf(wv.w, xv.w, acc[t]);
+#pragma unroll
+                for (int j = 0; j < PF_LOGIT_EXP; ++j) {
+                    acc[j][t] = fmaf(wv[j].x, xv.x, acc[j][t]);
+                    acc[j][t] = fmaf(wv[j].y, xv.y, acc[j][t]);
+                    acc[j][t] = fmaf(wv[j].z, xv.z, acc[j][t]);
+                    acc[j][t] = fmaf(wv[j].w, xv.w, acc[j][t]);
+                }
             }
         }
 #pragma unroll
-        for (int t = 0; t < PF_LOGIT_TOK; ++t) {
-            float v = acc[t];
+        for (int j = 0; j < PF_LOGIT_EXP; ++j)
 #pragma unroll
-            for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-            if (lane == 0 && t < nt) a.logits[(size_t)(t0 + t) * a.E + e] = a.rbias ? v + a.rbias[e] : v;
-        }
+            for (int t = 0; t < PF_LOGIT_TOK; ++t) {
+                float v = acc[j][t];
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+                const int e = e0 + j;
+                if (lane == 0 && t < nt && e < a.E) a.logits[(size_t)(t0 + t) * a.E + e] = a.rbias ? v + a.rbias[e] : v;
+            }
     }
 }
 
@@ -460,8 +484,9 @@ extern "C" {
 moearc_x_prefill *moearc_x_prefill_create(moearc_ctx *c, const moearc_x_moe_desc *d) {
     if (!c || !d) return nullptr;
     if (d->wtype != T_MXFP4 && d->wtype != T_Q4_0) return nullptr;
+    // the router kernel holds PF_LOGIT_TOK f32 activations in shared memory (n_embd <= 3584)
     if (d->n_embd % 64 || d->n_ff % 64 || d->n_expert == 0 || d->n_expert > 1024 || d->k == 0 || d->k > 32 ||
-        d->k > d->n_expert || d->max_tokens == 0)
+        d->k > d->n_expert || d->max_tokens == 0 || (size_t)PF_LOGIT_TOK * d->n_embd * 4 > 227 * 1024)
         return nullptr;
     auto *p = new moearc_x_prefill();
     p->c = c;
