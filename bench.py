@@ -347,7 +347,89 @@ def prefill_bench(args) -> dict:
             "counts": cnt, "clocks": clocks, "T": T, "H": H, "I": I, "E": E, "k": k}
 
 
+def prefill_ep_bench(args, rank: int, world: int) -> dict:
+    """configs[3] with the experts split over `world` GPUs (16 per GPU at 8): each rank holds
+    tokens / world tokens, routes them, dispatches rows to the experts' owners and combines the
+    returned rows (moearc_b200.ep over NCCL). Per step the device time is taken on every rank
+    (events on the library stream around whole steps, which wait for their collectives) and the
+    maximum over ranks is reported."""
+    import datetime
+
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+
+    from moearc_b200 import Context
+    from moearc_b200.ep import ExpertParallelPrefill
+    from moearc_b200.moe import MoeLayer
+
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300))
+    torch.cuda.set_device(0)
+    ctx = Context()
+    lib = ctx.lib
+    H = I = 2880
+    E, k = args.experts, 4
+    T = args.tokens // world
+    nb = E * I * H // 32
+    banks = [ctx.alloc(nb * 17) for _ in range(3)]
+    for i, b in enumerate(banks):
+        ctx._finish(lib.moearc_x_synth(ctx.raw, b.ptr, nb, 2, 0x9F00 + i, 0.0, -8, -4), "synth")
+    router = ctx.alloc(E * H * 4)
+    ctx._finish(lib.moearc_x_synth(ctx.raw, router.ptr, E * H, 0, 0x9F07, 0.02, 0, 0), "synth")
+    rank_e = np.random.default_rng(0x21FF).permutation(E) + 1
+    pz = rank_e.astype(np.float64) ** -1.1
+    bias = ctx.upload_new(np.log(pz / pz.sum()).astype(np.float32))
+    packer = MoeLayer(ctx, H, I, E, k, 2, 1, 39, max_tokens=1)
+    packer.pack(*banks)
+    for b in banks:
+        b.free()
+    ep = ExpertParallelPrefill(ctx, None, H, I, E, k, 2, 1, 39, max_tokens=T, max_rows=args.tokens * k)
+    ep.load(packer.gateup, packer.down)
+    x = ctx.alloc(T * H * 2)
+    ctx._finish(lib.moearc_x_synth(ctx.raw, x.ptr, T * H, 1, 0x9F08 + rank, 1.0, 0, 0), "synth")
+    out = ctx.alloc(T * H * 4)
+    for _ in range(args.warmup):
+        ep.forward(x, T, router, out.ptr, router_b=bias)
+    ctx.sync()
+    dist.barrier()
+    ctx.timer_start()
+    recv = []
+    for _ in range(args.steps):
+        pl = ep.forward(x, T, router, out.ptr, router_b=bias)
+        recv.append(pl["n_recv"])
+    ms = ctx.timer_stop()
+    t = torch.tensor([ms, float(max(recv))], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    dist.barrier()
+    ep.close()
+    packer.close()
+    dist.destroy_process_group()
+    ctx.close()
+    return {"ms_step": float(t[0]) / args.steps, "max_rows": int(t[1]), "T": T * world, "H": H, "I": I, "E": E,
+            "k": k}
+
+
 def prefill_main(args) -> None:
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    if world > 1:
+        rank = int(os.environ.get("RANK", "0"))
+        r = prefill_ep_bench(args, rank, world)
+        if rank != 0:
+            return
+        T, H, I, k = r["T"], r["H"], r["I"], r["k"]
+        flops = 6.0 * T * k * H * I
+        line = {
+            "metric": "MoE prefill TFLOP/s, one gpt-oss-120b-shaped MoE block, experts split over the GPUs (configs[3])",
+            "value": flops / (r["ms_step"] / 1000.0) / 1e12, "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": r["ms_step"], "tokens_per_s": T / (r["ms_step"] / 1000.0),
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": "bf16 operands, f32 accumulate", "data": "synthetic (as the 1-GPU prefill line)",
+            "config": {"workload": f"configs[3] MoE block: {T} tokens, {r['E']} experts top-4, {r['E'] // world} per GPU, "
+                                   "dispatch and combine by NCCL all-to-all", "max_rows_on_a_rank": r["max_rows"],
+                       "parallelism": f"ep{world}"},
+        }
+        print(json.dumps(line))
+        return
     r = prefill_bench(args)
     T, H, I, k = r["T"], r["H"], r["I"], r["k"]
     flops = 6.0 * T * k * H * I  # gate and up (2 x 2 H I) and down (2 H I) per (token, expert)
@@ -396,8 +478,7 @@ def main() -> None:
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.config == "prefill":
-        if int(os.environ.get("RANK", "0")) == 0:
-            prefill_main(args)
+        prefill_main(args)
         return
 
     from moearc_b200.decoder import DecoderConfig

@@ -216,6 +216,27 @@ int moearc_x_prefill_forward(moearc_x_prefill *p, const unsigned short *x, unsig
 void *moearc_x_prefill_buffer(moearc_x_prefill *p, int which);
 /* Reads and clears the device status word: 0, or bit 0 = a pipeline wait gave up. */
 int moearc_x_prefill_status(moearc_x_prefill *p);
+/* Experts [e_first, e_first + n) only, into the object's weight slots 0 .. n-1 (the experts a
+ * rank owns under expert parallelism); moearc_x_prefill_load is the range [0, E). */
+int moearc_x_prefill_load_range(moearc_x_prefill *p, const void *gateup_packed, const void *down_packed,
+                                unsigned int e_first, unsigned int n);
+/* The three parts of moearc_x_prefill_forward, for expert parallelism:
+ * route: routing and grouping of n_tokens; the activations are then in expert order (buffer 6:
+ *   rows of expert e at [offsets[e], offsets[e+1]), buffer 10), counts in buffer 3.
+ * experts: the expert FFN over n_rows rows of rows_in (bf16 [n_rows][n_embd]) given as n_seg
+ *   consecutive segments, segment s holding seg_counts[s] rows of the loaded expert slot
+ *   seg_expert[s] (host arrays, n_seg <= 1024, counts summing to n_rows); y_out (f32
+ *   [n_rows][n_embd]) gets one row per input row in the same order; act_scratch is bf16
+ *   [n_rows][n_ff]. -2 on inconsistent segments.
+ * combine: out[t] = residual[t] (if not NULL) + sum_m w[t,m] y[row(t,m)] for the tokens of the
+ *   last route call, y_rows f32 [n_tokens k][n_embd] in that call's expert order. */
+int moearc_x_prefill_route(moearc_x_prefill *p, const unsigned short *x, unsigned int n_tokens,
+                           const float *router_w, const float *router_b);
+int moearc_x_prefill_experts(moearc_x_prefill *p, const unsigned short *rows_in, unsigned int n_rows,
+                             const int *seg_counts, const int *seg_expert, unsigned int n_seg,
+                             unsigned short *act_scratch, float *y_out);
+int moearc_x_prefill_combine(moearc_x_prefill *p, const float *y_rows, unsigned int n_tokens,
+                             const float *residual, float *out);
 /* moearc_x_prefill_forward with an event between its kernels, waited for: ms[i] = device time of
  * kernel i (0 router logits, 1 top-k, 2 scan, 3 scatter, 4 gate-up GEMM, 5 down GEMM, 6 combine);
  * n >= 7. */

@@ -80,6 +80,10 @@ SIGNATURES: dict[str, tuple] = {
     "moearc_x_prefill_buffer": (P, [P, I]),
     "moearc_x_prefill_status": (I, [P]),
     "moearc_x_prefill_profile": (I, [P, P, U, P, P, P, P, P, I]),
+    "moearc_x_prefill_load_range": (I, [P, P, P, U, U]),
+    "moearc_x_prefill_route": (I, [P, P, U, P, P]),
+    "moearc_x_prefill_experts": (I, [P, P, U, P, P, U, P, P]),
+    "moearc_x_prefill_combine": (I, [P, P, U, P, P]),
     "moearc_x_decoder_create": (P, [P, P]),
     "moearc_x_decoder_destroy": (None, [P]),
     "moearc_x_decoder_input": (P, [P]),

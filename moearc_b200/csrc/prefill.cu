@@ -249,9 +249,10 @@ __global__ void __launch_bounds__(256) k_pf_unpack(const uint8_t *bank, int E, i
 struct pf_gemm_args {
     int Mrows;        // feature rows of one matrix per expert (gate-up: n_ff; down: n_embd)
     int K;            // reduction length (gate-up: n_embd; down: n_ff)
-    int E;
-    const int *off;   // [E + 1] row offsets of the expert segments
+    int E;            // segments (runs of rows of one expert; one per expert on one GPU)
+    const int *off;   // [E + 1] row offsets of the segments
     const int *toff;  // [E + 1] 128-row tile offsets
+    const int *seg_w; // [E] expert (weight block) of each segment; null: segment e is expert e
     int act;          // gate-up epilogue
     float alpha, limit;
     uint16_t *act_out;  // gate-up: [rows][n_ff] bf16
@@ -328,7 +329,8 @@ __global__ void __launch_bounds__(192, 1) k_pf_gemm(const __grid_constant__ CUte
             for (long tile = blockIdx.x; tile < total && !abort_; tile += gridDim.x) {
                 int e, nt, mt;
                 locate(tile, e, nt, mt);
-                const int rowA = MODE == 0 ? e * 2 * a.Mrows + mt * PF_BM : e * a.Mrows + mt * PF_BM;
+                const int we = a.seg_w ? a.seg_w[e] : e;
+                const int rowA = MODE == 0 ? we * 2 * a.Mrows + mt * PF_BM : we * a.Mrows + mt * PF_BM;
                 const int rowB = a.off[e] + nt * PF_BN;
                 for (int kb = 0; kb < KB; ++kb, ++g) {
                     const int s = (int)(g % C::STAGES);
@@ -475,6 +477,7 @@ struct moearc_x_prefill {
     float *logits, *y, *wts;
     unsigned *idx;
     int *cnt, *off, *toff, *cursor, *perm, *status;
+    int *seg_cnt, *seg_off, *seg_toff, *seg_w, *seg_cur;  // expert-parallel segments (<= 1024)
     uint16_t *xp, *actb, *wgu, *wdn;
     CUtensorMap map_wgu, map_xp, map_wdn, map_act;
 };
@@ -513,6 +516,7 @@ moearc_x_prefill *moearc_x_prefill_create(moearc_ctx *c, const moearc_x_moe_desc
     const size_t o_cnt = take(sizeof(int) * (p->E + 1)), o_off = take(sizeof(int) * (p->E + 1));
     const size_t o_toff = take(sizeof(int) * (p->E + 1)), o_cur = take(sizeof(int) * (p->E + 1));
     const size_t o_perm = take(sizeof(int) * rows), o_st = take(sizeof(int));
+    const size_t o_seg = take(sizeof(int) * 5 * 1025);
     const size_t o_xp = take(2 * rows * p->H), o_act = take(2 * rows * p->I);
     const size_t o_wgu = take(2 * (size_t)p->E * 2 * p->I * p->H), o_wdn = take(2 * (size_t)p->E * p->H * p->I);
     if (cudaMalloc(&p->mem, off) != cudaSuccess) {
@@ -531,6 +535,11 @@ moearc_x_prefill *moearc_x_prefill_create(moearc_ctx *c, const moearc_x_moe_desc
     p->cursor = reinterpret_cast<int *>(b + o_cur);
     p->perm = reinterpret_cast<int *>(b + o_perm);
     p->status = reinterpret_cast<int *>(b + o_st);
+    p->seg_cnt = reinterpret_cast<int *>(b + o_seg);
+    p->seg_off = p->seg_cnt + 1025;
+    p->seg_toff = p->seg_off + 1025;
+    p->seg_w = p->seg_toff + 1025;
+    p->seg_cur = p->seg_w + 1025;
     p->xp = reinterpret_cast<uint16_t *>(b + o_xp);
     p->actb = reinterpret_cast<uint16_t *>(b + o_act);
     p->wgu = reinterpret_cast<uint16_t *>(b + o_wgu);
@@ -560,24 +569,30 @@ void moearc_x_prefill_destroy(moearc_x_prefill *p) {
     delete p;
 }
 
-int moearc_x_prefill_load(moearc_x_prefill *p, const void *gateup_packed, const void *down_packed) {
+int moearc_x_prefill_load_range(moearc_x_prefill *p, const void *gateup_packed, const void *down_packed,
+                                unsigned e_first, unsigned n) {
     if (!p || !gateup_packed || !down_packed) return ERR;
+    if (n == 0 || e_first + n > (unsigned)p->E) return ERR_ARG;
     moearc_ctx *c = p->c;
-    const long gu_tiles = (long)p->E * (p->I / 16) * (p->H / 64) * 2, dn_tiles = (long)p->E * (p->H / 16) * (p->I / 64);
+    const int E = (int)n;
+    const size_t gu_e = (size_t)(p->I / 16) * (p->H / 64) * 2 * p->tile_bytes, dn_e = (size_t)(p->H / 16) * (p->I / 64) * p->tile_bytes;
+    const uint8_t *gu = static_cast<const uint8_t *>(gateup_packed) + e_first * gu_e;
+    const uint8_t *dn = static_cast<const uint8_t *>(down_packed) + e_first * dn_e;
+    const long gu_tiles = (long)E * (p->I / 16) * (p->H / 64) * 2, dn_tiles = (long)E * (p->H / 16) * (p->I / 64);
     const bool mx = p->wtype == T_MXFP4;
     auto grid = [](long warps) { return dim3((unsigned)((warps + 7) / 8)); };
     if (mx) {
-        k_pf_unpack<39><<<grid(gu_tiles), 256, 0, c->stream>>>(static_cast<const uint8_t *>(gateup_packed), p->E, p->I,
-                                                               p->H, 2, p->tile_bytes, p->wgu);
-        k_pf_unpack<39><<<grid(dn_tiles), 256, 0, c->stream>>>(static_cast<const uint8_t *>(down_packed), p->E, p->H,
-                                                               p->I, 1, p->tile_bytes, p->wdn);
+        k_pf_unpack<39><<<grid(gu_tiles), 256, 0, c->stream>>>(gu, E, p->I, p->H, 2, p->tile_bytes, p->wgu);
+        k_pf_unpack<39><<<grid(dn_tiles), 256, 0, c->stream>>>(dn, E, p->H, p->I, 1, p->tile_bytes, p->wdn);
     } else {
-        k_pf_unpack<2><<<grid(gu_tiles), 256, 0, c->stream>>>(static_cast<const uint8_t *>(gateup_packed), p->E, p->I,
-                                                              p->H, 2, p->tile_bytes, p->wgu);
-        k_pf_unpack<2><<<grid(dn_tiles), 256, 0, c->stream>>>(static_cast<const uint8_t *>(down_packed), p->E, p->H,
-                                                              p->I, 1, p->tile_bytes, p->wdn);
+        k_pf_unpack<2><<<grid(gu_tiles), 256, 0, c->stream>>>(gu, E, p->I, p->H, 2, p->tile_bytes, p->wgu);
+        k_pf_unpack<2><<<grid(dn_tiles), 256, 0, c->stream>>>(dn, E, p->H, p->I, 1, p->tile_bytes, p->wdn);
     }
     return cudaGetLastError() == cudaSuccess ? OK : ERR;
+}
+
+int moearc_x_prefill_load(moearc_x_prefill *p, const void *gateup_packed, const void *down_packed) {
+    return p ? moearc_x_prefill_load_range(p, gateup_packed, down_packed, 0, (unsigned)p->E) : ERR;
 }
 
 }  // extern "C"
@@ -659,6 +674,89 @@ int moearc_x_prefill_profile(moearc_x_prefill *p, const uint16_t *x, unsigned n_
     }
     for (auto &e : ev) cudaEventDestroy(e);
     return rc;
+}
+
+// Routing and grouping only (the first four kernels of moearc_x_prefill_forward): the tokens'
+// activations end up in expert order (buffer 6), with the counts (3), the segment offsets (10)
+// and the row of each (token, choice) (9). For expert parallelism, where the rows of each
+// expert range travel to the rank that owns it before moearc_x_prefill_experts.
+int moearc_x_prefill_route(moearc_x_prefill *p, const uint16_t *x, unsigned n_tokens, const float *router_w,
+                           const float *router_b) {
+    if (!p || !x || !router_w) return ERR;
+    if (n_tokens == 0) return OK;
+    if ((int)n_tokens > p->T_max) return ERR_ARG;
+    if ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(router_w)) & 15) return ERR_ARG;
+    cudaStream_t st = p->c->stream;
+    const int T = (int)n_tokens;
+    if (cudaMemsetAsync(p->cnt, 0, sizeof(int) * (p->E + 1), st) != cudaSuccess) return ERR;
+    pf_route_args ra{x, router_w, router_b, T, p->H, p->E, p->K, p->gating, p->logits, p->idx, p->wts, p->cnt};
+    k_pf_logits<<<(T + PF_LOGIT_TOK - 1) / PF_LOGIT_TOK, 256, PF_LOGIT_TOK * p->H * 4, st>>>(ra);
+    k_pf_topk<<<(T + 7) / 8, 256, 0, st>>>(ra);
+    k_pf_scan<<<1, 1024, 0, st>>>(p->cnt, p->E, p->off, p->toff, p->cursor);
+    const long pairs = (long)T * p->K;
+    k_pf_scatter<<<(unsigned)((pairs + 7) / 8), 256, 0, st>>>(x, p->idx, T, p->K, p->H, p->off, p->cursor, p->perm, p->xp);
+    return cudaGetLastError() == cudaSuccess ? OK : ERR;
+}
+
+// The expert FFN over rows given in segments: segment s holds seg_counts[s] consecutive rows of
+// rows_in (bf16 [n_rows][n_embd]) for expert seg_expert[s], an index into the experts last
+// loaded by moearc_x_prefill_load_range (0 = its e_first). y_out (f32 [n_rows][n_embd]) gets one
+// row per input row, in the same order; act_scratch is bf16 [n_rows][n_ff]. seg_counts and
+// seg_expert are host arrays of n_seg <= 1024 entries whose counts sum to n_rows.
+int moearc_x_prefill_experts(moearc_x_prefill *p, const uint16_t *rows_in, unsigned n_rows, const int *seg_counts,
+                             const int *seg_expert, unsigned n_seg, uint16_t *act_scratch, float *y_out) {
+    if (!p || !seg_counts || !seg_expert) return ERR;
+    if (n_seg == 0 || n_seg > 1024) return ERR_ARG;
+    long sum = 0;
+    for (unsigned s = 0; s < n_seg; ++s) {
+        if (seg_counts[s] < 0 || seg_expert[s] < 0 || seg_expert[s] >= p->E) return ERR_ARG;
+        sum += seg_counts[s];
+    }
+    if (sum != (long)n_rows) return ERR_ARG;
+    if (n_rows == 0) return OK;
+    if (!rows_in || !act_scratch || !y_out) return ERR;
+    if ((reinterpret_cast<uintptr_t>(rows_in) | reinterpret_cast<uintptr_t>(act_scratch)) & 15) return ERR_ARG;
+    moearc_ctx *c = p->c;
+    cudaStream_t st = c->stream;
+    CUtensorMap map_rows, map_act;
+    if (!make_map(&map_rows, rows_in, (long)n_rows, p->H) || !make_map(&map_act, act_scratch, (long)n_rows, p->I))
+        return ERR_ARG;
+    if (cudaMemcpyAsync(p->seg_cnt, seg_counts, sizeof(int) * n_seg, cudaMemcpyHostToDevice, st) != cudaSuccess ||
+        cudaMemcpyAsync(p->seg_w, seg_expert, sizeof(int) * n_seg, cudaMemcpyHostToDevice, st) != cudaSuccess)
+        return ERR;
+    launch_scope ls(c, "moe_prefill_experts", (unsigned long)p->H, n_rows);
+    k_pf_scan<<<1, 1024, 0, st>>>(p->seg_cnt, (int)n_seg, p->seg_off, p->seg_toff, p->seg_cur);
+    pf_gemm_args g{};
+    g.E = (int)n_seg;
+    g.off = p->seg_off;
+    g.toff = p->seg_toff;
+    g.seg_w = p->seg_w;
+    g.act = p->act;
+    g.alpha = p->alpha;
+    g.limit = p->limit;
+    g.act_out = act_scratch;
+    g.y_out = y_out;
+    g.status = p->status;
+    g.Mrows = p->I;
+    g.K = p->H;
+    k_pf_gemm<0><<<c->sm_count, 192, pf_cfg<0>::SMEM, st>>>(p->map_wgu, map_rows, g);
+    g.Mrows = p->H;
+    g.K = p->I;
+    k_pf_gemm<1><<<c->sm_count, 192, pf_cfg<1>::SMEM, st>>>(p->map_wdn, map_act, g);
+    return ls.finish();
+}
+
+// out[t] = residual[t] (if not NULL) + sum_m w[t,m] y[row(t,m)] for the tokens of the last
+// moearc_x_prefill_route call, y_rows (f32 [T k][n_embd]) in the expert order that call produced.
+int moearc_x_prefill_combine(moearc_x_prefill *p, const float *y_rows, unsigned n_tokens, const float *residual,
+                             float *out) {
+    if (!p || !y_rows || !out) return ERR;
+    if (n_tokens == 0) return OK;
+    if ((int)n_tokens > p->T_max) return ERR_ARG;
+    const long n = (long)n_tokens * p->H;
+    k_pf_combine<<<(unsigned)((n + 255) / 256), 256, 0, p->c->stream>>>(y_rows, p->perm, p->wts, residual, out,
+                                                                        (int)n_tokens, p->K, p->H);
+    return cudaGetLastError() == cudaSuccess ? OK : ERR;
 }
 
 // 0 expert ids [T x k] (u32), 1 gating weights [T x k], 2 logits [T x E], 3 per-expert counts

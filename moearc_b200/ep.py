@@ -1,0 +1,110 @@
+"""Expert parallelism for the prefill MoE block: the experts are split into
+contiguous ranges over the ranks of a process group (one process per GPU); each rank routes its
+own tokens, sends each (token, choice) row to the rank that owns its expert, runs its experts on
+the rows it received and sends the results back, where the combine runs in router order.
+
+The device work is the library's (moearc_x_prefill_route / _experts / _combine); the exchange is
+torch.distributed's all-to-all over NCCL. Rows leave a rank already grouped by expert (the route
+step orders them so), and with contiguous expert ranges that is also destination order, so the
+dispatch needs no packing; the receiver runs its grouped GEMMs over the (source, expert) blocks
+as they arrive, and its result rows go back in the same order, so the combine reads them where
+the route step put the rows.
+"""
+from __future__ import annotations
+
+import numpy as np
+
+
+def plan(counts_all: np.ndarray, rank: int, world: int) -> dict:
+    """Exchange plan from every rank's per-expert row counts (counts_all[src][e]).
+
+    send[r]   rows this rank sends to rank r (its rows for r's experts, in expert order)
+    recv[s]   rows this rank receives from rank s
+    seg_counts, seg_expert: the received rows as segments, source-major then expert, each
+              naming the local expert slot (0 .. n_local-1) it belongs to.
+    """
+    counts_all = np.asarray(counts_all, np.int64)
+    E = counts_all.shape[1]
+    if counts_all.shape[0] != world or E % world:
+        raise ValueError("counts_all must be [world][E] with E divisible by world")
+    nl = E // world
+    lo = rank * nl
+    send = [int(counts_all[rank, r * nl:(r + 1) * nl].sum()) for r in range(world)]
+    recv = [int(counts_all[s, lo:lo + nl].sum()) for s in range(world)]
+    seg_counts = counts_all[:, lo:lo + nl].reshape(-1).astype(np.int32)
+    seg_expert = np.tile(np.arange(nl, dtype=np.int32), world)
+    return {"n_local": nl, "e_first": lo, "send": send, "recv": recv, "seg_counts": seg_counts,
+            "seg_expert": seg_expert, "n_recv": int(sum(recv))}
+
+
+class _Dev:
+    """A device pointer seen by torch (zero copy) through __cuda_array_interface__."""
+
+    def __init__(self, ptr: int, shape: tuple, typestr: str):
+        self.__cuda_array_interface__ = {"data": (int(ptr), False), "shape": shape, "typestr": typestr,
+                                         "version": 3, "strides": None}
+
+
+class ExpertParallelPrefill:
+    """One rank's share of an expert-parallel MoE block. `max_rows` bounds the rows a rank may
+    receive (all ranks' tokens x k at most)."""
+
+    def __init__(self, ctx, group, n_embd: int, n_ff: int, n_expert: int, k: int, gating: int, act: int,
+                 wtype: int, max_tokens: int, max_rows: int):
+        import torch
+        import torch.distributed as dist
+
+        from .moe import MoePrefill
+
+        self.torch, self.dist, self.group = torch, dist, group
+        self.ctx = ctx
+        self.rank = dist.get_rank(group)
+        self.world = dist.get_world_size(group)
+        if n_expert % self.world:
+            raise ValueError("the experts must split evenly over the ranks")
+        self.H, self.I, self.E, self.k = n_embd, n_ff, n_expert, k
+        self.pf = MoePrefill(ctx, n_embd, n_ff, n_expert, k, gating, act, wtype, max_tokens)
+        self.nl = n_expert // self.world
+        self.e_first = self.rank * self.nl
+        dev = torch.device("cuda")
+        self.recv = torch.empty((max_rows, n_embd * 2), dtype=torch.uint8, device=dev)
+        self.act = torch.empty((max_rows, n_ff * 2), dtype=torch.uint8, device=dev)
+        self.y = torch.empty((max_rows, n_embd), dtype=torch.float32, device=dev)
+        self.y_back = torch.empty((max_tokens * k, n_embd), dtype=torch.float32, device=dev)
+        self.max_rows = max_rows
+        self.last = None
+
+    def close(self) -> None:
+        self.pf.close()
+
+    def load(self, gateup, down) -> None:
+        """Expand this rank's experts from the full packed banks."""
+        self.pf.load_range(gateup, down, self.e_first, self.nl)
+
+    def forward(self, x_bf16, n_tokens: int, router_w, out_ptr: int, router_b=None, residual_ptr=None) -> dict:
+        torch, dist = self.torch, self.dist
+        T, k, H = n_tokens, self.k, self.H
+        self.pf.route(x_bf16, T, router_w, router_b)
+        counts = self.pf.buffer(3, np.int32, self.E)  # waits for the route step
+        mine = torch.from_numpy(counts.astype(np.int64)).cuda()
+        gathered = [torch.empty_like(mine) for _ in range(self.world)]
+        dist.all_gather(gathered, mine, group=self.group)
+        counts_all = torch.stack(gathered).cpu().numpy()
+        pl = plan(counts_all, self.rank, self.world)
+        if pl["n_recv"] > self.max_rows:
+            raise ValueError(f"rank {self.rank} would receive {pl['n_recv']} rows > max_rows {self.max_rows}")
+        xp = torch.as_tensor(_Dev(self.pf.buffer_ptr(6), (T * k, H * 2), "|u1"), device="cuda")
+        recv = self.recv[:pl["n_recv"]]
+        dist.all_to_all_single(recv, xp, output_split_sizes=pl["recv"], input_split_sizes=pl["send"],
+                               group=self.group)
+        torch.cuda.synchronize()
+        y = self.y[:pl["n_recv"]]
+        self.pf.experts(recv.data_ptr(), pl["n_recv"], pl["seg_counts"], pl["seg_expert"], self.act.data_ptr(),
+                        y.data_ptr())
+        self.ctx.sync()
+        yb = self.y_back[:T * k]
+        dist.all_to_all_single(yb, y, output_split_sizes=pl["send"], input_split_sizes=pl["recv"], group=self.group)
+        torch.cuda.synchronize()
+        self.pf.combine(yb.data_ptr(), T, out_ptr, residual_ptr)
+        self.last = pl
+        return pl

@@ -110,3 +110,38 @@ class MoePrefill:
         out = np.empty(n, dtype)
         self.ctx._finish(self.ctx.lib.moearc_copy_d2h(self.ctx.raw, out.ctypes.data, p, out.nbytes), "download")
         return out
+
+
+def _prefill_split_methods():
+    """The expert-parallel parts of MoePrefill (route / experts / combine, ranged load)."""
+
+    def load_range(self, gateup: DeviceBuffer, down: DeviceBuffer, e_first: int, n: int) -> None:
+        self.ctx._finish(self.ctx.lib.moearc_x_prefill_load_range(self.h, gateup.ptr, down.ptr, e_first, n),
+                         "prefill_load_range")
+
+    def route(self, x_bf16, n_tokens: int, router_w: DeviceBuffer, router_b: DeviceBuffer | None = None) -> None:
+        ptr = x_bf16 if isinstance(x_bf16, int) else x_bf16.ptr
+        rc = self.ctx.lib.moearc_x_prefill_route(self.h, ptr, n_tokens, router_w.ptr,
+                                                 None if router_b is None else router_b.ptr)
+        self.ctx._finish(rc, "prefill_route")
+
+    def experts(self, rows_ptr: int, n_rows: int, seg_counts: np.ndarray, seg_expert: np.ndarray,
+                act_ptr: int, y_ptr: int) -> None:
+        sc = np.ascontiguousarray(seg_counts, np.int32)
+        se = np.ascontiguousarray(seg_expert, np.int32)
+        rc = self.ctx.lib.moearc_x_prefill_experts(self.h, rows_ptr, n_rows, sc.ctypes.data, se.ctypes.data,
+                                                   len(sc), act_ptr, y_ptr)
+        self.ctx._finish(rc, "prefill_experts")
+
+    def combine(self, y_ptr: int, n_tokens: int, out_ptr: int, residual_ptr: int | None = None) -> None:
+        rc = self.ctx.lib.moearc_x_prefill_combine(self.h, y_ptr, n_tokens, residual_ptr, out_ptr)
+        self.ctx._finish(rc, "prefill_combine")
+
+    def buffer_ptr(self, which: int) -> int:
+        return self.ctx.lib.moearc_x_prefill_buffer(self.h, which)
+
+    for f in (load_range, route, experts, combine, buffer_ptr):
+        setattr(MoePrefill, f.__name__, f)
+
+
+_prefill_split_methods()

@@ -155,3 +155,57 @@ def test_skewed_routing_many_tokens_against_torch(ctx):
     assert err <= 1e-2
     pf.close()
     packer.close()
+
+
+@pytest.mark.parametrize("world", [2, 4])
+def test_expert_parallel_split_gives_the_same_bits(ctx, world):
+    """Expert parallelism emulated on one GPU: each virtual rank routes its own tokens, owns a
+    contiguous expert range (moearc_x_prefill_load_range), receives the rows of its experts from
+    every rank as (source, expert) segments and returns the result rows; the combine on each rank
+    then gives the single-GPU block's output bit for bit (a row's arithmetic does not depend on
+    where its segment sits)."""
+    torch = pytest.importorskip("torch")
+    from moearc_b200.ep import plan
+
+    H, I, E, k, T = 1024, 512, 32, 4, 600
+    whole, packer, host = build(ctx, H, I, E, k, 2, 1, O.MXFP4, T, 0x9F41)
+    xb = O.synth_normal_bf16(0x9F42, T * H, 1.0)
+    rw = ctx.upload_new(host[3])
+    ref = ctx.alloc_n(np.float32, T * H)
+    whole.forward(ctx.upload_new(xb), T, rw, ref)
+    want = ctx.download(ref, np.float32, T * H).reshape(T, H)
+    Tr = T // world
+    nl = E // world
+    ranks = []
+    for r in range(world):
+        pf = MoePrefill(ctx, H, I, E, k, 2, 1, O.MXFP4, max_tokens=Tr)
+        pf.load_range(packer.gateup, packer.down, r * nl, nl)
+        x = ctx.upload_new(xb[r * Tr * H:(r + 1) * Tr * H])
+        pf.route(x, Tr, rw)
+        ranks.append((pf, x, pf.buffer(3, np.int32, E)))
+    counts_all = np.stack([c for _, _, c in ranks])
+    plans = [plan(counts_all, r, world) for r in range(world)]
+    xps = [torch.as_tensor(O.bf16_to_f32(pf.buffer(6, np.uint16, Tr * k * H)).reshape(Tr * k, H)) for pf, _, _ in ranks]
+    send_off = [np.concatenate([[0], np.cumsum(p["send"])]) for p in plans]
+    ys = []
+    for r, (pf, _, _) in enumerate(ranks):
+        rows = torch.cat([xps[s][send_off[s][r]:send_off[s][r + 1]] for s in range(world)])
+        n = rows.shape[0]
+        assert n == plans[r]["n_recv"]
+        rows_dev = ctx.upload_new(O.f32_to_bf16(rows.numpy().ravel()))
+        act = ctx.alloc_n(np.uint16, max(n, 1) * I)
+        y = ctx.alloc_n(np.float32, max(n, 1) * H)
+        pf.experts(rows_dev.ptr, n, plans[r]["seg_counts"], plans[r]["seg_expert"], act.ptr, y.ptr)
+        ys.append(ctx.download(y, np.float32, n * H).reshape(n, H))
+    recv_off = [np.concatenate([[0], np.cumsum(p["recv"])]) for p in plans]
+    for s, (pf, _, _) in enumerate(ranks):
+        back = np.concatenate([ys[r][recv_off[r][s]:recv_off[r][s + 1]] for r in range(world)])
+        out = ctx.alloc_n(np.float32, Tr * H)
+        back_dev = ctx.upload_new(back)  # held: the buffer must outlive the enqueued combine
+        pf.combine(back_dev.ptr, Tr, out.ptr)
+        got = ctx.download(out, np.float32, Tr * H).reshape(Tr, H)
+        assert np.array_equal(got.view(np.uint32), want[s * Tr:(s + 1) * Tr].view(np.uint32)), (world, s)
+        assert pf.status() == 0
+        pf.close()
+    whole.close()
+    packer.close()
