@@ -38,9 +38,15 @@ import time
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
-# One process per GPU: pin this rank's device before anything initialises CUDA.
-if "LOCAL_RANK" in os.environ and "CUDA_VISIBLE_DEVICES" not in os.environ:
-    os.environ["CUDA_VISIBLE_DEVICES"] = os.environ["LOCAL_RANK"]
+# One process per GPU: pin this rank's device before anything initialises CUDA (the rank's entry
+# of an existing device list, or the device numbered by the local rank).
+if "LOCAL_RANK" in os.environ:
+    _lr = int(os.environ["LOCAL_RANK"])
+    _vis = [d for d in os.environ.get("CUDA_VISIBLE_DEVICES", "").split(",") if d.strip()]
+    if len(_vis) > 1:
+        os.environ["CUDA_VISIBLE_DEVICES"] = _vis[_lr % len(_vis)]
+    elif not _vis:
+        os.environ["CUDA_VISIBLE_DEVICES"] = str(_lr)
 
 METRIC = "MoE decode tok/s at gpt-oss-120b shape; expert-GEMM HBM GB/s vs 8 TB/s"
 UNIT = "tok/s"
@@ -388,6 +394,8 @@ def prefill_ep_bench(args, rank: int, world: int) -> dict:
     x = ctx.alloc(T * H * 2)
     ctx._finish(lib.moearc_x_synth(ctx.raw, x.ptr, T * H, 1, 0x9F08 + rank, 1.0, 0, 0), "synth")
     out = ctx.alloc(T * H * 4)
+    ep.forward(x, T, router, out.ptr, router_b=bias)
+    ep.rebalance()  # place the experts by the popularity one step saw (every rank agrees)
     for _ in range(args.warmup):
         ep.forward(x, T, router, out.ptr, router_b=bias)
     ctx.sync()
@@ -406,7 +414,7 @@ def prefill_ep_bench(args, rank: int, world: int) -> dict:
     dist.destroy_process_group()
     ctx.close()
     return {"ms_step": float(t[0]) / args.steps, "max_rows": int(t[1]), "T": T * world, "H": H, "I": I, "E": E,
-            "k": k}
+            "k": k, "rows_total": args.tokens * k}
 
 
 def prefill_main(args) -> None:
@@ -425,7 +433,8 @@ def prefill_main(args) -> None:
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
             "dtype": "bf16 operands, f32 accumulate", "data": "synthetic (as the 1-GPU prefill line)",
             "config": {"workload": f"configs[3] MoE block: {T} tokens, {r['E']} experts top-4, {r['E'] // world} per GPU, "
-                                   "dispatch and combine by NCCL all-to-all", "max_rows_on_a_rank": r["max_rows"],
+                                   "dispatch and combine by NCCL all-to-all; experts placed by the popularity of one "
+                                   "warm-up step", "max_rows_on_a_rank": r["max_rows"], "rows_total": r["rows_total"],
                        "parallelism": f"ep{world}"},
         }
         print(json.dumps(line))

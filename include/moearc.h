@@ -220,6 +220,15 @@ int moearc_x_prefill_status(moearc_x_prefill *p);
  * rank owns under expert parallelism); moearc_x_prefill_load is the range [0, E). */
 int moearc_x_prefill_load_range(moearc_x_prefill *p, const void *gateup_packed, const void *down_packed,
                                 unsigned int e_first, unsigned int n);
+/* Expert experts[i] into weight slot i, i < n (host array of distinct expert ids): the experts a
+ * rank owns under a placement other than contiguous ranges. */
+int moearc_x_prefill_load_list(moearc_x_prefill *p, const void *gateup_packed, const void *down_packed,
+                               const int *experts, unsigned int n);
+/* Row order of the route step: expert e's rows form segment pos[e] (host array, a permutation of
+ * 0 .. E-1); buffers 3 and 10 are then indexed by position. Identity at create, which
+ * moearc_x_prefill_forward requires (-2 otherwise). Under expert parallelism the positions are
+ * owner-major, so each rank's experts are one contiguous range of rows. */
+int moearc_x_prefill_set_order(moearc_x_prefill *p, const int *pos);
 /* The three parts of moearc_x_prefill_forward, for expert parallelism:
  * route: routing and grouping of n_tokens; the activations are then in expert order (buffer 6:
  *   rows of expert e at [offsets[e], offsets[e+1]), buffer 10), counts in buffer 3.

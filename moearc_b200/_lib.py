@@ -84,6 +84,8 @@ SIGNATURES: dict[str, tuple] = {
     "moearc_x_prefill_route": (I, [P, P, U, P, P]),
     "moearc_x_prefill_experts": (I, [P, P, U, P, P, U, P, P]),
     "moearc_x_prefill_combine": (I, [P, P, U, P, P]),
+    "moearc_x_prefill_load_list": (I, [P, P, P, P, U]),
+    "moearc_x_prefill_set_order": (I, [P, P]),
     "moearc_x_decoder_create": (P, [P, P]),
     "moearc_x_decoder_destroy": (None, [P]),
     "moearc_x_decoder_input": (P, [P]),

@@ -58,7 +58,8 @@ struct pf_route_args {
     float *logits;      // [T][E]
     unsigned *idx;      // [T][K]
     float *wts;         // [T][K]
-    int *cnt;           // [E], zeroed before
+    int *cnt;           // [E] counts by position, zeroed before
+    const int *epos;    // [E] position of each expert in the row order
 };
 
 // Logits of PF_LOGIT_TOK tokens against every expert. Per (token, expert) the fold is that of
@@ -131,7 +132,7 @@ __global__ void __launch_bounds__(256) k_pf_topk(pf_route_args a) {
     if (t >= a.T) return;
     xtopk(a.logits + (size_t)t * a.E, a.E, a.K, a.gating, lane, a.idx + (size_t)t * a.K, a.wts + (size_t)t * a.K);
     __syncwarp();
-    if (lane < a.K) atomicAdd(a.cnt + __ldcg(a.idx + (size_t)t * a.K + lane), 1);
+    if (lane < a.K) atomicAdd(a.cnt + a.epos[__ldcg(a.idx + (size_t)t * a.K + lane)], 1);
 }
 
 // Row offsets (off[e], off[E] = T K), 128-row tile offsets (toff[e], toff[E] = all tiles) and
@@ -162,17 +163,19 @@ __global__ void k_pf_scan(const int *cnt, int E, int *off, int *toff, int *curso
     }
 }
 
-// One warp per (token, choice): its row in the expert's segment, and the token's bf16 activation
-// copied there. Rows within a segment are in arrival order; every row's results depend only on
+// One warp per (token, choice): its row in the segment of its expert's position (experts sit in
+// the row order at epos[e]: the identity on one GPU, owner-major under expert parallelism), and
+// the token's bf16 activation copied there. Rows within a segment are in arrival order; every row's results depend only on
 // its own activation, so the order does not reach the output.
-__global__ void __launch_bounds__(256) k_pf_scatter(const uint16_t *x, const unsigned *idx, int T, int K, int H,
-                                                    const int *off, int *cursor, int *perm, uint16_t *xp) {
+__global__ void __launch_bounds__(256) k_pf_scatter(const uint16_t *x, const unsigned *idx, const int *epos, int T,
+                                                    int K, int H, const int *off, int *cursor, int *perm,
+                                                    uint16_t *xp) {
     const int lane = threadIdx.x & 31;
     const long p = (long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
     if (p >= (long)T * K) return;
     int row = 0;
     if (lane == 0) {
-        const int e = (int)idx[p];
+        const int e = epos[idx[p]];
         row = off[e] + atomicAdd(cursor + e, 1);
         perm[p] = row;
     }
@@ -478,6 +481,8 @@ struct moearc_x_prefill {
     unsigned *idx;
     int *cnt, *off, *toff, *cursor, *perm, *status;
     int *seg_cnt, *seg_off, *seg_toff, *seg_w, *seg_cur;  // expert-parallel segments (<= 1024)
+    int *epos;                                          // [E] position of each expert in the row order
+    bool order_identity = true;
     uint16_t *xp, *actb, *wgu, *wdn;
     CUtensorMap map_wgu, map_xp, map_wdn, map_act;
 };
@@ -516,7 +521,7 @@ moearc_x_prefill *moearc_x_prefill_create(moearc_ctx *c, const moearc_x_moe_desc
     const size_t o_cnt = take(sizeof(int) * (p->E + 1)), o_off = take(sizeof(int) * (p->E + 1));
     const size_t o_toff = take(sizeof(int) * (p->E + 1)), o_cur = take(sizeof(int) * (p->E + 1));
     const size_t o_perm = take(sizeof(int) * rows), o_st = take(sizeof(int));
-    const size_t o_seg = take(sizeof(int) * 5 * 1025);
+    const size_t o_seg = take(sizeof(int) * 6 * 1025);
     const size_t o_xp = take(2 * rows * p->H), o_act = take(2 * rows * p->I);
     const size_t o_wgu = take(2 * (size_t)p->E * 2 * p->I * p->H), o_wdn = take(2 * (size_t)p->E * p->H * p->I);
     if (cudaMalloc(&p->mem, off) != cudaSuccess) {
@@ -540,6 +545,7 @@ moearc_x_prefill *moearc_x_prefill_create(moearc_ctx *c, const moearc_x_moe_desc
     p->seg_toff = p->seg_off + 1025;
     p->seg_w = p->seg_toff + 1025;
     p->seg_cur = p->seg_w + 1025;
+    p->epos = p->seg_cur + 1025;
     p->xp = reinterpret_cast<uint16_t *>(b + o_xp);
     p->actb = reinterpret_cast<uint16_t *>(b + o_act);
     p->wgu = reinterpret_cast<uint16_t *>(b + o_wgu);
@@ -551,9 +557,13 @@ moearc_x_prefill *moearc_x_prefill_create(moearc_ctx *c, const moearc_x_moe_desc
                     set_smem(k_pf_gemm<0>, pf_cfg<0>::SMEM) == cudaSuccess &&
                     set_smem(k_pf_gemm<1>, pf_cfg<1>::SMEM) == cudaSuccess &&
                     set_smem(k_pf_logits, PF_LOGIT_TOK * p->H * 4) == cudaSuccess &&
-                    cudaMemsetAsync(p->mem, 0, off, c->stream) == cudaSuccess &&
-                    cudaStreamSynchronize(c->stream) == cudaSuccess;
-    if (!ok) {
+                    cudaMemsetAsync(p->mem, 0, off, c->stream) == cudaSuccess;
+    std::vector<int> ident(p->E);
+    for (int e = 0; e < p->E; ++e) ident[e] = e;
+    const bool ok2 = ok && cudaMemcpyAsync(p->epos, ident.data(), sizeof(int) * p->E, cudaMemcpyHostToDevice,
+                                           c->stream) == cudaSuccess &&
+                     cudaStreamSynchronize(c->stream) == cudaSuccess;
+    if (!ok2) {
         cudaGetLastError();
         cudaFree(p->mem);
         delete p;
@@ -591,6 +601,50 @@ int moearc_x_prefill_load_range(moearc_x_prefill *p, const void *gateup_packed, 
     return cudaGetLastError() == cudaSuccess ? OK : ERR;
 }
 
+// Expert experts[i] into weight slot i, for i < n (host array of distinct expert ids).
+int moearc_x_prefill_load_list(moearc_x_prefill *p, const void *gateup_packed, const void *down_packed,
+                               const int *experts, unsigned n) {
+    if (!p || !gateup_packed || !down_packed || !experts) return ERR;
+    if (n == 0 || n > (unsigned)p->E) return ERR_ARG;
+    for (unsigned i = 0; i < n; ++i)
+        if (experts[i] < 0 || experts[i] >= p->E) return ERR_ARG;
+    moearc_ctx *c = p->c;
+    const size_t gu_e = (size_t)(p->I / 16) * (p->H / 64) * 2 * p->tile_bytes, dn_e = (size_t)(p->H / 16) * (p->I / 64) * p->tile_bytes;
+    const long gu_tiles = (long)(p->I / 16) * (p->H / 64) * 2, dn_tiles = (long)(p->H / 16) * (p->I / 64);
+    const bool mx = p->wtype == T_MXFP4;
+    auto grid = [](long warps) { return dim3((unsigned)((warps + 7) / 8)); };
+    for (unsigned i = 0; i < n; ++i) {
+        const uint8_t *gu = static_cast<const uint8_t *>(gateup_packed) + experts[i] * gu_e;
+        const uint8_t *dn = static_cast<const uint8_t *>(down_packed) + experts[i] * dn_e;
+        uint16_t *wg = p->wgu + (size_t)i * 2 * p->I * p->H, *wd = p->wdn + (size_t)i * p->H * p->I;
+        if (mx) {
+            k_pf_unpack<39><<<grid(gu_tiles), 256, 0, c->stream>>>(gu, 1, p->I, p->H, 2, p->tile_bytes, wg);
+            k_pf_unpack<39><<<grid(dn_tiles), 256, 0, c->stream>>>(dn, 1, p->H, p->I, 1, p->tile_bytes, wd);
+        } else {
+            k_pf_unpack<2><<<grid(gu_tiles), 256, 0, c->stream>>>(gu, 1, p->I, p->H, 2, p->tile_bytes, wg);
+            k_pf_unpack<2><<<grid(dn_tiles), 256, 0, c->stream>>>(dn, 1, p->H, p->I, 1, p->tile_bytes, wd);
+        }
+    }
+    return cudaGetLastError() == cudaSuccess ? OK : ERR;
+}
+
+// The row order of the route step: expert e's rows form segment pos[e] (host array, a permutation
+// of 0 .. E-1). The identity at create; moearc_x_prefill_forward needs the identity.
+int moearc_x_prefill_set_order(moearc_x_prefill *p, const int *pos) {
+    if (!p || !pos) return ERR;
+    std::vector<char> seen(p->E, 0);
+    for (int e = 0; e < p->E; ++e) {
+        if (pos[e] < 0 || pos[e] >= p->E || seen[pos[e]]) return ERR_ARG;
+        seen[pos[e]] = 1;
+    }
+    p->order_identity = true;
+    for (int e = 0; e < p->E; ++e) p->order_identity = p->order_identity && pos[e] == e;
+    return cudaMemcpyAsync(p->epos, pos, sizeof(int) * p->E, cudaMemcpyHostToDevice, p->c->stream) == cudaSuccess &&
+                   cudaStreamSynchronize(p->c->stream) == cudaSuccess
+               ? OK
+               : ERR;
+}
+
 int moearc_x_prefill_load(moearc_x_prefill *p, const void *gateup_packed, const void *down_packed) {
     return p ? moearc_x_prefill_load_range(p, gateup_packed, down_packed, 0, (unsigned)p->E) : ERR;
 }
@@ -605,7 +659,7 @@ int prefill_forward(moearc_x_prefill *p, const uint16_t *x, unsigned n_tokens, c
                     const float *router_b, const float *residual, float *out, cudaEvent_t *ev) {
     if (!p || !x || !router_w || !out) return ERR;
     if (n_tokens == 0) return OK;
-    if ((int)n_tokens > p->T_max) return ERR_ARG;
+    if ((int)n_tokens > p->T_max || !p->order_identity) return ERR_ARG;
     if ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(router_w)) & 15) return ERR_ARG;
     moearc_ctx *c = p->c;
     cudaStream_t st = c->stream;
@@ -616,7 +670,7 @@ int prefill_forward(moearc_x_prefill *p, const uint16_t *x, unsigned n_tokens, c
     };
     if (cudaMemsetAsync(p->cnt, 0, sizeof(int) * (p->E + 1), st) != cudaSuccess) return ERR;
     mark(0);
-    pf_route_args ra{x, router_w, router_b, T, p->H, p->E, p->K, p->gating, p->logits, p->idx, p->wts, p->cnt};
+    pf_route_args ra{x, router_w, router_b, T, p->H, p->E, p->K, p->gating, p->logits, p->idx, p->wts, p->cnt, p->epos};
     k_pf_logits<<<(T + PF_LOGIT_TOK - 1) / PF_LOGIT_TOK, 256, PF_LOGIT_TOK * p->H * 4, st>>>(ra);
     mark(1);
     k_pf_topk<<<(T + 7) / 8, 256, 0, st>>>(ra);
@@ -624,7 +678,8 @@ int prefill_forward(moearc_x_prefill *p, const uint16_t *x, unsigned n_tokens, c
     k_pf_scan<<<1, 1024, 0, st>>>(p->cnt, p->E, p->off, p->toff, p->cursor);
     mark(3);
     const long pairs = (long)T * p->K;
-    k_pf_scatter<<<(unsigned)((pairs + 7) / 8), 256, 0, st>>>(x, p->idx, T, p->K, p->H, p->off, p->cursor, p->perm, p->xp);
+    k_pf_scatter<<<(unsigned)((pairs + 7) / 8), 256, 0, st>>>(x, p->idx, p->epos, T, p->K, p->H, p->off, p->cursor,
+                                                              p->perm, p->xp);
     mark(4);
     pf_gemm_args g{};
     g.E = p->E;
@@ -689,12 +744,13 @@ int moearc_x_prefill_route(moearc_x_prefill *p, const uint16_t *x, unsigned n_to
     cudaStream_t st = p->c->stream;
     const int T = (int)n_tokens;
     if (cudaMemsetAsync(p->cnt, 0, sizeof(int) * (p->E + 1), st) != cudaSuccess) return ERR;
-    pf_route_args ra{x, router_w, router_b, T, p->H, p->E, p->K, p->gating, p->logits, p->idx, p->wts, p->cnt};
+    pf_route_args ra{x, router_w, router_b, T, p->H, p->E, p->K, p->gating, p->logits, p->idx, p->wts, p->cnt, p->epos};
     k_pf_logits<<<(T + PF_LOGIT_TOK - 1) / PF_LOGIT_TOK, 256, PF_LOGIT_TOK * p->H * 4, st>>>(ra);
     k_pf_topk<<<(T + 7) / 8, 256, 0, st>>>(ra);
     k_pf_scan<<<1, 1024, 0, st>>>(p->cnt, p->E, p->off, p->toff, p->cursor);
     const long pairs = (long)T * p->K;
-    k_pf_scatter<<<(unsigned)((pairs + 7) / 8), 256, 0, st>>>(x, p->idx, T, p->K, p->H, p->off, p->cursor, p->perm, p->xp);
+    k_pf_scatter<<<(unsigned)((pairs + 7) / 8), 256, 0, st>>>(x, p->idx, p->epos, T, p->K, p->H, p->off, p->cursor,
+                                                              p->perm, p->xp);
     return cudaGetLastError() == cudaSuccess ? OK : ERR;
 }
 

@@ -1,12 +1,13 @@
-"""Expert parallelism for the prefill MoE block: the experts are split into
-contiguous ranges over the ranks of a process group (one process per GPU); each rank routes its
+"""Expert parallelism for the prefill MoE block: the experts are split over the
+ranks of a process group (one process per GPU); each rank routes its
 own tokens, sends each (token, choice) row to the rank that owns its expert, runs its experts on
 the rows it received and sends the results back, where the combine runs in router order.
 
 The device work is the library's (moearc_x_prefill_route / _experts / _combine); the exchange is
-torch.distributed's all-to-all over NCCL. Rows leave a rank already grouped by expert (the route
-step orders them so), and with contiguous expert ranges that is also destination order, so the
-dispatch needs no packing; the receiver runs its grouped GEMMs over the (source, expert) blocks
+torch.distributed's all-to-all over NCCL. Rows leave a rank already grouped by expert position
+(the route step orders them so), and the positions are owner-major (rank r's experts are one
+contiguous position range, whatever the placement: interleaved ids by default, or balanced by
+measured popularity), so the dispatch needs no packing; the receiver runs its grouped GEMMs over the (source, expert) blocks
 as they arrive, and its result rows go back in the same order, so the combine reads them where
 the route step put the rows.
 """
@@ -15,8 +16,41 @@ from __future__ import annotations
 import numpy as np
 
 
+def interleaved(n_expert: int, world: int) -> list[list[int]]:
+    """Rank r owns experts r, r + world, ... (spreads a popular run of neighbouring ids)."""
+    return [list(range(r, n_expert, world)) for r in range(world)]
+
+
+def balanced(counts: np.ndarray, world: int) -> list[list[int]]:
+    """Experts placed by measured popularity: the busiest first, each to the rank with the fewest
+    rows so far among those with a free slot (every rank owns n_expert / world experts). Ties
+    break by lower rank and lower expert id, so every rank computes the same placement."""
+    counts = np.asarray(counts, np.int64)
+    E = len(counts)
+    nl = E // world
+    order = sorted(range(E), key=lambda e: (-int(counts[e]), e))
+    lists: list[list[int]] = [[] for _ in range(world)]
+    load = [0] * world
+    for e in order:
+        r = min((r for r in range(world) if len(lists[r]) < nl), key=lambda r: (load[r], r))
+        lists[r].append(e)
+        load[r] += int(counts[e])
+    return [sorted(l) for l in lists]
+
+
+def positions(lists: list[list[int]]) -> np.ndarray:
+    """Owner-major row order: expert lists[r][j] sits at position r * n_local + j."""
+    nl = len(lists[0])
+    pos = np.zeros(sum(len(l) for l in lists), np.int32)
+    for r, l in enumerate(lists):
+        for j, e in enumerate(l):
+            pos[e] = r * nl + j
+    return pos
+
+
 def plan(counts_all: np.ndarray, rank: int, world: int) -> dict:
-    """Exchange plan from every rank's per-expert row counts (counts_all[src][e]).
+    """Exchange plan from every rank's per-position row counts (counts_all[src][position]; with
+    owner-major positions rank r owns positions r * n_local .. (r + 1) * n_local - 1).
 
     send[r]   rows this rank sends to rank r (its rows for r's experts, in expert order)
     recv[s]   rows this rank receives from rank s
@@ -65,7 +99,8 @@ class ExpertParallelPrefill:
         self.H, self.I, self.E, self.k = n_embd, n_ff, n_expert, k
         self.pf = MoePrefill(ctx, n_embd, n_ff, n_expert, k, gating, act, wtype, max_tokens)
         self.nl = n_expert // self.world
-        self.e_first = self.rank * self.nl
+        self.lists = interleaved(n_expert, self.world)
+        self.banks = None
         dev = torch.device("cuda")
         self.recv = torch.empty((max_rows, n_embd * 2), dtype=torch.uint8, device=dev)
         self.act = torch.empty((max_rows, n_ff * 2), dtype=torch.uint8, device=dev)
@@ -77,9 +112,27 @@ class ExpertParallelPrefill:
     def close(self) -> None:
         self.pf.close()
 
-    def load(self, gateup, down) -> None:
-        """Expand this rank's experts from the full packed banks."""
-        self.pf.load_range(gateup, down, self.e_first, self.nl)
+    def load(self, gateup, down, lists: list[list[int]] | None = None) -> None:
+        """Place the experts (default: interleaved) and expand this rank's from the full packed
+        banks."""
+        self.banks = (gateup, down)
+        self.place(lists or self.lists)
+
+    def place(self, lists: list[list[int]]) -> None:
+        if len(lists) != self.world or any(len(l) != self.nl for l in lists):
+            raise ValueError("a placement lists n_expert / world experts for every rank")
+        self.lists = [list(l) for l in lists]
+        self.pos = positions(self.lists)
+        self.pf.set_order(self.pos)
+        self.pf.load_list(self.banks[0], self.banks[1], self.lists[self.rank])
+
+    def rebalance(self) -> list[list[int]]:
+        """Re-place the experts by the popularity the last forward saw (summed over all ranks;
+        every rank computes the same placement)."""
+        counts = self.last["counts_all"].sum(axis=0)[self.pos]  # by expert
+        lists = balanced(counts, self.world)
+        self.place(lists)
+        return lists
 
     def forward(self, x_bf16, n_tokens: int, router_w, out_ptr: int, router_b=None, residual_ptr=None) -> dict:
         torch, dist = self.torch, self.dist
@@ -106,5 +159,6 @@ class ExpertParallelPrefill:
         dist.all_to_all_single(yb, y, output_split_sizes=pl["send"], input_split_sizes=pl["recv"], group=self.group)
         torch.cuda.synchronize()
         self.pf.combine(yb.data_ptr(), T, out_ptr, residual_ptr)
+        pl["counts_all"] = counts_all
         self.last = pl
         return pl

@@ -140,7 +140,16 @@ def _prefill_split_methods():
     def buffer_ptr(self, which: int) -> int:
         return self.ctx.lib.moearc_x_prefill_buffer(self.h, which)
 
-    for f in (load_range, route, experts, combine, buffer_ptr):
+    def load_list(self, gateup: DeviceBuffer, down: DeviceBuffer, experts) -> None:
+        ids = np.ascontiguousarray(experts, np.int32)
+        self.ctx._finish(self.ctx.lib.moearc_x_prefill_load_list(self.h, gateup.ptr, down.ptr, ids.ctypes.data,
+                                                                 len(ids)), "prefill_load_list")
+
+    def set_order(self, pos) -> None:
+        pos = np.ascontiguousarray(pos, np.int32)
+        self.ctx._finish(self.ctx.lib.moearc_x_prefill_set_order(self.h, pos.ctypes.data), "prefill_set_order")
+
+    for f in (load_range, route, experts, combine, buffer_ptr, load_list, set_order):
         setattr(MoePrefill, f.__name__, f)
 
 

@@ -8,7 +8,7 @@ import os
 import numpy as np
 import pytest
 
-from moearc_b200.ep import plan
+from moearc_b200.ep import balanced, interleaved, plan, positions
 
 
 def test_plans_agree_pairwise():
@@ -27,6 +27,23 @@ def test_plans_agree_pairwise():
             # segments: source-major, each source's block in expert order
             nl = E // world
             assert np.array_equal(plans[a]["seg_expert"], np.tile(np.arange(nl), world))
+
+
+def test_placements_are_owner_major_permutations():
+    rng = np.random.default_rng(5)
+    for world in (2, 4, 8):
+        E = 16 * world
+        counts = np.floor(1e4 * (1.0 + np.arange(E)) ** -1.1).astype(int)[rng.permutation(E)]
+        for lists in (interleaved(E, world), balanced(counts, world)):
+            assert sorted(e for l in lists for e in l) == list(range(E))
+            assert all(len(l) == E // world for l in lists)
+            pos = positions(lists)
+            assert sorted(pos) == list(range(E))
+            for r, l in enumerate(lists):
+                assert all(r * (E // world) <= pos[e] < (r + 1) * (E // world) for e in l)
+        # balanced is no worse than interleaved on a Zipf-like load
+        load = lambda lists: max(sum(counts[e] for e in l) for l in lists)
+        assert load(balanced(counts, world)) <= load(interleaved(E, world))
 
 
 def test_plan_rejects_uneven_split():

@@ -157,15 +157,15 @@ def test_skewed_routing_many_tokens_against_torch(ctx):
     packer.close()
 
 
-@pytest.mark.parametrize("world", [2, 4])
-def test_expert_parallel_split_gives_the_same_bits(ctx, world):
+@pytest.mark.parametrize("world,placement", [(2, "contiguous"), (4, "interleaved"), (4, "balanced")])
+def test_expert_parallel_split_gives_the_same_bits(ctx, world, placement):
     """Expert parallelism emulated on one GPU: each virtual rank routes its own tokens, owns a
     contiguous expert range (moearc_x_prefill_load_range), receives the rows of its experts from
     every rank as (source, expert) segments and returns the result rows; the combine on each rank
     then gives the single-GPU block's output bit for bit (a row's arithmetic does not depend on
     where its segment sits)."""
     torch = pytest.importorskip("torch")
-    from moearc_b200.ep import plan
+    from moearc_b200.ep import balanced, interleaved, plan, positions
 
     H, I, E, k, T = 1024, 512, 32, 4, 600
     whole, packer, host = build(ctx, H, I, E, k, 2, 1, O.MXFP4, T, 0x9F41)
@@ -176,10 +176,21 @@ def test_expert_parallel_split_gives_the_same_bits(ctx, world):
     want = ctx.download(ref, np.float32, T * H).reshape(T, H)
     Tr = T // world
     nl = E // world
+    if placement == "contiguous":
+        lists = [list(range(r * nl, (r + 1) * nl)) for r in range(world)]
+    elif placement == "interleaved":
+        lists = interleaved(E, world)
+    else:
+        lists = balanced(whole.buffer(3, np.int32, E), world)  # the whole batch's popularity
+    pos = positions(lists)
     ranks = []
     for r in range(world):
         pf = MoePrefill(ctx, H, I, E, k, 2, 1, O.MXFP4, max_tokens=Tr)
-        pf.load_range(packer.gateup, packer.down, r * nl, nl)
+        pf.set_order(pos)
+        if placement == "contiguous":
+            pf.load_range(packer.gateup, packer.down, r * nl, nl)
+        else:
+            pf.load_list(packer.gateup, packer.down, lists[r])
         x = ctx.upload_new(xb[r * Tr * H:(r + 1) * Tr * H])
         pf.route(x, Tr, rw)
         ranks.append((pf, x, pf.buffer(3, np.int32, E)))
