@@ -305,6 +305,27 @@ void *moearc_x_decoder_tensor(moearc_x_decoder *d, int which, unsigned int layer
 unsigned long long moearc_x_decoder_seed(moearc_x_decoder *d, int kind, unsigned int layer,
                                          unsigned long long base);
 
+/* ---- batched decoder (batch.cu; no counterpart in the reference, whose engine decodes one
+ * sequence) ---------------------------------------------------------------------------------
+ * n_batch independent sequences, one token each per step, through the decoder of cfg (same
+ * weights as moearc_x_decoder_create would generate from it): bf16 activations into tcgen05
+ * GEMMs for Q/K/V and O, RoPE and paged bf16 KV per sequence, one batched decode-attention launch,
+ * and the prefill MoE block, with the experts expanded to bf16 once at create and the router on
+ * the f32 activations. Requires n_swa == 0, no sinks, n_offload == 0; NULL otherwise. */
+typedef struct moearc_x_batch_decoder moearc_x_batch_decoder;
+moearc_x_batch_decoder *moearc_x_batch_decoder_create(moearc_ctx *c, const moearc_x_decoder_cfg *cfg,
+                                                      unsigned int n_batch);
+void moearc_x_batch_decoder_destroy(moearc_x_batch_decoder *d);
+void *moearc_x_batch_decoder_input(moearc_x_batch_decoder *d);   /* device, n_batch x n_embd f32 */
+void *moearc_x_batch_decoder_output(moearc_x_batch_decoder *d);  /* device, n_batch x n_embd f32 */
+/* Every sequence at position pos; with fill, every KV page first gets synthetic bf16 N(0, 0.02). */
+int moearc_x_batch_decoder_set_pos(moearc_x_batch_decoder *d, unsigned int pos, int fill,
+                                   unsigned long long seed);
+/* One token for every sequence; the first call captures the step as a CUDA graph. */
+int moearc_x_batch_decoder_step(moearc_x_batch_decoder *d);
+/* Reads and clears the status words: 0, or nonzero when a bounded wait gave up. */
+int moearc_x_batch_decoder_status(moearc_x_batch_decoder *d);
+
 /* ---- decode attention without allocation (no counterpart in the reference) ----------------
  * Same arguments, result and return codes as moearc_attn_decode, but the split-K partials live
  * in a fixed per-device array of MOEARC_X_ATTN_STATIC_SCRATCH_BYTES compiled into the library,

@@ -85,6 +85,13 @@ SIGNATURES: dict[str, tuple] = {
     "moearc_x_prefill_experts": (I, [P, P, U, P, P, U, P, P]),
     "moearc_x_prefill_combine": (I, [P, P, U, P, P]),
     "moearc_x_prefill_load_list": (I, [P, P, P, P, U]),
+    "moearc_x_batch_decoder_create": (P, [P, P, U]),
+    "moearc_x_batch_decoder_destroy": (None, [P]),
+    "moearc_x_batch_decoder_input": (P, [P]),
+    "moearc_x_batch_decoder_output": (P, [P]),
+    "moearc_x_batch_decoder_set_pos": (I, [P, U, I, C.c_ulonglong]),
+    "moearc_x_batch_decoder_step": (I, [P]),
+    "moearc_x_batch_decoder_status": (I, [P]),
     "moearc_x_prefill_set_order": (I, [P, P]),
     "moearc_x_decoder_create": (P, [P, P]),
     "moearc_x_decoder_destroy": (None, [P]),

@@ -324,10 +324,22 @@ __global__ void __launch_bounds__(128)
     k_attn_mma(float *part_ml, float *part_acc, float *out, const float *q, const uint16_t *kp,
                const uint16_t *vp, const unsigned *table, const float *sinks, int n_heads,
                int n_kv_heads, int group, size_t kv_begin, size_t n_kv, size_t pt, float scale,
-               size_t kps, int n_splits, const int *dpos, int window, unsigned *ctr) {
+               size_t kps, int n_splits, const int *dpos, int window, unsigned *ctr, size_t bs_tab) {
     extern __shared__ __align__(16) uint16_t smem[];
     constexpr int CH = D / 8;  // 16-byte chunks per row
     const int kvh = blockIdx.x, split = blockIdx.y;
+    if (gridDim.z > 1) {
+        // sequence blockIdx.z of a batch: its own query and output rows, page table, position,
+        // split partials and merge counters; the page pool and the sinks are shared
+        const size_t bz = blockIdx.z;
+        q += bz * n_heads * D;
+        out += bz * n_heads * D;
+        table += bz * bs_tab;
+        if (dpos) dpos += bz;
+        part_ml += bz * n_heads * gridDim.y * 2;
+        part_acc += bz * n_heads * gridDim.y * D;
+        if (ctr) ctr += bz * n_kv_heads;
+    }
     const int trace_row = (int)(blockIdx.y * gridDim.x + blockIdx.x);
     (void)trace_row;
     TRACE(0);
@@ -571,19 +583,19 @@ int attn_launch(moearc_ctx *c, float *out, const float *q, const void *kp, const
             constexpr size_t sm = 4 * warp_smem_elems<64>() * 2;
             if (kv_type == T_BF16) {
                 set_mma_smem<64, true>();
-                err = launch_pdl(k_attn_mma<64, true>, grid, dim3(128), sm, c->stream, ml, acc, out, q, k16, v16, table, sinks, (int)n_heads, (int)n_kv_heads, group, kv_begin, n_kv, pt, scale, kps, n_splits, dpos, window, ctr);
+                err = launch_pdl(k_attn_mma<64, true>, grid, dim3(128), sm, c->stream, ml, acc, out, q, k16, v16, table, sinks, (int)n_heads, (int)n_kv_heads, group, kv_begin, n_kv, pt, scale, kps, n_splits, dpos, window, ctr, (size_t)0);
             } else {
                 set_mma_smem<64, false>();
-                err = launch_pdl(k_attn_mma<64, false>, grid, dim3(128), sm, c->stream, ml, acc, out, q, k16, v16, table, sinks, (int)n_heads, (int)n_kv_heads, group, kv_begin, n_kv, pt, scale, kps, n_splits, dpos, window, ctr);
+                err = launch_pdl(k_attn_mma<64, false>, grid, dim3(128), sm, c->stream, ml, acc, out, q, k16, v16, table, sinks, (int)n_heads, (int)n_kv_heads, group, kv_begin, n_kv, pt, scale, kps, n_splits, dpos, window, ctr, (size_t)0);
             }
         } else {
             constexpr size_t sm = 4 * warp_smem_elems<128>() * 2;
             if (kv_type == T_BF16) {
                 set_mma_smem<128, true>();
-                err = launch_pdl(k_attn_mma<128, true>, grid, dim3(128), sm, c->stream, ml, acc, out, q, k16, v16, table, sinks, (int)n_heads, (int)n_kv_heads, group, kv_begin, n_kv, pt, scale, kps, n_splits, dpos, window, ctr);
+                err = launch_pdl(k_attn_mma<128, true>, grid, dim3(128), sm, c->stream, ml, acc, out, q, k16, v16, table, sinks, (int)n_heads, (int)n_kv_heads, group, kv_begin, n_kv, pt, scale, kps, n_splits, dpos, window, ctr, (size_t)0);
             } else {
                 set_mma_smem<128, false>();
-                err = launch_pdl(k_attn_mma<128, false>, grid, dim3(128), sm, c->stream, ml, acc, out, q, k16, v16, table, sinks, (int)n_heads, (int)n_kv_heads, group, kv_begin, n_kv, pt, scale, kps, n_splits, dpos, window, ctr);
+                err = launch_pdl(k_attn_mma<128, false>, grid, dim3(128), sm, c->stream, ml, acc, out, q, k16, v16, table, sinks, (int)n_heads, (int)n_kv_heads, group, kv_begin, n_kv, pt, scale, kps, n_splits, dpos, window, ctr, (size_t)0);
             }
         }
     } else {
@@ -607,6 +619,40 @@ int attn_launch(moearc_ctx *c, float *out, const float *q, const void *kp, const
         k_attn_combine<<<(unsigned)n_heads, 128, 0, c->stream>>>(out, ml, acc, sinks, (int)hd, n_splits, dpos,
                                                                 window, n_splits);
     return OK;
+}
+
+// n_batch sequences at once (bf16 KV, head_dim 64 or 128, tensor-core kernel): sequence b reads
+// q + b n_heads hd, writes out + b n_heads hd, pages through table + b table_stride, attends over
+// [window-limited start, dpos[b]]; scratch holds n_batch x n_heads x max_splits x (hd + 2) floats,
+// ctr n_batch x n_kv_heads zeroed counters (the last split of a head group merges and re-zeroes).
+int attn_launch_batched(moearc_ctx *c, float *out, const float *q, const void *kp, const void *vp,
+                        const unsigned *table, size_t table_stride, const float *sinks, size_t n_heads,
+                        size_t n_kv_heads, size_t hd, size_t n_ctx, size_t pt, float scale, float *scratch,
+                        size_t scratch_bytes, const int *dpos, int window, int max_splits, unsigned *ctr,
+                        int n_batch) {
+    if (!attn_mma_ok(n_heads, n_kv_heads, hd, T_BF16, kp, vp) || !dpos || !ctr || n_batch < 1 || max_splits < 1)
+        return ERR_ARG;
+    if (scratch_bytes < (size_t)n_batch * attn_scratch_bytes(n_heads, hd, max_splits)) return ERR_ARG;
+    const int group = (int)(n_heads / n_kv_heads);
+    float *ml = scratch, *acc = scratch + (size_t)n_batch * n_heads * max_splits * 2;
+    const dim3 grid((unsigned)n_kv_heads, (unsigned)max_splits, (unsigned)n_batch);
+    const auto *k16 = static_cast<const uint16_t *>(kp);
+    const auto *v16 = static_cast<const uint16_t *>(vp);
+    cudaError_t err;
+    if (hd == 64) {
+        constexpr size_t sm = 4 * warp_smem_elems<64>() * 2;
+        set_mma_smem<64, true>();
+        err = launch_pdl(k_attn_mma<64, true>, grid, dim3(128), sm, c->stream, ml, acc, out, q, k16, v16, table, sinks,
+                         (int)n_heads, (int)n_kv_heads, group, (size_t)0, n_ctx, pt, scale, (size_t)0, max_splits, dpos,
+                         window, ctr, table_stride);
+    } else {
+        constexpr size_t sm = 4 * warp_smem_elems<128>() * 2;
+        set_mma_smem<128, true>();
+        err = launch_pdl(k_attn_mma<128, true>, grid, dim3(128), sm, c->stream, ml, acc, out, q, k16, v16, table, sinks,
+                         (int)n_heads, (int)n_kv_heads, group, (size_t)0, n_ctx, pt, scale, (size_t)0, max_splits, dpos,
+                         window, ctr, table_stride);
+    }
+    return err == cudaSuccess ? OK : ERR;
 }
 
 }  // namespace moearc

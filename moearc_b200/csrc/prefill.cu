@@ -53,6 +53,7 @@ __device__ __forceinline__ uint16_t f32_to_bf16_rn(float f) {
 
 struct pf_route_args {
     const uint16_t *x;  // [T][H] bf16
+    const float *x32;   // [T][H] f32 the logits are taken from instead of x (null: x)
     const float *router, *rbias;
     int T, H, E, K, gating;
     float *logits;      // [T][E]
@@ -72,10 +73,14 @@ __global__ void __launch_bounds__(256) k_pf_logits(pf_route_args a) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int t0 = blockIdx.x * PF_LOGIT_TOK, nt = min(PF_LOGIT_TOK, a.T - t0);
     const int H = a.H, n4 = H / 4;
-    for (int i = threadIdx.x; i < nt * H / 2; i += blockDim.x) {
-        const uint32_t v = reinterpret_cast<const uint32_t *>(a.x + (size_t)t0 * H)[i];
-        xs[2 * i] = __uint_as_float(v << 16);
-        xs[2 * i + 1] = __uint_as_float(v & 0xFFFF0000u);
+    if (a.x32) {
+        for (int i = threadIdx.x; i < nt * H; i += blockDim.x) xs[i] = a.x32[(size_t)t0 * H + i];
+    } else {
+        for (int i = threadIdx.x; i < nt * H / 2; i += blockDim.x) {
+            const uint32_t v = reinterpret_cast<const uint32_t *>(a.x + (size_t)t0 * H)[i];
+            xs[2 * i] = __uint_as_float(v << 16);
+            xs[2 * i + 1] = __uint_as_float(v & 0xFFFF0000u);
+        }
     }
     __syncthreads();
     const int nwarps = blockDim.x >> 5;
@@ -471,6 +476,36 @@ bool make_map(CUtensorMap *map, const void *base, long rows, int cols) {
 
 }  // namespace
 
+namespace moearc {
+
+// For other translation units (the batched decoder): the 128 x 64 bf16 K-major tensor map, and a
+// dense GEMM on the same kernel, out[n][m] = sum_k W[m][k] x[n][k] (f32), as one segment of
+// n rows: seg_off = {0, n} and seg_toff = {0, ceil(n / 128)} in device memory.
+bool tc_make_map_bf16(CUtensorMap *map, const void *base, long rows, int cols) { return make_map(map, base, rows, cols); }
+
+int tc_dense_gemm(moearc_ctx *c, const CUtensorMap &w, int M, int K, const CUtensorMap &x, const int *seg_off,
+                  const int *seg_toff, float *out, int *status) {
+    static bool ready = false;
+    if (!ready) {
+        if (set_smem(k_pf_gemm<1>, pf_cfg<1>::SMEM) != cudaSuccess) return ERR;
+        ready = true;
+    }
+    if (K % PF_BK) return ERR_ARG;
+    pf_gemm_args g{};
+    g.Mrows = M;
+    g.K = K;
+    g.E = 1;
+    g.off = seg_off;
+    g.toff = seg_toff;
+    g.y_out = out;
+    g.status = status;
+    const int grid = std::min(c->sm_count, (M + PF_BM - 1) / PF_BM * 8);  // tiles are few: n is small
+    k_pf_gemm<1><<<grid, 192, pf_cfg<1>::SMEM, c->stream>>>(w, x, g);
+    return cudaGetLastError() == cudaSuccess ? OK : ERR;
+}
+
+}  // namespace moearc
+
 struct moearc_x_prefill {
     moearc_ctx *c;
     int H, I, E, K, wtype, gating, act;
@@ -656,7 +691,8 @@ namespace {
 // The forward sequence; with `ev`, an event is recorded before the first kernel and after each
 // of the 7 kernels (routing, top-k, scan, scatter, gate-up GEMM, down GEMM, combine).
 int prefill_forward(moearc_x_prefill *p, const uint16_t *x, unsigned n_tokens, const float *router_w,
-                    const float *router_b, const float *residual, float *out, cudaEvent_t *ev) {
+                    const float *router_b, const float *residual, float *out, cudaEvent_t *ev,
+                    const float *x32 = nullptr) {
     if (!p || !x || !router_w || !out) return ERR;
     if (n_tokens == 0) return OK;
     if ((int)n_tokens > p->T_max || !p->order_identity) return ERR_ARG;
@@ -670,7 +706,7 @@ int prefill_forward(moearc_x_prefill *p, const uint16_t *x, unsigned n_tokens, c
     };
     if (cudaMemsetAsync(p->cnt, 0, sizeof(int) * (p->E + 1), st) != cudaSuccess) return ERR;
     mark(0);
-    pf_route_args ra{x, router_w, router_b, T, p->H, p->E, p->K, p->gating, p->logits, p->idx, p->wts, p->cnt, p->epos};
+    pf_route_args ra{x, x32, router_w, router_b, T, p->H, p->E, p->K, p->gating, p->logits, p->idx, p->wts, p->cnt, p->epos};
     k_pf_logits<<<(T + PF_LOGIT_TOK - 1) / PF_LOGIT_TOK, 256, PF_LOGIT_TOK * p->H * 4, st>>>(ra);
     mark(1);
     k_pf_topk<<<(T + 7) / 8, 256, 0, st>>>(ra);
@@ -707,6 +743,15 @@ int prefill_forward(moearc_x_prefill *p, const uint16_t *x, unsigned n_tokens, c
 
 }  // namespace
 
+namespace moearc {
+// moearc_x_prefill_forward with the router logits taken from x32 (f32 [T][H]) instead of the bf16
+// activations: for a caller whose decode path routes on f32 activations.
+int prefill_forward_x32(moearc_x_prefill *p, const uint16_t *x, const float *x32, unsigned n_tokens,
+                        const float *router_w, const float *router_b, const float *residual, float *out) {
+    return prefill_forward(p, x, n_tokens, router_w, router_b, residual, out, nullptr, x32);
+}
+}  // namespace moearc
+
 extern "C" {
 
 int moearc_x_prefill_forward(moearc_x_prefill *p, const uint16_t *x, unsigned n_tokens, const float *router_w,
@@ -737,6 +782,7 @@ int moearc_x_prefill_profile(moearc_x_prefill *p, const uint16_t *x, unsigned n_
 // expert range travel to the rank that owns it before moearc_x_prefill_experts.
 int moearc_x_prefill_route(moearc_x_prefill *p, const uint16_t *x, unsigned n_tokens, const float *router_w,
                            const float *router_b) {
+    const float *x32 = nullptr;
     if (!p || !x || !router_w) return ERR;
     if (n_tokens == 0) return OK;
     if ((int)n_tokens > p->T_max) return ERR_ARG;
@@ -744,7 +790,7 @@ int moearc_x_prefill_route(moearc_x_prefill *p, const uint16_t *x, unsigned n_to
     cudaStream_t st = p->c->stream;
     const int T = (int)n_tokens;
     if (cudaMemsetAsync(p->cnt, 0, sizeof(int) * (p->E + 1), st) != cudaSuccess) return ERR;
-    pf_route_args ra{x, router_w, router_b, T, p->H, p->E, p->K, p->gating, p->logits, p->idx, p->wts, p->cnt, p->epos};
+    pf_route_args ra{x, x32, router_w, router_b, T, p->H, p->E, p->K, p->gating, p->logits, p->idx, p->wts, p->cnt, p->epos};
     k_pf_logits<<<(T + PF_LOGIT_TOK - 1) / PF_LOGIT_TOK, 256, PF_LOGIT_TOK * p->H * 4, st>>>(ra);
     k_pf_topk<<<(T + 7) / 8, 256, 0, st>>>(ra);
     k_pf_scan<<<1, 1024, 0, st>>>(p->cnt, p->E, p->off, p->toff, p->cursor);

@@ -149,6 +149,47 @@ class Decoder:
         return self.ctx.lib.moearc_x_decoder_seed(self.h, kind, layer, self.cfg.seed)
 
 
+class BatchDecoder:
+    """n_batch independent sequences decoding one token each per step (moearc_x_batch_decoder_*):
+    the batched serving case (configs[4]: 64 streams of a Qwen3-MoE-shaped model)."""
+
+    def __init__(self, ctx: Context, cfg: DecoderConfig, n_batch: int):
+        self.ctx, self.cfg, self.n_batch = ctx, cfg, n_batch
+        self._c = cfg.to_c()
+        self.h = ctx.lib.moearc_x_batch_decoder_create(ctx.raw, C.byref(self._c), n_batch)
+        if not self.h:
+            raise BadArgument("moearc_x_batch_decoder_create refused the configuration or ran out of memory")
+        self.in_ptr = ctx.lib.moearc_x_batch_decoder_input(self.h)
+        self.out_ptr = ctx.lib.moearc_x_batch_decoder_output(self.h)
+
+    def close(self) -> None:
+        if self.h:
+            self.ctx.lib.moearc_x_batch_decoder_destroy(self.h)
+            self.h = None
+
+    def set_pos(self, pos: int, fill: bool = False, seed: int = 0xC0DE) -> None:
+        self.ctx._finish(self.ctx.lib.moearc_x_batch_decoder_set_pos(self.h, pos, 1 if fill else 0, seed), "set_pos")
+
+    def step(self) -> None:
+        self.ctx._finish(self.ctx.lib.moearc_x_batch_decoder_step(self.h), "batch decoder step")
+
+    def set_input(self, x: np.ndarray) -> None:
+        x = np.ascontiguousarray(x, np.float32)
+        assert x.size == self.n_batch * self.cfg.n_embd
+        self.ctx._finish(self.ctx.lib.moearc_copy_h2d(self.ctx.raw, self.in_ptr, x.ctypes.data, x.nbytes), "input")
+
+    def output(self) -> np.ndarray:
+        out = np.empty((self.n_batch, self.cfg.n_embd), np.float32)
+        self.ctx._finish(self.ctx.lib.moearc_copy_d2h(self.ctx.raw, out.ctypes.data, self.out_ptr, out.nbytes), "output")
+        return out
+
+    def status(self) -> int:
+        st = self.ctx.lib.moearc_x_batch_decoder_status(self.h)
+        if st < 0:
+            raise Failed("reading the batch decoder status")
+        return st
+
+
 def unpack_dense(packed: np.ndarray, n_rows: int, n_cols: int) -> np.ndarray:
     """Invert the packed bf16 tile layout (dense.cuh) back to a row-major [n_rows][n_cols] bf16
     matrix: tile (tr, tk) = 16 rows x 64 cols; inside it, for each 16-column sub-block s, lane

@@ -140,3 +140,41 @@ def test_expert_offload_matches_the_resident_decoder(ctx, etype, n_expert, k):
         assert np.array_equal(a.view(np.uint32), b.view(np.uint32)), f"token {pos}"
     off.close()
     res.close()
+
+
+@pytest.mark.parametrize("etype", [O.MXFP4, O.Q4_0])
+def test_batch_decoder_matches_single_stream_decoders(ctx, etype):
+    """Three sequences decoded together (moearc_x_batch_decoder: tcgen05 GEMMs for the
+    projections and the experts on bf16 activations, one batched attention launch) against three
+    single-stream decoders of the same configuration (the same weights, checked against the
+    oracle above) fed the same tokens: every sequence's output agrees within the reference's
+    bf16-activation bound, max |a - b| <= 3e-2 max |b| (bf16 rounding of the activations into
+    each projection and expert, over two blocks), and the routing agrees exactly (the router
+    sees the f32 activations in both)."""
+    from moearc_b200.decoder import BatchDecoder
+
+    kw = dict(n_layer=2, n_embd=256, n_head=8, n_head_kv=2, head_dim=64, n_expert=8, n_expert_used=2, n_ff=128,
+              expert_type=etype, n_swa=0, has_sinks=0, n_ctx=96, seed=0xBA7C)
+    B = 3
+    bd = BatchDecoder(ctx, DecoderConfig(**kw), B)
+    bd.set_pos(0)
+    singles = [Decoder(ctx, DecoderConfig(**kw)) for _ in range(B)]
+    for d in singles:
+        d.set_pos(0)
+    worst = 0.0
+    for pos in range(40):  # past a page boundary
+        x = np.stack([O.synth_normal_f32(0x3000 + 97 * b + pos, kw["n_embd"], 1.0) for b in range(B)])
+        bd.set_input(x)
+        bd.step()
+        got = bd.output()
+        for b, d in enumerate(singles):
+            d.set_input(x[b])
+            d.step()
+            want = d.output().astype(np.float64)
+            worst = max(worst, float(np.max(np.abs(got[b] - want)) / np.max(np.abs(want))))
+    assert bd.status() == 0
+    print(f"batch decoder etype={etype}: 3 streams x 40 tokens, max |a-b| / max|b| = {worst:.3e}")
+    assert worst <= 3e-2
+    for d in singles:
+        d.close()
+    bd.close()
