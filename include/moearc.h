@@ -224,6 +224,13 @@ int moearc_x_prefill_load_range(moearc_x_prefill *p, const void *gateup_packed, 
  * rank owns under a placement other than contiguous ranges. */
 int moearc_x_prefill_load_list(moearc_x_prefill *p, const void *gateup_packed, const void *down_packed,
                                const int *experts, unsigned int n);
+/* The 4-bit form of the same experts (all, or experts[i] -> slot i): the packed banks are
+ * repacked into chunks of 128 rows x 64 columns that one bulk copy moves, and the GEMMs expand
+ * them to bf16 in shared memory as they go (the same values as the bf16 expansion, so the same
+ * results bit for bit, with a quarter of the weight bytes). The last load picks the form. */
+int moearc_x_prefill_load4(moearc_x_prefill *p, const void *gateup_packed, const void *down_packed);
+int moearc_x_prefill_load4_list(moearc_x_prefill *p, const void *gateup_packed, const void *down_packed,
+                                const int *experts, unsigned int n);
 /* Row order of the route step: expert e's rows form segment pos[e] (host array, a permutation of
  * 0 .. E-1); buffers 3 and 10 are then indexed by position. Identity at create, which
  * moearc_x_prefill_forward requires (-2 otherwise). Under expert parallelism the positions are

@@ -93,6 +93,8 @@ SIGNATURES: dict[str, tuple] = {
     "moearc_x_batch_decoder_step": (I, [P]),
     "moearc_x_batch_decoder_status": (I, [P]),
     "moearc_x_prefill_set_order": (I, [P, P]),
+    "moearc_x_prefill_load4": (I, [P, P, P]),
+    "moearc_x_prefill_load4_list": (I, [P, P, P, P, U]),
     "moearc_x_decoder_create": (P, [P, P]),
     "moearc_x_decoder_destroy": (None, [P]),
     "moearc_x_decoder_input": (P, [P]),

@@ -34,6 +34,7 @@
 #include "common.cuh"
 #include "route.cuh"
 #include "tc.cuh"
+#include "tma.cuh"
 
 using namespace moearc;
 
@@ -441,6 +442,300 @@ __global__ void __launch_bounds__(192, 1) k_pf_gemm(const __grid_constant__ CUte
     }
 }
 
+// ---- 4-bit expert weights on the tensor cores ---------------------------------------------------
+//
+// "tc4" layout of one weight matrix [R][K] (R rounded up to 128): chunks of 128 rows x 64 columns,
+// chunk (rb, kb) at index rb * (K / 64) + kb, each one contiguous run: 128 rows of 32 bytes (byte j
+// holds column 2j in its low nibble and 2j + 1 in its high nibble), then the rows' two block
+// scales (MXFP4: one e8m0 byte per 32 columns; Q4_0: one f16 delta). Rows past R are zeros. A
+// chunk is one bulk copy; decoder warps turn it into the bf16 operand tile the MMA reads, with
+// the values the bf16 expansion (k_pf_unpack) would hold, so both paths give the same bits.
+
+constexpr int TC4_NIB = 128 * 32;  // nibble bytes of a chunk
+
+template <int WT>
+constexpr int tc4_sb() { return WT == 39 ? 1 : 2; }
+template <int WT>
+constexpr int tc4_chunk() { return TC4_NIB + 128 * 2 * tc4_sb<WT>(); }  // 4352 (MXFP4) or 4608 (Q4_0)
+
+// One thread per (chunk, row): the row's 64 nibbles and 2 scales gathered from the packed tiles
+// (moearc_x_moe_pack layout; mats = 2: gate-up pairs, 1: down tiles) of experts[i] -> slot i.
+template <int WT>
+__global__ void k_pf_pack4(const uint8_t *bank, const int *experts, int n_exp, int R, int K, int mats,
+                           int tile_bytes, uint8_t *dst) {
+    constexpr int sb = tc4_sb<WT>();
+    const int RB = (R + 127) / 128, KB = K / 64;
+    const long per_mat = (long)RB * KB;
+    const long gid = blockIdx.x * (long)blockDim.x + threadIdx.x;
+    if (gid >= (long)n_exp * mats * per_mat * 128) return;
+    const int row = (int)(gid & 127);
+    const long chunk = gid >> 7;
+    const long em = chunk / per_mat;
+    const int slot = (int)(em / mats), mat = (int)(em - (long)slot * mats);
+    const long rk = chunk - em * per_mat;
+    const int rb = (int)(rk / KB), kb = (int)(rk - (long)rb * KB);
+    uint8_t *out = dst + (size_t)chunk * tc4_chunk<WT>();
+    const int grow = rb * 128 + row;
+    uint32_t nib[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    uint8_t sc[2 * sb];
+    if (grow >= R) {
+        for (int i = 0; i < 8; ++i) nib[i] = WT == 39 ? 0u : 0x88888888u;
+        for (int i = 0; i < 2 * sb; ++i) sc[i] = 0;
+    } else {
+        const int e = experts ? experts[slot] : slot;
+        const long ntr = R / 16, nkt = K / 64;
+        const int tr = grow >> 4, lr = grow & 15, r = lr & 7, half = lr >> 3;
+        const uint8_t *tile = bank + (((size_t)e * ntr * nkt + (size_t)tr * nkt + kb) * mats + mat) * tile_bytes;
+        for (int k = 0; k < 64; ++k) {
+            const int b = k >> 5, kk = k & 31, j = kk & 15;
+            const uint8_t byte = tile[(4 * r + (j >> 2)) * 16 + (half + 2 * b) * 4 + (j & 3)];
+            const uint32_t v = (kk >= 16) ? (byte >> 4) : (byte & 15u);
+            nib[k >> 3] |= v << (4 * (k & 7));
+        }
+        for (int b = 0; b < 2; ++b)
+            for (int i = 0; i < sb; ++i) sc[b * sb + i] = tile[512 + r * 4 * sb + (half + 2 * b) * sb + i];
+    }
+    uint4 *o = reinterpret_cast<uint4 *>(out + row * 32);
+    o[0] = make_uint4(nib[0], nib[1], nib[2], nib[3]);
+    o[1] = make_uint4(nib[4], nib[5], nib[6], nib[7]);
+    for (int i = 0; i < 2 * sb; ++i) out[TC4_NIB + row * 2 * sb + i] = sc[i];
+}
+
+struct pf_gemm4_args {
+    pf_gemm_args g;
+    const uint8_t *w4;  // the matrix set's chunks: [slot][mat][rb][kb]
+    int RB, KB;         // row blocks and 64-column blocks of one matrix
+};
+
+template <int MODE, int WT>
+struct pf4_cfg {
+    static constexpr int NA = MODE == 0 ? 2 : 1;
+    static constexpr int CB = tc4_chunk<WT>();
+    static constexpr int STAGE_RAW = ((NA * CB + 1023) / 1024) * 1024;
+    static constexpr int STAGE = (NA + 1) * PF_TILE_BYTES + STAGE_RAW;  // bf16 A tiles, B tile, 4-bit chunks
+    static constexpr int STAGES = MODE == 0 ? 3 : 5;
+    static constexpr int SMEM = STAGES * STAGE + 1024;
+    static constexpr int ACC_COLS = NA * PF_BN;
+    static constexpr int TMEM_COLS = 2 * ACC_COLS;
+    static constexpr int DEC_WARPS = 8;
+    static constexpr int THREADS = (6 + DEC_WARPS) * 32;
+};
+
+// Decode one thread's half row (32 columns: one scale block) of a staged chunk into the bf16 A
+// tile in the 128-byte swizzle layout (row `row`, 16-byte unit u at (u ^ (row & 7)) * 16).
+template <int WT>
+__device__ __forceinline__ void tc4_decode_half(const uint8_t *chunk, uint8_t *tile, int row, int half) {
+    constexpr int sb = tc4_sb<WT>();
+    const uint4 w = *reinterpret_cast<const uint4 *>(chunk + row * 32 + half * 16);
+    float s;
+    if constexpr (WT == 39) {
+        s = __uint_as_float((uint32_t)chunk[TC4_NIB + row * 2 + half] << 23);
+    } else {
+        s = f16_bits_to_f32(*reinterpret_cast<const uint16_t *>(chunk + TC4_NIB + row * 4 + half * 2));
+    }
+    const uint32_t words[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {  // 8 columns: bytes 4i .. 4i+3 of the half row
+        uint32_t pr[4];
+        decode4<WT>(words[i], pr);  // pr[j]: (column 2j, 2j + 1) of these 8, true values
+        uint32_t o[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const __half2 h = *reinterpret_cast<const __half2 *>(&pr[j]);
+            o[j] = (uint32_t)f32_to_bf16_rn(__low2float(h) * s) | ((uint32_t)f32_to_bf16_rn(__high2float(h) * s) << 16);
+        }
+        const int u = half * 4 + i;
+        *reinterpret_cast<uint4 *>(tile + row * 128 + ((u ^ (row & 7)) * 16)) = make_uint4(o[0], o[1], o[2], o[3]);
+    }
+}
+
+// As k_pf_gemm, with the A operand (expert weights) staged as 4-bit chunks by bulk copies and
+// expanded to bf16 tiles in shared memory by DEC_WARPS decoder warps (warps 6 ..): per stage the
+// producer's copies complete on full[s]; the decoders wait for it, write the tiles, fence them to
+// the async proxy and arrive on dec[s] (one arrival per decoder warp); the MMA issuer waits for
+// both.
+template <int MODE, int WT>
+__global__ void __launch_bounds__(pf4_cfg<MODE, WT>::THREADS, 1)
+    k_pf_gemm4(const __grid_constant__ CUtensorMap xmap, pf_gemm4_args a4) {
+    using C = pf4_cfg<MODE, WT>;
+    const pf_gemm_args &a = a4.g;
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+    __shared__ __align__(8) uint64_t full[C::STAGES], dec[C::STAGES], empty[C::STAGES], acc_full[2], acc_empty[2], done;
+    __shared__ uint32_t tmem_slot;
+    __shared__ volatile int abort_;
+    __shared__ int s_toff[1025];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    for (int i = threadIdx.x; i <= a.E; i += blockDim.x) s_toff[i] = a.toff[i];
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < C::STAGES; ++s) {
+            tc::bar_init(&full[s], 1);
+            tc::bar_init(&dec[s], C::DEC_WARPS);
+            tc::bar_init(&empty[s], 1);
+        }
+        for (int b = 0; b < 2; ++b) {
+            tc::bar_init(&acc_full[b], 1);
+            tc::bar_init(&acc_empty[b], 4);
+        }
+        tc::bar_init(&done, 1);
+        abort_ = 0;
+        tc::bar_init_fence();
+    }
+    if (warp == 0) tc::tmem_alloc(&tmem_slot, C::TMEM_COLS);
+    tc::fence_before_sync();
+    __syncthreads();
+    tc::fence_after_sync();
+    const uint32_t tmem = tmem_slot;
+    const int MT = (a.Mrows + PF_BM - 1) / PF_BM, KB = a.K / PF_BK;
+    const long total = (long)s_toff[a.E] * MT;
+    auto locate = [&](long tile, int &e, int &nt, int &mt) {
+        const int ntg = (int)(tile / MT);
+        mt = (int)(tile - (long)ntg * MT);
+        int lo = 0, hi = a.E;
+        while (hi - lo > 1) {
+            const int mid = (lo + hi) >> 1;
+            if (s_toff[mid] <= ntg) lo = mid;
+            else hi = mid;
+        }
+        e = lo;
+        nt = ntg - s_toff[e];
+    };
+    auto stage_a = [&](int s) { return smem + (size_t)s * C::STAGE; };                 // bf16 A tiles
+    auto stage_b = [&](int s) { return stage_a(s) + C::NA * PF_TILE_BYTES; };           // B tile
+    auto stage_raw = [&](int s) { return stage_a(s) + (C::NA + 1) * PF_TILE_BYTES; };   // 4-bit chunks
+
+    if (warp == 0) {
+        long g = 0;
+        if (lane == 0) {
+            for (long tile = blockIdx.x; tile < total && !abort_; tile += gridDim.x) {
+                int e, nt, mt;
+                locate(tile, e, nt, mt);
+                const int we = a.seg_w ? a.seg_w[e] : e;
+                const int rowB = a.off[e] + nt * PF_BN;
+                for (int kb = 0; kb < KB; ++kb, ++g) {
+                    const int s = (int)(g % C::STAGES);
+                    if (g >= C::STAGES &&
+                        !tc::bar_wait(&empty[s], (unsigned)(((g / C::STAGES) - 1) & 1), &abort_, a.status, PF_STATUS_WAIT))
+                        break;
+                    tc::bar_expect_tx(&full[s], C::NA * C::CB + PF_TILE_BYTES);
+                    for (int m = 0; m < C::NA; ++m) {
+                        const uint8_t *src = a4.w4 + ((((size_t)we * C::NA + m) * a4.RB + mt) * a4.KB + kb) * C::CB;
+                        bulk_g2s(stage_raw(s) + m * C::CB, src, (unsigned)C::CB, &full[s]);
+                    }
+                    tc::tma_load_2d(stage_b(s), &xmap, kb * PF_BK, rowB, &full[s]);
+                }
+            }
+            if (abort_)
+                for (long j = std::max(0L, g - C::STAGES); j < g; ++j)
+                    tc::bar_drain(&full[j % C::STAGES], (unsigned)((j / C::STAGES) & 1));
+        }
+        __syncwarp();
+    } else if (warp == 1) {
+        if (lane == 0) {
+            constexpr uint32_t idesc = tc::idesc_bf16_f32(PF_BM, PF_BN);
+            long g = 0, i = 0;
+            for (long tile = blockIdx.x; tile < total && !abort_; tile += gridDim.x, ++i) {
+                const int ab = (int)(i & 1);
+                const uint32_t dcol = tmem + (uint32_t)(ab * C::ACC_COLS);
+                if (i >= 2 && !tc::bar_wait(&acc_empty[ab], (unsigned)(((i >> 1) - 1) & 1), &abort_, a.status, PF_STATUS_WAIT))
+                    break;
+                tc::fence_after_sync();
+                bool ok = true;
+                for (int kb = 0; kb < KB; ++kb, ++g) {
+                    const int s = (int)(g % C::STAGES);
+                    const unsigned ph = (unsigned)((g / C::STAGES) & 1);
+                    if (!tc::bar_wait(&full[s], ph, &abort_, a.status, PF_STATUS_WAIT) ||
+                        !tc::bar_wait(&dec[s], ph, &abort_, a.status, PF_STATUS_WAIT)) {
+                        ok = false;
+                        break;
+                    }
+                    tc::fence_after_sync();
+                    const uint32_t a0 = tc::sa(stage_a(s)), b0 = tc::sa(stage_b(s));
+#pragma unroll
+                    for (int k = 0; k < PF_BK / 16; ++k) {
+                        const uint32_t acc = (kb > 0 || k > 0) ? 1u : 0u;
+                        tc::mma_bf16(dcol, tc::desc_k_sw128(a0 + k * 32), tc::desc_k_sw128(b0 + k * 32), idesc, acc);
+                        if (MODE == 0)
+                            tc::mma_bf16(dcol + PF_BN, tc::desc_k_sw128(a0 + PF_TILE_BYTES + k * 32),
+                                         tc::desc_k_sw128(b0 + k * 32), idesc, acc);
+                    }
+                    tc::mma_commit(&empty[s]);
+                }
+                if (!ok) break;
+                tc::mma_commit(&acc_full[ab]);
+            }
+            tc::mma_commit(&done);
+            tc::bar_drain(&done, 0);
+        }
+        __syncwarp();
+    } else if (warp < 6) {
+        const int qd = warp & 3;
+        const uint32_t lane_base = tmem + ((uint32_t)(32 * qd) << 16);
+        long i = 0;
+        for (long tile = blockIdx.x; tile < total; tile += gridDim.x, ++i) {
+            const int ab = (int)(i & 1);
+            if (!tc::bar_wait(&acc_full[ab], (unsigned)((i >> 1) & 1), &abort_, a.status, PF_STATUS_WAIT)) break;
+            tc::fence_after_sync();
+            int e, nt, mt;
+            locate(tile, e, nt, mt);
+            const int seg = a.off[e], n_rows = a.off[e + 1] - seg;
+            const int f = mt * PF_BM + 32 * qd + lane;
+            const bool fok = f < a.Mrows;
+            const uint32_t acc_base = lane_base + (uint32_t)(ab * C::ACC_COLS);
+            for (int c0 = 0; c0 < PF_BN; c0 += 16) {
+                float d[16];
+                tc::tmem_ld16(acc_base + c0, d);
+                if (MODE == 0) {
+                    float u[16];
+                    tc::tmem_ld16(acc_base + PF_BN + c0, u);
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) {
+                        const int n = nt * PF_BN + c0 + j;
+                        if (fok && n < n_rows)
+                            a.act_out[(size_t)(seg + n) * a.Mrows + f] = f32_to_bf16_rn(act_fn(a.act, d[j], u[j], a.alpha, a.limit));
+                    }
+                } else {
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) {
+                        const int n = nt * PF_BN + c0 + j;
+                        if (fok && n < n_rows) a.y_out[(size_t)(seg + n) * a.Mrows + f] = d[j];
+                    }
+                }
+            }
+            tc::fence_before_sync();
+            __syncwarp();
+            if (lane == 0) tc::bar_arrive(&acc_empty[ab]);
+        }
+    } else {
+        // decoder warps: thread t takes row t / 2, half t % 2 of every staged chunk
+        const int t = threadIdx.x - 6 * 32, row = t >> 1, half = t & 1;
+        long g = 0;
+        for (long tile = blockIdx.x; tile < total && !abort_; tile += gridDim.x) {
+            bool ok = true;
+            for (int kb = 0; kb < KB; ++kb, ++g) {
+                const int s = (int)(g % C::STAGES);
+                if (!tc::bar_wait(&full[s], (unsigned)((g / C::STAGES) & 1), &abort_, a.status, PF_STATUS_WAIT)) {
+                    ok = false;
+                    break;
+                }
+#pragma unroll
+                for (int m = 0; m < C::NA; ++m)
+                    tc4_decode_half<WT>(stage_raw(s) + m * C::CB, stage_a(s) + m * PF_TILE_BYTES, row, half);
+                fence_proxy_async();  // the generic-proxy tile writes, visible to the MMA's reads
+                __syncwarp();
+                if (lane == 0) tc::bar_arrive(&dec[s]);
+            }
+            if (!ok) break;
+        }
+    }
+    tc::fence_before_sync();
+    __syncthreads();
+    if (warp == 0) {
+        tc::fence_after_sync();
+        tc::tmem_dealloc(tmem, C::TMEM_COLS);
+    }
+}
+
 // ---- host ---------------------------------------------------------------------------------
 
 typedef CUresult (*encode_tiled_fn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
@@ -518,9 +813,73 @@ struct moearc_x_prefill {
     int *seg_cnt, *seg_off, *seg_toff, *seg_w, *seg_cur;  // expert-parallel segments (<= 1024)
     int *epos;                                          // [E] position of each expert in the row order
     bool order_identity = true;
-    uint16_t *xp, *actb, *wgu, *wdn;
-    CUtensorMap map_wgu, map_xp, map_wdn, map_act;
+    uint16_t *xp, *actb;
+    CUtensorMap map_xp, map_act;
+    // expert weights, allocated by the first load of each form: the bf16 expansion
+    // ([E][2][I][H] and [E][H][I]) or the 4-bit chunks (tc4 layout); the last load picks the form
+    void *w16 = nullptr;
+    uint16_t *wgu = nullptr, *wdn = nullptr;
+    CUtensorMap map_wgu, map_wdn;
+    uint8_t *w4 = nullptr, *w4gu = nullptr, *w4dn = nullptr;
+    bool mode4 = false;
+    int *elist = nullptr;  // [E] device copy of a load list
 };
+
+namespace {
+
+bool ensure_bf16(moearc_x_prefill *p) {
+    if (p->w16) return true;
+    const size_t ngu = (size_t)p->E * 2 * p->I * p->H, ndn = (size_t)p->E * p->H * p->I;
+    if (cudaMalloc(&p->w16, 2 * (ngu + ndn)) != cudaSuccess) {
+        cudaGetLastError();
+        p->w16 = nullptr;
+        return false;
+    }
+    p->wgu = static_cast<uint16_t *>(p->w16);
+    p->wdn = p->wgu + ngu;
+    return make_map(&p->map_wgu, p->wgu, (long)p->E * 2 * p->I, p->H) && make_map(&p->map_wdn, p->wdn, (long)p->E * p->H, p->I);
+}
+
+int tc4_bytes(const moearc_x_prefill *p) { return p->wtype == T_MXFP4 ? tc4_chunk<39>() : tc4_chunk<2>(); }
+
+bool ensure_4bit(moearc_x_prefill *p) {
+    if (p->w4) return true;
+    const size_t cb = (size_t)tc4_bytes(p);
+    const size_t gu = (size_t)p->E * 2 * ((p->I + 127) / 128) * (p->H / 64) * cb;
+    const size_t dn = (size_t)p->E * ((p->H + 127) / 128) * (p->I / 64) * cb;
+    if (cudaMalloc(reinterpret_cast<void **>(&p->w4), gu + dn) != cudaSuccess) {
+        cudaGetLastError();
+        p->w4 = nullptr;
+        return false;
+    }
+    p->w4gu = p->w4;
+    p->w4dn = p->w4 + gu;
+    return true;
+}
+
+// The grouped GEMM of one matrix set (MODE 0 gate-up, 1 down) on whichever weight form is loaded.
+int launch_gemm(moearc_x_prefill *p, int mode, const pf_gemm_args &g, const CUtensorMap &xmap) {
+    moearc_ctx *c = p->c;
+    cudaStream_t st = c->stream;
+    if (!p->mode4) {
+        if (mode == 0) k_pf_gemm<0><<<c->sm_count, 192, pf_cfg<0>::SMEM, st>>>(p->map_wgu, xmap, g);
+        else k_pf_gemm<1><<<c->sm_count, 192, pf_cfg<1>::SMEM, st>>>(p->map_wdn, xmap, g);
+        return cudaGetLastError() == cudaSuccess ? OK : ERR;
+    }
+    pf_gemm4_args a4{g, mode == 0 ? p->w4gu : p->w4dn, 0, 0};
+    a4.RB = mode == 0 ? (p->I + 127) / 128 : (p->H + 127) / 128;
+    a4.KB = mode == 0 ? p->H / 64 : p->I / 64;
+    if (p->wtype == T_MXFP4) {
+        if (mode == 0) k_pf_gemm4<0, 39><<<c->sm_count, pf4_cfg<0, 39>::THREADS, pf4_cfg<0, 39>::SMEM, st>>>(xmap, a4);
+        else k_pf_gemm4<1, 39><<<c->sm_count, pf4_cfg<1, 39>::THREADS, pf4_cfg<1, 39>::SMEM, st>>>(xmap, a4);
+    } else {
+        if (mode == 0) k_pf_gemm4<0, 2><<<c->sm_count, pf4_cfg<0, 2>::THREADS, pf4_cfg<0, 2>::SMEM, st>>>(xmap, a4);
+        else k_pf_gemm4<1, 2><<<c->sm_count, pf4_cfg<1, 2>::THREADS, pf4_cfg<1, 2>::SMEM, st>>>(xmap, a4);
+    }
+    return cudaGetLastError() == cudaSuccess ? OK : ERR;
+}
+
+}  // namespace
 
 extern "C" {
 
@@ -556,9 +915,8 @@ moearc_x_prefill *moearc_x_prefill_create(moearc_ctx *c, const moearc_x_moe_desc
     const size_t o_cnt = take(sizeof(int) * (p->E + 1)), o_off = take(sizeof(int) * (p->E + 1));
     const size_t o_toff = take(sizeof(int) * (p->E + 1)), o_cur = take(sizeof(int) * (p->E + 1));
     const size_t o_perm = take(sizeof(int) * rows), o_st = take(sizeof(int));
-    const size_t o_seg = take(sizeof(int) * 6 * 1025);
+    const size_t o_seg = take(sizeof(int) * 7 * 1025);
     const size_t o_xp = take(2 * rows * p->H), o_act = take(2 * rows * p->I);
-    const size_t o_wgu = take(2 * (size_t)p->E * 2 * p->I * p->H), o_wdn = take(2 * (size_t)p->E * p->H * p->I);
     if (cudaMalloc(&p->mem, off) != cudaSuccess) {
         cudaGetLastError();
         delete p;
@@ -581,14 +939,15 @@ moearc_x_prefill *moearc_x_prefill_create(moearc_ctx *c, const moearc_x_moe_desc
     p->seg_w = p->seg_toff + 1025;
     p->seg_cur = p->seg_w + 1025;
     p->epos = p->seg_cur + 1025;
+    p->elist = p->epos + 1025;
     p->xp = reinterpret_cast<uint16_t *>(b + o_xp);
     p->actb = reinterpret_cast<uint16_t *>(b + o_act);
-    p->wgu = reinterpret_cast<uint16_t *>(b + o_wgu);
-    p->wdn = reinterpret_cast<uint16_t *>(b + o_wdn);
-    const bool ok = make_map(&p->map_wgu, p->wgu, (long)p->E * 2 * p->I, p->H) &&
-                    make_map(&p->map_xp, p->xp, (long)rows, p->H) &&
-                    make_map(&p->map_wdn, p->wdn, (long)p->E * p->H, p->I) &&
+    const bool ok = make_map(&p->map_xp, p->xp, (long)rows, p->H) &&
                     make_map(&p->map_act, p->actb, (long)rows, p->I) &&
+                    set_smem(k_pf_gemm4<0, 39>, pf4_cfg<0, 39>::SMEM) == cudaSuccess &&
+                    set_smem(k_pf_gemm4<1, 39>, pf4_cfg<1, 39>::SMEM) == cudaSuccess &&
+                    set_smem(k_pf_gemm4<0, 2>, pf4_cfg<0, 2>::SMEM) == cudaSuccess &&
+                    set_smem(k_pf_gemm4<1, 2>, pf4_cfg<1, 2>::SMEM) == cudaSuccess &&
                     set_smem(k_pf_gemm<0>, pf_cfg<0>::SMEM) == cudaSuccess &&
                     set_smem(k_pf_gemm<1>, pf_cfg<1>::SMEM) == cudaSuccess &&
                     set_smem(k_pf_logits, PF_LOGIT_TOK * p->H * 4) == cudaSuccess &&
@@ -610,6 +969,8 @@ moearc_x_prefill *moearc_x_prefill_create(moearc_ctx *c, const moearc_x_moe_desc
 void moearc_x_prefill_destroy(moearc_x_prefill *p) {
     if (!p) return;
     cudaStreamSynchronize(p->c->stream);
+    cudaFree(p->w16);
+    cudaFree(p->w4);
     cudaFree(p->mem);
     delete p;
 }
@@ -618,6 +979,8 @@ int moearc_x_prefill_load_range(moearc_x_prefill *p, const void *gateup_packed, 
                                 unsigned e_first, unsigned n) {
     if (!p || !gateup_packed || !down_packed) return ERR;
     if (n == 0 || e_first + n > (unsigned)p->E) return ERR_ARG;
+    if (!ensure_bf16(p)) return ERR;
+    p->mode4 = false;
     moearc_ctx *c = p->c;
     const int E = (int)n;
     const size_t gu_e = (size_t)(p->I / 16) * (p->H / 64) * 2 * p->tile_bytes, dn_e = (size_t)(p->H / 16) * (p->I / 64) * p->tile_bytes;
@@ -643,6 +1006,8 @@ int moearc_x_prefill_load_list(moearc_x_prefill *p, const void *gateup_packed, c
     if (n == 0 || n > (unsigned)p->E) return ERR_ARG;
     for (unsigned i = 0; i < n; ++i)
         if (experts[i] < 0 || experts[i] >= p->E) return ERR_ARG;
+    if (!ensure_bf16(p)) return ERR;
+    p->mode4 = false;
     moearc_ctx *c = p->c;
     const size_t gu_e = (size_t)(p->I / 16) * (p->H / 64) * 2 * p->tile_bytes, dn_e = (size_t)(p->H / 16) * (p->I / 64) * p->tile_bytes;
     const long gu_tiles = (long)(p->I / 16) * (p->H / 64) * 2, dn_tiles = (long)(p->H / 16) * (p->I / 64);
@@ -678,6 +1043,40 @@ int moearc_x_prefill_set_order(moearc_x_prefill *p, const int *pos) {
                    cudaStreamSynchronize(p->c->stream) == cudaSuccess
                ? OK
                : ERR;
+}
+
+// The 4-bit form: experts[i] (host array) repacked into chunk slot i of the tc4 layout; the
+// GEMMs then decode the chunks on the fly (same values as the bf16 expansion).
+int moearc_x_prefill_load4_list(moearc_x_prefill *p, const void *gateup_packed, const void *down_packed,
+                                const int *experts, unsigned n) {
+    if (!p || !gateup_packed || !down_packed || !experts) return ERR;
+    if (n == 0 || n > (unsigned)p->E) return ERR_ARG;
+    for (unsigned i = 0; i < n; ++i)
+        if (experts[i] < 0 || experts[i] >= p->E) return ERR_ARG;
+    if (!ensure_4bit(p)) return ERR;
+    moearc_ctx *c = p->c;
+    if (cudaMemcpyAsync(p->elist, experts, sizeof(int) * n, cudaMemcpyHostToDevice, c->stream) != cudaSuccess) return ERR;
+    const uint8_t *gu = static_cast<const uint8_t *>(gateup_packed), *dn = static_cast<const uint8_t *>(down_packed);
+    const long rows_gu = (long)n * 2 * ((p->I + 127) / 128) * (p->H / 64) * 128;
+    const long rows_dn = (long)n * ((p->H + 127) / 128) * (p->I / 64) * 128;
+    auto grid = [](long t) { return dim3((unsigned)((t + 255) / 256)); };
+    if (p->wtype == T_MXFP4) {
+        k_pf_pack4<39><<<grid(rows_gu), 256, 0, c->stream>>>(gu, p->elist, (int)n, p->I, p->H, 2, p->tile_bytes, p->w4gu);
+        k_pf_pack4<39><<<grid(rows_dn), 256, 0, c->stream>>>(dn, p->elist, (int)n, p->H, p->I, 1, p->tile_bytes, p->w4dn);
+    } else {
+        k_pf_pack4<2><<<grid(rows_gu), 256, 0, c->stream>>>(gu, p->elist, (int)n, p->I, p->H, 2, p->tile_bytes, p->w4gu);
+        k_pf_pack4<2><<<grid(rows_dn), 256, 0, c->stream>>>(dn, p->elist, (int)n, p->H, p->I, 1, p->tile_bytes, p->w4dn);
+    }
+    if (cudaGetLastError() != cudaSuccess) return ERR;
+    p->mode4 = true;
+    return cudaStreamSynchronize(c->stream) == cudaSuccess ? OK : ERR;  // the host list may go
+}
+
+int moearc_x_prefill_load4(moearc_x_prefill *p, const void *gateup_packed, const void *down_packed) {
+    if (!p) return ERR;
+    std::vector<int> all(p->E);
+    for (int e = 0; e < p->E; ++e) all[e] = e;
+    return moearc_x_prefill_load4_list(p, gateup_packed, down_packed, all.data(), (unsigned)p->E);
 }
 
 int moearc_x_prefill_load(moearc_x_prefill *p, const void *gateup_packed, const void *down_packed) {
@@ -729,11 +1128,12 @@ int prefill_forward(moearc_x_prefill *p, const uint16_t *x, unsigned n_tokens, c
     g.status = p->status;
     g.Mrows = p->I;
     g.K = p->H;
-    k_pf_gemm<0><<<c->sm_count, 192, pf_cfg<0>::SMEM, st>>>(p->map_wgu, p->map_xp, g);
+    if (!p->w16 && !p->w4) return ERR_ARG;  // no weights loaded
+    if (launch_gemm(p, 0, g, p->map_xp) != OK) return ERR;
     mark(5);
     g.Mrows = p->H;
     g.K = p->I;
-    k_pf_gemm<1><<<c->sm_count, 192, pf_cfg<1>::SMEM, st>>>(p->map_wdn, p->map_act, g);
+    if (launch_gemm(p, 1, g, p->map_act) != OK) return ERR;
     mark(6);
     const long n = (long)T * p->H;
     k_pf_combine<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(p->y, p->perm, p->wts, residual, out, T, p->K, p->H);
@@ -841,10 +1241,11 @@ int moearc_x_prefill_experts(moearc_x_prefill *p, const uint16_t *rows_in, unsig
     g.status = p->status;
     g.Mrows = p->I;
     g.K = p->H;
-    k_pf_gemm<0><<<c->sm_count, 192, pf_cfg<0>::SMEM, st>>>(p->map_wgu, map_rows, g);
+    if (!p->w16 && !p->w4) return ERR_ARG;
+    if (launch_gemm(p, 0, g, map_rows) != OK) return ERR;
     g.Mrows = p->H;
     g.K = p->I;
-    k_pf_gemm<1><<<c->sm_count, 192, pf_cfg<1>::SMEM, st>>>(p->map_wdn, map_act, g);
+    if (launch_gemm(p, 1, g, map_act) != OK) return ERR;
     return ls.finish();
 }
 

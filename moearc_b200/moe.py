@@ -149,7 +149,16 @@ def _prefill_split_methods():
         pos = np.ascontiguousarray(pos, np.int32)
         self.ctx._finish(self.ctx.lib.moearc_x_prefill_set_order(self.h, pos.ctypes.data), "prefill_set_order")
 
-    for f in (load_range, route, experts, combine, buffer_ptr, load_list, set_order):
+    def load4(self, gateup: DeviceBuffer, down: DeviceBuffer, experts=None) -> None:
+        """The 4-bit form (all experts, or experts[i] -> slot i); same results as the bf16 form."""
+        if experts is None:
+            rc = self.ctx.lib.moearc_x_prefill_load4(self.h, gateup.ptr, down.ptr)
+        else:
+            ids = np.ascontiguousarray(experts, np.int32)
+            rc = self.ctx.lib.moearc_x_prefill_load4_list(self.h, gateup.ptr, down.ptr, ids.ctypes.data, len(ids))
+        self.ctx._finish(rc, "prefill_load4")
+
+    for f in (load_range, route, experts, combine, buffer_ptr, load_list, set_order, load4):
         setattr(MoePrefill, f.__name__, f)
 
 

@@ -157,7 +157,8 @@ def test_skewed_routing_many_tokens_against_torch(ctx):
     packer.close()
 
 
-@pytest.mark.parametrize("world,placement", [(2, "contiguous"), (4, "interleaved"), (4, "balanced")])
+@pytest.mark.parametrize("world,placement", [(2, "contiguous"), (4, "interleaved"), (4, "balanced"),
+                                             (4, "balanced-4bit")])
 def test_expert_parallel_split_gives_the_same_bits(ctx, world, placement):
     """Expert parallelism emulated on one GPU: each virtual rank routes its own tokens, owns a
     contiguous expert range (moearc_x_prefill_load_range), receives the rows of its experts from
@@ -189,6 +190,8 @@ def test_expert_parallel_split_gives_the_same_bits(ctx, world, placement):
         pf.set_order(pos)
         if placement == "contiguous":
             pf.load_range(packer.gateup, packer.down, r * nl, nl)
+        elif placement == "balanced-4bit":
+            pf.load4(packer.gateup, packer.down, lists[r])
         else:
             pf.load_list(packer.gateup, packer.down, lists[r])
         x = ctx.upload_new(xb[r * Tr * H:(r + 1) * Tr * H])
@@ -219,4 +222,30 @@ def test_expert_parallel_split_gives_the_same_bits(ctx, world, placement):
         assert pf.status() == 0
         pf.close()
     whole.close()
+    packer.close()
+
+
+@pytest.mark.parametrize("wtype", [O.MXFP4, O.Q4_0])
+def test_4bit_weights_give_the_same_bits(ctx, wtype):
+    """The 4-bit weight form (chunks bulk-copied and expanded to bf16 in shared memory by decoder
+    warps) gives the bf16-expansion form's output bit for bit, over a skewed routing that leaves
+    some experts empty and others with several 128-row tiles."""
+    H, I, E, k, T = 2880, 2880, 16, 4, 700
+    pf, packer, host = build(ctx, H, I, E, k, 2, 1, wtype, T, 0x9F51)
+    bias = np.zeros(E, np.float32)
+    bias[:3] = [2.0, 1.5, 1.0]
+    bias[12:] = -5.0
+    xb = ctx.upload_new(O.synth_normal_bf16(0x9F52, T * H, 1.0))
+    rw, rb = ctx.upload_new(host[3]), ctx.upload_new(bias)
+    res = ctx.upload_new(O.synth_normal_f32(0x9F53, T * H, 1.0))
+    a, b = ctx.alloc_n(np.float32, T * H), ctx.alloc_n(np.float32, T * H)
+    pf.forward(xb, T, rw, a, router_b=rb, residual=res)
+    pf.load4(packer.gateup, packer.down)
+    pf.forward(xb, T, rw, b, router_b=rb, residual=res)
+    ga, gb = ctx.download(a, np.float32, T * H), ctx.download(b, np.float32, T * H)
+    assert pf.status() == 0
+    cnt = pf.buffer(3, np.int32, E)
+    assert cnt.max() > 128 and (cnt == 0).any()
+    assert np.array_equal(ga.view(np.uint32), gb.view(np.uint32))
+    pf.close()
     packer.close()
