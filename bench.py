@@ -312,7 +312,10 @@ def prefill_bench(args) -> dict:
     out = ctx.alloc(T * H * 4)
     ctx.sync()
     ctx.timer_start()
-    pf.load(packer.gateup, packer.down)
+    if args.weights == "4bit":
+        pf.load4(packer.gateup, packer.down)
+    else:
+        pf.load(packer.gateup, packer.down)
     load_ms = ctx.timer_stop()
     for _ in range(args.warmup):
         pf.forward(x, T, router, out, router_b=bias)
@@ -453,7 +456,9 @@ def prefill_main(args) -> None:
         "metric": "MoE prefill TFLOP/s, one gpt-oss-120b-shaped MoE block (configs[3] shape, 1 GPU)",
         "value": value, "unit": "TFLOP/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": r["ms_step"], "tokens_per_s": T / (r["ms_step"] / 1000.0), "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "bf16 operands, f32 accumulate (MXFP4 weights expanded to bf16)",
+        "scaling": "weak", "vs_baseline": None, "dtype": ("bf16 operands, f32 accumulate (MXFP4 weights staged at 4 bits, expanded in shared memory)"
+                                                           if args.weights == "4bit" else
+                                                           "bf16 operands, f32 accumulate (MXFP4 weights expanded to bf16)"),
         "data": "synthetic (seeded MXFP4 experts, bf16 N(0,1) activations, Zipf(1.1) router bias)",
         "config": {"workload": f"configs[3] MoE block: {T} tokens (8 x 4096 at full size), {r['E']} experts top-4, 2880 x 2880",
                    "tokens": T, "expert_load_max": int(cnt.max()), "expert_load_mean": float(cnt.mean()),
@@ -461,7 +466,7 @@ def prefill_main(args) -> None:
         "roofline": {"bound": "tensor", "kernel": "gate-up grouped GEMM (tcgen05 kind::f16, SwiGLU epilogue)",
                      "achieved": gu_tflops, "peak": peak, "unit": "TFLOP/s", "frac": gu_tflops / peak,
                      "peak_kind": "measured bf16 (MEASURED_PEAKS.json)" if peaks else "fallback", "traffic": None},
-        "kernel_ms": r["kernel_ms"], "weight_expand_ms": r["load_ms"],
+        "kernel_ms": r["kernel_ms"], "weight_load_ms": r["load_ms"], "weights": args.weights,
         "e2e": {"value": flops * args.steps / r["e2e_s"] / 1e12, "unit": "TFLOP/s",
                 "h2d_bytes_per_step": T * H * 2, "d2h_bytes_per_step": T * H * 4},
         "gpu_launches": 7 * args.steps, "clocks": r["clocks"],
@@ -532,24 +537,22 @@ def batch_main(args) -> None:
     Dq, Dkv = cfg.n_head * cfg.head_dim, cfg.n_head_kv * cfg.head_dim
     distinct = E * (1.0 - (1.0 - k / E) ** B)  # expected experts a step touches per block
     dense_b = (H * (Dq + 2 * Dkv) + H * Dq) * 2
-    expert_bf16 = distinct * 3 * I * H * 2
     expert_q4 = distinct * 3 * I * H * 18 / 32
     kv_b = B * (depth + 1) * Dkv * 2 * 2
-    step_b = cfg.n_layer * (dense_b + E * H * 4 + expert_bf16 + kv_b)
+    step_b = cfg.n_layer * (dense_b + E * H * 4 + expert_q4 + kv_b)
     peak, peak_kind = load_peaks()
     achieved = step_b / (ms_step / 1000.0) / 1e9
     line = {
         "metric": f"batched decode tok/s (all streams), Qwen3-MoE shape, {B} streams at depth {depth} (configs[4], 1 GPU)",
         "value": B / (ms_step / 1000.0), "unit": "tok/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-        "dtype": "bf16 operands, f32 accumulate (Q4_0 experts expanded to bf16)",
+        "dtype": "bf16 operands, f32 accumulate (Q4_0 experts staged at 4 bits, expanded in shared memory)",
         "data": "synthetic (seeded weights of the configs[4] architecture, synthetic KV at the depth)",
         "config": {"workload": f"configs[4] Qwen3-MoE shape, {cfg.n_layer} blocks, {B} streams, depth {depth}",
                    "batch": B, "depth": depth, "l2": "weights and KV (~100 GB) far exceed the 126 MB L2"},
-        "roofline": {"bound": "hbm", "kernel": "whole step (algorithmic bytes: bf16 dense and experts as read, KV span)",
+        "roofline": {"bound": "hbm", "kernel": "whole step (algorithmic bytes: bf16 dense weights, 4-bit experts, KV span)",
                      "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak, "peak_kind": peak_kind,
-                     "traffic": None, "bytes_per_step": step_b,
-                     "bytes_per_step_if_experts_stayed_4bit": cfg.n_layer * (dense_b + E * H * 4 + expert_q4 + kv_b)},
+                     "traffic": None, "bytes_per_step": step_b},
         "e2e": {"value": B * args.steps / e2e_s, "unit": "tok/s", "h2d_bytes_per_step": 4 * B * H,
                 "d2h_bytes_per_step": 4 * B * H},
         "gpu_launches": None, "clocks": clocks, "build_s": build_s,
@@ -565,6 +568,8 @@ def main() -> None:
     ap.add_argument("--depth", type=int, default=0)
     ap.add_argument("--config", default="120b", choices=["120b", "20b", "prefill", "qwen3"])
     ap.add_argument("--batch", type=int, default=64, help="qwen3: concurrent streams (configs[4]: 64)")
+    ap.add_argument("--weights", default="bf16", choices=["4bit", "bf16"],
+                    help="prefill: expert weights staged at 4 bits (expanded in shared memory) or expanded to bf16")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--layers", type=int, default=0,

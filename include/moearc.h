@@ -226,8 +226,10 @@ int moearc_x_prefill_load_list(moearc_x_prefill *p, const void *gateup_packed, c
                                const int *experts, unsigned int n);
 /* The 4-bit form of the same experts (all, or experts[i] -> slot i): the packed banks are
  * repacked into chunks of 128 rows x 64 columns that one bulk copy moves, and the GEMMs expand
- * them to bf16 in shared memory as they go (the same values as the bf16 expansion, so the same
- * results bit for bit, with a quarter of the weight bytes). The last load picks the form. */
+ * them in shared memory as they go, a quarter of the weight bytes of the bf16 form. This form
+ * computes in f16 (weights, activations, SwiGLU outputs): -2 when the weights' scaled values do
+ * not fit f16 exactly (MXFP4 e8m0 exponents outside [105, 140], or Q4_0 8|d| > 65504), leaving
+ * the previous form in place. The last successful load picks the form. */
 int moearc_x_prefill_load4(moearc_x_prefill *p, const void *gateup_packed, const void *down_packed);
 int moearc_x_prefill_load4_list(moearc_x_prefill *p, const void *gateup_packed, const void *down_packed,
                                 const int *experts, unsigned int n);

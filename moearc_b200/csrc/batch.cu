@@ -351,6 +351,8 @@ moearc_x_batch_decoder *moearc_x_batch_decoder_create(moearc_ctx *c, const moear
         ok &= moearc_x_synth(c, s8 + bank, blocks, ekind, seed(9, l), 0.01f, -8, -4) == OK;
         ok &= moearc_x_synth(c, s8 + 2 * bank, blocks, ekind, seed(10, l), 0.01f, -8, -4) == OK;
         ok &= moearc_x_moe_pack(packer, s8, s8 + bank, s8 + 2 * bank, g.n_expert, p8, p8 + 2 * bank) == OK;
+        // the bf16 form: faster here than the 4-bit one (whose shared-memory expansion shortens
+        // the copy pipeline), at 4x the expert memory
         ok &= moearc_x_prefill_load(b.moe, p8, p8 + 2 * bank) == OK;
         ok &= cudaMemsetAsync(b.k_pages, 0, 2 * pool, c->stream) == cudaSuccess;
         ok &= cudaMemsetAsync(b.v_pages, 0, 2 * pool, c->stream) == cudaSuccess;

@@ -45,6 +45,7 @@ constexpr int PF_TILE_BYTES = PF_BM * PF_BK * 2;  // one 128 x 64 bf16 operand t
 constexpr int PF_LOGIT_TOK = 16;                  // tokens per router CTA
 constexpr int PF_LOGIT_EXP = 4;                   // experts a warp folds at once
 constexpr int PF_STATUS_WAIT = 1;                 // a pipeline wait gave up
+constexpr int PF_STATUS_RANGE = 2;                // 4-bit weights whose scaled values leave f16
 
 __device__ __forceinline__ uint16_t f32_to_bf16_rn(float f) {
     return __bfloat16_as_ushort(__float2bfloat16_rn(f));
@@ -175,7 +176,7 @@ __global__ void k_pf_scan(const int *cnt, int E, int *off, int *toff, int *curso
 // its own activation, so the order does not reach the output.
 __global__ void __launch_bounds__(256) k_pf_scatter(const uint16_t *x, const unsigned *idx, const int *epos, int T,
                                                     int K, int H, const int *off, int *cursor, int *perm,
-                                                    uint16_t *xp) {
+                                                    uint16_t *xp, int to_f16) {
     const int lane = threadIdx.x & 31;
     const long p = (long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
     if (p >= (long)T * K) return;
@@ -188,7 +189,22 @@ __global__ void __launch_bounds__(256) k_pf_scatter(const uint16_t *x, const uns
     row = __shfl_sync(0xffffffffu, row, 0);
     const uint4 *src = reinterpret_cast<const uint4 *>(x + (size_t)(p / K) * H);
     uint4 *dst = reinterpret_cast<uint4 *>(xp + (size_t)row * H);
-    for (int i = lane; i < H / 8; i += 32) dst[i] = __ldg(src + i);
+    if (!to_f16) {
+        for (int i = lane; i < H / 8; i += 32) dst[i] = __ldg(src + i);
+        return;
+    }
+    // the 4-bit path's f16 operands: bf16 -> f16 (exact within f16's range)
+    for (int i = lane; i < H / 8; i += 32) {
+        const uint4 v = __ldg(src + i);
+        const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+        uint32_t o[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const __half2 h = __floats2half2_rn(__uint_as_float(w[j] << 16), __uint_as_float(w[j] & 0xFFFF0000u));
+            o[j] = *reinterpret_cast<const uint32_t *>(&h);
+        }
+        dst[i] = make_uint4(o[0], o[1], o[2], o[3]);
+    }
 }
 
 // out[t] = residual[t] + sum_m w[t,m] y[perm[t,m]] (fmaf chain, m ascending).
@@ -448,8 +464,12 @@ __global__ void __launch_bounds__(192, 1) k_pf_gemm(const __grid_constant__ CUte
 // chunk (rb, kb) at index rb * (K / 64) + kb, each one contiguous run: 128 rows of 32 bytes (byte j
 // holds column 2j in its low nibble and 2j + 1 in its high nibble), then the rows' two block
 // scales (MXFP4: one e8m0 byte per 32 columns; Q4_0: one f16 delta). Rows past R are zeros. A
-// chunk is one bulk copy; decoder warps turn it into the bf16 operand tile the MMA reads, with
-// the values the bf16 expansion (k_pf_unpack) would hold, so both paths give the same bits.
+// chunk is one bulk copy; decoder warps turn it into an f16 operand tile for the MMA (one
+// conversion and one multiply per pair of weights). The whole 4-bit path runs in f16 (weights,
+// activations, SwiGLU outputs; A and B of an MMA always share the type): the MXFP4 weights are
+// exact in f16 while their e8m0 exponents lie in [105, 140] (the pack kernel checks, and the load
+// refuses weights outside it), Q4_0's (n - 8) d rounds once to f16, and bf16 activations convert
+// exactly.
 
 constexpr int TC4_NIB = 128 * 32;  // nibble bytes of a chunk
 
@@ -462,7 +482,7 @@ constexpr int tc4_chunk() { return TC4_NIB + 128 * 2 * tc4_sb<WT>(); }  // 4352 
 // (moearc_x_moe_pack layout; mats = 2: gate-up pairs, 1: down tiles) of experts[i] -> slot i.
 template <int WT>
 __global__ void k_pf_pack4(const uint8_t *bank, const int *experts, int n_exp, int R, int K, int mats,
-                           int tile_bytes, uint8_t *dst) {
+                           int tile_bytes, uint8_t *dst, int *status) {
     constexpr int sb = tc4_sb<WT>();
     const int RB = (R + 127) / 128, KB = K / 64;
     const long per_mat = (long)RB * KB;
@@ -494,6 +514,19 @@ __global__ void k_pf_pack4(const uint8_t *bank, const int *experts, int n_exp, i
         }
         for (int b = 0; b < 2; ++b)
             for (int i = 0; i < sb; ++i) sc[b * sb + i] = tile[512 + r * 4 * sb + (half + 2 * b) * sb + i];
+        // f16 must hold every scaled value exactly (MXFP4: 0.5 .. 6 times 2^(e - 127), e = 0 for an
+        // all-zero block) or at least in range (Q4_0: 8 |d| <= 65504)
+        bool bad = false;
+        for (int b = 0; b < 2; ++b) {
+            if constexpr (WT == 39) {
+                const int e = sc[b];
+                bad |= e != 0 && (e < 105 || e > 140);
+            } else {
+                const float d = fabsf(f16_bits_to_f32((uint16_t)(sc[2 * b] | (sc[2 * b + 1] << 8))));
+                bad |= !(d * 8.0f <= 65504.0f);
+            }
+        }
+        if (bad) atomicOr(status, PF_STATUS_RANGE);
     }
     uint4 *o = reinterpret_cast<uint4 *>(out + row * 32);
     o[0] = make_uint4(nib[0], nib[1], nib[2], nib[3]);
@@ -521,17 +554,18 @@ struct pf4_cfg {
     static constexpr int THREADS = (6 + DEC_WARPS) * 32;
 };
 
-// Decode one thread's half row (32 columns: one scale block) of a staged chunk into the bf16 A
+// Decode one thread's half row (32 columns: one scale block) of a staged chunk into the f16 A
 // tile in the 128-byte swizzle layout (row `row`, 16-byte unit u at (u ^ (row & 7)) * 16).
 template <int WT>
 __device__ __forceinline__ void tc4_decode_half(const uint8_t *chunk, uint8_t *tile, int row, int half) {
-    constexpr int sb = tc4_sb<WT>();
     const uint4 w = *reinterpret_cast<const uint4 *>(chunk + row * 32 + half * 16);
-    float s;
+    __half2 s2;
     if constexpr (WT == 39) {
-        s = __uint_as_float((uint32_t)chunk[TC4_NIB + row * 2 + half] << 23);
+        // 2^(e - 127) (e = 0: a zero block), exact in f16 for the exponents the load accepts
+        s2 = __float2half2_rn(__uint_as_float((uint32_t)chunk[TC4_NIB + row * 2 + half] << 23));
     } else {
-        s = f16_bits_to_f32(*reinterpret_cast<const uint16_t *>(chunk + TC4_NIB + row * 4 + half * 2));
+        const __half d = __ushort_as_half(*reinterpret_cast<const uint16_t *>(chunk + TC4_NIB + row * 4 + half * 2));
+        s2 = __halves2half2(d, d);
     }
     const uint32_t words[4] = {w.x, w.y, w.z, w.w};
 #pragma unroll
@@ -541,8 +575,8 @@ __device__ __forceinline__ void tc4_decode_half(const uint8_t *chunk, uint8_t *t
         uint32_t o[4];
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
-            const __half2 h = *reinterpret_cast<const __half2 *>(&pr[j]);
-            o[j] = (uint32_t)f32_to_bf16_rn(__low2float(h) * s) | ((uint32_t)f32_to_bf16_rn(__high2float(h) * s) << 16);
+            const __half2 h = __hmul2(*reinterpret_cast<const __half2 *>(&pr[j]), s2);
+            o[j] = *reinterpret_cast<const uint32_t *>(&h);
         }
         const int u = half * 4 + i;
         *reinterpret_cast<uint4 *>(tile + row * 128 + ((u ^ (row & 7)) * 16)) = make_uint4(o[0], o[1], o[2], o[3]);
@@ -632,7 +666,7 @@ __global__ void __launch_bounds__(pf4_cfg<MODE, WT>::THREADS, 1)
         __syncwarp();
     } else if (warp == 1) {
         if (lane == 0) {
-            constexpr uint32_t idesc = tc::idesc_bf16_f32(PF_BM, PF_BN);
+            constexpr uint32_t idesc = tc::idesc_f16_f32(PF_BM, PF_BN);  // A and B both f16
             long g = 0, i = 0;
             for (long tile = blockIdx.x; tile < total && !abort_; tile += gridDim.x, ++i) {
                 const int ab = (int)(i & 1);
@@ -692,7 +726,8 @@ __global__ void __launch_bounds__(pf4_cfg<MODE, WT>::THREADS, 1)
                     for (int j = 0; j < 16; ++j) {
                         const int n = nt * PF_BN + c0 + j;
                         if (fok && n < n_rows)
-                            a.act_out[(size_t)(seg + n) * a.Mrows + f] = f32_to_bf16_rn(act_fn(a.act, d[j], u[j], a.alpha, a.limit));
+                            a.act_out[(size_t)(seg + n) * a.Mrows + f] =
+                                __half_as_ushort(__float2half_rn(act_fn(a.act, d[j], u[j], a.alpha, a.limit)));
                     }
                 } else {
 #pragma unroll
@@ -1060,16 +1095,23 @@ int moearc_x_prefill_load4_list(moearc_x_prefill *p, const void *gateup_packed, 
     const long rows_gu = (long)n * 2 * ((p->I + 127) / 128) * (p->H / 64) * 128;
     const long rows_dn = (long)n * ((p->H + 127) / 128) * (p->I / 64) * 128;
     auto grid = [](long t) { return dim3((unsigned)((t + 255) / 256)); };
+    if (cudaMemsetAsync(p->status, 0, sizeof(int), c->stream) != cudaSuccess) return ERR;
     if (p->wtype == T_MXFP4) {
-        k_pf_pack4<39><<<grid(rows_gu), 256, 0, c->stream>>>(gu, p->elist, (int)n, p->I, p->H, 2, p->tile_bytes, p->w4gu);
-        k_pf_pack4<39><<<grid(rows_dn), 256, 0, c->stream>>>(dn, p->elist, (int)n, p->H, p->I, 1, p->tile_bytes, p->w4dn);
+        k_pf_pack4<39><<<grid(rows_gu), 256, 0, c->stream>>>(gu, p->elist, (int)n, p->I, p->H, 2, p->tile_bytes, p->w4gu, p->status);
+        k_pf_pack4<39><<<grid(rows_dn), 256, 0, c->stream>>>(dn, p->elist, (int)n, p->H, p->I, 1, p->tile_bytes, p->w4dn, p->status);
     } else {
-        k_pf_pack4<2><<<grid(rows_gu), 256, 0, c->stream>>>(gu, p->elist, (int)n, p->I, p->H, 2, p->tile_bytes, p->w4gu);
-        k_pf_pack4<2><<<grid(rows_dn), 256, 0, c->stream>>>(dn, p->elist, (int)n, p->H, p->I, 1, p->tile_bytes, p->w4dn);
+        k_pf_pack4<2><<<grid(rows_gu), 256, 0, c->stream>>>(gu, p->elist, (int)n, p->I, p->H, 2, p->tile_bytes, p->w4gu, p->status);
+        k_pf_pack4<2><<<grid(rows_dn), 256, 0, c->stream>>>(dn, p->elist, (int)n, p->H, p->I, 1, p->tile_bytes, p->w4dn, p->status);
     }
     if (cudaGetLastError() != cudaSuccess) return ERR;
+    int st = 0;
+    if (cudaMemcpyAsync(&st, p->status, sizeof(int), cudaMemcpyDeviceToHost, c->stream) != cudaSuccess ||
+        cudaMemsetAsync(p->status, 0, sizeof(int), c->stream) != cudaSuccess ||
+        cudaStreamSynchronize(c->stream) != cudaSuccess)
+        return ERR;
+    if (st & PF_STATUS_RANGE) return ERR_ARG;  // scales f16 cannot hold: keep the bf16 form
     p->mode4 = true;
-    return cudaStreamSynchronize(c->stream) == cudaSuccess ? OK : ERR;  // the host list may go
+    return OK;
 }
 
 int moearc_x_prefill_load4(moearc_x_prefill *p, const void *gateup_packed, const void *down_packed) {
@@ -1114,7 +1156,7 @@ int prefill_forward(moearc_x_prefill *p, const uint16_t *x, unsigned n_tokens, c
     mark(3);
     const long pairs = (long)T * p->K;
     k_pf_scatter<<<(unsigned)((pairs + 7) / 8), 256, 0, st>>>(x, p->idx, p->epos, T, p->K, p->H, p->off, p->cursor,
-                                                              p->perm, p->xp);
+                                                              p->perm, p->xp, p->mode4 ? 1 : 0);
     mark(4);
     pf_gemm_args g{};
     g.E = p->E;
@@ -1196,7 +1238,7 @@ int moearc_x_prefill_route(moearc_x_prefill *p, const uint16_t *x, unsigned n_to
     k_pf_scan<<<1, 1024, 0, st>>>(p->cnt, p->E, p->off, p->toff, p->cursor);
     const long pairs = (long)T * p->K;
     k_pf_scatter<<<(unsigned)((pairs + 7) / 8), 256, 0, st>>>(x, p->idx, p->epos, T, p->K, p->H, p->off, p->cursor,
-                                                              p->perm, p->xp);
+                                                              p->perm, p->xp, p->mode4 ? 1 : 0);
     return cudaGetLastError() == cudaSuccess ? OK : ERR;
 }
 
