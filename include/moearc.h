@@ -255,6 +255,26 @@ int moearc_x_prefill_experts(moearc_x_prefill *p, const unsigned short *rows_in,
                              unsigned short *act_scratch, float *y_out);
 int moearc_x_prefill_combine(moearc_x_prefill *p, const float *y_rows, unsigned int n_tokens,
                              const float *residual, float *out);
+/* Expert parallelism over peer memory (no collective library): route_begin routes and counts
+ * (buffer 3 per position); after the caller has all-gathered every rank's counts,
+ * route_dispatch stores each row straight into the receive buffer of the rank owning its
+ * position (dst_rows[r], starting at row dst_base[r]; host arrays of n_ranks, n_ranks *
+ * n_local == E); after a barrier, experts_to runs the expert FFN on the received segments and
+ * stores segment s's result rows straight to seg_dst[s] (the source rank's y buffer at the rows
+ * its combine reads); after another barrier, combine. Both dispatch and experts_to return once
+ * their stores are done. Pointers may be local or opened with moearc_x_ipc_open. */
+int moearc_x_prefill_route_begin(moearc_x_prefill *p, const unsigned short *x, unsigned int n_tokens,
+                                 const float *router_w, const float *router_b);
+int moearc_x_prefill_route_dispatch(moearc_x_prefill *p, void *const *dst_rows, const int *dst_base,
+                                    unsigned int n_ranks, unsigned int n_local);
+int moearc_x_prefill_experts_to(moearc_x_prefill *p, const unsigned short *rows_in, unsigned int n_rows,
+                                const int *seg_counts, const int *seg_expert, unsigned int n_seg,
+                                unsigned short *act_scratch, float *const *seg_dst);
+/* CUDA IPC for the exchange buffers: the 64-byte handle of a cudaMalloc'd allocation (its start),
+ * its mapping in another process on the node, and the mapping's release. */
+int moearc_x_ipc_handle(const void *ptr, void *handle);
+int moearc_x_ipc_open(const void *handle, void **ptr);
+int moearc_x_ipc_close(void *ptr);
 /* moearc_x_prefill_forward with an event between its kernels, waited for: ms[i] = device time of
  * kernel i (0 router logits, 1 top-k, 2 scan, 3 scatter, 4 gate-up GEMM, 5 down GEMM, 6 combine);
  * n >= 7. */

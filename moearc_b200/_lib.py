@@ -95,6 +95,12 @@ SIGNATURES: dict[str, tuple] = {
     "moearc_x_prefill_set_order": (I, [P, P]),
     "moearc_x_prefill_load4": (I, [P, P, P]),
     "moearc_x_prefill_load4_list": (I, [P, P, P, P, U]),
+    "moearc_x_prefill_route_begin": (I, [P, P, U, P, P]),
+    "moearc_x_prefill_route_dispatch": (I, [P, P, P, U, U]),
+    "moearc_x_prefill_experts_to": (I, [P, P, U, P, P, U, P, P]),
+    "moearc_x_ipc_handle": (I, [P, P]),
+    "moearc_x_ipc_open": (I, [P, P]),
+    "moearc_x_ipc_close": (I, [P]),
     "moearc_x_decoder_create": (P, [P, P]),
     "moearc_x_decoder_destroy": (None, [P]),
     "moearc_x_decoder_input": (P, [P]),

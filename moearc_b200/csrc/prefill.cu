@@ -29,6 +29,7 @@
 
 #include <algorithm>
 #include <cmath>
+#include <cstring>
 #include <vector>
 
 #include "common.cuh"
@@ -174,23 +175,35 @@ __global__ void k_pf_scan(const int *cnt, int E, int *off, int *toff, int *curso
 // the row order at epos[e]: the identity on one GPU, owner-major under expert parallelism), and
 // the token's bf16 activation copied there. Rows within a segment are in arrival order; every row's results depend only on
 // its own activation, so the order does not reach the output.
+// Under expert parallelism with peer memory (dst_rows set): the row does not stay here but is
+// stored straight into the receive buffer of the rank owning its position (positions are
+// owner-major, n_local per rank): dst_rows[r] + (dst_base[r] + row - off[r * n_local]) rows.
 __global__ void __launch_bounds__(256) k_pf_scatter(const uint16_t *x, const unsigned *idx, const int *epos, int T,
                                                     int K, int H, const int *off, int *cursor, int *perm,
-                                                    uint16_t *xp, int to_f16) {
+                                                    uint16_t *xp, int to_f16, uint16_t *const *dst_rows,
+                                                    const int *dst_base, int n_local) {
     const int lane = threadIdx.x & 31;
     const long p = (long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
     if (p >= (long)T * K) return;
-    int row = 0;
+    int row = 0, pos = 0;
     if (lane == 0) {
-        const int e = epos[idx[p]];
-        row = off[e] + atomicAdd(cursor + e, 1);
+        pos = epos[idx[p]];
+        row = off[pos] + atomicAdd(cursor + pos, 1);
         perm[p] = row;
     }
     row = __shfl_sync(0xffffffffu, row, 0);
+    pos = __shfl_sync(0xffffffffu, pos, 0);
     const uint4 *src = reinterpret_cast<const uint4 *>(x + (size_t)(p / K) * H);
-    uint4 *dst = reinterpret_cast<uint4 *>(xp + (size_t)row * H);
+    uint4 *dst;
+    if (dst_rows) {
+        const int r = pos / n_local;
+        dst = reinterpret_cast<uint4 *>(dst_rows[r] + (size_t)(dst_base[r] + row - off[r * n_local]) * H);
+    } else {
+        dst = reinterpret_cast<uint4 *>(xp + (size_t)row * H);
+    }
     if (!to_f16) {
         for (int i = lane; i < H / 8; i += 32) dst[i] = __ldg(src + i);
+        if (dst_rows) __threadfence_system();  // peer stores performed before the kernel ends
         return;
     }
     // the 4-bit path's f16 operands: bf16 -> f16 (exact within f16's range)
@@ -205,6 +218,7 @@ __global__ void __launch_bounds__(256) k_pf_scatter(const uint16_t *x, const uns
         }
         dst[i] = make_uint4(o[0], o[1], o[2], o[3]);
     }
+    if (dst_rows) __threadfence_system();
 }
 
 // out[t] = residual[t] + sum_m w[t,m] y[perm[t,m]] (fmaf chain, m ascending).
@@ -282,6 +296,8 @@ struct pf_gemm_args {
     float alpha, limit;
     uint16_t *act_out;  // gate-up: [rows][n_ff] bf16
     float *y_out;       // down: [rows][n_embd] f32
+    float *const *seg_y;  // down, if set: segment e's rows go to seg_y[e] + n * n_embd instead (a peer
+                          // rank's memory under expert parallelism: the return leg of the exchange)
     int *status;
 };
 
@@ -438,13 +454,15 @@ __global__ void __launch_bounds__(192, 1) k_pf_gemm(const __grid_constant__ CUte
                             a.act_out[(size_t)(seg + n) * a.Mrows + f] = f32_to_bf16_rn(act_fn(a.act, d[j], u[j], a.alpha, a.limit));
                     }
                 } else {
+                    float *ybase = a.seg_y ? a.seg_y[e] : a.y_out + (size_t)seg * a.Mrows;
 #pragma unroll
                     for (int j = 0; j < 16; ++j) {
                         const int n = nt * PF_BN + c0 + j;
-                        if (fok && n < n_rows) a.y_out[(size_t)(seg + n) * a.Mrows + f] = d[j];
+                        if (fok && n < n_rows) ybase[(size_t)n * a.Mrows + f] = d[j];
                     }
                 }
             }
+            if (MODE == 1 && a.seg_y) __threadfence_system();  // peer stores performed
             tc::fence_before_sync();
             __syncwarp();
             if (lane == 0) tc::bar_arrive(&acc_empty[ab]);
@@ -730,13 +748,15 @@ __global__ void __launch_bounds__(pf4_cfg<MODE, WT>::THREADS, 1)
                                 __half_as_ushort(__float2half_rn(act_fn(a.act, d[j], u[j], a.alpha, a.limit)));
                     }
                 } else {
+                    float *ybase = a.seg_y ? a.seg_y[e] : a.y_out + (size_t)seg * a.Mrows;
 #pragma unroll
                     for (int j = 0; j < 16; ++j) {
                         const int n = nt * PF_BN + c0 + j;
-                        if (fok && n < n_rows) a.y_out[(size_t)(seg + n) * a.Mrows + f] = d[j];
+                        if (fok && n < n_rows) ybase[(size_t)n * a.Mrows + f] = d[j];
                     }
                 }
             }
+            if (MODE == 1 && a.seg_y) __threadfence_system();  // peer stores performed
             tc::fence_before_sync();
             __syncwarp();
             if (lane == 0) tc::bar_arrive(&acc_empty[ab]);
@@ -858,6 +878,12 @@ struct moearc_x_prefill {
     uint8_t *w4 = nullptr, *w4gu = nullptr, *w4dn = nullptr;
     bool mode4 = false;
     int *elist = nullptr;  // [E] device copy of a load list
+    // peer-memory exchange: destination row pointers and bases per rank, y pointers per segment
+    uint16_t **dst_rows = nullptr;
+    int *dst_base = nullptr;
+    float **seg_y = nullptr;
+    const uint16_t *route_x = nullptr;  // the activations of the last route_begin call
+    int route_T = 0;
 };
 
 namespace {
@@ -951,6 +977,7 @@ moearc_x_prefill *moearc_x_prefill_create(moearc_ctx *c, const moearc_x_moe_desc
     const size_t o_toff = take(sizeof(int) * (p->E + 1)), o_cur = take(sizeof(int) * (p->E + 1));
     const size_t o_perm = take(sizeof(int) * rows), o_st = take(sizeof(int));
     const size_t o_seg = take(sizeof(int) * 7 * 1025);
+    const size_t o_ptrs = take(sizeof(void *) * (1024 + 1024) + sizeof(int) * 1024);
     const size_t o_xp = take(2 * rows * p->H), o_act = take(2 * rows * p->I);
     if (cudaMalloc(&p->mem, off) != cudaSuccess) {
         cudaGetLastError();
@@ -975,6 +1002,9 @@ moearc_x_prefill *moearc_x_prefill_create(moearc_ctx *c, const moearc_x_moe_desc
     p->seg_cur = p->seg_w + 1025;
     p->epos = p->seg_cur + 1025;
     p->elist = p->epos + 1025;
+    p->dst_rows = reinterpret_cast<uint16_t **>(b + o_ptrs);
+    p->seg_y = reinterpret_cast<float **>(b + o_ptrs + sizeof(void *) * 1024);
+    p->dst_base = reinterpret_cast<int *>(b + o_ptrs + sizeof(void *) * 2048);
     p->xp = reinterpret_cast<uint16_t *>(b + o_xp);
     p->actb = reinterpret_cast<uint16_t *>(b + o_act);
     const bool ok = make_map(&p->map_xp, p->xp, (long)rows, p->H) &&
@@ -1156,7 +1186,7 @@ int prefill_forward(moearc_x_prefill *p, const uint16_t *x, unsigned n_tokens, c
     mark(3);
     const long pairs = (long)T * p->K;
     k_pf_scatter<<<(unsigned)((pairs + 7) / 8), 256, 0, st>>>(x, p->idx, p->epos, T, p->K, p->H, p->off, p->cursor,
-                                                              p->perm, p->xp, p->mode4 ? 1 : 0);
+                                                              p->perm, p->xp, p->mode4 ? 1 : 0, nullptr, nullptr, 0);
     mark(4);
     pf_gemm_args g{};
     g.E = p->E;
@@ -1238,7 +1268,7 @@ int moearc_x_prefill_route(moearc_x_prefill *p, const uint16_t *x, unsigned n_to
     k_pf_scan<<<1, 1024, 0, st>>>(p->cnt, p->E, p->off, p->toff, p->cursor);
     const long pairs = (long)T * p->K;
     k_pf_scatter<<<(unsigned)((pairs + 7) / 8), 256, 0, st>>>(x, p->idx, p->epos, T, p->K, p->H, p->off, p->cursor,
-                                                              p->perm, p->xp, p->mode4 ? 1 : 0);
+                                                              p->perm, p->xp, p->mode4 ? 1 : 0, nullptr, nullptr, 0);
     return cudaGetLastError() == cudaSuccess ? OK : ERR;
 }
 
@@ -1289,6 +1319,131 @@ int moearc_x_prefill_experts(moearc_x_prefill *p, const uint16_t *rows_in, unsig
     g.K = p->I;
     if (launch_gemm(p, 1, g, map_act) != OK) return ERR;
     return ls.finish();
+}
+
+// ---- expert parallelism over peer memory ----------------------------------------------------
+//
+// The exchange without a collective library: route_begin counts the rows per position; once the
+// counts of every rank are known (the caller all-gathers them), route_dispatch's scatter stores
+// each row straight into the receive buffer of the rank that owns it (peer memory, opened with
+// moearc_x_ipc_open), and experts_to's down GEMM stores each result row straight into the
+// y buffer of the rank it came from, at the row that rank's combine reads. The caller
+// synchronises the ranks between the three steps (every rank's stream done, then a barrier).
+
+int moearc_x_prefill_route_begin(moearc_x_prefill *p, const uint16_t *x, unsigned n_tokens, const float *router_w,
+                                 const float *router_b) {
+    if (!p || !x || !router_w) return ERR;
+    if ((int)n_tokens > p->T_max) return ERR_ARG;
+    if ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(router_w)) & 15) return ERR_ARG;
+    p->route_x = x;
+    p->route_T = (int)n_tokens;
+    cudaStream_t st = p->c->stream;
+    if (cudaMemsetAsync(p->cnt, 0, sizeof(int) * (p->E + 1), st) != cudaSuccess) return ERR;
+    if (n_tokens == 0) return OK;
+    const int T = (int)n_tokens;
+    const float *x32 = nullptr;
+    pf_route_args ra{x, x32, router_w, router_b, T, p->H, p->E, p->K, p->gating, p->logits, p->idx, p->wts, p->cnt, p->epos};
+    k_pf_logits<<<(T + PF_LOGIT_TOK - 1) / PF_LOGIT_TOK, 256, PF_LOGIT_TOK * p->H * 4, st>>>(ra);
+    k_pf_topk<<<(T + 7) / 8, 256, 0, st>>>(ra);
+    return cudaGetLastError() == cudaSuccess ? OK : ERR;
+}
+
+// dst_rows[r]: rank r's receive buffer (device or peer pointer, n_embd 16-bit words a row);
+// dst_base[r]: the row of that buffer where this rank's rows start; positions are owner-major,
+// n_local per rank (host arrays of n_ranks entries, n_ranks * n_local == E).
+int moearc_x_prefill_route_dispatch(moearc_x_prefill *p, void *const *dst_rows, const int *dst_base, unsigned n_ranks,
+                                    unsigned n_local) {
+    if (!p || !dst_rows || !dst_base) return ERR;
+    if (n_ranks == 0 || n_ranks > 1024 || n_ranks * n_local != (unsigned)p->E) return ERR_ARG;
+    cudaStream_t st = p->c->stream;
+    if (cudaMemcpyAsync(p->dst_rows, dst_rows, sizeof(void *) * n_ranks, cudaMemcpyHostToDevice, st) != cudaSuccess ||
+        cudaMemcpyAsync(p->dst_base, dst_base, sizeof(int) * n_ranks, cudaMemcpyHostToDevice, st) != cudaSuccess)
+        return ERR;
+    k_pf_scan<<<1, 1024, 0, st>>>(p->cnt, p->E, p->off, p->toff, p->cursor);
+    const long pairs = (long)p->route_T * p->K;
+    if (pairs > 0)
+        k_pf_scatter<<<(unsigned)((pairs + 7) / 8), 256, 0, st>>>(p->route_x, p->idx, p->epos, p->route_T, p->K, p->H,
+                                                                  p->off, p->cursor, p->perm, p->xp, p->mode4 ? 1 : 0,
+                                                                  p->dst_rows, p->dst_base, (int)n_local);
+    if (cudaGetLastError() != cudaSuccess) return ERR;
+    // the host arrays may go once the copies have been made
+    return cudaStreamSynchronize(st) == cudaSuccess ? OK : ERR;
+}
+
+// moearc_x_prefill_experts with segment s's result rows stored to seg_dst[s] (host array of
+// n_seg device or peer pointers, f32 rows of n_embd) instead of y_out.
+int moearc_x_prefill_experts_to(moearc_x_prefill *p, const uint16_t *rows_in, unsigned n_rows, const int *seg_counts,
+                                const int *seg_expert, unsigned n_seg, uint16_t *act_scratch, float *const *seg_dst) {
+    if (!p || !seg_counts || !seg_expert || !seg_dst) return ERR;
+    if (n_seg == 0 || n_seg > 1024) return ERR_ARG;
+    long sum = 0;
+    for (unsigned s = 0; s < n_seg; ++s) {
+        if (seg_counts[s] < 0 || seg_expert[s] < 0 || seg_expert[s] >= p->E) return ERR_ARG;
+        sum += seg_counts[s];
+    }
+    if (sum != (long)n_rows) return ERR_ARG;
+    if (n_rows == 0) return OK;
+    if (!rows_in || !act_scratch) return ERR;
+    if ((reinterpret_cast<uintptr_t>(rows_in) | reinterpret_cast<uintptr_t>(act_scratch)) & 15) return ERR_ARG;
+    if (!p->w16 && !p->w4) return ERR_ARG;
+    moearc_ctx *c = p->c;
+    cudaStream_t st = c->stream;
+    CUtensorMap map_rows, map_act;
+    if (!make_map(&map_rows, rows_in, (long)n_rows, p->H) || !make_map(&map_act, act_scratch, (long)n_rows, p->I))
+        return ERR_ARG;
+    if (cudaMemcpyAsync(p->seg_cnt, seg_counts, sizeof(int) * n_seg, cudaMemcpyHostToDevice, st) != cudaSuccess ||
+        cudaMemcpyAsync(p->seg_w, seg_expert, sizeof(int) * n_seg, cudaMemcpyHostToDevice, st) != cudaSuccess ||
+        cudaMemcpyAsync(p->seg_y, seg_dst, sizeof(float *) * n_seg, cudaMemcpyHostToDevice, st) != cudaSuccess)
+        return ERR;
+    k_pf_scan<<<1, 1024, 0, st>>>(p->seg_cnt, (int)n_seg, p->seg_off, p->seg_toff, p->seg_cur);
+    pf_gemm_args g{};
+    g.E = (int)n_seg;
+    g.off = p->seg_off;
+    g.toff = p->seg_toff;
+    g.seg_w = p->seg_w;
+    g.act = p->act;
+    g.alpha = p->alpha;
+    g.limit = p->limit;
+    g.act_out = act_scratch;
+    g.status = p->status;
+    g.Mrows = p->I;
+    g.K = p->H;
+    if (launch_gemm(p, 0, g, map_rows) != OK) return ERR;
+    g.Mrows = p->H;
+    g.K = p->I;
+    g.seg_y = p->seg_y;
+    if (launch_gemm(p, 1, g, map_act) != OK) return ERR;
+    return cudaStreamSynchronize(st) == cudaSuccess ? OK : ERR;
+}
+
+// Device memory shared between the processes of one node: the 64-byte handle of an allocation
+// (cudaMalloc'd, its start), its mapping in another process, and the mapping's release.
+int moearc_x_ipc_handle(const void *ptr, void *handle) {
+    if (!ptr || !handle) return ERR;
+    cudaIpcMemHandle_t h;
+    if (cudaIpcGetMemHandle(&h, const_cast<void *>(ptr)) != cudaSuccess) {
+        cudaGetLastError();
+        return ERR;
+    }
+    std::memcpy(handle, &h, sizeof(h));
+    return OK;
+}
+
+int moearc_x_ipc_open(const void *handle, void **ptr) {
+    if (!handle || !ptr) return ERR;
+    cudaIpcMemHandle_t h;
+    std::memcpy(&h, handle, sizeof(h));
+    if (cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
+        cudaGetLastError();
+        *ptr = nullptr;
+        return ERR;
+    }
+    return OK;
+}
+
+int moearc_x_ipc_close(void *ptr) {
+    if (!ptr) return ERR;
+    return cudaIpcCloseMemHandle(ptr) == cudaSuccess ? OK : ERR;
 }
 
 // out[t] = residual[t] (if not NULL) + sum_m w[t,m] y[row(t,m)] for the tokens of the last

@@ -71,6 +71,26 @@ def plan(counts_all: np.ndarray, rank: int, world: int) -> dict:
             "seg_expert": seg_expert, "n_recv": int(sum(recv))}
 
 
+def peer_plan(counts_all: np.ndarray, rank: int, world: int) -> dict:
+    """Offsets for the exchange over peer memory, from every rank's per-position counts.
+
+    dst_base[r]  the row of rank r's receive buffer where this rank's rows start (receive
+                 buffers are source-major: all of rank 0's rows, then rank 1's, ...)
+    seg_row[i]   for received segment i (source s, local expert j, source-major): the row of
+                 source s's result buffer where the segment's rows go (the rows its route step
+                 gave position r * n_local + j)
+    plus the segments themselves (as plan()).
+    """
+    counts_all = np.asarray(counts_all, np.int64)
+    p = plan(counts_all, rank, world)
+    nl = p["n_local"]
+    offs = np.concatenate([np.zeros((world, 1), np.int64), np.cumsum(counts_all, axis=1)], axis=1)  # [src][pos]
+    dst_base = [int(sum(counts_all[s, r * nl:(r + 1) * nl].sum() for s in range(rank))) for r in range(world)]
+    seg_row = np.array([offs[s, rank * nl + j] for s in range(world) for j in range(nl)], np.int64)
+    p.update(dst_base=dst_base, seg_row=seg_row)
+    return p
+
+
 class _Dev:
     """A device pointer seen by torch (zero copy) through __cuda_array_interface__."""
 
@@ -159,6 +179,88 @@ class ExpertParallelPrefill:
         dist.all_to_all_single(yb, y, output_split_sizes=pl["send"], input_split_sizes=pl["recv"], group=self.group)
         torch.cuda.synchronize()
         self.pf.combine(yb.data_ptr(), T, out_ptr, residual_ptr)
+        pl["counts_all"] = counts_all
+        self.last = pl
+        return pl
+
+
+class PeerExpertParallelPrefill(ExpertParallelPrefill):
+    """Expert parallelism with the exchange fused into the kernels over NVLink: the route step's
+    scatter stores every row straight into the receive buffer of the rank owning its expert, and
+    the down GEMM's epilogue stores every result row straight back into the y buffer of the rank
+    it came from (peer memory opened through CUDA IPC). Only the per-position counts travel by
+    all-gather; the ranks meet at two barriers per block (after the dispatch, after the experts)."""
+
+    def __init__(self, ctx, group, n_embd, n_ff, n_expert, k, gating, act, wtype, max_tokens, max_rows):
+        super().__init__(ctx, group, n_embd, n_ff, n_expert, k, gating, act, wtype, max_tokens, max_rows)
+        import ctypes as C
+
+        torch, dist = self.torch, self.dist
+        lib = ctx.lib
+        self._recv = ctx.alloc(max_rows * n_embd * 2)
+        self._yb = ctx.alloc(max_tokens * k * n_embd * 4)
+        self._act = ctx.alloc(max_rows * n_ff * 2)
+        hs = []
+        for buf in (self._recv, self._yb):
+            h = (C.c_uint8 * 64)()
+            ctx._finish(lib.moearc_x_ipc_handle(buf.ptr, h), "ipc handle")
+            hs.append(bytes(h))
+        mine = torch.tensor(list(hs[0] + hs[1]), dtype=torch.uint8, device="cuda")
+        got = [torch.empty_like(mine) for _ in range(self.world)]
+        dist.all_gather(got, mine, group=group)
+        self.recv_ptrs, self.yb_ptrs, self._opened = [], [], []
+        for r, t in enumerate(got):
+            if r == self.rank:
+                self.recv_ptrs.append(self._recv.ptr)
+                self.yb_ptrs.append(self._yb.ptr)
+                continue
+            b = bytes(t.cpu().tolist())
+            ptrs = []
+            for i in range(2):
+                hb = (C.c_uint8 * 64).from_buffer_copy(b[64 * i:64 * (i + 1)])
+                p = C.c_void_p()
+                ctx._finish(lib.moearc_x_ipc_open(hb, C.byref(p)), "ipc open")
+                ptrs.append(p.value)
+                self._opened.append(p.value)
+            self.recv_ptrs.append(ptrs[0])
+            self.yb_ptrs.append(ptrs[1])
+
+    def close(self) -> None:
+        for p in self._opened:
+            self.ctx.lib.moearc_x_ipc_close(p)
+        self._opened = []
+        super().close()
+
+    def forward(self, x_bf16, n_tokens: int, router_w, out_ptr: int, router_b=None, residual_ptr=None) -> dict:
+        import ctypes as C
+
+        torch, dist, lib = self.torch, self.dist, self.ctx.lib
+        T, H = n_tokens, self.H
+        ptr = x_bf16 if isinstance(x_bf16, int) else x_bf16.ptr
+        self.ctx._finish(lib.moearc_x_prefill_route_begin(self.pf.h, ptr, T, router_w.ptr,
+                                                          None if router_b is None else router_b.ptr), "route_begin")
+        counts = self.pf.buffer(3, np.int32, self.E)
+        mine = torch.from_numpy(counts.astype(np.int64)).cuda()
+        gathered = [torch.empty_like(mine) for _ in range(self.world)]
+        dist.all_gather(gathered, mine, group=self.group)
+        counts_all = torch.stack(gathered).cpu().numpy()
+        pl = peer_plan(counts_all, self.rank, self.world)
+        if pl["n_recv"] > self.max_rows:
+            raise ValueError(f"rank {self.rank} would receive {pl['n_recv']} rows > max_rows {self.max_rows}")
+        dst = (C.c_void_p * self.world)(*self.recv_ptrs)
+        base = np.ascontiguousarray(pl["dst_base"], np.int32)
+        self.ctx._finish(lib.moearc_x_prefill_route_dispatch(self.pf.h, dst, base.ctypes.data, self.world, self.nl),
+                         "route_dispatch")
+        dist.barrier(group=self.group)  # every rank's rows have landed
+        seg_dst = (C.c_void_p * len(pl["seg_row"]))(
+            *[self.yb_ptrs[i // self.nl] + int(row) * H * 4 for i, row in enumerate(pl["seg_row"])])
+        sc = np.ascontiguousarray(pl["seg_counts"], np.int32)
+        se = np.ascontiguousarray(pl["seg_expert"], np.int32)
+        self.ctx._finish(lib.moearc_x_prefill_experts_to(self.pf.h, self._recv.ptr, pl["n_recv"], sc.ctypes.data,
+                                                         se.ctypes.data, len(sc), self._act.ptr, seg_dst),
+                         "experts_to")
+        dist.barrier(group=self.group)  # every result row is home
+        self.pf.combine(self._yb.ptr, T, out_ptr, residual_ptr)
         pl["counts_all"] = counts_all
         self.last = pl
         return pl

@@ -82,3 +82,22 @@ def test_plan_over_two_gloo_ranks():
         p.join(timeout=60)
     for rank, ok, n_recv, want in res:
         assert ok and n_recv == want, rank
+
+
+def test_peer_plan_offsets():
+    """The peer-memory offsets: a source's rows start in every receiver after all lower sources'
+    rows, and each received segment's results go to the rows its source's route step used."""
+    from moearc_b200.ep import peer_plan
+
+    rng = np.random.default_rng(9)
+    world, E = 4, 32
+    nl = E // world
+    counts = rng.integers(0, 20, size=(world, E))
+    plans = [peer_plan(counts, r, world) for r in range(world)]
+    for r in range(world):
+        recv_starts = np.concatenate([[0], np.cumsum(plans[r]["recv"])])[:-1]
+        for s in range(world):
+            assert plans[s]["dst_base"][r] == recv_starts[s]
+        for i, row in enumerate(plans[r]["seg_row"]):
+            s, j = divmod(i, nl)
+            assert row == counts[s, :r * nl + j].sum()

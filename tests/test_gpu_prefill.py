@@ -273,3 +273,61 @@ def test_4bit_weights_match_the_oracle(ctx, wtype):
     assert err <= 1e-2
     pf.close()
     packer.close()
+
+
+@pytest.mark.parametrize("world", [2, 4])
+def test_peer_memory_exchange_gives_the_same_bits(ctx, world):
+    """The exchange fused into the kernels (moearc_x_prefill_route_begin / _route_dispatch /
+    _experts_to): each virtual rank's scatter stores its rows straight into the owners' receive
+    buffers and each owner's down GEMM stores the results straight into the sources' y buffers.
+    Here the 'peer' buffers are other virtual ranks' buffers on the same GPU, so the addressing of
+    both legs is checked against the single-GPU block, bit for bit, with a balanced placement."""
+    import ctypes as C
+
+    from moearc_b200.ep import balanced, peer_plan, positions
+
+    H, I, E, k, T = 1024, 512, 32, 4, 600
+    whole, packer, host = build(ctx, H, I, E, k, 2, 1, O.MXFP4, T, 0x9F61)
+    xb = O.synth_normal_bf16(0x9F62, T * H, 1.0)
+    rw = ctx.upload_new(host[3])
+    ref = ctx.alloc_n(np.float32, T * H)
+    whole.forward(ctx.upload_new(xb), T, rw, ref)
+    want = ctx.download(ref, np.float32, T * H).reshape(T, H)
+    Tr, nl = T // world, E // world
+    lists = balanced(whole.buffer(3, np.int32, E), world)
+    pos = positions(lists)
+    lib = ctx.lib
+    ranks = []
+    for r in range(world):
+        pf = MoePrefill(ctx, H, I, E, k, 2, 1, O.MXFP4, max_tokens=Tr)
+        pf.set_order(pos)
+        pf.load_list(packer.gateup, packer.down, lists[r])
+        x = ctx.upload_new(xb[r * Tr * H:(r + 1) * Tr * H])
+        recv = ctx.alloc(T * k * H * 2)
+        yb = ctx.alloc(Tr * k * H * 4)
+        act = ctx.alloc(T * k * I * 2)
+        ctx._finish(lib.moearc_x_prefill_route_begin(pf.h, x.ptr, Tr, rw.ptr, None), "route_begin")
+        ranks.append(dict(pf=pf, x=x, recv=recv, yb=yb, act=act, counts=pf.buffer(3, np.int32, E)))
+    counts_all = np.stack([d["counts"] for d in ranks])
+    plans = [peer_plan(counts_all, r, world) for r in range(world)]
+    dst = (C.c_void_p * world)(*[d["recv"].ptr for d in ranks])
+    for r, d in enumerate(ranks):
+        base = np.ascontiguousarray(plans[r]["dst_base"], np.int32)
+        ctx._finish(lib.moearc_x_prefill_route_dispatch(d["pf"].h, dst, base.ctypes.data, world, nl), "dispatch")
+    for r, d in enumerate(ranks):
+        pl = plans[r]
+        seg_dst = (C.c_void_p * len(pl["seg_row"]))(
+            *[ranks[i // nl]["yb"].ptr + int(row) * H * 4 for i, row in enumerate(pl["seg_row"])])
+        sc = np.ascontiguousarray(pl["seg_counts"], np.int32)
+        se = np.ascontiguousarray(pl["seg_expert"], np.int32)
+        ctx._finish(lib.moearc_x_prefill_experts_to(d["pf"].h, d["recv"].ptr, pl["n_recv"], sc.ctypes.data,
+                                                    se.ctypes.data, len(sc), d["act"].ptr, seg_dst), "experts_to")
+    for s, d in enumerate(ranks):
+        out = ctx.alloc_n(np.float32, Tr * H)
+        d["pf"].combine(d["yb"].ptr, Tr, out.ptr)
+        got = ctx.download(out, np.float32, Tr * H).reshape(Tr, H)
+        assert np.array_equal(got.view(np.uint32), want[s * Tr:(s + 1) * Tr].view(np.uint32)), (world, s)
+        assert d["pf"].status() == 0
+        d["pf"].close()
+    whole.close()
+    packer.close()
