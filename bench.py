@@ -369,7 +369,7 @@ def prefill_ep_bench(args, rank: int, world: int) -> dict:
     import torch.distributed as dist
 
     from moearc_b200 import Context
-    from moearc_b200.ep import ExpertParallelPrefill
+    from moearc_b200.ep import ExpertParallelPrefill, PeerExpertParallelPrefill
     from moearc_b200.moe import MoeLayer
 
     dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300))
@@ -392,7 +392,8 @@ def prefill_ep_bench(args, rank: int, world: int) -> dict:
     packer.pack(*banks)
     for b in banks:
         b.free()
-    ep = ExpertParallelPrefill(ctx, None, H, I, E, k, 2, 1, 39, max_tokens=T, max_rows=args.tokens * k)
+    cls = PeerExpertParallelPrefill if args.exchange == "peer" else ExpertParallelPrefill
+    ep = cls(ctx, None, H, I, E, k, 2, 1, 39, max_tokens=T, max_rows=args.tokens * k)
     ep.load(packer.gateup, packer.down)
     x = ctx.alloc(T * H * 2)
     ctx._finish(lib.moearc_x_synth(ctx.raw, x.ptr, T * H, 1, 0x9F08 + rank, 1.0, 0, 0), "synth")
@@ -436,8 +437,10 @@ def prefill_main(args) -> None:
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
             "dtype": "bf16 operands, f32 accumulate", "data": "synthetic (as the 1-GPU prefill line)",
             "config": {"workload": f"configs[3] MoE block: {T} tokens, {r['E']} experts top-4, {r['E'] // world} per GPU, "
-                                   "dispatch and combine by NCCL all-to-all; experts placed by the popularity of one "
-                                   "warm-up step", "max_rows_on_a_rank": r["max_rows"], "rows_total": r["rows_total"],
+                                   + ("rows stored into the owners' buffers by the route scatter and results back by "
+                                      "the down GEMM epilogue over NVLink peer memory" if args.exchange == "peer" else
+                                      "dispatch and combine by NCCL all-to-all")
+                                   + "; experts placed by the popularity of one warm-up step", "max_rows_on_a_rank": r["max_rows"], "rows_total": r["rows_total"],
                        "parallelism": f"ep{world}"},
         }
         print(json.dumps(line))
@@ -568,6 +571,8 @@ def main() -> None:
     ap.add_argument("--depth", type=int, default=0)
     ap.add_argument("--config", default="120b", choices=["120b", "20b", "prefill", "qwen3"])
     ap.add_argument("--batch", type=int, default=64, help="qwen3: concurrent streams (configs[4]: 64)")
+    ap.add_argument("--exchange", default="peer", choices=["peer", "nccl"],
+                    help="prefill on several GPUs: rows exchanged by the kernels over peer memory, or NCCL all-to-all")
     ap.add_argument("--weights", default="bf16", choices=["4bit", "bf16"],
                     help="prefill: expert weights staged at 4 bits (expanded in shared memory) or expanded to bf16")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
