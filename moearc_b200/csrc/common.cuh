@@ -166,6 +166,15 @@ static __device__ unsigned long long *g_trace;
             g_trace[(size_t)(trace_row) * 32 + (slot)] = t_;                             \
         }                                                                                \
     } while (0)
+// TRACE_WARP(slot): the same for lane 0 of every warp (slot chosen per warp by the caller)
+#define TRACE_WARP(slot)                                                                 \
+    do {                                                                                 \
+        if ((threadIdx.x & 31) == 0 && g_trace) {                                        \
+            unsigned long long t_;                                                       \
+            asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t_));                      \
+            g_trace[(size_t)(trace_row) * 32 + (slot)] = t_;                             \
+        }                                                                                \
+    } while (0)
 #define TRACE_SETTER(unit)                                                               \
     extern "C" int moearc_trace_set_##unit(void *p) {                                    \
         unsigned long long *v = static_cast<unsigned long long *>(p);                     \
@@ -174,6 +183,9 @@ static __device__ unsigned long long *g_trace;
 #else
 #define TRACE(slot) \
     do {            \
+    } while (0)
+#define TRACE_WARP(slot) \
+    do {                 \
     } while (0)
 #define TRACE_SETTER(unit)
 #endif

@@ -53,8 +53,10 @@ struct moearc_x_moe {
     int warps_dn, ranges_dn, tpr_dn, stages_dn, stage_dn, smem_dn, grid_dn;
     // decode path (T_max * K <= MAX_TK columns): k_xroute + k_xexpert
     bool xpath;
-    int x_grid, x_warps, x_route_grid, x_route_smem, x_ch_gu, x_ch_dn, x_stage_gu, x_stage_dn, x_ntok, x_maxc;
-    float *x_part_gu, *x_part_dn;
+    int x_grid, x_warps, x_route_grid, x_route_smem, x_ch_gu, x_ch_dn, x_stage_gu, x_stage_dn, x_ntok;
+    float *x_part_gu, *x_part_dn;  // expert kernels' piece partials (PART_EMPTY when idle)
+    size_t x_part_gu_n, x_part_dn_n;
+    float *f_part_gu, *f_part_dn;  // the opt-in fused kernels' (arrival counters instead)
     unsigned *x_ctr_gu, *x_ctr_dn;
     // the fused decode kernel (k_moe_fused): one cooperative launch per layer
     bool fused;
@@ -736,6 +738,7 @@ constexpr int XSTAGES = 3;     // ring stages per warp
 constexpr int MAX_TK = 32;     // columns (token, expert choices) of the decode path
 constexpr int XREC_GU = 2 * 16 * GROUP;  // floats in one gate-up partial (gate, up x 16 rows x 4 cols)
 constexpr int XREC_DN = 16 * GROUP;      // floats in one down partial
+constexpr int XREC_XDN = 4 * 8 * GROUP;  // the expert kernel's down partial: 4 accumulators a lane
 constexpr int XROUTE_WARPS = 4;
 constexpr int XMAX_PIECES = 24;          // pieces per segment (k-extent / piece length)
 constexpr int XMAX_K = 8;                // experts per token the decode path's combine unrolls
@@ -943,14 +946,95 @@ struct xexp_args {
     const float *residual;
     float *out;
     int H;
-    float *part;
-    unsigned *ctr;
-    int maxc;
+    float *part;              // piece partials, PART_EMPTY where none is pending
     int by_slot;              // bank holds one expert per slot (staged offload), not all experts
     int *status;
 };
 
 __device__ __forceinline__ int xcta(long P, long NW, long p) { return (int)(((p + 1) * NW - 1) / P); }
+
+// A partial slot of the expert kernels holds PART_EMPTY until its piece stores the partial, and
+// is set back to PART_EMPTY by the warp that reads it, so a finished buffer is all PART_EMPTY
+// again. The pattern is a NaN that no arithmetic produces (results that are NaN carry the
+// canonical 0x7FFFFFFF). Slots are written and polled with relaxed gpu-scope accesses.
+constexpr uint32_t PART_EMPTY = 0xFFC0DEADu;
+constexpr unsigned long long XPOLL_NS = 200000000ull;  // a poll on other warps gives up after 0.2 s
+
+__device__ __forceinline__ uint4 ld_part4(const float *p) {
+    uint4 v;
+    asm volatile("ld.relaxed.gpu.global.v4.b32 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                 : "l"(p)
+                 : "memory");
+    return v;
+}
+__device__ __forceinline__ void st_part4(float *p, float x, float y, float z, float w) {
+    asm volatile("st.relaxed.gpu.global.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(p), "f"(x), "f"(y), "f"(z), "f"(w)
+                 : "memory");
+}
+// Set the first used4 float4s of nrec consecutive records (rec floats apart) back to PART_EMPTY,
+// whole sectors, the warp's lanes striding.
+__device__ __forceinline__ void empty_recs(float *p, int nrec, int rec, int used4, int lane) {
+    for (int i = lane; i < nrec * used4; i += 32) {
+        const int r = i / used4, k = i - r * used4;
+        asm volatile("st.relaxed.gpu.global.v4.b32 [%0], {%1, %1, %1, %1};" ::"l"(p + (size_t)r * rec + k * 4),
+                     "r"(PART_EMPTY)
+                     : "memory");
+    }
+}
+__device__ __forceinline__ unsigned long long xnow() {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+// The np piece partials of one (record run, float4): pieces seg * np .. + np - 1, rec floats
+// apart, the float4 at offset off of each; read as soon as every one has been stored and summed
+// in piece order from 0, per component (sum[0..3]) or, PAIR, per pair (sum[0] = x + y, sum[1] =
+// z + w). False (and STATUS_WAIT_TIMEOUT) when a piece does not arrive within XPOLL_NS.
+template <bool PAIR>
+__device__ bool take_quads(const float *part, int rec, int np, int seg, int off, float (&sum)[4], int *status,
+                           int *rounds = nullptr) {
+    uint4 v[XMAX_PIECES];
+    unsigned long long t0 = 0;
+    for (;;) {
+        if (rounds) ++*rounds;
+        // every load issued before any is looked at; the check has no branch per value
+#pragma unroll
+        for (int j = 0; j < XMAX_PIECES; ++j)
+            v[j] = j < np ? ld_part4(part + ((size_t)seg * np + j) * rec + off) : make_uint4(0u, 0u, 0u, 0u);
+        uint32_t empty = 0;
+#pragma unroll
+        for (int j = 0; j < XMAX_PIECES; ++j)
+            empty |= (uint32_t)(v[j].x == PART_EMPTY) | (uint32_t)(v[j].y == PART_EMPTY) |
+                     (uint32_t)(v[j].z == PART_EMPTY) | (uint32_t)(v[j].w == PART_EMPTY);
+        if (!empty) break;
+        const unsigned long long t = xnow();
+        if (t0 == 0) {
+            t0 = t;
+        } else if (t - t0 > XPOLL_NS) {
+            atomicOr(status, STATUS_WAIT_TIMEOUT);
+            return false;
+        }
+    }
+    sum[0] = sum[1] = sum[2] = sum[3] = 0.f;
+#pragma unroll
+    for (int j = 0; j < XMAX_PIECES; ++j)
+        if (j < np) {
+            const float x = __uint_as_float(v[j].x), y = __uint_as_float(v[j].y);
+            const float z = __uint_as_float(v[j].z), w = __uint_as_float(v[j].w);
+            if (PAIR) {
+                sum[0] += x + y;
+                sum[1] += z + w;
+            } else {
+                sum[0] += x;
+                sum[1] += y;
+                sum[2] += z;
+                sum[3] += w;
+            }
+        }
+    return true;
+}
 
 template <int WT, int MODE>
 __global__ void __launch_bounds__(XW * 32, 1) k_xexpert(xexp_args a) {
@@ -1079,7 +1163,7 @@ __global__ void __launch_bounds__(XW * 32, 1) k_xexpert(xexp_args a) {
     // consume: lane (r = lane / 4, q = lane % 4) holds rows r, r + 8 of column q; B column
     // n = lane / 4 is token n / 2, part n % 2
     const int r = lane >> 2, qd = lane & 3;
-    const int rec = MODE == 0 ? XREC_GU : XREC_DN;
+    const int rec = MODE == 0 ? XREC_GU : XREC_XDN;
     cur cc = start;
     long k = 0, kf = -1;
     while (cc.q < qb) {
@@ -1108,15 +1192,17 @@ __global__ void __launch_bounds__(XW * 32, 1) k_xexpert(xexp_args a) {
             step(ic);
             ++n_issued;
         }
-        // the piece's partial: column q = (f16 part + residual part) of rows r and r + 8
+        // the piece's partial of column q and rows r, r + 8, laid [column][r][4] so the columns
+        // in use fill whole 128-byte lines: gate-up stores the sums (f16 part + residual part)
+        // of gate r, gate r + 8, up r, up r + 8; down stores its four accumulators (row r is
+        // [0] + [1], row r + 8 is [2] + [3], added by the reader)
         float *pr = a.part + (size_t)cc.q * rec;  // piece q = segment * np + j
         if (qd < ntok) {
-            pr[r * GROUP + qd] = acc0[0] + acc0[1];
-            pr[(r + 8) * GROUP + qd] = acc0[2] + acc0[3];
-            if (MATS == 2) {
-                pr[64 + r * GROUP + qd] = acc1[0] + acc1[1];
-                pr[64 + (r + 8) * GROUP + qd] = acc1[2] + acc1[3];
-            }
+            if (MATS == 2)
+                st_part4(pr + (qd * 8 + r) * 4, acc0[0] + acc0[1], acc0[2] + acc0[3], acc1[0] + acc1[1],
+                         acc1[2] + acc1[3]);
+            else
+                st_part4(pr + (qd * 8 + r) * 4, acc0[0], acc0[1], acc0[2], acc0[3]);
         }
         step(cc);
     }
@@ -1129,123 +1215,124 @@ __global__ void __launch_bounds__(XW * 32, 1) k_xexpert(xexp_args a) {
     }
     if (qb <= qa) return;
     TRACE(10);
-    fence_acq_rel_gpu();
-    __syncwarp();
-    // arrivals: gate-up one per segment touched; down one per tile-row, counting the segments
-    // of that tile-row this warp touched. The warps on a segment are a contiguous run.
-    auto seg_warps = [&](long s) {
-        if (Q < NW) return (unsigned)np;  // fewer pieces than warps: one warp per piece
-        return (unsigned)(xcta(Q, NW, (s + 1) * np - 1) - xcta(Q, NW, s * np) + 1);
-    };
-    const int seg_first = (int)(qa / np), seg_last = (int)((qb - 1) / np);
-    const int u_first = MODE == 0 ? seg_first : seg_first / G, u_last = MODE == 0 ? seg_last : seg_last / G;
-    bool mine = false;
-    if (lane <= u_last - u_first) {
-        const int u = u_first + lane;
-        unsigned target = 0, inc = 0;
+    TRACE_WARP(14 + warp);
+    // This warp finishes the units (gate-up: segment; down: tile-row) whose last piece lies in
+    // its run, reading every piece's partial as soon as it has landed: no arrival count and no
+    // fence stand between the last piece and the unit's result.
+    const long upc = MODE == 0 ? (long)np : (long)G * np;  // pieces per unit
+    const int u_lo = (int)((qa + upc) / upc) - 1, u_hi = (int)(qb / upc) - 1;
+    if (u_lo > u_hi) return;
+#ifdef MOEARC_TRACE
+    int n_rounds = 0;
+#define TRACE_ROUNDS (&n_rounds)
+    if (lane == 0 && g_trace) atomicMax(&g_trace[(size_t)trace_row * 32 + 9], xnow());
+#else
+#define TRACE_ROUNDS nullptr
+#endif
+    for (int u = u_lo; u <= u_hi; ++u) {
+        bool failed = false;
         if (MODE == 0) {
-            target = seg_warps(u);
-            inc = 1;
-        } else {
-            for (int gg = 0; gg < G; ++gg) {
-                const int s = u * G + gg;
-                target += seg_warps(s);
-                if (s >= seg_first && s <= seg_last) ++inc;
-            }
-        }
-        const unsigned old = atomicAdd(a.ctr + u, inc);
-        if (old + inc == target) {
-            mine = true;
-            a.ctr[u] = 0;
-        }
-    }
-    unsigned done_mask = __ballot_sync(0xffffffffu, mine);
-    if (!done_mask) return;
-    fence_acq_rel_gpu();
-    TRACE(11);
-    // a segment's pieces summed in piece order; the loads are all issued before the adds
-    auto sum_seg = [&](int s, int off) {
-        const float *pp = a.part + (size_t)s * np * rec + off;
-        float t[XMAX_PIECES];
-#pragma unroll
-        for (int j = 0; j < XMAX_PIECES; ++j) t[j] = (j < np) ? __ldcg(pp + (size_t)j * rec) : 0.f;
-        float v = 0.f;
-#pragma unroll
-        for (int j = 0; j < XMAX_PIECES; ++j)
-            if (j < np) v += t[j];
-        return v;
-    };
-    // two sums of one segment (gate and up) with all loads issued before any add
-    auto sum_seg2 = [&](int s, int off0, int off1, float &v0, float &v1) {
-        const float *pp = a.part + (size_t)s * np * rec;
-        float t0[XMAX_PIECES], t1[XMAX_PIECES];
-#pragma unroll
-        for (int j = 0; j < XMAX_PIECES; ++j) {
-            t0[j] = (j < np) ? __ldcg(pp + (size_t)j * rec + off0) : 0.f;
-            t1[j] = (j < np) ? __ldcg(pp + (size_t)j * rec + off1) : 0.f;
-        }
-        v0 = 0.f;
-        v1 = 0.f;
-#pragma unroll
-        for (int j = 0; j < XMAX_PIECES; ++j)
-            if (j < np) {
-                v0 += t0[j];
-                v1 += t1[j];
-            }
-    };
-    while (done_mask) {
-        const int u = u_first + __ffs(done_mask) - 1;
-        done_mask &= done_mask - 1;
-        if (MODE == 0) {
-            // gate-up segment (group g, tile-row tr): the activation of 16 rows x ntok columns
+            // gate-up segment (group g, tile-row tr): the activation of 16 rows x ntok columns;
+            // lane t * 8 + r takes column t, rows r and r + 8 (one float4 a piece)
             const int g = u / ntr, tr = u % ntr;
             const int ntok = tb.grp_ntok[g], col0 = tb.grp_col0[g];
             const int nblk_i = a.I / 32;
-            for (int e = lane; e < 16 * ntok; e += 32) {
-                const int rr = e & 15, t = e >> 4;
-                float gs, us;
-                sum_seg2(u, rr * GROUP + t, 64 + rr * GROUP + t, gs, us);
-                const int col = col0 + t, row = tr * 16 + rr;
-                const float v = act_fn(a.act, gs, us, a.alpha, a.limit);
-                a.act_out[(size_t)col * a.I + row] = v;
-                const __half hh = __float2half_rn(v);
-                const __half hl = __float2half_rn(v - __half2float(hh));
-                // element el of block blk sits in pair j = el & 3 of lane q = (el & 15) >> 2, in
-                // the low half for el < 16 and the high half for el >= 16
-                const int blk = row / 32, el = row % 32;
-                const int qq = (el & 15) >> 2, jj = el & 3, half = el >> 4;
-                const size_t ihi = ((((size_t)col * nblk_i + blk) * 2 + 0) * 4 + qq) * 4 + jj;
-                const size_t ilo = ((((size_t)col * nblk_i + blk) * 2 + 1) * 4 + qq) * 4 + jj;
-                reinterpret_cast<uint16_t *>(a.actfrag + ihi)[half] = __half_as_ushort(hh);
-                reinterpret_cast<uint16_t *>(a.actfrag + ilo)[half] = __half_as_ushort(hl);
+            for (int e = lane; e < 8 * ntok; e += 32) {
+                const int r = e & 7, t = e >> 3;
+                float gu[4];  // gate r, gate r + 8, up r, up r + 8
+                if (!take_quads<false>(a.part, rec, np, u, e * 4, gu, a.status, TRACE_ROUNDS)) {
+                    failed = true;
+                    break;
+                }
+                const int col = col0 + t;
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
+                    const int row = tr * 16 + r + 8 * h;
+                    const float v = act_fn(a.act, gu[h], gu[2 + h], a.alpha, a.limit);
+                    a.act_out[(size_t)col * a.I + row] = v;
+                    const __half hh = __float2half_rn(v);
+                    const __half hl = __float2half_rn(v - __half2float(hh));
+                    // element el of block blk sits in pair j = el & 3 of lane q = (el & 15) >> 2, in
+                    // the low half for el < 16 and the high half for el >= 16
+                    const int blk = row / 32, el = row % 32;
+                    const int qq = (el & 15) >> 2, jj = el & 3, half = el >> 4;
+                    const size_t ihi = ((((size_t)col * nblk_i + blk) * 2 + 0) * 4 + qq) * 4 + jj;
+                    const size_t ilo = ((((size_t)col * nblk_i + blk) * 2 + 1) * 4 + qq) * 4 + jj;
+                    reinterpret_cast<uint16_t *>(a.actfrag + ihi)[half] = __half_as_ushort(hh);
+                    reinterpret_cast<uint16_t *>(a.actfrag + ilo)[half] = __half_as_ushort(hl);
+                }
             }
+            if (__any_sync(0xffffffffu, failed)) return;
+#ifdef MOEARC_TRACE
+            {
+                const int mr = __reduce_max_sync(0xffffffffu, n_rounds);
+                if (lane == 0 && g_trace && u == u_lo) {
+                    atomicMax(&g_trace[(size_t)trace_row * 32 + 11], xnow());
+                    atomicMax(&g_trace[(size_t)trace_row * 32 + 13], (unsigned long long)mr);
+                }
+            }
+#endif
+            // the segment's records, the columns in use, back to empty
+            empty_recs(a.part + (size_t)u * np * rec, np, rec, ntok * 8, lane);
         } else {
             // down tile-row tr: per token, the router-weighted sum over its k experts in router
-            // order (moe.rs:2395-2421), plus the residual
+            // order (moe.rs:2395-2421), plus the residual. Lane (t, m, r) sums the outputs of
+            // rows r and r + 8 for token t's m-th expert (one float4 a piece) into this warp's
+            // ring (all its copies have landed), staged [T][16][K]; then per (token, row) the
+            // fmaf chain in router order. The residual of the lane's first (token, row) is
+            // read before the poll.
             const int tr = u;
-            // every (token, row, expert) output of the tile-row on its own lane (one batch of
-            // piece loads each), staged in this warp's ring (all its copies have landed), then
-            // per (token, row) the fmaf chain in router order
-            float *os = reinterpret_cast<float *>(ring);  // [T][16][K]
-            const int n_o = a.T * 16 * a.K;
-            for (int e = lane; e < n_o; e += 32) {
-                const int m = e % a.K, rr = (e / a.K) & 15, t = e / (16 * a.K);
+            float *os = reinterpret_cast<float *>(ring);
+            const int n_q = a.T * a.K * 8;
+            const float res_first = (a.residual && lane < a.T * 16)
+                                        ? a.residual[(size_t)(lane >> 4) * a.H + tr * 16 + (lane & 15)]
+                                        : 0.f;
+            for (int e = lane; e < n_q; e += 32) {
+                const int r = e & 7, m = (e >> 3) % a.K, t = (e >> 3) / a.K;
                 const int col = tb.col_of[t * a.K + m];
                 const int g = tb.col_grp[col];
-                os[e] = sum_seg(tr * G + g, rr * GROUP + (col - tb.grp_col0[g]));
+                float o[4];
+                if (!take_quads<true>(a.part, rec, np, tr * G + g, ((col - tb.grp_col0[g]) * 8 + r) * 4, o, a.status,
+                                      TRACE_ROUNDS)) {
+                    failed = true;
+                    break;
+                }
+                os[(t * 16 + r) * a.K + m] = o[0];
+                os[(t * 16 + r + 8) * a.K + m] = o[1];
             }
+            if (__any_sync(0xffffffffu, failed)) return;
+#ifdef MOEARC_TRACE
+            {
+                const int mr = __reduce_max_sync(0xffffffffu, n_rounds);
+                if (lane == 0 && g_trace && u == u_lo) {
+                    atomicMax(&g_trace[(size_t)trace_row * 32 + 11], xnow());
+                    atomicMax(&g_trace[(size_t)trace_row * 32 + 13], (unsigned long long)mr);
+                }
+            }
+#endif
             __syncwarp();
             for (int e = lane; e < a.T * 16; e += 32) {
                 const int t = e >> 4, rr = e & 15;
                 const size_t oi = (size_t)t * a.H + tr * 16 + rr;
-                const float res = a.residual ? a.residual[oi] : 0.f;
+                const float res = a.residual ? (e == lane ? res_first : a.residual[oi]) : 0.f;
                 float acc = 0.f;
                 for (int m = 0; m < a.K; ++m) acc = fmaf(tb.wts[t * a.K + m], os[e * a.K + m], acc);
                 a.out[oi] = a.residual ? res + acc : acc;
             }
+            // the tile-row's records (every group's, the columns in use) back to empty
+            for (int g = 0; g < G; ++g)
+                empty_recs(a.part + (size_t)(tr * G + g) * np * rec, np, rec, tb.grp_ntok[g] * 8, lane);
             __syncwarp();
         }
     }
+#undef TRACE_ROUNDS
+#ifdef MOEARC_TRACE
+    if (lane == 0 && g_trace) {
+        unsigned long long t_;
+        asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t_));
+        atomicMax(&g_trace[(size_t)trace_row * 32 + 30], t_);
+    }
+#endif
     TRACE(31);
 }
 
@@ -1874,6 +1961,21 @@ int occupancy_grid(moearc_ctx *c, int smem_per_cta) {
     return c->sm_count * per_sm;
 }
 
+__global__ void k_part_fill(uint32_t *p, size_t n) {
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
+        p[i] = PART_EMPTY;
+}
+
+// Every partial slot of the expert kernels back to PART_EMPTY (at creation, and after a wait
+// gave up).
+void x_parts_empty(moearc_x_moe *m) {
+    cudaStream_t st = m->ctx->stream;
+    if (m->x_part_gu_n)
+        k_part_fill<<<m->ctx->sm_count, 256, 0, st>>>(reinterpret_cast<uint32_t *>(m->x_part_gu), m->x_part_gu_n);
+    if (m->x_part_dn_n)
+        k_part_fill<<<m->ctx->sm_count, 256, 0, st>>>(reinterpret_cast<uint32_t *>(m->x_part_dn), m->x_part_dn_n);
+}
+
 }  // namespace
 
 extern "C" {
@@ -1945,7 +2047,6 @@ moearc_x_moe *moearc_x_moe_create(moearc_ctx *c, const moearc_x_moe_desc *d) {
     m->x_ch_dn = 5;
     m->x_stage_gu = round128((long)m->x_ch_gu * 2 * m->tile_bytes + (long)m->x_ntok * m->x_ch_gu * 256);
     m->x_stage_dn = round128((long)m->x_ch_dn * m->tile_bytes + (long)m->x_ntok * m->x_ch_dn * 256);
-    m->x_maxc = 0;  // unused: partials are per piece
     m->x_route_grid = (m->E + XROUTE_WARPS - 1) / XROUTE_WARPS;
     m->x_route_smem = (XROUTE_WARPS + 1) * m->H * 4;
     // 16 warps per CTA when their rings fit (one token: 192 KB for gpt-oss-120b), else 8
@@ -2010,7 +2111,10 @@ moearc_x_moe *moearc_x_moe_create(moearc_ctx *c, const moearc_x_moe_desc *d) {
     const size_t x_segs_gu = (size_t)TK * m->ntr_i, x_segs_dn = (size_t)m->ntr_h * TK;
     const size_t np_gu = (m->nkt_h + m->x_ch_gu - 1) / m->x_ch_gu, np_dn = (m->nkt_i + m->x_ch_dn - 1) / m->x_ch_dn;
     const size_t o_xpg = take(m->xpath ? sizeof(float) * x_segs_gu * np_gu * XREC_GU : 0);
-    const size_t o_xpd = take(m->xpath ? sizeof(float) * x_segs_dn * np_dn * XREC_DN : 0);
+    const size_t o_xpd = take(m->xpath ? sizeof(float) * x_segs_dn * np_dn * XREC_XDN : 0);
+    const bool fz_any = m->fused || m->fused_gd;
+    const size_t o_fpg = take(fz_any ? sizeof(float) * x_segs_gu * np_gu * XREC_GU : 0);
+    const size_t o_fpd = take(fz_any ? sizeof(float) * x_segs_dn * np_dn * XREC_DN : 0);
     const size_t o_xcg = take(m->xpath ? sizeof(unsigned) * x_segs_gu : 0);
     const size_t o_xcd = take(m->xpath ? sizeof(unsigned) * m->ntr_h : 0);
     const size_t o_frd = take(m->xpath ? sizeof(unsigned) * (size_t)TK * np_dn : 0);
@@ -2033,11 +2137,16 @@ moearc_x_moe *moearc_x_moe_create(moearc_ctx *c, const moearc_x_moe_desc *d) {
     m->act_f32 = reinterpret_cast<float *>(b + o_act);
     m->x_part_gu = reinterpret_cast<float *>(b + o_xpg);
     m->x_part_dn = reinterpret_cast<float *>(b + o_xpd);
+    m->x_part_gu_n = m->xpath ? x_segs_gu * np_gu * XREC_GU : 0;
+    m->x_part_dn_n = m->xpath ? x_segs_dn * np_dn * XREC_XDN : 0;
+    m->f_part_gu = reinterpret_cast<float *>(b + o_fpg);
+    m->f_part_dn = reinterpret_cast<float *>(b + o_fpd);
     m->x_ctr_gu = reinterpret_cast<unsigned *>(b + o_xcg);
     m->x_ctr_dn = reinterpret_cast<unsigned *>(b + o_xcd);
     m->f_ready = reinterpret_cast<unsigned *>(b + o_frd);
     m->f_bar = reinterpret_cast<unsigned *>(b + o_fbar);
     cudaMemsetAsync(m->mem, 0, off, c->stream);
+    x_parts_empty(m);
     // per-kernel attribute shared by every layer object: the most any of them may use
     const int smem_attr = 226 * 1024;
     if (set_smem(k_moe_rows<39>, smem_attr) != cudaSuccess ||
@@ -2161,8 +2270,8 @@ int moe_forward_impl(moearc_x_moe *m, const float *x, unsigned n_tokens, const f
         f.wts_out = m->wts;
         f.residual = residual;
         f.out = out;
-        f.part_gu = m->x_part_gu;
-        f.part_dn = m->x_part_dn;
+        f.part_gu = m->f_part_gu;
+        f.part_dn = m->f_part_dn;
         f.ctr_gu = m->x_ctr_gu;
         f.ctr_dn = m->x_ctr_dn;
         f.ready = m->f_ready;
@@ -2230,8 +2339,6 @@ int moe_forward_impl(moearc_x_moe *m, const float *x, unsigned n_tokens, const f
         xa.wts_out = m->wts;
         xa.H = m->H;
         xa.part = m->x_part_gu;
-        xa.ctr = m->x_ctr_gu;
-        xa.maxc = m->x_maxc;
         xa.status = m->status;
         const bool mx = m->wtype == T_MXFP4;
         // More than half an SM's shared memory, so no SM takes two gate-up CTAs: at launch the
@@ -2264,7 +2371,6 @@ int moe_forward_impl(moearc_x_moe *m, const float *x, unsigned n_tokens, const f
         xd.residual = residual;
         xd.out = out;
         xd.part = m->x_part_dn;
-        xd.ctr = m->x_ctr_dn;
         if (launch_pdl(mx ? k_xexpert<39, 1> : k_xexpert<2, 1>, dim3(m->x_grid), dim3(m->x_warps * 32),
                        (size_t)m->x_warps * XSTAGES * m->x_stage_dn, c->stream, xd) != cudaSuccess)
             return ERR;
@@ -2362,7 +2468,11 @@ int moearc_x_moe_status(moearc_x_moe *m) {
     int st = 0;
     if (cudaMemcpyAsync(&st, m->status, sizeof(int), cudaMemcpyDeviceToHost, m->ctx->stream) != cudaSuccess) return ERR;
     if (cudaStreamSynchronize(m->ctx->stream) != cudaSuccess) return ERR;
-    if (st) cudaMemsetAsync(m->status, 0, sizeof(int), m->ctx->stream);
+    if (st) {
+        // a wait that gave up can leave partial slots stored and never read: empty them all
+        cudaMemsetAsync(m->status, 0, sizeof(int), m->ctx->stream);
+        x_parts_empty(m);
+    }
     return st;
 }
 
