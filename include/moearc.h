@@ -320,6 +320,10 @@ int moearc_x_decoder_fill_kv(moearc_x_decoder *d, unsigned int depth, unsigned l
  * captures the step as a CUDA graph (unless disabled) and later calls replay it. */
 int moearc_x_decoder_step(moearc_x_decoder *d);
 int moearc_x_decoder_use_graph(moearc_x_decoder *d, int on);
+/* Reads and clears the device status words of the decoder's kernels: 0, or nonzero when a
+ * bounded wait gave up (the step's output is then invalid). No reference counterpart: the
+ * reference's decode loop has no device-side waits. */
+int moearc_x_decoder_status(moearc_x_decoder *d);
 /* One step without the graph and with an event after every kernel: ms[k] gets the device time
  * of kernel kind k (0 Q/K/V, 1 attention, 2 O projection, 3 MoE route, 4 MoE gate-up, 5 MoE
  * down, 6 final norm, 7 expert fetch of an offloaded block) summed over the blocks, counts[k]

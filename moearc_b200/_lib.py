@@ -110,6 +110,7 @@ SIGNATURES: dict[str, tuple] = {
     "moearc_x_decoder_fill_kv": (I, [P, U, C.c_ulonglong]),
     "moearc_x_decoder_step": (I, [P]),
     "moearc_x_decoder_use_graph": (I, [P, I]),
+    "moearc_x_decoder_status": (I, [P]),
     "moearc_x_decoder_profile": (I, [P, C.POINTER(F), C.POINTER(I), I]),
     "moearc_x_decoder_tensor": (P, [P, I, U, C.POINTER(UL)]),
     "moearc_x_decoder_seed": (C.c_ulonglong, [P, I, U, C.c_ulonglong]),

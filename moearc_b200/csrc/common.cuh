@@ -195,6 +195,54 @@ static __device__ unsigned long long *g_trace;
 // after seeing the count, before it reads them. Cheaper than __threadfence (fence.sc).
 __device__ __forceinline__ void fence_acq_rel_gpu() { asm volatile("fence.acq_rel.gpu;\n" ::: "memory"); }
 
+// ---- partial slots polled by their reader ----------------------------------------------------
+// A partial slot (of the expert and dense decode kernels) holds PART_EMPTY until its producer
+// stores the partial, and is set back to PART_EMPTY by the warp that reads it, so a finished
+// buffer is all PART_EMPTY again. The pattern is a NaN that no arithmetic produces (results that
+// are NaN carry the canonical 0x7FFFFFFF). Slots are written and polled with relaxed gpu-scope
+// accesses, and written in whole 32-byte sectors: a read of a sector that was only partly
+// written waits for the L2 to fill the rest from DRAM.
+constexpr uint32_t PART_EMPTY = 0xFFC0DEADu;
+constexpr unsigned long long XPOLL_NS = 200000000ull;  // a poll on other CTAs gives up after 0.2 s
+
+__device__ __forceinline__ uint32_t ld_part(const float *p) {
+    uint32_t v;
+    asm volatile("ld.relaxed.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ uint4 ld_part4(const float *p) {
+    uint4 v;
+    asm volatile("ld.relaxed.gpu.global.v4.b32 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                 : "l"(p)
+                 : "memory");
+    return v;
+}
+__device__ __forceinline__ void st_part(float *p, float x) {
+    asm volatile("st.relaxed.gpu.global.f32 [%0], %1;" ::"l"(p), "f"(x) : "memory");
+}
+__device__ __forceinline__ void st_part4(float *p, float x, float y, float z, float w) {
+    asm volatile("st.relaxed.gpu.global.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(p), "f"(x), "f"(y), "f"(z), "f"(w)
+                 : "memory");
+}
+// Set the first used4 float4s of nrec consecutive records (rec floats apart) back to PART_EMPTY,
+// whole sectors, the warp's lanes striding.
+__device__ __forceinline__ void empty_recs(float *p, int nrec, int rec, int used4, int lane) {
+    for (int i = lane; i < nrec * used4; i += 32) {
+        const int r = i / used4, k = i - r * used4;
+        asm volatile("st.relaxed.gpu.global.v4.b32 [%0], {%1, %1, %1, %1};" ::"l"(p + (size_t)r * rec + k * 4),
+                     "r"(PART_EMPTY)
+                     : "memory");
+    }
+}
+__device__ __forceinline__ unsigned long long xnow() {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+// Fill n 32-bit words with PART_EMPTY (stream-ordered).
+void parts_empty(float *p, size_t n, cudaStream_t s, int sm_count);
+
 // ---- programmatic dependent launch ---------------------------------------------------------
 // A kernel launched with launch_pdl may begin while the kernel before it in the stream is
 // still running. Everything it does before pdl_wait() must not read that kernel's outputs nor

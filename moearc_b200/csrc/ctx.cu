@@ -69,6 +69,17 @@ void *ctx_scratch(moearc_ctx *c, size_t bytes) {
     return c->scratch;
 }
 
+namespace {
+__global__ void k_parts_empty(uint32_t *p, size_t n) {
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
+        p[i] = PART_EMPTY;
+}
+}  // namespace
+
+void parts_empty(float *p, size_t n, cudaStream_t s, int sm_count) {
+    if (p && n) k_parts_empty<<<sm_count, 256, 0, s>>>(reinterpret_cast<uint32_t *>(p), n);
+}
+
 }  // namespace moearc
 
 extern "C" {

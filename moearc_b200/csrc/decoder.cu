@@ -411,6 +411,13 @@ int moearc_x_decoder_fill_kv(moearc_x_decoder *d, unsigned depth, unsigned long 
     return moearc_x_decoder_set_pos(d, depth);
 }
 
+int moearc_x_decoder_status(moearc_x_decoder *d) {
+    if (!d) return ERR;
+    const int sm = moearc_x_moe_status(d->moe), sq = dense_status(d->qkv), so = dense_status(d->wo);
+    if (sm < 0 || sq < 0 || so < 0) return ERR;
+    return sm | sq | so;
+}
+
 int moearc_x_decoder_use_graph(moearc_x_decoder *d, int on) {
     if (!d) return ERR;
     d->use_graph = on != 0;

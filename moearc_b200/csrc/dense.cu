@@ -77,7 +77,6 @@ __global__ void __launch_bounds__(WARPS * 32, 1) k_dense(dense_args a) {
     __shared__ __align__(8) uint64_t bars[WARPS][STAGES];
     __shared__ float red[WARPS];
     __shared__ int fin[MAX_LOCAL];
-    __shared__ double rfreq[64];
     const int trace_row = (int)blockIdx.x + (a.mode == 0 ? 0 : 1024);
     (void)trace_row;
     TRACE(0);
@@ -123,8 +122,6 @@ __global__ void __launch_bounds__(WARPS * 32, 1) k_dense(dense_args a) {
             nw[m] = __ldg(reinterpret_cast<const float2 *>(a.norm_w + 16 * kb + 2 * q + 8 * reg));
         }
     }
-    if (a.mode == 0)
-        for (int p = threadIdx.x; p < a.rope.head_dim / 2; p += WARPS * 32) rfreq[p] = __ldg(a.rope.freq + p);
     // the position and this step's K/V page: the position advances only at the end of a step,
     // after the last kernel of the step, so both can be read before the wait
     int pos = 0;
@@ -132,6 +129,29 @@ __global__ void __launch_bounds__(WARPS * 32, 1) k_dense(dense_args a) {
     if (a.mode == 0) {
         pos = *a.pos;
         page = a.kv.table[pos / a.kv.page_tokens];
+    }
+    // Warp i finishes the i-th unit this CTA touches if the CTA turns out to be the unit's last
+    // to arrive; for a query or key head the rotations of its RoPE pairs are known now, before
+    // the wait. NeoX RoPE: pairs (d, d + D/2), the lane holding d = lane + 32 i; the angle of
+    // pair p is pos * freq[p] (the YaRN blend folded into freq on the host), reduced by 2 pi in
+    // two steps before the sine and cosine so large positions keep full precision; both
+    // factors carry mscale.
+    const int u0 = tr0 / a.unit_trs, u1 = tr1 / a.unit_trs;
+    double rot_c[2] = {1.0, 1.0}, rot_s[2] = {0.0, 0.0};
+    if (a.mode == 0 && warp <= u1 - u0 && u0 + warp < a.rope.n_q_heads + a.rope.n_kv_heads) {
+#pragma unroll
+        for (int i = 0; i < 2; ++i)
+            if (i < a.rope.head_dim / 64) {
+                const int p = lane + 32 * i;  // pair index < D/2
+                const double th = (double)pos * __ldg(a.rope.freq + p);
+                const double k = rint(th * 0.15915494309189535);
+                double r = fma(-k, 6.283185307179586, th);
+                r = fma(-k, 2.4492935982947064e-16, r);
+                double sn, cs;
+                sincos(r, &sn, &cs);
+                rot_c[i] = cs * a.rope.mscale;
+                rot_s[i] = sn * a.rope.mscale;
+            }
     }
     pdl_trigger();
     pdl_wait();
@@ -270,7 +290,6 @@ __global__ void __launch_bounds__(WARPS * 32, 1) k_dense(dense_args a) {
     fence_acq_rel_gpu();
     __syncthreads();
     // one arrival per unit touched; the CTAs that touch a unit are a contiguous run
-    const int u0 = tr0 / a.unit_trs, u1 = tr1 / a.unit_trs;
     if ((int)threadIdx.x <= u1 - u0) {
         const int u = u0 + threadIdx.x;
         const long first = (long)u * a.unit_trs * a.nkt, last = (long)(u + 1) * a.unit_trs * a.nkt - 1;
@@ -316,22 +335,18 @@ __global__ void __launch_bounds__(WARPS * 32, 1) k_dense(dense_args a) {
     for (int i = 0; i < 4; ++i) v[i] = (i < per) ? row_value(row0 + lane + 32 * i) : 0.f;
     const int hq = a.rope.n_q_heads, hk = a.rope.n_kv_heads;
     if (unit < hq + hk) {
-        // NeoX RoPE: pairs (d, d + D/2); this lane holds d = lane + 32 i. The angle of pair p
-        // is pos * freq[p] (the YaRN blend folded into freq on the host), reduced by 2 pi in
-        // two steps before the sine and cosine so large positions keep full precision.
-        for (int i = 0; i < per / 2; ++i) {
-            const int p = lane + 32 * i;  // pair index < D/2
-            const double th = (double)pos * rfreq[p];
-            const double k = rint(th * 0.15915494309189535);
-            double r = fma(-k, 6.283185307179586, th);
-            r = fma(-k, 2.4492935982947064e-16, r);
-            double sn, cs;
-            sincos(r, &sn, &cs);
-            cs *= a.rope.mscale;
-            sn *= a.rope.mscale;
-            const double x0 = v[i], x1 = v[i + per / 2];
-            v[i] = (float)(x0 * cs - x1 * sn);
-            v[i + per / 2] = (float)(x0 * sn + x1 * cs);
+        // the rotations computed before the wait
+        if (per == 2) {
+            const double x0 = v[0], x1 = v[1];
+            v[0] = (float)(x0 * rot_c[0] - x1 * rot_s[0]);
+            v[1] = (float)(x0 * rot_s[0] + x1 * rot_c[0]);
+        } else {
+#pragma unroll
+            for (int i = 0; i < 2; ++i) {
+                const double x0 = v[i], x1 = v[i + 2];
+                v[i] = (float)(x0 * rot_c[i] - x1 * rot_s[i]);
+                v[i + 2] = (float)(x0 * rot_s[i] + x1 * rot_c[i]);
+            }
         }
     }
     if (unit < hq) {
@@ -428,6 +443,19 @@ dense_gemv *dense_create(moearc_ctx *c, int n_rows, int n_cols, int mode) {
         return nullptr;
     }
     return g;
+}
+
+int dense_status(dense_gemv *g) {
+    int st = 0;
+    if (cudaMemcpyAsync(&st, g->status, sizeof(int), cudaMemcpyDeviceToHost, g->c->stream) != cudaSuccess ||
+        cudaStreamSynchronize(g->c->stream) != cudaSuccess)
+        return ERR;
+    if (st) {
+        // a wait that gave up can leave arrival counts behind: zero them
+        cudaMemsetAsync(g->status, 0, sizeof(int), g->c->stream);
+        cudaMemsetAsync(g->ctr, 0, sizeof(unsigned) * (size_t)g->ntr, g->c->stream);
+    }
+    return st;
 }
 
 void dense_destroy(dense_gemv *g) {

@@ -53,6 +53,9 @@ struct dense_gemv;  // plan: sizes, chunking, scratch
 
 dense_gemv *dense_create(moearc_ctx *c, int n_rows, int n_cols, int mode);
 void dense_destroy(dense_gemv *g);
+// Reads and clears the plan's status word (0, or STATUS_WAIT_TIMEOUT when a poll gave up; then
+// every partial slot is emptied again); ERR when the read fails.
+int dense_status(dense_gemv *g);
 
 // mode 0 (QKV): out_q = rope(q), K/V -> cache; input = rmsnorm(h) * norm_w.
 // mode 1 (residual): out = residual + W . x; input x as is.

@@ -864,7 +864,12 @@ struct xtab {
 // Every token's top-k (warp t of nw takes tokens t, t + nw, ...), then the tables by warp 0: the
 // columns are the choices sorted by (expert, token) — distinct experts ascending, a slot's
 // tokens in token order — cut into groups of at most GROUP columns of one expert.
-__device__ void xbuild(xtab &tb, const float *logits, int T, int E, int K, int gating, int warp, int lane) {
+#ifdef XB_TWICE
+__device__ __noinline__
+#else
+__device__
+#endif
+void xbuild(xtab &tb, const float *logits, int T, int E, int K, int gating, int warp, int lane) {
     const int nw = (int)(blockDim.x >> 5);
     for (int t = warp; t < T; t += nw) xtopk(logits + (size_t)t * E, E, K, gating, lane, tb.idx + t * K, tb.wts + t * K);
     __syncthreads();
@@ -953,41 +958,6 @@ struct xexp_args {
 
 __device__ __forceinline__ int xcta(long P, long NW, long p) { return (int)(((p + 1) * NW - 1) / P); }
 
-// A partial slot of the expert kernels holds PART_EMPTY until its piece stores the partial, and
-// is set back to PART_EMPTY by the warp that reads it, so a finished buffer is all PART_EMPTY
-// again. The pattern is a NaN that no arithmetic produces (results that are NaN carry the
-// canonical 0x7FFFFFFF). Slots are written and polled with relaxed gpu-scope accesses.
-constexpr uint32_t PART_EMPTY = 0xFFC0DEADu;
-constexpr unsigned long long XPOLL_NS = 200000000ull;  // a poll on other warps gives up after 0.2 s
-
-__device__ __forceinline__ uint4 ld_part4(const float *p) {
-    uint4 v;
-    asm volatile("ld.relaxed.gpu.global.v4.b32 {%0, %1, %2, %3}, [%4];"
-                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
-                 : "l"(p)
-                 : "memory");
-    return v;
-}
-__device__ __forceinline__ void st_part4(float *p, float x, float y, float z, float w) {
-    asm volatile("st.relaxed.gpu.global.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(p), "f"(x), "f"(y), "f"(z), "f"(w)
-                 : "memory");
-}
-// Set the first used4 float4s of nrec consecutive records (rec floats apart) back to PART_EMPTY,
-// whole sectors, the warp's lanes striding.
-__device__ __forceinline__ void empty_recs(float *p, int nrec, int rec, int used4, int lane) {
-    for (int i = lane; i < nrec * used4; i += 32) {
-        const int r = i / used4, k = i - r * used4;
-        asm volatile("st.relaxed.gpu.global.v4.b32 [%0], {%1, %1, %1, %1};" ::"l"(p + (size_t)r * rec + k * 4),
-                     "r"(PART_EMPTY)
-                     : "memory");
-    }
-}
-__device__ __forceinline__ unsigned long long xnow() {
-    unsigned long long t;
-    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-    return t;
-}
-
 // The np piece partials of one (record run, float4): pieces seg * np .. + np - 1, rec floats
 // apart, the float4 at offset off of each; read as soon as every one has been stored and summed
 // in piece order from 0, per component (sum[0..3]) or, PAIR, per pair (sum[0] = x + y, sum[1] =
@@ -1047,11 +1017,25 @@ __global__ void __launch_bounds__(XW * 32, 1) k_xexpert(xexp_args a) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     constexpr int MATS = MODE == 0 ? 2 : 1;
     if (MODE == 0) {
+#ifdef XB_TWICE
+        // experiment: a dry run of the table build before the wait
+        xbuild(tb, a.logits, a.T, a.E, a.K, a.gating, warp, lane);
+        TRACE(13);
+#endif
         // the logits are the previous kernel's output; release the down kernel, which reads
         // them before its own wait
         pdl_wait();
         pdl_trigger();
         TRACE(12);
+#ifdef MOEARC_TRACE
+        if (threadIdx.x == 0 && g_trace) {
+            // probe: one logit load and its return time
+            const float lv = __ldcg(a.logits);
+            unsigned long long t_;
+            asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t_));
+            g_trace[(size_t)trace_row * 32 + 2] = t_ + (lv == 12345.f ? 1 : 0);
+        }
+#endif
     }
     xbuild(tb, a.logits, a.T, a.E, a.K, a.gating, warp, lane);
     TRACE(1);
@@ -1961,19 +1945,11 @@ int occupancy_grid(moearc_ctx *c, int smem_per_cta) {
     return c->sm_count * per_sm;
 }
 
-__global__ void k_part_fill(uint32_t *p, size_t n) {
-    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
-        p[i] = PART_EMPTY;
-}
-
 // Every partial slot of the expert kernels back to PART_EMPTY (at creation, and after a wait
 // gave up).
 void x_parts_empty(moearc_x_moe *m) {
-    cudaStream_t st = m->ctx->stream;
-    if (m->x_part_gu_n)
-        k_part_fill<<<m->ctx->sm_count, 256, 0, st>>>(reinterpret_cast<uint32_t *>(m->x_part_gu), m->x_part_gu_n);
-    if (m->x_part_dn_n)
-        k_part_fill<<<m->ctx->sm_count, 256, 0, st>>>(reinterpret_cast<uint32_t *>(m->x_part_dn), m->x_part_dn_n);
+    parts_empty(m->x_part_gu, m->x_part_gu_n, m->ctx->stream, m->ctx->sm_count);
+    parts_empty(m->x_part_dn, m->x_part_dn_n, m->ctx->stream, m->ctx->sm_count);
 }
 
 }  // namespace

@@ -121,6 +121,14 @@ class Decoder:
     def use_graph(self, on: bool) -> None:
         self.ctx._finish(self.ctx.lib.moearc_x_decoder_use_graph(self.h, 1 if on else 0), "use_graph")
 
+    def status(self) -> int:
+        """Reads and clears the kernels' device status words: 0, or nonzero when a bounded
+        wait gave up (the steps since the last read are then invalid)."""
+        st = self.ctx.lib.moearc_x_decoder_status(self.h)
+        if st < 0:
+            self.ctx._finish(st, "status")
+        return st
+
     def step(self) -> None:
         """Enqueue one decode step (the caller synchronises when it needs the output)."""
         self.ctx._finish(self.ctx.lib.moearc_x_decoder_step(self.h), "decoder step")
