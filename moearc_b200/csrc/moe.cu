@@ -57,6 +57,7 @@ struct moearc_x_moe {
     float *x_part_gu, *x_part_dn;  // expert kernels' piece partials (PART_EMPTY when idle)
     size_t x_part_gu_n, x_part_dn_n;
     float *f_part_gu, *f_part_dn;  // the opt-in fused kernels' (arrival counters instead)
+    void *x_tab_pub;               // the gate-up kernel's routing tables, read by the down kernel
     unsigned *x_ctr_gu, *x_ctr_dn;
     // the fused decode kernel (k_moe_fused): one cooperative launch per layer
     bool fused;
@@ -864,12 +865,9 @@ struct xtab {
 // Every token's top-k (warp t of nw takes tokens t, t + nw, ...), then the tables by warp 0: the
 // columns are the choices sorted by (expert, token) — distinct experts ascending, a slot's
 // tokens in token order — cut into groups of at most GROUP columns of one expert.
-#ifdef XB_TWICE
-__device__ __noinline__
-#else
-__device__
-#endif
-void xbuild(xtab &tb, const float *logits, int T, int E, int K, int gating, int warp, int lane) {
+// Not inlined: the gate-up kernel runs it twice (a dry run before its wait, then the real one)
+// and the second call finds the code in the instruction cache.
+__device__ __noinline__ void xbuild(xtab &tb, const float *logits, int T, int E, int K, int gating, int warp, int lane) {
     const int nw = (int)(blockDim.x >> 5);
     for (int t = warp; t < T; t += nw) xtopk(logits + (size_t)t * E, E, K, gating, lane, tb.idx + t * K, tb.wts + t * K);
     __syncthreads();
@@ -952,6 +950,7 @@ struct xexp_args {
     float *out;
     int H;
     float *part;              // piece partials, PART_EMPTY where none is pending
+    xtab *tab_pub;            // gate-up: CTA 0 publishes its tables here; down: read them (or null)
     int by_slot;              // bank holds one expert per slot (staged offload), not all experts
     int *status;
 };
@@ -1017,28 +1016,35 @@ __global__ void __launch_bounds__(XW * 32, 1) k_xexpert(xexp_args a) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     constexpr int MATS = MODE == 0 ? 2 : 1;
     if (MODE == 0) {
-#ifdef XB_TWICE
-        // experiment: a dry run of the table build before the wait
+        // Before the wait, a dry run of the table build on whatever the logits hold now (the
+        // router kernel is still writing them; these tables are discarded): it brings the
+        // code into the instruction cache while the router runs.
         xbuild(tb, a.logits, a.T, a.E, a.K, a.gating, warp, lane);
         TRACE(13);
-#endif
-        // the logits are the previous kernel's output; release the down kernel, which reads
-        // them before its own wait
+        // the logits are the previous kernel's output
         pdl_wait();
-        pdl_trigger();
         TRACE(12);
-#ifdef MOEARC_TRACE
-        if (threadIdx.x == 0 && g_trace) {
-            // probe: one logit load and its return time
-            const float lv = __ldcg(a.logits);
-            unsigned long long t_;
-            asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t_));
-            g_trace[(size_t)trace_row * 32 + 2] = t_ + (lv == 12345.f ? 1 : 0);
-        }
-#endif
+        // CTA 0 releases the down kernel only once it has published the tables (below)
+        if (blockIdx.x != 0 || !a.tab_pub) pdl_trigger();
     }
-    xbuild(tb, a.logits, a.T, a.E, a.K, a.gating, warp, lane);
+    if (MODE == 1 && a.tab_pub) {
+        // the gate-up kernel's published tables: final before this kernel was launched
+        const uint32_t *src = reinterpret_cast<const uint32_t *>(a.tab_pub);
+        uint32_t *dst = reinterpret_cast<uint32_t *>(&tb);
+        for (int i = threadIdx.x; i < (int)(sizeof(xtab) / 4); i += blockDim.x) dst[i] = __ldcg(src + i);
+        __syncthreads();
+    } else {
+        xbuild(tb, a.logits, a.T, a.E, a.K, a.gating, warp, lane);
+    }
     TRACE(1);
+    if (MODE == 0 && blockIdx.x == 0 && a.tab_pub) {
+        const uint32_t *src = reinterpret_cast<const uint32_t *>(&tb);
+        uint32_t *dst = reinterpret_cast<uint32_t *>(a.tab_pub);
+        for (int i = threadIdx.x; i < (int)(sizeof(xtab) / 4); i += blockDim.x) dst[i] = src[i];
+        __threadfence();
+        __syncthreads();
+        pdl_trigger();
+    }
     if (MODE == 0 && blockIdx.x == 0)
         for (int i = threadIdx.x; i < tb.C; i += blockDim.x) {
             a.idx_out[i] = tb.idx[i];
@@ -2091,6 +2097,7 @@ moearc_x_moe *moearc_x_moe_create(moearc_ctx *c, const moearc_x_moe_desc *d) {
     const bool fz_any = m->fused || m->fused_gd;
     const size_t o_fpg = take(fz_any ? sizeof(float) * x_segs_gu * np_gu * XREC_GU : 0);
     const size_t o_fpd = take(fz_any ? sizeof(float) * x_segs_dn * np_dn * XREC_DN : 0);
+    const size_t o_xtp = take(m->xpath ? sizeof(xtab) : 0);
     const size_t o_xcg = take(m->xpath ? sizeof(unsigned) * x_segs_gu : 0);
     const size_t o_xcd = take(m->xpath ? sizeof(unsigned) * m->ntr_h : 0);
     const size_t o_frd = take(m->xpath ? sizeof(unsigned) * (size_t)TK * np_dn : 0);
@@ -2115,6 +2122,7 @@ moearc_x_moe *moearc_x_moe_create(moearc_ctx *c, const moearc_x_moe_desc *d) {
     m->x_part_dn = reinterpret_cast<float *>(b + o_xpd);
     m->x_part_gu_n = m->xpath ? x_segs_gu * np_gu * XREC_GU : 0;
     m->x_part_dn_n = m->xpath ? x_segs_dn * np_dn * XREC_XDN : 0;
+    m->x_tab_pub = m->xpath ? b + o_xtp : nullptr;
     m->f_part_gu = reinterpret_cast<float *>(b + o_fpg);
     m->f_part_dn = reinterpret_cast<float *>(b + o_fpd);
     m->x_ctr_gu = reinterpret_cast<unsigned *>(b + o_xcg);
@@ -2315,6 +2323,9 @@ int moe_forward_impl(moearc_x_moe *m, const float *x, unsigned n_tokens, const f
         xa.wts_out = m->wts;
         xa.H = m->H;
         xa.part = m->x_part_gu;
+        // offloaded blocks: the down fetch runs between the two kernels and the down kernel
+        // builds its own tables after its wait
+        xa.tab_pub = off ? nullptr : static_cast<xtab *>(m->x_tab_pub);
         xa.status = m->status;
         const bool mx = m->wtype == T_MXFP4;
         // More than half an SM's shared memory, so no SM takes two gate-up CTAs: at launch the
