@@ -226,13 +226,13 @@ __device__ __forceinline__ void st_part4(float *p, float x, float y, float z, fl
                  : "memory");
 }
 // Set the first used4 float4s of nrec consecutive records (rec floats apart) back to PART_EMPTY,
-// whole sectors, the warp's lanes striding.
+// whole sectors, the warp's lanes striding. Plain stores: a slot is next written in a later
+// launch, after this kernel has completed, and read after that.
 __device__ __forceinline__ void empty_recs(float *p, int nrec, int rec, int used4, int lane) {
+    const uint4 e = make_uint4(PART_EMPTY, PART_EMPTY, PART_EMPTY, PART_EMPTY);
     for (int i = lane; i < nrec * used4; i += 32) {
         const int r = i / used4, k = i - r * used4;
-        asm volatile("st.relaxed.gpu.global.v4.b32 [%0], {%1, %1, %1, %1};" ::"l"(p + (size_t)r * rec + k * 4),
-                     "r"(PART_EMPTY)
-                     : "memory");
+        *reinterpret_cast<uint4 *>(p + (size_t)r * rec + k * 4) = e;
     }
 }
 __device__ __forceinline__ unsigned long long xnow() {
