@@ -359,6 +359,47 @@ int moearc_x_batch_decoder_step(moearc_x_batch_decoder *d);
 /* Reads and clears the status words: 0, or nonzero when a bounded wait gave up. */
 int moearc_x_batch_decoder_status(moearc_x_batch_decoder *d);
 
+/* ---- GGUF model files (no counterpart in the reference's ABI) -------------------------------
+ * A read-only view of a GGUF v2/v3 file, replacing the reference's Rust reader
+ * (crates/moearc-model/src/gguf.rs:166-279, the header parse with its plausibility checks) and
+ * its expert addressing (crates/moearc-model/src/tensors.rs:237-289, slice_last_dim). The file
+ * is mapped, not read: a tensor's bytes are a pointer into the mapping, valid until close, and
+ * can go straight to moearc_copy_h2d / moearc_x_moe_pack. Every count and length in the header
+ * is checked against the file size before it is used; a malformed file is refused at open. */
+typedef struct moearc_x_gguf moearc_x_gguf;
+typedef struct {
+    unsigned int n_dims;                /* 1..4 */
+    unsigned long long dims[4];         /* fastest-varying first, as stored */
+    unsigned int type_id;               /* ggml type id: F32 0, F16 1, Q4_0 2, Q8_0 8, BF16 30, MXFP4 39 ... */
+    unsigned long long offset;          /* of the tensor's first byte, from the start of the file */
+    unsigned long long nbytes;          /* elements / block size x block bytes */
+    const void *data;                   /* in the mapping */
+} moearc_x_gguf_tensor;
+/* NULL on any failure; moearc_x_gguf_last_error() then names it. */
+moearc_x_gguf *moearc_x_gguf_open(const char *path);
+void moearc_x_gguf_close(moearc_x_gguf *g);
+/* The calling thread's message for its last failed moearc_x_gguf_* call ("" if none). */
+const char *moearc_x_gguf_last_error(void);
+unsigned int moearc_x_gguf_version(moearc_x_gguf *g);
+unsigned long long moearc_x_gguf_alignment(moearc_x_gguf *g);
+unsigned long long moearc_x_gguf_n_tensors(moearc_x_gguf *g);
+/* Metadata: 0, or -2 when the key is absent or holds another kind of value. Integer keys of any
+ * width (and bools) read as u64 when non-negative; f32 and f64 keys read as double; strings
+ * are returned NUL-terminated, valid until close. */
+int moearc_x_gguf_key_u64(moearc_x_gguf *g, const char *key, unsigned long long *out);
+int moearc_x_gguf_key_f64(moearc_x_gguf *g, const char *key, double *out);
+int moearc_x_gguf_key_str(moearc_x_gguf *g, const char *key, const char **out);
+/* Tensor by name, or by index (name through *name); -2 when absent. */
+int moearc_x_gguf_find(moearc_x_gguf *g, const char *name, moearc_x_gguf_tensor *out);
+int moearc_x_gguf_tensor_at(moearc_x_gguf *g, unsigned long long i, moearc_x_gguf_tensor *out, const char **name);
+/* Slice `index` of a stacked tensor along its last dimension (one expert of a
+ * blk.N.ffn_{gate,up,down}_exps.weight bank): the n_dims - 1 inner dimensions, at a byte
+ * stride of inner elements / block size x block bytes. -2 when the tensor is absent or rank 1,
+ * the index is out of range, the inner elements are not whole blocks, or the slices do not
+ * tile the tensor exactly. */
+int moearc_x_gguf_slice_last(moearc_x_gguf *g, const char *name, unsigned long long index,
+                             moearc_x_gguf_tensor *out);
+
 /* ---- decode attention without allocation (no counterpart in the reference) ----------------
  * Same arguments, result and return codes as moearc_attn_decode, but the split-K partials live
  * in a fixed per-device array of MOEARC_X_ATTN_STATIC_SCRATCH_BYTES compiled into the library,

@@ -114,8 +114,26 @@ SIGNATURES: dict[str, tuple] = {
     "moearc_x_decoder_profile": (I, [P, C.POINTER(F), C.POINTER(I), I]),
     "moearc_x_decoder_tensor": (P, [P, I, U, C.POINTER(UL)]),
     "moearc_x_decoder_seed": (C.c_ulonglong, [P, I, U, C.c_ulonglong]),
+    "moearc_x_gguf_open": (P, [C.c_char_p]),
+    "moearc_x_gguf_close": (None, [P]),
+    "moearc_x_gguf_last_error": (C.c_char_p, []),
+    "moearc_x_gguf_version": (U, [P]),
+    "moearc_x_gguf_alignment": (C.c_ulonglong, [P]),
+    "moearc_x_gguf_n_tensors": (C.c_ulonglong, [P]),
+    "moearc_x_gguf_key_u64": (I, [P, C.c_char_p, C.POINTER(C.c_ulonglong)]),
+    "moearc_x_gguf_key_f64": (I, [P, C.c_char_p, C.POINTER(C.c_double)]),
+    "moearc_x_gguf_key_str": (I, [P, C.c_char_p, C.POINTER(C.c_char_p)]),
+    "moearc_x_gguf_find": (I, [P, C.c_char_p, P]),
+    "moearc_x_gguf_tensor_at": (I, [P, C.c_ulonglong, P, C.POINTER(C.c_char_p)]),
+    "moearc_x_gguf_slice_last": (I, [P, C.c_char_p, C.c_ulonglong, P]),
     "moearc_x_attn_decode_static": (I, [P, P, P, P, P, P, P, UL, UL, UL, UL, UL, UL, F, U]),
 }
+
+
+class GgufTensor(C.Structure):
+    """moearc_x_gguf_tensor (include/moearc.h)."""
+    _fields_ = [("n_dims", U), ("dims", C.c_ulonglong * 4), ("type_id", U), ("offset", C.c_ulonglong),
+                ("nbytes", C.c_ulonglong), ("data", P)]
 
 
 class DecoderCfg(C.Structure):
