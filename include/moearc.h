@@ -16,9 +16,10 @@
  * 0 for "accepted", not "completed"; a device fault surfaces at moearc_sync or at the next
  * device-to-host copy. `unsigned long` is 64 bits (LP64), as in the reference's c_ulong.
  *
- * Type ids are GGUF's (reference.rs:21-40): F32 0, F16 1, Q4_0 2, Q8_0 8, BF16 30, MXFP4 39.
- * This library expands F32, F16, BF16, Q4_0, Q8_0 and MXFP4 (the K-quants 12/13/14 answer
- * -2). KV caches may be F32, F16 or BF16.
+ * Type ids are GGUF's (reference.rs:21-40): F32 0, F16 1, Q4_0 2, Q8_0 8, Q4_K 12, Q5_K 13,
+ * Q6_K 14, BF16 30, MXFP4 39. Every one expands (dequant, embed_rows) and multiplies
+ * (matvec_q, matvec_q_batched): the reference's seven plus Q4_0 and BF16. The fused MoE paths
+ * take MXFP4 and Q4_0 experts. KV caches may be F32, F16 or BF16.
  */
 #ifndef MOEARC_H
 #define MOEARC_H

@@ -22,6 +22,7 @@ constexpr int ERR_ARG = -2;
 
 // GGUF type ids (reference.rs:21-40; crates/moearc-model/src/quant.rs:51-107).
 constexpr unsigned T_F32 = 0, T_F16 = 1, T_Q4_0 = 2, T_Q8_0 = 8, T_BF16 = 30, T_MXFP4 = 39;
+constexpr unsigned T_Q4_K = 12, T_Q5_K = 13, T_Q6_K = 14;  // 256-element super-blocks
 
 // Largest k the router selects and largest matrix count one batched launch takes
 // (kernels.cpp:451, 651): both bound by-value kernel arguments, not allocations.
@@ -36,6 +37,9 @@ inline int block_bytes(unsigned t) {
     case T_Q4_0: return 18;
     case T_Q8_0: return 34;
     case T_MXFP4: return 17;
+    case T_Q4_K: return 144;
+    case T_Q5_K: return 176;
+    case T_Q6_K: return 210;
     default: return 0;
     }
 }
@@ -47,6 +51,9 @@ inline int block_elems(unsigned t) {
     case T_Q4_0:
     case T_Q8_0:
     case T_MXFP4: return 32;
+    case T_Q4_K:
+    case T_Q5_K:
+    case T_Q6_K: return 256;
     default: return 0;
     }
 }

@@ -1,12 +1,14 @@
 // dequant.cu — block expansion, embedding gather, narrowing, expert gather, synthetic fills.
 //
 // moearc_dequant restates kernels.cpp:1009-1026 (one work-item per element there, each
-// recomputing its block's scale). Here one thread expands four consecutive elements of a block
+// recomputing its block's scale), for every type the reference expands (F32, F16, Q8_0, Q4_K,
+// Q5_K, Q6_K, MXFP4) plus Q4_0 and BF16. Here one thread expands four consecutive elements of a block
 // and writes them as one 16-byte store, so a warp writes 512 contiguous bytes: the expansion
 // is bound by its output stream, which is 7.5x (MXFP4) the input.
 #include <cmath>
 
 #include "common.cuh"
+#include "kquant.cuh"
 
 using namespace moearc;
 
@@ -75,6 +77,27 @@ __global__ void k_dequant_blocks(float *__restrict__ dst, const uint8_t *__restr
     }
 }
 
+// K-quant super-blocks: one thread expands eight consecutive elements (32 threads a block).
+template <unsigned T, int BB>
+__global__ void k_dequant_kq(float *__restrict__ dst, const uint8_t *__restrict__ src,
+                             const unsigned *__restrict__ ids, size_t rows, size_t nb, bool vec) {
+    const size_t per_row = nb * 32;
+    const size_t total = rows * per_row;
+    for (size_t g = blockIdx.x * (size_t)blockDim.x + threadIdx.x; g < total;
+         g += (size_t)gridDim.x * blockDim.x) {
+        const size_t r = g / per_row;
+        const size_t gi = g - r * per_row;
+        const size_t blk = gi >> 5;
+        const int e0 = (int)(gi & 31) * 8;
+        const size_t row = ids ? (size_t)ids[r] : r;
+        float v[8];
+        kq_decode8<T>(src + (row * nb + blk) * BB, e0, v);
+        const size_t o = r * nb * 256 + blk * 256 + e0;
+        store4(dst, o, make_float4(v[0], v[1], v[2], v[3]), vec);
+        store4(dst, o + 4, make_float4(v[4], v[5], v[6], v[7]), vec);
+    }
+}
+
 // One-element "blocks": f32, f16, bf16.
 template <unsigned T>
 __global__ void k_dequant_scalar(float *__restrict__ dst, const uint8_t *__restrict__ src,
@@ -103,7 +126,15 @@ int launch_expand(moearc_ctx *c, unsigned t, float *dst, const uint8_t *src, con
     launch_scope ls(c, what, rows, 1);
     const bool vec = (reinterpret_cast<uintptr_t>(dst) & 15) == 0;
     const unsigned th = 256;
-    if (block_elems(t) == 32) {
+    if (block_elems(t) == 256) {
+        const size_t nb = n_per_row / 256;
+        const unsigned g = grid_for(c, rows * nb * 32, th);
+        switch (t) {
+        case T_Q4_K: k_dequant_kq<T_Q4_K, 144><<<g, th, 0, c->stream>>>(dst, src, ids, rows, nb, vec); break;
+        case T_Q5_K: k_dequant_kq<T_Q5_K, 176><<<g, th, 0, c->stream>>>(dst, src, ids, rows, nb, vec); break;
+        default: k_dequant_kq<T_Q6_K, 210><<<g, th, 0, c->stream>>>(dst, src, ids, rows, nb, vec); break;
+        }
+    } else if (block_elems(t) == 32) {
         const size_t nb = n_per_row / 32;
         const unsigned g = grid_for(c, rows * nb * 8, th);
         switch (t) {

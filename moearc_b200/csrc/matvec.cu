@@ -12,6 +12,7 @@
 // This is the drop-in path for callers that hand over GGUF pointers; the fused MoE path
 // (moe.cu) reads a re-laid bank on the tensor cores instead.
 #include "common.cuh"
+#include "kquant.cuh"
 
 using namespace moearc;
 
@@ -146,6 +147,34 @@ __global__ void __launch_bounds__(WARPS * 32)
     }
 }
 
+// K-quant rows (256-element super-blocks): warp per row, each super-block spread over the warp,
+// lane l expanding its elements 8l .. 8l + 7 (kquant.cuh) and folding them with x in order; a
+// butterfly sums the lanes.
+template <unsigned T, int BB>
+__global__ void __launch_bounds__(WARPS * 32)
+    k_matvec_kq(float *__restrict__ out, mat_table w, const float *__restrict__ x, size_t x_stride,
+                size_t n_rows, size_t n_cols) {
+    const unsigned m = blockIdx.y;
+    const float *xm = x + (size_t)m * x_stride;
+    const size_t nb = n_cols / 256;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    for (int i = 0; i < ROWS_PER_WARP; ++i) {
+        const size_t r = (size_t)blockIdx.x * ROWS_PER_CTA + warp * ROWS_PER_WARP + i;
+        if (r >= n_rows) break;  // uniform across the warp
+        const uint8_t *row = w.p[m] + r * nb * BB;
+        float acc = 0.f;
+        for (size_t b = 0; b < nb; ++b) {
+            float v[8];
+            kq_decode8<T>(row + b * BB, 8 * lane, v);
+            const float *xb = xm + b * 256 + 8 * lane;
+#pragma unroll
+            for (int e = 0; e < 8; ++e) acc = fmaf(v[e], __ldg(xb + e), acc);
+        }
+        acc = warp_sum(acc);
+        if (lane == 0) out[(size_t)m * n_rows + r] = acc;
+    }
+}
+
 // f32 / f16 / bf16 rows: warp per row, lanes stride the columns (kernels.cpp:1027-1044).
 template <unsigned T>
 __global__ void __launch_bounds__(WARPS * 32)
@@ -208,7 +237,13 @@ int launch_matvec(moearc_ctx *c, unsigned t, float *out, const mat_table &tab, u
     launch_scope ls(c, what, n_rows, n_mat);
     const dim3 grid(cdiv(n_rows, ROWS_PER_CTA), n_mat);
     const dim3 block(WARPS * 32);
-    if (block_elems(t) == 32) {
+    if (block_elems(t) == 256) {
+        switch (t) {
+        case T_Q4_K: k_matvec_kq<T_Q4_K, 144><<<grid, block, 0, c->stream>>>(out, tab, x, x_stride, n_rows, n_cols); break;
+        case T_Q5_K: k_matvec_kq<T_Q5_K, 176><<<grid, block, 0, c->stream>>>(out, tab, x, x_stride, n_rows, n_cols); break;
+        default: k_matvec_kq<T_Q6_K, 210><<<grid, block, 0, c->stream>>>(out, tab, x, x_stride, n_rows, n_cols); break;
+        }
+    } else if (block_elems(t) == 32) {
         const size_t smem = (n_cols + 32) * sizeof(float);
         bool aligned = true;
         for (unsigned m = 0; m < n_mat; ++m) aligned &= (reinterpret_cast<uintptr_t>(tab.p[m]) & 3) == 0;

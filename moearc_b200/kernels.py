@@ -17,8 +17,9 @@ import numpy as np
 from . import _lib
 
 F32, F16, Q4_0, Q8_0, BF16, MXFP4 = 0, 1, 2, 8, 30, 39
-BLOCK_BYTES = {F32: 4, F16: 2, BF16: 2, Q4_0: 18, Q8_0: 34, MXFP4: 17}
-BLOCK_ELEMS = {F32: 1, F16: 1, BF16: 1, Q4_0: 32, Q8_0: 32, MXFP4: 32}
+Q4_K, Q5_K, Q6_K = 12, 13, 14
+BLOCK_BYTES = {F32: 4, F16: 2, BF16: 2, Q4_0: 18, Q8_0: 34, MXFP4: 17, Q4_K: 144, Q5_K: 176, Q6_K: 210}
+BLOCK_ELEMS = {F32: 1, F16: 1, BF16: 1, Q4_0: 32, Q8_0: 32, MXFP4: 32, Q4_K: 256, Q5_K: 256, Q6_K: 256}
 KV_ELEM_BYTES = {F32: 4, F16: 2, BF16: 2}
 MAX_BATCHED_MATS = 32
 MAX_TOPK = 32

@@ -127,6 +127,9 @@ int or_block_bytes(unsigned t) {
     case OR_Q4_0: return 18;  /* f16 delta + 16 bytes of nibble pairs */
     case OR_Q8_0: return 34;  /* f16 delta + 32 signed bytes */
     case OR_MXFP4: return 17; /* e8m0 byte + 16 bytes of nibble pairs */
+    case OR_Q4_K: return 144; /* d, dmin, 12 scale bytes, 128 nibble bytes (reference.rs:74-89) */
+    case OR_Q5_K: return 176; /* as Q4_K plus 32 high-bit bytes */
+    case OR_Q6_K: return 210; /* 128 low nibbles, 64 high-pair bytes, 16 int8 scales, d */
     default: return 0;
     }
 }
@@ -139,11 +142,71 @@ int or_block_elems(unsigned t) {
     case OR_Q4_0:
     case OR_Q8_0:
     case OR_MXFP4: return 32;
+    case OR_Q4_K:
+    case OR_Q5_K:
+    case OR_Q6_K: return 256; /* QK_K super-blocks (reference.rs:42, 93-100) */
     default: return 0;
     }
 }
 
 static inline float ld_f16(const uint8_t *p) { return or_f16_to_f32((uint16_t)(p[0] | (p[1] << 8))); }
+
+/* The 6-bit scale and min of sub-block j of a Q4_K / Q5_K super-block from its 12 packed
+ * bytes (ggml's get_scale_min_k4, reference.rs:154-160): sub-blocks 0-3 keep theirs in the
+ * low six bits of bytes j and j+4; 4-7 take four bits from bytes j+4 and the top two of bytes
+ * j-4 and j. */
+static void scale_min_k4(const uint8_t *q, int j, uint8_t *sc, uint8_t *m) {
+    if (j < 4) {
+        *sc = q[j] & 63;
+        *m = q[j + 4] & 63;
+    } else {
+        *sc = (uint8_t)((q[j + 4] & 0xF) | ((q[j - 4] >> 6) << 4));
+        *m = (uint8_t)((q[j + 4] >> 4) | ((q[j] >> 6) << 4));
+    }
+}
+
+/* A Q4_K (hb = 0) or Q5_K (hb = 1) super-block (reference.rs:218-276): four 64-element runs,
+ * each two 32-element sub-blocks sharing the run's 32 nibble bytes (low nibbles first); an
+ * element is (d * scale) * q - (dmin * min), with Q5_K adding 16 to q when its bit in the
+ * run's high-bit plane is set. */
+static void dequant_kq45(const uint8_t *b, float *y, int hb) {
+    const float d = ld_f16(b), dmin = ld_f16(b + 2);
+    const uint8_t *scales = b + 4;
+    const uint8_t *qh = b + 16;
+    const uint8_t *qs = b + (hb ? 48 : 16);
+    for (int run = 0; run < 4; ++run) {
+        for (int half = 0; half < 2; ++half) {
+            uint8_t sc, m;
+            scale_min_k4(scales, 2 * run + half, &sc, &m);
+            const float d1 = d * (float)sc, m1 = dmin * (float)m;
+            const uint8_t bit = (uint8_t)(1u << (2 * run + half));
+            for (int l = 0; l < 32; ++l) {
+                const uint8_t byte = qs[32 * run + l];
+                int q = half ? (byte >> 4) : (byte & 0xF);
+                if (hb && (qh[l] & bit)) q += 16;
+                y[64 * run + 32 * half + l] = d1 * (float)q - m1;
+            }
+        }
+    }
+}
+
+/* A Q6_K super-block (reference.rs:278-300): two 128-element halves; element l of quarter k of
+ * a half takes four low bits from byte l (k even) or l + 32 (k odd) of the half's 64 low-nibble
+ * bytes (low nibble for k < 2, high for k >= 2) and two high bits from bits 2k..2k+1 of byte l
+ * of the half's 32 high bytes; q - 32 is scaled by d times int8 scale 2k + l/16 of the half. */
+static void dequant_q6k(const uint8_t *b, float *y) {
+    const float d = ld_f16(b + 208);
+    for (int n = 0; n < 2; ++n) {
+        const uint8_t *ql = b + 64 * n, *qh = b + 128 + 32 * n;
+        const int8_t *sc = (const int8_t *)(b + 192 + 8 * n);
+        for (int k = 0; k < 4; ++k)
+            for (int l = 0; l < 32; ++l) {
+                const uint8_t lo = ql[l + 32 * (k & 1)];
+                const int q = (((k >= 2) ? (lo >> 4) : (lo & 0xF)) | (((qh[l] >> (2 * k)) & 3) << 4)) - 32;
+                y[128 * n + 32 * k + l] = d * (float)sc[2 * k + l / 16] * (float)q;
+            }
+    }
+}
 
 /* One block of each format. The nibble formats share one rule: byte j's low nibble is element
  * j and its high nibble is element j+16 — the two halves of the block, not an adjacent pair
@@ -176,6 +239,9 @@ static void dequant_block(unsigned t, const uint8_t *b, float *y) {
         }
         break;
     }
+    case OR_Q4_K: dequant_kq45(b, y, 0); break;
+    case OR_Q5_K: dequant_kq45(b, y, 1); break;
+    case OR_Q6_K: dequant_q6k(b, y); break;
     default: break;
     }
 }

@@ -49,6 +49,16 @@ def synth_blocks(t, nblocks, seed):
         b[:, 0] = scale & 0xFF
         b[:, 1] = scale >> 8
         return b.ravel()
+    if t in (O.Q4_K, O.Q5_K, O.Q6_K):
+        # random payload (every nibble, 6-bit scale split and high-bit position), finite f16
+        # deltas: d and dmin at the front of Q4_K / Q5_K, d at the end of Q6_K (common/mod.rs:50-80)
+        bb = O.BLOCK_BYTES[t]
+        b = rng.integers(0, 256, size=(nblocks, bb), dtype=np.uint8)
+        for off in ((208,) if t == O.Q6_K else (0, 2)):
+            scale = (0x1000 + rng.integers(0, 0x1800, size=nblocks)).astype(np.uint16)
+            b[:, off] = scale & 0xFF
+            b[:, off + 1] = scale >> 8
+        return b.ravel()
     if t == O.F32:
         return rng.uniform(-1, 1, nblocks).astype(np.float32).view(np.uint8)
     if t == O.F16:
@@ -60,9 +70,9 @@ def synth_blocks(t, nblocks, seed):
 
 # ---- dequant ---------------------------------------------------------------------------------
 
-@pytest.mark.parametrize("t", [O.MXFP4, O.Q4_0, O.Q8_0, O.F32, O.F16, O.BF16])
+@pytest.mark.parametrize("t", [O.MXFP4, O.Q4_0, O.Q8_0, O.Q4_K, O.Q5_K, O.Q6_K, O.F32, O.F16, O.BF16])
 def test_dequant_is_bit_exact(ctx, t):
-    nblocks = 1000 if O.BLOCK_ELEMS[t] == 32 else 4099
+    nblocks = {1: 4099, 32: 1000, 256: 128}[O.BLOCK_ELEMS[t]]
     blocks = synth_blocks(t, nblocks, 0xC0FFEE ^ t)
     want = O.dequant(t, blocks, nblocks)
     src = ctx.upload_new(blocks)
@@ -95,15 +105,40 @@ def test_synthetic_mxfp4_is_identical_on_host_and_device(ctx):
 def test_unsupported_types_are_refused(ctx):
     b = ctx.alloc(1024)
     with pytest.raises(BadArgument):
-        ctx.dequant(12, b, b, 1)  # Q4_K: not expanded by this library
+        ctx.dequant(3, b, b, 1)  # Q4_1: expanded by neither the reference nor this library
+    x, o = ctx.alloc_n(np.float32, 300), ctx.alloc_n(np.float32, 4)
+    with pytest.raises(BadArgument):
+        ctx.matvec_q(O.Q4_K, o, b, x, 4, 300)  # kernels_gpu.rs:183: 300 is not whole super-blocks
+
+
+@pytest.mark.parametrize("t", [O.Q4_K, O.Q8_0, O.F16, O.Q6_K])
+def test_embed_rows_gathers_and_expands_exactly(ctx, t):
+    """forward_pass_gpu.rs:201-242: the rows of the named tokens, expanded exactly as dequant
+    expands them (Q4_K is OLMoE's token_embd type), and a row width that is not whole blocks
+    refused."""
+    n_vocab, n_embd = 50, 512
+    nb_row = n_embd // O.BLOCK_ELEMS[t]
+    table = synth_blocks(t, n_vocab * nb_row, 0xE3B ^ t)
+    ids = np.array([7, 0, 49, 7, 23], np.uint32)
+    full = O.dequant(t, table, n_vocab * nb_row).reshape(n_vocab, n_embd)
+    out = ctx.alloc_n(np.float32, ids.size * n_embd)
+    dt, di = ctx.upload_new(table), ctx.upload_new(ids)
+    ctx.embed_rows(t, out, dt, di, ids.size, n_embd)
+    got = ctx.download(out, np.float32, ids.size * n_embd).reshape(ids.size, n_embd)
+    assert np.array_equal(got.view(np.uint32), full[ids].view(np.uint32))
+    if O.BLOCK_ELEMS[t] > 1:
+        with pytest.raises(BadArgument):
+            ctx.embed_rows(t, out, dt, di, 1, 300)
 
 
 # ---- matvecs ---------------------------------------------------------------------------------
 
-@pytest.mark.parametrize("t", [O.MXFP4, O.Q4_0, O.Q8_0, O.F32, O.F16, O.BF16])
+@pytest.mark.parametrize("t", [O.MXFP4, O.Q4_0, O.Q8_0, O.Q4_K, O.Q5_K, O.Q6_K, O.F32, O.F16, O.BF16])
 @pytest.mark.parametrize("shape", [(37, 1024), (64, 2880), (5, 96)])
 def test_matvec_q_matches_the_oracle(ctx, t, shape):
     rows, cols = shape
+    if cols % O.BLOCK_ELEMS[t]:
+        cols = 2048 if cols == 2880 else 512  # whole 256-element super-blocks
     nb = rows * cols // O.BLOCK_ELEMS[t]
     w = synth_blocks(t, nb, 0x0BA7 + rows)
     x = np.random.default_rng(rows).uniform(-1, 1, cols).astype(np.float32)

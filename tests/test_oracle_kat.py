@@ -103,6 +103,12 @@ def test_block_sizes_match_the_reference():
     assert lib.or_block_bytes(O.MXFP4) == 17            # reference.rs:86-87
     assert lib.or_block_bytes(O.Q4_0) == 18             # crates/moearc-model/src/quant.rs:54
     assert lib.or_block_elems(O.MXFP4) == lib.or_block_elems(O.Q4_0) == 32
+    # reference.rs:896-905: the K-quant super-blocks ggml asserts, 256 elements each
+    QK_K = 256
+    assert lib.or_block_bytes(O.Q4_K) == 2 + 2 + 12 + QK_K // 2 == 144
+    assert lib.or_block_bytes(O.Q5_K) == 2 + 2 + 12 + QK_K // 8 + QK_K // 2 == 176
+    assert lib.or_block_bytes(O.Q6_K) == 2 + QK_K // 16 + 3 * QK_K // 4 == 210
+    assert lib.or_block_elems(O.Q4_K) == lib.or_block_elems(O.Q5_K) == lib.or_block_elems(O.Q6_K) == QK_K
 
 
 def test_mxfp4_block_by_hand():
@@ -133,11 +139,77 @@ def test_q4_0_block_by_hand():
 
 
 def test_a_zero_scale_block_dequantises_to_zero():
-    """reference.rs:907-920 for the formats with an f16 delta."""
-    for t in (O.Q8_0, O.Q4_0):
+    """reference.rs:907-920 for the formats with an f16 delta (Q6_K keeps its at the end,
+    Q4_K / Q5_K keep d and dmin at the front): a block at a wrong offset would not collapse."""
+    for t in (O.Q8_0, O.Q4_0, O.Q4_K, O.Q5_K, O.Q6_K):
         blk = np.full(O.BLOCK_BYTES[t], 0xAB, np.uint8)
-        blk[0:2] = 0
+        if t == O.Q6_K:
+            blk[208:210] = 0
+        elif t in (O.Q4_K, O.Q5_K):
+            blk[0:4] = 0
+        else:
+            blk[0:2] = 0
         assert np.all(O.dequant(t, blk, 1) == 0.0), t
+
+
+def _scale_min_bytes(pairs):
+    """The 12 packed bytes that give sub-block j the (6-bit scale, 6-bit min) pairs[j]: the
+    inverse of ggml's get_scale_min_k4."""
+    q = [0] * 12
+    for j, (sc, m) in enumerate(pairs):
+        if j < 4:
+            q[j] |= sc & 63
+            q[j + 4] |= m & 63
+        else:
+            q[j + 4] |= (sc & 15) | ((m & 15) << 4)
+            q[j - 4] |= (sc >> 4) << 6
+            q[j] |= (m >> 4) << 6
+    return q
+
+
+def test_q4_k_and_q5_k_blocks_by_hand():
+    """Element 64r + 32h + l of a Q4_K super-block is (d * scale) * q - (dmin * min) of
+    sub-block 2r + h, q the low (h = 0) or high (h = 1) nibble of byte l of run r (reference.rs:
+    218-243); Q5_K adds 16 where bit 2r + h of high-plane byte l is set (reference.rs:245-276).
+    Scales 4-7 exercise the split six-bit encoding."""
+    pairs = [(1, 0), (2, 1), (3, 2), (63, 63), (17, 33), (40, 5), (9, 62), (32, 16)]
+    d, dmin = 0.5, 0.25  # f16 0x3800, 0x3400
+    qs = np.array([(l % 16) | (((l * 7) % 16) << 4) for l in range(32)] * 4, np.uint8)
+    for r in range(4):
+        qs[32 * r:32 * r + 32] = np.roll(qs[32 * r:32 * r + 32], r)
+    qh = np.array([(l * 37) & 0xFF for l in range(32)], np.uint8)
+    head = np.array([0x00, 0x38, 0x00, 0x34] + _scale_min_bytes(pairs), np.uint8)
+    for t in (O.Q4_K, O.Q5_K):
+        blk = np.concatenate([head, qh, qs]) if t == O.Q5_K else np.concatenate([head, qs])
+        want = np.zeros(256, np.float32)
+        for r in range(4):
+            for h in range(2):
+                sc, m = pairs[2 * r + h]
+                for l in range(32):
+                    byte = int(qs[32 * r + l])
+                    q = (byte >> 4) if h else (byte & 15)
+                    if t == O.Q5_K and (int(qh[l]) >> (2 * r + h)) & 1:
+                        q += 16
+                    want[64 * r + 32 * h + l] = np.float32(np.float32(d * sc) * np.float32(q)) - np.float32(dmin * m)
+        assert np.array_equal(O.dequant(t, blk, 1), want), t
+
+
+def test_q6_k_block_by_hand():
+    """Element 128n + 32k + l of a Q6_K super-block: low four bits from byte l (+32 for odd k)
+    of half n's low bytes (high nibble for k >= 2), two high bits from bits 2k, 2k+1 of half n's
+    high byte l, minus 32, times d times int8 scale 2k + l/16 of the half (reference.rs:278-300)."""
+    rng = np.random.default_rng(6)
+    blk = rng.integers(0, 256, 210, dtype=np.uint8)
+    blk[208:210] = [0x00, 0x30]  # d = 0.125
+    want = np.zeros(256, np.float32)
+    for n in range(2):
+        ql, qh, sc = blk[64 * n:64 * n + 64], blk[128 + 32 * n:160 + 32 * n], blk[192 + 8 * n:200 + 8 * n].view(np.int8)
+        for k in range(4):
+            for l in range(32):
+                lo = int(ql[l + 32 * (k & 1)])
+                q = ((lo >> 4) if k >= 2 else (lo & 15)) | (((int(qh[l]) >> (2 * k)) & 3) << 4)
+                want[128 * n + 32 * k + l] = np.float32(0.125 * int(sc[2 * k + l // 16])) * np.float32(q - 32)
+    assert np.array_equal(O.dequant(O.Q6_K, blk, 1), want)
 
 
 def test_synthetic_mxfp4_matches_the_spec():
