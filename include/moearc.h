@@ -308,6 +308,12 @@ typedef struct {
      * memory (the -ncmoe mirror, moe.rs:1179-1299); each step fetches the routed experts of
      * such a block over PCIe into device slots, with no host round trip. 0: all resident. */
     unsigned int n_offload;
+    /* Residency cache of each offloaded block (the reference's ExpertCache, cache.rs:177, in
+     * place of pure streaming): n_cache device slots per block keep fetched experts across
+     * steps, so an expert routed again is not fetched again; a miss takes the least recently
+     * used slot the step does not need. 0: no cache (one slot per routed expert, refilled every
+     * step); otherwise at least n_expert_used and at most n_expert. */
+    unsigned int n_cache;
 } moearc_x_decoder_cfg;
 moearc_x_decoder *moearc_x_decoder_create(moearc_ctx *c, const moearc_x_decoder_cfg *cfg);
 void moearc_x_decoder_destroy(moearc_x_decoder *d);
@@ -325,6 +331,9 @@ int moearc_x_decoder_use_graph(moearc_x_decoder *d, int on);
  * bounded wait gave up (the step's output is then invalid). No reference counterpart: the
  * reference's decode loop has no device-side waits. */
 int moearc_x_decoder_status(moearc_x_decoder *d);
+/* Experts fetched over PCIe since create by the offloaded blocks' residency caches (0 without a
+ * cache); synchronises the stream. No reference counterpart. */
+unsigned long long moearc_x_decoder_fetched(moearc_x_decoder *d);
 /* One step without the graph and with an event after every kernel: ms[k] gets the device time
  * of kernel kind k (0 Q/K/V, 1 attention, 2 O projection, 3 MoE route, 4 MoE gate-up, 5 MoE
  * down, 6 final norm, 7 expert fetch of an offloaded block) summed over the blocks, counts[k]

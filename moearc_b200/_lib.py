@@ -111,6 +111,7 @@ SIGNATURES: dict[str, tuple] = {
     "moearc_x_decoder_step": (I, [P]),
     "moearc_x_decoder_use_graph": (I, [P, I]),
     "moearc_x_decoder_status": (I, [P]),
+    "moearc_x_decoder_fetched": (C.c_ulonglong, [P]),
     "moearc_x_decoder_profile": (I, [P, C.POINTER(F), C.POINTER(I), I]),
     "moearc_x_decoder_tensor": (P, [P, I, U, C.POINTER(UL)]),
     "moearc_x_decoder_seed": (C.c_ulonglong, [P, I, U, C.c_ulonglong]),
@@ -143,7 +144,7 @@ class DecoderCfg(C.Structure):
                 ("act", U), ("alpha", F), ("limit", F), ("n_swa", U), ("swa_pattern", U),
                 ("rope_base", F), ("rope_freq_scale", F), ("rope_ext_factor", F), ("rope_attn_factor", F),
                 ("rope_corr_lo", F), ("rope_corr_hi", F), ("rms_eps", F), ("has_sinks", U), ("n_ctx", U),
-                ("seed", C.c_ulonglong), ("n_offload", U)]
+                ("seed", C.c_ulonglong), ("n_offload", U), ("n_cache", U)]
 
 
 class MoeDesc(C.Structure):

@@ -263,6 +263,15 @@ __device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.lau
 // one slot per distinct routed expert, filled from pinned host memory each step.
 struct moe_offload {
     uint8_t *gu_stage, *dn_stage;
+    // With a residency cache (slot_of non-null) the stage holds n_cache slots of the block's
+    // own, and the experts stay there across steps: slot_of[e] is expert e's slot or -1,
+    // owner[s] the expert in slot s or -1, stamp[s] the position slot s was last used at; each
+    // step's plan lists the misses to fetch ([0] = count, then (expert, slot) pairs), and
+    // fetched counts the experts copied over PCIe.
+    int *slot_of = nullptr, *owner = nullptr, *stamp = nullptr, *plan = nullptr;
+    unsigned long long *fetched = nullptr;
+    const int *clock = nullptr;  // device position, advanced once a step: the cache's clock
+    int n_cache = 0;
 };
 
 template <typename... KArgs, typename... Args>

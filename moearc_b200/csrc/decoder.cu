@@ -21,6 +21,7 @@
 // the step stays one graph with no host round trip.
 #include <algorithm>
 #include <cmath>
+#include <climits>
 #include <vector>
 
 #include "common.cuh"
@@ -81,6 +82,7 @@ struct moearc_x_decoder {
         float *attn_norm, *ffn_norm, *sinks, *router;
         void *wqkv, *wo, *gateup, *down;  // gateup/down: device-visible host banks when offloaded
         void *gu_host, *dn_host;           // pinned host allocations of an offloaded block
+        moe_offload off;                   // an offloaded block's own residency cache (n_cache)
         uint16_t *k_pages, *v_pages;
         const unsigned *table;
         int window;
@@ -103,6 +105,7 @@ struct moearc_x_decoder {
     std::vector<void *> allocs;
     std::vector<void *> host_allocs;  // pinned (cudaHostAlloc) banks of offloaded blocks
     moe_offload off{};                // device slots the offloaded blocks' experts are fetched into
+    unsigned long long *fetched = nullptr;  // experts the residency caches fetched
     cudaGraph_t graph = nullptr;
     cudaGraphExec_t exec = nullptr;
     bool use_graph = true;
@@ -169,7 +172,7 @@ int enqueue_step(moearc_x_decoder *d, step_marks *pm = nullptr) {
         if (pm) pm->mark(c->stream, 2);
         rc = moe_forward_impl(d->moe, d->h, 1, b.ffn_norm, cfg.rms_eps, b.router, nullptr, b.gateup, b.down,
                               d->h, d->h, pm ? &pm->ev : nullptr, pm ? &pm->kind : nullptr,
-                              l < cfg.n_offload ? &d->off : nullptr);
+                              l < cfg.n_offload ? (cfg.n_cache ? &b.off : &d->off) : nullptr);
         if (rc) return rc;
     }
     if (launch_pdl(k_step_end, dim3(1), dim3(512), 0, c->stream, d->out, (const float *)d->h,
@@ -193,6 +196,7 @@ moearc_x_decoder *moearc_x_decoder_create(moearc_ctx *c, const moearc_x_decoder_
     if (g.n_layer == 0 || g.n_head % std::max(1u, g.n_head_kv) || (g.head_dim != 64 && g.head_dim != 128))
         return nullptr;
     if (g.n_head / g.n_head_kv > 8 || g.n_ctx == 0 || g.n_offload > g.n_layer) return nullptr;
+    if (g.n_cache && (g.n_cache < g.n_expert_used || g.n_cache > g.n_expert || !g.n_offload)) return nullptr;
     auto *d = new moearc_x_decoder();
     d->c = c;
     d->cfg = g;
@@ -287,6 +291,35 @@ moearc_x_decoder *moearc_x_decoder_create(moearc_ctx *c, const moearc_x_decoder_
     // one device slot per expert a token routes to
     const size_t gu_stride = moearc_x_moe_packed_bytes(&md, 0), dn_stride = moearc_x_moe_packed_bytes(&md, 1);
     void *pack_tmp = nullptr;
+    if (g.n_offload && g.n_cache) {
+        // one residency cache per offloaded block: its slots, the tables (every expert out,
+        // every slot empty and older than any position) and a plan; one shared fetch count
+        d->L.resize(g.n_layer);
+        d->fetched = static_cast<unsigned long long *>(d->alloc(sizeof(unsigned long long)));
+        const std::vector<int> older(g.n_cache, INT_MIN);
+        bool okc = d->fetched && cudaMemset(d->fetched, 0, sizeof(unsigned long long)) == cudaSuccess;
+        for (unsigned l = 0; l < g.n_offload && okc; ++l) {
+            moe_offload &o = d->L[l].off;
+            o.gu_stage = static_cast<uint8_t *>(d->alloc(g.n_cache * gu_stride));
+            o.dn_stage = static_cast<uint8_t *>(d->alloc(g.n_cache * dn_stride));
+            o.slot_of = static_cast<int *>(d->alloc(sizeof(int) * g.n_expert));
+            o.owner = static_cast<int *>(d->alloc(sizeof(int) * g.n_cache));
+            o.stamp = static_cast<int *>(d->alloc(sizeof(int) * g.n_cache));
+            o.plan = static_cast<int *>(d->alloc(sizeof(int) * (1 + 2 * 32)));
+            o.fetched = d->fetched;
+            o.clock = d->dpos;
+            o.n_cache = (int)g.n_cache;
+            okc = o.gu_stage && o.dn_stage && o.slot_of && o.owner && o.stamp && o.plan &&
+                  cudaMemset(o.slot_of, 0xFF, sizeof(int) * g.n_expert) == cudaSuccess &&
+                  cudaMemset(o.owner, 0xFF, sizeof(int) * g.n_cache) == cudaSuccess &&
+                  cudaMemcpy(o.stamp, older.data(), sizeof(int) * g.n_cache, cudaMemcpyHostToDevice) == cudaSuccess;
+        }
+        if (!okc) {
+            cudaGetLastError();
+            cudaFree(staging);
+            return fail();
+        }
+    }
     if (g.n_offload) {
         d->off.gu_stage = static_cast<uint8_t *>(d->alloc(g.n_expert_used * gu_stride));
         d->off.dn_stage = static_cast<uint8_t *>(d->alloc(g.n_expert_used * dn_stride));
@@ -409,6 +442,15 @@ int moearc_x_decoder_fill_kv(moearc_x_decoder *d, unsigned depth, unsigned long 
         if (synth(d->c, b.v_pages, n, 1, tensor_seed(seed, 13, l), 0.02f) != OK) return ERR;
     }
     return moearc_x_decoder_set_pos(d, depth);
+}
+
+unsigned long long moearc_x_decoder_fetched(moearc_x_decoder *d) {
+    if (!d || !d->fetched) return 0;
+    unsigned long long n = 0;
+    if (cudaMemcpyAsync(&n, d->fetched, sizeof(n), cudaMemcpyDeviceToHost, d->c->stream) != cudaSuccess ||
+        cudaStreamSynchronize(d->c->stream) != cudaSuccess)
+        return 0;
+    return n;
 }
 
 int moearc_x_decoder_status(moearc_x_decoder *d) {

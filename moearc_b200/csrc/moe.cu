@@ -34,6 +34,8 @@
 
 #include "common.cuh"
 #include "route.cuh"
+
+#include <climits>
 #include "tma.cuh"
 
 using namespace moearc;
@@ -951,6 +953,7 @@ struct xexp_args {
     int H;
     float *part;              // piece partials, PART_EMPTY where none is pending
     xtab *tab_pub;            // gate-up: CTA 0 publishes its tables here; down: read them (or null)
+    const int *slot_of;       // residency cache: expert -> slot of the bank (or null)
     int by_slot;              // bank holds one expert per slot (staged offload), not all experts
     int *status;
 };
@@ -1129,6 +1132,13 @@ __global__ void __launch_bounds__(XW * 32, 1) k_xexpert(xexp_args a) {
         // staged down banks are the previous kernel's output: nothing streams before the wait
         pdl_trigger();
         pdl_wait();
+    }
+    if (a.slot_of) {
+        // cached offload: the block's residency table (final before either kernel's wait
+        // returned) names each expert's slot
+        // (an unplaced expert, possible only after a reported planning error, reads slot 0)
+        if ((int)threadIdx.x < tb.G) tb.grp_slot[threadIdx.x] = max(0, __ldcg(a.slot_of + tb.grp_expert[threadIdx.x]));
+        __syncthreads();
     }
     if (lane == 0)
         for (int s = 0; s < XSTAGES && ic.q < qb; ++s) {
@@ -1397,7 +1407,8 @@ struct xfetch_args {
     int T, E, K, gating;
     const uint8_t *host;  // device-visible pointer of the pinned bank (all experts)
     size_t stride;        // packed bytes per expert (a multiple of 16)
-    uint8_t *stage;       // device slots, one per distinct routed expert
+    uint8_t *stage;       // device slots, one per distinct routed expert (or the cache's)
+    const int *plan;      // residency cache: the misses to copy, (expert, slot) pairs (or null)
 };
 
 // Copy n16 16-byte words, the grid's threads striding, eight loads in flight per thread (host
@@ -1429,14 +1440,100 @@ __global__ void __launch_bounds__(XFETCH_THREADS, 5) k_xfetch(xfetch_args a) {
         pdl_wait();
         pdl_trigger();
     }
-    xbuild(tb, a.logits, a.T, a.E, a.K, a.gating, warp, lane);
     const size_t n16 = a.stride / 16;
-    for (int s = 0; s < tb.n_slots; ++s)
-        copy16(reinterpret_cast<const uint4 *>(a.host + (size_t)tb.slot_expert[s] * a.stride),
-               reinterpret_cast<uint4 *>(a.stage + (size_t)s * a.stride), n16);
+    if (a.plan) {
+        // cached: only the plan's misses, each into the slot the plan gave it
+        const int n = __ldcg(a.plan);
+        for (int i = 0; i < n; ++i)
+            copy16(reinterpret_cast<const uint4 *>(a.host + (size_t)__ldcg(a.plan + 1 + 2 * i) * a.stride),
+                   reinterpret_cast<uint4 *>(a.stage + (size_t)__ldcg(a.plan + 2 + 2 * i) * a.stride), n16);
+    } else {
+        xbuild(tb, a.logits, a.T, a.E, a.K, a.gating, warp, lane);
+        for (int s = 0; s < tb.n_slots; ++s)
+            copy16(reinterpret_cast<const uint4 *>(a.host + (size_t)tb.slot_expert[s] * a.stride),
+                   reinterpret_cast<uint4 *>(a.stage + (size_t)s * a.stride), n16);
+    }
     if (MODE == 1) {
         pdl_trigger();
         pdl_wait();
+    }
+}
+
+// ---- residency cache of an offloaded block (the reference's ExpertCache, cache.rs:177, with
+// StaticSplit's rule that a step never evicts an expert it still needs, moe.rs:1226-1255) ------
+//
+// One warp, after the router: the step's distinct experts (ascending) that are resident keep
+// their slots and are stamped with the current position; each one that is not takes the least
+// recently used slot no expert of this step holds (an empty slot first, the lowest index on a
+// tie), evicting its owner, and is listed in the plan for the fetch kernels. Deterministic, so
+// the slot tables are the same for any timing.
+struct xplan_args {
+    const float *logits;
+    int T, E, K, gating;
+    const int *pos;  // the decode position: the cache's clock
+    int *slot_of, *owner, *stamp, *plan;
+    int n_cache;
+    unsigned long long *fetched;
+    int *status;
+};
+
+__global__ void __launch_bounds__(32) k_xplan(xplan_args a) {
+    __shared__ xtab tb;
+    extern __shared__ unsigned char used[];  // [n_cache]: a slot this step's experts hold
+    const int lane = threadIdx.x;
+    pdl_wait();
+    pdl_trigger();
+    xbuild(tb, a.logits, a.T, a.E, a.K, a.gating, 0, lane);
+    const int clock = *a.pos;
+    for (int j = lane; j < a.n_cache; j += 32) used[j] = 0;
+    __syncwarp();
+    const int S = tb.n_slots;
+    const int e = lane < S ? tb.slot_expert[lane] : -1;
+    int slot = e >= 0 ? a.slot_of[e] : -1;
+    if (slot >= 0) {
+        used[slot] = 1;
+        a.stamp[slot] = clock;
+    }
+    __syncwarp();
+    unsigned misses = __ballot_sync(0xffffffffu, e >= 0 && slot < 0);
+    int n = 0;
+    while (misses) {
+        const int ml = __ffs(misses) - 1;
+        misses &= misses - 1;
+        const int me = __shfl_sync(0xffffffffu, e, ml);
+        // least recently used free slot: smallest stamp (empty slots hold INT_MIN), lowest index
+        int best = INT_MAX, bi = INT_MAX;
+        for (int j = lane; j < a.n_cache; j += 32) {
+            const int key = used[j] ? INT_MAX : a.stamp[j];
+            if (key < best) {
+                best = key;
+                bi = j;
+            }
+        }
+        const int kmin = __reduce_min_sync(0xffffffffu, best);
+        const int v = (int)__reduce_min_sync(0xffffffffu, best == kmin ? (unsigned)bi : 0xFFFFFFFFu);
+        if (kmin == INT_MAX) {
+            // every slot is held by this step (fewer slots than distinct experts): refused by
+            // the host at create; reported, and the expert stays unplaced
+            if (lane == 0) atomicOr(a.status, STATUS_RANGE);
+            break;
+        }
+        if (lane == 0) {
+            const int old = a.owner[v];
+            if (old >= 0) a.slot_of[old] = -1;
+            a.owner[v] = me;
+            a.slot_of[me] = v;
+            a.stamp[v] = clock;
+            used[v] = 1;
+            a.plan[1 + 2 * n] = me;
+            a.plan[2 + 2 * n] = v;
+        }
+        ++n;
+        __syncwarp();
+    }
+    if (lane == 0) {
+        a.plan[0] = n;
+        if (a.fetched) *a.fetched += (unsigned long long)n;
     }
 }
 
@@ -2286,7 +2383,16 @@ int moe_forward_impl(moearc_x_moe *m, const float *x, unsigned n_tokens, const f
         }
         const size_t gu_stride = (size_t)2 * m->ntr_i * m->nkt_h * m->tile_bytes;
         const size_t dn_stride = (size_t)m->ntr_h * m->nkt_i * m->tile_bytes;
-        xfetch_args fa{m->logits, T, m->E, m->K, m->gating, nullptr, 0, nullptr};
+        xfetch_args fa{m->logits, T, m->E, m->K, m->gating, nullptr, 0, nullptr, nullptr};
+        if (off && off->slot_of) {
+            // residency cache: plan the step's slots (hits stay, misses evict the least recently
+            // used slot), then fetch only the misses
+            xplan_args pa{m->logits, T, m->E, m->K, m->gating, off->clock, off->slot_of, off->owner, off->stamp,
+                          off->plan, off->n_cache, off->fetched, m->status};
+            if (launch_pdl(k_xplan, dim3(1), dim3(32), (size_t)off->n_cache, c->stream, pa) != cudaSuccess)
+                return ERR;
+            fa.plan = off->plan;
+        }
         if (off) {
             fa.host = static_cast<const uint8_t *>(gateup_packed);
             fa.stride = gu_stride;
@@ -2326,6 +2432,7 @@ int moe_forward_impl(moearc_x_moe *m, const float *x, unsigned n_tokens, const f
         // offloaded blocks: the down fetch runs between the two kernels and the down kernel
         // builds its own tables after its wait
         xa.tab_pub = off ? nullptr : static_cast<xtab *>(m->x_tab_pub);
+        xa.slot_of = off ? off->slot_of : nullptr;
         xa.status = m->status;
         const bool mx = m->wtype == T_MXFP4;
         // More than half an SM's shared memory, so no SM takes two gate-up CTAs: at launch the

@@ -48,6 +48,9 @@ class DecoderConfig:
     # blocks 0 .. n_offload-1 keep their experts in pinned host memory, fetched over PCIe each
     # step (the -ncmoe mirror, moe.rs:1179-1299); 0 = all resident
     n_offload: int = 0
+    # device slots per offloaded block that keep fetched experts across steps (the reference's
+    # ExpertCache); 0 = pure streaming, else n_expert_used <= n_cache <= n_expert
+    n_cache: int = 0
 
     def yarn(self, factor: float, n_ctx_orig: int, beta_fast: float = 32.0, beta_slow: float = 1.0):
         """YaRN parameters the way reference.rs:572-591 derives them (RopeScaling::yarn)."""
@@ -120,6 +123,10 @@ class Decoder:
 
     def use_graph(self, on: bool) -> None:
         self.ctx._finish(self.ctx.lib.moearc_x_decoder_use_graph(self.h, 1 if on else 0), "use_graph")
+
+    def fetched(self) -> int:
+        """Experts the offloaded blocks' residency caches fetched over PCIe since create."""
+        return self.ctx.lib.moearc_x_decoder_fetched(self.h)
 
     def status(self) -> int:
         """Reads and clears the kernels' device status words: 0, or nonzero when a bounded

@@ -14,6 +14,7 @@ import pytest
 
 import oracle as O
 from moearc_b200 import Context
+from moearc_b200.kernels import BadArgument
 from moearc_b200.decoder import Decoder, DecoderConfig, unpack_dense
 
 pytestmark = pytest.mark.gpu
@@ -142,6 +143,43 @@ def test_expert_offload_matches_the_resident_decoder(ctx, etype, n_expert, k):
     assert res.status() == 0 and off.status() == 0
     off.close()
     res.close()
+
+
+@pytest.mark.parametrize("etype,n_expert,k", [(O.MXFP4, 8, 2), (O.Q4_0, 16, 4)])
+@pytest.mark.parametrize("extra", [1, None])  # slots beyond k (evictions every step), or every expert
+def test_expert_residency_cache_gives_the_resident_bits_and_fetches_less(ctx, etype, n_expert, k, extra):
+    """Offloaded blocks with a residency cache (cfg.n_cache device slots per block, the
+    reference's ExpertCache with StaticSplit's never-evict-what-the-step-needs rule): the output
+    is bit-identical to the all-resident decoder, the first step fetches every routed expert,
+    no step fetches more than pure streaming would, and a cache that holds every expert stops
+    fetching once each has been seen."""
+    n_cache = n_expert if extra is None else k + extra
+    kw = dict(n_layer=3, n_embd=256, n_head=8, n_head_kv=2, head_dim=64, n_expert=n_expert,
+              n_expert_used=k, n_ff=128, expert_type=etype, n_swa=40, swa_pattern=2, n_ctx=128,
+              seed=0x0FF1)
+    res = Decoder(ctx, DecoderConfig(**kw))
+    cached = Decoder(ctx, DecoderConfig(**kw, n_offload=2, n_cache=n_cache))
+    steps, prev = 16, 0
+    for pos in range(steps):
+        x = O.synth_normal_f32(0x2100 + pos, kw["n_embd"], 1.0)
+        for d in (res, cached):
+            d.set_input(x)
+            d.step()
+        a, b = res.output(), cached.output()
+        assert np.array_equal(a.view(np.uint32), b.view(np.uint32)), f"token {pos}"
+        n = cached.fetched()
+        if pos == 0:
+            assert n == 2 * k  # two offloaded blocks, each fetches its k distinct experts
+        assert 0 <= n - prev <= 2 * k
+        prev = n
+    if extra is None:
+        assert prev <= 2 * n_expert  # each expert of each block fetched at most once
+    assert prev < steps * 2 * k
+    assert res.status() == 0 and cached.status() == 0
+    cached.close()
+    res.close()
+    with pytest.raises(BadArgument):
+        Decoder(ctx, DecoderConfig(**kw, n_offload=2, n_cache=k - 1))  # fewer slots than a step needs
 
 
 @pytest.mark.parametrize("etype", [O.MXFP4, O.Q4_0])
