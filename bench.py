@@ -229,8 +229,20 @@ def gpu_run(args, cfg, rank: int, world: int, dist) -> dict:
     host_out = lib.moearc_x_host_alloc(4 * H)
     C.memmove(host_in, np.random.default_rng(rank).standard_normal(H).astype(np.float32).ctypes.data, 4 * H)
     lib.moearc_copy_h2d(ctx.raw, dec.in_ptr, host_in, 4 * H)
+    # with a residency cache the routing must change from step to step as it does when decoding
+    # text: each step takes the next of 64 distinct N(0, 1) inputs from pinned host memory
+    n_pool = 64 if cfg.n_cache else 0
+    pool = lib.moearc_x_host_alloc(4 * H * max(n_pool, 1))
+    if n_pool:
+        C.memmove(pool, np.random.default_rng(100 + rank).standard_normal((n_pool, H)).astype(np.float32).ctypes.data,
+                  4 * H * n_pool)
 
-    for _ in range(args.warmup):
+    def next_input(i):
+        if n_pool:
+            lib.moearc_copy_h2d_async(ctx.raw, dec.in_ptr, pool + 4 * H * (i % n_pool), 4 * H)
+
+    for i in range(args.warmup):
+        next_input(i)
         dec.step()
     ctx.sync()
 
@@ -249,16 +261,19 @@ def gpu_run(args, cfg, rank: int, world: int, dist) -> dict:
     if dist:
         dist.barrier()
     ctx.sync()
+    fetched0 = dec.fetched()
     ctx.timer_start()
-    for _ in range(args.steps):
+    for i in range(args.steps):
+        next_input(i)
         dec.step()
     ms_total = ctx.timer_stop()
+    fetched = dec.fetched() - fetched0
 
     # end to end through the public API: host input in, host output out, every step
     ctx.sync()
     t1 = time.perf_counter()
-    for _ in range(args.steps):
-        lib.moearc_copy_h2d_async(ctx.raw, dec.in_ptr, host_in, 4 * H)
+    for i in range(args.steps):
+        lib.moearc_copy_h2d_async(ctx.raw, dec.in_ptr, pool + 4 * H * (i % n_pool) if n_pool else host_in, 4 * H)
         dec.step()
         lib.moearc_x_copy_d2h_async(ctx.raw, host_out, dec.out_ptr, 4 * H)
         ctx.sync()
@@ -269,10 +284,12 @@ def gpu_run(args, cfg, rank: int, world: int, dist) -> dict:
     assert np.all(np.isfinite(out)), "non-finite decoder output"
     lib.moearc_x_host_free(host_in)
     lib.moearc_x_host_free(host_out)
+    lib.moearc_x_host_free(pool)
     dec.close()
     ctx.close()
     return {"ms_total": ms_total, "e2e_s": e2e_s, "kernel_ms": kernel_ms, "counts": [cnt[i] for i in range(8)],
-            "launches_per_step": launches_per_step, "clocks": clocks, "build_s": build_s, "pcie_gbs": pcie}
+            "launches_per_step": launches_per_step, "clocks": clocks, "build_s": build_s, "pcie_gbs": pcie,
+            "fetched_per_step": fetched / args.steps}
 
 
 # ---- MoE prefill on the tensor cores, one GPU -------------------------------------
@@ -583,6 +600,8 @@ def main() -> None:
     ap.add_argument("--experts", type=int, default=128, help="prefill: experts (configs[3]: 128)")
     ap.add_argument("--offload", type=int, default=0,
                     help="blocks whose experts stay in pinned host memory (configs[2] mode (b): 30)")
+    ap.add_argument("--cache", type=int, default=0,
+                    help="with --offload: device slots per offloaded block that keep fetched experts (0: none)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.config == "prefill":
@@ -599,9 +618,13 @@ def main() -> None:
     if args.layers:
         cfg.n_layer = args.layers
     cfg.n_offload = min(args.offload, cfg.n_layer)
+    cfg.n_cache = args.cache if cfg.n_offload else 0
     residency = ("experts resident in HBM" if not cfg.n_offload else
                  f"mode (b): experts of blocks 0-{cfg.n_offload - 1} in pinned host memory, the routed ones "
-                 f"fetched over PCIe every step")
+                 f"fetched over PCIe every step" if not cfg.n_cache else
+                 f"mode (b) with a residency cache: experts of blocks 0-{cfg.n_offload - 1} in pinned host memory, "
+                 f"{cfg.n_cache} device slots per block keep fetched experts (least recently used evicted), "
+                 f"a new N(0,1) input every step")
     workload = (f"configs[{2 if args.config == '120b' else 1}] gpt-oss-{args.config} shape, batch-1 decode, "
                 f"depth {args.depth}, {residency}")
     config = {"workload": workload, "n_layer": cfg.n_layer, "n_embd": cfg.n_embd, "n_expert": cfg.n_expert,
@@ -698,7 +721,12 @@ def main() -> None:
     }
     if cfg.n_offload:
         # mode (b) is bound by PCIe: the offloaded blocks' routed experts cross it every step
+        # (with a cache, only the misses: the experts counted as fetched)
         pcie_b = cfg.n_offload * expert_b
+        if cfg.n_cache:
+            pcie_b = r["fetched_per_step"] * expert_b / cfg.n_expert_used
+            line["cache"] = {"slots_per_block": cfg.n_cache, "experts_fetched_per_step": r["fetched_per_step"],
+                             "hit_rate": 1.0 - r["fetched_per_step"] / (cfg.n_offload * cfg.n_expert_used)}
         pcie_gbs = pcie_b / (ms_step / 1000.0) / 1e9
         line["roofline_hbm_gate_up"] = line["roofline"]
         line["roofline"] = {"bound": "pcie", "kernel": "expert fetch of the offloaded blocks (whole step)",
