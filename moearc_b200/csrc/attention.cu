@@ -56,8 +56,10 @@ __device__ __forceinline__ bool device_span(const int *dpos, int window, int max
     n_kv = (size_t)(*dpos) + 1;
     kv_begin = (window > 0 && n_kv > (size_t)window) ? n_kv - (size_t)window : 0;
     const size_t span = n_kv - kv_begin;
+    // at least 256 keys a split: below that a second split costs more (its partials, the
+    // arrival and the merge) than the keys it takes off the first
     kps = (span + max_splits - 1) / max_splits;
-    kps = ((kps + 63) / 64) * 64;
+    kps = ((kps + 255) / 256) * 256;
     n_splits = (int)((span + kps - 1) / kps);
     return (int)blockIdx.y < n_splits;
 }
