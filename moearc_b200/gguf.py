@@ -148,6 +148,50 @@ class GgufFile:
         return self.tensor(f"blk.{block}.{suffix}")
 
 
+EXPERT_BANKS = (FFN_GATE_EXPS, FFN_UP_EXPS, FFN_DOWN_EXPS)
+
+
+@dataclass(frozen=True)
+class MoeLayout:
+    """What sizing an expert pool or residency cache needs to know about a model file (the
+    expert half of the reference's ModelInfo, crates/moearc-model/src/lib.rs:142-230)."""
+    architecture: str
+    block_count: int
+    moe_blocks: tuple[int, ...]   # blocks that hold stacked expert banks
+    n_expert: int
+    n_expert_used: int
+    per_expert_bytes: int         # gate + up + down of one expert (the largest, if they differ)
+    per_expert_uniform: bool      # every MoE block's experts are the same size
+    expert_bytes: int             # every stacked expert bank
+    dense_bytes: int              # every other tensor
+
+
+def moe_layout(g: GgufFile) -> MoeLayout:
+    """The expert geometry of a MoE model file: which blocks hold stacked banks, one expert's
+    bytes per block (each bank sliced exactly, tensors.rs:237-289), and the split of the file's
+    weights into expert and dense bytes. ValueError for a file without experts."""
+    arch = g.str("general.architecture")
+    n_expert = g.u64(f"{arch}.expert_count", default=0)
+    if not n_expert:
+        raise ValueError(f"{g.path}: a {arch} file with no {arch}.expert_count is not a mixture of experts")
+    used = g.u64(f"{arch}.expert_used_count")
+    blocks = g.u64(f"{arch}.block_count")
+    expert_bytes = dense_bytes = 0
+    per_block: dict[int, int] = {}
+    for t in g.tensors():
+        parts = t.name.split(".", 2)
+        if len(parts) == 3 and parts[0] == "blk" and parts[1].isdigit() and parts[2] in EXPERT_BANKS:
+            if t.dims[-1] != n_expert:
+                raise ValueError(f"{t.name} stacks {t.dims[-1]} experts, the file says {n_expert}")
+            expert_bytes += t.nbytes
+            per_block[int(parts[1])] = per_block.get(int(parts[1]), 0) + g.slice_last(t.name, 0).nbytes
+        else:
+            dense_bytes += t.nbytes
+    sizes = set(per_block.values())
+    return MoeLayout(arch, blocks, tuple(sorted(per_block)), n_expert, used, max(sizes, default=0),
+                     len(sizes) <= 1, expert_bytes, dense_bytes)
+
+
 @dataclass
 class MoeBlockBanks:
     """A MoE block's tensors on the device, as stored in the file."""

@@ -14,7 +14,7 @@ import numpy as np
 import pytest
 
 import gguf_writer as W
-from moearc_b200.gguf import GgufError, GgufFile
+from moearc_b200.gguf import GgufError, GgufFile, moe_layout
 
 MXFP4, Q4_0, F32 = 39, 2, 0
 
@@ -225,3 +225,29 @@ def test_the_mapping_outlives_a_rename_of_the_file(tmp_path):
     os.rename(path, str(tmp_path / "moved.gguf"))
     assert g.tensor("blk.0.ffn_gate_exps.weight").bytes().tobytes() == banks["ffn_gate_exps"]
     g.close()
+
+
+def test_moe_layout_sizes_the_expert_pool(tmp_path):
+    """The expert half of the reference's ModelInfo (lib.rs:142-230): the blocks with stacked
+    banks, one expert's bytes, and the expert / dense split of the weights."""
+    H, I, E = 64, 96, 4
+    w, banks = model_writer(H=H, I=I, E=E)
+    w.add("gpt-oss.block_count", W.U32, 2)
+    w.add_tensor("blk.1.ffn_gate_exps.weight", (H, I, E), MXFP4, bytes(H * I * E // 32 * 17))
+    w.add_tensor("blk.1.ffn_up_exps.weight", (H, I, E), MXFP4, bytes(H * I * E // 32 * 17))
+    w.add_tensor("blk.1.ffn_down_exps.weight", (I, H, E), MXFP4, bytes(H * I * E // 32 * 17))
+    w.add_tensor("output_norm.weight", (H,), F32, bytes(4 * H))
+    path = str(tmp_path / "m.gguf")
+    w.write(path)
+    with GgufFile(path) as g:
+        lay = moe_layout(g)
+        per = 3 * H * I // 32 * 17
+        assert (lay.architecture, lay.block_count, lay.moe_blocks) == ("gpt-oss", 2, (0, 1))
+        assert (lay.n_expert, lay.n_expert_used, lay.per_expert_bytes, lay.per_expert_uniform) == (E, 2, per, True)
+        assert lay.expert_bytes == 2 * E * per
+        assert lay.dense_bytes == 4 * H * E + 32 * 3 * 2 // 32 * 18 + 4 * H
+    d = W.GgufWriter().add("general.architecture", W.STRING, "llama")
+    d.write(str(tmp_path / "dense.gguf"))
+    with GgufFile(str(tmp_path / "dense.gguf")) as g:
+        with pytest.raises(ValueError, match="not a mixture of experts"):
+            moe_layout(g)
