@@ -160,6 +160,16 @@ class Decoder:
             self.ctx._finish(self.ctx.lib.moearc_copy_d2h(self.ctx.raw, out.ctypes.data, p, n.value), "tensor")
         return out
 
+    def set_tensor(self, which: int, layer: int, data: np.ndarray) -> None:
+        """Overwrite one block's tensor (the `tensor` numbering) with `data`, which must have its
+        exact size; ordered before the next step on the context stream."""
+        n = C.c_ulong()
+        p = self.ctx.lib.moearc_x_decoder_tensor(self.h, which, layer, C.byref(n))
+        data = np.ascontiguousarray(data)
+        if not p or data.nbytes != n.value:
+            raise BadArgument(f"tensor {which} of block {layer} holds {n.value} bytes, not {data.nbytes}")
+        self.ctx._finish(self.ctx.lib.moearc_copy_h2d(self.ctx.raw, p, data.ctypes.data, data.nbytes), "tensor")
+
     def seed(self, kind: int, layer: int) -> int:
         return self.ctx.lib.moearc_x_decoder_seed(self.h, kind, layer, self.cfg.seed)
 

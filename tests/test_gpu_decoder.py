@@ -8,6 +8,7 @@ bf16 projections by unpacking the packed tiles, the f32 tensors by download — 
 KV pools.
 """
 import ctypes as C
+import os
 
 import numpy as np
 import pytest
@@ -180,6 +181,64 @@ def test_expert_residency_cache_gives_the_resident_bits_and_fetches_less(ctx, et
     res.close()
     with pytest.raises(BadArgument):
         Decoder(ctx, DecoderConfig(**kw, n_offload=2, n_cache=k - 1))  # fewer slots than a step needs
+
+
+def _steer(dec: Decoder, layer: int, experts) -> None:
+    """Make block `layer` route to `experts` whatever the activation: the router row of each
+    named expert has one nonzero column, 0, whose normalised activation the step input keeps
+    large and positive (ffn_norm[0] = 1), so those logits are positive and distinct and every
+    other logit is exactly 0."""
+    H, E = dec.cfg.n_embd, dec.cfg.n_expert
+    norm = dec.tensor(1, layer, np.float32)
+    norm[0] = 1.0
+    dec.set_tensor(1, layer, norm)
+    w = np.zeros((E, H), np.float32)
+    for r, e in enumerate(experts):
+        w[e, 0] = 2.0 - 0.25 * r
+    dec.set_tensor(3, layer, w)
+
+
+@pytest.mark.parametrize("source,n_expert,k,n_cache,steps", [
+    ("random", 16, 4, 6, 24),
+    ("prose", 128, 4, 12, 48),   # blocks 0 and 1 of the reference's captured gpt-oss-120b trace
+])
+def test_residency_cache_fetches_exactly_what_the_host_replay_predicts(ctx, source, n_expert, k, n_cache, steps):
+    """The device plan (k_xplan) against its host replay (moearc_b200.residency, policy
+    "block"): the decoder's router is steered to a given routing each step and the experts the
+    two offloaded blocks fetch over PCIe are counted step by step; they equal the replay's
+    misses exactly, so the hit rates the replay reports for captured traces are the device's."""
+    from moearc_b200.residency import Trace, simulate
+    if source == "random":
+        rng = np.random.default_rng(0x5EED)
+        hot = [rng.permutation(n_expert)[: k + 3] for _ in range(2)]  # skewed: a few hot experts
+        route = [[sorted(rng.choice(hot[l] if rng.random() < 0.7 else np.arange(n_expert), k, replace=False))
+                  for l in range(2)] for _ in range(steps)]
+    else:
+        z = np.load(os.path.join(os.path.dirname(__file__), "golden", "traces_gptoss120b.npz"))
+        pairs = z[source][:steps]
+        route = [[[int(e) for l2, e in s if l2 == l] for l in range(2)] for s in pairs]
+    kw = dict(n_layer=3, n_embd=256, n_head=8, n_head_kv=2, head_dim=64, n_expert=n_expert,
+              n_expert_used=k, n_ff=128, expert_type=O.MXFP4, n_swa=40, swa_pattern=2, n_ctx=128,
+              seed=0x0FF2)
+    dec = Decoder(ctx, DecoderConfig(**kw, n_offload=2, n_cache=n_cache))
+    prev, got, want = 0, [], []
+    trace = Trace([])
+    for pos in range(steps):
+        for l in range(2):
+            _steer(dec, l, route[pos][l])
+        x = O.synth_normal_f32(0x2200 + pos, kw["n_embd"], 1.0)
+        x[0] = 1000.0
+        dec.set_input(x)
+        dec.step()
+        n = dec.fetched()
+        got.append(n - prev)
+        prev = n
+        trace.steps.append([(l, e) for l in range(2) for e in route[pos][l]])
+        want.append(simulate(trace, n_cache, "block").misses - sum(want))
+    assert dec.status() == 0
+    dec.close()
+    assert got == want
+    assert sum(got) < steps * 2 * k  # the cache kept something
 
 
 @pytest.mark.parametrize("etype", [O.MXFP4, O.Q4_0])
