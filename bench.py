@@ -205,6 +205,47 @@ def pcie_h2d_gbs(ctx, nbytes: int = 256 << 20, reps: int = 5) -> float:
     return nbytes * reps / (ms / 1000.0) / 1e9
 
 
+class TraceRoute:
+    """Routes blocks 0 .. n-1 of a decoder as a captured gpt-oss-120b decode trace routed them
+    (the reference's bench/traces/gptoss120b-*.decode.ndjson, packed under tests/golden): before
+    each step every such block's router gets one nonzero column, 0, with positive, distinct
+    values at that step's experts, and ffn_norm[0] = 1; the step inputs keep activation 0 large
+    and positive, so those experts win the top-k and every other logit is exactly 0."""
+
+    def __init__(self, dec, name: str, n: int):
+        import numpy as np
+
+        z = np.load(os.path.join(os.path.dirname(os.path.abspath(__file__)), "tests", "golden",
+                                 "traces_gptoss120b.npz"))
+        pairs = z[name]
+        self.steps = [[[int(e) for l2, e in s if l2 == l] for l in range(n)] for s in pairs]
+        self.dec, self.n, self.i, self.history = dec, n, 0, []
+        self.w = np.zeros((dec.cfg.n_expert, dec.cfg.n_embd), np.float32)
+        for l in range(n):
+            norm = dec.tensor(1, l, np.float32)
+            norm[0] = 1.0
+            dec.set_tensor(1, l, norm)
+
+    def apply(self) -> None:
+        """Set the routers for the next step (blocking copies, outside any timed region)."""
+        s = self.steps[self.i % len(self.steps)]
+        for l, es in enumerate(s):
+            self.w[:, 0] = 0.0
+            for r, e in enumerate(es):
+                self.w[e, 0] = 2.0 - 0.25 * r
+            self.dec.set_tensor(3, l, self.w)
+        self.history.append(s)
+        self.i += 1
+
+    def replay_fetches(self, n_cache: int, upto: int) -> int:
+        """Experts the device cache must have fetched over the first `upto` steps (the host
+        replay of its slot rule)."""
+        from moearc_b200.residency import Trace, simulate
+
+        t = Trace([[(l, e) for l, es in enumerate(s) for e in es] for s in self.history[:upto]])
+        return simulate(t, n_cache, "block").misses if upto else 0
+
+
 def gpu_run(args, cfg, rank: int, world: int, dist) -> dict:
     import ctypes as C
 
@@ -234,10 +275,15 @@ def gpu_run(args, cfg, rank: int, world: int, dist) -> dict:
     n_pool = 64 if cfg.n_cache else 0
     pool = lib.moearc_x_host_alloc(4 * H * max(n_pool, 1))
     if n_pool:
-        C.memmove(pool, np.random.default_rng(100 + rank).standard_normal((n_pool, H)).astype(np.float32).ctypes.data,
-                  4 * H * n_pool)
+        xs = np.random.default_rng(100 + rank).standard_normal((n_pool, H)).astype(np.float32)
+        if args.trace:
+            xs[:, 0] = 1000.0  # keeps the steered routers' one column decisive
+        C.memmove(pool, xs.ctypes.data, 4 * H * n_pool)
+    route = TraceRoute(dec, args.trace, cfg.n_offload) if args.trace else None
 
     def next_input(i):
+        if route:
+            route.apply()
         if n_pool:
             lib.moearc_copy_h2d_async(ctx.raw, dec.in_ptr, pool + 4 * H * (i % n_pool), 4 * H)
 
@@ -253,6 +299,8 @@ def gpu_run(args, cfg, rank: int, world: int, dist) -> dict:
     kernel_ms = {k: ms[i] for i, k in enumerate(["qkv", "attention", "o_proj", "moe_route", "moe_gate_up",
                                                   "moe_down", "final_norm", "expert_fetch"])}
     launches_per_step = sum(cnt[i] for i in range(8))
+    if route:
+        route.history.append(route.history[-1])  # the profiled step repeated the last routing
 
     sampler = ClockSampler() if rank == 0 else None
     if sampler:
@@ -262,22 +310,42 @@ def gpu_run(args, cfg, rank: int, world: int, dist) -> dict:
         dist.barrier()
     ctx.sync()
     fetched0 = dec.fetched()
-    ctx.timer_start()
-    for i in range(args.steps):
-        next_input(i)
-        dec.step()
-    ms_total = ctx.timer_stop()
+    h0 = len(route.history) if route else 0
+    if route:
+        # the routers are set between steps, so each step is timed on its own
+        ms_total = 0.0
+        for i in range(args.steps):
+            route.apply()
+            lib.moearc_copy_h2d_async(ctx.raw, dec.in_ptr, pool + 4 * H * (i % n_pool), 4 * H)
+            ctx.timer_start()
+            dec.step()
+            ms_total += ctx.timer_stop()
+    else:
+        ctx.timer_start()
+        for i in range(args.steps):
+            next_input(i)
+            dec.step()
+        ms_total = ctx.timer_stop()
     fetched = dec.fetched() - fetched0
+    replay = (route.replay_fetches(cfg.n_cache, len(route.history)) - route.replay_fetches(cfg.n_cache, h0)
+              if route else None)
 
     # end to end through the public API: host input in, host output out, every step
     ctx.sync()
+    e2e_s = 0.0
     t1 = time.perf_counter()
     for i in range(args.steps):
+        if route:
+            route.apply()
+            t1 = time.perf_counter()
         lib.moearc_copy_h2d_async(ctx.raw, dec.in_ptr, pool + 4 * H * (i % n_pool) if n_pool else host_in, 4 * H)
         dec.step()
         lib.moearc_x_copy_d2h_async(ctx.raw, host_out, dec.out_ptr, 4 * H)
         ctx.sync()
-    e2e_s = time.perf_counter() - t1
+        if route:
+            e2e_s += time.perf_counter() - t1
+    if not route:
+        e2e_s = time.perf_counter() - t1
     clocks = sampler.stop() if sampler else None
     pcie = pcie_h2d_gbs(ctx) if cfg.n_offload else None
     out = np.ctypeslib.as_array(C.cast(host_out, C.POINTER(C.c_float)), (H,)).copy()
@@ -289,7 +357,7 @@ def gpu_run(args, cfg, rank: int, world: int, dist) -> dict:
     ctx.close()
     return {"ms_total": ms_total, "e2e_s": e2e_s, "kernel_ms": kernel_ms, "counts": [cnt[i] for i in range(8)],
             "launches_per_step": launches_per_step, "clocks": clocks, "build_s": build_s, "pcie_gbs": pcie,
-            "fetched_per_step": fetched / args.steps}
+            "fetched_per_step": fetched / args.steps, "replay_fetches": replay, "fetched": fetched}
 
 
 # ---- MoE prefill on the tensor cores, one GPU -------------------------------------
@@ -602,6 +670,9 @@ def main() -> None:
                     help="blocks whose experts stay in pinned host memory (configs[2] mode (b): 30)")
     ap.add_argument("--cache", type=int, default=0,
                     help="with --offload: device slots per offloaded block that keep fetched experts (0: none)")
+    ap.add_argument("--trace", default=None, choices=["prose", "code", "reasoning"],
+                    help="with --offload and --cache on the 120b shape: route the offloaded blocks as the "
+                         "captured gpt-oss-120b decode trace of that name did")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.config == "prefill":
@@ -624,7 +695,10 @@ def main() -> None:
                  f"fetched over PCIe every step" if not cfg.n_cache else
                  f"mode (b) with a residency cache: experts of blocks 0-{cfg.n_offload - 1} in pinned host memory, "
                  f"{cfg.n_cache} device slots per block keep fetched experts (least recently used evicted), "
-                 f"a new N(0,1) input every step")
+                 + (f"the offloaded blocks routed as the captured gpt-oss-120b {args.trace} decode trace"
+                    if args.trace else "a new N(0,1) input every step"))
+    if args.trace and not (cfg.n_cache and args.config == "120b" and cfg.n_offload <= 36):
+        raise SystemExit("--trace needs --config 120b, --offload and --cache")
     workload = (f"configs[{2 if args.config == '120b' else 1}] gpt-oss-{args.config} shape, batch-1 decode, "
                 f"depth {args.depth}, {residency}")
     config = {"workload": workload, "n_layer": cfg.n_layer, "n_embd": cfg.n_embd, "n_expert": cfg.n_expert,
@@ -727,6 +801,10 @@ def main() -> None:
             pcie_b = r["fetched_per_step"] * expert_b / cfg.n_expert_used
             line["cache"] = {"slots_per_block": cfg.n_cache, "experts_fetched_per_step": r["fetched_per_step"],
                              "hit_rate": 1.0 - r["fetched_per_step"] / (cfg.n_offload * cfg.n_expert_used)}
+            if args.trace:
+                # the fetch count the host replay of the slot rule predicts for the same steps
+                line["cache"].update(trace=args.trace, fetched=r["fetched"], replay_fetches=r["replay_fetches"],
+                                     matches_replay=r["fetched"] == r["replay_fetches"])
         pcie_gbs = pcie_b / (ms_step / 1000.0) / 1e9
         line["roofline_hbm_gate_up"] = line["roofline"]
         line["roofline"] = {"bound": "pcie", "kernel": "expert fetch of the offloaded blocks (whole step)",
