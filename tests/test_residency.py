@@ -233,3 +233,39 @@ def test_the_command_line_prints_a_table(tmp_path, capsys):
     main([str(f), "--capacity", "4", "--per-block", "2", "--expert-mib", "1"])
     out = capsys.readouterr().out
     assert "working set 5" in out and "lru" in out and "2/block" in out
+
+
+def test_the_bench_steers_each_offloaded_block_to_the_trace(captured):
+    """bench.py --trace: the router of each steered block has one nonzero column holding
+    positive, distinct values at exactly that step's experts, ffn_norm[0] is set to 1 once, and
+    the fetch prediction is the block replay of the steps applied."""
+    import bench
+
+    class FakeDecoder:
+        class cfg:
+            n_expert, n_embd = 128, 64
+
+        def __init__(self):
+            self.t = {}
+
+        def tensor(self, which, layer, dtype):
+            return np.full(self.cfg.n_embd, -0.5, np.float32)
+
+        def set_tensor(self, which, layer, data):
+            self.t[(which, layer)] = np.array(data)
+
+    dec = FakeDecoder()
+    route = bench.TraceRoute(dec, "code", 3)
+    assert all(dec.t[(1, l)][0] == 1.0 and dec.t[(1, l)][1] == -0.5 for l in range(3))
+    steps = [[[e for l2, e in s if l2 == l] for l in range(3)] for s in captured["code"].steps[:5]]
+    for s in steps:
+        route.apply()
+        for l in range(3):
+            w = dec.t[(3, l)]
+            assert not w[:, 1:].any()
+            col = w[:, 0]
+            assert sorted(np.flatnonzero(col)) == sorted(s[l]) and np.all(col[s[l]] > 0)
+            assert len(set(col[s[l]])) == len(s[l])
+    t = Trace([[(l, e) for l in range(3) for e in s[l]] for s in steps])
+    assert route.replay_fetches(8, 5) == simulate(t, 8, "block").misses
+    assert route.replay_fetches(8, 0) == 0
