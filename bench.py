@@ -4,6 +4,9 @@
     python bench.py --impl reference ...   # the reference's CPU path, timed on the host cores
     python bench.py --offload 30 ...       # configs[2] mode (b): experts of blocks 0-29 in
                                            # pinned host memory, fetched over PCIe every step
+    python bench.py --offload 30 --cache 32 [--trace code]
+                                           # with 32 HBM slots per offloaded block keeping
+                                           # fetched experts; routed as a captured trace
 
 A step is one batch-1 decode token through the whole synthetic decoder (36 blocks: RMSNorm,
 Q/K/V, RoPE, paged-KV append, attention with sinks over a full or 128-key window, O
@@ -648,6 +651,25 @@ def batch_main(args) -> None:
     print(json.dumps(line))
 
 
+def slowest_rank(ms_total: float, e2e_s: float, dist) -> tuple[float, float]:
+    """The timed region's device time and the end-to-end wall time, each the maximum over the
+    ranks (every rank calls this, the same collectives in the same order)."""
+    if not dist:
+        return ms_total, e2e_s
+    import torch
+
+    t = torch.tensor([ms_total, e2e_s], dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    dist.barrier()
+    return float(t[0]), float(t[1])
+
+
+def replica_throughput(world: int, steps: int, ms_total: float, e2e_s: float) -> tuple[float, float]:
+    """Whole-job tokens per second of `world` independent replicas that each decoded `steps`
+    tokens, over the slowest rank's device time and end-to-end time."""
+    return world * steps / (ms_total / 1000.0), world * steps / e2e_s
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -733,22 +755,13 @@ def main() -> None:
         tdist.init_process_group("gloo", timeout=datetime.timedelta(seconds=300))
         dist = tdist
     r = gpu_run(args, cfg, rank, world, dist)
-    ms_total = r["ms_total"]
+    ms_total, e2e_s = slowest_rank(r["ms_total"], r["e2e_s"], dist)
     if dist:
-        import torch
-
-        t = torch.tensor([ms_total, r["e2e_s"]], dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms_total, e2e_s = float(t[0]), float(t[1])
-        dist.barrier()
         dist.destroy_process_group()
-    else:
-        e2e_s = r["e2e_s"]
     if rank != 0:
         return
     ms_step = ms_total / args.steps
-    value = world * args.steps / (ms_total / 1000.0)
-    e2e = world * args.steps / e2e_s
+    value, e2e = replica_throughput(world, args.steps, ms_total, e2e_s)
 
     peak, peak_kind = load_peaks()
     H, I, k = cfg.n_embd, cfg.n_ff, cfg.n_expert_used
