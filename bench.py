@@ -218,10 +218,18 @@ class TraceRoute:
     def __init__(self, dec, name: str, n: int):
         import numpy as np
 
-        z = np.load(os.path.join(os.path.dirname(os.path.abspath(__file__)), "tests", "golden",
-                                 "traces_gptoss120b.npz"))
-        pairs = z[name]
+        if os.path.exists(name):  # any moearc-trace-v1 capture
+            from moearc_b200.residency import Trace
+
+            pairs = Trace.from_file(name).steps
+        else:
+            pairs = np.load(os.path.join(ROOT, "tests", "golden", "traces_gptoss120b.npz"))[name]
         self.steps = [[[int(e) for l2, e in s if l2 == l] for l in range(n)] for s in pairs]
+        k, E = dec.cfg.n_expert_used, dec.cfg.n_expert
+        for i, s in enumerate(self.steps):
+            for l, es in enumerate(s):
+                if len(es) != k or len(set(es)) != k or max(es) >= E:
+                    raise SystemExit(f"{name}: step {i} routes block {l} to {es}, not {k} distinct of {E} experts")
         self.dec, self.n, self.i, self.history = dec, n, 0, []
         self.w = np.zeros((dec.cfg.n_expert, dec.cfg.n_embd), np.float32)
         for l in range(n):
@@ -692,9 +700,10 @@ def main() -> None:
                     help="blocks whose experts stay in pinned host memory (configs[2] mode (b): 30)")
     ap.add_argument("--cache", type=int, default=0,
                     help="with --offload: device slots per offloaded block that keep fetched experts (0: none)")
-    ap.add_argument("--trace", default=None, choices=["prose", "code", "reasoning"],
+    ap.add_argument("--trace", default=None,
                     help="with --offload and --cache on the 120b shape: route the offloaded blocks as the "
-                         "captured gpt-oss-120b decode trace of that name did")
+                         "captured gpt-oss-120b decode trace prose, code or reasoning did, or as a "
+                         "moearc-trace-v1 file")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.config == "prefill":

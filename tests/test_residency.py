@@ -243,7 +243,7 @@ def test_the_bench_steers_each_offloaded_block_to_the_trace(captured):
 
     class FakeDecoder:
         class cfg:
-            n_expert, n_embd = 128, 64
+            n_expert, n_embd, n_expert_used = 128, 64, 4
 
         def __init__(self):
             self.t = {}
@@ -269,3 +269,25 @@ def test_the_bench_steers_each_offloaded_block_to_the_trace(captured):
     t = Trace([[(l, e) for l in range(3) for e in s[l]] for s in steps])
     assert route.replay_fetches(8, 5) == simulate(t, 8, "block").misses
     assert route.replay_fetches(8, 0) == 0
+
+
+def test_the_bench_reads_a_trace_file_and_refuses_one_that_does_not_fit(tmp_path):
+    import bench
+
+    class FakeDecoder:
+        class cfg:
+            n_expert, n_embd, n_expert_used = 8, 16, 2
+
+        def tensor(self, which, layer, dtype):
+            return np.zeros(self.cfg.n_embd, np.float32)
+
+        def set_tensor(self, which, layer, data):
+            pass
+
+    f = tmp_path / "t.ndjson"
+    f.write_text(HEADER + '\n{"e":[0,1,0,2,1,3,1,4]}\n{"e":[0,1,0,5,1,3,1,7]}\n')
+    route = bench.TraceRoute(FakeDecoder(), str(f), 2)
+    assert route.steps == [[[1, 2], [3, 4]], [[1, 5], [3, 7]]]
+    f.write_text(HEADER + '\n{"e":[0,1,0,9,1,3,1,4]}\n')
+    with pytest.raises(SystemExit, match="not 2 distinct of 8"):
+        bench.TraceRoute(FakeDecoder(), str(f), 2)
