@@ -11,6 +11,9 @@ crates/moearc-engine/src/residency.rs:163-219) and replays it through
   reaches (residency.rs:937-941, next-use index 970-1000);
 - ``static``: the first `resident_layers` blocks wholly resident, every other activation a
   fetch, charged no compulsory misses (residency.rs:433-456; `widest_static_split` 87-99);
+- ``lru2`` and ``slru``: the two online candidates the reference found to beat LRU on every
+  content type, LRU-2 and segmented LRU with `protected_pct` of the pool protected
+  (residency.rs:942-956, 746-812), over the same shared pool;
 - ``block``: the policy the device runs (`k_xplan` in csrc/moe.cu): each block owns its own
   `n_cache` slots; per step a block's distinct experts, ascending, keep their slots if resident,
   and each miss takes the slot with the oldest step stamp no expert of that step holds (an empty
@@ -258,6 +261,90 @@ def _pool(trace: Trace, capacity: int, belady: bool, per_expert_bytes: int) -> R
     return r
 
 
+def _lru2(trace: Trace, capacity: int, per_expert_bytes: int) -> Residency:
+    """LRU-2 over one shared pool (residency.rs:942-956): the victim is the unpinned resident
+    expert with the oldest reference before its last one (0 for an expert referenced once), the
+    last reference breaking ties; reference history survives eviction."""
+    r = Residency("lru2", capacity, len(trace.steps), per_layer_misses=[0] * trace.n_layers())
+    seen: set = set()
+    last: dict = {}
+    prev: dict = {}
+    resident: set = set()
+    heap: list = []                  # ((prev, last), expert) per reference; stale ones skipped
+    clock = 0
+    for s in trace.steps:
+        pinned = set(s)
+        for x in s:
+            clock += 1
+            prev[x] = last.get(x, 0)
+            last[x] = clock
+            first = x not in seen
+            seen.add(x)
+            if x in resident:
+                _count(r, x[0], True, False, per_expert_bytes)
+            else:
+                _count(r, x[0], False, first, per_expert_bytes)
+                if len(resident) >= capacity:
+                    held = []
+                    while True:
+                        key, v = heapq.heappop(heap)
+                        if v not in resident or key != (prev[v], last[v]):
+                            continue
+                        if v in pinned:
+                            held.append((key, v))
+                            continue
+                        break
+                    for ent in held:
+                        heapq.heappush(heap, ent)
+                    resident.discard(v)
+                resident.add(x)
+            heapq.heappush(heap, ((prev[x], last[x]), x))
+    return r
+
+
+def _slru(trace: Trace, capacity: int, protected_pct: int, per_expert_bytes: int) -> Residency:
+    """Segmented LRU over one shared pool (residency.rs:746-812): a miss enters probation, a hit
+    there promotes to protected, protected's overflow is demoted to probation's recent end, and
+    the victim is probation's least recent unpinned expert, else protected's."""
+    r = Residency(f"slru{protected_pct}", capacity, len(trace.steps), per_layer_misses=[0] * trace.n_layers())
+    protected_cap = capacity * min(protected_pct, 100) // 100
+    seen: set = set()
+    probation: OrderedDict = OrderedDict()   # least recently stamped first
+    protected: OrderedDict = OrderedDict()
+
+    def oldest(seg, pinned):
+        return next((y for y in seg if y not in pinned), None)
+
+    for s in trace.steps:
+        pinned = set(s)
+        for x in s:
+            first = x not in seen
+            seen.add(x)
+            if x in probation or x in protected:
+                _count(r, x[0], True, False, per_expert_bytes)
+                if x in probation:
+                    del probation[x]
+                    protected[x] = True
+                    while len(protected) > protected_cap:
+                        v = oldest(protected, pinned)
+                        if v is None:
+                            break
+                        del protected[v]
+                        probation[v] = True
+                else:
+                    protected.move_to_end(x)
+                continue
+            _count(r, x[0], False, first, per_expert_bytes)
+            if len(probation) + len(protected) >= capacity:
+                v = oldest(probation, pinned)
+                if v is not None:
+                    del probation[v]
+                else:
+                    del protected[oldest(protected, pinned)]
+            probation[x] = True
+    return r
+
+
 def _static(trace: Trace, capacity: int, resident_layers: int | None, per_expert_bytes: int) -> Residency:
     if resident_layers is None:
         resident_layers = trace.widest_static_split(capacity)
@@ -321,11 +408,11 @@ def _block(trace: Trace, n_cache, per_expert_bytes: int) -> Residency:
     return r
 
 
-POLICIES = ("lru", "optimal", "static", "block")
+POLICIES = ("lru", "optimal", "static", "block", "lru2", "slru")
 
 
 def simulate(trace: Trace, capacity, policy: str = "lru", per_expert_bytes: int = 0,
-             resident_layers: int | None = None) -> Residency:
+             resident_layers: int | None = None, protected_pct: int = 80) -> Residency:
     """Replay `trace` at `capacity` slots under `policy` (see the module docstring). For
     ``block`` the capacity is slots per block (an int, or one per block); for the others the
     total. ``static`` takes the widest split that fits unless `resident_layers` is given."""
@@ -339,11 +426,15 @@ def simulate(trace: Trace, capacity, policy: str = "lru", per_expert_bytes: int 
         raise SimError("capacity must be at least one expert")
     if policy == "static":
         return _static(trace, capacity, resident_layers, per_expert_bytes)
-    if policy not in ("lru", "optimal"):
+    if policy not in POLICIES:
         raise ValueError(f"unknown policy {policy!r}; one of {POLICIES}")
     if capacity < trace.peak_step_demand():  # activations, repeats included (residency.rs:423)
         raise SimError(f"capacity {capacity} cannot hold the {trace.peak_step_demand()} experts one "
                        "step activates: unservable at this capacity under any policy")
+    if policy == "lru2":
+        return _lru2(trace, capacity, per_expert_bytes)
+    if policy == "slru":
+        return _slru(trace, capacity, protected_pct, per_expert_bytes)
     return _pool(trace, capacity, policy == "optimal", per_expert_bytes)
 
 
@@ -363,7 +454,7 @@ def main(argv=None) -> None:
           f"{t.working_set()}, top 10% {100 * t.top_share(0.1):.1f}%, step reuse "
           f"{100 * t.step_reuse():.1f}%")
     for c in args.capacity:
-        row = [simulate(t, c, p, b) for p in ("static", "lru", "optimal")]
+        row = [simulate(t, c, p, b) for p in ("static", "lru", "lru2", "slru", "optimal")]
         print(f"  {c:6d} slots  " + "  ".join(f"{x.policy} {100 * x.hit_rate:5.1f}%" for x in row))
     for c in args.per_block:
         x = simulate(t, c, "block", b)

@@ -10,8 +10,9 @@ read them, never the reference tree.
   the step activations as uint8 [steps, 144, 2] (layer, expert) in file order, and the header
   line verbatim. Every step of these captures names exactly 36 blocks x 4 experts; the script
   refuses a file that does not, rather than pad it.
-- policy_sweep_gptoss120b.json: the trace shape table and the static / lru / belady columns of
-  the capacity sweeps in bench/policy-sweep.md, each entry with the line it came from.
+- policy_sweep_gptoss120b.json: the trace shape table and the static / lru / slru80 / lru-2 /
+  belady columns of the capacity sweeps in bench/policy-sweep.md, each entry with the line it
+  came from.
 """
 from __future__ import annotations
 
@@ -58,14 +59,20 @@ def sweep_tables(md_path: str) -> dict:
             current = m.group(1)
             sweeps[current] = []
             continue
-        if current and ln.startswith("|") and not ln.startswith("| slots") and not ln.startswith("|---"):
+        if current and ln.startswith("| slots"):
+            cols = [c.strip().strip("*") for c in ln.strip("|").split("|")]
+            continue
+        if current and ln.startswith("|") and not ln.startswith("|---"):
             cells = [c.strip().strip("*") for c in ln.strip("|").split("|")]
             try:
                 slots = int(cells[0])
             except ValueError:
                 continue
-            sweeps[current].append({"slots": slots, "static": float(cells[2]), "lru": float(cells[3]),
-                                    "belady": float(cells[-1]), "at": f"bench/policy-sweep.md:{i}"})
+            row = {"slots": slots}
+            for name in ("static", "lru", "slru80", "lru-2", "belady"):
+                row[name] = float(cells[cols.index(name)])
+            row["at"] = f"bench/policy-sweep.md:{i}"
+            sweeps[current].append(row)
         elif current and not ln.strip() and sweeps[current]:
             current = None
     return {"source": "chrisdesrochers/MoEArc", "shape": shape, "sweeps": sweeps}

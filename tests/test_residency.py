@@ -133,6 +133,19 @@ def test_a_static_split_may_not_exceed_the_shared_capacity():
         simulate(t, 3, "static", resident_layers=2)
 
 
+def test_lru2_keeps_an_expert_used_twice_over_one_used_once():
+    # capacity 2: a is used twice, then b once; c's miss evicts b (one reference) not a
+    t = trace_of([(0, 0)], [(0, 0)], [(0, 1)], [(0, 2)], [(0, 0)])
+    assert simulate(t, 2, "lru").hits == 1          # LRU evicts a, the least recent
+    assert simulate(t, 2, "lru2").hits == 2
+
+
+def test_slru_lets_a_once_used_expert_leave_before_a_reused_one():
+    # capacity 2, one protected slot: a is promoted by its second use, b and c pass through
+    t = trace_of([(0, 0)], [(0, 0)], [(0, 1)], [(0, 2)], [(0, 0)])
+    assert simulate(t, 2, "slru", protected_pct=50).hits == 2
+
+
 def test_transfer_time_converts_bytes_into_seconds():
     t = trace_of([(0, 0)], [(0, 1)])
     r = simulate(t, 1, "lru", 10 * MIB)
@@ -207,11 +220,13 @@ def test_captured_traces_have_the_shape_the_reference_published(captured, publis
 
 
 def test_replays_reproduce_the_published_hit_rates(captured, published):
-    """static / lru / belady at nine capacities on three traces, to the published 0.1 %."""
+    """static / lru / slru80 / lru-2 / belady at nine capacities on three traces, to the
+    published 0.1 %."""
     got, want = [], []
     for name, t in captured.items():
         for row in published["sweeps"][name]:
-            for ours, theirs in (("static", "static"), ("lru", "lru"), ("optimal", "belady")):
+            for ours, theirs in (("static", "static"), ("lru", "lru"), ("slru", "slru80"), ("lru2", "lru-2"),
+                                 ("optimal", "belady")):
                 got.append((name, row["slots"], ours, round(100 * simulate(t, row["slots"], ours).hit_rate, 1)))
                 want.append((name, row["slots"], ours, row[theirs]))
     assert got == want
