@@ -520,13 +520,12 @@ __global__ void __launch_bounds__(128)
     TRACE(5);
 }
 
+// The tensor-core kernel's shared-memory limit (64 KiB at head_dim 128, above the default 48),
+// set once on each device that launches it.
 template <int D, bool BF>
-void set_mma_smem() {
-    static bool done = false;
-    if (!done) {
-        set_smem(k_attn_mma<D, BF>, 4 * warp_smem_elems<D>() * 2);
-        done = true;
-    }
+cudaError_t set_mma_smem() {
+    static std::atomic<bool> done[MOEARC_MAX_DEVICES];
+    return once_per_device(done, [] { return set_smem(k_attn_mma<D, BF>, 4 * warp_smem_elems<D>() * 2); });
 }
 
 }  // namespace
@@ -584,20 +583,20 @@ int attn_launch(moearc_ctx *c, float *out, const float *q, const void *kp, const
         if (hd == 64) {
             constexpr size_t sm = 4 * warp_smem_elems<64>() * 2;
             if (kv_type == T_BF16) {
-                set_mma_smem<64, true>();
-                err = launch_pdl(k_attn_mma<64, true>, grid, dim3(128), sm, c->stream, ml, acc, out, q, k16, v16, table, sinks, (int)n_heads, (int)n_kv_heads, group, kv_begin, n_kv, pt, scale, kps, n_splits, dpos, window, ctr, (size_t)0);
+                err = set_mma_smem<64, true>();
+                if (err == cudaSuccess) err = launch_pdl(k_attn_mma<64, true>, grid, dim3(128), sm, c->stream, ml, acc, out, q, k16, v16, table, sinks, (int)n_heads, (int)n_kv_heads, group, kv_begin, n_kv, pt, scale, kps, n_splits, dpos, window, ctr, (size_t)0);
             } else {
-                set_mma_smem<64, false>();
-                err = launch_pdl(k_attn_mma<64, false>, grid, dim3(128), sm, c->stream, ml, acc, out, q, k16, v16, table, sinks, (int)n_heads, (int)n_kv_heads, group, kv_begin, n_kv, pt, scale, kps, n_splits, dpos, window, ctr, (size_t)0);
+                err = set_mma_smem<64, false>();
+                if (err == cudaSuccess) err = launch_pdl(k_attn_mma<64, false>, grid, dim3(128), sm, c->stream, ml, acc, out, q, k16, v16, table, sinks, (int)n_heads, (int)n_kv_heads, group, kv_begin, n_kv, pt, scale, kps, n_splits, dpos, window, ctr, (size_t)0);
             }
         } else {
             constexpr size_t sm = 4 * warp_smem_elems<128>() * 2;
             if (kv_type == T_BF16) {
-                set_mma_smem<128, true>();
-                err = launch_pdl(k_attn_mma<128, true>, grid, dim3(128), sm, c->stream, ml, acc, out, q, k16, v16, table, sinks, (int)n_heads, (int)n_kv_heads, group, kv_begin, n_kv, pt, scale, kps, n_splits, dpos, window, ctr, (size_t)0);
+                err = set_mma_smem<128, true>();
+                if (err == cudaSuccess) err = launch_pdl(k_attn_mma<128, true>, grid, dim3(128), sm, c->stream, ml, acc, out, q, k16, v16, table, sinks, (int)n_heads, (int)n_kv_heads, group, kv_begin, n_kv, pt, scale, kps, n_splits, dpos, window, ctr, (size_t)0);
             } else {
-                set_mma_smem<128, false>();
-                err = launch_pdl(k_attn_mma<128, false>, grid, dim3(128), sm, c->stream, ml, acc, out, q, k16, v16, table, sinks, (int)n_heads, (int)n_kv_heads, group, kv_begin, n_kv, pt, scale, kps, n_splits, dpos, window, ctr, (size_t)0);
+                err = set_mma_smem<128, false>();
+                if (err == cudaSuccess) err = launch_pdl(k_attn_mma<128, false>, grid, dim3(128), sm, c->stream, ml, acc, out, q, k16, v16, table, sinks, (int)n_heads, (int)n_kv_heads, group, kv_begin, n_kv, pt, scale, kps, n_splits, dpos, window, ctr, (size_t)0);
             }
         }
     } else {
@@ -614,12 +613,20 @@ int attn_launch(moearc_ctx *c, float *out, const float *q, const void *kp, const
         }
 #undef GEN
     }
-    if (err != cudaSuccess) return ERR;
+    if (err != cudaSuccess) {
+        cudaGetLastError();  // the failed launch's error, not left for an unrelated later check
+        return ERR;
+    }
     // with counters the last split of each head group merges in the kernel; without, a
     // second kernel merges
-    if (n_splits > 1 && !ctr)
+    if (n_splits > 1 && !ctr) {
         k_attn_combine<<<(unsigned)n_heads, 128, 0, c->stream>>>(out, ml, acc, sinks, (int)hd, n_splits, dpos,
                                                                 window, n_splits);
+        if (cudaPeekAtLastError() != cudaSuccess) {
+            cudaGetLastError();
+            return ERR;
+        }
+    }
     return OK;
 }
 
@@ -643,14 +650,14 @@ int attn_launch_batched(moearc_ctx *c, float *out, const float *q, const void *k
     cudaError_t err;
     if (hd == 64) {
         constexpr size_t sm = 4 * warp_smem_elems<64>() * 2;
-        set_mma_smem<64, true>();
-        err = launch_pdl(k_attn_mma<64, true>, grid, dim3(128), sm, c->stream, ml, acc, out, q, k16, v16, table, sinks,
+        err = set_mma_smem<64, true>();
+        if (err == cudaSuccess) err = launch_pdl(k_attn_mma<64, true>, grid, dim3(128), sm, c->stream, ml, acc, out, q, k16, v16, table, sinks,
                          (int)n_heads, (int)n_kv_heads, group, (size_t)0, n_ctx, pt, scale, (size_t)0, max_splits, dpos,
                          window, ctr, table_stride);
     } else {
         constexpr size_t sm = 4 * warp_smem_elems<128>() * 2;
-        set_mma_smem<128, true>();
-        err = launch_pdl(k_attn_mma<128, true>, grid, dim3(128), sm, c->stream, ml, acc, out, q, k16, v16, table, sinks,
+        err = set_mma_smem<128, true>();
+        if (err == cudaSuccess) err = launch_pdl(k_attn_mma<128, true>, grid, dim3(128), sm, c->stream, ml, acc, out, q, k16, v16, table, sinks,
                          (int)n_heads, (int)n_kv_heads, group, (size_t)0, n_ctx, pt, scale, (size_t)0, max_splits, dpos,
                          window, ctr, table_stride);
     }

@@ -31,6 +31,11 @@ constexpr size_t STATIC_PARTIAL_BYTES = MOEARC_X_ATTN_STATIC_SCRATCH_BYTES;
 // One copy per device (each device loads its own instance of this module). Every split writes
 // its partial (max, sum, accumulator row) before the merge kernel that follows it on the same
 // stream reads it, so nothing here has to start at zero.
+//
+// The address below is looked up once per device and kept for the life of the process. It is
+// valid for as long as the device's primary context lives: after cudaDeviceReset (or a release
+// and re-creation of the primary context) the module loads again at a new address, and a
+// process that resets a device must not call this entry point on it again.
 __device__ __align__(256) float g_attn_partials[STATIC_PARTIAL_BYTES / sizeof(float)];
 
 constexpr int MAX_DEVICES = 64;
@@ -83,11 +88,10 @@ int moearc_x_attn_decode_static(moearc_ctx *c, float *out, const float *q, const
         scratch = partials_on(c->device);
         if (!scratch) return ERR;
     }
-    const int rc = attn_launch(c, out, q, k_pages, v_pages, block_table, sinks, n_heads, n_kv_heads,
-                               head_dim, kv_begin, n_kv, page_tokens, scale, kv_type, scratch, sb,
-                               nullptr, 0, 0, nullptr);
-    if (rc != OK) return rc;
-    return cudaGetLastError() == cudaSuccess ? OK : ERR;
+    // attn_launch checks each of its own launches, so an unrelated error pending on this thread
+    // is neither reported here nor cleared
+    return attn_launch(c, out, q, k_pages, v_pages, block_table, sinks, n_heads, n_kv_heads, head_dim,
+                       kv_begin, n_kv, page_tokens, scale, kv_type, scratch, sb, nullptr, 0, 0, nullptr);
 }
 
 }  // extern "C"

@@ -2,6 +2,8 @@
 // formats' element rules, and the launch bookkeeping every entry point uses.
 #pragma once
 
+#include <atomic>
+
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
@@ -298,6 +300,25 @@ inline cudaError_t set_smem(void (*kernel)(KArgs...), int max_dynamic) {
     cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, max_dynamic);
     if (e != cudaSuccess) return e;
     return cudaFuncSetAttribute(kernel, cudaFuncAttributePreferredSharedMemoryCarveout, cudaSharedmemCarveoutMaxShared);
+}
+
+// Kernel attributes such as the shared-memory limit belong to the device they were set on: a
+// process driving two GPUs has to set them on each. once_per_device(done, f) runs f (which
+// returns a cudaError_t) with the current device the first time that device asks, and again
+// after a failure. Two threads asking at once may both run f; setting the same attribute to
+// the same value twice is harmless.
+constexpr int MOEARC_MAX_DEVICES = 64;
+
+template <typename F>
+inline cudaError_t once_per_device(std::atomic<bool> (&done)[MOEARC_MAX_DEVICES], F &&f) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    if (dev < 0 || dev >= MOEARC_MAX_DEVICES) return f();
+    if (done[dev].load(std::memory_order_acquire)) return cudaSuccess;
+    e = f();
+    if (e == cudaSuccess) done[dev].store(true, std::memory_order_release);
+    return e;
 }
 
 // A cooperative launch (every CTA resident at once, so CTAs may wait on one another), with

@@ -835,11 +835,8 @@ bool tc_make_map_bf16(CUtensorMap *map, const void *base, long rows, int cols) {
 
 int tc_dense_gemm(moearc_ctx *c, const CUtensorMap &w, int M, int K, const CUtensorMap &x, const int *seg_off,
                   const int *seg_toff, float *out, int *status) {
-    static bool ready = false;
-    if (!ready) {
-        if (set_smem(k_pf_gemm<1>, pf_cfg<1>::SMEM) != cudaSuccess) return ERR;
-        ready = true;
-    }
+    static std::atomic<bool> ready[MOEARC_MAX_DEVICES];
+    if (once_per_device(ready, [] { return set_smem(k_pf_gemm<1>, pf_cfg<1>::SMEM); }) != cudaSuccess) return ERR;
     if (K % PF_BK) return ERR_ARG;
     pf_gemm_args g{};
     g.Mrows = M;

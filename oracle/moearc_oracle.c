@@ -13,6 +13,58 @@
 #include <stdlib.h>
 #include <string.h>
 
+#include <pthread.h>
+#include <unistd.h>
+
+/* ---- row-parallel loops ------------------------------------------------------------------
+ * Large matvecs and attention spread their rows (heads) over host threads. Rows are
+ * independent and each keeps its own sequential sum, so the split changes no result; it only
+ * makes full-size parity checks finish in seconds. Calls below 2^20 multiply-adds stay on the
+ * calling thread. MOEARC_ORACLE_THREADS caps the count. */
+typedef void (*or_rows_fn)(void *arg, size_t r0, size_t r1, int tid);
+
+struct or_chunk {
+    or_rows_fn fn;
+    void *arg;
+    size_t r0, r1;
+    int tid;
+};
+
+static void *or_chunk_run(void *p) {
+    struct or_chunk *c = (struct or_chunk *)p;
+    c->fn(c->arg, c->r0, c->r1, c->tid);
+    return NULL;
+}
+
+static int or_threads(size_t work) {
+    if (work < ((size_t)1 << 20)) return 1;
+    long n = sysconf(_SC_NPROCESSORS_ONLN);
+    const char *e = getenv("MOEARC_ORACLE_THREADS");
+    if (e && atoi(e) > 0) n = atoi(e);
+    return n < 1 ? 1 : (n > 64 ? 64 : (int)n);
+}
+
+/* fn over [0, n) in nt contiguous chunks (chunk i on thread i; thread 0 is the caller). */
+static void or_parallel(size_t n, int nt, or_rows_fn fn, void *arg) {
+    if (nt > (int)n) nt = n ? (int)n : 1;
+    if (nt <= 1) {
+        fn(arg, 0, n, 0);
+        return;
+    }
+    struct or_chunk ch[64];
+    pthread_t th[64];
+    int started[64] = {0};
+    for (int i = 0; i < nt; ++i) {
+        ch[i] = (struct or_chunk){fn, arg, n * (size_t)i / (size_t)nt, n * (size_t)(i + 1) / (size_t)nt, i};
+        if (i > 0) started[i] = pthread_create(&th[i], NULL, or_chunk_run, &ch[i]) == 0;
+    }
+    fn(arg, ch[0].r0, ch[0].r1, 0);
+    for (int i = 1; i < nt; ++i) {
+        if (started[i]) pthread_join(th[i], NULL);
+        else fn(arg, ch[i].r0, ch[i].r1, 0); /* no thread: run it here (buffer 0 is free now) */
+    }
+}
+
 /* ====================================================================================== */
 /* scalar formats                                                                          */
 /* ====================================================================================== */
@@ -258,31 +310,60 @@ int or_dequant(unsigned t, const uint8_t *src, size_t nblocks, float *dst) {
 /* matvecs                                                                                 */
 /* ====================================================================================== */
 
+struct mvq_arg {
+    unsigned t;
+    int bb;
+    size_t nb, n_cols;
+    const uint8_t *w;
+    const float *x;
+    float *out, *rows;
+};
+
+static void mvq_rows(void *p, size_t r0, size_t r1, int tid) {
+    const struct mvq_arg *a = (const struct mvq_arg *)p;
+    float *row = a->rows + (size_t)tid * a->n_cols;
+    for (size_t r = r0; r < r1; ++r) {
+        or_dequant(a->t, a->w + r * a->nb * (size_t)a->bb, a->nb, row);
+        double acc = 0.0;
+        for (size_t c = 0; c < a->n_cols; ++c) acc += (double)row[c] * (double)a->x[c];
+        a->out[r] = (float)acc;
+    }
+}
+
 int or_matvec_q(unsigned t, const uint8_t *w, const float *x, size_t n_rows, size_t n_cols,
                 float *out) {
     const int bb = or_block_bytes(t);
     const int be = or_block_elems(t);
     if (!bb) return -2;
     if (n_cols % (size_t)be) return -2;
-    const size_t nb = n_cols / (size_t)be;
-    float *row = (float *)malloc(n_cols * sizeof(float));
-    if (!row) return -1;
-    for (size_t r = 0; r < n_rows; ++r) {
-        or_dequant(t, w + r * nb * (size_t)bb, nb, row);
-        double acc = 0.0;
-        for (size_t c = 0; c < n_cols; ++c) acc += (double)row[c] * (double)x[c];
-        out[r] = (float)acc;
-    }
-    free(row);
+    const int nt = or_threads(n_rows * n_cols);
+    float *rows = (float *)malloc((size_t)nt * n_cols * sizeof(float));
+    if (!rows) return -1;
+    struct mvq_arg a = {t, bb, n_cols / (size_t)be, n_cols, w, x, out, rows};
+    or_parallel(n_rows, nt, mvq_rows, &a);
+    free(rows);
     return 0;
 }
 
-void or_matvec_f32(const float *w, const float *x, size_t n_rows, size_t n_cols, float *out) {
-    for (size_t r = 0; r < n_rows; ++r) {
+struct mvf_arg {
+    const float *w, *x;
+    size_t n_cols;
+    float *out;
+};
+
+static void mvf_rows(void *p, size_t r0, size_t r1, int tid) {
+    const struct mvf_arg *a = (const struct mvf_arg *)p;
+    (void)tid;
+    for (size_t r = r0; r < r1; ++r) {
         double acc = 0.0;
-        for (size_t c = 0; c < n_cols; ++c) acc += (double)w[r * n_cols + c] * (double)x[c];
-        out[r] = (float)acc;
+        for (size_t c = 0; c < a->n_cols; ++c) acc += (double)a->w[r * a->n_cols + c] * (double)a->x[c];
+        a->out[r] = (float)acc;
     }
+}
+
+void or_matvec_f32(const float *w, const float *x, size_t n_rows, size_t n_cols, float *out) {
+    struct mvf_arg a = {w, x, n_cols, out};
+    or_parallel(n_rows, or_threads(n_rows * n_cols), mvf_rows, &a);
 }
 
 void or_matvec_f32_gpu_order(const float *w, const float *x, size_t n_rows, size_t n_cols,
@@ -568,6 +649,56 @@ int or_kv_append(void *k_pages, void *v_pages, const float *k, const float *v, u
     return 0;
 }
 
+struct attn_arg {
+    const float *q;
+    const void *k_pages, *v_pages;
+    const uint32_t *block_table;
+    const float *sinks;
+    size_t group, n_kv_heads, head_dim, kv_begin, span, page_tokens;
+    float scale;
+    unsigned t;
+    float *out;
+    double *scs;
+};
+
+/* Heads h0 .. h1-1 (reference.rs:821-873, the sink seeding of kernels.cpp:1856-1880). */
+static void attn_heads(void *p, size_t h0, size_t h1, int tid) {
+    const struct attn_arg *a = (const struct attn_arg *)p;
+    const size_t span = a->span, head_dim = a->head_dim, page_tokens = a->page_tokens;
+    double *sc = a->scs + span * (size_t)tid;
+    for (size_t h = h0; h < h1; ++h) {
+        const size_t kvh = h / a->group;
+        const float *qh = a->q + h * head_dim;
+        double mx = a->sinks ? (double)a->sinks[h] : -INFINITY;
+        for (size_t i = 0; i < span; ++i) {
+            const size_t j = a->kv_begin + i;
+            const uint32_t page = a->block_table[j / page_tokens];
+            const uint32_t slot = (uint32_t)(j % page_tokens);
+            const size_t base = or_kv_index(page, slot, kvh, 0, a->n_kv_heads, head_dim, page_tokens);
+            double dot = 0.0;
+            for (size_t d = 0; d < head_dim; ++d) dot += (double)qh[d] * (double)kv_get(a->k_pages, base + d, a->t);
+            sc[i] = dot * (double)a->scale;
+            if (sc[i] > mx) mx = sc[i];
+        }
+        double denom = a->sinks ? exp((double)a->sinks[h] - mx) : 0.0;
+        for (size_t i = 0; i < span; ++i) {
+            sc[i] = exp(sc[i] - mx);
+            denom += sc[i];
+        }
+        for (size_t d = 0; d < head_dim; ++d) {
+            double acc = 0.0;
+            for (size_t i = 0; i < span; ++i) {
+                const size_t j = a->kv_begin + i;
+                const uint32_t page = a->block_table[j / page_tokens];
+                const uint32_t slot = (uint32_t)(j % page_tokens);
+                const size_t base = or_kv_index(page, slot, kvh, 0, a->n_kv_heads, head_dim, page_tokens);
+                acc += sc[i] * (double)kv_get(a->v_pages, base + d, a->t);
+            }
+            a->out[h * head_dim + d] = (float)(acc / denom);
+        }
+    }
+}
+
 int or_attn_decode(const float *q, const void *k_pages, const void *v_pages,
                    const uint32_t *block_table, const float *sinks, size_t n_heads,
                    size_t n_kv_heads, size_t head_dim, size_t kv_begin, size_t n_kv,
@@ -576,41 +707,14 @@ int or_attn_decode(const float *q, const void *k_pages, const void *v_pages,
         return -2;
     if (n_heads % n_kv_heads) return -2;
     if (kv_begin >= n_kv) return -2;
-    const size_t group = n_heads / n_kv_heads;
     const size_t span = n_kv - kv_begin;
-    double *sc = (double *)malloc(sizeof(double) * span);
-    for (size_t h = 0; h < n_heads; ++h) {
-        const size_t kvh = h / group;
-        const float *qh = q + h * head_dim;
-        double mx = sinks ? (double)sinks[h] : -INFINITY;
-        for (size_t i = 0; i < span; ++i) {
-            const size_t j = kv_begin + i;
-            const uint32_t page = block_table[j / page_tokens];
-            const uint32_t slot = (uint32_t)(j % page_tokens);
-            const size_t base = or_kv_index(page, slot, kvh, 0, n_kv_heads, head_dim, page_tokens);
-            double dot = 0.0;
-            for (size_t d = 0; d < head_dim; ++d) dot += (double)qh[d] * (double)kv_get(k_pages, base + d, t);
-            sc[i] = dot * (double)scale;
-            if (sc[i] > mx) mx = sc[i];
-        }
-        double denom = sinks ? exp((double)sinks[h] - mx) : 0.0;
-        for (size_t i = 0; i < span; ++i) {
-            sc[i] = exp(sc[i] - mx);
-            denom += sc[i];
-        }
-        for (size_t d = 0; d < head_dim; ++d) {
-            double acc = 0.0;
-            for (size_t i = 0; i < span; ++i) {
-                const size_t j = kv_begin + i;
-                const uint32_t page = block_table[j / page_tokens];
-                const uint32_t slot = (uint32_t)(j % page_tokens);
-                const size_t base = or_kv_index(page, slot, kvh, 0, n_kv_heads, head_dim, page_tokens);
-                acc += sc[i] * (double)kv_get(v_pages, base + d, t);
-            }
-            out[h * head_dim + d] = (float)(acc / denom);
-        }
-    }
-    free(sc);
+    const int nt = or_threads(n_heads * span * head_dim);
+    double *scs = (double *)malloc(sizeof(double) * span * (size_t)nt);
+    if (!scs) return -1;
+    struct attn_arg a = {q, k_pages, v_pages, block_table, sinks, n_heads / n_kv_heads, n_kv_heads,
+                         head_dim, kv_begin, span, page_tokens, scale, t, out, scs};
+    or_parallel(n_heads, nt, attn_heads, &a);
+    free(scs);
     return 0;
 }
 

@@ -296,6 +296,61 @@ def test_swiglu_oai_matches_the_oracle(ctx):
     report("swiglu_oai", rel_err(ctx.download(out, np.float32, n), want, 1e-6), 16 * U)
 
 
+def test_add_bias_id_adds_each_matrix_its_experts_bias_row(ctx):
+    """kernels.cpp:1654-1670 as moe.rs:2310-2331 uses it: out[m * n_rows + r] += bias[idx[m]
+    * n_rows + r], gathered by router id, repeats and a 37-row (non-multiple) stride included;
+    a single f32 add per element, so bit-exact against the oracle."""
+    n_expert, n_rows = 32, 37
+    idx = [5, 0, 31, 5, 17, 2]
+    rng = np.random.default_rng(21)
+    bias = rng.uniform(-1, 1, (n_expert, n_rows)).astype(np.float32)
+    base = rng.uniform(-1, 1, (len(idx), n_rows)).astype(np.float32)
+    out = ctx.upload_new(base)
+    ctx.add_bias_id(out, ctx.upload_new(bias), idx, n_rows)
+    got = ctx.download(out, np.float32, base.size)
+    want = base.ravel().copy()
+    idx_a = np.asarray(idx, np.uint32)
+    O.lib().or_add_bias_id(O.ptr(want), O.ptr(bias), O.ptr(idx_a), len(idx), n_rows)
+    assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
+    assert np.array_equal(want.reshape(len(idx), n_rows), base + bias[idx])
+
+
+def test_silu_and_mul_match_the_oracle(ctx):
+    """reference.rs:363-366 (silu) and 700-703 (mul) over a length that is not a multiple of a
+    warp; mul is one f32 product per element (bit-exact), silu goes through expf (a few ulp)."""
+    n = 4099
+    rng = np.random.default_rng(22)
+    x = (rng.standard_normal(n) * 8).astype(np.float32)
+    y = rng.uniform(-2, 2, n).astype(np.float32)
+    dx, dy = ctx.upload_new(x), ctx.upload_new(y)
+    out = ctx.alloc_n(np.float32, n)
+    ctx.silu(out, dx, n)
+    want = np.zeros(n, np.float32)
+    O.lib().or_silu(O.ptr(x), n, O.ptr(want))
+    report("silu", rel_err(ctx.download(out, np.float32, n), want, 1e-6), 8 * U)
+    ctx.mul(out, dx, dy, n)
+    O.lib().or_mul(O.ptr(x), O.ptr(y), n, O.ptr(want))
+    assert np.array_equal(ctx.download(out, np.float32, n).view(np.uint32), want.view(np.uint32))
+
+
+def test_quantize_f16_rounds_like_the_twin(ctx):
+    """reference.rs:647-691 (round to nearest even, NaN kept, overflow to infinity, subnormals):
+    every value, including the edges, gives the twin's f16 bits."""
+    edge = np.array([0.0, -0.0, 65504.0, 65520.0, -65520.0, 1e9, 2.0 ** -24, 2.0 ** -25,
+                     3 * 2.0 ** -26, 2.0 ** -14, 2.0 ** -14 - 2.0 ** -25, 1.0 + 2.0 ** -11,
+                     1.0 + 3 * 2.0 ** -11, np.inf, -np.inf, np.nan], np.float32)
+    rng = np.random.default_rng(23)
+    x = np.concatenate([edge, (rng.standard_normal(5000) * 10.0 ** rng.uniform(-8, 5, 5000)).astype(np.float32)])
+    n = x.size
+    dst = ctx.alloc_n(np.uint16, n)
+    ctx.quantize_f16(dst, ctx.upload_new(x), n)
+    got = ctx.download(dst, np.uint16, n)
+    want = np.array([O.lib().or_f32_to_f16(float(v)) for v in x], np.uint16)
+    nan = np.isnan(x)
+    assert np.array_equal(got[~nan], want[~nan])
+    assert np.all((got[nan] & 0x7C00) == 0x7C00) and np.all((got[nan] & 0x03FF) != 0)
+
+
 def test_rmsnorm_and_softmax_match_the_oracle(ctx):
     rng = np.random.default_rng(6)
     rows, cols = 3, 2880

@@ -117,3 +117,22 @@ def test_partials_above_the_fixed_size_are_refused(ctx):
     assert call(ctx, "moearc_x_attn_decode_static", c, out, 0) == -2
     ctx.sync()
     assert np.array_equal(ctx.download(out, np.float32, H * D), sentinel)
+
+
+def test_calls_leave_the_free_device_memory_unchanged(ctx):
+    """What the entry point is for: no call takes device memory. After one warm-up call (which
+    loads the kernels' code and looks the array's address up), twenty more calls over spans
+    that split differently leave the device's free memory exactly where it was; the scratch
+    path would have grown its buffer (a cudaMalloc) on its first split call."""
+    torch = pytest.importorskip("torch")
+    c = make_case(ctx, 64, 8, 64, 6000, 32, BF16, seed=17, sinks=True)
+    out = ctx.alloc_n(np.float32, 64 * 64)
+    assert call(ctx, "moearc_x_attn_decode_static", c, out, 0) == 0
+    ctx.sync()
+    free0, _ = torch.cuda.mem_get_info(0)
+    for i in range(20):
+        assert call(ctx, "moearc_x_attn_decode_static", c, out, (i * 997) % 5000) == 0
+    ctx.sync()
+    free1, _ = torch.cuda.mem_get_info(0)
+    print(f"free device memory before / after 20 calls: {free0} / {free1} bytes")
+    assert free1 == free0
