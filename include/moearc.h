@@ -368,6 +368,9 @@ int moearc_x_batch_decoder_set_pos(moearc_x_batch_decoder *d, unsigned int pos, 
 int moearc_x_batch_decoder_step(moearc_x_batch_decoder *d);
 /* Reads and clears the status words: 0, or nonzero when a bounded wait gave up. */
 int moearc_x_batch_decoder_status(moearc_x_batch_decoder *d);
+/* Device pointer to block `layer`'s expert choice of the last step, n_batch x k u32 in router
+ * order (NULL for a layer out of range). */
+void *moearc_x_batch_decoder_routing(moearc_x_batch_decoder *d, unsigned int layer);
 
 /* ---- GGUF model files (no counterpart in the reference's ABI) -------------------------------
  * A read-only view of a GGUF v2/v3 file, replacing the reference's Rust reader

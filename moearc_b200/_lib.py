@@ -92,6 +92,7 @@ SIGNATURES: dict[str, tuple] = {
     "moearc_x_batch_decoder_set_pos": (I, [P, U, I, C.c_ulonglong]),
     "moearc_x_batch_decoder_step": (I, [P]),
     "moearc_x_batch_decoder_status": (I, [P]),
+    "moearc_x_batch_decoder_routing": (P, [P, U]),
     "moearc_x_prefill_set_order": (I, [P, P]),
     "moearc_x_prefill_load4": (I, [P, P, P]),
     "moearc_x_prefill_load4_list": (I, [P, P, P, P, U]),

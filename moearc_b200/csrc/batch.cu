@@ -427,6 +427,11 @@ int moearc_x_batch_decoder_step(moearc_x_batch_decoder *d) {
 
 // Reads and clears the status words of the step's kernels (GEMM waits and the MoE blocks'):
 // 0, or a nonzero bit pattern when a bounded wait gave up.
+void *moearc_x_batch_decoder_routing(moearc_x_batch_decoder *d, unsigned int layer) {
+    if (!d || layer >= d->L.size()) return nullptr;
+    return moearc_x_prefill_buffer(d->L[layer].moe, 0);
+}
+
 int moearc_x_batch_decoder_status(moearc_x_batch_decoder *d) {
     if (!d) return ERR;
     int s = 0;

@@ -206,12 +206,25 @@ __global__ void k_synth(uint8_t *dst, size_t n, unsigned kind, uint64_t seed, fl
             const double u2 = (double)(r0 & 0xFFFFFFFFu) * 0x1.0p-32;
             const double z = sqrt(-2.0 * log(u1)) * cospi(2.0 * u2);
             const uint16_t d = __half_as_ushort(__float2half_rn((float)fabs(z * (double)sigma)));
-            p[0] = (uint8_t)d;
-            p[1] = (uint8_t)(d >> 8);
+            // the block's nine 16-bit words: the delta, then the nibble bytes of r1 and r2 in
+            // little-endian order; a block is 18 bytes, so on an even destination every word
+            // is 2-byte aligned and goes out as one store
+            uint16_t w[9];
+            w[0] = d;
 #pragma unroll
-            for (int j = 0; j < 8; ++j) {
-                p[2 + j] = (uint8_t)(r1 >> (8 * j));
-                p[10 + j] = (uint8_t)(r2 >> (8 * j));
+            for (int j = 0; j < 4; ++j) {
+                w[1 + j] = (uint16_t)(r1 >> (16 * j));
+                w[5 + j] = (uint16_t)(r2 >> (16 * j));
+            }
+            if ((reinterpret_cast<uintptr_t>(p) & 1) == 0) {
+#pragma unroll
+                for (int j = 0; j < 9; ++j) reinterpret_cast<uint16_t *>(p)[j] = w[j];
+            } else {
+#pragma unroll
+                for (int j = 0; j < 9; ++j) {
+                    p[2 * j] = (uint8_t)w[j];
+                    p[2 * j + 1] = (uint8_t)(w[j] >> 8);
+                }
             }
         }
     }

@@ -73,13 +73,15 @@ class DecoderConfig:
     @staticmethod
     def gpt_oss_20b(**kw) -> "DecoderConfig":
         """24 layers, hidden 2880, 64 q / 8 kv heads of 64, 32 experts top-4, I 2880."""
-        c = DecoderConfig(24, 2880, 64, 8, 64, 32, 4, 2880, **kw)
+        c = DecoderConfig(**{**dict(n_layer=24, n_embd=2880, n_head=64, n_head_kv=8, head_dim=64, n_expert=32,
+                                    n_expert_used=4, n_ff=2880), **kw})
         return c.yarn(32.0, 4096)
 
     @staticmethod
     def gpt_oss_120b(**kw) -> "DecoderConfig":
         """as configs[1] with 36 layers and 128 experts."""
-        c = DecoderConfig(36, 2880, 64, 8, 64, 128, 4, 2880, **kw)
+        c = DecoderConfig(**{**dict(n_layer=36, n_embd=2880, n_head=64, n_head_kv=8, head_dim=64, n_expert=128,
+                                    n_expert_used=4, n_ff=2880), **kw})
         return c.yarn(32.0, 4096)
 
     @staticmethod
@@ -93,7 +95,8 @@ class DecoderConfig:
         kw.setdefault("has_sinks", 0)
         kw.setdefault("rope_base", 1000000.0)
         kw.setdefault("rms_eps", 1e-6)
-        return DecoderConfig(48, 2048, 32, 4, 128, 128, 8, 768, **kw)
+        return DecoderConfig(**{**dict(n_layer=48, n_embd=2048, n_head=32, n_head_kv=4, head_dim=128, n_expert=128,
+                                       n_expert_used=8, n_ff=768), **kw})
 
 
 class Decoder:
@@ -160,6 +163,18 @@ class Decoder:
             self.ctx._finish(self.ctx.lib.moearc_copy_d2h(self.ctx.raw, out.ctypes.data, p, n.value), "tensor")
         return out
 
+    def read(self, which: int, layer: int, offset: int, n: int, dtype) -> np.ndarray:
+        """n elements of one block's tensor (the `tensor` numbering) from element `offset`."""
+        size = C.c_ulong()
+        p = self.ctx.lib.moearc_x_decoder_tensor(self.h, which, layer, C.byref(size))
+        item = np.dtype(dtype).itemsize
+        if not p or (offset + n) * item > size.value:
+            raise BadArgument(f"elements [{offset}, {offset + n}) of tensor {which} of block {layer}")
+        out = np.empty(n, dtype)
+        self.ctx._finish(self.ctx.lib.moearc_copy_d2h(self.ctx.raw, out.ctypes.data, p + offset * item, n * item),
+                         "tensor read")
+        return out
+
     def set_tensor(self, which: int, layer: int, data: np.ndarray) -> None:
         """Overwrite one block's tensor (the `tensor` numbering) with `data`, which must have its
         exact size; ordered before the next step on the context stream."""
@@ -206,6 +221,15 @@ class BatchDecoder:
     def output(self) -> np.ndarray:
         out = np.empty((self.n_batch, self.cfg.n_embd), np.float32)
         self.ctx._finish(self.ctx.lib.moearc_copy_d2h(self.ctx.raw, out.ctypes.data, self.out_ptr, out.nbytes), "output")
+        return out
+
+    def routing(self, layer: int) -> np.ndarray:
+        """Block `layer`'s expert choice of the last step, [n_batch][k] in router order."""
+        p = self.ctx.lib.moearc_x_batch_decoder_routing(self.h, layer)
+        if not p:
+            raise BadArgument(f"no block {layer}")
+        out = np.empty((self.n_batch, self.cfg.n_expert_used), np.uint32)
+        self.ctx._finish(self.ctx.lib.moearc_copy_d2h(self.ctx.raw, out.ctypes.data, p, out.nbytes), "routing")
         return out
 
     def status(self) -> int:

@@ -110,6 +110,7 @@ def _declare(l: C.CDLL) -> None:
         "hx_ffn": (C.c_int, [P, U, SZ, SZ, U, P, P, P, P, P, C.c_int, F, F, P]),
         "hx_matvec": (C.c_int, [P, U, P, P, SZ, SZ, P]),
         "cd_step": (C.c_int, [C.POINTER(CdCfg), P, P, P, SZ, P, P, P]),
+        "cd_step_margins": (C.c_int, [C.POINTER(CdCfg), P, P, P, SZ, P, P, P]),
         "cd_layers": (C.c_int, [C.POINTER(CdCfg), P, SZ, SZ, P, SZ, P, P]),
     }
     for name, (res, args) in sig.items():

@@ -24,8 +24,32 @@ static int mv(hx_pool *pool, unsigned t, const void *w, const float *x, size_t r
     return or_matvec_q(t, (const uint8_t *)w, x, rows, cols, out);
 }
 
-int cd_layers(const cd_cfg *c, const cd_layer *L, size_t l0, size_t l1, float *h, size_t pos,
-              hx_pool *pool, uint32_t *idx_out) {
+/* The gap between the k-th and the (k+1)-th largest router logit (0 when E <= k): how far the
+ * routing is from a tie, so a test can tell a near-tie flip from a routing error. */
+static float topk_margin(const float *logits, size_t E, unsigned k) {
+    if (E <= k) return 0.f;
+    float kth = -INFINITY, next = -INFINITY;
+    /* k + 1 rounds of "largest value not above the previous, counted with multiplicity" */
+    unsigned seen = 0;
+    float prev = INFINITY;
+    while (seen <= k) {
+        float m = -INFINITY;
+        for (size_t e = 0; e < E; ++e)
+            if (logits[e] < prev && logits[e] > m) m = logits[e];
+        unsigned cnt = 0;
+        for (size_t e = 0; e < E; ++e) cnt += logits[e] == m;
+        if (cnt == 0) break;
+        for (unsigned i = 0; i < cnt && seen <= k; ++i, ++seen) {
+            if (seen == k - 1) kth = m;
+            if (seen == k) next = m;
+        }
+        prev = m;
+    }
+    return kth - next;
+}
+
+static int layers_impl(const cd_cfg *c, const cd_layer *L, size_t l0, size_t l1, float *h, size_t pos,
+                       hx_pool *pool, uint32_t *idx_out, float *margin_out) {
     const size_t H = c->n_embd, Dq = c->n_head * c->head_dim, Dkv = c->n_head_kv * c->head_dim;
     const size_t E = c->n_expert;
     float *x = (float *)malloc(sizeof(float) * H);
@@ -88,6 +112,10 @@ int cd_layers(const cd_cfg *c, const cd_layer *L, size_t l0, size_t l1, float *h
                 break;
             if (idx_out) memcpy(idx_out + l * c->k, idx, sizeof(uint32_t) * c->k);
         } else {
+            if (margin_out) {
+                or_matvec_f32(b->router, x, E, H, logits);
+                margin_out[l] = topk_margin(logits, E, c->k);
+            }
             if ((rc = or_moe_ffn_token(&mc, x, b->router, NULL, b->gate, b->up, b->down, NULL,
                                        NULL, NULL, ffn, idx_out ? idx_out + l * c->k : NULL,
                                        NULL)))
@@ -108,11 +136,26 @@ int cd_layers(const cd_cfg *c, const cd_layer *L, size_t l0, size_t l1, float *h
     return rc;
 }
 
+int cd_layers(const cd_cfg *c, const cd_layer *L, size_t l0, size_t l1, float *h, size_t pos,
+              hx_pool *pool, uint32_t *idx_out) {
+    return layers_impl(c, L, l0, l1, h, pos, pool, idx_out, NULL);
+}
+
+int cd_step_margins(const cd_cfg *c, const cd_layer *layers, const float *output_norm,
+                    const float *h_in, size_t pos, float *out, uint32_t *idx_out, float *margin_out) {
+    float *h = (float *)malloc(sizeof(float) * c->n_embd);
+    memcpy(h, h_in, sizeof(float) * c->n_embd);
+    int rc = layers_impl(c, layers, 0, c->n_layer, h, pos, NULL, idx_out, margin_out);
+    if (!rc) or_rmsnorm(h, output_norm, 1, c->n_embd, c->eps, out);
+    free(h);
+    return rc;
+}
+
 int cd_step(const cd_cfg *c, const cd_layer *layers, const float *output_norm, const float *h_in,
             size_t pos, hx_pool *pool, float *out, uint32_t *idx_out) {
     float *h = (float *)malloc(sizeof(float) * c->n_embd);
     memcpy(h, h_in, sizeof(float) * c->n_embd);
-    int rc = cd_layers(c, layers, 0, c->n_layer, h, pos, pool, idx_out);
+    int rc = layers_impl(c, layers, 0, c->n_layer, h, pos, pool, idx_out, NULL);
     if (!rc) or_rmsnorm(h, output_norm, 1, c->n_embd, c->eps, out);
     free(h);
     return rc;

@@ -49,6 +49,11 @@ typedef struct {
 int cd_step(const cd_cfg *c, const cd_layer *layers, const float *output_norm, const float *h_in,
             size_t pos, hx_pool *pool, float *out, uint32_t *idx_out);
 
+/* cd_step without the pool, also recording per layer in margin_out (n_layer floats) the gap
+ * between the k-th and the (k+1)-th largest router logit: how close that routing is to a tie. */
+int cd_step_margins(const cd_cfg *c, const cd_layer *layers, const float *output_norm,
+                    const float *h_in, size_t pos, float *out, uint32_t *idx_out, float *margin_out);
+
 /* The same sequence over layers [l0, l1) only, from h (updated in place), with no final
  * norm: the bounded sample the bench times. */
 int cd_layers(const cd_cfg *c, const cd_layer *layers, size_t l0, size_t l1, float *h,

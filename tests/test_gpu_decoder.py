@@ -30,10 +30,11 @@ def ctx():
     c.close()
 
 
-@pytest.mark.parametrize("graph", [False, True])
-def test_small_gpt_oss_shaped_decoder_matches_the_oracle(ctx, graph):
+@pytest.mark.parametrize("graph,etype", [(False, O.MXFP4), (True, O.MXFP4), (True, O.Q4_0)])
+def test_small_gpt_oss_shaped_decoder_matches_the_oracle(ctx, graph, etype):
     cfg = DecoderConfig(n_layer=3, n_embd=256, n_head=8, n_head_kv=2, head_dim=64, n_expert=8,
-                        n_expert_used=2, n_ff=128, n_swa=40, swa_pattern=2, n_ctx=256, seed=0xDEC0DE)
+                        n_expert_used=2, n_ff=128, n_swa=40, swa_pattern=2, n_ctx=256, seed=0xDEC0DE,
+                        expert_type=etype)
     cfg.yarn(32.0, 4096)
     dec = Decoder(ctx, cfg)
     dec.use_graph(graph)
@@ -48,7 +49,7 @@ def test_small_gpt_oss_shaped_decoder_matches_the_oracle(ctx, graph):
         assert O.lib().cd_step(C.byref(c), arr, O.ptr(out_norm), O.ptr(x), pos, None, O.ptr(want), None) == 0
         err = float(np.max(np.abs(got.astype(np.float64) - want) / np.maximum(np.abs(want), 1.0)))
         worst = max(worst, err)
-    print(f"decoder graph={graph}: 70 tokens, max rel err {worst:.3e}")
+    print(f"decoder graph={graph} etype={etype}: 70 tokens, max rel err {worst:.3e}")
     assert dec.pos == 70
     assert dec.status() == 0  # no bounded wait in any kernel gave up
     # bf16 K/V rounding amplifies last-bit differences of k and v into 2^-9 relative steps, so the
@@ -74,23 +75,47 @@ def test_gpt_oss_120b_shaped_blocks_match_the_oracle(big, graph):
     """The configuration the benchmark times, token by token against the oracle's decode step
     for 144 tokens: past the 128-key window of block 0 (crates/moearc-engine/tests/
     gptoss_forward.rs:393-418 runs past the window for the same reason) and across page
-    boundaries of block 1, with and without the captured graph."""
+    boundaries of block 1, with and without the captured graph.
+
+    Each step's K/V entries are compared too (bf16: equal, or one bf16 step apart where the f32
+    values of the two sides straddle a rounding edge), and the oracle then continues from the
+    device's entries. Left to run free, the two caches would differ by those single bf16 steps
+    at a few entries a token, and attention to them would amplify the difference over the
+    tokens (about 3e-3 after 20 tokens at this shape). Fed the same cache, a step differs only
+    through its own token's K/V entries, which each side rounds to bf16 itself: in the first
+    tokens that key carries much of the attention, and a one-step difference in one of its
+    values moves the output by up to ~3e-4; the bound is the composed decoder's 1e-3."""
     dec, (c, arr, keep, out_norm) = big
     dec.use_graph(graph)
     dec.set_pos(0)
     for t in keep:  # a fresh sequence on both sides
         t["k"][:] = 0
         t["v"][:] = 0
-    worst = 0.0
+    Dkv = c.n_head_kv * c.head_dim
+    worst, kv_steps, kv_entries = 0.0, 0, 0
     for pos in range(144):
         x = O.synth_normal_f32(0x4000 + pos, c.n_embd, 1.0)
         dec.set_input(x)
         dec.step()
         got = dec.output()
         worst = max(worst, rel_to_oracle(got, oracle_step(c, arr, out_norm, x, pos)))
+        for l, t in enumerate(keep):
+            off = (int(t["table"][pos // 32]) * 32 + pos % 32) * Dkv
+            for which, name in ((4, "k"), (5, "v")):
+                dev = dec.read(which, l, off, Dkv, np.uint16)
+                mine = t[name][off:off + Dkv]
+                gd, gm = O.bf16_to_f32(dev), O.bf16_to_f32(mine)
+                # half a bf16 step on each side, plus the f32 difference of the two projections
+                bound = 2 ** -8 * (np.abs(gd) + np.abs(gm)) + 1e-5 * max(1.0, float(np.abs(gm).max()))
+                assert np.all(np.abs(gd - gm) <= bound), (pos, l, name)
+                kv_steps += int(np.sum(dev != mine))
+                kv_entries += Dkv
+                mine[:] = dev
     assert dec.status() == 0
-    print(f"gpt-oss-120b shape, 2 blocks, graph={graph}: 144 tokens, max rel err {worst:.3e} (tolerance 1e-3)")
+    print(f"gpt-oss-120b shape, 2 blocks, graph={graph}: 144 tokens, max rel err {worst:.3e} (tolerance 1e-3); "
+          f"K/V entries one bf16 step apart: {kv_steps} of {kv_entries}")
     assert worst <= 1e-3
+    assert kv_steps <= kv_entries // 100
 
 
 @pytest.mark.parametrize("depth", [8192, 32768])
@@ -112,8 +137,8 @@ def test_gpt_oss_120b_shaped_blocks_at_depth_match_the_oracle(big, depth):
         dec.step()
         worst = max(worst, rel_to_oracle(dec.output(), oracle_step(c, arr, out_norm, x, depth + i)))
     assert dec.pos == depth + 2 and dec.status() == 0
-    print(f"gpt-oss-120b shape at depth {depth}: 2 steps, max rel err {worst:.3e} (tolerance 1e-3)")
-    assert worst <= 1e-3
+    print(f"gpt-oss-120b shape at depth {depth}: 2 steps, max rel err {worst:.3e} (tolerance 1e-4)")
+    assert worst <= 1e-4
 
 
 def test_the_kv_cache_holds_the_roped_keys(ctx):
@@ -289,23 +314,43 @@ def test_batch_decoder_matches_single_stream_decoders(ctx, etype):
     for d in singles:
         d.set_pos(0)
     models = [host_model(d) for d in singles]  # the same weights; each its own KV pools
+    L, k = kw["n_layer"], kw["n_expert_used"]
     worst = worst_or = 0.0
+    diverged = {}  # stream -> (token, block, oracle margin) of a near-tie routing flip
     for pos in range(40):  # past a page boundary
         x = np.stack([O.synth_normal_f32(0x3000 + 97 * b + pos, kw["n_embd"], 1.0) for b in range(B)])
         bd.set_input(x)
         bd.step()
         got = bd.output()
+        routes = [bd.routing(l) for l in range(L)]
         for b, d in enumerate(singles):
             d.set_input(x[b])
             d.step()
+            if b in diverged:
+                continue
             want = d.output().astype(np.float64)
-            worst = max(worst, float(np.max(np.abs(got[b] - want)) / np.max(np.abs(want))))
             c, arr, keep, out_norm = models[b]
-            ow = oracle_step(c, arr, out_norm, x[b], pos).astype(np.float64)
+            ow = np.zeros(c.n_embd, np.float32)
+            idx = np.zeros(L * k, np.uint32)
+            margin = np.zeros(L, np.float32)
+            assert O.lib().cd_step_margins(C.byref(c), arr, O.ptr(out_norm), O.ptr(x[b]), pos, O.ptr(ow),
+                                           O.ptr(idx), O.ptr(margin)) == 0
+            flip = [l for l in range(L) if not np.array_equal(np.sort(routes[l][b]), np.sort(idx[l * k:(l + 1) * k]))]
+            if flip:
+                # bf16 activations move the router's logits by ~1e-3 of their scale; only a
+                # routing that close to a tie may differ from the oracle's, and the stream is
+                # compared no further (its hidden state now follows other experts)
+                l = flip[0]
+                assert margin[l] < 1e-2, (pos, b, l, routes[l][b], idx[l * k:(l + 1) * k], margin[l])
+                diverged[b] = (pos, l, float(margin[l]))
+                continue
+            worst = max(worst, float(np.max(np.abs(got[b] - want)) / np.max(np.abs(want))))
             worst_or = max(worst_or, float(np.max(np.abs(got[b] - ow)) / np.max(np.abs(ow))))
     assert bd.status() == 0
     print(f"batch decoder etype={etype}: 3 streams x 40 tokens, max |a-b| / max|b| = {worst_or:.3e} "
-          f"against the oracle, {worst:.3e} against single-stream decoders (tolerance 1e-2)")
+          f"against the oracle, {worst:.3e} against single-stream decoders (tolerance 1e-2); "
+          f"near-tie routing flips (stream: token, block, margin): {diverged}")
+    assert len(diverged) <= 1
     assert worst_or <= 1e-2 and worst <= 1e-2
     for d in singles:
         d.close()

@@ -102,6 +102,19 @@ def test_synthetic_mxfp4_is_identical_on_host_and_device(ctx):
     assert np.array_equal(ctx.download(dst, np.uint8, n * 17), want)
 
 
+@pytest.mark.parametrize("offset", [0, 1])
+def test_synthetic_q4_0_is_identical_on_host_and_device(ctx, offset):
+    """The decoder's Q4_0 expert banks are generated on the device; the oracle rebuilds them on
+    the host. The f16 deltas (|N(0, 0.01)| rounded to nearest even) and the nibble bytes agree
+    byte for byte, at an even and at an odd destination address."""
+    n = 4096
+    want = O.synth_q4_0(0x5EED, n, 0.01)
+    dst = ctx.alloc(n * 18 + 2)
+    ctx.synth(dst.view(offset, n * 18), n, 3, 0x5EED, 0.01)
+    got = ctx.download(dst.view(offset, n * 18), np.uint8, n * 18)
+    assert np.array_equal(got, want), f"{int(np.sum(got != want))} bytes differ"
+
+
 def test_unsupported_types_are_refused(ctx):
     b = ctx.alloc(1024)
     with pytest.raises(BadArgument):
