@@ -341,12 +341,34 @@ unsigned long long moearc_x_decoder_fetched(moearc_x_decoder *d);
 int moearc_x_decoder_profile(moearc_x_decoder *d, float *ms, int *counts, int n);
 /* Device pointer (and size) of one block's tensor: 0 attn_norm, 1 ffn_norm, 2 sinks,
  * 3 router, 4 K pool, 5 V pool, 6 page table, 7 packed Q/K/V, 8 packed O, 9 packed gate-up,
- * 10 packed down, 11 output norm. For an offloaded block, 9 and 10 are device-visible
- * pointers of the pinned host banks. */
+ * 10 packed down, 11 output norm; with the persistent step kernel, 12 the block's expert ids
+ * of the last step (k u32, router order) and 13 their gating weights (k f32). For an offloaded
+ * block, 9 and 10 are device-visible pointers of the pinned host banks. */
 void *moearc_x_decoder_tensor(moearc_x_decoder *d, int which, unsigned int layer, unsigned long *bytes);
 /* The seed tensor `kind` of block `layer` was generated from, given the model seed. */
 unsigned long long moearc_x_decoder_seed(moearc_x_decoder *d, int kind, unsigned int layer,
                                          unsigned long long base);
+/* ---- the decode step as one persistent kernel (no reference counterpart) ----------------
+ * Resident-expert decoders with head_dim 64 (the gpt-oss family) run the whole step as one
+ * cooperative launch: a CTA per SM, the phases of every block separated by grid barriers, each
+ * warp streaming its share of the weights through a ring of bulk copies that runs ahead across
+ * phase boundaries. Other shapes run the chain of per-block kernels. */
+/* 1 when steps run the persistent kernel, 0 when they run the kernel chain. */
+int moearc_x_decoder_uses_step_kernel(moearc_x_decoder *d);
+/* Choose the persistent kernel (on, when the shape has one; -2 otherwise) or the chain. */
+int moearc_x_decoder_use_step_kernel(moearc_x_decoder *d, int on);
+/* The persistent kernel's grid-barrier wait limit (ns; 0 = the default 0.2 s) and a count of
+ * arrivals each barrier waits for beyond the CTAs' own (0 in use; 1 makes the first barrier
+ * run out, for testing the bounded wait: the step then sets the status word and returns, its
+ * output invalid). Synchronises the stream; the next step re-captures its graph. */
+int moearc_x_decoder_set_wait(moearc_x_decoder *d, unsigned long long limit_ns, unsigned int phantom);
+/* Phase timestamps of the persistent kernel: with a device buffer of trace_words u64 set,
+ * every following step writes %globaltimer (ns) at the start and end of each phase of each
+ * block in each CTA: word ((layer * 6 + phase) * 2 + end) * n_cta + cta, phases 0 Q/K/V,
+ * 1 attention, 2 O projection, 3 router, 4 expert gate-up, 5 expert down. NULL turns it off.
+ * Synchronises the stream; the next step re-captures its graph. */
+unsigned long moearc_x_decoder_trace_words(moearc_x_decoder *d);
+int moearc_x_decoder_set_trace(moearc_x_decoder *d, void *device_buffer);
 
 /* ---- batched decoder (batch.cu; no counterpart in the reference, whose engine decodes one
  * sequence) ---------------------------------------------------------------------------------

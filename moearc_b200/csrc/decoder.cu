@@ -22,10 +22,12 @@
 #include <algorithm>
 #include <cmath>
 #include <climits>
+#include <cstdlib>
 #include <vector>
 
 #include "common.cuh"
 #include "dense.cuh"
+#include "step.cuh"
 
 namespace moearc {
 int moe_forward_impl(moearc_x_moe *m, const float *x, unsigned n_tokens, const float *norm_w, float eps,
@@ -109,6 +111,17 @@ struct moearc_x_decoder {
     cudaGraph_t graph = nullptr;
     cudaGraphExec_t exec = nullptr;
     bool use_graph = true;
+    // the whole step as one persistent kernel (step.cuh) when the shape allows it; the chain
+    // of per-block kernels otherwise (offloaded experts, head_dim 128, ...) or on request
+    step_plan *step = nullptr;
+    bool use_step = true;
+
+    void drop_graph() {
+        if (exec) cudaGraphExecDestroy(exec);
+        if (graph) cudaGraphDestroy(graph);
+        exec = nullptr;
+        graph = nullptr;
+    }
 
     void *alloc(size_t bytes) {
         void *p = nullptr;
@@ -146,6 +159,7 @@ struct step_marks {
 int enqueue_step(moearc_x_decoder *d, step_marks *pm = nullptr) {
     moearc_ctx *c = d->c;
     const auto &cfg = d->cfg;
+    if (d->step && d->use_step && !pm) return step_run(d->step, d->in, d->out, d->output_norm, d->dpos);
     if (cudaMemcpyAsync(d->h, d->in, sizeof(float) * cfg.n_embd, cudaMemcpyDeviceToDevice, c->stream) != cudaSuccess)
         return ERR;
     if (pm) pm->mark(c->stream, -1);
@@ -401,14 +415,30 @@ moearc_x_decoder *moearc_x_decoder_create(moearc_ctx *c, const moearc_x_decoder_
     cudaFree(staging);
     if (pack_tmp) cudaFree(pack_tmp);
     if (!ok) return fail();
+    if (!g.n_offload) {
+        std::vector<step_layer> sl(g.n_layer);
+        for (unsigned l = 0; l < g.n_layer; ++l) {
+            const auto &b = d->L[l];
+            sl[l] = step_layer{b.attn_norm, b.ffn_norm, b.sinks, b.router,
+                               static_cast<const uint8_t *>(b.wqkv), static_cast<const uint8_t *>(b.wo),
+                               static_cast<const uint8_t *>(b.gateup), static_cast<const uint8_t *>(b.down),
+                               b.k_pages, b.v_pages, b.table, b.window};
+        }
+        const step_shape ss{(int)g.n_layer, H, (int)g.n_head, (int)g.n_head_kv, (int)g.head_dim, (int)g.n_expert,
+                            (int)g.n_expert_used, (int)g.n_ff, (int)g.gating, (int)g.act, (int)g.expert_type,
+                            g.alpha, g.limit, g.rms_eps, d->rope_freq, d->rope_mscale};
+        d->step = step_create(c, ss, sl.data());
+        const char *e = std::getenv("MOEARC_DECODER_CHAIN");
+        d->use_step = !(e && e[0] == '1');
+    }
     return d;
 }
 
 void moearc_x_decoder_destroy(moearc_x_decoder *d) {
     if (!d) return;
     cudaStreamSynchronize(d->c->stream);
-    if (d->exec) cudaGraphExecDestroy(d->exec);
-    if (d->graph) cudaGraphDestroy(d->graph);
+    d->drop_graph();
+    step_destroy(d->step);
     if (d->moe) moearc_x_moe_destroy(d->moe);
     if (d->qkv) dense_destroy(d->qkv);
     if (d->wo) dense_destroy(d->wo);
@@ -456,8 +486,39 @@ unsigned long long moearc_x_decoder_fetched(moearc_x_decoder *d) {
 int moearc_x_decoder_status(moearc_x_decoder *d) {
     if (!d) return ERR;
     const int sm = moearc_x_moe_status(d->moe), sq = dense_status(d->qkv), so = dense_status(d->wo);
-    if (sm < 0 || sq < 0 || so < 0) return ERR;
-    return sm | sq | so;
+    const int st = d->step ? step_status(d->step) : 0;
+    if (sm < 0 || sq < 0 || so < 0 || st < 0) return ERR;
+    return sm | sq | so | st;
+}
+
+int moearc_x_decoder_uses_step_kernel(moearc_x_decoder *d) { return d && d->step && d->use_step ? 1 : 0; }
+
+int moearc_x_decoder_use_step_kernel(moearc_x_decoder *d, int on) {
+    if (!d) return ERR;
+    if (on && !d->step) return ERR_ARG;
+    if (d->use_step != (on != 0)) d->drop_graph();
+    d->use_step = on != 0;
+    return OK;
+}
+
+int moearc_x_decoder_set_wait(moearc_x_decoder *d, unsigned long long limit_ns, unsigned int phantom) {
+    if (!d || !d->step) return ERR;
+    if (cudaStreamSynchronize(d->c->stream) != cudaSuccess) return ERR;
+    step_set_wait(d->step, limit_ns, phantom);
+    d->drop_graph();
+    return OK;
+}
+
+unsigned long moearc_x_decoder_trace_words(moearc_x_decoder *d) {
+    return d && d->step ? (unsigned long)step_trace_words(d->step) : 0;
+}
+
+int moearc_x_decoder_set_trace(moearc_x_decoder *d, void *device_buffer) {
+    if (!d || !d->step) return ERR;
+    if (cudaStreamSynchronize(d->c->stream) != cudaSuccess) return ERR;
+    step_set_trace(d->step, static_cast<unsigned long long *>(device_buffer));
+    d->drop_graph();
+    return OK;
 }
 
 int moearc_x_decoder_use_graph(moearc_x_decoder *d, int on) {
@@ -552,6 +613,10 @@ void *moearc_x_decoder_tensor(moearc_x_decoder *d, int which, unsigned layer, un
         case 8: p = b.wo; n = H * d->Dq * 2; break;
         case 9: p = b.gateup; n = 2 * bank; break;
         case 10: p = b.down; n = bank; break;
+        case 12: p = d->step ? static_cast<unsigned *>(step_buffer(d->step, 0)) + (size_t)layer * g.n_expert_used : nullptr;
+                 n = p ? g.n_expert_used * 4 : 0; break;
+        case 13: p = d->step ? static_cast<float *>(step_buffer(d->step, 1)) + (size_t)layer * g.n_expert_used : nullptr;
+                 n = p ? g.n_expert_used * 4 : 0; break;
         default: return nullptr;
         }
     }

@@ -127,6 +127,29 @@ class Decoder:
     def use_graph(self, on: bool) -> None:
         self.ctx._finish(self.ctx.lib.moearc_x_decoder_use_graph(self.h, 1 if on else 0), "use_graph")
 
+    def uses_step_kernel(self) -> bool:
+        """True when steps run as one persistent kernel, False for the per-block kernel chain."""
+        return self.ctx.lib.moearc_x_decoder_uses_step_kernel(self.h) == 1
+
+    def use_step_kernel(self, on: bool) -> None:
+        self.ctx._finish(self.ctx.lib.moearc_x_decoder_use_step_kernel(self.h, 1 if on else 0), "use_step_kernel")
+
+    def set_wait(self, limit_ns: int = 0, phantom: int = 0) -> None:
+        """The persistent kernel's barrier wait limit (0: default) and phantom arrivals (testing)."""
+        self.ctx._finish(self.ctx.lib.moearc_x_decoder_set_wait(self.h, limit_ns, phantom), "set_wait")
+
+    def trace_words(self) -> int:
+        return self.ctx.lib.moearc_x_decoder_trace_words(self.h)
+
+    def set_trace(self, buf) -> None:
+        """Phase timestamps into a device buffer of trace_words() u64 (None: off)."""
+        self.ctx._finish(self.ctx.lib.moearc_x_decoder_set_trace(self.h, buf.ptr if buf is not None else None),
+                         "set_trace")
+
+    def routing(self, layer: int) -> tuple[np.ndarray, np.ndarray]:
+        """Block `layer`'s expert ids and gating weights of the last step (persistent kernel)."""
+        return self.tensor(12, layer, np.uint32), self.tensor(13, layer, np.float32)
+
     def fetched(self) -> int:
         """Experts the offloaded blocks' residency caches fetched over PCIe since create."""
         return self.ctx.lib.moearc_x_decoder_fetched(self.h)
