@@ -363,9 +363,10 @@ int moearc_x_decoder_use_step_kernel(moearc_x_decoder *d, int on);
  * output invalid). Synchronises the stream; the next step re-captures its graph. */
 int moearc_x_decoder_set_wait(moearc_x_decoder *d, unsigned long long limit_ns, unsigned int phantom);
 /* Phase timestamps of the persistent kernel: with a device buffer of trace_words u64 set,
- * every following step writes %globaltimer (ns) at the start and end of each phase of each
- * block in each CTA: word ((layer * 6 + phase) * 2 + end) * n_cta + cta, phases 0 Q/K/V,
- * 1 attention, 2 O projection, 3 router, 4 expert gate-up, 5 expert down. NULL turns it off.
+ * every following step writes %globaltimer (ns) at four points of each phase of each block in
+ * each CTA: word ((layer * 6 + phase) * 4 + point) * n_cta + cta; phases 0 Q/K/V, 1 attention,
+ * 2 O projection, 3 router, 4 expert gate-up, 5 expert down; points 0 start (the grid barrier
+ * opened), 1 inputs ready, 2 the CTA's warp 0 done with its share, 3 end. NULL turns it off.
  * Synchronises the stream; the next step re-captures its graph. */
 unsigned long moearc_x_decoder_trace_words(moearc_x_decoder *d);
 int moearc_x_decoder_set_trace(moearc_x_decoder *d, void *device_buffer);

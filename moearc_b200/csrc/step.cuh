@@ -69,7 +69,7 @@ int step_status(step_plan *p);
 // The next step's barrier limit (ns) and a count of phantom arrivals its first barrier waits
 // for in addition to the CTAs' (0 in normal use: a test makes the barrier run out with 1).
 void step_set_wait(step_plan *p, unsigned long long limit_ns, unsigned phantom);
-// Per-phase timestamps of the following steps: (layer, phase 0-5, start/end, CTA) in ns of
+// Per-phase timestamps of the following steps: (layer, phase 0-5, point 0-3, CTA) in ns of
 // %globaltimer into a device buffer of step_trace_words() u64 (null: off).
 size_t step_trace_words(step_plan *p);
 void step_set_trace(step_plan *p, unsigned long long *buf);
