@@ -349,10 +349,13 @@ void *moearc_x_decoder_tensor(moearc_x_decoder *d, int which, unsigned int layer
 unsigned long long moearc_x_decoder_seed(moearc_x_decoder *d, int kind, unsigned int layer,
                                          unsigned long long base);
 /* ---- the decode step as one persistent kernel (no reference counterpart) ----------------
- * Resident-expert decoders with head_dim 64 (the gpt-oss family) run the whole step as one
+ * Resident-expert decoders with head_dim 64 (the gpt-oss family) can run the whole step as one
  * cooperative launch: a CTA per SM, the phases of every block separated by grid barriers, each
  * warp streaming its share of the weights through a ring of bulk copies that runs ahead across
- * phase boundaries. Other shapes run the chain of per-block kernels. */
+ * phase boundaries. The chain of per-block kernels is the default (MOEARC_STEP_KERNEL=1 at
+ * create, or use_step_kernel, selects the persistent kernel). */
+/* 1 when the shape has the persistent kernel. */
+int moearc_x_decoder_has_step_kernel(moearc_x_decoder *d);
 /* 1 when steps run the persistent kernel, 0 when they run the kernel chain. */
 int moearc_x_decoder_uses_step_kernel(moearc_x_decoder *d);
 /* Choose the persistent kernel (on, when the shape has one; -2 otherwise) or the chain. */

@@ -86,6 +86,7 @@ SIGNATURES: dict[str, tuple] = {
     "moearc_x_prefill_combine": (I, [P, P, U, P, P]),
     "moearc_x_prefill_load_list": (I, [P, P, P, P, U]),
     "moearc_x_decoder_uses_step_kernel": (I, [P]),
+    "moearc_x_decoder_has_step_kernel": (I, [P]),
     "moearc_x_decoder_use_step_kernel": (I, [P, I]),
     "moearc_x_decoder_set_wait": (I, [P, C.c_ulonglong, U]),
     "moearc_x_decoder_trace_words": (C.c_ulong, [P]),

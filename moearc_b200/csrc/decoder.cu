@@ -114,7 +114,7 @@ struct moearc_x_decoder {
     // the whole step as one persistent kernel (step.cuh) when the shape allows it; the chain
     // of per-block kernels otherwise (offloaded experts, head_dim 128, ...) or on request
     step_plan *step = nullptr;
-    bool use_step = true;
+    bool use_step = false;
 
     void drop_graph() {
         if (exec) cudaGraphExecDestroy(exec);
@@ -428,8 +428,10 @@ moearc_x_decoder *moearc_x_decoder_create(moearc_ctx *c, const moearc_x_decoder_
                             (int)g.n_expert_used, (int)g.n_ff, (int)g.gating, (int)g.act, (int)g.expert_type,
                             g.alpha, g.limit, g.rms_eps, d->rope_freq, d->rope_mscale};
         d->step = step_create(c, ss, sl.data());
-        const char *e = std::getenv("MOEARC_DECODER_CHAIN");
-        d->use_step = !(e && e[0] == '1');
+        // the kernel chain is the default (measured faster at the gpt-oss-120b shape); the
+        // persistent kernel on request
+        const char *e = std::getenv("MOEARC_STEP_KERNEL");
+        d->use_step = e && e[0] == '1';
     }
     return d;
 }
@@ -492,6 +494,8 @@ int moearc_x_decoder_status(moearc_x_decoder *d) {
 }
 
 int moearc_x_decoder_uses_step_kernel(moearc_x_decoder *d) { return d && d->step && d->use_step ? 1 : 0; }
+
+int moearc_x_decoder_has_step_kernel(moearc_x_decoder *d) { return d && d->step ? 1 : 0; }
 
 int moearc_x_decoder_use_step_kernel(moearc_x_decoder *d, int on) {
     if (!d) return ERR;

@@ -1115,8 +1115,8 @@ __global__ void __launch_bounds__(XW * 32, 1) k_xexpert(xexp_args a) {
             fence_proxy_async();
             mbar_expect_tx(bar, (unsigned)(n * a.elem_bytes + ntok * n * 256));
             const int bank_ix = a.by_slot ? tb.grp_slot[c.g] : tb.grp_expert[c.g];
-            bulk_g2s(st, a.bank + (size_t)bank_ix * a.bank_stride + (size_t)((c.tr * nkt + kt) * a.elem_bytes),
-                     (unsigned)(n * a.elem_bytes), bar);
+            bulk_g2s_hint(st, a.bank + (size_t)bank_ix * a.bank_stride + (size_t)((c.tr * nkt + kt) * a.elem_bytes),
+                          (unsigned)(n * a.elem_bytes), bar, policy_evict_first());
         }
         if (acts)
             for (int t = 0; t < ntok; ++t) {
@@ -1146,6 +1146,7 @@ __global__ void __launch_bounds__(XW * 32, 1) k_xexpert(xexp_args a) {
             step(ic);
             ++n_issued;
         }
+
     if (MODE == 1) {
         // the weights are static and stream now; the activation fragments are the gate-up
         // kernel's output and follow the wait

@@ -77,29 +77,6 @@ __device__ __forceinline__ unsigned ld_rlx(const unsigned *p) {
 // thread's later bulk copies read them.
 __device__ __forceinline__ void fence_proxy_all() { asm volatile("fence.proxy.async;\n" ::: "memory"); }
 
-// L2 policies: weights streamed once are marked to leave L2 first; the next block's dense
-// weights, asked into L2 ahead of their use, to stay until then.
-__device__ __forceinline__ uint64_t policy_evict_first() {
-    uint64_t p;
-    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
-    return p;
-}
-__device__ __forceinline__ uint64_t policy_evict_last() {
-    uint64_t p;
-    asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(p));
-    return p;
-}
-__device__ __forceinline__ void bulk_g2s_hint(void *dst, const void *src, unsigned bytes, uint64_t *bar, uint64_t pol) {
-    asm volatile(
-        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;\n" ::"r"(
-            smem_addr(dst)),
-        "l"(src), "r"(bytes), "r"(smem_addr(bar)), "l"(pol)
-        : "memory");
-}
-__device__ __forceinline__ void prefetch_l2_hint(const void *src, unsigned bytes, uint64_t pol) {
-    asm volatile("cp.async.bulk.prefetch.L2.global.L2::cache_hint [%0], %1, %2;\n" ::"l"(src), "r"(bytes), "l"(pol)
-                 : "memory");
-}
 __device__ __forceinline__ void bar_att() { asm volatile("bar.sync 1, %0;" ::"n"(AW * 32) : "memory"); }
 
 // The CTA (of G) whose share [T c / G, T (c + 1) / G) holds item t.

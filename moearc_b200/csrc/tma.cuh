@@ -51,6 +51,37 @@ __device__ __forceinline__ void bulk_prefetch_l2(const void *src, unsigned bytes
     asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;\n" ::"l"(src), "r"(bytes) : "memory");
 }
 
+// L2 policies: weights streamed once are marked to leave L2 first; bytes asked into L2 ahead of
+// their use, to stay until then.
+__device__ __forceinline__ uint64_t policy_evict_first() {
+    uint64_t p;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+    return p;
+}
+__device__ __forceinline__ uint64_t policy_evict_last() {
+    uint64_t p;
+    asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(p));
+    return p;
+}
+// bulk_g2s with an L2 cache policy for the bytes read.
+__device__ __forceinline__ void bulk_g2s_hint(void *dst, const void *src, unsigned bytes, uint64_t *bar, uint64_t pol) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;\n" ::"r"(
+            smem_addr(dst)),
+        "l"(src), "r"(bytes), "r"(smem_addr(bar)), "l"(pol)
+        : "memory");
+}
+// bulk_prefetch_l2 with an L2 cache policy.
+__device__ __forceinline__ void prefetch_l2_hint(const void *src, unsigned bytes, uint64_t pol) {
+    asm volatile("cp.async.bulk.prefetch.L2.global.L2::cache_hint [%0], %1, %2;\n" ::"l"(src), "r"(bytes), "l"(pol)
+                 : "memory");
+}
+// CTA c of G asks L2 for its share of [p, p + bytes) (16-byte aligned), in 32 KB requests.
+__device__ __forceinline__ void prefetch_share_l2(const uint8_t *p, size_t bytes, int c, int G, uint64_t pol) {
+    const size_t n16 = bytes / 16, a = n16 * c / G * 16, b = n16 * (c + 1) / G * 16;
+    for (size_t o = a; o < b; o += 32768) prefetch_l2_hint(p + o, (unsigned)(b - o < 32768 ? b - o : 32768), pol);
+}
+
 __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, unsigned parity) {
     unsigned ok;
     asm volatile(

@@ -127,6 +127,10 @@ class Decoder:
     def use_graph(self, on: bool) -> None:
         self.ctx._finish(self.ctx.lib.moearc_x_decoder_use_graph(self.h, 1 if on else 0), "use_graph")
 
+    def has_step_kernel(self) -> bool:
+        """True when this shape can run the step as one persistent kernel."""
+        return self.ctx.lib.moearc_x_decoder_has_step_kernel(self.h) == 1
+
     def uses_step_kernel(self) -> bool:
         """True when steps run as one persistent kernel, False for the per-block kernel chain."""
         return self.ctx.lib.moearc_x_decoder_uses_step_kernel(self.h) == 1

@@ -41,7 +41,7 @@ def test_small_gpt_oss_shaped_decoder_matches_the_oracle(ctx, graph, etype, step
                         expert_type=etype)
     cfg.yarn(32.0, 4096)
     dec = Decoder(ctx, cfg)
-    assert dec.uses_step_kernel()
+    assert dec.has_step_kernel() and not dec.uses_step_kernel()  # the chain by default
     dec.use_step_kernel(step_kernel)
     dec.use_graph(graph)
     c, arr, keep, out_norm = host_model(dec)
@@ -76,12 +76,13 @@ def big(ctx):
     dec.close()
 
 
-@pytest.mark.parametrize("graph", [False, True])
-def test_gpt_oss_120b_shaped_blocks_match_the_oracle(big, graph):
+@pytest.mark.parametrize("graph,step_kernel", [(False, False), (True, False), (True, True)])
+def test_gpt_oss_120b_shaped_blocks_match_the_oracle(big, graph, step_kernel):
     """The configuration the benchmark times, token by token against the oracle's decode step
     for 144 tokens: past the 128-key window of block 0 (crates/moearc-engine/tests/
     gptoss_forward.rs:393-418 runs past the window for the same reason) and across page
-    boundaries of block 1, with and without the captured graph.
+    boundaries of block 1, with and without the captured graph; the kernel chain and the
+    persistent step kernel.
 
     Each step's K/V entries are compared too (bf16: equal, or one bf16 step apart where the f32
     values of the two sides straddle a rounding edge), and the oracle then continues from the
@@ -92,13 +93,13 @@ def test_gpt_oss_120b_shaped_blocks_match_the_oracle(big, graph):
     tokens that key carries much of the attention, and a one-step difference in one of its
     values moves the output by up to ~3e-4; the bound is the composed decoder's 1e-3."""
     dec, (c, arr, keep, out_norm) = big
+    dec.use_step_kernel(step_kernel)
     dec.use_graph(graph)
     dec.set_pos(0)
     for t in keep:  # a fresh sequence on both sides
         t["k"][:] = 0
         t["v"][:] = 0
     Dkv = c.n_head_kv * c.head_dim
-    assert dec.uses_step_kernel()
     worst, kv_steps, kv_entries, route_flips = 0.0, 0, 0, 0
     for pos in range(144):
         x = O.synth_normal_f32(0x4000 + pos, c.n_embd, 1.0)
@@ -115,7 +116,7 @@ def test_gpt_oss_120b_shaped_blocks_match_the_oracle(big, graph):
         # token then takes other experts from that block on and is compared no further (its
         # later blocks' K/V still pass to the oracle below).
         flip = c.n_layer
-        for l in range(c.n_layer):
+        for l in range(c.n_layer if step_kernel else 0):  # the chain keeps no per-block routing
             ids, _ = dec.routing(l)
             if not np.array_equal(ids, idx[l * c.k:(l + 1) * c.k]):
                 assert margin[l] < 1e-4, (pos, l, ids, idx[l * c.k:(l + 1) * c.k], margin[l])
@@ -132,26 +133,28 @@ def test_gpt_oss_120b_shaped_blocks_match_the_oracle(big, graph):
                 if l <= flip:
                     gd, gm = O.bf16_to_f32(dev), O.bf16_to_f32(mine)
                     # half a bf16 step on each side, plus the f32 difference of the projections
-                    bound = 2 ** -8 * (np.abs(gd) + np.abs(gm)) + 1e-5 * max(1.0, float(np.abs(gm).max()))
+                    # (their inputs differ by the f32 rounding of every kernel before them)
+                    bound = 2 ** -8 * (np.abs(gd) + np.abs(gm)) + 1e-4 * max(1.0, float(np.abs(gm).max()))
                     bad = np.nonzero(np.abs(gd - gm) > bound)[0]
                     assert bad.size == 0, (pos, l, name, bad[:4], gd[bad[:4]], gm[bad[:4]])
                     kv_steps += int(np.sum(dev != mine))
                     kv_entries += Dkv
                 mine[:] = dev
     assert dec.status() == 0
-    print(f"gpt-oss-120b shape, 2 blocks, graph={graph}: 144 tokens, max rel err {worst:.3e} (tolerance 1e-3); "
+    print(f"gpt-oss-120b shape, 2 blocks, graph={graph} step_kernel={step_kernel}: 144 tokens, max rel err {worst:.3e} (tolerance 1e-3); "
           f"K/V entries one bf16 step apart: {kv_steps} of {kv_entries}; near-tie routing differences {route_flips}")
     assert worst <= 1e-3 and route_flips <= 2
     assert kv_steps <= kv_entries // 100
 
 
-@pytest.mark.parametrize("depth", [8192, 32768])
-def test_gpt_oss_120b_shaped_blocks_at_depth_match_the_oracle(big, depth):
+@pytest.mark.parametrize("depth,step_kernel", [(8192, False), (32768, False), (8192, True), (32768, True)])
+def test_gpt_oss_120b_shaped_blocks_at_depth_match_the_oracle(big, depth, step_kernel):
     """A decode step after `depth` cached tokens (configs[2] at 8K and 32K): the attention split
     count is decided on the device from the span (at least 256 keys a split; 33 splits at
     32768), the windowed block reads the last 128 keys of its ring, the full block all of them.
     The device's synthetic cache is copied into the oracle's pools before two steps."""
     dec, (c, arr, keep, out_norm) = big
+    dec.use_step_kernel(step_kernel)
     dec.use_graph(True)
     dec.fill_kv(depth, seed=0xD00 + depth)
     for l, t in enumerate(keep):
@@ -164,7 +167,7 @@ def test_gpt_oss_120b_shaped_blocks_at_depth_match_the_oracle(big, depth):
         dec.step()
         worst = max(worst, rel_to_oracle(dec.output(), oracle_step(c, arr, out_norm, x, depth + i)))
     assert dec.pos == depth + 2 and dec.status() == 0
-    print(f"gpt-oss-120b shape at depth {depth}: 2 steps, max rel err {worst:.3e} (tolerance 1e-4)")
+    print(f"gpt-oss-120b shape at depth {depth} step_kernel={step_kernel}: 2 steps, max rel err {worst:.3e} (tolerance 1e-4)")
     assert worst <= 1e-4
 
 
@@ -213,9 +216,8 @@ def test_expert_offload_matches_the_resident_decoder(ctx, etype, n_expert, k):
               n_expert_used=k, n_ff=128, expert_type=etype, n_swa=40, swa_pattern=2, n_ctx=128,
               seed=0x0FF1)
     res = Decoder(ctx, DecoderConfig(**kw))
-    res.use_step_kernel(False)  # the same kernels as the offloaded decoder, so the same sums
     off = Decoder(ctx, DecoderConfig(**kw, n_offload=2))
-    assert not off.uses_step_kernel()
+    assert not off.has_step_kernel()
     for pos in range(12):
         x = O.synth_normal_f32(0x2000 + pos, kw["n_embd"], 1.0)
         for d in (res, off):
@@ -241,7 +243,6 @@ def test_expert_residency_cache_gives_the_resident_bits_and_fetches_less(ctx, et
               n_expert_used=k, n_ff=128, expert_type=etype, n_swa=40, swa_pattern=2, n_ctx=128,
               seed=0x0FF1)
     res = Decoder(ctx, DecoderConfig(**kw))
-    res.use_step_kernel(False)  # the same kernels as the offloaded decoder, so the same sums
     cached = Decoder(ctx, DecoderConfig(**kw, n_offload=2, n_cache=n_cache))
     steps, prev = 16, 0
     for pos in range(steps):
@@ -395,7 +396,7 @@ def test_a_grid_barrier_that_runs_out_reports_it_and_the_next_step_is_exact(ctx)
     cfg = DecoderConfig(n_layer=2, n_embd=256, n_head=8, n_head_kv=2, head_dim=64, n_expert=8,
                         n_expert_used=2, n_ff=128, n_swa=40, n_ctx=64, seed=0x71AE)
     dec = Decoder(ctx, cfg)
-    assert dec.uses_step_kernel()
+    dec.use_step_kernel(True)
     x0 = O.synth_normal_f32(0x7100, cfg.n_embd, 1.0)
     x1 = O.synth_normal_f32(0x7101, cfg.n_embd, 1.0)
     for x in (x0, x1):
