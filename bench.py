@@ -359,6 +359,56 @@ def gpu_run(args, cfg, rank: int, world: int, dist) -> dict:
         e2e_s = time.perf_counter() - t1
     clocks = sampler.stop() if sampler else None
     pcie = pcie_h2d_gbs(ctx) if cfg.n_offload else None
+
+    # the expert kernels timed from inside graphed steps: every CTA stamps its start, the end of
+    # its dependency wait and its end; per block, the latest end minus the earliest wait-over
+    in_graph = None
+    if not cfg.n_offload:
+        dec.kernel_spans(True)
+        gu, dn = [], []
+        for i in range(4):
+            next_input(i)
+            dec.step()
+            ctx.sync()
+            if i:  # the first step captured the graph again
+                g, d_ = dec.expert_kernel_ms()
+                gu.append(g)
+                dn.append(d_)
+        dec.kernel_spans(False)
+        in_graph = {"gate_up": statistics.mean(gu), "down": statistics.mean(dn), "steps": len(gu)}
+
+    # the same decoder with the whole step as one persistent kernel (opt-in path), for comparison
+    step_kernel = None
+    if not args.no_step_kernel and dec.has_step_kernel():
+        dec.use_step_kernel(True)
+        for i in range(3):
+            next_input(i)
+            dec.step()
+        ctx.sync()
+        n_sk = min(args.steps, 20)
+        ctx.timer_start()
+        for i in range(n_sk):
+            next_input(i)
+            dec.step()
+        sk_ms = ctx.timer_stop() / n_sk
+        # per phase: latest CTA end minus earliest CTA start, averaged over the blocks
+        words = dec.trace_words()
+        buf = ctx.alloc(8 * words)
+        dec.set_trace(buf)
+        dec.step()
+        ctx.sync()
+        tr = np.empty(words, np.uint64)
+        ctx._finish(lib.moearc_copy_d2h(ctx.raw, tr.ctypes.data, buf.ptr, 8 * words), "trace")
+        dec.set_trace(None)
+        buf.free()
+        n_cta = words // (cfg.n_layer * 6 * 4)
+        t = tr.astype(np.int64).reshape(cfg.n_layer, 6, 4, n_cta)
+        span = (t[:, :, 3, :].max(axis=2) - t[:, :, 0, :].min(axis=2)) / 1e3
+        names = ["qkv", "attention", "o_proj", "route", "gate_up", "down"]
+        step_kernel = {"ms_per_step": sk_ms, "tok_s": 1000.0 / sk_ms, "steps": n_sk,
+                       "status": dec.status(),
+                       "phase_span_us_per_block": {n: float(span[:, j].mean()) for j, n in enumerate(names)}}
+        dec.use_step_kernel(False)
     out = np.ctypeslib.as_array(C.cast(host_out, C.POINTER(C.c_float)), (H,)).copy()
     assert np.all(np.isfinite(out)), "non-finite decoder output"
     lib.moearc_x_host_free(host_in)
@@ -368,7 +418,8 @@ def gpu_run(args, cfg, rank: int, world: int, dist) -> dict:
     ctx.close()
     return {"ms_total": ms_total, "e2e_s": e2e_s, "kernel_ms": kernel_ms, "counts": [cnt[i] for i in range(8)],
             "launches_per_step": launches_per_step, "clocks": clocks, "build_s": build_s, "pcie_gbs": pcie,
-            "fetched_per_step": fetched / args.steps, "replay_fetches": replay, "fetched": fetched}
+            "fetched_per_step": fetched / args.steps, "replay_fetches": replay, "fetched": fetched,
+            "in_graph": in_graph, "step_kernel": step_kernel}
 
 
 # ---- MoE prefill on the tensor cores, one GPU -------------------------------------
@@ -452,7 +503,7 @@ def prefill_bench(args) -> dict:
             "counts": cnt, "clocks": clocks, "T": T, "H": H, "I": I, "E": E, "k": k}
 
 
-def prefill_ep_bench(args, rank: int, world: int) -> dict:
+def prefill_ep_bench(args, rank: int, world: int, own_group: bool = True) -> dict:
     """configs[3] with the experts split over `world` GPUs (16 per GPU at 8): each rank holds
     tokens / world tokens, routes them, dispatches rows to the experts' owners and combines the
     returned rows (moearc_b200.ep over NCCL). Per step the device time is taken on every rank
@@ -468,7 +519,8 @@ def prefill_ep_bench(args, rank: int, world: int) -> dict:
     from moearc_b200.ep import ExpertParallelPrefill, PeerExpertParallelPrefill
     from moearc_b200.moe import MoeLayer
 
-    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300))
+    if own_group:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300))
     torch.cuda.set_device(0)
     ctx = Context()
     lib = ctx.lib
@@ -511,7 +563,8 @@ def prefill_ep_bench(args, rank: int, world: int) -> dict:
     dist.barrier()
     ep.close()
     packer.close()
-    dist.destroy_process_group()
+    if own_group:
+        dist.destroy_process_group()
     ctx.close()
     return {"ms_step": float(t[0]) / args.steps, "max_rows": int(t[1]), "T": T * world, "H": H, "I": I, "E": E,
             "k": k, "rows_total": args.tokens * k}
@@ -659,6 +712,28 @@ def batch_main(args) -> None:
     print(json.dumps(line))
 
 
+def shard_sample(args, rank: int, world: int) -> dict | None:
+    """A short sample of the path that does shard over GPUs: configs[3]'s MoE prefill block with
+    the experts split over the `world` ranks (at 1, the same block on one GPU), so the scaling run
+    measures expert parallelism beside the decode replicas. Every rank runs it (the same
+    collectives in the same order); rank 0 gets the numbers."""
+    import copy
+
+    a = copy.copy(args)
+    a.steps, a.warmup, a.tokens, a.experts = 5, 3, 8 * 4096, 128
+    a.weights = "bf16"
+    if world > 1:
+        r = prefill_ep_bench(a, rank, world, own_group=False)
+        label = f"ep{world}, rows exchanged over " + ("NVLink peer memory" if a.exchange == "peer" else "NCCL all-to-all")
+    else:
+        r = prefill_bench(a)
+        label = "1 GPU"
+    flops = 6.0 * r["T"] * r["k"] * r["H"] * r["I"]
+    return {"metric": "MoE prefill TFLOP/s, configs[3] block (32768 tokens, 128 experts top-4, 2880 x 2880)",
+            "value": flops / (r["ms_step"] / 1000.0) / 1e12, "unit": "TFLOP/s", "ms_per_step": r["ms_step"],
+            "steps": a.steps, "warmup": a.warmup, "parallelism": label, "scaling": "strong"}
+
+
 def slowest_rank(ms_total: float, e2e_s: float, dist) -> tuple[float, float]:
     """The timed region's device time and the end-to-end wall time, each the maximum over the
     ranks (every rank calls this, the same collectives in the same order)."""
@@ -704,6 +779,10 @@ def main() -> None:
                     help="with --offload and --cache on the 120b shape: route the offloaded blocks as the "
                          "captured gpt-oss-120b decode trace prose, code or reasoning did, or as a "
                          "moearc-trace-v1 file")
+    ap.add_argument("--no-step-kernel", action="store_true",
+                    help="skip the comparison run of the persistent step kernel")
+    ap.add_argument("--no-ep", action="store_true",
+                    help="skip the expert-parallel prefill sample (configs[3] over the N GPUs)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.config == "prefill":
@@ -745,13 +824,18 @@ def main() -> None:
         if rank != 0:
             return
         cpu = cpu_decode_sample(cfg, budget_s=12.0)
-        line = {"impl": "reference", "metric": METRIC, "value": cpu["value"], "unit": UNIT, "n_gpus": args.gpus,
+        # Our arm at N GPUs runs N independent replicas and sums their tokens/s; the reference arm
+        # is the same sum of N replicas of the reference's CPU path, each timed as one replica on
+        # this host's cores (the reference has no multi-GPU decode).
+        value = cpu["value"] * world
+        line = {"impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
                 "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000.0 / cpu["value"],
                 "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
-                "data": "synthetic", "config": config,
-                "cpu_baseline": {"value": cpu["value"], "unit": UNIT, "cores": cpu["cores"], "kind": "port",
+                "data": "synthetic", "config": config, "replicas": world, "per_replica_value": cpu["value"],
+                "note": "value = replicas x one replica's tokens/s, as our arm sums its N replicas",
+                "cpu_baseline": {"value": value, "unit": UNIT, "cores": cpu["cores"], "kind": "port",
                                  "sample": cpu["sample"]},
-                "e2e": {"value": cpu["value"], "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+                "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
         print(json.dumps(line))
         return
 
@@ -761,11 +845,15 @@ def main() -> None:
 
         import torch.distributed as tdist
 
-        tdist.init_process_group("gloo", timeout=datetime.timedelta(seconds=300))
+        # CPU tensors (the replicas' timing) over gloo, CUDA tensors (the expert-parallel
+        # sample) over NCCL
+        tdist.init_process_group("cpu:gloo,cuda:nccl", timeout=datetime.timedelta(seconds=300))
         dist = tdist
     r = gpu_run(args, cfg, rank, world, dist)
     ms_total, e2e_s = slowest_rank(r["ms_total"], r["e2e_s"], dist)
+    ep = None if args.no_ep else shard_sample(args, rank, world)
     if dist:
+        dist.barrier()
         dist.destroy_process_group()
     if rank != 0:
         return
@@ -777,7 +865,10 @@ def main() -> None:
     fused = r["counts"][5] == 0  # gate-up and down in one launch (the default decode path)
     gu_bytes = k * (3 if fused else 2) * I * H // 32 * 17
     n_gu = max(1, r["counts"][4])
-    gu_ms = r["kernel_ms"]["moe_gate_up"] / n_gu
+    gu_ms_serial = r["kernel_ms"]["moe_gate_up"] / n_gu
+    # the launch time inside the timed graph (CTA timestamps), else the serialised profile's
+    ig = r["in_graph"]
+    gu_ms = ig["gate_up"] / cfg.n_layer if ig and not fused else gu_ms_serial
     achieved = gu_bytes / (gu_ms / 1000.0) / 1e9
     # the whole step's algorithmic bytes: dense bf16 projections, routers, the 4 chosen experts'
     # three matrices, the KV span each block reads
@@ -806,10 +897,16 @@ def main() -> None:
                      "peak_kind": peak_kind, "traffic": expert_traffic(fused),
                      "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum, profiles/",
                      "bytes_per_launch": gu_bytes, "avg_launch_ms": gu_ms,
+                     "avg_launch_ms_source": ("in the timed graph: latest CTA end minus earliest end of a CTA's "
+                                              "dependency wait (%globaltimer), mean over blocks and steps"
+                                              if ig and not fused else "serialised profile (events between launches)"),
+                     "avg_launch_ms_serialised": gu_ms_serial,
                      "frac_of_8tbs": achieved / 8000.0},
         "step_hbm": {"algorithmic_bytes": step_bytes, "achieved_gbs": step_gbs, "frac": step_gbs / peak,
                      "frac_of_8tbs": step_gbs / 8000.0},
-        "kernel_ms_per_step": r["kernel_ms"],
+        "kernel_ms_per_step_serialised": r["kernel_ms"],
+        "expert_kernels_in_graph_ms_per_step": ig,
+        "step_kernel": r["step_kernel"],
         "e2e": {"value": e2e, "unit": UNIT, "h2d_bytes_per_step": 4 * H, "d2h_bytes_per_step": 4 * H},
         "gpu_launches": r["launches_per_step"] * args.steps,
         "clocks": r["clocks"],
@@ -833,6 +930,8 @@ def main() -> None:
                             "achieved": pcie_gbs, "peak": r["pcie_gbs"], "unit": "GB/s",
                             "frac": pcie_gbs / r["pcie_gbs"], "peak_kind": "measured in this run (pinned H2D copy)",
                             "traffic": None, "bytes_per_step": pcie_b}
+    if ep:
+        line["ep_prefill"] = ep
     if world == 1 and not args.no_cpu:
         line["cpu_baseline"] = cpu_decode_sample(cfg, budget_s=12.0)
     print(json.dumps(line))

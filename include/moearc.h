@@ -342,9 +342,15 @@ int moearc_x_decoder_profile(moearc_x_decoder *d, float *ms, int *counts, int n)
 /* Device pointer (and size) of one block's tensor: 0 attn_norm, 1 ffn_norm, 2 sinks,
  * 3 router, 4 K pool, 5 V pool, 6 page table, 7 packed Q/K/V, 8 packed O, 9 packed gate-up,
  * 10 packed down, 11 output norm; with the persistent step kernel, 12 the block's expert ids
- * of the last step (k u32, router order) and 13 their gating weights (k f32). For an offloaded
- * block, 9 and 10 are device-visible pointers of the pinned host banks. */
+ * of the last step (k u32, router order) and 13 their gating weights (k f32); with kernel spans
+ * on, 14 the kernel chain's expert-kernel timestamps of the last step (u64 [2 kernels: gate-up,
+ * down][CTA][start, dependency wait over, end], ns of %globaltimer). For an offloaded block, 9
+ * and 10 are device-visible pointers of the pinned host banks. */
 void *moearc_x_decoder_tensor(moearc_x_decoder *d, int which, unsigned int layer, unsigned long *bytes);
+/* Turn on (1) or off (0) the expert kernels' per-CTA timestamps in the kernel chain (tensor 14),
+ * so their duration can be read from inside a graphed step. Synchronises the stream; the next
+ * step re-captures its graph. No reference counterpart. */
+int moearc_x_decoder_kernel_spans(moearc_x_decoder *d, int on);
 /* The seed tensor `kind` of block `layer` was generated from, given the model seed. */
 unsigned long long moearc_x_decoder_seed(moearc_x_decoder *d, int kind, unsigned int layer,
                                          unsigned long long base);

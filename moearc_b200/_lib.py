@@ -117,6 +117,7 @@ SIGNATURES: dict[str, tuple] = {
     "moearc_x_decoder_fill_kv": (I, [P, U, C.c_ulonglong]),
     "moearc_x_decoder_step": (I, [P]),
     "moearc_x_decoder_use_graph": (I, [P, I]),
+    "moearc_x_decoder_kernel_spans": (I, [P, I]),
     "moearc_x_decoder_status": (I, [P]),
     "moearc_x_decoder_fetched": (C.c_ulonglong, [P]),
     "moearc_x_decoder_profile": (I, [P, C.POINTER(F), C.POINTER(I), I]),

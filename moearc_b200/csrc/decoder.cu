@@ -34,7 +34,8 @@ int moe_forward_impl(moearc_x_moe *m, const float *x, unsigned n_tokens, const f
                      const float *router_w, const float *router_b, const void *gateup_packed,
                      const void *down_packed, const float *residual, float *out,
                      std::vector<cudaEvent_t> *marks = nullptr, std::vector<int> *kinds = nullptr,
-                     const moe_offload *off = nullptr);
+                     const moe_offload *off = nullptr, unsigned long long *span = nullptr);
+int moe_decode_grid(moearc_x_moe *m);
 size_t attn_scratch_bytes(size_t n_heads, size_t head_dim, int n_splits);
 int attn_launch(moearc_ctx *c, float *out, const float *q, const void *kp, const void *vp,
                 const unsigned *table, const float *sinks, size_t n_heads, size_t n_kv_heads,
@@ -115,6 +116,9 @@ struct moearc_x_decoder {
     // of per-block kernels otherwise (offloaded experts, head_dim 128, ...) or on request
     step_plan *step = nullptr;
     bool use_step = false;
+    // the chain's expert kernels' CTA timestamps per block (moearc_x_decoder_kernel_spans), or null
+    unsigned long long *spans = nullptr;
+    int span_cta = 0;
 
     void drop_graph() {
         if (exec) cudaGraphExecDestroy(exec);
@@ -186,7 +190,8 @@ int enqueue_step(moearc_x_decoder *d, step_marks *pm = nullptr) {
         if (pm) pm->mark(c->stream, 2);
         rc = moe_forward_impl(d->moe, d->h, 1, b.ffn_norm, cfg.rms_eps, b.router, nullptr, b.gateup, b.down,
                               d->h, d->h, pm ? &pm->ev : nullptr, pm ? &pm->kind : nullptr,
-                              l < cfg.n_offload ? (cfg.n_cache ? &b.off : &d->off) : nullptr);
+                              l < cfg.n_offload ? (cfg.n_cache ? &b.off : &d->off) : nullptr,
+                              d->spans ? d->spans + (size_t)l * 2 * d->span_cta * 3 : nullptr);
         if (rc) return rc;
     }
     if (launch_pdl(k_step_end, dim3(1), dim3(512), 0, c->stream, d->out, (const float *)d->h,
@@ -441,6 +446,7 @@ void moearc_x_decoder_destroy(moearc_x_decoder *d) {
     cudaStreamSynchronize(d->c->stream);
     d->drop_graph();
     step_destroy(d->step);
+    if (d->spans) cudaFree(d->spans);
     if (d->moe) moearc_x_moe_destroy(d->moe);
     if (d->qkv) dense_destroy(d->qkv);
     if (d->wo) dense_destroy(d->wo);
@@ -525,6 +531,27 @@ int moearc_x_decoder_set_trace(moearc_x_decoder *d, void *device_buffer) {
     return OK;
 }
 
+int moearc_x_decoder_kernel_spans(moearc_x_decoder *d, int on) {
+    if (!d) return ERR;
+    if (cudaStreamSynchronize(d->c->stream) != cudaSuccess) return ERR;
+    if (on && !d->spans) {
+        d->span_cta = moe_decode_grid(d->moe);
+        if (!d->span_cta) return ERR_ARG;
+        const size_t bytes = sizeof(unsigned long long) * d->cfg.n_layer * 2 * d->span_cta * 3;
+        if (cudaMalloc(&d->spans, bytes) != cudaSuccess) {
+            cudaGetLastError();
+            d->spans = nullptr;
+            return ERR;
+        }
+        if (cudaMemset(d->spans, 0, bytes) != cudaSuccess) return ERR;
+    } else if (!on && d->spans) {
+        cudaFree(d->spans);
+        d->spans = nullptr;
+    }
+    d->drop_graph();
+    return OK;
+}
+
 int moearc_x_decoder_use_graph(moearc_x_decoder *d, int on) {
     if (!d) return ERR;
     d->use_graph = on != 0;
@@ -591,7 +618,10 @@ int moearc_x_decoder_profile(moearc_x_decoder *d, float *ms, int *counts, int n)
 
 // Device pointers of one block's tensors, for inspection: 0 attn_norm, 1 ffn_norm, 2 sinks,
 // 3 router, 4 K pool, 5 V pool, 6 page table, 7 packed Q/K/V, 8 packed O, 9 packed gate-up,
-// 10 packed down; 11 output norm (layer ignored). `bytes` receives the size.
+// 10 packed down; 11 output norm (layer ignored); 12/13 the step kernel's expert ids and gating
+// weights of the last step; 14 the chain's expert-kernel spans of the last step (u64
+// [2 kernels][CTA][start, wait over, end] in ns, while kernel spans are on). `bytes` receives
+// the size.
 void *moearc_x_decoder_tensor(moearc_x_decoder *d, int which, unsigned layer, unsigned long *bytes) {
     if (!d || (which != 11 && layer >= d->cfg.n_layer)) return nullptr;
     const auto &g = d->cfg;
@@ -621,6 +651,8 @@ void *moearc_x_decoder_tensor(moearc_x_decoder *d, int which, unsigned layer, un
                  n = p ? g.n_expert_used * 4 : 0; break;
         case 13: p = d->step ? static_cast<float *>(step_buffer(d->step, 1)) + (size_t)layer * g.n_expert_used : nullptr;
                  n = p ? g.n_expert_used * 4 : 0; break;
+        case 14: p = d->spans ? d->spans + (size_t)layer * 2 * d->span_cta * 3 : nullptr;
+                 n = p ? (unsigned long)2 * d->span_cta * 3 * 8 : 0; break;
         default: return nullptr;
         }
     }

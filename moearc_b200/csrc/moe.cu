@@ -955,6 +955,9 @@ struct xexp_args {
     xtab *tab_pub;            // gate-up: CTA 0 publishes its tables here; down: read them (or null)
     const int *slot_of;       // residency cache: expert -> slot of the bank (or null)
     int by_slot;              // bank holds one expert per slot (staged offload), not all experts
+    // per CTA [start, dependency wait over, end] in ns of %globaltimer (the end the last warp's),
+    // rewritten every launch, or null
+    unsigned long long *span;
     int *status;
 };
 
@@ -1018,6 +1021,16 @@ __global__ void __launch_bounds__(XW * 32, 1) k_xexpert(xexp_args a) {
     TRACE(0);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     constexpr int MATS = MODE == 0 ? 2 : 1;
+    unsigned long long *span = a.span ? a.span + (size_t)blockIdx.x * 3 : nullptr;
+    if (span && threadIdx.x == 0) {
+        span[0] = xnow();
+        span[2] = 0;  // before the CTA's first barrier; the warps' ends are taken after it
+    }
+    // the CTA's end: the latest of its warps' returns
+#define XSPAN_END()                                          \
+    do {                                                     \
+        if (span && lane == 0) atomicMax(span + 2, xnow()); \
+    } while (0)
     if (MODE == 0) {
         // Before the wait, a dry run of the table build on whatever the logits hold now (the
         // router kernel is still writing them; these tables are discarded): it brings the
@@ -1026,6 +1039,7 @@ __global__ void __launch_bounds__(XW * 32, 1) k_xexpert(xexp_args a) {
         TRACE(13);
         // the logits are the previous kernel's output
         pdl_wait();
+        if (span && threadIdx.x == 0) span[1] = xnow();
         TRACE(12);
         // CTA 0 releases the down kernel only once it has published the tables (below)
         if (blockIdx.x != 0 || !a.tab_pub) pdl_trigger();
@@ -1132,6 +1146,7 @@ __global__ void __launch_bounds__(XW * 32, 1) k_xexpert(xexp_args a) {
         // staged down banks are the previous kernel's output: nothing streams before the wait
         pdl_trigger();
         pdl_wait();
+        if (span && threadIdx.x == 0) span[1] = xnow();
     }
     if (a.slot_of) {
         // cached offload: the block's residency table (final before either kernel's wait
@@ -1152,6 +1167,7 @@ __global__ void __launch_bounds__(XW * 32, 1) k_xexpert(xexp_args a) {
         // kernel's output and follow the wait
         pdl_trigger();
         pdl_wait();
+        if (span && threadIdx.x == 0 && !a.by_slot) span[1] = xnow();
         TRACE(2);
         if (lane == 0) {
             cur c = start;
@@ -1214,7 +1230,10 @@ __global__ void __launch_bounds__(XW * 32, 1) k_xexpert(xexp_args a) {
         for (long j = kf; j < n_issued; ++j) mbar_wait(&bars[warp][j % XSTAGES], (unsigned)((j / XSTAGES) & 1), a.status);
         return;
     }
-    if (qb <= qa) return;
+    if (qb <= qa) {
+        XSPAN_END();
+        return;
+    }
     TRACE(10);
     TRACE_WARP(14 + warp);
     // This warp finishes the units (gate-up: segment; down: tile-row) whose last piece lies in
@@ -1222,7 +1241,10 @@ __global__ void __launch_bounds__(XW * 32, 1) k_xexpert(xexp_args a) {
     // fence stand between the last piece and the unit's result.
     const long upc = MODE == 0 ? (long)np : (long)G * np;  // pieces per unit
     const int u_lo = (int)((qa + upc) / upc) - 1, u_hi = (int)(qb / upc) - 1;
-    if (u_lo > u_hi) return;
+    if (u_lo > u_hi) {
+        XSPAN_END();
+        return;
+    }
 #ifdef MOEARC_TRACE
     int n_rounds = 0;
 #define TRACE_ROUNDS (&n_rounds)
@@ -1327,6 +1349,8 @@ __global__ void __launch_bounds__(XW * 32, 1) k_xexpert(xexp_args a) {
         }
     }
 #undef TRACE_ROUNDS
+    XSPAN_END();
+#undef XSPAN_END
 #ifdef MOEARC_TRACE
     if (lane == 0 && g_trace) {
         unsigned long long t_;
@@ -2290,7 +2314,8 @@ namespace moearc {
 int moe_forward_impl(moearc_x_moe *m, const float *x, unsigned n_tokens, const float *norm_w, float eps,
                      const float *router_w, const float *router_b, const void *gateup_packed,
                      const void *down_packed, const float *residual, float *out,
-                     std::vector<cudaEvent_t> *marks, std::vector<int> *kinds, const moe_offload *off) {
+                     std::vector<cudaEvent_t> *marks, std::vector<int> *kinds, const moe_offload *off,
+                     unsigned long long *span) {
     auto mark = [&](int k) {
         if (!marks) return;
         cudaEvent_t e;
@@ -2435,6 +2460,7 @@ int moe_forward_impl(moearc_x_moe *m, const float *x, unsigned n_tokens, const f
         xa.tab_pub = off ? nullptr : static_cast<xtab *>(m->x_tab_pub);
         xa.slot_of = off ? off->slot_of : nullptr;
         xa.status = m->status;
+        xa.span = span;  // the gate-up kernel's CTAs, then the down kernel's
         const bool mx = m->wtype == T_MXFP4;
         // More than half an SM's shared memory, so no SM takes two gate-up CTAs: at launch the
         // router's CTAs still hold some SMs, and a CTA that fits beside another gate-up CTA
@@ -2454,6 +2480,7 @@ int moe_forward_impl(moearc_x_moe *m, const float *x, unsigned n_tokens, const f
             mark(7);
         }
         xexp_args xd = xa;
+        xd.span = span ? span + (size_t)m->x_grid * 3 : nullptr;
         xd.bank = off ? off->dn_stage : static_cast<const uint8_t *>(down_packed);
         xd.bank_stride = dn_stride;
         xd.ntr = m->ntr_h;
@@ -2535,6 +2562,9 @@ int moe_forward_impl(moearc_x_moe *m, const float *x, unsigned n_tokens, const f
     return ls.finish();
 }
 
+// CTAs of each decode-path expert kernel (their span records, per kernel).
+int moe_decode_grid(moearc_x_moe *m) { return m && m->xpath ? m->x_grid : 0; }
+
 }  // namespace moearc
 
 extern "C" {
@@ -2543,7 +2573,7 @@ int moearc_x_moe_forward(moearc_x_moe *m, const float *x, unsigned n_tokens, con
                          const float *router_b, const void *gateup_packed, const void *down_packed,
                          const float *residual, float *out) {
     return moe_forward_impl(m, x, n_tokens, nullptr, 0.f, router_w, router_b, gateup_packed, down_packed,
-                            residual, out, nullptr, nullptr, nullptr);
+                            residual, out, nullptr, nullptr, nullptr, nullptr);
 }
 
 void *moearc_x_moe_buffer(moearc_x_moe *m, int which) {

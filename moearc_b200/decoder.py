@@ -154,6 +154,22 @@ class Decoder:
         """Block `layer`'s expert ids and gating weights of the last step (persistent kernel)."""
         return self.tensor(12, layer, np.uint32), self.tensor(13, layer, np.float32)
 
+    def kernel_spans(self, on: bool) -> None:
+        """Per-CTA timestamps of the kernel chain's expert kernels in every following step."""
+        self.ctx._finish(self.ctx.lib.moearc_x_decoder_kernel_spans(self.h, 1 if on else 0), "kernel_spans")
+
+    def expert_kernel_ms(self) -> tuple[float, float]:
+        """The last step's gate-up and down expert kernels, each timed from inside the step (a
+        graph replay included) as the latest CTA end minus the earliest moment a CTA's
+        dependency wait was over, summed over the blocks: (gate-up ms, down ms)."""
+        tot = [0.0, 0.0]
+        for layer in range(self.cfg.n_layer):
+            s = self.tensor(14, layer, np.uint64).reshape(2, -1, 3).astype(np.int64)
+            for k in range(2):
+                ends, waits = s[k, :, 2], s[k, :, 1]
+                tot[k] += (ends.max() - waits.min()) / 1e6
+        return tot[0], tot[1]
+
     def fetched(self) -> int:
         """Experts the offloaded blocks' residency caches fetched over PCIe since create."""
         return self.ctx.lib.moearc_x_decoder_fetched(self.h)
