@@ -275,6 +275,12 @@ def gpu_run(args, cfg, rank: int, world: int, dist) -> dict:
         dec.fill_kv(args.depth)
     else:
         dec.set_pos(0)
+    if args.host:
+        kind, _, val = args.host.partition(":")
+        if kind == "fraction":
+            dec.host_experts("fraction", fraction=float(val), threads=args.host_threads)
+        else:
+            dec.host_experts("over", over=int(val), threads=args.host_threads)
     lib = ctx.lib
     H = cfg.n_embd
     host_in = lib.moearc_x_host_alloc(4 * H)
@@ -321,6 +327,7 @@ def gpu_run(args, cfg, rank: int, world: int, dist) -> dict:
         dist.barrier()
     ctx.sync()
     fetched0 = dec.fetched()
+    host0 = dec.host_stats() if args.host else None
     h0 = len(route.history) if route else 0
     if route:
         # the routers are set between steps, so each step is timed on its own
@@ -338,6 +345,10 @@ def gpu_run(args, cfg, rank: int, world: int, dist) -> dict:
             dec.step()
         ms_total = ctx.timer_stop()
     fetched = dec.fetched() - fetched0
+    host = None
+    if args.host:
+        h1 = dec.host_stats()
+        host = {k: (h1[k] - host0[k]) / args.steps for k in h1}
     replay = (route.replay_fetches(cfg.n_cache, len(route.history)) - route.replay_fetches(cfg.n_cache, h0)
               if route else None)
 
@@ -419,7 +430,7 @@ def gpu_run(args, cfg, rank: int, world: int, dist) -> dict:
     return {"ms_total": ms_total, "e2e_s": e2e_s, "kernel_ms": kernel_ms, "counts": [cnt[i] for i in range(8)],
             "launches_per_step": launches_per_step, "clocks": clocks, "build_s": build_s, "pcie_gbs": pcie,
             "fetched_per_step": fetched / args.steps, "replay_fetches": replay, "fetched": fetched,
-            "in_graph": in_graph, "step_kernel": step_kernel}
+            "in_graph": in_graph, "step_kernel": step_kernel, "host": host}
 
 
 # ---- MoE prefill on the tensor cores, one GPU -------------------------------------
@@ -779,6 +790,11 @@ def main() -> None:
                     help="with --offload and --cache on the 120b shape: route the offloaded blocks as the "
                          "captured gpt-oss-120b decode trace prose, code or reasoning did, or as a "
                          "moearc-trace-v1 file")
+    ap.add_argument("--host", default=None,
+                    help="with --offload: part of the offloaded blocks' experts on host threads beside the GPU, "
+                         "'fraction:F' (the first ceil(misses x F) of each block's misses) or 'over:N' (the misses "
+                         "beyond the first N)")
+    ap.add_argument("--host-threads", type=int, default=0, help="host pool threads (0: the online cores - 1)")
     ap.add_argument("--no-step-kernel", action="store_true",
                     help="skip the comparison run of the persistent step kernel")
     ap.add_argument("--no-ep", action="store_true",
@@ -807,6 +823,10 @@ def main() -> None:
                  f"{cfg.n_cache} device slots per block keep fetched experts (least recently used evicted), "
                  + (f"the offloaded blocks routed as the captured gpt-oss-120b {args.trace} decode trace"
                     if args.trace else "a new N(0,1) input every step"))
+    if args.host and not cfg.n_offload:
+        raise SystemExit("--host needs --offload")
+    if args.host:
+        residency += f"; host experts {args.host} of each offloaded block's misses on the host cores beside the GPU"
     if args.trace and not (cfg.n_cache and args.config == "120b" and cfg.n_offload <= 36):
         raise SystemExit("--trace needs --config 120b, --offload and --cache")
     workload = (f"configs[{2 if args.config == '120b' else 1}] gpt-oss-{args.config} shape, batch-1 decode, "
@@ -916,6 +936,9 @@ def main() -> None:
         # mode (b) is bound by PCIe: the offloaded blocks' routed experts cross it every step
         # (with a cache, only the misses: the experts counted as fetched)
         pcie_b = cfg.n_offload * expert_b
+        if r["host"] and not cfg.n_cache:
+            # the experts the host computes do not cross PCIe
+            pcie_b = (cfg.n_offload * k - r["host"]["experts"]) * expert_b / k
         if cfg.n_cache:
             pcie_b = r["fetched_per_step"] * expert_b / cfg.n_expert_used
             line["cache"] = {"slots_per_block": cfg.n_cache, "experts_fetched_per_step": r["fetched_per_step"],
@@ -930,6 +953,11 @@ def main() -> None:
                             "achieved": pcie_gbs, "peak": r["pcie_gbs"], "unit": "GB/s",
                             "frac": pcie_gbs / r["pcie_gbs"], "peak_kind": "measured in this run (pinned H2D copy)",
                             "traffic": None, "bytes_per_step": pcie_b}
+    if r["host"]:
+        h = r["host"]
+        line["host_experts"] = {"policy": args.host, "experts_per_step": h["experts"], "jobs_per_step": h["jobs"],
+                                "pool_busy_ms_per_step": h["busy_ns"] / 1e6,
+                                "sync_wait_ms_per_step": h["wait_ns"] / 1e6}
     if ep:
         line["ep_prefill"] = ep
     if world == 1 and not args.no_cpu:

@@ -188,6 +188,53 @@ int moearc_x_moe_forward(moearc_x_moe *m, const float *x, unsigned int n_tokens,
 void *moearc_x_moe_buffer(moearc_x_moe *m, int which);
 /* Reads and clears the device status word: 0, or bit 1 = a bounded wait gave up. */
 int moearc_x_moe_status(moearc_x_moe *m);
+/* Per-expert biases for the following forward calls (moe.rs:2310-2331, 2362-2372, gpt-oss):
+ * gate_up_bias f32 [2 n_expert][n_ff] (expert e's gate bias at row e, its up bias at row
+ * n_expert + e), added after the expert matvecs and before the activation; down_bias f32
+ * [n_expert][n_embd], added to each expert's output inside the router weighting. Device
+ * pointers (NULL: none), kept until the next call; moearc_add_bias_id's semantics fused into the
+ * decode kernels. */
+int moearc_x_moe_set_bias(moearc_x_moe *m, const float *gate_up_bias, const float *down_bias);
+/* The decode-path expert kernels' wait for one another's partial sums (ns; 0 = the default
+ * 0.2 s); phantom 1 makes every such wait run out (testing the bounded wait). No reference
+ * counterpart. */
+int moearc_x_moe_set_wait(moearc_x_moe *m, unsigned long long poll_ns, int phantom);
+
+/* ---- expert FFNs on the host cores (host_experts.cpp; no GPU needed) ---------------------
+ * The reference's HostExecutor (crates/moearc-engine/src/host_experts.rs:423-761): a pool of
+ * worker threads that computes a token's FFN through a few experts on the CPU while the device
+ * works, phase A (gate, up, activation) then phase B (down), the experts folded in router order
+ * by the syncing thread (dst = 0; dst += w * part). The banks are the packed ones
+ * (moearc_x_moe_pack layout) in host memory, so an offloaded block keeps one copy of its
+ * experts; rows are decoded with AVX2 + FMA + F16C when the CPU has them (MOEARC_HOST_SCALAR=1
+ * at create: the portable kernel). */
+typedef struct moearc_x_host_pool moearc_x_host_pool;
+/* host_experts.rs:445-456 HostExecutor::new: n_threads <= 0 takes MOEARC_HOST_THREADS, else the
+ * online cores - 1. NULL when threads cannot start. */
+moearc_x_host_pool *moearc_x_host_pool_create(int n_threads);
+void moearc_x_host_pool_destroy(moearc_x_host_pool *p);
+int moearc_x_host_pool_threads(const moearc_x_host_pool *p);
+/* host_experts.rs:624-714 submit: publish out = sum over i < n of weights[i] *
+ * down_e . act(gate_e . x, up_e . x), e = experts[i] (n <= 32; the shape, act, alpha, limit and
+ * wtype from d), and return without waiting. The pool copies experts, weights and x; the banks
+ * (every expert, HOST pointers) stay in use until sync returns. -1 while a job is pending or on
+ * NULL, -2 on a shape the pool does not serve (n_embd, n_ff multiples of 64; MXFP4 or Q4_0). */
+int moearc_x_host_submit(moearc_x_host_pool *p, const moearc_x_moe_desc *d, const void *gateup_packed,
+                         const void *down_packed, const unsigned int *experts, const float *weights,
+                         unsigned int n, const float *x);
+/* host_experts.rs:717-761 sync: work on the pending job beside the workers, wait for it, write
+ * its sum (n_embd floats) to out. -1 with no job pending. */
+int moearc_x_host_sync(moearc_x_host_pool *p, float *out);
+/* submit + sync. */
+int moearc_x_host_ffn(moearc_x_host_pool *p, const moearc_x_moe_desc *d, const void *gateup_packed,
+                      const void *down_packed, const unsigned int *experts, const float *weights,
+                      unsigned int n, const float *x, float *out);
+/* host_experts.rs:604-611 HostStats: out4 = jobs, experts, ns the threads spent inside jobs, ns
+ * sync waited for the workers. */
+void moearc_x_host_stats(const moearc_x_host_pool *p, unsigned long long *out4);
+/* moearc_x_moe_pack on the host: the same packed bytes from GGUF-layout banks in host memory. */
+int moearc_x_moe_pack_host(const moearc_x_moe_desc *d, const void *gate, const void *up, const void *down,
+                           unsigned int n_expert, void *gateup_packed, void *down_packed);
 
 /* ---- MoE prefill on tcgen05 (prefill.cu; no counterpart in the reference, whose engine
  * decodes one token at a time through matvec kernels, crates/moearc-engine/src/moe.rs:2074-2427)
@@ -314,10 +361,18 @@ typedef struct {
      * used slot the step does not need. 0: no cache (one slot per routed expert, refilled every
      * step); otherwise at least n_expert_used and at most n_expert. */
     unsigned int n_cache;
+    /* QK-norm (moe.rs:1961-1985, the qwen3moe form): q and k normalised per head over head_dim
+     * channels with one head_dim-wide weight per block, before RoPE. */
+    unsigned int has_qk_norm;
+    /* The output head (moe.rs:2434-2437): logits = W_out . rmsnorm(h) with W_out bf16
+     * [n_vocab][n_embd] (n_vocab a multiple of 16), after every step; 0 = none. */
+    unsigned int n_vocab;
 } moearc_x_decoder_cfg;
 moearc_x_decoder *moearc_x_decoder_create(moearc_ctx *c, const moearc_x_decoder_cfg *cfg);
 void moearc_x_decoder_destroy(moearc_x_decoder *d);
-void *moearc_x_decoder_input(moearc_x_decoder *d);   /* device, n_embd f32 */
+void *moearc_x_decoder_input(moearc_x_decoder *d);
+/* Device pointer of the last step's logits (n_vocab f32), or NULL without an output head. */
+void *moearc_x_decoder_logits(moearc_x_decoder *d);   /* device, n_embd f32 */
 void *moearc_x_decoder_output(moearc_x_decoder *d);  /* device, n_embd f32 */
 int moearc_x_decoder_pos(moearc_x_decoder *d);       /* the next position to decode */
 int moearc_x_decoder_set_pos(moearc_x_decoder *d, unsigned int pos);
@@ -339,13 +394,35 @@ unsigned long long moearc_x_decoder_fetched(moearc_x_decoder *d);
  * down, 6 final norm, 7 expert fetch of an offloaded block) summed over the blocks, counts[k]
  * the launches; n >= 7 (kinds >= n are not reported). */
 int moearc_x_decoder_profile(moearc_x_decoder *d, float *ms, int *counts, int n);
+/* Host execution of part of the offloaded blocks' experts (moe.rs:2169-2211 the split,
+ * 2389-2420 the fold; HostPolicy host_experts.rs:91-127): kind 0 off, 1 the first
+ * ceil(misses x fraction) of a block's misses in router order, 2 the misses beyond the first
+ * `over`; a miss is a routed expert the block's residency cache does not hold (without a cache,
+ * every routed expert). Those experts are computed by a pool of n_threads host threads
+ * (moearc_x_host_pool_create's rule for <= 0) from the block's pinned packed banks while the device
+ * streams the others; a cache admits only the device's share. Needs n_offload > 0 (-2
+ * otherwise). The split and the answer pass through a mailbox in pinned memory that a host
+ * thread polls (no host function in the step's graph). Synchronises the stream; the next step
+ * re-captures its graph. */
+int moearc_x_decoder_host_experts(moearc_x_decoder *d, int kind, float fraction, unsigned int over,
+                                  int n_threads);
+/* The fold's wait for the host's answer: limit_ns (0: the default 2 s), after which the step
+ * raises the status (STATUS bit 1) and leaves the host's share out; hold = 1 makes the host
+ * thread ignore new jobs (for testing that the wait runs out), 0 resumes. No reference
+ * counterpart (its sync waits without a limit, host_experts.rs:717-745). Synchronises the stream. */
+int moearc_x_decoder_host_wait(moearc_x_decoder *d, unsigned long long limit_ns, int hold);
+/* The host pool's counters since create (moearc_x_host_stats); zeros without a pool.
+ * Synchronises the stream. */
+int moearc_x_decoder_host_stats(moearc_x_decoder *d, unsigned long long *out4);
 /* Device pointer (and size) of one block's tensor: 0 attn_norm, 1 ffn_norm, 2 sinks,
  * 3 router, 4 K pool, 5 V pool, 6 page table, 7 packed Q/K/V, 8 packed O, 9 packed gate-up,
  * 10 packed down, 11 output norm; with the persistent step kernel, 12 the block's expert ids
  * of the last step (k u32, router order) and 13 their gating weights (k f32); with kernel spans
  * on, 14 the kernel chain's expert-kernel timestamps of the last step (u64 [2 kernels: gate-up,
- * down][CTA][start, dependency wait over, end], ns of %globaltimer). For an offloaded block, 9
- * and 10 are device-visible pointers of the pinned host banks. */
+ * down][CTA][start, dependency wait over, end], ns of %globaltimer); 15 / 16 the QK-norm
+ * weights (head_dim f32, with has_qk_norm); 17 the packed bf16 output head (layer ignored, with
+ * n_vocab). For an offloaded block, 9 and 10 are device-visible pointers of the pinned host
+ * banks. */
 void *moearc_x_decoder_tensor(moearc_x_decoder *d, int which, unsigned int layer, unsigned long *bytes);
 /* Turn on (1) or off (0) the expert kernels' per-CTA timestamps in the kernel chain (tensor 14),
  * so their duration can be read from inside a graphed step. Synchronises the stream; the next
@@ -366,10 +443,13 @@ int moearc_x_decoder_has_step_kernel(moearc_x_decoder *d);
 int moearc_x_decoder_uses_step_kernel(moearc_x_decoder *d);
 /* Choose the persistent kernel (on, when the shape has one; -2 otherwise) or the chain. */
 int moearc_x_decoder_use_step_kernel(moearc_x_decoder *d, int on);
-/* The persistent kernel's grid-barrier wait limit (ns; 0 = the default 0.2 s) and a count of
- * arrivals each barrier waits for beyond the CTAs' own (0 in use; 1 makes the first barrier
- * run out, for testing the bounded wait: the step then sets the status word and returns, its
- * output invalid). Synchronises the stream; the next step re-captures its graph. */
+/* The decode kernels' wait limits (ns; 0 = the default 0.2 s): the persistent kernel's grid
+ * barriers and the chain's expert kernels' waits for one another's partial sums. phantom 1
+ * makes them run out, for testing the bounded waits: the persistent kernel's first barrier
+ * waits for one arrival beyond the CTAs', the expert kernels' finishing warps never see their
+ * partials; the step then sets the status word and returns, its output invalid (reading the
+ * status restores the partial buffers). Synchronises the stream; the next step re-captures
+ * its graph. */
 int moearc_x_decoder_set_wait(moearc_x_decoder *d, unsigned long long limit_ns, unsigned int phantom);
 /* Phase timestamps of the persistent kernel: with a device buffer of trace_words u64 set,
  * every following step writes %globaltimer (ns) at four points of each phase of each block in
@@ -386,7 +466,8 @@ int moearc_x_decoder_set_trace(moearc_x_decoder *d, void *device_buffer);
  * weights as moearc_x_decoder_create would generate from it): bf16 activations into tcgen05
  * GEMMs for Q/K/V and O, RoPE and paged bf16 KV per sequence, one batched decode-attention launch,
  * and the prefill MoE block, with the experts expanded to bf16 once at create and the router on
- * the f32 activations. Requires n_swa == 0, no sinks, n_offload == 0; NULL otherwise. */
+ * the f32 activations; QK-norm with has_qk_norm. Requires n_swa == 0, no sinks, n_offload == 0,
+ * n_vocab == 0; NULL otherwise. */
 typedef struct moearc_x_batch_decoder moearc_x_batch_decoder;
 moearc_x_batch_decoder *moearc_x_batch_decoder_create(moearc_ctx *c, const moearc_x_decoder_cfg *cfg,
                                                       unsigned int n_batch);

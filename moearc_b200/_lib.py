@@ -73,6 +73,16 @@ SIGNATURES: dict[str, tuple] = {
     "moearc_x_moe_forward": (I, [P, P, U, P, P, P, P, P, P]),
     "moearc_x_moe_buffer": (P, [P, I]),
     "moearc_x_moe_status": (I, [P]),
+    "moearc_x_moe_set_wait": (I, [P, C.c_ulonglong, I]),
+    "moearc_x_moe_set_bias": (I, [P, P, P]),
+    "moearc_x_host_pool_create": (P, [I]),
+    "moearc_x_host_pool_destroy": (None, [P]),
+    "moearc_x_host_pool_threads": (I, [P]),
+    "moearc_x_host_submit": (I, [P, P, P, P, P, P, U, P]),
+    "moearc_x_host_sync": (I, [P, P]),
+    "moearc_x_host_ffn": (I, [P, P, P, P, P, P, U, P, P]),
+    "moearc_x_host_stats": (None, [P, P]),
+    "moearc_x_moe_pack_host": (I, [P, P, P, P, U, P, P]),
     "moearc_x_prefill_create": (P, [P, P]),
     "moearc_x_prefill_destroy": (None, [P]),
     "moearc_x_prefill_load": (I, [P, P, P]),
@@ -112,12 +122,16 @@ SIGNATURES: dict[str, tuple] = {
     "moearc_x_decoder_destroy": (None, [P]),
     "moearc_x_decoder_input": (P, [P]),
     "moearc_x_decoder_output": (P, [P]),
+    "moearc_x_decoder_logits": (P, [P]),
     "moearc_x_decoder_pos": (I, [P]),
     "moearc_x_decoder_set_pos": (I, [P, U]),
     "moearc_x_decoder_fill_kv": (I, [P, U, C.c_ulonglong]),
     "moearc_x_decoder_step": (I, [P]),
     "moearc_x_decoder_use_graph": (I, [P, I]),
     "moearc_x_decoder_kernel_spans": (I, [P, I]),
+    "moearc_x_decoder_host_experts": (I, [P, I, F, U, I]),
+    "moearc_x_decoder_host_stats": (I, [P, P]),
+    "moearc_x_decoder_host_wait": (I, [P, C.c_ulonglong, I]),
     "moearc_x_decoder_status": (I, [P]),
     "moearc_x_decoder_fetched": (C.c_ulonglong, [P]),
     "moearc_x_decoder_profile": (I, [P, C.POINTER(F), C.POINTER(I), I]),
@@ -152,7 +166,7 @@ class DecoderCfg(C.Structure):
                 ("act", U), ("alpha", F), ("limit", F), ("n_swa", U), ("swa_pattern", U),
                 ("rope_base", F), ("rope_freq_scale", F), ("rope_ext_factor", F), ("rope_attn_factor", F),
                 ("rope_corr_lo", F), ("rope_corr_hi", F), ("rms_eps", F), ("has_sinks", U), ("n_ctx", U),
-                ("seed", C.c_ulonglong), ("n_offload", U), ("n_cache", U)]
+                ("seed", C.c_ulonglong), ("n_offload", U), ("n_cache", U), ("has_qk_norm", U), ("n_vocab", U)]
 
 
 class MoeDesc(C.Structure):

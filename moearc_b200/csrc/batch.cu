@@ -69,15 +69,30 @@ __global__ void __launch_bounds__(256) k_bd_norm(const float *h, const float *w,
 // NeoX RoPE at each stream's position on its q heads (-> q) and k heads, and k, v appended to the
 // stream's pages (bf16). Block (head, stream), D / 2 threads; the angle of pair p is pos * freq[p]
 // (YaRN folded into freq on the host), reduced by 2 pi in double before the sine and cosine.
+// With QK-norm weights (q_norm, k_norm [D]; moe.rs:1961-1985) each q and k head is first
+// RMS-normalised over its D values and scaled by them.
 __global__ void k_bd_rope_kv(const float *qkv, int nq, int nkv, int D, const double *freq, double mscale,
                              const int *pos, const unsigned *tables, int table_stride, float *q, uint16_t *kpool,
-                             uint16_t *vpool) {
+                             uint16_t *vpool, const float *q_norm, const float *k_norm, float eps) {
+    __shared__ float red[32];
     const int head = blockIdx.x, b = blockIdx.y, p = threadIdx.x, half = D / 2;
     const int n_qkv = (nq + 2 * nkv) * D;
     const float *row = qkv + (size_t)b * n_qkv + (size_t)head * D;
     const int ps = pos[b];
     const unsigned page = tables[(size_t)b * table_stride + ps / BD_PAGE];
     const size_t slot = (size_t)page * BD_PAGE + ps % BD_PAGE;
+    float a0 = row[p], a1 = row[p + half];
+    if (head < nq + nkv && q_norm) {
+        float ss = warp_sum(fmaf(a0, a0, a1 * a1));
+        if ((p & 31) == 0) red[p >> 5] = ss;
+        __syncthreads();
+        ss = 0.f;
+        for (int w = 0; w < (int)(blockDim.x >> 5); ++w) ss += red[w];
+        const float sc = 1.0f / sqrtf(ss / (float)D + eps);
+        const float *w = head < nq ? q_norm : k_norm;
+        a0 = (a0 * sc) * w[p];
+        a1 = (a1 * sc) * w[p + half];
+    }
     if (head < nq + nkv) {
         const double th = (double)ps * freq[p];
         const double k = rint(th * 0.15915494309189535);
@@ -87,7 +102,7 @@ __global__ void k_bd_rope_kv(const float *qkv, int nq, int nkv, int D, const dou
         sincos(r, &sn, &cs);
         cs *= mscale;
         sn *= mscale;
-        const double x0 = row[p], x1 = row[p + half];
+        const double x0 = a0, x1 = a1;
         const float y0 = (float)(x0 * cs - x1 * sn), y1 = (float)(x0 * sn + x1 * cs);
         if (head < nq) {
             q[((size_t)b * nq + head) * D + p] = y0;
@@ -99,8 +114,8 @@ __global__ void k_bd_rope_kv(const float *qkv, int nq, int nkv, int D, const dou
         }
     } else {
         uint16_t *dst = vpool + (slot * nkv + (head - nq - nkv)) * D;
-        dst[p] = bf16_rn(row[p]);
-        dst[p + half] = bf16_rn(row[p + half]);
+        dst[p] = bf16_rn(a0);
+        dst[p + half] = bf16_rn(a1);
     }
 }
 
@@ -141,6 +156,7 @@ struct moearc_x_batch_decoder {
     int B, Dq, Dkv, n_qkv, pages, max_splits;
     struct layer {
         float *attn_norm, *ffn_norm, *router;
+        float *q_norm, *k_norm;  // QK-norm weights [head_dim] or null
         uint16_t *wqkv, *wo;
         CUtensorMap map_qkv, map_o;
         uint16_t *k_pages, *v_pages;
@@ -190,7 +206,7 @@ int enqueue(moearc_x_batch_decoder *d) {
         if (rc) return rc;
         k_bd_rope_kv<<<dim3((unsigned)(g.n_head + 2 * g.n_head_kv), (unsigned)B), (unsigned)(D / 2), 0, st>>>(
             d->qkv, (int)g.n_head, (int)g.n_head_kv, D, d->rope_freq, d->rope_mscale, d->dpos, d->tables, d->pages,
-            d->q, b.k_pages, b.v_pages);
+            d->q, b.k_pages, b.v_pages, b.q_norm, b.k_norm, g.rms_eps);
         rc = attn_launch_batched(c, d->att, d->q, b.k_pages, b.v_pages, d->tables, (size_t)d->pages, nullptr,
                                  g.n_head, g.n_head_kv, D, g.n_ctx, BD_PAGE, scale, d->attn_scratch,
                                  d->attn_scratch_b, d->dpos, 0, d->max_splits, d->attn_ctr, B);
@@ -218,7 +234,7 @@ moearc_x_batch_decoder *moearc_x_batch_decoder_create(moearc_ctx *c, const moear
     if (!c || !cfg || n_batch == 0 || n_batch > 128) return nullptr;
     const auto &g = *cfg;
     if (g.n_layer == 0 || g.n_head_kv == 0 || g.n_head % g.n_head_kv || (g.head_dim != 64 && g.head_dim != 128) ||
-        g.n_head / g.n_head_kv > 8 || g.n_ctx == 0 || g.n_swa != 0 || g.has_sinks || g.n_offload)
+        g.n_head / g.n_head_kv > 8 || g.n_ctx == 0 || g.n_swa != 0 || g.has_sinks || g.n_offload || g.n_vocab)
         return nullptr;
     if (g.n_embd % 64 || ((g.n_head * g.head_dim) % 64)) return nullptr;
     auto *d = new moearc_x_batch_decoder();
@@ -330,6 +346,8 @@ moearc_x_batch_decoder *moearc_x_batch_decoder_create(moearc_ctx *c, const moear
         b.attn_norm = static_cast<float *>(d->alloc(sizeof(float) * H));
         b.ffn_norm = static_cast<float *>(d->alloc(sizeof(float) * H));
         b.router = static_cast<float *>(d->alloc(sizeof(float) * g.n_expert * H));
+        b.q_norm = g.has_qk_norm ? static_cast<float *>(d->alloc(sizeof(float) * g.head_dim)) : nullptr;
+        b.k_norm = g.has_qk_norm ? static_cast<float *>(d->alloc(sizeof(float) * g.head_dim)) : nullptr;
         b.wqkv = static_cast<uint16_t *>(d->alloc(2 * (size_t)d->n_qkv * H));
         b.wo = static_cast<uint16_t *>(d->alloc(2 * (size_t)H * d->Dq));
         b.k_pages = static_cast<uint16_t *>(d->alloc(2 * pool));
@@ -342,6 +360,11 @@ moearc_x_batch_decoder *moearc_x_batch_decoder_create(moearc_ctx *c, const moear
         ok &= moearc_x_synth(c, b.attn_norm, H, 4, seed(0, l), 0.1f, 0, 0) == OK;
         ok &= moearc_x_synth(c, b.ffn_norm, H, 4, seed(1, l), 0.1f, 0, 0) == OK;
         ok &= moearc_x_synth(c, b.router, (size_t)g.n_expert * H, 0, seed(7, l), 0.02f, 0, 0) == OK;
+        if (g.has_qk_norm) {
+            ok &= b.q_norm && b.k_norm;
+            ok &= ok && moearc_x_synth(c, b.q_norm, g.head_dim, 4, seed(14, l), 0.1f, 0, 0) == OK;
+            ok &= ok && moearc_x_synth(c, b.k_norm, g.head_dim, 4, seed(15, l), 0.1f, 0, 0) == OK;
+        }
         ok &= moearc_x_synth(c, b.wqkv, (size_t)d->Dq * H, 1, seed(2, l), 0.02f, 0, 0) == OK;
         ok &= moearc_x_synth(c, b.wqkv + (size_t)d->Dq * H, (size_t)d->Dkv * H, 1, seed(3, l), 0.02f, 0, 0) == OK;
         ok &= moearc_x_synth(c, b.wqkv + (size_t)(d->Dq + d->Dkv) * H, (size_t)d->Dkv * H, 1, seed(4, l), 0.02f, 0, 0) == OK;

@@ -274,6 +274,34 @@ struct moe_offload {
     unsigned long long *fetched = nullptr;
     const int *clock = nullptr;  // device position, advanced once a step: the cache's clock
     int n_cache = 0;
+    const struct moe_host *host = nullptr;  // part of the block's experts on the host cores, or null
+};
+
+// Host execution of part of an offloaded block's experts, beside the device (moe.rs:2169-2211,
+// 2389-2420), through a mailbox in pinned, device-mapped host memory. After the router a
+// one-warp kernel splits the token's choices by the policy, leaves the device's mask in `hmask`,
+// writes the host's share (block, experts, weights, the routed activation) into the mail and
+// then, last, the next sequence number; a host thread polling the mail runs the pool on it and
+// writes the result and the same number into `done`. The main stream meanwhile runs the
+// device's share into `ffn`; the fold kernel waits (bounded) for `done` to show the number and
+// adds h + (ffn + host share).
+// Mail layout (bytes): [0] u64 sequence, [8] u32 experts n, [12] u32 block, [16] u32 experts[32],
+// [144] f32 weights[32], [512] f32 x[n_embd]. Done layout: [0] u64 sequence, [64] f32 out[n_embd].
+constexpr int MAIL_SEQ = 0, MAIL_N = 8, MAIL_BLOCK = 12, MAIL_IDS = 16, MAIL_WTS = 144, MAIL_X = 512;
+constexpr int DONE_SEQ = 0, DONE_OUT = 64;
+
+struct moe_host {
+    int kind = 0;  // 0 off, 1 a fraction of the misses (rounded up), 2 the misses beyond `over`
+    float frac = 0.f;
+    int over = 0;
+    int block = 0;                          // the block's index, for the host thread
+    unsigned *hmask = nullptr;              // device word: the choices the host takes
+    unsigned long long *seq = nullptr;      // device counter: the last sequence number issued
+    uint8_t *mail = nullptr;                // device pointer of the pinned mail
+    const uint8_t *done = nullptr;          // device pointer of the pinned done record
+    float *ffn = nullptr;                   // device [n_embd]: the device's share
+    unsigned long long wait_ns = 0;         // the fold's wait limit
+    int *status = nullptr;                  // raised when the wait runs out
 };
 
 template <typename... KArgs, typename... Args>

@@ -18,16 +18,28 @@
 // Blocks below cfg.n_offload keep their packed expert banks in pinned, device-mapped host memory
 // (the -ncmoe mirror, moe.rs:1179-1299 StaticSplit with every expert of the block streamed);
 // their MoE adds two fetch kernels that copy the routed experts over PCIe into device slots, so
-// the step stays one graph with no host round trip.
+// the step stays one graph with no host round trip. With a host policy
+// (moearc_x_decoder_host_experts) part of those experts is computed by a pool of host threads
+// from the same pinned banks while the device streams the rest (moe.rs:2169-2211, 2389-2420):
+// the split and the answer pass through a mailbox in pinned memory that a host thread polls, so
+// the step stays one graph with no host function in it.
 #include <algorithm>
+#include <atomic>
+#include <chrono>
 #include <cmath>
 #include <climits>
 #include <cstdlib>
+#include <cstring>
+#include <thread>
 #include <vector>
+
+#include <unistd.h>
 
 #include "common.cuh"
 #include "dense.cuh"
+#include "host_experts.hpp"
 #include "step.cuh"
+#include "tma.cuh"
 
 namespace moearc {
 int moe_forward_impl(moearc_x_moe *m, const float *x, unsigned n_tokens, const float *norm_w, float eps,
@@ -83,6 +95,7 @@ struct moearc_x_decoder {
     int Dq, Dkv, n_qkv;
     struct layer {
         float *attn_norm, *ffn_norm, *sinks, *router;
+        float *q_norm, *k_norm;           // QK-norm weights [head_dim] (has_qk_norm) or null
         void *wqkv, *wo, *gateup, *down;  // gateup/down: device-visible host banks when offloaded
         void *gu_host, *dn_host;           // pinned host allocations of an offloaded block
         moe_offload off;                   // an offloaded block's own residency cache (n_cache)
@@ -94,6 +107,9 @@ struct moearc_x_decoder {
     std::vector<layer> L;
     float *output_norm = nullptr;
     dense_gemv *qkv = nullptr, *wo = nullptr;
+    dense_gemv *head = nullptr;  // the output head (n_vocab rows), or null
+    void *w_out = nullptr;       // its packed bf16 weights
+    float *logits = nullptr;     // [n_vocab]
     moearc_x_moe *moe = nullptr;
     int *dpos = nullptr;
     unsigned *table_full = nullptr, *table_swa = nullptr;
@@ -119,6 +135,64 @@ struct moearc_x_decoder {
     // the chain's expert kernels' CTA timestamps per block (moearc_x_decoder_kernel_spans), or null
     unsigned long long *spans = nullptr;
     int span_cta = 0;
+    // host execution of part of the offloaded blocks' experts (moearc_x_decoder_host_experts):
+    // the pool, the per-block split records, the pinned mail and done records (host pointers),
+    // and the thread that polls the mail
+    host_pool *pool = nullptr;
+    std::vector<moe_host> hosts;  // per offloaded block (kind 0: off)
+    uint8_t *mail = nullptr, *done = nullptr;
+    unsigned *hmask = nullptr;
+    unsigned long long *hseq = nullptr;
+    float *hffn = nullptr;
+    int *hstatus = nullptr;
+    std::thread poller;
+    std::atomic<bool> poll_stop{false}, poll_hold{false};
+    std::atomic<int> host_failed{0};
+    host_shape hshape{};
+
+    // The host side of the mailbox: a new sequence number in the mail is a job; its answer (the
+    // host's share, then the same number) goes to the done record. Polls continuously while
+    // jobs come; after 20 ms without one it naps 50 us between polls.
+    void poll_mail() {
+        const auto *seqp = reinterpret_cast<const std::atomic<unsigned long long> *>(mail + MAIL_SEQ);
+        auto *donep = reinterpret_cast<std::atomic<unsigned long long> *>(done + DONE_SEQ);
+        unsigned long long last = seqp->load(std::memory_order_acquire);
+        auto idle0 = std::chrono::steady_clock::now();
+        while (!poll_stop.load(std::memory_order_relaxed)) {
+            const unsigned long long sq = seqp->load(std::memory_order_acquire);
+            if (sq == last || poll_hold.load(std::memory_order_relaxed)) {
+                if (std::chrono::steady_clock::now() - idle0 > std::chrono::milliseconds(20))
+                    std::this_thread::sleep_for(std::chrono::microseconds(50));
+                else
+                    __builtin_ia32_pause();
+                continue;
+            }
+            last = sq;
+            unsigned n, blk;
+            std::memcpy(&n, mail + MAIL_N, 4);
+            std::memcpy(&blk, mail + MAIL_BLOCK, 4);
+            float *out = reinterpret_cast<float *>(done + DONE_OUT);
+            if (n == 0 || n > 32 || blk >= cfg.n_offload ||
+                host_submit(pool, hshape, static_cast<const uint8_t *>(L[blk].gu_host),
+                            static_cast<const uint8_t *>(L[blk].dn_host),
+                            reinterpret_cast<const unsigned *>(mail + MAIL_IDS),
+                            reinterpret_cast<const float *>(mail + MAIL_WTS), n,
+                            reinterpret_cast<const float *>(mail + MAIL_X)) != 0 ||
+                host_sync(pool, out) != 0) {
+                for (unsigned i = 0; i < cfg.n_embd; ++i) out[i] = NAN;
+                host_failed.store(1);
+            }
+            donep->store(sq, std::memory_order_release);
+            idle0 = std::chrono::steady_clock::now();
+        }
+    }
+
+    void stop_poller() {
+        if (poller.joinable()) {
+            poll_stop.store(true);
+            poller.join();
+        }
+    }
 
     void drop_graph() {
         if (exec) cudaGraphExecDestroy(exec);
@@ -163,7 +237,12 @@ struct step_marks {
 int enqueue_step(moearc_x_decoder *d, step_marks *pm = nullptr) {
     moearc_ctx *c = d->c;
     const auto &cfg = d->cfg;
-    if (d->step && d->use_step && !pm) return step_run(d->step, d->in, d->out, d->output_norm, d->dpos);
+    if (d->step && d->use_step && !pm) {
+        int rc = step_run(d->step, d->in, d->out, d->output_norm, d->dpos);
+        if (rc == OK && d->head)
+            rc = dense_run(d->head, d->w_out, d->out, nullptr, 0.f, d->logits, nullptr, d->dpos, nullptr, nullptr);
+        return rc;
+    }
     if (cudaMemcpyAsync(d->h, d->in, sizeof(float) * cfg.n_embd, cudaMemcpyDeviceToDevice, c->stream) != cudaSuccess)
         return ERR;
     if (pm) pm->mark(c->stream, -1);
@@ -177,6 +256,9 @@ int enqueue_step(moearc_x_decoder *d, step_marks *pm = nullptr) {
     for (unsigned l = 0; l < cfg.n_layer; ++l) {
         auto &b = d->L[l];
         dense_kv kv{b.k_pages, b.v_pages, b.table, PAGE_TOKENS};
+        rope.q_norm = b.q_norm;
+        rope.k_norm = b.k_norm;
+        rope.norm_eps = cfg.rms_eps;
         int rc = dense_run(d->qkv, b.wqkv, d->h, b.attn_norm, cfg.rms_eps, d->q, nullptr, d->dpos, &rope, &kv);
         if (rc) return rc;
         if (pm) pm->mark(c->stream, 0);
@@ -188,15 +270,25 @@ int enqueue_step(moearc_x_decoder *d, step_marks *pm = nullptr) {
         rc = dense_run(d->wo, b.wo, d->att, nullptr, 0.f, d->h, d->h, d->dpos, nullptr, nullptr);
         if (rc) return rc;
         if (pm) pm->mark(c->stream, 2);
+        moe_offload off{};
+        if (l < cfg.n_offload) {
+            off = cfg.n_cache ? b.off : d->off;
+            off.host = l < d->hosts.size() && d->hosts[l].kind ? &d->hosts[l] : nullptr;
+        }
         rc = moe_forward_impl(d->moe, d->h, 1, b.ffn_norm, cfg.rms_eps, b.router, nullptr, b.gateup, b.down,
                               d->h, d->h, pm ? &pm->ev : nullptr, pm ? &pm->kind : nullptr,
-                              l < cfg.n_offload ? (cfg.n_cache ? &b.off : &d->off) : nullptr,
+                              l < cfg.n_offload ? &off : nullptr,
                               d->spans ? d->spans + (size_t)l * 2 * d->span_cta * 3 : nullptr);
         if (rc) return rc;
     }
     if (launch_pdl(k_step_end, dim3(1), dim3(512), 0, c->stream, d->out, (const float *)d->h,
                    (const float *)d->output_norm, (int)cfg.n_embd, cfg.rms_eps, d->dpos) != cudaSuccess)
         return ERR;
+    if (d->head) {
+        // the output head on the normalised final state (moe.rs:2434-2437)
+        const int rc = dense_run(d->head, d->w_out, d->out, nullptr, 0.f, d->logits, nullptr, d->dpos, nullptr, nullptr);
+        if (rc) return rc;
+    }
     if (pm) pm->mark(c->stream, 6);
     return cudaGetLastError() == cudaSuccess ? OK : ERR;
 }
@@ -216,6 +308,7 @@ moearc_x_decoder *moearc_x_decoder_create(moearc_ctx *c, const moearc_x_decoder_
         return nullptr;
     if (g.n_head / g.n_head_kv > 8 || g.n_ctx == 0 || g.n_offload > g.n_layer) return nullptr;
     if (g.n_cache && (g.n_cache < g.n_expert_used || g.n_cache > g.n_expert || !g.n_offload)) return nullptr;
+    if (g.n_vocab % 16) return nullptr;
     auto *d = new moearc_x_decoder();
     d->c = c;
     d->cfg = g;
@@ -236,6 +329,12 @@ moearc_x_decoder *moearc_x_decoder_create(moearc_ctx *c, const moearc_x_decoder_
     d->qkv = dense_create(c, d->n_qkv, H, 0);
     d->wo = dense_create(c, H, d->Dq, 1);
     if (!d->moe || !d->qkv || !d->wo) return fail();
+    if (g.n_vocab) {
+        d->head = dense_create(c, (int)g.n_vocab, H, 1);
+        d->w_out = d->alloc((size_t)g.n_vocab * H * 2);
+        d->logits = static_cast<float *>(d->alloc(sizeof(float) * g.n_vocab));
+        if (!d->head || !d->w_out || !d->logits) return fail();
+    }
 
     // page tables: the sequence's (a seeded permutation, so pages are scattered as a pool that
     // has served other sequences would hand them out) and the windowed blocks' ring
@@ -300,7 +399,7 @@ moearc_x_decoder *moearc_x_decoder_create(moearc_ctx *c, const moearc_x_decoder_
     const size_t blocks = (size_t)g.n_expert * g.n_ff * g.n_embd / 32;
     const size_t bank_bytes = blocks * bb;
     const size_t qkv_elems = (size_t)d->n_qkv * H, wo_elems = (size_t)H * d->Dq;
-    const size_t stage_bytes = std::max({3 * bank_bytes, qkv_elems * 2, wo_elems * 2});
+    const size_t stage_bytes = std::max({3 * bank_bytes, qkv_elems * 2, wo_elems * 2, (size_t)g.n_vocab * H * 2});
     void *staging = nullptr;
     if (cudaMalloc(&staging, stage_bytes) != cudaSuccess) {
         cudaGetLastError();
@@ -360,6 +459,8 @@ moearc_x_decoder *moearc_x_decoder_create(moearc_ctx *c, const moearc_x_decoder_
         b.attn_norm = static_cast<float *>(d->alloc(sizeof(float) * H));
         b.ffn_norm = static_cast<float *>(d->alloc(sizeof(float) * H));
         b.sinks = g.has_sinks ? static_cast<float *>(d->alloc(sizeof(float) * g.n_head)) : nullptr;
+        b.q_norm = g.has_qk_norm ? static_cast<float *>(d->alloc(sizeof(float) * g.head_dim)) : nullptr;
+        b.k_norm = g.has_qk_norm ? static_cast<float *>(d->alloc(sizeof(float) * g.head_dim)) : nullptr;
         b.router = static_cast<float *>(d->alloc(sizeof(float) * g.n_expert * H));
         b.wqkv = d->alloc(qkv_elems * 2);
         b.wo = d->alloc(wo_elems * 2);
@@ -382,6 +483,11 @@ moearc_x_decoder *moearc_x_decoder_create(moearc_ctx *c, const moearc_x_decoder_
         ok &= synth(c, b.attn_norm, H, 4, tensor_seed(g.seed, 0, l), 0.1f) == OK;
         ok &= synth(c, b.ffn_norm, H, 4, tensor_seed(g.seed, 1, l), 0.1f) == OK;
         if (b.sinks) ok &= synth(c, b.sinks, g.n_head, 0, tensor_seed(g.seed, 6, l), 1.0f) == OK;
+        if (g.has_qk_norm) {
+            ok &= b.q_norm && b.k_norm;
+            ok &= ok && synth(c, b.q_norm, g.head_dim, 4, tensor_seed(g.seed, 14, l), 0.1f) == OK;
+            ok &= ok && synth(c, b.k_norm, g.head_dim, 4, tensor_seed(g.seed, 15, l), 0.1f) == OK;
+        }
         ok &= synth(c, b.router, (size_t)g.n_expert * H, 0, tensor_seed(g.seed, 7, l), 0.02f) == OK;
         // Q, K, V rows concatenated into one [Dq + 2 Dkv] x H matrix
         uint16_t *s16 = static_cast<uint16_t *>(staging);
@@ -416,11 +522,15 @@ moearc_x_decoder *moearc_x_decoder_create(moearc_ctx *c, const moearc_x_decoder_
         ok &= cudaMemsetAsync(b.k_pages, 0, b.pool_tokens * d->Dkv * 2, c->stream) == cudaSuccess;
         ok &= cudaMemsetAsync(b.v_pages, 0, b.pool_tokens * d->Dkv * 2, c->stream) == cudaSuccess;
     }
+    if (g.n_vocab && ok) {
+        ok &= synth(c, staging, (size_t)g.n_vocab * H, 1, tensor_seed(g.seed, 16, 0), 0.02f) == OK;
+        ok &= dense_pack(c, d->w_out, staging, (int)g.n_vocab, H) == OK;
+    }
     ok &= cudaStreamSynchronize(c->stream) == cudaSuccess;
     cudaFree(staging);
     if (pack_tmp) cudaFree(pack_tmp);
     if (!ok) return fail();
-    if (!g.n_offload) {
+    if (!g.n_offload && !g.has_qk_norm) {
         std::vector<step_layer> sl(g.n_layer);
         for (unsigned l = 0; l < g.n_layer; ++l) {
             const auto &b = d->L[l];
@@ -447,9 +557,14 @@ void moearc_x_decoder_destroy(moearc_x_decoder *d) {
     d->drop_graph();
     step_destroy(d->step);
     if (d->spans) cudaFree(d->spans);
+    d->stop_poller();
+    if (d->mail) cudaFreeHost(d->mail);
+    if (d->done) cudaFreeHost(d->done);
+    host_pool_destroy(d->pool);
     if (d->moe) moearc_x_moe_destroy(d->moe);
     if (d->qkv) dense_destroy(d->qkv);
     if (d->wo) dense_destroy(d->wo);
+    if (d->head) dense_destroy(d->head);
     for (void *p : d->allocs) cudaFree(p);
     for (void *p : d->host_allocs) cudaFreeHost(p);
     delete d;
@@ -457,6 +572,7 @@ void moearc_x_decoder_destroy(moearc_x_decoder *d) {
 
 void *moearc_x_decoder_input(moearc_x_decoder *d) { return d ? d->in : nullptr; }
 void *moearc_x_decoder_output(moearc_x_decoder *d) { return d ? d->out : nullptr; }
+void *moearc_x_decoder_logits(moearc_x_decoder *d) { return d ? d->logits : nullptr; }
 
 int moearc_x_decoder_pos(moearc_x_decoder *d) { return d ? d->pos : -1; }
 
@@ -494,9 +610,119 @@ unsigned long long moearc_x_decoder_fetched(moearc_x_decoder *d) {
 int moearc_x_decoder_status(moearc_x_decoder *d) {
     if (!d) return ERR;
     const int sm = moearc_x_moe_status(d->moe), sq = dense_status(d->qkv), so = dense_status(d->wo);
+    const int sd = d->head ? dense_status(d->head) : 0;
+    if (sd < 0) return ERR;
     const int st = d->step ? step_status(d->step) : 0;
     if (sm < 0 || sq < 0 || so < 0 || st < 0) return ERR;
-    return sm | sq | so | st;
+    // a host job the pool refused (the block's output was then NaN), or a fold that gave up
+    // waiting for the host's answer
+    int sh = d->host_failed.exchange(0) ? STATUS_RANGE : 0;
+    if (d->hstatus) {
+        int v = 0;
+        if (cudaMemcpy(&v, d->hstatus, sizeof(int), cudaMemcpyDeviceToHost) != cudaSuccess ||
+            cudaMemset(d->hstatus, 0, sizeof(int)) != cudaSuccess)
+            return ERR;
+        sh |= v;
+    }
+    return sm | sq | so | st | sh | sd;
+}
+
+int moearc_x_decoder_host_experts(moearc_x_decoder *d, int kind, float fraction, unsigned over, int n_threads) {
+    if (!d) return ERR;
+    const auto &g = d->cfg;
+    if (kind < 0 || kind > 2 || !g.n_offload || (kind == 1 && !(fraction >= 0.f))) return ERR_ARG;
+    if (cudaStreamSynchronize(d->c->stream) != cudaSuccess) return ERR;
+    d->drop_graph();
+    if (kind == 0) {
+        for (auto &h : d->hosts) h.kind = 0;
+        return OK;
+    }
+    if (d->pool && n_threads > 0 && host_pool_threads(d->pool) != n_threads) {
+        d->stop_poller();
+        host_pool_destroy(d->pool);
+        d->pool = nullptr;
+    }
+    if (n_threads <= 0 && !std::getenv("MOEARC_HOST_THREADS")) {
+        // the online cores less two: one for the thread polling the mail (which works in every
+        // job too) and one for the thread driving the device
+        const long nc = sysconf(_SC_NPROCESSORS_ONLN);
+        n_threads = nc > 3 ? (int)(nc - 2) : 1;
+    }
+    if (!d->pool && !(d->pool = host_pool_create(n_threads))) return ERR;
+    if (!d->mail) {
+        // one mailbox for every block: a block's job is answered before the next block posts
+        const size_t mail_bytes = MAIL_X + sizeof(float) * g.n_embd, done_bytes = DONE_OUT + sizeof(float) * g.n_embd;
+        void *m = nullptr, *dn = nullptr;
+        if (cudaHostAlloc(&m, mail_bytes, cudaHostAllocMapped | cudaHostAllocPortable) != cudaSuccess) m = nullptr;
+        if (m && cudaHostAlloc(&dn, done_bytes, cudaHostAllocMapped | cudaHostAllocPortable) != cudaSuccess) dn = nullptr;
+        if (!m || !dn) {
+            cudaGetLastError();
+            if (m) cudaFreeHost(m);
+            return ERR;
+        }
+        std::memset(m, 0, mail_bytes);
+        std::memset(dn, 0, done_bytes);
+        d->mail = static_cast<uint8_t *>(m);
+        d->done = static_cast<uint8_t *>(dn);
+        d->hmask = static_cast<unsigned *>(d->alloc(sizeof(unsigned) * g.n_offload));
+        d->hseq = static_cast<unsigned long long *>(d->alloc(sizeof(unsigned long long)));
+        d->hffn = static_cast<float *>(d->alloc(sizeof(float) * g.n_embd));
+        d->hstatus = static_cast<int *>(d->alloc(sizeof(int)));
+        void *mail_dev = nullptr, *done_dev = nullptr;
+        if (!d->hmask || !d->hseq || !d->hffn || !d->hstatus ||
+            cudaMemset(d->hmask, 0, sizeof(unsigned) * g.n_offload) != cudaSuccess ||
+            cudaMemset(d->hseq, 0, sizeof(unsigned long long)) != cudaSuccess ||
+            cudaMemset(d->hstatus, 0, sizeof(int)) != cudaSuccess ||
+            cudaHostGetDevicePointer(&mail_dev, d->mail, 0) != cudaSuccess ||
+            cudaHostGetDevicePointer(&done_dev, d->done, 0) != cudaSuccess) {
+            cudaGetLastError();
+            return ERR;
+        }
+        d->hosts.assign(g.n_offload, moe_host{});
+        for (unsigned l = 0; l < g.n_offload; ++l) {
+            moe_host &h = d->hosts[l];
+            h.block = (int)l;
+            h.hmask = d->hmask + l;
+            h.seq = d->hseq;
+            h.mail = static_cast<uint8_t *>(mail_dev);
+            h.done = static_cast<const uint8_t *>(done_dev);
+            h.ffn = d->hffn;
+            h.wait_ns = 2000000000ull;
+            h.status = d->hstatus;
+        }
+    }
+    d->hshape = host_shape{(int)g.n_embd, (int)g.n_ff, (int)g.expert_type, (int)g.act, g.alpha, g.limit};
+    for (auto &h : d->hosts) {
+        h.kind = kind;
+        h.frac = fraction;
+        h.over = (int)std::min(over, 64u);
+    }
+    if (!d->poller.joinable()) {
+        d->poll_stop.store(false);
+        try {
+            d->poller = std::thread([d] { d->poll_mail(); });
+        } catch (...) {
+            for (auto &h : d->hosts) h.kind = 0;
+            return ERR;
+        }
+    }
+    return OK;
+}
+
+int moearc_x_decoder_host_wait(moearc_x_decoder *d, unsigned long long limit_ns, int hold) {
+    if (!d || d->hosts.empty()) return ERR;
+    if (cudaStreamSynchronize(d->c->stream) != cudaSuccess) return ERR;
+    for (auto &h : d->hosts) h.wait_ns = limit_ns ? limit_ns : 2000000000ull;
+    d->poll_hold.store(hold != 0);
+    d->drop_graph();
+    return OK;
+}
+
+int moearc_x_decoder_host_stats(moearc_x_decoder *d, unsigned long long *out4) {
+    if (!d || !out4) return ERR;
+    if (cudaStreamSynchronize(d->c->stream) != cudaSuccess) return ERR;
+    host_stats(d->pool, out4);
+    return OK;
 }
 
 int moearc_x_decoder_uses_step_kernel(moearc_x_decoder *d) { return d && d->step && d->use_step ? 1 : 0; }
@@ -512,9 +738,10 @@ int moearc_x_decoder_use_step_kernel(moearc_x_decoder *d, int on) {
 }
 
 int moearc_x_decoder_set_wait(moearc_x_decoder *d, unsigned long long limit_ns, unsigned int phantom) {
-    if (!d || !d->step) return ERR;
+    if (!d) return ERR;
     if (cudaStreamSynchronize(d->c->stream) != cudaSuccess) return ERR;
-    step_set_wait(d->step, limit_ns, phantom);
+    if (d->step) step_set_wait(d->step, limit_ns, phantom);
+    moearc_x_moe_set_wait(d->moe, limit_ns, phantom ? 1 : 0);
     d->drop_graph();
     return OK;
 }
@@ -620,10 +847,10 @@ int moearc_x_decoder_profile(moearc_x_decoder *d, float *ms, int *counts, int n)
 // 3 router, 4 K pool, 5 V pool, 6 page table, 7 packed Q/K/V, 8 packed O, 9 packed gate-up,
 // 10 packed down; 11 output norm (layer ignored); 12/13 the step kernel's expert ids and gating
 // weights of the last step; 14 the chain's expert-kernel spans of the last step (u64
-// [2 kernels][CTA][start, wait over, end] in ns, while kernel spans are on). `bytes` receives
-// the size.
+// [2 kernels][CTA][start, wait over, end] in ns, while kernel spans are on); 15/16 the QK-norm
+// weights; 17 the packed output head (layer ignored). `bytes` receives the size.
 void *moearc_x_decoder_tensor(moearc_x_decoder *d, int which, unsigned layer, unsigned long *bytes) {
-    if (!d || (which != 11 && layer >= d->cfg.n_layer)) return nullptr;
+    if (!d || (which != 11 && which != 17 && layer >= d->cfg.n_layer)) return nullptr;
     const auto &g = d->cfg;
     const size_t H = g.n_embd;
     const size_t bb = (g.expert_type == T_MXFP4) ? 17 : 18;
@@ -633,6 +860,9 @@ void *moearc_x_decoder_tensor(moearc_x_decoder *d, int which, unsigned layer, un
     if (which == 11) {
         p = d->output_norm;
         n = H * 4;
+    } else if (which == 17) {
+        p = d->w_out;
+        n = p ? (unsigned long)g.n_vocab * H * 2 : 0;
     } else {
         auto &b = d->L[layer];
         switch (which) {
@@ -653,6 +883,8 @@ void *moearc_x_decoder_tensor(moearc_x_decoder *d, int which, unsigned layer, un
                  n = p ? g.n_expert_used * 4 : 0; break;
         case 14: p = d->spans ? d->spans + (size_t)layer * 2 * d->span_cta * 3 : nullptr;
                  n = p ? (unsigned long)2 * d->span_cta * 3 * 8 : 0; break;
+        case 15: p = b.q_norm; n = p ? g.head_dim * 4 : 0; break;
+        case 16: p = b.k_norm; n = p ? g.head_dim * 4 : 0; break;
         default: return nullptr;
         }
     }
@@ -662,7 +894,8 @@ void *moearc_x_decoder_tensor(moearc_x_decoder *d, int which, unsigned layer, un
 
 // The seed the decoder generated tensor `kind` of block `layer` from (kinds: 0 attn_norm,
 // 1 ffn_norm, 2 wq, 3 wk, 4 wv, 5 wo, 6 sinks, 7 router, 8 gate, 9 up, 10 down,
-// 11 output_norm, 12/13 K/V fill), so a checker can regenerate the GGUF-layout tensors.
+// 11 output_norm, 12/13 K/V fill, 14/15 QK-norm q/k, 16 output head), so a checker can
+// regenerate the GGUF-layout tensors.
 unsigned long long moearc_x_decoder_seed(moearc_x_decoder *d, int kind, unsigned layer, unsigned long long base) {
     (void)d;
     return tensor_seed(base, kind, (int)layer);

@@ -334,6 +334,20 @@ __global__ void __launch_bounds__(WARPS * 32, 1) k_dense(dense_args a) {
 #pragma unroll
     for (int i = 0; i < 4; ++i) v[i] = (i < per) ? row_value(row0 + lane + 32 * i) : 0.f;
     const int hq = a.rope.n_q_heads, hk = a.rope.n_kv_heads;
+    if (unit < hq + hk && a.rope.q_norm) {
+        // QK-norm: the head's mean square over its D values (a fixed butterfly), then the
+        // reference's (x * scale) * w
+        const float *w = unit < hq ? a.rope.q_norm : a.rope.k_norm;
+        float ss = 0.f;
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+            if (i < per) ss = fmaf(v[i], v[i], ss);
+        ss = warp_sum(ss);
+        const float sc = 1.0f / sqrtf(ss / (float)D + a.rope.norm_eps);
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+            if (i < per) v[i] = (v[i] * sc) * __ldg(w + lane + 32 * i);
+    }
     if (unit < hq + hk) {
         // the rotations computed before the wait
         if (per == 2) {

@@ -37,6 +37,10 @@ struct dense_rope {
     int n_q_heads, n_kv_heads, head_dim;
     const double *freq;
     double mscale;
+    // QK-norm before the rotation (moe.rs:1961-1985): each q and k head RMS-normalised over its
+    // head_dim values and scaled by q_norm / k_norm [head_dim] (both null: none)
+    const float *q_norm = nullptr, *k_norm = nullptr;
+    float norm_eps = 0.f;
 };
 
 struct dense_kv {

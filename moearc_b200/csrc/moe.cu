@@ -57,6 +57,9 @@ struct moearc_x_moe {
     bool xpath;
     int x_grid, x_warps, x_route_grid, x_route_smem, x_ch_gu, x_ch_dn, x_stage_gu, x_stage_dn, x_ntok;
     float *x_part_gu, *x_part_dn;  // expert kernels' piece partials (PART_EMPTY when idle)
+    unsigned long long x_poll_ns = XPOLL_NS;  // their wait for one another's partials
+    const float *bias_gu = nullptr, *bias_dn = nullptr;  // moearc_x_moe_set_bias
+    int x_phantom = 0;                        // testing: every such wait runs out
     size_t x_part_gu_n, x_part_dn_n;
     float *f_part_gu, *f_part_dn;  // the opt-in fused kernels' (arrival counters instead)
     void *x_tab_pub;               // the gate-up kernel's routing tables, read by the down kernel
@@ -476,6 +479,10 @@ struct rows_args {
     const float *residual;    // [T][H] or null
     float *out;               // [T][H]
     int T, K, H;
+    // per-expert biases (moe.rs:2310-2331, 2362-2372) or null: gate rows of expert e at e, up
+    // rows at E + e ([2E][I]); down [E][H]
+    const float *bias_gu, *bias_dn;
+    int E;
     int *status;
 };
 
@@ -673,6 +680,12 @@ __global__ void __launch_bounds__(256) k_moe_rows(rows_args a) {
                     us += part[((size_t)rg * 2 + 1) * 16 * GROUP + rr * GROUP + t];
                 }
                 const int col = col0 + t, row = tr * 16 + rr;
+                if (a.bias_gu) {
+                    // ggml_add_id right after each expert matvec, before the activation
+                    const int ex = tb.slot_expert()[tb.grp_slot()[g]];
+                    gs += a.bias_gu[(size_t)ex * a.I + row];
+                    us += a.bias_gu[(size_t)(a.E + ex) * a.I + row];
+                }
                 const float v = act_fn(a.act, gs, us, a.alpha, a.limit);
                 a.act_out[(size_t)col * a.I + row] = v;
                 const __half hh = __float2half_rn(v);
@@ -695,6 +708,8 @@ __global__ void __launch_bounds__(256) k_moe_rows(rows_args a) {
                 if (t >= tb.grp_ntok()[g]) continue;
                 float o = 0.f;
                 for (int rg = 0; rg < a.ranges; ++rg) o += part[((size_t)g * a.ranges + rg) * 16 * GROUP + rr * GROUP + t];
+                // the down bias inside the router weighting: added to each expert's output
+                if (a.bias_dn) o += a.bias_dn[(size_t)tb.slot_expert()[tb.grp_slot()[g]] * a.H + tr * 16 + rr];
                 osum[(size_t)(tb.grp_col0()[g] + t) * 16 + rr] = o;
             }
             __syncthreads();
@@ -756,6 +771,7 @@ struct xroute_args {
     int T, H, E;
     float *logits;        // [T][E]
     uint32_t *xfrag;      // [T][H/32][2][4][4]
+    float *x_out;         // [T][H]: the routed activation (normalised), for the host's experts; or null
     int *status;
 };
 
@@ -812,6 +828,9 @@ __global__ void __launch_bounds__(XROUTE_WARPS * 32) k_xroute(xroute_args a) {
             }
         }
         __syncthreads();
+        if (a.x_out && blockIdx.x == 0)
+            for (int c = threadIdx.x; c < n4; c += XROUTE_WARPS * 32)
+                reinterpret_cast<float4 *>(a.x_out + (size_t)t * H)[c] = reinterpret_cast<const float4 *>(xs)[c];
         for (int e = e0; e < a.E; e += nw) {
             const float *w = wrow;
             if (e != e0) {
@@ -852,7 +871,7 @@ __global__ void __launch_bounds__(XROUTE_WARPS * 32) k_xroute(xroute_args a) {
 
 // Routing tables of the decode path, in shared memory.
 struct xtab {
-    int G, C;                         // groups, columns (= T * K)
+    int G, C;                         // groups, columns (T * K less the choices the host takes)
     int n_slots;                      // distinct experts, ascending
     int grp_slot[MAX_TK], slot_expert[MAX_TK];
     int grp_expert[MAX_TK], grp_col0[MAX_TK], grp_ntok[MAX_TK];
@@ -866,17 +885,20 @@ struct xtab {
 
 // Every token's top-k (warp t of nw takes tokens t, t + nw, ...), then the tables by warp 0: the
 // columns are the choices sorted by (expert, token) — distinct experts ascending, a slot's
-// tokens in token order — cut into groups of at most GROUP columns of one expert.
+// tokens in token order — cut into groups of at most GROUP columns of one expert. Choices whose
+// bit is set in `hmask` (bit t * K + m) are computed on the host: they get no column
+// (col_of = -1) and their experts no slot unless another choice keeps them.
 // Not inlined: the gate-up kernel runs it twice (a dry run before its wait, then the real one)
 // and the second call finds the code in the instruction cache.
-__device__ __noinline__ void xbuild(xtab &tb, const float *logits, int T, int E, int K, int gating, int warp, int lane) {
+__device__ __noinline__ void xbuild(xtab &tb, const float *logits, int T, int E, int K, int gating, int warp, int lane,
+                                   unsigned hmask = 0u) {
     const int nw = (int)(blockDim.x >> 5);
     for (int t = warp; t < T; t += nw) xtopk(logits + (size_t)t * E, E, K, gating, lane, tb.idx + t * K, tb.wts + t * K);
     __syncthreads();
     if (warp == 0) {
-        const int C = T * K;
-        const bool live = lane < C;
-        const int key = live ? (int)tb.idx[lane] * 64 + lane / K : 0x7FFFFFFF;
+        const bool chosen = lane < T * K && !((hmask >> lane) & 1u);
+        const int C = __popc(__ballot_sync(0xffffffffu, chosen));
+        const int key = chosen ? (int)tb.idx[lane] * 64 + lane / K : 0x7FFFFFFF;
         // rank = number of smaller keys; the keys go through shared memory, which the unrolled
         // compares read as broadcasts (a loop of 32 shuffles took several times as long)
         tb.key[lane] = key;
@@ -884,12 +906,15 @@ __device__ __noinline__ void xbuild(xtab &tb, const float *logits, int T, int E,
         int rank = 0;
 #pragma unroll
         for (int j = 0; j < 32; ++j) rank += (tb.key[j] < key);
-        if (live) {
+        if (chosen) {
             tb.col_of[lane] = rank;
             tb.col_tok[rank] = lane / K;
             tb.grp_expert[rank] = (int)tb.idx[lane];  // expert of column `rank`, for now
+        } else if (lane < T * K) {
+            tb.col_of[lane] = -1;
         }
         __syncwarp();
+        const bool live = lane < C;  // from here on a lane is a column
         const int ex = live ? tb.grp_expert[lane] : -1;
         const int prev = __shfl_up_sync(0xffffffffu, ex, 1);
         const bool start = live && (lane == 0 || prev != ex);
@@ -955,6 +980,12 @@ struct xexp_args {
     xtab *tab_pub;            // gate-up: CTA 0 publishes its tables here; down: read them (or null)
     const int *slot_of;       // residency cache: expert -> slot of the bank (or null)
     int by_slot;              // bank holds one expert per slot (staged offload), not all experts
+    const unsigned *hmask;    // choices the host computes (bit t * K + m), or null
+    unsigned long long poll_ns;  // the wait for other warps' partials (XPOLL_NS in use)
+    int phantom;                 // 1: every such wait runs out (testing)
+    // per-expert biases or null: gate rows of expert e at e, up rows at E + e ([2E][I]); down
+    // [E][H] (moe.rs:2310-2331, 2362-2372)
+    const float *bias_gu, *bias_dn;
     // per CTA [start, dependency wait over, end] in ns of %globaltimer (the end the last warp's),
     // rewritten every launch, or null
     unsigned long long *span;
@@ -966,10 +997,11 @@ __device__ __forceinline__ int xcta(long P, long NW, long p) { return (int)(((p 
 // The np piece partials of one (record run, float4): pieces seg * np .. + np - 1, rec floats
 // apart, the float4 at offset off of each; read as soon as every one has been stored and summed
 // in piece order from 0, per component (sum[0..3]) or, PAIR, per pair (sum[0] = x + y, sum[1] =
-// z + w). False (and STATUS_WAIT_TIMEOUT) when a piece does not arrive within XPOLL_NS.
+// z + w). False (and STATUS_WAIT_TIMEOUT) when a piece does not arrive within poll_ns
+// (`phantom`: as if one never did — a test of this path).
 template <bool PAIR>
 __device__ bool take_quads(const float *part, int rec, int np, int seg, int off, float (&sum)[4], int *status,
-                           int *rounds = nullptr) {
+                           unsigned long long poll_ns, int phantom, int *rounds = nullptr) {
     uint4 v[XMAX_PIECES];
     unsigned long long t0 = 0;
     for (;;) {
@@ -983,11 +1015,11 @@ __device__ bool take_quads(const float *part, int rec, int np, int seg, int off,
         for (int j = 0; j < XMAX_PIECES; ++j)
             empty |= (uint32_t)(v[j].x == PART_EMPTY) | (uint32_t)(v[j].y == PART_EMPTY) |
                      (uint32_t)(v[j].z == PART_EMPTY) | (uint32_t)(v[j].w == PART_EMPTY);
-        if (!empty) break;
+        if (!empty && !phantom) break;
         const unsigned long long t = xnow();
         if (t0 == 0) {
             t0 = t;
-        } else if (t - t0 > XPOLL_NS) {
+        } else if (t - t0 > poll_ns) {
             atomicOr(status, STATUS_WAIT_TIMEOUT);
             return false;
         }
@@ -1044,6 +1076,8 @@ __global__ void __launch_bounds__(XW * 32, 1) k_xexpert(xexp_args a) {
         // CTA 0 releases the down kernel only once it has published the tables (below)
         if (blockIdx.x != 0 || !a.tab_pub) pdl_trigger();
     }
+    // final before this kernel's wait (gate-up) or before it was launched (down)
+    const unsigned hm = a.hmask ? __ldcg(a.hmask) : 0u;
     if (MODE == 1 && a.tab_pub) {
         // the gate-up kernel's published tables: final before this kernel was launched
         const uint32_t *src = reinterpret_cast<const uint32_t *>(a.tab_pub);
@@ -1051,7 +1085,7 @@ __global__ void __launch_bounds__(XW * 32, 1) k_xexpert(xexp_args a) {
         for (int i = threadIdx.x; i < (int)(sizeof(xtab) / 4); i += blockDim.x) dst[i] = __ldcg(src + i);
         __syncthreads();
     } else {
-        xbuild(tb, a.logits, a.T, a.E, a.K, a.gating, warp, lane);
+        xbuild(tb, a.logits, a.T, a.E, a.K, a.gating, warp, lane, hm);
     }
     TRACE(1);
     if (MODE == 0 && blockIdx.x == 0 && a.tab_pub) {
@@ -1063,7 +1097,7 @@ __global__ void __launch_bounds__(XW * 32, 1) k_xexpert(xexp_args a) {
         pdl_trigger();
     }
     if (MODE == 0 && blockIdx.x == 0)
-        for (int i = threadIdx.x; i < tb.C; i += blockDim.x) {
+        for (int i = threadIdx.x; i < a.T * a.K; i += blockDim.x) {
             a.idx_out[i] = tb.idx[i];
             a.wts_out[i] = tb.wts[i];
         }
@@ -1147,6 +1181,13 @@ __global__ void __launch_bounds__(XW * 32, 1) k_xexpert(xexp_args a) {
         pdl_trigger();
         pdl_wait();
         if (span && threadIdx.x == 0) span[1] = xnow();
+    }
+    if (MODE == 1 && a.by_slot && G == 0) {
+        // the host took every choice: the device's share is zero
+        for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < a.T * a.H; i += gridDim.x * blockDim.x)
+            a.out[i] = a.residual ? a.residual[i] : 0.f;
+        XSPAN_END();
+        return;
     }
     if (a.slot_of) {
         // cached offload: the block's residency table (final before either kernel's wait
@@ -1263,11 +1304,20 @@ __global__ void __launch_bounds__(XW * 32, 1) k_xexpert(xexp_args a) {
             for (int e = lane; e < 8 * ntok; e += 32) {
                 const int r = e & 7, t = e >> 3;
                 float gu[4];  // gate r, gate r + 8, up r, up r + 8
-                if (!take_quads<false>(a.part, rec, np, u, e * 4, gu, a.status, TRACE_ROUNDS)) {
+                if (!take_quads<false>(a.part, rec, np, u, e * 4, gu, a.status, a.poll_ns, a.phantom, TRACE_ROUNDS)) {
                     failed = true;
                     break;
                 }
                 const int col = col0 + t;
+                if (a.bias_gu) {
+                    const int ex = tb.grp_expert[g];
+#pragma unroll
+                    for (int h = 0; h < 2; ++h) {
+                        const int row = tr * 16 + r + 8 * h;
+                        gu[h] += a.bias_gu[(size_t)ex * a.I + row];
+                        gu[2 + h] += a.bias_gu[(size_t)(a.E + ex) * a.I + row];
+                    }
+                }
 #pragma unroll
                 for (int h = 0; h < 2; ++h) {
                     const int row = tr * 16 + r + 8 * h;
@@ -1313,12 +1363,24 @@ __global__ void __launch_bounds__(XW * 32, 1) k_xexpert(xexp_args a) {
             for (int e = lane; e < n_q; e += 32) {
                 const int r = e & 7, m = (e >> 3) % a.K, t = (e >> 3) / a.K;
                 const int col = tb.col_of[t * a.K + m];
+                if (col < 0) {
+                    // a choice the host computes: nothing here (fmaf(w, 0, acc) leaves acc as it is)
+                    os[(t * 16 + r) * a.K + m] = 0.f;
+                    os[(t * 16 + r + 8) * a.K + m] = 0.f;
+                    continue;
+                }
                 const int g = tb.col_grp[col];
                 float o[4];
                 if (!take_quads<true>(a.part, rec, np, tr * G + g, ((col - tb.grp_col0[g]) * 8 + r) * 4, o, a.status,
+                                      a.poll_ns, a.phantom,
                                       TRACE_ROUNDS)) {
                     failed = true;
                     break;
+                }
+                if (a.bias_dn) {
+                    const float *bd = a.bias_dn + (size_t)tb.idx[t * a.K + m] * a.H + tr * 16 + r;
+                    o[0] += bd[0];
+                    o[1] += bd[8];
                 }
                 os[(t * 16 + r) * a.K + m] = o[0];
                 os[(t * 16 + r + 8) * a.K + m] = o[1];
@@ -1434,6 +1496,7 @@ struct xfetch_args {
     size_t stride;        // packed bytes per expert (a multiple of 16)
     uint8_t *stage;       // device slots, one per distinct routed expert (or the cache's)
     const int *plan;      // residency cache: the misses to copy, (expert, slot) pairs (or null)
+    const unsigned *hmask;  // choices the host computes (their experts are not copied), or null
 };
 
 // Copy n16 16-byte words, the grid's threads striding, eight loads in flight per thread (host
@@ -1473,7 +1536,7 @@ __global__ void __launch_bounds__(XFETCH_THREADS, 5) k_xfetch(xfetch_args a) {
             copy16(reinterpret_cast<const uint4 *>(a.host + (size_t)__ldcg(a.plan + 1 + 2 * i) * a.stride),
                    reinterpret_cast<uint4 *>(a.stage + (size_t)__ldcg(a.plan + 2 + 2 * i) * a.stride), n16);
     } else {
-        xbuild(tb, a.logits, a.T, a.E, a.K, a.gating, warp, lane);
+        xbuild(tb, a.logits, a.T, a.E, a.K, a.gating, warp, lane, a.hmask ? __ldcg(a.hmask) : 0u);
         for (int s = 0; s < tb.n_slots; ++s)
             copy16(reinterpret_cast<const uint4 *>(a.host + (size_t)tb.slot_expert[s] * a.stride),
                    reinterpret_cast<uint4 *>(a.stage + (size_t)s * a.stride), n16);
@@ -1492,6 +1555,48 @@ __global__ void __launch_bounds__(XFETCH_THREADS, 5) k_xfetch(xfetch_args a) {
 // recently used slot no expert of this step holds (an empty slot first, the lowest index on a
 // tie), evicting its owner, and is listed in the plan for the fetch kernels. Deterministic, so
 // the slot tables are the same for any timing.
+// The reference's host split (moe.rs:2180-2193 with HostPolicy::host_count,
+// host_experts.rs:111-118): of one token's choices whose experts the device does not hold (bit
+// m of `miss`, lane m holding choice m), the first host_count(misses) in router order are
+// computed on the host. kind: 0 none, 1 ceil(misses x frac) (frac clamped to [0, 1]), 2 misses -
+// over. Leaves the mask in h.hmask; with a nonzero mask, posts the job to the host's mail — the
+// block, the experts and their gating weights in router order, the routed activation x (H
+// floats, device memory) — and then, after a system-scope fence, the next sequence number.
+// Returns the mask. One warp.
+__device__ unsigned host_split(unsigned miss, const unsigned *idx, const float *wts, int K, const moe_host &h,
+                               const float *x, int H, int lane) {
+    const int misses = __popc(miss);
+    int n = 0;
+    if (h.kind == 1) n = min((int)ceilf((float)misses * fminf(fmaxf(h.frac, 0.f), 1.f)), misses);
+    else if (h.kind == 2) n = max(misses - h.over, 0);
+    unsigned hm = 0u, mm = miss;
+    for (int i = 0; i < n; ++i) {
+        hm |= mm & (0u - mm);
+        mm &= mm - 1u;
+    }
+    if (lane == 0) *h.hmask = hm;
+    if (!hm) return 0u;
+    if (lane < K && ((hm >> lane) & 1u)) {
+        const int p = __popc(hm & ((1u << lane) - 1u));
+        reinterpret_cast<unsigned *>(h.mail + MAIL_IDS)[p] = idx[lane];
+        reinterpret_cast<float *>(h.mail + MAIL_WTS)[p] = wts[lane];
+    }
+    if (lane == 0) {
+        *reinterpret_cast<unsigned *>(h.mail + MAIL_N) = (unsigned)n;
+        *reinterpret_cast<unsigned *>(h.mail + MAIL_BLOCK) = (unsigned)h.block;
+    }
+    for (int c = lane; c < H / 4; c += 32)
+        reinterpret_cast<float4 *>(h.mail + MAIL_X)[c] = __ldcg(reinterpret_cast<const float4 *>(x) + c);
+    __threadfence_system();  // every lane's writes reach host memory before the number below
+    __syncwarp();
+    if (lane == 0) {
+        const unsigned long long seq = *h.seq + 1;
+        *h.seq = seq;
+        asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(h.mail + MAIL_SEQ), "l"(seq) : "memory");
+    }
+    return hm;
+}
+
 struct xplan_args {
     const float *logits;
     int T, E, K, gating;
@@ -1499,6 +1604,11 @@ struct xplan_args {
     int *slot_of, *owner, *stamp, *plan;
     int n_cache;
     unsigned long long *fetched;
+    // host split (one token) when has_host; x: the routed activation (device)
+    int has_host;
+    moe_host host;
+    const float *x;
+    int H;
     int *status;
 };
 
@@ -1509,6 +1619,13 @@ __global__ void __launch_bounds__(32) k_xplan(xplan_args a) {
     pdl_wait();
     pdl_trigger();
     xbuild(tb, a.logits, a.T, a.E, a.K, a.gating, 0, lane);
+    if (a.has_host && a.T == 1) {
+        // the host takes some of the choices that miss the cache; only the device's are admitted
+        const bool miss = lane < a.K && a.slot_of[tb.idx[lane]] < 0;
+        const unsigned hm = host_split(__ballot_sync(0xffffffffu, miss), tb.idx, tb.wts, a.K, a.host, a.x, a.H, lane);
+        __syncwarp();
+        if (hm) xbuild(tb, a.logits, a.T, a.E, a.K, a.gating, 0, lane, hm);
+    }
     const int clock = *a.pos;
     for (int j = lane; j < a.n_cache; j += 32) used[j] = 0;
     __syncwarp();
@@ -1560,6 +1677,84 @@ __global__ void __launch_bounds__(32) k_xplan(xplan_args a) {
         a.plan[0] = n;
         if (a.fetched) *a.fetched += (unsigned long long)n;
     }
+}
+
+// Host split of an offloaded block without a residency cache: every choice misses the device.
+struct xsplit_args {
+    const float *logits;  // [1][E]
+    int E, K, gating;
+    moe_host host;
+    const float *x;       // [H], the routed activation
+    int H;
+};
+
+__global__ void __launch_bounds__(32) k_xsplit(xsplit_args a) {
+    __shared__ unsigned idx[32];
+    __shared__ float wts[32];
+    const int lane = threadIdx.x;
+    pdl_wait();
+    pdl_trigger();
+    xtopk(a.logits, a.E, a.K, a.gating, lane, idx, wts);
+    __syncwarp();
+    host_split(a.K >= 32 ? 0xffffffffu : (1u << a.K) - 1u, idx, wts, a.K, a.host, a.x, a.H, lane);
+}
+
+// The fold of the host's share (moe.rs:2389-2420): ffn += host part, then h += ffn. The wait
+// for the host's answer (its sequence number in the done record) starts before the dependency
+// wait, so it overlaps the device's share; it is bounded by host.wait_ns, after which the
+// status is raised and the host's share left out.
+struct xfold_args {
+    float *out;
+    const float *residual;  // or null
+    moe_host host;
+    int n;
+};
+
+__device__ __forceinline__ unsigned long long ld_acquire_sys_u64(const void *p) {
+    unsigned long long v;
+    asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+
+__device__ __forceinline__ float ld_relaxed_sys_f32(const void *p) {
+    float v;
+    asm volatile("ld.relaxed.sys.global.f32 %0, [%1];" : "=f"(v) : "l"(p) : "memory");
+    return v;
+}
+
+__global__ void __launch_bounds__(256) k_xfold(xfold_args a) {
+    __shared__ int take;  // 1: the host answered for this block; 0: no host share or no answer
+    if (threadIdx.x == 0) {
+        // the split kernel finished before the kernel this one follows was allowed to start
+        const unsigned hm = __ldcg(a.host.hmask);
+        int ok = 0;
+        if (hm) {
+            const unsigned long long want = __ldcg(a.host.seq);
+            const unsigned long long t0 = xnow();
+            for (;;) {
+                if (ld_acquire_sys_u64(a.host.done + DONE_SEQ) == want) {
+                    ok = 1;
+                    break;
+                }
+                if (xnow() - t0 > a.host.wait_ns) {
+                    atomicOr(a.host.status, STATUS_WAIT_TIMEOUT);
+                    break;
+                }
+                __nanosleep(256);
+            }
+        }
+        take = ok;
+    }
+    __syncthreads();
+    const int ok = take;
+    if (ok) (void)ld_acquire_sys_u64(a.host.done + DONE_SEQ);  // this thread's own acquire
+    pdl_wait();  // the device's share is the previous kernel's output
+    const float *host = reinterpret_cast<const float *>(a.host.done + DONE_OUT);
+    for (int i = threadIdx.x; i < a.n; i += blockDim.x) {
+        const float f = a.host.ffn[i] + (ok ? ld_relaxed_sys_f32(host + i) : 0.f);
+        a.out[i] = a.residual ? a.residual[i] + f : f;
+    }
+    pdl_trigger();
 }
 
 constexpr unsigned long long XWAIT_NS = 200000000ull;  // a wait on other CTAs gives up after 0.2 s
@@ -2386,7 +2581,8 @@ int moe_forward_impl(moearc_x_moe *m, const float *x, unsigned n_tokens, const f
         f.status = m->status;
         return f;
     };
-    if (m->fused && !off) {
+    const bool biased = m->bias_gu || m->bias_dn;  // the opt-in single-launch kernels have no biases
+    if (m->fused && !off && !biased) {
         if (launch_coop(m->wtype == T_MXFP4 ? k_moe_fused<39, true> : k_moe_fused<2, true>, dim3(m->f_grid),
                         dim3(XW * 32), (size_t)m->f_smem, c->stream, fused_args()) != cudaSuccess)
             return ERR;
@@ -2394,12 +2590,18 @@ int moe_forward_impl(moearc_x_moe *m, const float *x, unsigned n_tokens, const f
         return ls.finish();
     }
     if (m->xpath) {
-        xroute_args xr{x, norm_w, eps, router_w, router_b, T, m->H, m->E, m->logits, m->xfrag, m->status};
+        // part of an offloaded block's experts on the host cores (one token per call)
+        const moe_host *hs = (off && off->host && off->host->kind && T == 1) ? off->host : nullptr;
+        if (hs && biased) return ERR_ARG;  // the host pool has no expert biases
+        // the routed activation goes to the host through the device's-share buffer, which the
+        // down kernel overwrites only after the split kernel has read it
+        xroute_args xr{x, norm_w, eps, router_w, router_b, T, m->H, m->E, m->logits, m->xfrag,
+                       hs ? hs->ffn : nullptr, m->status};
         if (launch_pdl(k_xroute, dim3(m->x_route_grid), dim3(XROUTE_WARPS * 32), (size_t)m->x_route_smem, c->stream,
                        xr) != cudaSuccess)
             return ERR;
         mark(3);
-        if (m->fused_gd && !off) {
+        if (m->fused_gd && !off && !biased) {
             // gate-up and down in one launch: down weights stream while gate-up finishes
             if (launch_pdl(m->wtype == T_MXFP4 ? k_moe_fused<39, false> : k_moe_fused<2, false>, dim3(m->f_grid),
                            dim3(XW * 32), (size_t)m->f_smem, c->stream, fused_args()) != cudaSuccess)
@@ -2409,15 +2611,20 @@ int moe_forward_impl(moearc_x_moe *m, const float *x, unsigned n_tokens, const f
         }
         const size_t gu_stride = (size_t)2 * m->ntr_i * m->nkt_h * m->tile_bytes;
         const size_t dn_stride = (size_t)m->ntr_h * m->nkt_i * m->tile_bytes;
-        xfetch_args fa{m->logits, T, m->E, m->K, m->gating, nullptr, 0, nullptr, nullptr};
+        xfetch_args fa{m->logits, T, m->E, m->K, m->gating, nullptr, 0, nullptr, nullptr, hs ? hs->hmask : nullptr};
         if (off && off->slot_of) {
             // residency cache: plan the step's slots (hits stay, misses evict the least recently
-            // used slot), then fetch only the misses
+            // used slot), then fetch only the misses; with a host policy the host first takes its
+            // share of the misses, which are neither admitted nor fetched
             xplan_args pa{m->logits, T, m->E, m->K, m->gating, off->clock, off->slot_of, off->owner, off->stamp,
-                          off->plan, off->n_cache, off->fetched, m->status};
+                          off->plan, off->n_cache, off->fetched, hs ? 1 : 0, hs ? *hs : moe_host{},
+                          hs ? hs->ffn : nullptr, m->H, m->status};
             if (launch_pdl(k_xplan, dim3(1), dim3(32), (size_t)off->n_cache, c->stream, pa) != cudaSuccess)
                 return ERR;
             fa.plan = off->plan;
+        } else if (hs) {
+            xsplit_args sa{m->logits, m->E, m->K, m->gating, *hs, hs->ffn, m->H};
+            if (launch_pdl(k_xsplit, dim3(1), dim3(32), 0, c->stream, sa) != cudaSuccess) return ERR;
         }
         if (off) {
             fa.host = static_cast<const uint8_t *>(gateup_packed);
@@ -2459,6 +2666,11 @@ int moe_forward_impl(moearc_x_moe *m, const float *x, unsigned n_tokens, const f
         // builds its own tables after its wait
         xa.tab_pub = off ? nullptr : static_cast<xtab *>(m->x_tab_pub);
         xa.slot_of = off ? off->slot_of : nullptr;
+        xa.hmask = hs ? hs->hmask : nullptr;
+        xa.poll_ns = m->x_poll_ns;
+        xa.phantom = m->x_phantom;
+        xa.bias_gu = m->bias_gu;
+        xa.bias_dn = m->bias_dn;
         xa.status = m->status;
         xa.span = span;  // the gate-up kernel's CTAs, then the down kernel's
         const bool mx = m->wtype == T_MXFP4;
@@ -2490,13 +2702,19 @@ int moe_forward_impl(moearc_x_moe *m, const float *x, unsigned n_tokens, const f
         xd.stage_bytes = m->x_stage_dn;
         xd.nblk_b = m->I / 32;
         xd.bsrc = m->actfrag;
-        xd.residual = residual;
-        xd.out = out;
+        xd.residual = hs ? nullptr : residual;  // with a host share: the device's share alone, folded below
+        xd.out = hs ? hs->ffn : out;
         xd.part = m->x_part_dn;
         if (launch_pdl(mx ? k_xexpert<39, 1> : k_xexpert<2, 1>, dim3(m->x_grid), dim3(m->x_warps * 32),
                        (size_t)m->x_warps * XSTAGES * m->x_stage_dn, c->stream, xd) != cudaSuccess)
             return ERR;
         mark(5);
+        if (hs) {
+            if (launch_pdl(k_xfold, dim3(1), dim3(256), 0, c->stream, xfold_args{out, residual, *hs, m->H}) !=
+                cudaSuccess)
+                return ERR;
+            mark(8);
+        }
         return ls.finish();
     }
 
@@ -2533,6 +2751,9 @@ int moe_forward_impl(moearc_x_moe *m, const float *x, unsigned n_tokens, const f
     ga.T = T;
     ga.K = m->K;
     ga.H = m->H;
+    ga.bias_gu = m->bias_gu;
+    ga.bias_dn = m->bias_dn;
+    ga.E = m->E;
     ga.status = m->status;
     if (launch_pdl(m->wtype == T_MXFP4 ? k_moe_rows<39> : k_moe_rows<2>, dim3(m->grid_gu), dim3(m->warps_gu * 32),
                    (size_t)m->smem_gu, c->stream, ga) != cudaSuccess)
@@ -2586,6 +2807,21 @@ void *moearc_x_moe_buffer(moearc_x_moe *m, int which) {
     case 4: return m->tables;
     default: return nullptr;
     }
+}
+
+int moearc_x_moe_set_bias(moearc_x_moe *m, const float *gate_up_bias, const float *down_bias) {
+    if (!m) return ERR;
+    if ((reinterpret_cast<uintptr_t>(gate_up_bias) | reinterpret_cast<uintptr_t>(down_bias)) & 3) return ERR_ARG;
+    m->bias_gu = gate_up_bias;
+    m->bias_dn = down_bias;
+    return OK;
+}
+
+int moearc_x_moe_set_wait(moearc_x_moe *m, unsigned long long poll_ns, int phantom) {
+    if (!m) return ERR;
+    m->x_poll_ns = poll_ns ? poll_ns : XPOLL_NS;
+    m->x_phantom = phantom ? 1 : 0;
+    return OK;
 }
 
 int moearc_x_moe_status(moearc_x_moe *m) {

@@ -51,6 +51,10 @@ class DecoderConfig:
     # device slots per offloaded block that keep fetched experts across steps (the reference's
     # ExpertCache); 0 = pure streaming, else n_expert_used <= n_cache <= n_expert
     n_cache: int = 0
+    # QK-norm per head before RoPE (moe.rs:1961-1985; qwen3moe has it, gpt-oss not)
+    has_qk_norm: int = 0
+    # rows of the output head (logits after the final norm, moe.rs:2434-2437); 0 = none
+    n_vocab: int = 0
 
     def yarn(self, factor: float, n_ctx_orig: int, beta_fast: float = 32.0, beta_slow: float = 1.0):
         """YaRN parameters the way reference.rs:572-591 derives them (RopeScaling::yarn)."""
@@ -87,7 +91,7 @@ class DecoderConfig:
     @staticmethod
     def qwen3_moe(**kw) -> "DecoderConfig":
         """48 layers, hidden 2048, 32 q / 4 kv heads of 128, 128 experts top-8,
-        I 768, Q4_0 experts, renormalised softmax gating, SwiGLU, no window, no sinks."""
+        I 768, Q4_0 experts, renormalised softmax gating, SwiGLU, QK-norm, no window, no sinks."""
         kw.setdefault("expert_type", Q4_0)
         kw.setdefault("gating", 1)
         kw.setdefault("act", 0)
@@ -95,6 +99,7 @@ class DecoderConfig:
         kw.setdefault("has_sinks", 0)
         kw.setdefault("rope_base", 1000000.0)
         kw.setdefault("rms_eps", 1e-6)
+        kw.setdefault("has_qk_norm", 1)
         return DecoderConfig(**{**dict(n_layer=48, n_embd=2048, n_head=32, n_head_kv=4, head_dim=128, n_expert=128,
                                        n_expert_used=8, n_ff=768), **kw})
 
@@ -139,7 +144,7 @@ class Decoder:
         self.ctx._finish(self.ctx.lib.moearc_x_decoder_use_step_kernel(self.h, 1 if on else 0), "use_step_kernel")
 
     def set_wait(self, limit_ns: int = 0, phantom: int = 0) -> None:
-        """The persistent kernel's barrier wait limit (0: default) and phantom arrivals (testing)."""
+        """The decode kernels' wait limits (0: default) and phantom=1 to make them run out (testing)."""
         self.ctx._finish(self.ctx.lib.moearc_x_decoder_set_wait(self.h, limit_ns, phantom), "set_wait")
 
     def trace_words(self) -> int:
@@ -153,6 +158,27 @@ class Decoder:
     def routing(self, layer: int) -> tuple[np.ndarray, np.ndarray]:
         """Block `layer`'s expert ids and gating weights of the last step (persistent kernel)."""
         return self.tensor(12, layer, np.uint32), self.tensor(13, layer, np.float32)
+
+    HOST_POLICIES = {"off": 0, "fraction": 1, "over": 2}
+
+    def host_experts(self, policy: str = "fraction", fraction: float = 0.5, over: int = 0,
+                     threads: int = 0) -> None:
+        """Compute part of the offloaded blocks' experts on host threads beside the device:
+        "fraction" takes the first ceil(misses x fraction) of a block's misses (router order),
+        "over" the misses beyond the first `over`, "off" none (the reference's HostPolicy)."""
+        self.ctx._finish(self.ctx.lib.moearc_x_decoder_host_experts(self.h, self.HOST_POLICIES[policy], fraction,
+                                                                    over, threads), "host_experts")
+
+    def host_wait(self, limit_ns: int = 0, hold: bool = False) -> None:
+        """The fold's wait limit for the host's answer (0: 2 s); hold=True makes the host thread
+        ignore new jobs, so the wait runs out (testing)."""
+        self.ctx._finish(self.ctx.lib.moearc_x_decoder_host_wait(self.h, limit_ns, 1 if hold else 0), "host_wait")
+
+    def host_stats(self) -> dict:
+        """The host pool's counters: jobs, experts, busy and wait nanoseconds."""
+        st = (C.c_ulonglong * 4)()
+        self.ctx._finish(self.ctx.lib.moearc_x_decoder_host_stats(self.h, st), "host_stats")
+        return {"jobs": st[0], "experts": st[1], "busy_ns": st[2], "wait_ns": st[3]}
 
     def kernel_spans(self, on: bool) -> None:
         """Per-CTA timestamps of the kernel chain's expert kernels in every following step."""
@@ -190,6 +216,15 @@ class Decoder:
         x = np.ascontiguousarray(x, np.float32)
         assert x.size == self.cfg.n_embd
         self.ctx._finish(self.ctx.lib.moearc_copy_h2d(self.ctx.raw, self.in_ptr, x.ctypes.data, x.nbytes), "input")
+
+    def logits(self) -> np.ndarray:
+        """The last step's output-head logits (n_vocab floats; the configuration must have a head)."""
+        p = self.ctx.lib.moearc_x_decoder_logits(self.h)
+        if not p:
+            raise BadArgument("the decoder has no output head (n_vocab = 0)")
+        out = np.empty(self.cfg.n_vocab, np.float32)
+        self.ctx._finish(self.ctx.lib.moearc_copy_d2h(self.ctx.raw, out.ctypes.data, p, out.nbytes), "logits")
+        return out
 
     def output(self) -> np.ndarray:
         out = np.empty(self.cfg.n_embd, np.float32)

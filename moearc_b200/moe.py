@@ -41,6 +41,18 @@ class MoeLayer:
                                             self.down.ptr)
         self.ctx._finish(rc, "moe_pack")
 
+    def set_bias(self, gate_up_bias: DeviceBuffer | None, down_bias: DeviceBuffer | None) -> None:
+        """Per-expert biases for the following forward calls: gate_up_bias f32 [2E][I] (gate of
+        expert e at row e, up at E + e), down_bias f32 [E][H]; None: none."""
+        E, H, I = self.desc.n_expert, self.desc.n_embd, self.desc.n_ff
+        if gate_up_bias is not None:
+            gate_up_bias.require("gate/up bias", 4 * 2 * E * I)
+        if down_bias is not None:
+            down_bias.require("down bias", 4 * E * H)
+        rc = self.ctx.lib.moearc_x_moe_set_bias(self.h, gate_up_bias.ptr if gate_up_bias is not None else None,
+                                                down_bias.ptr if down_bias is not None else None)
+        self.ctx._finish(rc, "moe_set_bias")
+
     def forward(self, x: DeviceBuffer, n_tokens: int, router_w: DeviceBuffer, out: DeviceBuffer,
                 router_b: DeviceBuffer | None = None, residual: DeviceBuffer | None = None) -> None:
         H = self.desc.n_embd

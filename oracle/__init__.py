@@ -58,13 +58,13 @@ class CdCfg(C.Structure):
                 ("act", U), ("wtype", U), ("kv_type", U), ("alpha", F), ("limit", F), ("eps", F),
                 ("n_swa", SZ), ("swa_pattern", SZ), ("page_tokens", SZ), ("rope_base", F),
                 ("freq_scale", F), ("ext_factor", F), ("attn_factor", F), ("corr_lo", F),
-                ("corr_hi", F)]
+                ("corr_hi", F), ("qk_norm", U)]
 
 
 class CdLayer(C.Structure):
     _fields_ = [("attn_norm", P), ("ffn_norm", P), ("wq", P), ("wk", P), ("wv", P), ("wo", P),
                 ("sinks", P), ("router", P), ("gate", P), ("up", P), ("down", P),
-                ("k_pages", P), ("v_pages", P), ("table", P)]
+                ("k_pages", P), ("v_pages", P), ("table", P), ("q_norm", P), ("k_norm", P)]
 
 
 def _declare(l: C.CDLL) -> None:
@@ -112,6 +112,7 @@ def _declare(l: C.CDLL) -> None:
         "cd_step": (C.c_int, [C.POINTER(CdCfg), P, P, P, SZ, P, P, P]),
         "cd_step_margins": (C.c_int, [C.POINTER(CdCfg), P, P, P, SZ, P, P, P]),
         "cd_layers": (C.c_int, [C.POINTER(CdCfg), P, SZ, SZ, P, SZ, P, P]),
+        "cd_logits": (C.c_int, [C.POINTER(CdCfg), P, SZ, P, P]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(l, name)

@@ -76,6 +76,16 @@ static int layers_impl(const cd_cfg *c, const cd_layer *L, size_t l0, size_t l1,
         if ((rc = mv(pool, OR_BF16, b->wq, x, Dq, H, q))) break;
         if ((rc = mv(pool, OR_BF16, b->wk, x, Dkv, H, k))) break;
         if ((rc = mv(pool, OR_BF16, b->wv, x, Dkv, H, v))) break;
+        if (c->qk_norm) {
+            /* QK-norm per head over head_dim channels, one weight row broadcast across heads
+             * (moe.rs:1969-1981, the qwen3moe spelling) */
+            if (!b->q_norm || !b->k_norm) {
+                rc = -2;
+                break;
+            }
+            or_rmsnorm(q, b->q_norm, c->n_head, c->head_dim, c->eps, q);
+            or_rmsnorm(k, b->k_norm, c->n_head_kv, c->head_dim, c->eps, k);
+        }
         or_rope_ext(q, &p32, 1, c->n_head, c->head_dim, c->head_dim, c->rope_base, c->freq_scale,
                     c->ext_factor, c->attn_factor, c->corr_lo, c->corr_hi, 1, qr);
         or_rope_ext(k, &p32, 1, c->n_head_kv, c->head_dim, c->head_dim, c->rope_base,
@@ -159,4 +169,9 @@ int cd_step(const cd_cfg *c, const cd_layer *layers, const float *output_norm, c
     if (!rc) or_rmsnorm(h, output_norm, 1, c->n_embd, c->eps, out);
     free(h);
     return rc;
+}
+
+int cd_logits(const cd_cfg *c, const uint16_t *w_out, size_t n_vocab, const float *x, float *logits) {
+    if (!c || !w_out || !x || !logits) return -1;
+    return or_matvec_q(OR_BF16, (const uint8_t *)w_out, x, n_vocab, c->n_embd, logits);
 }

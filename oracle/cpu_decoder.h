@@ -3,7 +3,8 @@
  * CPU. TEST / BENCH INFRASTRUCTURE ONLY.
  *
  * The step is the per-block kernel sequence of crates/moearc-engine/src/moe.rs:1935-2427:
- *   x = rmsnorm(h, attn_norm); q,k,v = W x; rope(q), rope(k) (NeoX, moe.rs:1987-2012);
+ *   x = rmsnorm(h, attn_norm); q,k,v = W x; [per-head rmsnorm of q, k: QK-norm, moe.rs:1961-1985];
+ *   rope(q), rope(k) (NeoX, moe.rs:1987-2012);
  *   kv_append at the layer's (page, slot); attention over [kv_begin, n_kv) with sinks;
  *   h += Wo . attn; x = rmsnorm(h, ffn_norm); h += moe_ffn(x)
  * and a final rmsnorm (moe.rs:2429-2433). Blocks l with l % swa_pattern < swa_pattern - 1
@@ -31,6 +32,7 @@ typedef struct {
     float alpha, limit, eps;
     size_t n_swa, swa_pattern, page_tokens;
     float rope_base, freq_scale, ext_factor, attn_factor, corr_lo, corr_hi;
+    unsigned qk_norm; /* 1: q and k normalised per head (head_dim-wide weights) before RoPE */
 } cd_cfg;
 
 typedef struct {
@@ -41,6 +43,7 @@ typedef struct {
     const uint8_t *gate, *up, *down;        /* expert banks, GGUF layout, wtype */
     void *k_pages, *v_pages;                /* this layer's KV pool, kv_type elements */
     const uint32_t *table;                  /* logical page -> physical page */
+    const float *q_norm, *k_norm;           /* [head_dim] QK-norm weights (qk_norm) or NULL */
 } cd_layer;
 
 /* Decode the token whose input hidden state is h_in (n_embd floats) at position pos; writes
@@ -58,6 +61,10 @@ int cd_step_margins(const cd_cfg *c, const cd_layer *layers, const float *output
  * norm: the bounded sample the bench times. */
 int cd_layers(const cd_cfg *c, const cd_layer *layers, size_t l0, size_t l1, float *h,
               size_t pos, hx_pool *pool, uint32_t *idx_out);
+
+/* The output head (moe.rs:2434-2437): logits = W_out . x, W_out bf16 [n_vocab][n_embd], x the
+ * normalised final hidden state (cd_step's out). */
+int cd_logits(const cd_cfg *c, const uint16_t *w_out, size_t n_vocab, const float *x, float *logits);
 
 #ifdef __cplusplus
 }

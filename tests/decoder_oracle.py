@@ -35,15 +35,17 @@ def host_model(dec: Decoder):
         kp = dec.tensor(4, l, np.uint16)
         t["k"], t["v"] = np.zeros_like(kp), np.zeros_like(kp)
         t["table"] = dec.tensor(6, l, np.uint32)
+        t["q_norm"] = dec.tensor(15, l, np.float32) if cfg.has_qk_norm else None
+        t["k_norm"] = dec.tensor(16, l, np.float32) if cfg.has_qk_norm else None
         keep.append(t)
         layers.append(O.CdLayer(*[O.ptr(t[n]) if t[n] is not None else None for n in
                                   ("attn_norm", "ffn_norm", "wq", "wk", "wv", "wo", "sinks", "router",
-                                   "gate", "up", "down", "k", "v", "table")]))
+                                   "gate", "up", "down", "k", "v", "table", "q_norm", "k_norm")]))
     arr = (O.CdLayer * cfg.n_layer)(*layers)
     c = O.CdCfg(cfg.n_layer, H, cfg.n_head, cfg.n_head_kv, cfg.head_dim, cfg.n_expert, cfg.n_ff,
                 cfg.n_expert_used, cfg.gating, cfg.act, cfg.expert_type, O.BF16, cfg.alpha, cfg.limit,
                 cfg.rms_eps, cfg.n_swa, cfg.swa_pattern, 32, cfg.rope_base, cfg.rope_freq_scale,
-                cfg.rope_ext_factor, cfg.rope_attn_factor, cfg.rope_corr_lo, cfg.rope_corr_hi)
+                cfg.rope_ext_factor, cfg.rope_attn_factor, cfg.rope_corr_lo, cfg.rope_corr_hi, cfg.has_qk_norm)
     return c, arr, keep, dec.tensor(11, 0, np.float32)
 
 
@@ -55,3 +57,13 @@ def oracle_step(c, arr, out_norm, x, pos):
 
 def rel_to_oracle(got, want):
     return float(np.max(np.abs(got.astype(np.float64) - want) / np.maximum(np.abs(want), 1.0)))
+
+
+def oracle_logits(c, dec: Decoder, x_normed):
+    """The output head on the oracle's normalised final state (cd_logits), from the decoder's
+    packed head weights unpacked to rows."""
+    w = np.ascontiguousarray(unpack_dense(dec.tensor(17, 0, np.uint16), dec.cfg.n_vocab, dec.cfg.n_embd))
+    out = np.zeros(dec.cfg.n_vocab, np.float32)
+    x = np.ascontiguousarray(x_normed, np.float32)
+    assert O.lib().cd_logits(C.byref(c), O.ptr(w), dec.cfg.n_vocab, O.ptr(x), O.ptr(out)) == 0
+    return out

@@ -267,6 +267,151 @@ def test_expert_residency_cache_gives_the_resident_bits_and_fetches_less(ctx, et
         Decoder(ctx, DecoderConfig(**kw, n_offload=2, n_cache=k - 1))  # fewer slots than a step needs
 
 
+@pytest.mark.parametrize("etype,n_expert,k,policy,value,n_cache,graph", [
+    (O.MXFP4, 8, 2, "fraction", 0.5, 0, True),   # one of the two routed experts on the host
+    (O.Q4_0, 16, 4, "over", 1, 0, False),        # three of four on the host, eager launches
+    (O.MXFP4, 8, 2, "fraction", 1.0, 3, True),   # every miss on the host: the cache admits nothing
+    (O.Q4_0, 16, 4, "fraction", 0.5, 6, True),   # half the misses on the host, the rest cached
+])
+def test_host_experts_beside_the_device_match_the_oracle(ctx, etype, n_expert, k, policy, value, n_cache, graph):
+    """Offloaded blocks with part of their experts computed by the host pool (moe.rs:2169-2211
+    the split, 2389-2420 the fold) against the oracle's decode step; the pool's counters show
+    the split the policy asks for (host_experts.rs:111-118)."""
+    kw = dict(n_layer=3, n_embd=256, n_head=8, n_head_kv=2, head_dim=64, n_expert=n_expert,
+              n_expert_used=k, n_ff=128, expert_type=etype, n_swa=40, swa_pattern=2, n_ctx=128,
+              seed=0x0FF1)
+    dec = Decoder(ctx, DecoderConfig(**kw, n_offload=2, n_cache=n_cache))
+    dec.use_graph(graph)
+    if policy == "fraction":
+        dec.host_experts("fraction", fraction=value, threads=3)
+    else:
+        dec.host_experts("over", over=value, threads=3)
+    c, arr, keep, out_norm = host_model(dec)
+    steps, worst = 24, 0.0
+    for pos in range(steps):
+        x = O.synth_normal_f32(0x2300 + pos, kw["n_embd"], 1.0)
+        dec.set_input(x)
+        dec.step()
+        worst = max(worst, rel_to_oracle(dec.output(), oracle_step(c, arr, out_norm, x, pos)))
+    st = dec.host_stats()
+    print(f"host experts {policy}={value} cache={n_cache}: {steps} tokens, max rel err {worst:.3e}, {st}")
+    assert dec.status() == 0
+    assert worst <= 1e-3
+    # one job per offloaded block per step that leaves the host something
+    assert st["jobs"] == 2 * steps if not n_cache or value == 1.0 else 0 < st["jobs"] <= 2 * steps
+    fetched = dec.fetched()
+    if not n_cache:
+        per_block = -(-k // 2) if policy == "fraction" else k - value
+        assert st["experts"] == 2 * steps * per_block
+    elif value == 1.0:
+        assert fetched == 0 and st["experts"] == 2 * steps * k  # nothing is ever admitted
+    else:
+        assert 0 < st["experts"] < 2 * steps * k and 0 < fetched < 2 * steps * k
+    # the split off again: the device computes every expert
+    dec.host_experts("off")
+    x = O.synth_normal_f32(0x2300 + steps, kw["n_embd"], 1.0)
+    dec.set_input(x)
+    dec.step()
+    assert rel_to_oracle(dec.output(), oracle_step(c, arr, out_norm, x, steps)) <= 1e-3
+    assert dec.host_stats()["jobs"] == st["jobs"]
+    dec.close()
+    resident = Decoder(ctx, DecoderConfig(**kw))
+    with pytest.raises(BadArgument):
+        resident.host_experts("fraction", 0.5)  # nothing offloaded
+    resident.close()
+
+
+def test_a_host_answer_that_does_not_come_is_reported_and_the_step_can_be_redone(ctx):
+    """The fold's wait for the host's share is bounded: with the host thread holding its jobs
+    the step ends after the limit with the status raised (the host's share left out); once the
+    host answers again, the same position decoded again matches the oracle."""
+    kw = dict(n_layer=3, n_embd=256, n_head=8, n_head_kv=2, head_dim=64, n_expert=8, n_expert_used=2,
+              n_ff=128, n_swa=40, swa_pattern=2, n_ctx=64, seed=0x0FF2)
+    dec = Decoder(ctx, DecoderConfig(**kw, n_offload=2))
+    dec.host_experts("fraction", fraction=0.5, threads=2)
+    c, arr, keep, out_norm = host_model(dec)
+    for pos in range(3):
+        x = O.synth_normal_f32(0x2400 + pos, kw["n_embd"], 1.0)
+        dec.set_input(x)
+        dec.step()
+        assert rel_to_oracle(dec.output(), oracle_step(c, arr, out_norm, x, pos)) <= 1e-3
+    assert dec.status() == 0
+    dec.host_wait(limit_ns=5_000_000, hold=True)
+    x = O.synth_normal_f32(0x2400 + 3, kw["n_embd"], 1.0)
+    dec.set_input(x)
+    dec.step()
+    dec.output()
+    assert dec.status() & 1  # the wait ran out
+    dec.host_wait(0, hold=False)
+    dec.set_pos(3)  # decode position 3 again: its K/V entries are rewritten
+    dec.set_input(x)
+    dec.step()
+    assert rel_to_oracle(dec.output(), oracle_step(c, arr, out_norm, x, 3)) <= 1e-3
+    assert dec.status() == 0
+    dec.close()
+
+
+def test_expert_kernel_waits_that_run_out_are_reported_and_the_next_step_is_exact(ctx):
+    """The chain's expert kernels wait for one another's partial sums with a time limit: made
+    to run out (1 ms, no partial ever seen), the step returns with the status raised; reading
+    the status empties the partial buffers, and the same position decoded again gives the bits
+    of a twin decoder that never failed."""
+    kw = dict(n_layer=2, n_embd=256, n_head=8, n_head_kv=2, head_dim=64, n_expert=8, n_expert_used=2,
+              n_ff=128, n_swa=40, swa_pattern=2, n_ctx=64, seed=0x0FF3)
+    dec, twin = Decoder(ctx, DecoderConfig(**kw)), Decoder(ctx, DecoderConfig(**kw))
+    xs = [O.synth_normal_f32(0x2500 + p, kw["n_embd"], 1.0) for p in range(4)]
+    for pos in range(2):
+        for d in (dec, twin):
+            d.set_input(xs[pos])
+            d.step()
+    dec.set_wait(1_000_000, phantom=1)
+    dec.set_input(xs[2])
+    dec.step()
+    dec.output()
+    assert dec.status() & 1
+    dec.set_wait(0, phantom=0)
+    dec.set_pos(2)
+    for pos in (2, 3):
+        for d in (dec, twin):
+            d.set_input(xs[pos])
+            d.step()
+        assert np.array_equal(dec.output().view(np.uint32), twin.output().view(np.uint32)), pos
+    assert dec.status() == 0 and twin.status() == 0
+    dec.close()
+    twin.close()
+
+
+@pytest.mark.parametrize("qk,step_kernel", [(1, False), (0, True)])
+def test_qk_norm_and_the_output_head_match_the_oracle(ctx, qk, step_kernel):
+    """The decoder ops beside the hot path (moe.rs:1961-1985 QK-norm per head before RoPE, in
+    the Q/K/V kernel's epilogue; moe.rs:2434-2437 the output head on the normalised state) against
+    the oracle: the hidden state at the decoder's bound (1e-3) and the logits within 1e-3 of their
+    largest magnitude, through the kernel chain (QK-norm) and after the persistent kernel."""
+    from decoder_oracle import oracle_logits
+
+    cfg = DecoderConfig(n_layer=3, n_embd=256, n_head=8, n_head_kv=2, head_dim=64, n_expert=8,
+                        n_expert_used=2, n_ff=128, n_swa=40, swa_pattern=2, n_ctx=96, seed=0x9C0D,
+                        has_qk_norm=qk, n_vocab=512)
+    dec = Decoder(ctx, cfg)
+    assert dec.has_step_kernel() == (not qk)  # the persistent kernel has no QK-norm
+    if step_kernel:
+        dec.use_step_kernel(True)
+    c, arr, keep, out_norm = host_model(dec)
+    worst = worst_l = 0.0
+    for pos in range(45):  # past the 40-key window
+        x = O.synth_normal_f32(0x2600 + pos, cfg.n_embd, 1.0)
+        dec.set_input(x)
+        dec.step()
+        want = oracle_step(c, arr, out_norm, x, pos)
+        worst = max(worst, rel_to_oracle(dec.output(), want))
+        lw = oracle_logits(c, dec, want)
+        worst_l = max(worst_l, float(np.max(np.abs(dec.logits() - lw)) / np.max(np.abs(lw))))
+    print(f"qk_norm={qk} step_kernel={step_kernel}: 45 tokens, hidden {worst:.3e}, logits {worst_l:.3e}")
+    assert dec.status() == 0
+    assert worst <= 1e-3 and worst_l <= 1e-3
+    dec.close()
+
+
 def _steer(dec: Decoder, layer: int, experts) -> None:
     """Make block `layer` route to `experts` whatever the activation: the router row of each
     named expert has one nonzero column, 0, whose normalised activation the step input keeps
@@ -325,8 +470,8 @@ def test_residency_cache_fetches_exactly_what_the_host_replay_predicts(ctx, sour
     assert sum(got) < steps * 2 * k  # the cache kept something
 
 
-@pytest.mark.parametrize("etype", [O.MXFP4, O.Q4_0])
-def test_batch_decoder_matches_single_stream_decoders(ctx, etype):
+@pytest.mark.parametrize("etype,qk", [(O.MXFP4, 0), (O.Q4_0, 1)])  # Q4_0 with QK-norm: the qwen3moe form
+def test_batch_decoder_matches_single_stream_decoders(ctx, etype, qk):
     """Three sequences decoded together (moearc_x_batch_decoder: tcgen05 GEMMs for the
     projections and the experts on bf16 activations, one batched attention launch) against the
     oracle's decode step run per sequence with its own KV pools, and against three single-stream
@@ -337,7 +482,7 @@ def test_batch_decoder_matches_single_stream_decoders(ctx, etype):
     from moearc_b200.decoder import BatchDecoder
 
     kw = dict(n_layer=2, n_embd=256, n_head=8, n_head_kv=2, head_dim=64, n_expert=8, n_expert_used=2, n_ff=128,
-              expert_type=etype, n_swa=0, has_sinks=0, n_ctx=96, seed=0xBA7C)
+              expert_type=etype, n_swa=0, has_sinks=0, n_ctx=96, seed=0xBA7C, has_qk_norm=qk)
     B = 3
     bd = BatchDecoder(ctx, DecoderConfig(**kw), B)
     bd.set_pos(0)
@@ -378,7 +523,7 @@ def test_batch_decoder_matches_single_stream_decoders(ctx, etype):
             worst = max(worst, float(np.max(np.abs(got[b] - want)) / np.max(np.abs(want))))
             worst_or = max(worst_or, float(np.max(np.abs(got[b] - ow)) / np.max(np.abs(ow))))
     assert bd.status() == 0
-    print(f"batch decoder etype={etype}: 3 streams x 40 tokens, max |a-b| / max|b| = {worst_or:.3e} "
+    print(f"batch decoder etype={etype} qk_norm={qk}: 3 streams x 40 tokens, max |a-b| / max|b| = {worst_or:.3e} "
           f"against the oracle, {worst:.3e} against single-stream decoders (tolerance 1e-2); "
           f"near-tie routing flips (stream: token, block, margin): {diverged}")
     assert len(diverged) <= 1

@@ -188,3 +188,55 @@ def test_opt_in_single_launch_paths_give_the_same_bits(ctx, env, monkeypatch):
         ga, gb = ctx.download(a, np.float32, n * H), ctx.download(b, np.float32, n * H)
         assert base.status() == 0 and alt.status() == 0
         assert np.array_equal(ga.view(np.uint32), gb.view(np.uint32)), (env, n)
+
+
+@pytest.mark.parametrize("wtype", [O.MXFP4, O.Q4_0])
+def test_host_packer_writes_the_device_packers_bytes(ctx, wtype):
+    """moearc_x_moe_pack_host (the host expert pool's layout source) against moearc_x_moe_pack."""
+    import ctypes as C
+
+    H, I, E = 2880, 2880, 3
+    layer, (gate, up, down, _) = make_layer(ctx, H, I, E, 2, 1, 1, wtype, 1, 0x9AC0 + wtype)
+    dev_gu = np.empty(E * layer.gu_bytes, np.uint8)
+    dev_dn = np.empty(E * layer.dn_bytes, np.uint8)
+    ctx._finish(ctx.lib.moearc_copy_d2h(ctx.raw, dev_gu.ctypes.data, layer.gateup.ptr, dev_gu.nbytes), "d2h")
+    ctx._finish(ctx.lib.moearc_copy_d2h(ctx.raw, dev_dn.ctypes.data, layer.down.ptr, dev_dn.nbytes), "d2h")
+    host_gu, host_dn = np.zeros_like(dev_gu), np.zeros_like(dev_dn)
+    rc = ctx.lib.moearc_x_moe_pack_host(C.byref(layer.desc), gate.ctypes.data, up.ctypes.data, down.ctypes.data,
+                                        E, host_gu.ctypes.data, host_dn.ctypes.data)
+    assert rc == 0
+    assert np.array_equal(host_gu, dev_gu) and np.array_equal(host_dn, dev_dn)
+    layer.close()
+
+
+@pytest.mark.parametrize("T", [1, 16])  # the decode kernels (one token) and the row kernels (64 columns)
+def test_expert_biases_match_the_oracle(ctx, T):
+    """gpt-oss's per-expert biases (moe.rs:2310-2331: gate/up after the matvecs, before the
+    activation; 2362-2372: down inside the router weighting) fused into the decode kernels,
+    against the oracle's MoE block with the same biases, at the f32 check bound."""
+    H, I, E, k = 2880, 1024, 32, 4
+    layer, host = make_layer(ctx, H, I, E, k, 2, 1, O.MXFP4, T, 0xB1A5)
+    gu_b = O.synth_normal_f32(0xB1A6, 2 * E * I, 0.5)
+    dn_b = O.synth_normal_f32(0xB1A7, E * H, 0.5)
+    layer.set_bias(ctx.upload_new(gu_b), ctx.upload_new(dn_b))
+    gate, up, down, router = host
+    x = np.stack([O.synth_normal_f32(0xB1A8 + t, H, 1.0) for t in range(T)])
+    xd, rd, od = ctx.upload_new(x), ctx.upload_new(router), ctx.alloc(4 * T * H)
+    layer.forward(xd, T, rd, od)
+    got = ctx.download(od, np.float32, T * H).reshape(T, H)
+    cfg = O.MoeCfg(H, I, E, k, 2, 1, 1.702, 7.0, O.MXFP4, 1)
+    worst = 0.0
+    for t in range(T):
+        want = np.zeros(H, np.float32)
+        rc = O.lib().or_moe_ffn_token(cfg, O.ptr(x[t]), O.ptr(router), None, O.ptr(gate), O.ptr(up), O.ptr(down),
+                                      O.ptr(gu_b[:E * I]), O.ptr(gu_b[E * I:]), O.ptr(dn_b), O.ptr(want), None, None)
+        assert rc == 0
+        worst = max(worst, rel_err(got[t], want))
+    print(f"expert biases T={T}: max rel err {worst:.3e}")
+    assert worst <= 1e-4
+    layer.set_bias(None, None)
+    layer.forward(xd, T, rd, od)
+    nob = ctx.download(od, np.float32, T * H).reshape(T, H)
+    assert not np.allclose(nob, got)  # the biases were applied, and are cleared
+    assert layer.status() == 0
+    layer.close()
