@@ -251,6 +251,13 @@ void moearc_x_prefill_destroy(moearc_x_prefill *p);
 /* Expand one block's packed banks (moearc_x_moe_pack layout, device) into the object's bf16
  * weight matrices; later forward calls use them until the next load. */
 int moearc_x_prefill_load(moearc_x_prefill *p, const void *gateup_packed, const void *down_packed);
+/* Per-expert biases for the following forward calls, as moearc_x_moe_set_bias but indexed by the
+ * object's weight blocks (the expert id after moearc_x_prefill_load; the list position after
+ * moearc_x_prefill_load_list): gate_up_bias f32 [2E][n_ff] (gate of block w at row w, up at
+ * E + w), added before the activation in the gate-up GEMM's epilogue; down_bias f32
+ * [E][n_embd], added to each expert row in the down GEMM's epilogue (inside the weighting).
+ * Device pointers (NULL: none), kept until the next call. */
+int moearc_x_prefill_set_bias(moearc_x_prefill *p, const float *gate_up_bias, const float *down_bias);
 /* out[t] = residual[t] (if not NULL) + MoE(x[t]) for t < n_tokens; x is bf16 [n_tokens][n_embd]
  * (16-byte aligned), router_w f32 [E][n_embd] (16-byte aligned), router_b [E] or NULL; out f32. */
 int moearc_x_prefill_forward(moearc_x_prefill *p, const unsigned short *x, unsigned int n_tokens,

@@ -85,6 +85,7 @@ SIGNATURES: dict[str, tuple] = {
     "moearc_x_moe_pack_host": (I, [P, P, P, P, U, P, P]),
     "moearc_x_prefill_create": (P, [P, P]),
     "moearc_x_prefill_destroy": (None, [P]),
+    "moearc_x_prefill_set_bias": (I, [P, P, P]),
     "moearc_x_prefill_load": (I, [P, P, P]),
     "moearc_x_prefill_forward": (I, [P, P, U, P, P, P, P]),
     "moearc_x_prefill_buffer": (P, [P, I]),

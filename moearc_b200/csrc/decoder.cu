@@ -547,6 +547,7 @@ moearc_x_decoder *moearc_x_decoder_create(moearc_ctx *c, const moearc_x_decoder_
         // persistent kernel on request
         const char *e = std::getenv("MOEARC_STEP_KERNEL");
         d->use_step = e && e[0] == '1';
+
     }
     return d;
 }

@@ -1101,6 +1101,7 @@ __global__ void __launch_bounds__(XW * 32, 1) k_xexpert(xexp_args a) {
             a.idx_out[i] = tb.idx[i];
             a.wts_out[i] = tb.wts[i];
         }
+
     // Work: segments (gate-up: group * ntr + tile-row; down: tile-row * G + group), each one
     // k-extent of nkt elements cut into np pieces of a.ch elements at fixed places. A warp
     // takes a contiguous run of pieces; every piece leaves its own partial, so the sums do not

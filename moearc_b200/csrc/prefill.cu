@@ -298,6 +298,11 @@ struct pf_gemm_args {
     float *y_out;       // down: [rows][n_embd] f32
     float *const *seg_y;  // down, if set: segment e's rows go to seg_y[e] + n * n_embd instead (a peer
                           // rank's memory under expert parallelism: the return leg of the exchange)
+    // per-expert biases indexed by weight block w (moe.rs:2310-2331, 2362-2372), or null:
+    // gate-up: gate rows of block w at w, up rows at n_blocks + w ([2 n_blocks][Mrows]), added
+    // before the activation; down: [n_blocks][Mrows], added to each row before the combine
+    const float *bias;
+    int n_blocks;
     int *status;
 };
 
@@ -441,6 +446,10 @@ __global__ void __launch_bounds__(192, 1) k_pf_gemm(const __grid_constant__ CUte
             const int f = mt * PF_BM + 32 * qd + lane;  // this thread's feature row
             const bool fok = f < a.Mrows;
             const uint32_t acc_base = lane_base + (uint32_t)(ab * C::ACC_COLS);
+            // this row's biases (gate-up: gate, up; down: the row's)
+            const int wblk = a.seg_w ? a.seg_w[e] : e;
+            const float bg = (a.bias && fok) ? a.bias[(size_t)wblk * a.Mrows + f] : 0.f;
+            const float bu = (MODE == 0 && a.bias && fok) ? a.bias[(size_t)(a.n_blocks + wblk) * a.Mrows + f] : 0.f;
             for (int c0 = 0; c0 < PF_BN; c0 += 16) {
                 float d[16];
                 tc::tmem_ld16(acc_base + c0, d);
@@ -451,14 +460,15 @@ __global__ void __launch_bounds__(192, 1) k_pf_gemm(const __grid_constant__ CUte
                     for (int j = 0; j < 16; ++j) {
                         const int n = nt * PF_BN + c0 + j;
                         if (fok && n < n_rows)
-                            a.act_out[(size_t)(seg + n) * a.Mrows + f] = f32_to_bf16_rn(act_fn(a.act, d[j], u[j], a.alpha, a.limit));
+                            a.act_out[(size_t)(seg + n) * a.Mrows + f] =
+                                f32_to_bf16_rn(act_fn(a.act, d[j] + bg, u[j] + bu, a.alpha, a.limit));
                     }
                 } else {
                     float *ybase = a.seg_y ? a.seg_y[e] : a.y_out + (size_t)seg * a.Mrows;
 #pragma unroll
                     for (int j = 0; j < 16; ++j) {
                         const int n = nt * PF_BN + c0 + j;
-                        if (fok && n < n_rows) ybase[(size_t)n * a.Mrows + f] = d[j];
+                        if (fok && n < n_rows) ybase[(size_t)n * a.Mrows + f] = d[j] + bg;
                     }
                 }
             }
@@ -734,6 +744,10 @@ __global__ void __launch_bounds__(pf4_cfg<MODE, WT>::THREADS, 1)
             const int f = mt * PF_BM + 32 * qd + lane;
             const bool fok = f < a.Mrows;
             const uint32_t acc_base = lane_base + (uint32_t)(ab * C::ACC_COLS);
+            // this row's biases (gate-up: gate, up; down: the row's)
+            const int wblk = a.seg_w ? a.seg_w[e] : e;
+            const float bg = (a.bias && fok) ? a.bias[(size_t)wblk * a.Mrows + f] : 0.f;
+            const float bu = (MODE == 0 && a.bias && fok) ? a.bias[(size_t)(a.n_blocks + wblk) * a.Mrows + f] : 0.f;
             for (int c0 = 0; c0 < PF_BN; c0 += 16) {
                 float d[16];
                 tc::tmem_ld16(acc_base + c0, d);
@@ -745,14 +759,14 @@ __global__ void __launch_bounds__(pf4_cfg<MODE, WT>::THREADS, 1)
                         const int n = nt * PF_BN + c0 + j;
                         if (fok && n < n_rows)
                             a.act_out[(size_t)(seg + n) * a.Mrows + f] =
-                                __half_as_ushort(__float2half_rn(act_fn(a.act, d[j], u[j], a.alpha, a.limit)));
+                                __half_as_ushort(__float2half_rn(act_fn(a.act, d[j] + bg, u[j] + bu, a.alpha, a.limit)));
                     }
                 } else {
                     float *ybase = a.seg_y ? a.seg_y[e] : a.y_out + (size_t)seg * a.Mrows;
 #pragma unroll
                     for (int j = 0; j < 16; ++j) {
                         const int n = nt * PF_BN + c0 + j;
-                        if (fok && n < n_rows) ybase[(size_t)n * a.Mrows + f] = d[j];
+                        if (fok && n < n_rows) ybase[(size_t)n * a.Mrows + f] = d[j] + bg;
                     }
                 }
             }
@@ -881,6 +895,9 @@ struct moearc_x_prefill {
     float **seg_y = nullptr;
     const uint16_t *route_x = nullptr;  // the activations of the last route_begin call
     int route_T = 0;
+    // per-expert biases (moearc_x_prefill_set_bias), indexed by weight block: gate-up
+    // [2E][I] (gate of block w at w, up at E + w), down [E][H]; null: none
+    const float *bias_gu = nullptr, *bias_dn = nullptr;
 };
 
 namespace {
@@ -916,9 +933,12 @@ bool ensure_4bit(moearc_x_prefill *p) {
 }
 
 // The grouped GEMM of one matrix set (MODE 0 gate-up, 1 down) on whichever weight form is loaded.
-int launch_gemm(moearc_x_prefill *p, int mode, const pf_gemm_args &g, const CUtensorMap &xmap) {
+int launch_gemm(moearc_x_prefill *p, int mode, const pf_gemm_args &g_in, const CUtensorMap &xmap) {
     moearc_ctx *c = p->c;
     cudaStream_t st = c->stream;
+    pf_gemm_args g = g_in;
+    g.bias = mode == 0 ? p->bias_gu : p->bias_dn;  // indexed by weight block (E of them)
+    g.n_blocks = p->E;
     if (!p->mode4) {
         if (mode == 0) k_pf_gemm<0><<<c->sm_count, 192, pf_cfg<0>::SMEM, st>>>(p->map_wgu, xmap, g);
         else k_pf_gemm<1><<<c->sm_count, 192, pf_cfg<1>::SMEM, st>>>(p->map_wdn, xmap, g);
@@ -1146,6 +1166,14 @@ int moearc_x_prefill_load4(moearc_x_prefill *p, const void *gateup_packed, const
     std::vector<int> all(p->E);
     for (int e = 0; e < p->E; ++e) all[e] = e;
     return moearc_x_prefill_load4_list(p, gateup_packed, down_packed, all.data(), (unsigned)p->E);
+}
+
+int moearc_x_prefill_set_bias(moearc_x_prefill *p, const float *gate_up_bias, const float *down_bias) {
+    if (!p) return ERR;
+    if ((reinterpret_cast<uintptr_t>(gate_up_bias) | reinterpret_cast<uintptr_t>(down_bias)) & 3) return ERR_ARG;
+    p->bias_gu = gate_up_bias;
+    p->bias_dn = down_bias;
+    return OK;
 }
 
 int moearc_x_prefill_load(moearc_x_prefill *p, const void *gateup_packed, const void *down_packed) {

@@ -52,6 +52,7 @@ class MoeLayer:
         rc = self.ctx.lib.moearc_x_moe_set_bias(self.h, gate_up_bias.ptr if gate_up_bias is not None else None,
                                                 down_bias.ptr if down_bias is not None else None)
         self.ctx._finish(rc, "moe_set_bias")
+        self._bias = (gate_up_bias, down_bias)  # the library keeps the pointers: keep the buffers alive
 
     def forward(self, x: DeviceBuffer, n_tokens: int, router_w: DeviceBuffer, out: DeviceBuffer,
                 router_b: DeviceBuffer | None = None, residual: DeviceBuffer | None = None) -> None:
@@ -95,6 +96,13 @@ class MoePrefill:
         if self.h:
             self.ctx.lib.moearc_x_prefill_destroy(self.h)
             self.h = None
+
+    def set_bias(self, gate_up_bias: DeviceBuffer | None, down_bias: DeviceBuffer | None) -> None:
+        """Per-expert biases (indexed by weight block) for the following forward calls."""
+        rc = self.ctx.lib.moearc_x_prefill_set_bias(self.h, gate_up_bias.ptr if gate_up_bias is not None else None,
+                                                    down_bias.ptr if down_bias is not None else None)
+        self.ctx._finish(rc, "prefill_set_bias")
+        self._bias = (gate_up_bias, down_bias)  # the library keeps the pointers
 
     def load(self, gateup: DeviceBuffer, down: DeviceBuffer) -> None:
         """Expand packed banks (MoeLayer.pack's output) into the bf16 weights the GEMMs read."""

@@ -331,3 +331,36 @@ def test_peer_memory_exchange_gives_the_same_bits(ctx, world):
         d["pf"].close()
     whole.close()
     packer.close()
+
+
+@pytest.mark.parametrize("four_bit", [False, True])
+def test_expert_biases_in_the_gemm_epilogues_match_the_oracle(ctx, four_bit):
+    """gpt-oss's per-expert biases (moe.rs:2310-2331 before the activation, 2362-2372 inside the
+    weighting) added in the gate-up and down GEMM epilogues, bf16 and 4-bit weight forms, against
+    the oracle's MoE block with the same biases at the bf16 bound."""
+    H, I, E, k, T = 2880, 2880, 32, 4, 40
+    pf, packer, host = build(ctx, H, I, E, k, 2, 1, O.MXFP4, T, 0x9F21)
+    if four_bit:
+        pf.load4(packer.gateup, packer.down)
+    gu_b = O.synth_normal_f32(0x9F22, 2 * E * I, 0.5)
+    dn_b = O.synth_normal_f32(0x9F23, E * H, 0.5)
+    pf.set_bias(ctx.upload_new(gu_b), ctx.upload_new(dn_b))
+    xb = O.synth_normal_bf16(0x9F24, T * H, 1.0)
+    out = ctx.alloc_n(np.float32, T * H)
+    pf.forward(ctx.upload_new(xb), T, ctx.upload_new(host[3]), out)
+    got = ctx.download(out, np.float32, T * H).reshape(T, H)
+    assert pf.status() == 0
+    gate, up, down, router = host
+    cfg = O.MoeCfg(H, I, E, k, 2, 1, 1.702, 7.0, O.MXFP4, 1)
+    x32 = O.bf16_to_f32(xb).reshape(T, H)
+    want = np.zeros((T, H), np.float32)
+    for t in range(T):
+        xt = np.ascontiguousarray(x32[t])
+        assert O.lib().or_moe_ffn_token(cfg, O.ptr(xt), O.ptr(router), None, O.ptr(gate), O.ptr(up), O.ptr(down),
+                                        O.ptr(gu_b[:E * I]), O.ptr(gu_b[E * I:]), O.ptr(dn_b), O.ptr(want[t]),
+                                        None, None) == 0
+    worst = bf16_err(got, want)
+    print(f"prefill expert biases four_bit={four_bit}: max rel err {worst:.3e} over {T} tokens (bound 1e-2)")
+    assert worst <= 1e-2
+    pf.close()
+    packer.close()
