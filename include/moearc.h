@@ -533,6 +533,14 @@ int moearc_x_gguf_tensor_at(moearc_x_gguf *g, unsigned long long i, moearc_x_ggu
 int moearc_x_gguf_slice_last(moearc_x_gguf *g, const char *name, unsigned long long index,
                              moearc_x_gguf_tensor *out);
 
+/* ---- tensor-core peaks (mma_peak.cu; no reference counterpart) ---------------------------
+ * Dense throughput of one MMA kind measured with the library's own tcgen05 loop (one CTA per
+ * SM, 128 x 256 MMAs from shared memory into TMEM, timed by the slowest SM): kind 0 kind::f16
+ * bf16, 1 kind::mxf8f6f4 E4M3 x E4M3, 2 kind::mxf4 E2M1 x E2M1, 3 kind::mxf8f6f4 E4M3 x E2M1
+ * (block-scaled kinds with E8M0 scales per 32). iters MMAs per SM (1 .. 2^20); TFLOP/s into
+ * *tflops. Synchronises the stream. */
+int moearc_x_mma_peak(moearc_ctx *c, int kind, int iters, double *tflops);
+
 /* ---- decode attention without allocation (no counterpart in the reference) ----------------
  * Same arguments, result and return codes as moearc_attn_decode, but the split-K partials live
  * in a fixed per-device array of MOEARC_X_ATTN_STATIC_SCRATCH_BYTES compiled into the library,

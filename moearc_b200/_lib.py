@@ -150,6 +150,7 @@ SIGNATURES: dict[str, tuple] = {
     "moearc_x_gguf_find": (I, [P, C.c_char_p, P]),
     "moearc_x_gguf_tensor_at": (I, [P, C.c_ulonglong, P, C.POINTER(C.c_char_p)]),
     "moearc_x_gguf_slice_last": (I, [P, C.c_char_p, C.c_ulonglong, P]),
+    "moearc_x_mma_peak": (I, [P, I, I, C.POINTER(C.c_double)]),
     "moearc_x_attn_decode_static": (I, [P, P, P, P, P, P, P, UL, UL, UL, UL, UL, UL, F, U]),
 }
 

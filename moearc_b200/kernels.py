@@ -325,6 +325,16 @@ class Context:
               hi: int = -4) -> None:
         self._finish(self.lib.moearc_x_synth(self.raw, dst.ptr, n, kind, seed, sigma, lo, hi), "synth")
 
+    MMA_KINDS = {"bf16": 0, "mxf8": 1, "mxf4": 2, "mxf8_e2m1": 3}
+
+    def mma_peak(self, kind: str, iters: int = 32768) -> float:
+        """Dense TFLOP/s of one tensor-core MMA kind on this device, from the library's own
+        tcgen05 loop: "bf16" (kind::f16), "mxf8" (E4M3 x E4M3), "mxf4" (E2M1 x E2M1),
+        "mxf8_e2m1" (E4M3 x E2M1), the block-scaled kinds with E8M0 scales per 32."""
+        v = C.c_double()
+        self._finish(self.lib.moearc_x_mma_peak(self.raw, self.MMA_KINDS[kind], iters, C.byref(v)), "mma_peak")
+        return v.value
+
     def timer_start(self) -> None:
         self._finish(self.lib.moearc_x_timer_start(self.raw), "timer")
 

@@ -542,3 +542,13 @@ def test_split_k_attention_at_model_geometry_with_sinks(ctx, geom):
     got = run_attn(ctx, q, dk, dv, table, sinks, H, KVH, D, begin, N, PT, scale, O.BF16)
     want = oracle_attn(q, kh, vh, table, sinks, H, KVH, D, begin, N, PT, scale, O.BF16)
     report(f"split-K attention {geom}", rel_err(got, want), 1e-4)
+
+
+def test_tensor_core_peaks_of_the_block_scaled_kinds(ctx):
+    """The library's own tcgen05 loop times each MMA kind: every rate is finite and positive, and
+    the block-scaled kinds run at least as fast as bf16 (fp8 about twice, fp4 about four times on
+    B200)."""
+    rates = {k: ctx.mma_peak(k) for k in ("bf16", "mxf8", "mxf4", "mxf8_e2m1")}
+    print("tensor-core peaks, TFLOP/s:", {k: round(v, 1) for k, v in rates.items()})
+    assert all(np.isfinite(v) and v > 0 for v in rates.values())
+    assert rates["mxf8"] >= 1.5 * rates["bf16"] and rates["mxf4"] >= 1.5 * rates["mxf8"]
