@@ -472,6 +472,8 @@ def prefill_bench(args) -> dict:
     ctx.timer_start()
     if args.weights == "4bit":
         pf.load4(packer.gateup, packer.down)
+    elif args.weights == "fp8":
+        pf.load8(packer.gateup, packer.down)
     else:
         pf.load(packer.gateup, packer.down)
     load_ms = ctx.timer_stop()
@@ -611,6 +613,14 @@ def prefill_main(args) -> None:
     peaks = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json"))) if os.path.exists(
         os.path.join(ROOT, "MEASURED_PEAKS.json")) else {}
     peak = float(peaks.get("bf16_tflops", 1590.0))
+    peak_kind = "measured bf16 (MEASURED_PEAKS.json)" if peaks else "fallback"
+    if args.weights == "fp8":
+        # the block-scaled FP8 MMA's peak, measured in this run by the library's own tcgen05 loop
+        from moearc_b200 import Context
+        pc = Context()
+        peak = pc.mma_peak("mxf8")
+        pc.close()
+        peak_kind = "measured in this run: kind::mxf8f6f4 E4M3 tcgen05 loop (moearc_x_mma_peak)"
     gu_ms = r["kernel_ms"]["gemm_gate_up"]
     gu_tflops = 4.0 * T * k * H * I / (gu_ms / 1000.0) / 1e12
     value = flops / (r["ms_step"] / 1000.0) / 1e12
@@ -621,14 +631,18 @@ def prefill_main(args) -> None:
         "ms_per_step": r["ms_step"], "tokens_per_s": T / (r["ms_step"] / 1000.0), "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": ("bf16 operands, f32 accumulate (MXFP4 weights staged at 4 bits, expanded in shared memory)"
                                                            if args.weights == "4bit" else
+                                                           "MXFP8 (E4M3 x E4M3, E8M0 per 32) operands, f32 accumulate: the perf mode"
+                                                           if args.weights == "fp8" else
                                                            "bf16 operands, f32 accumulate (MXFP4 weights expanded to bf16)"),
         "data": "synthetic (seeded MXFP4 experts, bf16 N(0,1) activations, Zipf(1.1) router bias)",
         "config": {"workload": f"configs[3] MoE block: {T} tokens (8 x 4096 at full size), {r['E']} experts top-4, 2880 x 2880",
                    "tokens": T, "expert_load_max": int(cnt.max()), "expert_load_mean": float(cnt.mean()),
                    "l2": "operands (1.5 GB activations, 6.4 GB bf16 weights) far exceed the 126 MB L2"},
-        "roofline": {"bound": "tensor", "kernel": "gate-up grouped GEMM (tcgen05 kind::f16, SwiGLU epilogue)",
+        "roofline": {"bound": "tensor", "kernel": ("gate-up grouped GEMM (tcgen05 kind::mxf8f6f4.block_scale, SwiGLU + "
+                                                   "MXFP8 quantisation epilogue)" if args.weights == "fp8" else
+                                                   "gate-up grouped GEMM (tcgen05 kind::f16, SwiGLU epilogue)"),
                      "achieved": gu_tflops, "peak": peak, "unit": "TFLOP/s", "frac": gu_tflops / peak,
-                     "peak_kind": "measured bf16 (MEASURED_PEAKS.json)" if peaks else "fallback", "traffic": None},
+                     "peak_kind": peak_kind, "traffic": None},
         "kernel_ms": r["kernel_ms"], "weight_load_ms": r["load_ms"], "weights": args.weights,
         "e2e": {"value": flops * args.steps / r["e2e_s"] / 1e12, "unit": "TFLOP/s",
                 "h2d_bytes_per_step": T * H * 2, "d2h_bytes_per_step": T * H * 4},
@@ -774,8 +788,9 @@ def main() -> None:
     ap.add_argument("--batch", type=int, default=64, help="qwen3: concurrent streams (configs[4]: 64)")
     ap.add_argument("--exchange", default="peer", choices=["peer", "nccl"],
                     help="prefill on several GPUs: rows exchanged by the kernels over peer memory, or NCCL all-to-all")
-    ap.add_argument("--weights", default="bf16", choices=["4bit", "bf16"],
-                    help="prefill: expert weights staged at 4 bits (expanded in shared memory) or expanded to bf16")
+    ap.add_argument("--weights", default="bf16", choices=["4bit", "bf16", "fp8"],
+                    help="prefill: expert weights staged at 4 bits (expanded in shared memory), expanded to bf16, "
+                         "or the MXFP8 perf mode (E4M3 weights and MXFP8 activations on the block-scaled FP8 MMA)")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--layers", type=int, default=0,

@@ -251,6 +251,14 @@ void moearc_x_prefill_destroy(moearc_x_prefill *p);
 /* Expand one block's packed banks (moearc_x_moe_pack layout, device) into the object's bf16
  * weight matrices; later forward calls use them until the next load. */
 int moearc_x_prefill_load(moearc_x_prefill *p, const void *gateup_packed, const void *down_packed);
+/* The MXFP8 perf mode (MXFP4 experts only): the packed banks expanded once to E4M3 elements (each
+ * E2M1 value exactly) with their E8M0 block scales, and following forward calls run the
+ * block-scaled FP8 GEMMs (tcgen05.mma kind::mxf8f6f4) on activations quantised to MXFP8 per 32
+ * along K (scale 2^X, X the smallest exponent keeping the block within E4M3's 448; elements round
+ * to nearest even) — the expert rows before gate-up and the SwiGLU output before down. Routing
+ * is unchanged (bit-exact). -2 for Q4_0 experts. The expert-parallel steps
+ * (moearc_x_prefill_route / _experts*) refuse this form; any other load leaves it. */
+int moearc_x_prefill_load8(moearc_x_prefill *p, const void *gateup_packed, const void *down_packed);
 /* Per-expert biases for the following forward calls, as moearc_x_moe_set_bias but indexed by the
  * object's weight blocks (the expert id after moearc_x_prefill_load; the list position after
  * moearc_x_prefill_load_list): gate_up_bias f32 [2E][n_ff] (gate of block w at row w, up at

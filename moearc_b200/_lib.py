@@ -86,6 +86,7 @@ SIGNATURES: dict[str, tuple] = {
     "moearc_x_prefill_create": (P, [P, P]),
     "moearc_x_prefill_destroy": (None, [P]),
     "moearc_x_prefill_set_bias": (I, [P, P, P]),
+    "moearc_x_prefill_load8": (I, [P, P, P]),
     "moearc_x_prefill_load": (I, [P, P, P]),
     "moearc_x_prefill_forward": (I, [P, P, U, P, P, P, P]),
     "moearc_x_prefill_buffer": (P, [P, I]),

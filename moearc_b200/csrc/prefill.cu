@@ -26,6 +26,7 @@
 // Weights: moearc_x_prefill_load expands a block's packed banks (moearc_x_moe_pack layout) into
 // bf16 K-major matrices [E][2][n_ff][n_embd] (gate block, up block) and [E][n_embd][n_ff].
 #include <cuda_bf16.h>
+#include <cuda_fp8.h>
 
 #include <algorithm>
 #include <cmath>
@@ -145,12 +146,12 @@ __global__ void __launch_bounds__(256) k_pf_topk(pf_route_args a) {
 
 // Row offsets (off[e], off[E] = T K), 128-row tile offsets (toff[e], toff[E] = all tiles) and
 // zeroed cursors. One CTA; E <= 1024.
-__global__ void k_pf_scan(const int *cnt, int E, int *off, int *toff, int *cursor) {
+__global__ void k_pf_scan(const int *cnt, int E, int *off, int *toff, int *cursor, int bn = PF_BN) {
     __shared__ int s_c[1024], s_t[1024];
     const int e = threadIdx.x;
     const int c = e < E ? cnt[e] : 0;
     s_c[e] = c;
-    s_t[e] = (c + PF_BN - 1) / PF_BN;
+    s_t[e] = (c + bn - 1) / bn;
     __syncthreads();
     // inclusive scans (Hillis-Steele; E is small)
     for (int d = 1; d < (int)blockDim.x; d <<= 1) {
@@ -562,6 +563,397 @@ __global__ void k_pf_pack4(const uint8_t *bank, const int *experts, int n_exp, i
     for (int i = 0; i < 2 * sb; ++i) out[TC4_NIB + row * 2 * sb + i] = sc[i];
 }
 
+// ---- MXFP8 mode: block-scaled FP8 GEMMs (tcgen05.mma kind::mxf8f6f4) ----------------------
+//
+// A perf mode beside the exact bf16 one. Weights: MXFP4 elements are E2M1 values, each exactly an
+// E4M3 value, and their E8M0 block scale is the MMA's block scale, so the weights enter the MMA
+// exactly (1 byte an element, the scale a byte per 32). Activations (the expert rows and the
+// SwiGLU output) are quantised to MXFP8 per 32 along K: scale 2^X with X the smallest exponent
+// that keeps the block's largest magnitude within E4M3's 448 (no saturation), elements E4M3 round
+// to nearest even. The quantisation of the activations is the mode's only change of arithmetic;
+// the oracle restates it (or_moe_ffn_token_mx8).
+//
+// Scale factors in TMEM (measured on B200): for M = 128, row m's scale for the MMA's K block is
+// byte sf_id of lane m, column base + m / 32; for N <= 128, column n's at lane n % 32, column
+// base + n / 32. tcgen05.cp.32x128b.warpx4 copies a 32-row x 16-byte shared-memory block to every
+// lane quarter (row i, word c -> lane 32 q + i, column c), so one 512-byte block — row i, word
+// c = the 4 K blocks' scales of matrix row 32 c + i — feeds one operand's scales for a 128-wide
+// K stage (sf_id = K block 0..3).
+constexpr int PF8_BN = 96, PF8_BK = 128;           // token rows per tile; K elements (bytes) a stage
+constexpr int PF8_ATILE = PF_BM * PF8_BK;          // 16 KB: 128 feature rows x 128 E4M3
+constexpr int PF8_BTILE = PF8_BN * PF8_BK;         // 12 KB
+constexpr int PF8_SFBLK = 512;                     // one 32 x 16-byte scale block
+
+template <int MODE>
+struct pf8_cfg {
+    static constexpr int NA = MODE == 0 ? 2 : 1;
+    static constexpr int STAGE = ((NA * PF8_ATILE + PF8_BTILE + (NA + 1) * PF8_SFBLK + 1023) / 1024) * 1024;
+    static constexpr int STAGES = MODE == 0 ? 4 : 6;
+    static constexpr int SMEM = STAGES * STAGE + 1024;
+    static constexpr int ACC_COLS = NA * PF8_BN;
+    static constexpr int SF_BASE = 2 * ACC_COLS;    // after the two accumulator sets
+    static constexpr int SF_SLOT = (NA + 1) * 4;    // one stage's scale columns (two slots alternate)
+    static constexpr int TMEM_COLS = MODE == 0 ? 512 : 256;
+    static_assert(SF_BASE + 2 * SF_SLOT <= TMEM_COLS, "TMEM columns");
+};
+
+// Scales are stored the way a stage consumes them: per (row tile, K stage) one 512-byte block,
+// row i (16 bytes) word c = the 4 scale bytes (K blocks 4 kb .. 4 kb + 3) of tile row 32 c + i.
+// A stage then fetches each operand's scales with one bulk copy. Byte offset of (tile row r,
+// 32-element K block b) inside tile t of a matrix with kbs stages: ((t kbs + b / 4) 512 + (r % 32)
+// 16 + (r / 32) 4 + b % 4. Unwritten bytes (rows past the matrix, K blocks past its end) hold
+// 127, a scale of 1 on zeros.
+__host__ __device__ __forceinline__ size_t sf_at(long tile, int kbs, int r, int b) {
+    return ((size_t)tile * kbs + (b >> 2)) * PF8_SFBLK + (size_t)(r & 31) * 16 + (size_t)(r >> 5) * 4 + (b & 3);
+}
+__host__ __device__ __forceinline__ int sf_stages(int k) { return (k + PF8_BK - 1) / PF8_BK; }
+
+// MXFP8 scale exponent of a block whose largest magnitude is amax: the smallest X with
+// amax / 2^X <= 448 (448 = 1.75 x 2^8): X = e - 8 if the significand of amax is at most 1.75,
+// else e - 7. 0 for a zero block.
+__device__ __forceinline__ int mx8_exp(float amax) {
+    const uint32_t b = __float_as_uint(amax);
+    if (amax == 0.f) return 0;
+    const int e = (int)((b >> 23) & 0xFF) - 127;
+    return max(-127, e - 8 + (((b & 0x7FFFFF) > 0x600000u) ? 1 : 0));
+}
+
+__device__ __forceinline__ uint8_t to_e4m3(float v) {
+    return (uint8_t)__nv_cvt_float_to_fp8(v, __NV_SATFINITE, __NV_E4M3);
+}
+
+// 2^-X for X in [-127, 126], built from the exponent bits: v * pow2_neg(X) is v scaled exactly
+// (rounded once, as ldexpf would, when the product leaves the normal range).
+__device__ __forceinline__ float pow2_neg(int X) { return __int_as_float((127 - X) << 23); }
+
+// One warp per packed tile (16 rows x 64 columns): MXFP4 -> E4M3 rows dst[E][mats][R][Kc] and
+// the scale bytes (the e8m0 byte itself: E2M1 value x 2^(e - 127)) in blocks per (expert, matrix,
+// 128-row tile, K stage).
+__global__ void __launch_bounds__(256) k_pf_unpack8(const uint8_t *bank, int E, int R, int Kc, int mats, int tile_bytes,
+                                                    uint8_t *dst, uint8_t *sdst) {
+    // E2M1 code -> E4M3 byte of the same value: 0, 0.5 = 0x30, and m / 2 = (m >= 2) 0x30 + 4 m
+    auto e4 = [](uint32_t code) -> uint32_t {
+        const uint32_t m = code & 7;
+        return ((code & 8) << 4) | (m == 0 ? 0u : (m == 1 ? 0x30u : 0x30u + 4u * m));
+    };
+    const int lane = threadIdx.x & 31, r = lane >> 2, q = lane & 3;
+    const long ntr = R / 16, nkt = Kc / 64;
+    const long per_e = ntr * nkt * mats;
+    const long g = (long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    if (g >= (long)E * per_e) return;
+    const int e = (int)(g / per_e);
+    const long rem = g - e * per_e;
+    const long pair = rem / mats;
+    const int mat = (int)(rem - pair * mats);
+    const int tr = (int)(pair / nkt), kt = (int)(pair - (long)tr * nkt);
+    const uint8_t *tile = bank + (size_t)g * tile_bytes;
+    const uint4 w = *reinterpret_cast<const uint4 *>(tile + lane * 16);
+    const size_t mbase = ((size_t)e * mats + mat) * (size_t)R;
+    const uint32_t words[4] = {w.x, w.y, w.z, w.w};  // (row r, blk 0), (r+8, 0), (r, 1), (r+8, 1)
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const int row = tr * 16 + r + ((i & 1) ? 8 : 0), blk = i >> 1;
+        uint8_t *d = dst + (mbase + row) * (size_t)Kc + kt * 64 + blk * 32;
+        uint32_t lo = 0, hi = 0;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const uint32_t byte = (words[i] >> (8 * j)) & 0xFF;
+            lo |= e4(byte & 15) << (8 * j);
+            hi |= e4(byte >> 4) << (8 * j);
+        }
+        *reinterpret_cast<uint32_t *>(d + 4 * q) = lo;        // elements 4q .. 4q + 3
+        *reinterpret_cast<uint32_t *>(d + 16 + 4 * q) = hi;   // elements 16 + 4q ..
+        if (q == 0)
+            sdst[sf_at(((long)e * mats + mat) * ((R + PF_BM - 1) / PF_BM) + row / PF_BM, sf_stages(Kc), row % PF_BM,
+                       kt * 2 + blk)] = tile[512 + 4 * r + i];
+    }
+}
+
+// k_pf_scatter with MXFP8 rows: one warp per (token, choice), its row as k_pf_scatter places it;
+// each 32-element block of the token's bf16 activation quantised (x8 [rows][H] E4M3; the scales
+// in the blocks of the row's 96-row tile, toff the segments' tile offsets).
+__global__ void __launch_bounds__(256) k_pf_scatter8(const uint16_t *x, const unsigned *idx, const int *epos, int T,
+                                                     int K, int H, const int *off, const int *toff, int *cursor,
+                                                     int *perm, uint8_t *x8, uint8_t *sx) {
+    const int lane = threadIdx.x & 31;
+    const long p = (long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    if (p >= (long)T * K) return;
+    int row = 0, pos = 0, n = 0;
+    if (lane == 0) {
+        pos = epos[idx[p]];
+        n = atomicAdd(cursor + pos, 1);
+        row = off[pos] + n;
+        perm[p] = row;
+    }
+    row = __shfl_sync(0xffffffffu, row, 0);
+    pos = __shfl_sync(0xffffffffu, pos, 0);
+    n = __shfl_sync(0xffffffffu, n, 0);
+    const long tile = toff[pos] + n / PF8_BN;
+    const int kbs = sf_stages(H);
+    const uint4 *src = reinterpret_cast<const uint4 *>(x + (size_t)(p / K) * H);
+    // lane l takes elements 8 l .. 8 l + 7 of each 256-element chunk: four lanes form a block
+    for (int c0 = 0; c0 < H; c0 += 256) {
+        const int e0 = c0 + 8 * lane;
+        const bool live = e0 < H;
+        float v[8];
+        if (live) {
+            const uint4 w = __ldg(src + e0 / 8);
+            const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                v[2 * j] = __uint_as_float(ws[j] << 16);
+                v[2 * j + 1] = __uint_as_float(ws[j] & 0xFFFF0000u);
+            }
+        } else {
+#pragma unroll
+            for (int j = 0; j < 8; ++j) v[j] = 0.f;
+        }
+        float m = 0.f;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) m = fmaxf(m, fabsf(v[j]));
+        m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 1));
+        m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 2));
+        const int X = mx8_exp(m);
+        if (live) {
+            uint32_t lo = 0, hi = 0;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                lo |= (uint32_t)to_e4m3(v[j] * pow2_neg(X)) << (8 * j);
+                hi |= (uint32_t)to_e4m3(v[4 + j] * pow2_neg(X)) << (8 * j);
+            }
+            *reinterpret_cast<uint2 *>(x8 + (size_t)row * H + e0) = make_uint2(lo, hi);
+            if ((lane & 3) == 0) sx[sf_at(tile, kbs, n % PF8_BN, e0 / 32)] = (uint8_t)(127 + X);
+        }
+    }
+}
+
+struct pf8_args {
+    int Mrows, K, E;
+    const int *off, *toff, *seg_w;
+    int act;
+    float alpha, limit;
+    const uint8_t *sfw;    // weight scale blocks [expert][NA][128-row tile][K stage]
+    const uint8_t *sfx;    // activation scale blocks [96-row tile][K stage]
+    uint8_t *act8;         // gate-up: E4M3 activations [rows][Mrows]
+    uint8_t *sact;         // gate-up: their scale blocks [96-row tile][Mrows stage]
+    float *y_out;          // down: [rows][Mrows] f32
+    const float *bias;     // as pf_gemm_args
+    int n_blocks;
+    int *status;
+};
+
+// Shared-memory descriptor of a 32-row x 16-byte block (no swizzle: rows 16 bytes apart, 8-row
+// core matrices 128 bytes apart), the source of tcgen05.cp.32x128b.
+__device__ __forceinline__ uint64_t desc_sfblk(uint32_t addr) {
+    return (uint64_t)((addr >> 4) & 0x3FFF) | ((uint64_t)(128 >> 4) << 32) | ((uint64_t)1 << 46);
+}
+
+// Block-scaled instruction descriptor (kind::mxf8f6f4): A and B E4M3 (formats 0), K-major, N >> 3
+// in bits 17-22, E8M0 scales (bit 23), M >> 4 in bits 24-28, scale ids for B (bits 4-5) and A
+// (bits 29-30).
+__host__ __device__ constexpr uint32_t idesc_mx8(int M, int N, int sf_id) {
+    return ((uint32_t)sf_id << 4) | ((uint32_t)(N >> 3) << 17) | (1u << 23) | ((uint32_t)(M >> 4) << 24) |
+           ((uint32_t)sf_id << 29);
+}
+
+__device__ __forceinline__ void mma_mx8(uint32_t d, uint64_t da, uint64_t db, uint32_t idesc, uint32_t sfa, uint32_t sfb,
+                                        uint32_t acc) {
+    asm volatile(
+        "{ .reg .pred p; setp.ne.b32 p, %6, 0;\n"
+        " tcgen05.mma.cta_group::1.kind::mxf8f6f4.block_scale [%0], %1, %2, %3, [%4], [%5], p; }" ::"r"(d),
+        "l"(da), "l"(db), "r"(idesc), "r"(sfa), "r"(sfb), "r"(acc));
+}
+
+__device__ __forceinline__ void cp_sf(uint32_t taddr, uint32_t saddr) {
+    asm volatile("tcgen05.cp.cta_group::1.32x128b.warpx4 [%0], %1;" ::"r"(taddr), "l"(desc_sfblk(saddr)));
+}
+
+// The MXFP8 GEMMs, laid out as k_pf_gemm (persistent, warp 0 producer and TMEM owner, warp 1 MMA
+// issuer, two accumulator sets) but with eight epilogue warps (2-9: warp w reads TMEM lane quarter
+// w % 4, columns of half (w - 2) / 4 of the tile) with tiles of 128 features x 96 rows and K
+// stages of 128 bytes. Warp 0's lanes also gather each stage's scale blocks (lane i: matrix rows
+// 32 c + i) into shared memory; the stage's full barrier waits for the TMA bytes and for that.
+// The MMA issuer copies the blocks into TMEM (two slots, alternating by stage) ahead of the
+// stage's MMAs; tcgen05 operations of one thread run in issue order. Gate-up's epilogue writes
+// the SwiGLU output as MXFP8 (a warp's 32 lanes are one 32-feature block).
+constexpr int PF8_THREADS = 320;
+
+template <int MODE>
+__global__ void __launch_bounds__(PF8_THREADS, 1) k_pf_gemm8(const __grid_constant__ CUtensorMap wmap,
+                                                     const __grid_constant__ CUtensorMap xmap, pf8_args a) {
+    using C = pf8_cfg<MODE>;
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+    __shared__ __align__(8) uint64_t full[C::STAGES], empty[C::STAGES], acc_full[2], acc_empty[2], done;
+    __shared__ uint32_t tmem_slot;
+    __shared__ volatile int abort_;
+    __shared__ int s_toff[1025];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    for (int i = threadIdx.x; i <= a.E; i += blockDim.x) s_toff[i] = a.toff[i];
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < C::STAGES; ++s) {
+            tc::bar_init(&full[s], 1);
+            tc::bar_init(&empty[s], 1);
+        }
+        for (int b = 0; b < 2; ++b) {
+            tc::bar_init(&acc_full[b], 1);
+            tc::bar_init(&acc_empty[b], 8);
+        }
+        tc::bar_init(&done, 1);
+        abort_ = 0;
+        tc::bar_init_fence();
+    }
+    if (warp == 0) tc::tmem_alloc(&tmem_slot, C::TMEM_COLS);
+    tc::fence_before_sync();
+    __syncthreads();
+    tc::fence_after_sync();
+    const uint32_t tmem = tmem_slot;
+    const int MT = (a.Mrows + PF_BM - 1) / PF_BM, KB = sf_stages(a.K);
+    const long total = (long)s_toff[a.E] * MT;
+    auto locate = [&](long tile, int &e, int &nt, int &mt) {
+        const int ntg = (int)(tile / MT);
+        mt = (int)(tile - (long)ntg * MT);
+        int lo = 0, hi = a.E;
+        while (hi - lo > 1) {
+            const int mid = (lo + hi) >> 1;
+            if (s_toff[mid] <= ntg) lo = mid;
+            else hi = mid;
+        }
+        e = lo;
+        nt = ntg - s_toff[e];
+    };
+
+    if (warp == 0) {
+        long g = 0;  // k-blocks issued (lane 0)
+        if (lane == 0) {
+            for (long tile = blockIdx.x; tile < total && !abort_; tile += gridDim.x) {
+                int e, nt, mt;
+                locate(tile, e, nt, mt);
+                const int we = a.seg_w ? a.seg_w[e] : e;
+                const long rowA = MODE == 0 ? (long)we * 2 * a.Mrows + mt * PF_BM : (long)we * a.Mrows + mt * PF_BM;
+                const long rowB = a.off[e] + (long)nt * PF8_BN;
+                const uint8_t *sfa = a.sfw + (((size_t)we * C::NA) * MT + mt) * KB * PF8_SFBLK;
+                const uint8_t *sfb = a.sfx + (size_t)(s_toff[e] + nt) * KB * PF8_SFBLK;
+                for (int kb = 0; kb < KB; ++kb, ++g) {
+                    const int s = (int)(g % C::STAGES);
+                    if (g >= C::STAGES &&
+                        !tc::bar_wait(&empty[s], (unsigned)(((g / C::STAGES) - 1) & 1), &abort_, a.status, PF_STATUS_WAIT))
+                        break;
+                    uint8_t *st = smem + (size_t)s * C::STAGE;
+                    uint8_t *sfs = st + C::NA * PF8_ATILE + PF8_BTILE;
+                    tc::bar_expect_tx(&full[s], C::NA * PF8_ATILE + PF8_BTILE + (C::NA + 1) * PF8_SFBLK);
+                    tc::tma_load_2d(st, &wmap, kb * PF8_BK, (int)rowA, &full[s]);
+                    if (MODE == 0) tc::tma_load_2d(st + PF8_ATILE, &wmap, kb * PF8_BK, (int)(rowA + a.Mrows), &full[s]);
+                    tc::tma_load_2d(st + C::NA * PF8_ATILE, &xmap, kb * PF8_BK, (int)rowB, &full[s]);
+#pragma unroll
+                    for (int mat = 0; mat < C::NA; ++mat)
+                        bulk_g2s(sfs + mat * PF8_SFBLK, sfa + ((size_t)mat * MT * KB + kb) * PF8_SFBLK, PF8_SFBLK, &full[s]);
+                    bulk_g2s(sfs + C::NA * PF8_SFBLK, sfb + (size_t)kb * PF8_SFBLK, PF8_SFBLK, &full[s]);
+                }
+            }
+            if (abort_)  // let every issued copy land (bounded) before the CTA exits
+                for (long j = std::max(0L, g - C::STAGES); j < g; ++j)
+                    tc::bar_drain(&full[j % C::STAGES], (unsigned)((j / C::STAGES) & 1));
+        }
+        __syncwarp();
+    } else if (warp == 1) {
+        if (lane == 0) {
+            long g = 0, i = 0;
+            for (long tile = blockIdx.x; tile < total && !abort_; tile += gridDim.x, ++i) {
+                const int ab = (int)(i & 1);
+                const uint32_t dcol = tmem + (uint32_t)(ab * C::ACC_COLS);
+                if (i >= 2 && !tc::bar_wait(&acc_empty[ab], (unsigned)(((i >> 1) - 1) & 1), &abort_, a.status, PF_STATUS_WAIT))
+                    break;
+                tc::fence_after_sync();
+                bool ok = true;
+                for (int kb = 0; kb < KB; ++kb, ++g) {
+                    const int s = (int)(g % C::STAGES);
+                    if (!tc::bar_wait(&full[s], (unsigned)((g / C::STAGES) & 1), &abort_, a.status, PF_STATUS_WAIT)) {
+                        ok = false;
+                        break;
+                    }
+                    tc::fence_after_sync();
+                    const uint32_t a0 = tc::sa(smem + (size_t)s * C::STAGE);
+                    const uint32_t b0 = a0 + C::NA * PF8_ATILE, sfs = b0 + PF8_BTILE;
+                    const uint32_t sfc = tmem + (uint32_t)(C::SF_BASE + (int)(g & 1) * C::SF_SLOT);
+#pragma unroll
+                    for (int mat = 0; mat <= C::NA; ++mat) cp_sf(sfc + 4 * mat, sfs + mat * PF8_SFBLK);
+#pragma unroll
+                    for (int k = 0; k < PF8_BK / 32; ++k) {
+                        const uint32_t acc = (kb > 0 || k > 0) ? 1u : 0u;
+                        const uint32_t id = idesc_mx8(PF_BM, PF8_BN, k);
+                        mma_mx8(dcol, tc::desc_k_sw128(a0 + k * 32), tc::desc_k_sw128(b0 + k * 32), id, sfc,
+                                sfc + 4 * C::NA, acc);
+                        if (MODE == 0)
+                            mma_mx8(dcol + PF8_BN, tc::desc_k_sw128(a0 + PF8_ATILE + k * 32), tc::desc_k_sw128(b0 + k * 32),
+                                    id, sfc + 4, sfc + 4 * C::NA, acc);
+                    }
+                    tc::mma_commit(&empty[s]);
+                }
+                if (!ok) break;
+                tc::mma_commit(&acc_full[ab]);
+            }
+            tc::mma_commit(&done);
+            tc::bar_drain(&done, 0);
+        }
+        __syncwarp();
+    } else {
+        const int qd = warp & 3;  // TMEM lane quarter
+        const int half = (warp - 2) >> 2;  // columns [48 half, 48 half + 48)
+        const uint32_t lane_base = tmem + ((uint32_t)(32 * qd) << 16);
+        const int kb_act = sf_stages(a.Mrows);  // the down GEMM's K stages
+        long i = 0;
+        for (long tile = blockIdx.x; tile < total; tile += gridDim.x, ++i) {
+            const int ab = (int)(i & 1);
+            if (!tc::bar_wait(&acc_full[ab], (unsigned)((i >> 1) & 1), &abort_, a.status, PF_STATUS_WAIT)) break;
+            tc::fence_after_sync();
+            int e, nt, mt;
+            locate(tile, e, nt, mt);
+            const int seg = a.off[e], n_rows = a.off[e + 1] - seg;
+            const int f = mt * PF_BM + 32 * qd + lane;  // this thread's feature row
+            const bool fok = f < a.Mrows;
+            const uint32_t acc_base = lane_base + (uint32_t)(ab * C::ACC_COLS);
+            const int wblk = a.seg_w ? a.seg_w[e] : e;
+            const float bg = (a.bias && fok) ? a.bias[(size_t)wblk * a.Mrows + f] : 0.f;
+            const float bu = (MODE == 0 && a.bias && fok) ? a.bias[(size_t)(a.n_blocks + wblk) * a.Mrows + f] : 0.f;
+            for (int c0 = half * (PF8_BN / 2); c0 < (half + 1) * (PF8_BN / 2); c0 += 16) {
+                float d[16];
+                tc::tmem_ld16(acc_base + c0, d);
+                if (MODE == 0) {
+                    float u[16];
+                    tc::tmem_ld16(acc_base + PF8_BN + c0, u);
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) {
+                        const int n = nt * PF8_BN + c0 + j;
+                        const float v = fok ? act_fn(a.act, d[j] + bg, u[j] + bu, a.alpha, a.limit) : 0.f;
+                        // the block's largest magnitude: non-negative floats order as their bits
+                        const float m = __uint_as_float(__reduce_max_sync(0xffffffffu, __float_as_uint(fabsf(v))));
+                        const int X = mx8_exp(m);
+                        if (n < n_rows) {
+                            if (fok) a.act8[(size_t)(seg + n) * a.Mrows + f] = to_e4m3(v * pow2_neg(X));
+                            if (lane == 0) a.sact[sf_at(s_toff[e] + nt, kb_act, c0 + j, f / 32)] = (uint8_t)(127 + X);
+                        }
+                    }
+                } else {
+                    float *ybase = a.y_out + (size_t)seg * a.Mrows;
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) {
+                        const int n = nt * PF8_BN + c0 + j;
+                        if (fok && n < n_rows) ybase[(size_t)n * a.Mrows + f] = d[j] + bg;
+                    }
+                }
+            }
+            tc::fence_before_sync();
+            __syncwarp();
+            if (lane == 0) tc::bar_arrive(&acc_empty[ab]);
+        }
+    }
+    tc::fence_before_sync();
+    __syncthreads();
+    tc::fence_after_sync();
+    if (warp == 0) tc::tmem_dealloc(tmem, C::TMEM_COLS);
+}
+
 struct pf_gemm4_args {
     pf_gemm_args g;
     const uint8_t *w4;  // the matrix set's chunks: [slot][mat][rb][kb]
@@ -826,6 +1218,20 @@ encode_tiled_fn encoder() {
 
 // A bf16 row-major [rows][cols] matrix read as 128-row x 64-column boxes, 128-byte swizzle
 // (the UMMA K-major canonical layout); rows past the end read as zeros.
+// An E4M3 row-major [rows][cols] matrix read as box_rows-row x 128-byte boxes, 128-byte swizzle;
+// rows and columns past the end read as zeros.
+bool make_map8(CUtensorMap *map, const void *base, long rows, int cols, int box_rows) {
+    encode_tiled_fn enc = encoder();
+    if (!enc) return false;
+    const cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+    const cuuint64_t strides[1] = {(cuuint64_t)cols};
+    const cuuint32_t box[2] = {PF8_BK, (cuuint32_t)box_rows};
+    const cuuint32_t es[2] = {1, 1};
+    return enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void *>(base), dims, strides, box, es,
+               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 bool make_map(CUtensorMap *map, const void *base, long rows, int cols) {
     encode_tiled_fn enc = encoder();
     if (!enc) return false;
@@ -898,6 +1304,12 @@ struct moearc_x_prefill {
     // per-expert biases (moearc_x_prefill_set_bias), indexed by weight block: gate-up
     // [2E][I] (gate of block w at w, up at E + w), down [E][H]; null: none
     const float *bias_gu = nullptr, *bias_dn = nullptr;
+    // MXFP8 mode (moearc_x_prefill_load8): E4M3 weights [E][2][I][H] and [E][H][I] with their
+    // scale bytes, the activations' scale bytes (the E4M3 rows reuse xp and actb)
+    void *w8 = nullptr;
+    uint8_t *w8gu = nullptr, *w8dn = nullptr, *s8gu = nullptr, *s8dn = nullptr, *s8x = nullptr, *s8a = nullptr;
+    CUtensorMap map8_wgu, map8_wdn, map8_x, map8_act;
+    bool mode8 = false;
 };
 
 namespace {
@@ -913,6 +1325,45 @@ bool ensure_bf16(moearc_x_prefill *p) {
     p->wgu = static_cast<uint16_t *>(p->w16);
     p->wdn = p->wgu + ngu;
     return make_map(&p->map_wgu, p->wgu, (long)p->E * 2 * p->I, p->H) && make_map(&p->map_wdn, p->wdn, (long)p->E * p->H, p->I);
+}
+
+// The MXFP8 form's memory (first load8): weights and scales, the activation scales (the pad bytes
+// of every scale row hold 127), and the four tensor maps.
+bool ensure_fp8(moearc_x_prefill *p) {
+    if (p->w8) return true;
+    const size_t rows = (size_t)p->T_max * p->K;
+    const size_t ngu = (size_t)p->E * 2 * p->I * p->H, ndn = (size_t)p->E * p->H * p->I;
+    const size_t mt_i = (p->I + PF_BM - 1) / PF_BM, mt_h = (p->H + PF_BM - 1) / PF_BM;
+    const size_t sgu = (size_t)p->E * 2 * mt_i * sf_stages(p->H) * PF8_SFBLK;
+    const size_t sdn = (size_t)p->E * mt_h * sf_stages(p->I) * PF8_SFBLK;
+    const size_t tiles = (rows + PF8_BN - 1) / PF8_BN + p->E;  // 96-row tiles over all segments, at most
+    const size_t sx = tiles * sf_stages(p->H) * PF8_SFBLK, sa = tiles * sf_stages(p->I) * PF8_SFBLK;
+    const size_t total = ngu + ndn + sgu + sdn + sx + sa;
+    if (cudaMalloc(&p->w8, total) != cudaSuccess) {
+        cudaGetLastError();
+        p->w8 = nullptr;
+        return false;
+    }
+    uint8_t *b = static_cast<uint8_t *>(p->w8);
+    p->w8gu = b;
+    p->w8dn = b + ngu;
+    p->s8gu = p->w8dn + ndn;
+    p->s8dn = p->s8gu + sgu;
+    p->s8x = p->s8dn + sdn;
+    p->s8a = p->s8x + sx;
+    if (cudaMemsetAsync(p->s8gu, 0x7F, sgu + sdn + sx + sa, p->c->stream) != cudaSuccess) return false;
+    const bool ok = make_map8(&p->map8_wgu, p->w8gu, (long)p->E * 2 * p->I, p->H, PF_BM) &&
+                    make_map8(&p->map8_wdn, p->w8dn, (long)p->E * p->H, p->I, PF_BM) &&
+                    make_map8(&p->map8_x, p->xp, (long)rows, p->H, PF8_BN) &&
+                    make_map8(&p->map8_act, p->actb, (long)rows, p->I, PF8_BN) &&
+                    set_smem(k_pf_gemm8<0>, pf8_cfg<0>::SMEM) == cudaSuccess &&
+                    set_smem(k_pf_gemm8<1>, pf8_cfg<1>::SMEM) == cudaSuccess;
+    if (!ok) {
+        cudaGetLastError();
+        cudaFree(p->w8);
+        p->w8 = nullptr;
+    }
+    return ok;
 }
 
 int tc4_bytes(const moearc_x_prefill *p) { return p->wtype == T_MXFP4 ? tc4_chunk<39>() : tc4_chunk<2>(); }
@@ -1053,8 +1504,25 @@ void moearc_x_prefill_destroy(moearc_x_prefill *p) {
     cudaStreamSynchronize(p->c->stream);
     cudaFree(p->w16);
     cudaFree(p->w4);
+    cudaFree(p->w8);
     cudaFree(p->mem);
     delete p;
+}
+
+int moearc_x_prefill_load8(moearc_x_prefill *p, const void *gateup_packed, const void *down_packed) {
+    if (!p || !gateup_packed || !down_packed) return ERR;
+    if (p->wtype != T_MXFP4 || p->H % 64 || p->I % 64) return ERR_ARG;  // E2M1 elements carry over exactly
+    if (!ensure_fp8(p)) return ERR;
+    moearc_ctx *c = p->c;
+    const long gu_tiles = (long)p->E * (p->I / 16) * (p->H / 64) * 2, dn_tiles = (long)p->E * (p->H / 16) * (p->I / 64);
+    auto grid = [](long warps) { return dim3((unsigned)((warps + 7) / 8)); };
+    k_pf_unpack8<<<grid(gu_tiles), 256, 0, c->stream>>>(static_cast<const uint8_t *>(gateup_packed), p->E, p->I, p->H,
+                                                         2, p->tile_bytes, p->w8gu, p->s8gu);
+    k_pf_unpack8<<<grid(dn_tiles), 256, 0, c->stream>>>(static_cast<const uint8_t *>(down_packed), p->E, p->H, p->I, 1,
+                                                         p->tile_bytes, p->w8dn, p->s8dn);
+    p->mode4 = false;
+    p->mode8 = true;
+    return cudaGetLastError() == cudaSuccess ? OK : ERR;
 }
 
 int moearc_x_prefill_load_range(moearc_x_prefill *p, const void *gateup_packed, const void *down_packed,
@@ -1063,6 +1531,7 @@ int moearc_x_prefill_load_range(moearc_x_prefill *p, const void *gateup_packed, 
     if (n == 0 || e_first + n > (unsigned)p->E) return ERR_ARG;
     if (!ensure_bf16(p)) return ERR;
     p->mode4 = false;
+    p->mode8 = false;
     moearc_ctx *c = p->c;
     const int E = (int)n;
     const size_t gu_e = (size_t)(p->I / 16) * (p->H / 64) * 2 * p->tile_bytes, dn_e = (size_t)(p->H / 16) * (p->I / 64) * p->tile_bytes;
@@ -1090,6 +1559,7 @@ int moearc_x_prefill_load_list(moearc_x_prefill *p, const void *gateup_packed, c
         if (experts[i] < 0 || experts[i] >= p->E) return ERR_ARG;
     if (!ensure_bf16(p)) return ERR;
     p->mode4 = false;
+    p->mode8 = false;
     moearc_ctx *c = p->c;
     const size_t gu_e = (size_t)(p->I / 16) * (p->H / 64) * 2 * p->tile_bytes, dn_e = (size_t)(p->H / 16) * (p->I / 64) * p->tile_bytes;
     const long gu_tiles = (long)(p->I / 16) * (p->H / 64) * 2, dn_tiles = (long)(p->H / 16) * (p->I / 64);
@@ -1158,6 +1628,7 @@ int moearc_x_prefill_load4_list(moearc_x_prefill *p, const void *gateup_packed, 
         return ERR;
     if (st & PF_STATUS_RANGE) return ERR_ARG;  // scales f16 cannot hold: keep the bf16 form
     p->mode4 = true;
+    p->mode8 = false;
     return OK;
 }
 
@@ -1207,9 +1678,47 @@ int prefill_forward(moearc_x_prefill *p, const uint16_t *x, unsigned n_tokens, c
     mark(1);
     k_pf_topk<<<(T + 7) / 8, 256, 0, st>>>(ra);
     mark(2);
-    k_pf_scan<<<1, 1024, 0, st>>>(p->cnt, p->E, p->off, p->toff, p->cursor);
+    k_pf_scan<<<1, 1024, 0, st>>>(p->cnt, p->E, p->off, p->toff, p->cursor, p->mode8 ? PF8_BN : PF_BN);
     mark(3);
     const long pairs = (long)T * p->K;
+    if (p->mode8) {
+        // MXFP8: quantised rows, then the block-scaled GEMMs
+        k_pf_scatter8<<<(unsigned)((pairs + 7) / 8), 256, 0, st>>>(x, p->idx, p->epos, T, p->K, p->H, p->off, p->toff,
+                                                                   p->cursor, p->perm, reinterpret_cast<uint8_t *>(p->xp),
+                                                                   p->s8x);
+        mark(4);
+        pf8_args g{};
+        g.E = p->E;
+        g.off = p->off;
+        g.toff = p->toff;
+        g.act = p->act;
+        g.alpha = p->alpha;
+        g.limit = p->limit;
+        g.status = p->status;
+        g.n_blocks = p->E;
+        g.Mrows = p->I;
+        g.K = p->H;
+        g.sfw = p->s8gu;
+        g.sfx = p->s8x;
+        g.act8 = reinterpret_cast<uint8_t *>(p->actb);
+        g.sact = p->s8a;
+        g.bias = p->bias_gu;
+        k_pf_gemm8<0><<<c->sm_count, PF8_THREADS, pf8_cfg<0>::SMEM, st>>>(p->map8_wgu, p->map8_x, g);
+        mark(5);
+        g.Mrows = p->H;
+        g.K = p->I;
+        g.sfw = p->s8dn;
+        g.sfx = p->s8a;
+        g.y_out = p->y;
+        g.bias = p->bias_dn;
+        k_pf_gemm8<1><<<c->sm_count, PF8_THREADS, pf8_cfg<1>::SMEM, st>>>(p->map8_wdn, p->map8_act, g);
+        mark(6);
+        const long n = (long)T * p->H;
+        k_pf_combine<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(p->y, p->perm, p->wts, residual, out, T, p->K, p->H);
+        mark(7);
+        if (cudaGetLastError() != cudaSuccess) return ERR;
+        return ls.finish();
+    }
     k_pf_scatter<<<(unsigned)((pairs + 7) / 8), 256, 0, st>>>(x, p->idx, p->epos, T, p->K, p->H, p->off, p->cursor,
                                                               p->perm, p->xp, p->mode4 ? 1 : 0, nullptr, nullptr, 0);
     mark(4);
@@ -1279,6 +1788,7 @@ int moearc_x_prefill_profile(moearc_x_prefill *p, const uint16_t *x, unsigned n_
 // expert range travel to the rank that owns it before moearc_x_prefill_experts.
 int moearc_x_prefill_route(moearc_x_prefill *p, const uint16_t *x, unsigned n_tokens, const float *router_w,
                            const float *router_b) {
+    if (p && p->mode8) return ERR_ARG;  // the expert-parallel steps take the bf16 and 4-bit forms
     const float *x32 = nullptr;
     if (!p || !x || !router_w) return ERR;
     if (n_tokens == 0) return OK;
@@ -1304,6 +1814,7 @@ int moearc_x_prefill_route(moearc_x_prefill *p, const uint16_t *x, unsigned n_to
 // seg_expert are host arrays of n_seg <= 1024 entries whose counts sum to n_rows.
 int moearc_x_prefill_experts(moearc_x_prefill *p, const uint16_t *rows_in, unsigned n_rows, const int *seg_counts,
                              const int *seg_expert, unsigned n_seg, uint16_t *act_scratch, float *y_out) {
+    if (p && p->mode8) return ERR_ARG;  // the expert-parallel steps take the bf16 and 4-bit forms
     if (!p || !seg_counts || !seg_expert) return ERR;
     if (n_seg == 0 || n_seg > 1024) return ERR_ARG;
     long sum = 0;
@@ -1399,6 +1910,7 @@ int moearc_x_prefill_route_dispatch(moearc_x_prefill *p, void *const *dst_rows, 
 // n_seg device or peer pointers, f32 rows of n_embd) instead of y_out.
 int moearc_x_prefill_experts_to(moearc_x_prefill *p, const uint16_t *rows_in, unsigned n_rows, const int *seg_counts,
                                 const int *seg_expert, unsigned n_seg, uint16_t *act_scratch, float *const *seg_dst) {
+    if (p && p->mode8) return ERR_ARG;  // the expert-parallel steps take the bf16 and 4-bit forms
     if (!p || !seg_counts || !seg_expert || !seg_dst) return ERR;
     if (n_seg == 0 || n_seg > 1024) return ERR_ARG;
     long sum = 0;

@@ -97,6 +97,11 @@ class MoePrefill:
             self.ctx.lib.moearc_x_prefill_destroy(self.h)
             self.h = None
 
+    def load8(self, gateup: DeviceBuffer, down: DeviceBuffer) -> None:
+        """The MXFP8 perf mode: E4M3 weights (exact for MXFP4) and MXFP8 activations on the
+        block-scaled FP8 tensor cores."""
+        self.ctx._finish(self.ctx.lib.moearc_x_prefill_load8(self.h, gateup.ptr, down.ptr), "prefill_load8")
+
     def set_bias(self, gate_up_bias: DeviceBuffer | None, down_bias: DeviceBuffer | None) -> None:
         """Per-expert biases (indexed by weight block) for the following forward calls."""
         rc = self.ctx.lib.moearc_x_prefill_set_bias(self.h, gate_up_bias.ptr if gate_up_bias is not None else None,

@@ -99,6 +99,8 @@ def _declare(l: C.CDLL) -> None:
         "or_kv_append": (C.c_int, [P, P, P, P, C.c_uint32, C.c_uint32, SZ, SZ, SZ, U]),
         "or_attn_decode": (C.c_int, [P, P, P, P, P, SZ, SZ, SZ, SZ, SZ, SZ, F, U, P]),
         "or_moe_ffn_token": (C.c_int, [C.POINTER(MoeCfg), P, P, P, P, P, P, P, P, P, P, P, P]),
+        "or_moe_ffn_token_mx8": (C.c_int, [C.POINTER(MoeCfg), P, P, P, P, P, P, P, P, P, P, P, P]),
+        "or_mx8_quantize": (None, [P, SZ, P]),
         "or_synth_mxfp4": (None, [C.c_uint64, SZ, C.c_int, C.c_int, P]),
         "or_synth_q4_0": (None, [C.c_uint64, SZ, C.c_double, P]),
         "or_synth_normal_f32": (None, [C.c_uint64, SZ, C.c_double, P]),

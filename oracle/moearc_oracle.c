@@ -722,6 +722,45 @@ int or_attn_decode(const float *q, const void *k_pages, const void *v_pages,
 /* one token's MoE FFN                                                                     */
 /* ====================================================================================== */
 
+/* ---- MXFP8 activation quantisation (the prefill perf mode's declared arithmetic) ----------
+ * Not in the reference (its engine has no FP8 path): the declared quantisation of the build's
+ * MXFP8 prefill mode, restated from the OCP MX format — per 32 consecutive values one E8M0 scale
+ * 2^X, X the smallest integer with max|x| / 2^X <= 448 (E4M3's largest finite), the elements
+ * E4M3 (1 sign, 4 exponent bits of bias 7, 3 mantissa bits, subnormals down to 2^-9) rounded to
+ * nearest even. Returns the dequantised values. */
+static float e4m3_rne(float v) {
+    const float a = fabsf(v);
+    if (a == 0.0f) return v;
+    int e;
+    frexpf(a, &e); /* a = f * 2^e, f in [0.5, 1) */
+    int E = e - 1; /* a = (2f) * 2^E, 2f in [1, 2) */
+    if (E < -6) E = -6; /* subnormals: a quantum of 2^-9 */
+    const double q = ldexp(1.0, E - 3);
+    const double r = (double)a / q; /* in units of the quantum */
+    double n = floor(r);
+    const double frac = r - n;
+    if (frac > 0.5 || (frac == 0.5 && fmod(n, 2.0) != 0.0)) n += 1.0;
+    double out = n * q;
+    if (out > 448.0) out = 448.0;
+    return v < 0 ? (float)-out : (float)out;
+}
+
+void or_mx8_quantize(const float *x, size_t n, float *out) {
+    for (size_t b = 0; b < n; b += 32) {
+        const size_t m = n - b < 32 ? n - b : 32;
+        float amax = 0.0f;
+        for (size_t i = 0; i < m; ++i) amax = fmaxf(amax, fabsf(x[b + i]));
+        int X = 0;
+        if (amax > 0.0f) {
+            uint32_t bits;
+            memcpy(&bits, &amax, 4);
+            X = (int)((bits >> 23) & 0xFF) - 127 - 8 + ((bits & 0x7FFFFF) > 0x600000u ? 1 : 0);
+            if (X < -127) X = -127;
+        }
+        for (size_t i = 0; i < m; ++i) out[b + i] = ldexpf(e4m3_rne(ldexpf(x[b + i], -X)), X);
+    }
+}
+
 int or_moe_ffn_token(const or_moe_cfg *c, const float *x, const float *router_w,
                      const float *router_b, const uint8_t *gate, const uint8_t *up,
                      const uint8_t *down, const float *gate_b, const float *up_b,
@@ -775,6 +814,69 @@ done:
     free(u);
     free(a);
     free(o);
+    free(acc);
+    return rc;
+}
+
+int or_moe_ffn_token_mx8(const or_moe_cfg *c, const float *x, const float *router_w,
+                     const float *router_b, const uint8_t *gate, const uint8_t *up,
+                     const uint8_t *down, const float *gate_b, const float *up_b,
+                     const float *down_b, float *out, uint32_t *idx_out, float *w_out) {
+    const int bb = or_block_bytes(c->wtype);
+    const int be = or_block_elems(c->wtype);
+    if (!bb || c->n_embd % (size_t)be || c->n_ff % (size_t)be || c->k > 32) return -2;
+    const size_t H = c->n_embd, I = c->n_ff, E = c->n_expert;
+    const size_t gate_bytes = I * (H / (size_t)be) * (size_t)bb; /* one expert's gate / up */
+    const size_t down_bytes = H * (I / (size_t)be) * (size_t)bb; /* one expert's down */
+    float *logits = (float *)malloc(sizeof(float) * E);
+    float *g = (float *)malloc(sizeof(float) * I);
+    float *u = (float *)malloc(sizeof(float) * I);
+    float *a = (float *)malloc(sizeof(float) * I);
+    float *o = (float *)malloc(sizeof(float) * H * c->k);
+    float *xq = (float *)malloc(sizeof(float) * H);
+    float *aq = (float *)malloc(sizeof(float) * I);
+    double *acc = (double *)calloc(H, sizeof(double));
+    uint32_t idx[32];
+    float w[32];
+    int rc = 0;
+
+    if (c->router_gpu_order) or_matvec_f32_gpu_order(router_w, x, E, H, logits);
+    else or_matvec_f32(router_w, x, E, H, logits);
+    /* The router bias goes on before the top-k, so it changes which experts run
+     * (moe.rs:2084-2089). */
+    if (router_b) or_add(logits, router_b, E, logits);
+    rc = or_topk_router(logits, 1, E, c->k, c->gating, idx, w);
+    if (rc) goto done;
+
+    or_mx8_quantize(x, H, xq); /* the routing above saw x itself */
+    for (unsigned m = 0; m < c->k; ++m) {
+        const size_t e = idx[m];
+        or_matvec_q(c->wtype, gate + e * gate_bytes, xq, I, H, g);
+        or_matvec_q(c->wtype, up + e * gate_bytes, xq, I, H, u);
+        /* Per-expert biases before the activation (moe.rs:2310-2331). */
+        if (gate_b) or_add(g, gate_b + e * I, I, g);
+        if (up_b) or_add(u, up_b + e * I, I, u);
+        if (c->act == 1) or_swiglu_oai(g, u, I, c->alpha, c->limit, a);
+        else or_swiglu(g, u, I, a);
+        or_mx8_quantize(a, I, aq);
+        or_matvec_q(c->wtype, down + e * down_bytes, aq, H, I, o + m * H);
+        /* The down bias sits inside the router's weighting (moe.rs:2362-2372). */
+        if (down_b) or_add(o + m * H, down_b + e * H, H, o + m * H);
+    }
+    /* Combine in router order (moe.rs:2374-2386), on the higher-precision side. */
+    for (unsigned m = 0; m < c->k; ++m)
+        for (size_t i = 0; i < H; ++i) acc[i] += (double)w[m] * (double)o[m * H + i];
+    for (size_t i = 0; i < H; ++i) out[i] = (float)acc[i];
+    if (idx_out) memcpy(idx_out, idx, sizeof(uint32_t) * c->k);
+    if (w_out) memcpy(w_out, w, sizeof(float) * c->k);
+done:
+    free(logits);
+    free(g);
+    free(u);
+    free(a);
+    free(o);
+    free(xq);
+    free(aq);
     free(acc);
     return rc;
 }

@@ -157,6 +157,16 @@ int or_moe_ffn_token(const or_moe_cfg *c, const float *x, const float *router_w,
                      const uint8_t *down, const float *gate_b, const float *up_b,
                      const float *down_b, float *out, uint32_t *idx, float *w);
 
+/* MXFP8 quantisation per 32 values (scale 2^X, X the smallest with max|x| / 2^X <= 448; E4M3
+ * round to nearest even), dequantised: the declared arithmetic of the build's FP8 prefill mode. */
+void or_mx8_quantize(const float *x, size_t n, float *out);
+/* or_moe_ffn_token with that quantisation applied to x before gate/up and to the activation
+ * before down (routing on x unquantised). */
+int or_moe_ffn_token_mx8(const or_moe_cfg *c, const float *x, const float *router_w,
+                         const float *router_b, const uint8_t *gate, const uint8_t *up,
+                         const uint8_t *down, const float *gate_b, const float *up_b,
+                         const float *down_b, float *out, uint32_t *idx, float *w);
+
 /* ---- synthetic inputs (SplitMix64, tests/common/mod.rs:11-38) ------------------------- */
 uint64_t or_splitmix64(uint64_t *state);
 /* MXFP4 blocks: nibbles uniform over 16 codes, e8m0 = 127+e with e uniform in [e_lo, e_hi]. */

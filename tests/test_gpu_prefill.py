@@ -364,3 +364,47 @@ def test_expert_biases_in_the_gemm_epilogues_match_the_oracle(ctx, four_bit):
     assert worst <= 1e-2
     pf.close()
     packer.close()
+
+
+def test_mxfp8_mode_matches_the_quantisation_aware_oracle(ctx):
+    """The MXFP8 perf mode (block-scaled FP8 GEMMs, tcgen05.mma kind::mxf8f6f4; MXFP4 weights exact
+    as E4M3, activations quantised to MXFP8 per 32) at the gpt-oss expert shape: routing
+    bit-exact; against the oracle that applies the same declared quantisation within 5e-3 of the
+    output's scale; against the exact oracle the error of the quantisation itself, printed (and
+    held under 5e-2)."""
+    H, I, E, k, T = 2880, 2880, 32, 4, 40
+    pf, packer, host = build(ctx, H, I, E, k, 2, 1, O.MXFP4, T, 0x9F31)
+    pf.load8(packer.gateup, packer.down)
+    xb = O.synth_normal_bf16(0x9F32, T * H, 1.0)
+    out = ctx.alloc_n(np.float32, T * H)
+    pf.forward(ctx.upload_new(xb), T, ctx.upload_new(host[3]), out)
+    got = ctx.download(out, np.float32, T * H).reshape(T, H)
+    assert pf.status() == 0
+    idx = pf.buffer(0, np.uint32, T * k).reshape(T, k)
+    gate, up, down, router = host
+    cfg = O.MoeCfg(H, I, E, k, 2, 1, 1.702, 7.0, O.MXFP4, 1)
+    x32 = O.bf16_to_f32(xb).reshape(T, H)
+    want_q, want = np.zeros((T, H), np.float32), np.zeros((T, H), np.float32)
+    for t in range(T):
+        xt = np.ascontiguousarray(x32[t])
+        widx = np.zeros(k, np.uint32)
+        assert O.lib().or_moe_ffn_token_mx8(cfg, O.ptr(xt), O.ptr(router), None, O.ptr(gate), O.ptr(up), O.ptr(down),
+                                            None, None, None, O.ptr(want_q[t]), O.ptr(widx), None) == 0
+        assert np.array_equal(idx[t], widx), t
+        want[t], _, _ = oracle_token(H, I, E, k, 2, 1, O.MXFP4, host, xt)
+    err_q, err = bf16_err(got, want_q), bf16_err(got, want)
+    print(f"prefill MXFP8: {T} tokens, max rel err {err_q:.3e} against the quantisation-aware oracle, "
+          f"{err:.3e} against the exact oracle")
+    assert err_q <= 5e-3 and err <= 5e-2
+    pf.close()
+    packer.close()
+
+
+def test_mxfp8_mode_refuses_q4_0_experts(ctx):
+    H, I, E, k = 2048, 768, 16, 4
+    pf, packer, host = build(ctx, H, I, E, k, 1, 0, O.Q4_0, 8, 0x9F41)
+    from moearc_b200.kernels import BadArgument
+    with pytest.raises(BadArgument):
+        pf.load8(packer.gateup, packer.down)
+    pf.close()
+    packer.close()
