@@ -387,7 +387,7 @@ moearc_x_decoder *moearc_x_decoder_create(moearc_ctx *c, const moearc_x_decoder_
 void moearc_x_decoder_destroy(moearc_x_decoder *d);
 void *moearc_x_decoder_input(moearc_x_decoder *d);
 /* Device pointer of the last step's logits (n_vocab f32), or NULL without an output head. */
-void *moearc_x_decoder_logits(moearc_x_decoder *d);   /* device, n_embd f32 */
+void *moearc_x_decoder_logits(moearc_x_decoder *d);
 void *moearc_x_decoder_output(moearc_x_decoder *d);  /* device, n_embd f32 */
 int moearc_x_decoder_pos(moearc_x_decoder *d);       /* the next position to decode */
 int moearc_x_decoder_set_pos(moearc_x_decoder *d, unsigned int pos);
