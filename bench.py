@@ -55,15 +55,16 @@ METRIC = "MoE decode tok/s at gpt-oss-120b shape; expert-GEMM HBM GB/s vs 8 TB/s
 UNIT = "tok/s"
 
 
-def expert_traffic(fused: bool) -> float | None:
+def expert_traffic(fused: bool, tc: bool = False) -> float | None:
     """DRAM read + write bytes of one launch of the roofline kernel, from the committed ncu
     capture summary (profiles/moe_and_dense_kernels_gpt_oss_120b_1layer.md: the fused gate-up +
-    down row, or the gate-up row of the split kernels); None if absent."""
+    down row, the gate-up row of the fragment kernels, or the tensor-core gate-up row); None if
+    absent."""
     import re
     p = os.path.join(ROOT, "profiles", "moe_and_dense_kernels_gpt_oss_120b_1layer.md")
     if not os.path.exists(p):
         return None
-    row = "| `k_moe_fused<39,false>`" if fused else "| `k_xexpert<39,0>`"
+    row = "| `k_moe_fused<39,false>`" if fused else ("| `k_xtc<0>`" if tc else "| `k_xexpert<39,0>`")
     for line in open(p):
         if line.startswith(row):
             m = re.search(r"\| ([\d.]+) MB / ([\d.]+) MB \|", line)
@@ -812,6 +813,9 @@ def main() -> None:
     ap.add_argument("--host-threads", type=int, default=0, help="host pool threads (0: the online cores - 1)")
     ap.add_argument("--no-step-kernel", action="store_true",
                     help="skip the comparison run of the persistent step kernel")
+    ap.add_argument("--layout", default="tc", choices=["tc", "fragment"],
+                    help="120b/20b: resident experts in the tensor-core layout (block-scaled FP4 MMA) or the "
+                         "fragment layout (mma.sync kernels; the persistent step kernel needs it)")
     ap.add_argument("--no-ep", action="store_true",
                     help="skip the expert-parallel prefill sample (configs[3] over the N GPUs)")
     args = ap.parse_args()
@@ -827,6 +831,7 @@ def main() -> None:
     from moearc_b200.decoder import DecoderConfig
 
     cfg = DecoderConfig.gpt_oss_120b() if args.config == "120b" else DecoderConfig.gpt_oss_20b()
+    cfg.expert_layout = 0 if args.layout == "tc" else 1
     if args.layers:
         cfg.n_layer = args.layers
     cfg.n_offload = min(args.offload, cfg.n_layer)
@@ -850,7 +855,9 @@ def main() -> None:
               "top_k": cfg.n_expert_used, "n_ff": cfg.n_ff, "expert_type": "MXFP4", "kv": "bf16, pages of 32",
               "attention": "64 q / 8 kv heads x 64, sinks, alternating full / 128-key window",
               "depth": args.depth, "batch": 1, "offloaded_blocks": cfg.n_offload,
-              "l2": "weights (~63 GB) far exceed the 126 MB L2; no flush"}
+              "l2": "weights (~63 GB) far exceed the 126 MB L2; no flush",
+              "expert_layout": ("tensor-core (block-scaled FP4 MMA)" if cfg.expert_layout == 0 and cfg.n_offload < cfg.n_layer
+                                else "fragment (mma.sync)")}
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -897,7 +904,8 @@ def main() -> None:
 
     peak, peak_kind = load_peaks()
     H, I, k = cfg.n_embd, cfg.n_ff, cfg.n_expert_used
-    fused = r["counts"][5] == 0  # gate-up and down in one launch (the default decode path)
+    fused = r["counts"][5] == 0  # gate-up and down in one launch (the opt-in fused decode path)
+    tc_layout = cfg.expert_layout == 0 and cfg.n_offload < cfg.n_layer
     gu_bytes = k * (3 if fused else 2) * I * H // 32 * 17
     n_gu = max(1, r["counts"][4])
     gu_ms_serial = r["kernel_ms"]["moe_gate_up"] / n_gu
@@ -927,9 +935,12 @@ def main() -> None:
         "config": config,
         "roofline": {"bound": "hbm",
                      "kernel": ("moe gate-up + SwiGLU + down + combine, one launch (k_moe_fused, MXFP4, tensor cores)"
-                                if fused else "moe gate-up grouped GEMV (MXFP4, tensor cores)"),
+                                if fused else
+                                "moe gate-up, MXFP4 on the block-scaled FP4 tensor cores (k_xtc<0>, tcgen05.mma "
+                                "kind::mxf4, 16 E2M1 digits of the activation)" if tc_layout else
+                                "moe gate-up grouped GEMV (MXFP4, mma.sync fragments, k_xexpert<39,0>)"),
                      "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
-                     "peak_kind": peak_kind, "traffic": expert_traffic(fused),
+                     "peak_kind": peak_kind, "traffic": expert_traffic(fused, tc_layout),
                      "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum, profiles/",
                      "bytes_per_launch": gu_bytes, "avg_launch_ms": gu_ms,
                      "avg_launch_ms_source": ("in the timed graph: latest CTA end minus earliest end of a CTA's "

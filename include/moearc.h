@@ -199,6 +199,27 @@ int moearc_x_moe_set_bias(moearc_x_moe *m, const float *gate_up_bias, const floa
  * 0.2 s); phantom 1 makes every such wait run out (testing the bounded wait). No reference
  * counterpart. */
 int moearc_x_moe_set_wait(moearc_x_moe *m, unsigned long long poll_ns, int phantom);
+/* ---- one token on the block-scaled FP4 tensor cores (xtc.cu; no reference counterpart) ----
+ * MXFP4 experts in the tensor-core ("tc") layout: per expert, the gate-up bank in tiles of 64
+ * gate rows and the 64 up rows of the same features, the down bank in tiles of 128 output rows,
+ * each tile in k-steps of 64 elements (E2M1 codes two per byte, 32-byte swizzle) with their E8M0
+ * scales laid out for tcgen05.cp; tcgen05.mma kind::mxf4.block_scale.block32 reads them as stored.
+ * The activation enters as 16 E2M1 digits per element (each digit an exact part of the value;
+ * together within 2e-8 of each 32-element block's largest magnitude), so the result keeps the f32
+ * check-mode bound of the fragment path. Same semantics, biases and status as moearc_x_moe_forward.
+ * Bytes of the whole tc-layout gate-up (which = 0) or down (1) bank of d->n_expert experts; 0
+ * when the shape has none (MXFP4, n_embd and n_ff multiples of 64). */
+unsigned long moearc_x_moe_tc_bytes(const moearc_x_moe_desc *d, int which);
+/* 1 when the layer can run the tc path (k <= 8 and the shape above), else 0. */
+int moearc_x_moe_has_tc(moearc_x_moe *m);
+/* Repack GGUF-layout MXFP4 banks (as moearc_x_moe_pack) into the tc layout. */
+int moearc_x_moe_pack_tc(moearc_x_moe *m, const void *gate, const void *up, const void *down,
+                         unsigned int n_expert, void *gateup_tc, void *down_tc);
+/* moearc_x_moe_forward for n_tokens <= 1 on tc-layout banks (-2 for more tokens or a layer
+ * without the tc path). */
+int moearc_x_moe_forward_tc(moearc_x_moe *m, const float *x, unsigned int n_tokens, const float *router_w,
+                            const float *router_b, const void *gateup_tc, const void *down_tc,
+                            const float *residual, float *out);
 
 /* ---- expert FFNs on the host cores (host_experts.cpp; no GPU needed) ---------------------
  * The reference's HostExecutor (crates/moearc-engine/src/host_experts.rs:423-761): a pool of
@@ -382,6 +403,11 @@ typedef struct {
     /* The output head (moe.rs:2434-2437): logits = W_out . rmsnorm(h) with W_out bf16
      * [n_vocab][n_embd] (n_vocab a multiple of 16), after every step; 0 = none. */
     unsigned int n_vocab;
+    /* Layout of the resident blocks' expert banks: 0 = the tensor-core layout (moearc_x_moe_pack_tc)
+     * where the shape has one (MXFP4 experts, n_embd and n_ff multiples of 64), decoded by the
+     * block-scaled FP4 tensor-core kernels; 1 = the fragment layout (moearc_x_moe_pack) everywhere,
+     * which the persistent step kernel needs. Offloaded blocks always keep the fragment layout. */
+    unsigned int expert_layout;
 } moearc_x_decoder_cfg;
 moearc_x_decoder *moearc_x_decoder_create(moearc_ctx *c, const moearc_x_decoder_cfg *cfg);
 void moearc_x_decoder_destroy(moearc_x_decoder *d);
@@ -437,7 +463,8 @@ int moearc_x_decoder_host_stats(moearc_x_decoder *d, unsigned long long *out4);
  * down][CTA][start, dependency wait over, end], ns of %globaltimer); 15 / 16 the QK-norm
  * weights (head_dim f32, with has_qk_norm); 17 the packed bf16 output head (layer ignored, with
  * n_vocab). For an offloaded block, 9 and 10 are device-visible pointers of the pinned host
- * banks. */
+ * banks; for a resident block of a decoder with expert_layout 0 on a shape that has one, they are
+ * in the tc layout (moearc_x_moe_pack_tc). */
 void *moearc_x_decoder_tensor(moearc_x_decoder *d, int which, unsigned int layer, unsigned long *bytes);
 /* Turn on (1) or off (0) the expert kernels' per-CTA timestamps in the kernel chain (tensor 14),
  * so their duration can be read from inside a graphed step. Synchronises the stream; the next

@@ -75,6 +75,10 @@ SIGNATURES: dict[str, tuple] = {
     "moearc_x_moe_status": (I, [P]),
     "moearc_x_moe_set_wait": (I, [P, C.c_ulonglong, I]),
     "moearc_x_moe_set_bias": (I, [P, P, P]),
+    "moearc_x_moe_tc_bytes": (UL, [P, I]),
+    "moearc_x_moe_has_tc": (I, [P]),
+    "moearc_x_moe_pack_tc": (I, [P, P, P, P, U, P, P]),
+    "moearc_x_moe_forward_tc": (I, [P, P, U, P, P, P, P, P, P]),
     "moearc_x_host_pool_create": (P, [I]),
     "moearc_x_host_pool_destroy": (None, [P]),
     "moearc_x_host_pool_threads": (I, [P]),
@@ -169,7 +173,8 @@ class DecoderCfg(C.Structure):
                 ("act", U), ("alpha", F), ("limit", F), ("n_swa", U), ("swa_pattern", U),
                 ("rope_base", F), ("rope_freq_scale", F), ("rope_ext_factor", F), ("rope_attn_factor", F),
                 ("rope_corr_lo", F), ("rope_corr_hi", F), ("rms_eps", F), ("has_sinks", U), ("n_ctx", U),
-                ("seed", C.c_ulonglong), ("n_offload", U), ("n_cache", U), ("has_qk_norm", U), ("n_vocab", U)]
+                ("seed", C.c_ulonglong), ("n_offload", U), ("n_cache", U), ("has_qk_norm", U), ("n_vocab", U),
+                ("expert_layout", U)]
 
 
 class MoeDesc(C.Structure):

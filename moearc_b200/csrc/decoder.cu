@@ -46,7 +46,8 @@ int moe_forward_impl(moearc_x_moe *m, const float *x, unsigned n_tokens, const f
                      const float *router_w, const float *router_b, const void *gateup_packed,
                      const void *down_packed, const float *residual, float *out,
                      std::vector<cudaEvent_t> *marks = nullptr, std::vector<int> *kinds = nullptr,
-                     const moe_offload *off = nullptr, unsigned long long *span = nullptr);
+                     const moe_offload *off = nullptr, unsigned long long *span = nullptr, bool tc = false,
+                     int span_cta = 0);
 int moe_decode_grid(moearc_x_moe *m);
 size_t attn_scratch_bytes(size_t n_heads, size_t head_dim, int n_splits);
 int attn_launch(moearc_ctx *c, float *out, const float *q, const void *kp, const void *vp,
@@ -132,6 +133,8 @@ struct moearc_x_decoder {
     // of per-block kernels otherwise (offloaded experts, head_dim 128, ...) or on request
     step_plan *step = nullptr;
     bool use_step = false;
+    // resident blocks' expert banks in the tc layout, run on the block-scaled FP4 tensor cores
+    bool tc = false;
     // the chain's expert kernels' CTA timestamps per block (moearc_x_decoder_kernel_spans), or null
     unsigned long long *spans = nullptr;
     int span_cta = 0;
@@ -278,7 +281,8 @@ int enqueue_step(moearc_x_decoder *d, step_marks *pm = nullptr) {
         rc = moe_forward_impl(d->moe, d->h, 1, b.ffn_norm, cfg.rms_eps, b.router, nullptr, b.gateup, b.down,
                               d->h, d->h, pm ? &pm->ev : nullptr, pm ? &pm->kind : nullptr,
                               l < cfg.n_offload ? &off : nullptr,
-                              d->spans ? d->spans + (size_t)l * 2 * d->span_cta * 3 : nullptr);
+                              d->spans ? d->spans + (size_t)l * 2 * d->span_cta * 3 : nullptr,
+                              d->tc && l >= cfg.n_offload, d->span_cta);
         if (rc) return rc;
     }
     if (launch_pdl(k_step_end, dim3(1), dim3(512), 0, c->stream, d->out, (const float *)d->h,
@@ -329,6 +333,8 @@ moearc_x_decoder *moearc_x_decoder_create(moearc_ctx *c, const moearc_x_decoder_
     d->qkv = dense_create(c, d->n_qkv, H, 0);
     d->wo = dense_create(c, H, d->Dq, 1);
     if (!d->moe || !d->qkv || !d->wo) return fail();
+    d->tc = g.expert_layout == 0 && g.expert_type == T_MXFP4 && moearc_x_moe_has_tc(d->moe) &&
+            g.n_offload < g.n_layer;
     if (g.n_vocab) {
         d->head = dense_create(c, (int)g.n_vocab, H, 1);
         d->w_out = d->alloc((size_t)g.n_vocab * H * 2);
@@ -469,6 +475,9 @@ moearc_x_decoder *moearc_x_decoder_create(moearc_ctx *c, const moearc_x_decoder_
         if (offl) {
             b.gateup = static_cast<uint8_t *>(pack_tmp);
             b.down = static_cast<uint8_t *>(pack_tmp) + g.n_expert * gu_stride;
+        } else if (d->tc) {
+            b.gateup = d->alloc(moearc_x_moe_tc_bytes(&md, 0));
+            b.down = d->alloc(moearc_x_moe_tc_bytes(&md, 1));
         } else {
             b.gateup = d->alloc(2 * bank_bytes);
             b.down = d->alloc(bank_bytes);
@@ -501,7 +510,10 @@ moearc_x_decoder *moearc_x_decoder_create(moearc_ctx *c, const moearc_x_decoder_
         ok &= synth(c, s8, blocks, ekind, tensor_seed(g.seed, 8, l), esig) == OK;
         ok &= synth(c, s8 + bank_bytes, blocks, ekind, tensor_seed(g.seed, 9, l), esig) == OK;
         ok &= synth(c, s8 + 2 * bank_bytes, blocks, ekind, tensor_seed(g.seed, 10, l), esig) == OK;
-        ok &= moearc_x_moe_pack(d->moe, s8, s8 + bank_bytes, s8 + 2 * bank_bytes, g.n_expert, b.gateup, b.down) == OK;
+        if (d->tc && !offl)
+            ok &= moearc_x_moe_pack_tc(d->moe, s8, s8 + bank_bytes, s8 + 2 * bank_bytes, g.n_expert, b.gateup, b.down) == OK;
+        else
+            ok &= moearc_x_moe_pack(d->moe, s8, s8 + bank_bytes, s8 + 2 * bank_bytes, g.n_expert, b.gateup, b.down) == OK;
         if (offl && ok) {
             const size_t gb = g.n_expert * gu_stride, db = g.n_expert * dn_stride;
             void *gdev = nullptr, *ddev = nullptr;
@@ -530,7 +542,7 @@ moearc_x_decoder *moearc_x_decoder_create(moearc_ctx *c, const moearc_x_decoder_
     cudaFree(staging);
     if (pack_tmp) cudaFree(pack_tmp);
     if (!ok) return fail();
-    if (!g.n_offload && !g.has_qk_norm) {
+    if (!g.n_offload && !g.has_qk_norm && !d->tc) {
         std::vector<step_layer> sl(g.n_layer);
         for (unsigned l = 0; l < g.n_layer; ++l) {
             const auto &b = d->L[l];
@@ -876,8 +888,16 @@ void *moearc_x_decoder_tensor(moearc_x_decoder *d, int which, unsigned layer, un
         case 6: p = (void *)b.table; n = (g.n_ctx + PAGE_TOKENS - 1) / PAGE_TOKENS * 4; break;
         case 7: p = b.wqkv; n = (unsigned long)d->n_qkv * H * 2; break;
         case 8: p = b.wo; n = H * d->Dq * 2; break;
-        case 9: p = b.gateup; n = 2 * bank; break;
-        case 10: p = b.down; n = bank; break;
+        case 9:
+        case 10: {
+            // the tc layout for resident blocks of a tc decoder, else the fragment layout
+            const bool tcl = d->tc && layer >= g.n_offload;
+            moearc_x_moe_desc md{g.n_embd, g.n_ff, g.n_expert, g.n_expert_used, g.gating, g.act, g.alpha, g.limit,
+                                 g.expert_type, 1};
+            p = which == 9 ? b.gateup : b.down;
+            n = tcl ? moearc_x_moe_tc_bytes(&md, which - 9) : (which == 9 ? 2 * bank : bank);
+            break;
+        }
         case 12: p = d->step ? static_cast<unsigned *>(step_buffer(d->step, 0)) + (size_t)layer * g.n_expert_used : nullptr;
                  n = p ? g.n_expert_used * 4 : 0; break;
         case 13: p = d->step ? static_cast<float *>(step_buffer(d->step, 1)) + (size_t)layer * g.n_expert_used : nullptr;

@@ -37,6 +37,7 @@
 
 #include <climits>
 #include "tma.cuh"
+#include "xtc.cuh"
 
 using namespace moearc;
 
@@ -81,6 +82,9 @@ struct moearc_x_moe {
     float *act_f32;    // [T_max*K][I], the activation, kept for inspection
     unsigned *ctr;     // route done counter, gate-up unit counters, down unit counters
     int *status;
+    // the batch-1 decode path on the block-scaled FP4 tensor cores (xtc.cu), for MXFP4 banks
+    // packed in the tc layout; null when the shape has none
+    xtc_plan *xtc = nullptr;
 };
 
 namespace {
@@ -773,6 +777,7 @@ struct xroute_args {
     uint32_t *xfrag;      // [T][H/32][2][4][4]
     float *x_out;         // [T][H]: the routed activation (normalised), for the host's experts; or null
     int *status;
+    uint8_t *xdig;        // one token: its E2M1 digits for the tc path (xtc.cuh) in place of xfrag; or null
 };
 
 // One router row per warp, staged in shared memory by a bulk copy issued before the wait; the
@@ -853,8 +858,15 @@ __global__ void __launch_bounds__(XROUTE_WARPS * 32) k_xroute(xroute_args a) {
             for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
             if (lane == 0) a.logits[(size_t)t * a.E + e] = a.rbias ? acc + a.rbias[e] : acc;
         }
-        // B fragments of this token: [block][part][q][j] = pair (x[32b+4q+j], x[32b+4q+16+j])
         const int nblk = H / 32;
+        if (a.xdig) {
+            // the tc path: each 32-element block's digits, one warp a block
+            for (int b = blockIdx.x * XROUTE_WARPS + warp; b < nblk; b += gridDim.x * XROUTE_WARPS)
+                tc_write_digits(xs[32 * b + lane], lane, a.xdig, b);
+            __syncthreads();
+            continue;
+        }
+        // B fragments of this token: [block][part][q][j] = pair (x[32b+4q+j], x[32b+4q+16+j])
         for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < nblk * 16; i += gridDim.x * blockDim.x) {
             const int j = i & 3, q = (i >> 2) & 3, b = i >> 4;
             uint32_t hi, lo;
@@ -2449,6 +2461,8 @@ moearc_x_moe *moearc_x_moe_create(moearc_ctx *c, const moearc_x_moe_desc *d) {
     m->f_bar = reinterpret_cast<unsigned *>(b + o_fbar);
     cudaMemsetAsync(m->mem, 0, off, c->stream);
     x_parts_empty(m);
+    if (m->wtype == T_MXFP4 && m->xpath)
+        m->xtc = xtc_create(c, m->H, m->I, m->E, m->K, m->gating, m->act, m->alpha, m->limit);
     // per-kernel attribute shared by every layer object: the most any of them may use
     const int smem_attr = 226 * 1024;
     if (set_smem(k_moe_rows<39>, smem_attr) != cudaSuccess ||
@@ -2474,6 +2488,7 @@ moearc_x_moe *moearc_x_moe_create(moearc_ctx *c, const moearc_x_moe_desc *d) {
 void moearc_x_moe_destroy(moearc_x_moe *m) {
     if (!m) return;
     cudaStreamSynchronize(m->ctx->stream);
+    xtc_destroy(m->xtc);
     cudaFree(m->mem);
     delete m;
 }
@@ -2511,7 +2526,7 @@ int moe_forward_impl(moearc_x_moe *m, const float *x, unsigned n_tokens, const f
                      const float *router_w, const float *router_b, const void *gateup_packed,
                      const void *down_packed, const float *residual, float *out,
                      std::vector<cudaEvent_t> *marks, std::vector<int> *kinds, const moe_offload *off,
-                     unsigned long long *span) {
+                     unsigned long long *span, bool tc, int span_cta) {
     auto mark = [&](int k) {
         if (!marks) return;
         cudaEvent_t e;
@@ -2535,6 +2550,38 @@ int moe_forward_impl(moearc_x_moe *m, const float *x, unsigned n_tokens, const f
     // an offloaded block runs the decode path with the fetch kernels (gateup_packed and
     // down_packed are then device-visible pointers of pinned host banks)
     if (off && (!m->xpath || !off->gu_stage || !off->dn_stage)) return ERR_ARG;
+    if (tc) {
+        // banks in the tc layout: one token, resident (xtc.cu)
+        if (!m->xtc || T != 1 || off) return ERR_ARG;
+        xroute_args xr{x, norm_w, eps, router_w, router_b, T, m->H, m->E, m->logits, m->xfrag, nullptr, m->status,
+                       xtc_xdig(m->xtc)};
+        if (launch_pdl(k_xroute, dim3(m->x_route_grid), dim3(XROUTE_WARPS * 32), (size_t)m->x_route_smem, c->stream,
+                       xr) != cudaSuccess)
+            return ERR;
+        mark(3);
+        xtc_run r{};
+        r.logits = m->logits;
+        r.xdig = xtc_xdig(m->xtc);
+        r.gu_bank = static_cast<const uint8_t *>(gateup_packed);
+        r.dn_bank = static_cast<const uint8_t *>(down_packed);
+        r.residual = residual;
+        r.out = out;
+        r.idx_out = m->idx;
+        r.wts_out = m->wts;
+        r.act_out = m->act_f32;
+        r.bias_gu = m->bias_gu;
+        r.bias_dn = m->bias_dn;
+        r.poll_ns = m->x_poll_ns;
+        r.phantom = m->x_phantom;
+        r.span = span;
+        r.span_cta = span_cta ? span_cta : xtc_grid(m->xtc);
+        r.status = m->status;
+        if (xtc_launch_gu(m->xtc, r) != OK) return ERR;
+        mark(4);
+        if (xtc_launch_dn(m->xtc, r) != OK) return ERR;
+        mark(5);
+        return ls.finish();
+    }
     auto fused_args = [&]() {
         xfused_args f{};
         f.x = x;
@@ -2785,7 +2832,7 @@ int moe_forward_impl(moearc_x_moe *m, const float *x, unsigned n_tokens, const f
 }
 
 // CTAs of each decode-path expert kernel (their span records, per kernel).
-int moe_decode_grid(moearc_x_moe *m) { return m && m->xpath ? m->x_grid : 0; }
+int moe_decode_grid(moearc_x_moe *m) { return m && m->xpath ? std::max(m->x_grid, xtc_grid(m->xtc)) : 0; }
 
 }  // namespace moearc
 
@@ -2795,7 +2842,34 @@ int moearc_x_moe_forward(moearc_x_moe *m, const float *x, unsigned n_tokens, con
                          const float *router_b, const void *gateup_packed, const void *down_packed,
                          const float *residual, float *out) {
     return moe_forward_impl(m, x, n_tokens, nullptr, 0.f, router_w, router_b, gateup_packed, down_packed,
-                            residual, out, nullptr, nullptr, nullptr, nullptr);
+                            residual, out, nullptr, nullptr, nullptr, nullptr, false, 0);
+}
+
+unsigned long moearc_x_moe_tc_bytes(const moearc_x_moe_desc *d, int which) {
+    if (!d || d->wtype != T_MXFP4 || d->n_embd % 64 || d->n_ff % 64) return 0;
+    return which == 0 ? (unsigned long)tc_gu_stride((int)d->n_embd, (int)d->n_ff) * d->n_expert
+                      : (unsigned long)tc_dn_stride((int)d->n_embd, (int)d->n_ff) * d->n_expert;
+}
+
+int moearc_x_moe_has_tc(moearc_x_moe *m) { return m && m->xtc ? 1 : 0; }
+
+int moearc_x_moe_pack_tc(moearc_x_moe *m, const void *gate, const void *up, const void *down, unsigned n_expert,
+                         void *gateup_tc, void *down_tc) {
+    if (!m || !gate || !up || !down || !gateup_tc || !down_tc) return ERR;
+    if (m->wtype != T_MXFP4 || m->H % 64 || m->I % 64 || n_expert == 0) return ERR_ARG;
+    if ((reinterpret_cast<uintptr_t>(gateup_tc) | reinterpret_cast<uintptr_t>(down_tc)) & 15) return ERR_ARG;
+    launch_scope ls(m->ctx, "moe_pack_tc", (unsigned long)n_expert, 2);
+    const int rc = xtc_pack(m->ctx, m->H, m->I, gate, up, down, n_expert, gateup_tc, down_tc);
+    return rc ? rc : ls.finish();
+}
+
+int moearc_x_moe_forward_tc(moearc_x_moe *m, const float *x, unsigned n_tokens, const float *router_w,
+                            const float *router_b, const void *gateup_tc, const void *down_tc, const float *residual,
+                            float *out) {
+    if (!m) return ERR;
+    if (!m->xtc || n_tokens > 1) return ERR_ARG;
+    return moe_forward_impl(m, x, n_tokens, nullptr, 0.f, router_w, router_b, gateup_tc, down_tc, residual, out,
+                            nullptr, nullptr, nullptr, nullptr, true, 0);
 }
 
 void *moearc_x_moe_buffer(moearc_x_moe *m, int which) {
@@ -2834,6 +2908,7 @@ int moearc_x_moe_status(moearc_x_moe *m) {
         // a wait that gave up can leave partial slots stored and never read: empty them all
         cudaMemsetAsync(m->status, 0, sizeof(int), m->ctx->stream);
         x_parts_empty(m);
+        xtc_reset(m->xtc);
     }
     return st;
 }

@@ -55,6 +55,10 @@ class DecoderConfig:
     has_qk_norm: int = 0
     # rows of the output head (logits after the final norm, moe.rs:2434-2437); 0 = none
     n_vocab: int = 0
+    # resident blocks' expert banks: 0 = the tensor-core layout run on the block-scaled FP4
+    # tensor cores where the shape has one (MXFP4), 1 = the fragment layout (the persistent step
+    # kernel needs it)
+    expert_layout: int = 0
 
     def yarn(self, factor: float, n_ctx_orig: int, beta_fast: float = 32.0, beta_slow: float = 1.0):
         """YaRN parameters the way reference.rs:572-591 derives them (RopeScaling::yarn)."""
@@ -192,7 +196,8 @@ class Decoder:
         for layer in range(self.cfg.n_layer):
             s = self.tensor(14, layer, np.uint64).reshape(2, -1, 3).astype(np.int64)
             for k in range(2):
-                ends, waits = s[k, :, 2], s[k, :, 1]
+                live = s[k, :, 1] > 0  # records of CTAs the kernel launched
+                ends, waits = s[k, live, 2], s[k, live, 1]
                 tot[k] += (ends.max() - waits.min()) / 1e6
         return tot[0], tot[1]
 

@@ -66,6 +66,34 @@ class MoeLayer:
                                                None if residual is None else residual.ptr, out.ptr)
         self.ctx._finish(rc, "moe_forward")
 
+    def has_tc(self) -> bool:
+        """Whether one-token calls can run on the block-scaled FP4 tensor cores (xtc.cu)."""
+        return bool(self.ctx.lib.moearc_x_moe_has_tc(self.h))
+
+    def pack_tc(self, gate: DeviceBuffer, up: DeviceBuffer, down: DeviceBuffer) -> None:
+        """Repack GGUF-layout MXFP4 banks (device) into the tensor-core layout for forward_tc."""
+        if not self.has_tc():
+            raise BadArgument("this layer has no tensor-core path")
+        E = self.desc.n_expert
+        self.gateup_tc = self.ctx.alloc(self.ctx.lib.moearc_x_moe_tc_bytes(C.byref(self.desc), 0))
+        self.down_tc = self.ctx.alloc(self.ctx.lib.moearc_x_moe_tc_bytes(C.byref(self.desc), 1))
+        rc = self.ctx.lib.moearc_x_moe_pack_tc(self.h, gate.ptr, up.ptr, down.ptr, E, self.gateup_tc.ptr,
+                                               self.down_tc.ptr)
+        self.ctx._finish(rc, "moe_pack_tc")
+
+    def forward_tc(self, x: DeviceBuffer, router_w: DeviceBuffer, out: DeviceBuffer,
+                   router_b: DeviceBuffer | None = None, residual: DeviceBuffer | None = None) -> None:
+        """forward for one token on the tensor-core layout banks of pack_tc."""
+        H = self.desc.n_embd
+        x.require("moe input", 4 * H)
+        out.require("moe output", 4 * H)
+        router_w.require("router weights", 4 * self.desc.n_expert * H)
+        rc = self.ctx.lib.moearc_x_moe_forward_tc(self.h, x.ptr, 1, router_w.ptr,
+                                                  None if router_b is None else router_b.ptr,
+                                                  self.gateup_tc.ptr, self.down_tc.ptr,
+                                                  None if residual is None else residual.ptr, out.ptr)
+        self.ctx._finish(rc, "moe_forward_tc")
+
     def status(self) -> int:
         st = self.ctx.lib.moearc_x_moe_status(self.h)
         if st < 0:

@@ -34,14 +34,16 @@ def ctx():
                                                      (True, O.Q4_0, True), (True, O.MXFP4, False),
                                                      (True, O.Q4_0, False)])
 def test_small_gpt_oss_shaped_decoder_matches_the_oracle(ctx, graph, etype, step_kernel):
-    """The decoder with the whole step as one persistent kernel (step_kernel) and as the chain
-    of per-block kernels, each against the oracle."""
+    """The decoder with the whole step as one persistent kernel (step_kernel, fragment-layout
+    experts) and as the chain of per-block kernels (MXFP4 experts on the block-scaled FP4 tensor
+    cores, Q4_0 on the fragment kernels), each against the oracle."""
     cfg = DecoderConfig(n_layer=3, n_embd=256, n_head=8, n_head_kv=2, head_dim=64, n_expert=8,
                         n_expert_used=2, n_ff=128, n_swa=40, swa_pattern=2, n_ctx=256, seed=0xDEC0DE,
-                        expert_type=etype)
+                        expert_type=etype, expert_layout=1 if step_kernel else 0)
     cfg.yarn(32.0, 4096)
     dec = Decoder(ctx, cfg)
-    assert dec.has_step_kernel() and not dec.uses_step_kernel()  # the chain by default
+    # the tc layout (MXFP4, expert_layout 0) has no persistent kernel; the chain is the default
+    assert dec.has_step_kernel() == (step_kernel or etype == O.Q4_0) and not dec.uses_step_kernel()
     dec.use_step_kernel(step_kernel)
     dec.use_graph(graph)
     c, arr, keep, out_norm = host_model(dec)
@@ -76,8 +78,17 @@ def big(ctx):
     dec.close()
 
 
+@pytest.fixture(scope="module")
+def big_frag(ctx):
+    """The same two blocks with fragment-layout experts, for the persistent step kernel."""
+    dec = Decoder(ctx, DecoderConfig.gpt_oss_120b(n_layer=2, n_ctx=32800, seed=0x120B, expert_layout=1))
+    model = host_model(dec)
+    yield dec, model
+    dec.close()
+
+
 @pytest.mark.parametrize("graph,step_kernel", [(False, False), (True, False), (True, True)])
-def test_gpt_oss_120b_shaped_blocks_match_the_oracle(big, graph, step_kernel):
+def test_gpt_oss_120b_shaped_blocks_match_the_oracle(request, graph, step_kernel):
     """The configuration the benchmark times, token by token against the oracle's decode step
     for 144 tokens: past the 128-key window of block 0 (crates/moearc-engine/tests/
     gptoss_forward.rs:393-418 runs past the window for the same reason) and across page
@@ -92,7 +103,7 @@ def test_gpt_oss_120b_shaped_blocks_match_the_oracle(big, graph, step_kernel):
     through its own token's K/V entries, which each side rounds to bf16 itself: in the first
     tokens that key carries much of the attention, and a one-step difference in one of its
     values moves the output by up to ~3e-4; the bound is the composed decoder's 1e-3."""
-    dec, (c, arr, keep, out_norm) = big
+    dec, (c, arr, keep, out_norm) = request.getfixturevalue("big_frag" if step_kernel else "big")
     dec.use_step_kernel(step_kernel)
     dec.use_graph(graph)
     dec.set_pos(0)
@@ -148,12 +159,12 @@ def test_gpt_oss_120b_shaped_blocks_match_the_oracle(big, graph, step_kernel):
 
 
 @pytest.mark.parametrize("depth,step_kernel", [(8192, False), (32768, False), (8192, True), (32768, True)])
-def test_gpt_oss_120b_shaped_blocks_at_depth_match_the_oracle(big, depth, step_kernel):
+def test_gpt_oss_120b_shaped_blocks_at_depth_match_the_oracle(request, depth, step_kernel):
     """A decode step after `depth` cached tokens (configs[2] at 8K and 32K): the attention split
     count is decided on the device from the span (at least 256 keys a split; 33 splits at
     32768), the windowed block reads the last 128 keys of its ring, the full block all of them.
     The device's synthetic cache is copied into the oracle's pools before two steps."""
-    dec, (c, arr, keep, out_norm) = big
+    dec, (c, arr, keep, out_norm) = request.getfixturevalue("big_frag" if step_kernel else "big")
     dec.use_step_kernel(step_kernel)
     dec.use_graph(True)
     dec.fill_kv(depth, seed=0xD00 + depth)
@@ -210,11 +221,11 @@ def test_fill_kv_sets_the_depth_and_decoding_continues(ctx):
 @pytest.mark.parametrize("etype,n_expert,k", [(O.MXFP4, 8, 2), (O.Q4_0, 16, 4)])
 def test_expert_offload_matches_the_resident_decoder(ctx, etype, n_expert, k):
     """Blocks whose experts live in pinned host memory (fetched over PCIe into device slots each
-    step) give the same bits as the all-resident decoder: the fetch changes where the banks are
-    read from, not the arithmetic."""
+    step) give the same bits as the all-resident decoder with the same (fragment) expert layout:
+    the fetch changes where the banks are read from, not the arithmetic."""
     kw = dict(n_layer=3, n_embd=256, n_head=8, n_head_kv=2, head_dim=64, n_expert=n_expert,
               n_expert_used=k, n_ff=128, expert_type=etype, n_swa=40, swa_pattern=2, n_ctx=128,
-              seed=0x0FF1)
+              seed=0x0FF1, expert_layout=1)
     res = Decoder(ctx, DecoderConfig(**kw))
     off = Decoder(ctx, DecoderConfig(**kw, n_offload=2))
     assert not off.has_step_kernel()
@@ -237,11 +248,11 @@ def test_expert_residency_cache_gives_the_resident_bits_and_fetches_less(ctx, et
     reference's ExpertCache with StaticSplit's never-evict-what-the-step-needs rule): the output
     is bit-identical to the all-resident decoder, the first step fetches every routed expert,
     no step fetches more than pure streaming would, and a cache that holds every expert stops
-    fetching once each has been seen."""
+    fetching once each has been seen (both decoders with fragment-layout experts)."""
     n_cache = n_expert if extra is None else k + extra
     kw = dict(n_layer=3, n_embd=256, n_head=8, n_head_kv=2, head_dim=64, n_expert=n_expert,
               n_expert_used=k, n_ff=128, expert_type=etype, n_swa=40, swa_pattern=2, n_ctx=128,
-              seed=0x0FF1)
+              seed=0x0FF1, expert_layout=1)
     res = Decoder(ctx, DecoderConfig(**kw))
     cached = Decoder(ctx, DecoderConfig(**kw, n_offload=2, n_cache=n_cache))
     steps, prev = 16, 0
@@ -391,9 +402,9 @@ def test_qk_norm_and_the_output_head_match_the_oracle(ctx, qk, step_kernel):
 
     cfg = DecoderConfig(n_layer=3, n_embd=256, n_head=8, n_head_kv=2, head_dim=64, n_expert=8,
                         n_expert_used=2, n_ff=128, n_swa=40, swa_pattern=2, n_ctx=96, seed=0x9C0D,
-                        has_qk_norm=qk, n_vocab=512)
+                        has_qk_norm=qk, n_vocab=512, expert_layout=1 if step_kernel else 0)
     dec = Decoder(ctx, cfg)
-    assert dec.has_step_kernel() == (not qk)  # the persistent kernel has no QK-norm
+    assert dec.has_step_kernel() == bool(step_kernel)  # no QK-norm and no tc layout in the persistent kernel
     if step_kernel:
         dec.use_step_kernel(True)
     c, arr, keep, out_norm = host_model(dec)
@@ -539,7 +550,7 @@ def test_a_grid_barrier_that_runs_out_reports_it_and_the_next_step_is_exact(ctx)
     the status word reports the timeout (and reading clears it). With the limit restored, the
     same step from the same position gives the bits of an undisturbed decoder."""
     cfg = DecoderConfig(n_layer=2, n_embd=256, n_head=8, n_head_kv=2, head_dim=64, n_expert=8,
-                        n_expert_used=2, n_ff=128, n_swa=40, n_ctx=64, seed=0x71AE)
+                        n_expert_used=2, n_ff=128, n_swa=40, n_ctx=64, seed=0x71AE, expert_layout=1)
     dec = Decoder(ctx, cfg)
     dec.use_step_kernel(True)
     x0 = O.synth_normal_f32(0x7100, cfg.n_embd, 1.0)
