@@ -57,11 +57,13 @@ UNIT = "tok/s"
 
 def expert_traffic(fused: bool, tc: bool = False) -> float | None:
     """DRAM read + write bytes of one launch of the roofline kernel, from the committed ncu
-    capture summary (profiles/moe_and_dense_kernels_gpt_oss_120b_1layer.md: the fused gate-up +
+    capture summaries (profiles/decode_expert_kernels_tc_gpt_oss_120b.md for the tensor-core gate-up;
+    profiles/moe_and_dense_kernels_gpt_oss_120b_1layer.md: the fused gate-up +
     down row, the gate-up row of the fragment kernels, or the tensor-core gate-up row); None if
     absent."""
     import re
-    p = os.path.join(ROOT, "profiles", "moe_and_dense_kernels_gpt_oss_120b_1layer.md")
+    p = os.path.join(ROOT, "profiles", "decode_expert_kernels_tc_gpt_oss_120b.md" if tc and not fused
+                     else "moe_and_dense_kernels_gpt_oss_120b_1layer.md")
     if not os.path.exists(p):
         return None
     row = "| `k_moe_fused<39,false>`" if fused else ("| `k_xtc<0>`" if tc else "| `k_xexpert<39,0>`")
@@ -937,7 +939,7 @@ def main() -> None:
                      "kernel": ("moe gate-up + SwiGLU + down + combine, one launch (k_moe_fused, MXFP4, tensor cores)"
                                 if fused else
                                 "moe gate-up, MXFP4 on the block-scaled FP4 tensor cores (k_xtc<0>, tcgen05.mma "
-                                "kind::mxf4, 16 E2M1 digits of the activation)" if tc_layout else
+                                "kind::mxf4, 12 E2M1 digits of the activation)" if tc_layout else
                                 "moe gate-up grouped GEMV (MXFP4, mma.sync fragments, k_xexpert<39,0>)"),
                      "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                      "peak_kind": peak_kind, "traffic": expert_traffic(fused, tc_layout),
