@@ -62,8 +62,7 @@ struct dense_args {
     const int *pos;
     dense_rope rope;
     dense_kv kv;
-    float *part;    // [ntr][maxc][16]
-    unsigned *ctr;  // per unit
+    float *part;    // [ntr][maxc][16] partial slots, PART_EMPTY when free
     int *status;
 };
 
@@ -76,7 +75,6 @@ __global__ void __launch_bounds__(WARPS * 32, 1) k_dense(dense_args a) {
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ __align__(8) uint64_t bars[WARPS][STAGES];
     __shared__ float red[WARPS];
-    __shared__ int fin[MAX_LOCAL];
     const int trace_row = (int)blockIdx.x + (a.mode == 0 ? 0 : 1024);
     (void)trace_row;
     TRACE(0);
@@ -285,37 +283,54 @@ __global__ void __launch_bounds__(WARPS * 32, 1) k_dense(dense_args a) {
         for (int w = 0; w < WARPS; ++w) s += psm[((size_t)w * MAX_LOCAL + ltr) * 16 + row];
         const int tr = tr0 + ltr;
         const int slot = cta - cta_of(a.T, G, (long)tr * a.nkt);
-        a.part[((size_t)tr * a.maxc + slot) * 16 + row] = s;
-    }
-    fence_acq_rel_gpu();
-    __syncthreads();
-    // one arrival per unit touched; the CTAs that touch a unit are a contiguous run
-    if ((int)threadIdx.x <= u1 - u0) {
-        const int u = u0 + threadIdx.x;
-        const long first = (long)u * a.unit_trs * a.nkt, last = (long)(u + 1) * a.unit_trs * a.nkt - 1;
-        const unsigned target = (unsigned)(cta_of(a.T, G, last) - cta_of(a.T, G, first) + 1);
-        fin[threadIdx.x] = atomicAdd(a.ctr + u, 1u) == target - 1;
+        st_part(a.part + ((size_t)tr * a.maxc + slot) * 16 + row, s);
     }
     __syncthreads();
     TRACE(9);
-    // finish the units this CTA completed last: warp i takes the i-th unit touched
-    if (warp > u1 - u0 || !fin[warp]) return;
-    fence_acq_rel_gpu();
+    // The unit's finisher is the CTA holding its first tile: warp i takes the i-th unit touched
+    // when this CTA is that one, and polls every contributor's partial slot (bounded), with no
+    // fence or arrival count between the last partial and the unit's result.
+    if (warp > u1 - u0) return;
     const int unit = u0 + warp;
-    if (lane == 0) a.ctr[unit] = 0;
-    // a row's contributors summed in CTA order; their loads are issued together first
+    if (cta_of(a.T, G, (long)unit * a.unit_trs * a.nkt) != cta) return;
+    // a row's contributors summed in CTA order; each slot is taken once stored, then emptied
     auto row_value = [&](int row) {
         const int tr = row >> 4;
         const int c0 = cta_of(a.T, G, (long)tr * a.nkt), c1 = cta_of(a.T, G, (long)(tr + 1) * a.nkt - 1);
         const int nc = c1 - c0 + 1;
-        const float *pp = a.part + (size_t)tr * a.maxc * 16 + (row & 15);
-        float t[MAX_CONTRIB];
-#pragma unroll
-        for (int k = 0; k < MAX_CONTRIB; ++k) t[k] = (k < nc) ? __ldcg(pp + k * 16) : 0.f;
-        float s = 0.f;
-#pragma unroll
-        for (int k = 0; k < MAX_CONTRIB; ++k)
-            if (k < nc) s += t[k];
+        float *pp = a.part + (size_t)tr * a.maxc * 16 + (row & 15);
+        static_assert(MAX_CONTRIB == 4, "four slots below");
+        uint32_t v0 = 0, v1 = 0, v2 = 0, v3 = 0;
+        unsigned long long t0 = 0;
+        for (;;) {
+            v0 = ld_part(pp);
+            v1 = nc > 1 ? ld_part(pp + 16) : 0u;
+            v2 = nc > 2 ? ld_part(pp + 32) : 0u;
+            v3 = nc > 3 ? ld_part(pp + 48) : 0u;
+            if (v0 != PART_EMPTY && v1 != PART_EMPTY && v2 != PART_EMPTY && v3 != PART_EMPTY) break;
+            const unsigned long long now = xnow();
+            if (t0 == 0) {
+                t0 = now;
+            } else if (now - t0 > XPOLL_NS) {
+                atomicOr(a.status, STATUS_WAIT_TIMEOUT);  // the step's output is then invalid
+                break;
+            }
+        }
+        const float e = __uint_as_float(PART_EMPTY);
+        float s = __uint_as_float(v0);
+        st_part(pp, e);
+        if (nc > 1) {
+            s += __uint_as_float(v1);
+            st_part(pp + 16, e);
+        }
+        if (nc > 2) {
+            s += __uint_as_float(v2);
+            st_part(pp + 32, e);
+        }
+        if (nc > 3) {
+            s += __uint_as_float(v3);
+            st_part(pp + 48, e);
+        }
         return s;
     };
     if (a.mode == 1) {
@@ -386,7 +401,6 @@ struct dense_gemv {
     int ntr, nkt, grid, smem, maxc;
     long T;
     float *part;
-    unsigned *ctr;
     int *status;
     void *mem;
 };
@@ -437,16 +451,15 @@ dense_gemv *dense_create(moearc_ctx *c, int n_rows, int n_cols, int mode) {
     g->maxc = maxc;
     g->smem = RING_BYTES + (n_cols / 16) * PARTS * 32 + WARPS * MAX_LOCAL * 16 * 4;
     const size_t part_b = sizeof(float) * (size_t)g->ntr * maxc * 16;
-    const size_t ctr_b = sizeof(unsigned) * (size_t)g->ntr;
-    if (cudaMalloc(&g->mem, part_b + ctr_b + 256) != cudaSuccess) {
+    if (cudaMalloc(&g->mem, part_b + 256) != cudaSuccess) {
         cudaGetLastError();
         delete g;
         return nullptr;
     }
     g->part = static_cast<float *>(g->mem);
-    g->ctr = reinterpret_cast<unsigned *>(static_cast<uint8_t *>(g->mem) + part_b);
-    g->status = reinterpret_cast<int *>(static_cast<uint8_t *>(g->mem) + part_b + ctr_b);
-    cudaMemsetAsync(g->mem, 0, part_b + ctr_b + 256, c->stream);
+    g->status = reinterpret_cast<int *>(static_cast<uint8_t *>(g->mem) + part_b);
+    cudaMemsetAsync(g->mem, 0, part_b + 256, c->stream);
+    parts_empty(g->part, (size_t)g->ntr * maxc * 16, c->stream, c->sm_count);
     // The attribute is per kernel, shared by every plan: set it to the most any plan may use,
     // not to this plan's need.
     if (g->smem > 200 * 1024 ||
@@ -465,9 +478,9 @@ int dense_status(dense_gemv *g) {
         cudaStreamSynchronize(g->c->stream) != cudaSuccess)
         return ERR;
     if (st) {
-        // a wait that gave up can leave arrival counts behind: zero them
+        // a wait that gave up can leave partials stored and never taken: empty every slot
         cudaMemsetAsync(g->status, 0, sizeof(int), g->c->stream);
-        cudaMemsetAsync(g->ctr, 0, sizeof(unsigned) * (size_t)g->ntr, g->c->stream);
+        parts_empty(g->part, (size_t)g->ntr * g->maxc * 16, g->c->stream, g->c->sm_count);
     }
     return st;
 }
@@ -506,7 +519,6 @@ int dense_run(dense_gemv *g, const void *w_packed, const float *in, const float 
     if (rope) a.rope = *rope;
     if (kv) a.kv = *kv;
     a.part = g->part;
-    a.ctr = g->ctr;
     a.status = g->status;
     return launch_pdl(k_dense, dim3(g->grid), dim3(WARPS * 32), (size_t)g->smem, g->c->stream, a) == cudaSuccess
                ? OK

@@ -13,10 +13,11 @@
 //   body      warps multiply 16x64 bf16 tiles on the tensor cores; the activation enters as
 //             three bf16 columns (its rounding and two rounding residuals), ~24 bits of the
 //             f32 value;
-//   epilogue  per-tile-row sums of the CTA's warps go to a partial buffer; the last CTA to
-//             finish a unit (a head for Q/K/V, a tile-row for O) sums its partials in a fixed
-//             order and either applies RoPE and writes q (f32) and K/V (bf16, into the paged
-//             cache at this step's page and slot), or adds the residual.
+//   epilogue  per-tile-row sums of the CTA's warps go to partial slots (an empty marker until
+//             stored); the CTA holding a unit's first tile (a head for Q/K/V, a tile-row for O)
+//             polls the unit's slots (bounded), sums them in a fixed order, empties them and
+//             either applies RoPE and writes q (f32) and K/V (bf16, into the paged cache at this
+//             step's page and slot), or adds the residual.
 #pragma once
 
 #include "common.cuh"
