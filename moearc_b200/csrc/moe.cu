@@ -794,6 +794,7 @@ __global__ void __launch_bounds__(XROUTE_WARPS * 32) k_xroute(xroute_args a) {
     const int H = a.H, n4 = H / 4;
     float *wrow = reinterpret_cast<float *>(smem) + (size_t)warp * H;
     float *xs = reinterpret_cast<float *>(smem) + (size_t)XROUTE_WARPS * H;
+    float *nws = xs + H;  // the norm weights, static: staged before the wait
     const int e0 = blockIdx.x * XROUTE_WARPS + warp;
     const int nw = gridDim.x * XROUTE_WARPS;
     if (lane == 0) {
@@ -804,6 +805,9 @@ __global__ void __launch_bounds__(XROUTE_WARPS * 32) k_xroute(xroute_args a) {
             bulk_g2s(wrow, a.router + (size_t)e0 * H, (unsigned)(H * 4), &bar[warp]);
         }
     }
+    if (a.norm_w)
+        for (int c = threadIdx.x; c < n4; c += XROUTE_WARPS * 32)
+            reinterpret_cast<float4 *>(nws)[c] = __ldg(reinterpret_cast<const float4 *>(a.norm_w) + c);
     __syncwarp();
     pdl_trigger();
     pdl_wait();
@@ -827,12 +831,13 @@ __global__ void __launch_bounds__(XROUTE_WARPS * 32) k_xroute(xroute_args a) {
             const float s = 1.0f / sqrtf(tot / (float)H + a.eps);
             for (int c = threadIdx.x; c < n4; c += XROUTE_WARPS * 32) {
                 float4 v = reinterpret_cast<float4 *>(xs)[c];
-                const float4 n = __ldg(reinterpret_cast<const float4 *>(a.norm_w) + c);
+                const float4 n = reinterpret_cast<const float4 *>(nws)[c];
                 v = make_float4((v.x * s) * n.x, (v.y * s) * n.y, (v.z * s) * n.z, (v.w * s) * n.w);
                 reinterpret_cast<float4 *>(xs)[c] = v;
             }
         }
         __syncthreads();
+        TRACE(3);
         if (a.x_out && blockIdx.x == 0)
             for (int c = threadIdx.x; c < n4; c += XROUTE_WARPS * 32)
                 reinterpret_cast<float4 *>(a.x_out + (size_t)t * H)[c] = reinterpret_cast<const float4 *>(xs)[c];
@@ -858,6 +863,7 @@ __global__ void __launch_bounds__(XROUTE_WARPS * 32) k_xroute(xroute_args a) {
             for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
             if (lane == 0) a.logits[(size_t)t * a.E + e] = a.rbias ? acc + a.rbias[e] : acc;
         }
+        TRACE(4);
         const int nblk = H / 32;
         if (a.xdig) {
             // the tc path: each 32-element block's digits, one warp a block
@@ -2360,7 +2366,7 @@ moearc_x_moe *moearc_x_moe_create(moearc_ctx *c, const moearc_x_moe_desc *d) {
     m->x_stage_gu = round128((long)m->x_ch_gu * 2 * m->tile_bytes + (long)m->x_ntok * m->x_ch_gu * 256);
     m->x_stage_dn = round128((long)m->x_ch_dn * m->tile_bytes + (long)m->x_ntok * m->x_ch_dn * 256);
     m->x_route_grid = (m->E + XROUTE_WARPS - 1) / XROUTE_WARPS;
-    m->x_route_smem = (XROUTE_WARPS + 1) * m->H * 4;
+    m->x_route_smem = (XROUTE_WARPS + 2) * m->H * 4;  // router rows, the activation, the norm weights
     // 16 warps per CTA when their rings fit (one token: 192 KB for gpt-oss-120b), else 8
     m->x_warps = XW * XSTAGES * std::max(m->x_stage_gu, m->x_stage_dn) <= 200 * 1024 ? XW : XW / 2;
     m->x_grid = (int)std::max(1L, std::min<long>(c->sm_count, x_pmin / (m->x_warps * 2 * 5)));
