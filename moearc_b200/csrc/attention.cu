@@ -353,15 +353,52 @@ __global__ void __launch_bounds__(128)
     const bool live = !dpos || device_span(dpos, window, gridDim.y, kv_begin, n_kv, kps, n_splits);
     pdl_trigger();
     if (!live) return;
-    pdl_wait();
-    TRACE(1);
-    TRACE(2);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int qd = lane & 3, hr = lane >> 2;  // quad position, head row
     const size_t s0 = kv_begin + (size_t)split * kps;
     const size_t s1 = min(s0 + kps, n_kv);
     uint16_t *ws = smem + warp * warp_smem_elems<D>();
 
+    float o[D / 8][4];
+#pragma unroll
+    for (int i = 0; i < D / 8; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
+    float m = -INFINITY, lsum = 0.f;
+
+    // sel 0: every row of the tile; 1: all but the newest key's; 2: the newest key's only
+    const size_t row_elems = (size_t)n_kv_heads * D;
+    const size_t newest = n_kv - 1;
+    auto load_tile = [&](size_t t0, int stage, int sel) {
+        uint16_t *kt = ws + stage * 2 * TK * D, *vt = kt + TK * D;
+#pragma unroll
+        for (int c = lane; c < TK * CH; c += 32) {
+            const int r = c / CH, ch = c % CH;
+            const size_t j = t0 + r;
+            if ((sel == 1 && j == newest) || (sel == 2 && j != newest)) continue;
+            const bool valid = j < s1;
+            const size_t jj = valid ? j : s0;
+            const size_t off = ((size_t)table[jj / pt] * pt + jj % pt) * row_elems + (size_t)kvh * D + ch * 8;
+            const int dst = r * D + ((ch ^ (r & 7)) * 8);
+            cp_async16(kt + dst, kp + off, valid);
+            cp_async16(vt + dst, vp + off, valid);
+        }
+    };
+
+    size_t t0 = s0 + (size_t)warp * TK;
+    int stage = 0;
+    // With the decoder's device position the Q/K/V kernel before this one wrote only this step's
+    // key (n_kv - 1); the older keys' rows (pages and ring slots the step does not touch) are
+    // copied before the wait, the newest after it.
+    const bool pre = dpos != nullptr;
+    if (pre) {
+        if (t0 < s1) load_tile(t0, 0, 1);
+        cp_async_commit();
+    }
+    pdl_wait();
+    TRACE(1);
+    TRACE(2);
+    if (t0 < s1) load_tile(t0, 0, pre ? 2 : 0);
+    cp_async_commit();
+    // q after the first tile's copies are in flight: the two reads overlap
     // Q as the A operand: rows 0-7 hi, rows 8-15 lo; k = channel.
     uint32_t qa[D / 16][4];
     {
@@ -377,34 +414,9 @@ __global__ void __launch_bounds__(128)
         }
     }
 
-    float o[D / 8][4];
-#pragma unroll
-    for (int i = 0; i < D / 8; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
-    float m = -INFINITY, lsum = 0.f;
-
-    const size_t row_elems = (size_t)n_kv_heads * D;
-    auto load_tile = [&](size_t t0, int stage) {
-        uint16_t *kt = ws + stage * 2 * TK * D, *vt = kt + TK * D;
-#pragma unroll
-        for (int c = lane; c < TK * CH; c += 32) {
-            const int r = c / CH, ch = c % CH;
-            const size_t j = t0 + r;
-            const bool valid = j < s1;
-            const size_t jj = valid ? j : s0;
-            const size_t off = ((size_t)table[jj / pt] * pt + jj % pt) * row_elems + (size_t)kvh * D + ch * 8;
-            const int dst = r * D + ((ch ^ (r & 7)) * 8);
-            cp_async16(kt + dst, kp + off, valid);
-            cp_async16(vt + dst, vp + off, valid);
-        }
-    };
-
-    size_t t0 = s0 + (size_t)warp * TK;
-    int stage = 0;
-    if (t0 < s1) load_tile(t0, 0);
-    cp_async_commit();
     for (; t0 < s1; t0 += 4 * TK) {
         const size_t tn = t0 + 4 * TK;
-        if (tn < s1) load_tile(tn, stage ^ 1);
+        if (tn < s1) load_tile(tn, stage ^ 1, 0);
         cp_async_commit();
         cp_async_wait<1>();
         __syncwarp();
