@@ -532,7 +532,7 @@ def prefill_ep_bench(args, rank: int, world: int, own_group: bool = True) -> dic
     import torch.distributed as dist
 
     from moearc_b200 import Context
-    from moearc_b200.ep import ExpertParallelPrefill, PeerExpertParallelPrefill
+    from moearc_b200.ep import ExpertParallelPrefill, NcclExpertParallelPrefill, PeerExpertParallelPrefill, nccl_unique_id
     from moearc_b200.moe import MoeLayer
 
     if own_group:
@@ -556,8 +556,16 @@ def prefill_ep_bench(args, rank: int, world: int, own_group: bool = True) -> dic
     packer.pack(*banks)
     for b in banks:
         b.free()
-    cls = PeerExpertParallelPrefill if args.exchange == "peer" else ExpertParallelPrefill
-    ep = cls(ctx, None, H, I, E, k, 2, 1, 39, max_tokens=T, max_rows=args.tokens * k)
+    if args.exchange == "nccl-c":
+        # the library's own NCCL communicator (moearc_x_ep_*): rank 0's unique id reaches the
+        # others over the process group
+        uid = [nccl_unique_id(lib) if rank == 0 else None]
+        dist.broadcast_object_list(uid, src=0)
+        ep = NcclExpertParallelPrefill(ctx, rank, world, H, I, E, k, 2, 1, 39, max_tokens=T,
+                                       max_rows=args.tokens * k, unique_id=uid[0])
+    else:
+        cls = PeerExpertParallelPrefill if args.exchange == "peer" else ExpertParallelPrefill
+        ep = cls(ctx, None, H, I, E, k, 2, 1, 39, max_tokens=T, max_rows=args.tokens * k)
     ep.load(packer.gateup, packer.down)
     x = ctx.alloc(T * H * 2)
     ctx._finish(lib.moearc_x_synth(ctx.raw, x.ptr, T * H, 1, 0x9F08 + rank, 1.0, 0, 0), "synth")
@@ -572,7 +580,7 @@ def prefill_ep_bench(args, rank: int, world: int, own_group: bool = True) -> dic
     recv = []
     for _ in range(args.steps):
         pl = ep.forward(x, T, router, out.ptr, router_b=bias)
-        recv.append(pl["n_recv"])
+        recv.append(pl if isinstance(pl, int) else pl["n_recv"])
     ms = ctx.timer_stop()
     t = torch.tensor([ms, float(max(recv))], dtype=torch.float64, device="cuda")
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -604,6 +612,8 @@ def prefill_main(args) -> None:
             "config": {"workload": f"configs[3] MoE block: {T} tokens, {r['E']} experts top-4, {r['E'] // world} per GPU, "
                                    + ("rows stored into the owners' buffers by the route scatter and results back by "
                                       "the down GEMM epilogue over NVLink peer memory" if args.exchange == "peer" else
+                                      "count all-gather, dispatch and return by NCCL inside the library's C ABI "
+                                      "(moearc_x_ep_forward; no torch in the forward)" if args.exchange == "nccl-c" else
                                       "dispatch and combine by NCCL all-to-all")
                                    + "; experts placed by the popularity of one warm-up step", "max_rows_on_a_rank": r["max_rows"], "rows_total": r["rows_total"],
                        "parallelism": f"ep{world}"},
@@ -752,7 +762,8 @@ def shard_sample(args, rank: int, world: int) -> dict | None:
     a.weights = "bf16"
     if world > 1:
         r = prefill_ep_bench(a, rank, world, own_group=False)
-        label = f"ep{world}, rows exchanged over " + ("NVLink peer memory" if a.exchange == "peer" else "NCCL all-to-all")
+        label = f"ep{world}, rows exchanged over " + ("NVLink peer memory" if a.exchange == "peer" else
+                                                     "NCCL inside the C ABI" if a.exchange == "nccl-c" else "NCCL all-to-all")
     else:
         r = prefill_bench(a)
         label = "1 GPU"
@@ -789,7 +800,7 @@ def main() -> None:
     ap.add_argument("--depth", type=int, default=0)
     ap.add_argument("--config", default="120b", choices=["120b", "20b", "prefill", "qwen3"])
     ap.add_argument("--batch", type=int, default=64, help="qwen3: concurrent streams (configs[4]: 64)")
-    ap.add_argument("--exchange", default="peer", choices=["peer", "nccl"],
+    ap.add_argument("--exchange", default="peer", choices=["peer", "nccl", "nccl-c"],
                     help="prefill on several GPUs: rows exchanged by the kernels over peer memory, or NCCL all-to-all")
     ap.add_argument("--weights", default="bf16", choices=["4bit", "bf16", "fp8"],
                     help="prefill: expert weights staged at 4 bits (expanded in shared memory), expanded to bf16, "

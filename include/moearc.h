@@ -366,6 +366,35 @@ int moearc_x_prefill_profile(moearc_x_prefill *p, const unsigned short *x, unsig
                              const float *router_w, const float *router_b, const float *residual,
                              float *out, float *ms, int n);
 
+/* ---- expert parallelism over NCCL (ep.cu; the reference has none: its engine serves one GPU) --
+ * The prefill MoE block with its experts split over n_ranks GPUs, one process (or thread) per GPU
+ * and an NCCL communicator between them, passed as an opaque ncclComm_t (void *). Each rank's
+ * moearc_x_prefill object holds its own experts (moearc_x_prefill_load_range / _load_list) and
+ * routes in owner-major order (moearc_x_prefill_set_order, rank r's experts at positions
+ * r * n_local .. (r + 1) * n_local - 1). moearc_x_ep_forward then routes the rank's tokens,
+ * all-gathers the per-position counts (ncclAllGather), plans the exchange on the host (its one
+ * synchronisation: NCCL's point-to-point sizes are host arguments), sends each rank's rows and
+ * receives its own (one ncclSend / ncclRecv group), runs the grouped GEMMs on the received
+ * (source, expert) segments, returns the result rows (a second group) and combines in router
+ * order, all on the context stream. The output is bit-identical to the single-GPU block's.
+ * NCCL is resolved at run time: the process's, if loaded with global symbols, else libnccl.so.2.
+ * unique_id / comm_init / comm_destroy wrap ncclGetUniqueId (128 bytes) / ncclCommInitRank /
+ * ncclCommDestroy for hosts without their own NCCL. max_rows bounds the rows a rank receives
+ * (-2 from forward past it). */
+typedef struct moearc_x_ep moearc_x_ep;
+int moearc_x_ep_unique_id(void *id128);
+int moearc_x_ep_comm_init(moearc_ctx *c, void **comm, int n_ranks, const void *id128, int rank);
+int moearc_x_ep_comm_destroy(void *comm);
+moearc_x_ep *moearc_x_ep_create(moearc_ctx *c, moearc_x_prefill *p, const moearc_x_moe_desc *d, void *nccl_comm,
+                               int rank, int n_ranks, unsigned int max_rows);
+void moearc_x_ep_destroy(moearc_x_ep *ep);
+int moearc_x_ep_forward(moearc_x_ep *ep, const unsigned short *x, unsigned int n_tokens, const float *router_w,
+                        const float *router_b, const float *residual, float *out);
+/* The last forward's counts of every rank ([n_ranks][n_expert] by position, host) and the rows
+ * this rank received. */
+int moearc_x_ep_counts(moearc_x_ep *ep, int *counts_all);
+unsigned int moearc_x_ep_received(moearc_x_ep *ep);
+
 /* ---- synthetic decoder (decoder.cu) ----------------------------------------------------- */
 /* One decode step of a routed-MoE transformer (crates/moearc-engine/src/moe.rs:1862-2443,
  * Model::decode) with random, seeded weights generated on the device: per block RMSNorm,

@@ -76,6 +76,14 @@ SIGNATURES: dict[str, tuple] = {
     "moearc_x_moe_set_wait": (I, [P, C.c_ulonglong, I]),
     "moearc_x_moe_set_bias": (I, [P, P, P]),
     "moearc_x_moe_tc_bytes": (UL, [P, I]),
+    "moearc_x_ep_unique_id": (I, [P]),
+    "moearc_x_ep_comm_init": (I, [P, P, I, P, I]),
+    "moearc_x_ep_comm_destroy": (I, [P]),
+    "moearc_x_ep_create": (P, [P, P, P, P, I, I, U]),
+    "moearc_x_ep_destroy": (None, [P]),
+    "moearc_x_ep_forward": (I, [P, P, U, P, P, P, P]),
+    "moearc_x_ep_counts": (I, [P, P]),
+    "moearc_x_ep_received": (U, [P]),
     "moearc_x_moe_has_tc": (I, [P]),
     "moearc_x_moe_pack_tc": (I, [P, P, P, P, U, P, P]),
     "moearc_x_moe_forward_tc": (I, [P, P, U, P, P, P, P, P, P]),

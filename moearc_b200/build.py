@@ -70,7 +70,7 @@ def build(verbose: bool = False) -> str:
     if not os.path.exists(LIB) or any(os.path.getmtime(o) > os.path.getmtime(LIB) for o in objs):
         # the CUDA runtime is linked statically: the library keeps its own runtime state (current
         # device, streams) whatever else the host process has loaded
-        cmd = [NVCC, *ARCH, "-shared", "-Xcompiler", "-fPIC", "-cudart", "static", "-o", LIB, *objs, "-lpthread"]
+        cmd = [NVCC, *ARCH, "-shared", "-Xcompiler", "-fPIC", "-cudart", "static", "-o", LIB, *objs, "-lpthread", "-ldl"]
         r = subprocess.run(cmd, capture_output=True, text=True)
         if r.returncode != 0:
             raise RuntimeError(f"link failed:\n{r.stdout}\n{r.stderr}")

@@ -264,3 +264,90 @@ class PeerExpertParallelPrefill(ExpertParallelPrefill):
         pl["counts_all"] = counts_all
         self.last = pl
         return pl
+
+
+def nccl_unique_id(lib) -> bytes:
+    """A fresh NCCL unique id (128 bytes) from the library's NCCL (moearc_x_ep_unique_id); rank 0
+    makes it and hands it to the other ranks by any channel."""
+    import ctypes as C
+
+    buf = (C.c_char * 128)()
+    if lib.moearc_x_ep_unique_id(buf) != 0:
+        raise RuntimeError("ncclGetUniqueId failed (no NCCL in the process or libnccl.so.2)")
+    return bytes(buf)
+
+
+class NcclExpertParallelPrefill:
+    """Expert parallelism through the library's C ABI (moearc_x_ep_*): the count all-gather, the
+    row exchange and the result return run inside the library on an NCCL communicator, on the
+    context stream; this class only places the experts and calls moearc_x_ep_forward — no torch.
+    The communicator is the library's own (from a unique id every rank shares) unless a host
+    passes its ncclComm_t pointer as `comm`."""
+
+    def __init__(self, ctx, rank: int, world: int, n_embd: int, n_ff: int, n_expert: int, k: int, gating: int,
+                 act: int, wtype: int, max_tokens: int, max_rows: int, unique_id: bytes | None = None,
+                 comm: int | None = None):
+        import ctypes as C
+
+        from .moe import MoePrefill
+
+        if n_expert % world:
+            raise ValueError("the experts must split evenly over the ranks")
+        self.ctx, self.rank, self.world = ctx, rank, world
+        self.H, self.I, self.E, self.k = n_embd, n_ff, n_expert, k
+        self.nl = n_expert // world
+        self.pf = MoePrefill(ctx, n_embd, n_ff, n_expert, k, gating, act, wtype, max_tokens)
+        self.own_comm = comm is None
+        if comm is None:
+            if unique_id is None:
+                raise ValueError("pass the shared NCCL unique id or a communicator")
+            p = C.c_void_p()
+            idb = (C.c_char * 128).from_buffer_copy(unique_id)
+            if ctx.lib.moearc_x_ep_comm_init(ctx.raw, C.byref(p), world, idb, rank) != 0:
+                raise RuntimeError("ncclCommInitRank failed")
+            comm = p.value
+        self.comm = comm
+        self.ep = ctx.lib.moearc_x_ep_create(ctx.raw, self.pf.h, C.byref(self.pf.desc), comm, rank, world, max_rows)
+        if not self.ep:
+            raise RuntimeError("moearc_x_ep_create refused the configuration")
+        self.lists = interleaved(n_expert, world)
+        self.banks = None
+
+    def close(self) -> None:
+        if self.ep:
+            self.ctx.lib.moearc_x_ep_destroy(self.ep)
+            self.ep = None
+        if self.own_comm and self.comm:
+            self.ctx.lib.moearc_x_ep_comm_destroy(self.comm)
+            self.comm = None
+        self.pf.close()
+
+    def load(self, gateup, down, lists: list[list[int]] | None = None) -> None:
+        """Place the experts (default: interleaved) and expand this rank's from the full packed banks."""
+        self.banks = (gateup, down)
+        self.lists = [list(l) for l in (lists or self.lists)]
+        self.pos = positions(self.lists)
+        self.pf.set_order(self.pos)
+        self.pf.load_list(gateup, down, self.lists[self.rank])
+
+    def forward(self, x_bf16, n_tokens: int, router_w, out_ptr: int, router_b=None, residual_ptr=None) -> int:
+        """Enqueue the block for this rank's tokens; returns the rows this rank received."""
+        lib = self.ctx.lib
+        x = x_bf16 if isinstance(x_bf16, int) else x_bf16.ptr
+        rc = lib.moearc_x_ep_forward(self.ep, x, n_tokens, router_w.ptr, None if router_b is None else router_b.ptr,
+                                     residual_ptr, out_ptr)
+        self.ctx._finish(rc, "ep_forward")
+        return lib.moearc_x_ep_received(self.ep)
+
+    def counts_all(self) -> np.ndarray:
+        """Every rank's per-position counts of the last forward, [world][n_expert]."""
+        out = np.zeros((self.world, self.E), np.int32)
+        self.ctx._finish(self.ctx.lib.moearc_x_ep_counts(self.ep, out.ctypes.data), "ep_counts")
+        return out
+
+    def rebalance(self) -> list[list[int]]:
+        """Re-place the experts by the popularity the last forward saw (summed over all ranks;
+        every rank computes the same placement)."""
+        lists = balanced(self.counts_all().sum(axis=0)[self.pos], self.world)
+        self.load(self.banks[0], self.banks[1], lists)
+        return lists
