@@ -677,51 +677,93 @@ def batch_main(args) -> None:
     from moearc_b200 import Context
     from moearc_b200.decoder import BatchDecoder, DecoderConfig
 
+    rank, world = int(os.environ.get("RANK", "0")), int(os.environ.get("WORLD_SIZE", "1"))
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as tdist
+
+        # the process group only hands out the NCCL unique id and takes the max over ranks; the
+        # step's exchanges run on the library's own communicator inside its graph
+        tdist.init_process_group("gloo", timeout=datetime.timedelta(seconds=300))
+        dist = tdist
     ctx = Context()
     lib = ctx.lib
     B = args.batch
+    if B % world:
+        raise SystemExit("qwen3: --batch must split evenly over the GPUs")
+    Bl = B // world  # this rank's streams
     depth = args.depth or 4096
     cfg = DecoderConfig.qwen3_moe()
+    weights = args.weights or "4bit"
+    if weights not in ("4bit", "bf16"):
+        raise SystemExit("qwen3: --weights 4bit or bf16")
+    cfg.expert_layout = 0 if weights == "4bit" else 1
     if args.layers:
         cfg.n_layer = args.layers
     cfg.n_ctx = depth + args.warmup + 2 * args.steps + 64
     t0 = time.time()
-    bd = BatchDecoder(ctx, cfg, B)
+    comm = None
+    if world > 1:
+        from moearc_b200.ep import nccl_comm, nccl_unique_id
+
+        uid = [nccl_unique_id(lib) if rank == 0 else None]
+        dist.broadcast_object_list(uid, src=0)
+        comm = nccl_comm(ctx, rank, world, uid[0])
+        bd = BatchDecoder(ctx, cfg, Bl, ep=(comm, rank, world))
+    else:
+        bd = BatchDecoder(ctx, cfg, B)
     bd.set_pos(depth, fill=True)
     ctx.sync()
     build_s = time.time() - t0
     H = cfg.n_embd
-    host_in = lib.moearc_x_host_alloc(4 * B * H)
-    host_out = lib.moearc_x_host_alloc(4 * B * H)
-    C.memmove(host_in, np.random.default_rng(4).standard_normal(B * H).astype(np.float32).ctypes.data, 4 * B * H)
-    lib.moearc_copy_h2d(ctx.raw, bd.in_ptr, host_in, 4 * B * H)
+    nb = 4 * Bl * H  # this rank's input and output bytes per step
+    host_in = lib.moearc_x_host_alloc(nb)
+    host_out = lib.moearc_x_host_alloc(nb)
+    C.memmove(host_in, np.random.default_rng(4 + rank).standard_normal(Bl * H).astype(np.float32).ctypes.data, nb)
+    lib.moearc_copy_h2d(ctx.raw, bd.in_ptr, host_in, nb)
     for _ in range(args.warmup):
         bd.step()
     ctx.sync()
-    sampler = ClockSampler()
-    sampler.start()
+    sampler = ClockSampler() if rank == 0 else None
+    if sampler:
+        sampler.start()
     time.sleep(0.3)
+    if dist:
+        dist.barrier()
     ctx.sync()
     ctx.timer_start()
     for _ in range(args.steps):
         bd.step()
     ms_total = ctx.timer_stop()
     ctx.sync()
+    if dist:
+        dist.barrier()
     t1 = time.perf_counter()
     for _ in range(args.steps):
-        lib.moearc_copy_h2d_async(ctx.raw, bd.in_ptr, host_in, 4 * B * H)
+        lib.moearc_copy_h2d_async(ctx.raw, bd.in_ptr, host_in, nb)
         bd.step()
-        lib.moearc_x_copy_d2h_async(ctx.raw, host_out, bd.out_ptr, 4 * B * H)
+        lib.moearc_x_copy_d2h_async(ctx.raw, host_out, bd.out_ptr, nb)
         ctx.sync()
     e2e_s = time.perf_counter() - t1
-    clocks = sampler.stop()
-    out = np.ctypeslib.as_array(C.cast(host_out, C.POINTER(C.c_float)), (B * H,)).copy()
+    clocks = sampler.stop() if sampler else None
+    out = np.ctypeslib.as_array(C.cast(host_out, C.POINTER(C.c_float)), (Bl * H,)).copy()
     assert np.all(np.isfinite(out)), "non-finite batch decoder output"
     assert bd.status() == 0, "a bounded wait gave up"
     lib.moearc_x_host_free(host_in)
     lib.moearc_x_host_free(host_out)
     bd.close()
+    if comm:
+        from moearc_b200.ep import nccl_comm_destroy
+
+        nccl_comm_destroy(ctx, comm)
     ctx.close()
+    ms_total, e2e_s = slowest_rank(ms_total, e2e_s, dist)
+    if dist:
+        dist.destroy_process_group()
+    if rank != 0:
+        return
     ms_step = ms_total / args.steps
     E, k, I = cfg.n_expert, cfg.n_expert_used, cfg.n_ff
     Dq, Dkv = cfg.n_head * cfg.head_dim, cfg.n_head_kv * cfg.head_dim
@@ -729,20 +771,29 @@ def batch_main(args) -> None:
     dense_b = (H * (Dq + 2 * Dkv) + H * Dq) * 2
     expert_q4 = distinct * 3 * I * H * 18 / 32
     kv_b = B * (depth + 1) * Dkv * 2 * 2
-    step_b = cfg.n_layer * (dense_b + E * H * 4 + expert_q4 + kv_b)
+    step_b = cfg.n_layer * (world * (dense_b + E * H * 4) + expert_q4 + kv_b)  # dense and router on every GPU
     peak, peak_kind = load_peaks()
     achieved = step_b / (ms_step / 1000.0) / 1e9
+    where = "1 GPU" if world == 1 else f"expert-parallel over {world} GPUs, {Bl} streams each"
     line = {
-        "metric": f"batched decode tok/s (all streams), Qwen3-MoE shape, {B} streams at depth {depth} (configs[4], 1 GPU)",
-        "value": B / (ms_step / 1000.0), "unit": "tok/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-        "dtype": "bf16 operands, f32 accumulate (Q4_0 experts staged at 4 bits, expanded in shared memory)",
+        "metric": f"batched decode tok/s (all streams), Qwen3-MoE shape, {B} streams at depth {depth} (configs[4], {where})",
+        "value": B / (ms_step / 1000.0), "unit": "tok/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak" if world == 1 else "strong",
+        "vs_baseline": None,
+        "dtype": ("f16 expert operands (Q4_0 read at 4 bits, expanded in shared memory), bf16 attention operands, "
+                  "f32 accumulate" if weights == "4bit" else
+                  "bf16 operands (Q4_0 experts expanded to bf16 at load), f32 accumulate"),
+        "weights": weights,
         "data": "synthetic (seeded weights of the configs[4] architecture, synthetic KV at the depth)",
         "config": {"workload": f"configs[4] Qwen3-MoE shape, {cfg.n_layer} blocks, {B} streams, depth {depth}",
-                   "batch": B, "depth": depth, "l2": "weights and KV (~100 GB) far exceed the 126 MB L2"},
-        "roofline": {"bound": "hbm", "kernel": "whole step (algorithmic bytes: bf16 dense weights, 4-bit experts, KV span)",
-                     "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak, "peak_kind": peak_kind,
-                     "traffic": None, "bytes_per_step": step_b},
+                   "batch": B, "depth": depth, "l2": "weights and KV (~100 GB) far exceed the 126 MB L2",
+                   "parallelism": "1 GPU" if world == 1 else
+                   f"ep{world}: experts split over the GPUs, attention and projections per GPU on its own "
+                   f"streams, rows all-gathered and results returned over NCCL inside each GPU's step graph"},
+        "roofline": {"bound": "hbm", "kernel": "whole step (algorithmic bytes: bf16 dense weights, 4-bit experts, KV span)"
+                     + ("" if world == 1 else f"; {world} GPUs: the dense weights read on each, the peak {world} x"),
+                     "achieved": achieved, "peak": peak * world, "unit": "GB/s", "frac": achieved / (peak * world),
+                     "peak_kind": peak_kind, "traffic": None, "bytes_per_step": step_b},
         "e2e": {"value": B * args.steps / e2e_s, "unit": "tok/s", "h2d_bytes_per_step": 4 * B * H,
                 "d2h_bytes_per_step": 4 * B * H},
         "gpu_launches": None, "clocks": clocks, "build_s": build_s,
@@ -802,9 +853,10 @@ def main() -> None:
     ap.add_argument("--batch", type=int, default=64, help="qwen3: concurrent streams (configs[4]: 64)")
     ap.add_argument("--exchange", default="peer", choices=["peer", "nccl", "nccl-c"],
                     help="prefill on several GPUs: rows exchanged by the kernels over peer memory, or NCCL all-to-all")
-    ap.add_argument("--weights", default="bf16", choices=["4bit", "bf16", "fp8"],
-                    help="prefill: expert weights staged at 4 bits (expanded in shared memory), expanded to bf16, "
-                         "or the MXFP8 perf mode (E4M3 weights and MXFP8 activations on the block-scaled FP8 MMA)")
+    ap.add_argument("--weights", default=None, choices=["4bit", "bf16", "fp8"],
+                    help="prefill (default bf16): expert weights staged at 4 bits (expanded in shared memory), "
+                         "expanded to bf16, or the MXFP8 perf mode (E4M3 weights and MXFP8 activations on the "
+                         "block-scaled FP8 MMA); qwen3 (default 4bit): 4bit or bf16")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--layers", type=int, default=0,
@@ -833,12 +885,13 @@ def main() -> None:
                     help="skip the expert-parallel prefill sample (configs[3] over the N GPUs)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
+    if args.weights is None and args.config != "qwen3":
+        args.weights = "bf16"
     if args.config == "prefill":
         prefill_main(args)
         return
     if args.config == "qwen3":
-        if int(os.environ.get("RANK", "0")) == 0:
-            batch_main(args)
+        batch_main(args)  # every rank: expert parallelism over the GPUs when launched on several
         return
 
     from moearc_b200.decoder import DecoderConfig

@@ -435,7 +435,8 @@ typedef struct {
     /* Layout of the resident blocks' expert banks: 0 = the tensor-core layout (moearc_x_moe_pack_tc)
      * where the shape has one (MXFP4 experts, n_embd and n_ff multiples of 64), decoded by the
      * block-scaled FP4 tensor-core kernels; 1 = the fragment layout (moearc_x_moe_pack) everywhere,
-     * which the persistent step kernel needs. Offloaded blocks always keep the fragment layout. */
+     * which the persistent step kernel needs. Offloaded blocks always keep the fragment layout.
+     * The batched decoder reads it as 0 = experts at 4 bits, 1 = their bf16 expansion. */
     unsigned int expert_layout;
 } moearc_x_decoder_cfg;
 moearc_x_decoder *moearc_x_decoder_create(moearc_ctx *c, const moearc_x_decoder_cfg *cfg);
@@ -536,12 +537,22 @@ int moearc_x_decoder_set_trace(moearc_x_decoder *d, void *device_buffer);
  * n_batch independent sequences, one token each per step, through the decoder of cfg (same
  * weights as moearc_x_decoder_create would generate from it): bf16 activations into tcgen05
  * GEMMs for Q/K/V and O, RoPE and paged bf16 KV per sequence, one batched decode-attention launch,
- * and the prefill MoE block, with the experts expanded to bf16 once at create and the router on
- * the f32 activations; QK-norm with has_qk_norm. Requires n_swa == 0, no sinks, n_offload == 0,
- * n_vocab == 0; NULL otherwise. */
+ * and the prefill MoE block with the router on the f32 activations; QK-norm with has_qk_norm. The
+ * experts stay at 4 bits (the prefill object's 4-bit form, f16 tiles expanded in shared memory)
+ * with expert_layout 0, or are expanded to bf16 once at create with expert_layout 1. Requires
+ * n_swa == 0, no sinks, n_offload == 0, n_vocab == 0; NULL otherwise. */
 typedef struct moearc_x_batch_decoder moearc_x_batch_decoder;
 moearc_x_batch_decoder *moearc_x_batch_decoder_create(moearc_ctx *c, const moearc_x_decoder_cfg *cfg,
                                                       unsigned int n_batch);
+/* Expert parallelism for the batched decoder (configs[4] over n_ranks GPUs; no reference
+ * counterpart): every rank decodes its own n_batch streams (attention and projections local) and
+ * holds experts rank * n_expert / n_ranks .. of every block, at 4 bits (expert_layout 0 only). Per
+ * block the ranks' routed rows are all-gathered, each owner runs its experts over every rank's
+ * rows, the results return in one grouped exchange and each rank combines its own tokens — all
+ * on comm (an ncclComm_t of the n_ranks ranks, e.g. from moearc_x_ep_comm_init) with fixed sizes,
+ * inside the captured step graph. Every rank must step together. NULL if n_expert % n_ranks. */
+moearc_x_batch_decoder *moearc_x_batch_decoder_create_ep(moearc_ctx *c, const moearc_x_decoder_cfg *cfg,
+                                                         unsigned int n_batch, void *comm, int rank, int n_ranks);
 void moearc_x_batch_decoder_destroy(moearc_x_batch_decoder *d);
 void *moearc_x_batch_decoder_input(moearc_x_batch_decoder *d);   /* device, n_batch x n_embd f32 */
 void *moearc_x_batch_decoder_output(moearc_x_batch_decoder *d);  /* device, n_batch x n_embd f32 */

@@ -116,6 +116,7 @@ SIGNATURES: dict[str, tuple] = {
     "moearc_x_decoder_trace_words": (C.c_ulong, [P]),
     "moearc_x_decoder_set_trace": (I, [P, P]),
     "moearc_x_batch_decoder_create": (P, [P, P, U]),
+    "moearc_x_batch_decoder_create_ep": (P, [P, P, U, P, I, I]),
     "moearc_x_batch_decoder_destroy": (None, [P]),
     "moearc_x_batch_decoder_input": (P, [P]),
     "moearc_x_batch_decoder_output": (P, [P]),

@@ -67,6 +67,32 @@ const nccl_api &nccl() {
 
 }  // namespace
 
+namespace moearc {
+// For the batched decoder's expert-parallel step (batch.cu): an all-gather of `bytes` from every
+// rank, and a grouped exchange in which block r of send (bytes, at send + r * send_stride) goes
+// to rank r and block r of recv comes from rank r. Both only enqueue on s (capturable in a CUDA
+// graph); ERR when NCCL is missing or a call fails.
+int ep_all_gather(void *comm, const void *send, void *recv, size_t bytes, cudaStream_t s) {
+    const nccl_api &n = nccl();
+    if (!n.ok || !comm) return ERR;
+    return n.all_gather(send, recv, bytes, ncclUint8, static_cast<ncclComm_t>(comm), s) == ncclSuccess ? OK : ERR;
+}
+
+int ep_exchange(void *comm, int world, const void *send, size_t send_stride, void *recv, size_t recv_stride,
+                size_t bytes, cudaStream_t s) {
+    const nccl_api &n = nccl();
+    if (!n.ok || !comm) return ERR;
+    ncclComm_t cm = static_cast<ncclComm_t>(comm);
+    if (n.group_start() != ncclSuccess) return ERR;
+    bool ok = true;
+    for (int r = 0; r < world; ++r) {
+        ok &= n.send(static_cast<const uint8_t *>(send) + r * send_stride, bytes, ncclUint8, r, cm, s) == ncclSuccess;
+        ok &= n.recv(static_cast<uint8_t *>(recv) + r * recv_stride, bytes, ncclUint8, r, cm, s) == ncclSuccess;
+    }
+    return (n.group_end() == ncclSuccess && ok) ? OK : ERR;
+}
+}  // namespace moearc
+
 struct moearc_x_ep {
     moearc_ctx *c;
     moearc_x_prefill *p;

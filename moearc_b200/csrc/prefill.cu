@@ -10,7 +10,7 @@
 //   out[t] = residual[t] + sum_m w[t,m] (W_down[e] a[t,m])   (router order, moe.rs:2395-2421)
 //
 // Kernels, in stream order (no host round trip; the GEMMs read their tile counts on the device):
-//   k_pf_logits   8 tokens per CTA, every expert; bf16 x -> f32, fixed lane order
+//   k_pf_logits   16 tokens x 32 experts per CTA; bf16 x -> f32, fixed lane order
 //   k_pf_topk     one warp per token; expert counts
 //   k_pf_scan     row offsets and 128-token tile counts per expert
 //   k_pf_scatter  each (token, choice) gets a row of its expert's segment; x copied there (bf16)
@@ -43,6 +43,8 @@ using namespace moearc;
 namespace {
 
 constexpr int PF_BM = 128, PF_BN = 128, PF_BK = 64;
+constexpr int PF4_BN_SMALL = 32;    // the 4-bit form's tile rows for decode-sized batches
+constexpr int PF4_SMALL_ROWS = 16;  // ... taken while the mean rows per expert is at most this
 constexpr int PF_TILE_BYTES = PF_BM * PF_BK * 2;  // one 128 x 64 bf16 operand tile (16 KB)
 constexpr int PF_LOGIT_TOK = 16;                  // tokens per router CTA
 constexpr int PF_LOGIT_EXP = 4;                   // experts a warp folds at once
@@ -77,38 +79,69 @@ __global__ void __launch_bounds__(256) k_pf_logits(pf_route_args a) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int t0 = blockIdx.x * PF_LOGIT_TOK, nt = min(PF_LOGIT_TOK, a.T - t0);
     const int H = a.H, n4 = H / 4;
+    // staged with 16-byte loads, eight in flight per thread (H is a multiple of 64)
     if (a.x32) {
-        for (int i = threadIdx.x; i < nt * H; i += blockDim.x) xs[i] = a.x32[(size_t)t0 * H + i];
+        const float4 *src = reinterpret_cast<const float4 *>(a.x32 + (size_t)t0 * H);
+        float4 *dst = reinterpret_cast<float4 *>(xs);
+        const int n = nt * H / 4;
+        for (int i0 = threadIdx.x; i0 < n; i0 += 8 * blockDim.x) {
+            float4 v[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                const int i = i0 + j * blockDim.x;
+                if (i < n) v[j] = src[i];
+            }
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                const int i = i0 + j * blockDim.x;
+                if (i < n) dst[i] = v[j];
+            }
+        }
     } else {
-        for (int i = threadIdx.x; i < nt * H / 2; i += blockDim.x) {
-            const uint32_t v = reinterpret_cast<const uint32_t *>(a.x + (size_t)t0 * H)[i];
-            xs[2 * i] = __uint_as_float(v << 16);
-            xs[2 * i + 1] = __uint_as_float(v & 0xFFFF0000u);
+        const uint4 *src = reinterpret_cast<const uint4 *>(a.x + (size_t)t0 * H);
+        const int n = nt * H / 8;
+        for (int i0 = threadIdx.x; i0 < n; i0 += 4 * blockDim.x) {
+            uint4 v[4];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const int i = i0 + j * blockDim.x;
+                if (i < n) v[j] = src[i];
+            }
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const int i = i0 + j * blockDim.x;
+                if (i < n) {
+                    const uint32_t w[4] = {v[j].x, v[j].y, v[j].z, v[j].w};
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) {
+                        xs[8 * i + 2 * e] = __uint_as_float(w[e] << 16);
+                        xs[8 * i + 2 * e + 1] = __uint_as_float(w[e] & 0xFFFF0000u);
+                    }
+                }
+            }
         }
     }
     __syncthreads();
     const int nwarps = blockDim.x >> 5;
-    for (int e0 = warp * PF_LOGIT_EXP; e0 < a.E; e0 += nwarps * PF_LOGIT_EXP) {
+    // blockIdx.y: a group of nwarps * PF_LOGIT_EXP experts (a decode-sized batch has few token
+    // groups, so the experts spread the work over more SMs)
+    for (int e0 = (blockIdx.y * nwarps + warp) * PF_LOGIT_EXP; e0 < a.E; e0 += gridDim.y * nwarps * PF_LOGIT_EXP) {
         float acc[PF_LOGIT_EXP][PF_LOGIT_TOK];
 #pragma unroll
         for (int j = 0; j < PF_LOGIT_EXP; ++j)
 #pragma unroll
             for (int t = 0; t < PF_LOGIT_TOK; ++t) acc[j][t] = 0.f;
-        // the router columns of the next step are loaded one step ahead (L2 latency is long and
-        // few warps share an SM)
+        // the router columns are loaded three steps ahead (few warps share an SM, and each step
+        // would otherwise wait out a whole memory latency); every lane still adds its columns
+        // c = lane, lane + 32, ... in ascending order
         auto load_w = [&](int c, float4 (&w)[PF_LOGIT_EXP]) {
 #pragma unroll
             for (int j = 0; j < PF_LOGIT_EXP; ++j)
                 w[j] = (c < n4 && e0 + j < a.E) ? __ldg(reinterpret_cast<const float4 *>(a.router + (size_t)(e0 + j) * H) + c)
                                                 : make_float4(0.f, 0.f, 0.f, 0.f);
         };
-        float4 wn[PF_LOGIT_EXP];
-        load_w(lane, wn);
-        for (int c = lane; c < n4; c += 32) {
-            float4 wv[PF_LOGIT_EXP];
-#pragma unroll
-            for (int j = 0; j < PF_LOGIT_EXP; ++j) wv[j] = wn[j];
-            load_w(c + 32, wn);
+        auto step = [&](int c, const float4 (&wv)[PF_LOGIT_EXP]) {
+            if (c >= n4) return;
 #pragma unroll
             for (int t = 0; t < PF_LOGIT_TOK; ++t) {
                 const float4 xv = reinterpret_cast<const float4 *>(xs + (size_t)t * H)[c];
@@ -120,6 +153,18 @@ __global__ void __launch_bounds__(256) k_pf_logits(pf_route_args a) {
                     acc[j][t] = fmaf(wv[j].w, xv.w, acc[j][t]);
                 }
             }
+        };
+        float4 w0[PF_LOGIT_EXP], w1[PF_LOGIT_EXP], w2[PF_LOGIT_EXP];
+        load_w(lane, w0);
+        load_w(lane + 32, w1);
+        load_w(lane + 64, w2);
+        for (int c = lane; c < n4; c += 96) {
+            step(c, w0);
+            load_w(c + 96, w0);
+            step(c + 32, w1);
+            load_w(c + 128, w1);
+            step(c + 64, w2);
+            load_w(c + 160, w2);
         }
 #pragma unroll
         for (int j = 0; j < PF_LOGIT_EXP; ++j)
@@ -132,6 +177,11 @@ __global__ void __launch_bounds__(256) k_pf_logits(pf_route_args a) {
                 if (lane == 0 && t < nt && e < a.E) a.logits[(size_t)(t0 + t) * a.E + e] = a.rbias ? v + a.rbias[e] : v;
             }
     }
+}
+
+// Token groups x expert groups (8 warps of PF_LOGIT_EXP experts each).
+inline dim3 logit_grid(int T, int E) {
+    return dim3((unsigned)((T + PF_LOGIT_TOK - 1) / PF_LOGIT_TOK), (unsigned)((E + 8 * PF_LOGIT_EXP - 1) / (8 * PF_LOGIT_EXP)));
 }
 
 // Top-k of each token (one warp per token) and the per-expert counts.
@@ -305,6 +355,10 @@ struct pf_gemm_args {
     const float *bias;
     int n_blocks;
     int *status;
+    // down only (the dense projections of a decode-sized batch): the K blocks split into ksplit
+    // runs (<= K / 64), each tile's partial sum written to y_out + ks * split_stride; 0 or 1: none
+    int ksplit;
+    size_t split_stride;
 };
 
 template <int MODE>
@@ -355,7 +409,8 @@ __global__ void __launch_bounds__(192, 1) k_pf_gemm(const __grid_constant__ CUte
     tc::fence_after_sync();
     const uint32_t tmem = tmem_slot;
     const int MT = (a.Mrows + PF_BM - 1) / PF_BM, KB = a.K / PF_BK;
-    const long total = (long)s_toff[a.E] * MT;
+    const int KS = (MODE == 1 && a.ksplit > 1) ? a.ksplit : 1;  // K runs (tile % KS: the run)
+    const long total = (long)s_toff[a.E] * MT * KS;
     // tile -> expert, n-tile within the expert, m-tile
     auto locate = [&](long tile, int &e, int &nt, int &mt) {
         const int ntg = (int)(tile / MT);
@@ -375,11 +430,12 @@ __global__ void __launch_bounds__(192, 1) k_pf_gemm(const __grid_constant__ CUte
         if (lane == 0) {
             for (long tile = blockIdx.x; tile < total && !abort_; tile += gridDim.x) {
                 int e, nt, mt;
-                locate(tile, e, nt, mt);
+                const int ks = (int)(tile % KS);
+                locate(tile / KS, e, nt, mt);
                 const int we = a.seg_w ? a.seg_w[e] : e;
                 const int rowA = MODE == 0 ? we * 2 * a.Mrows + mt * PF_BM : we * a.Mrows + mt * PF_BM;
                 const int rowB = a.off[e] + nt * PF_BN;
-                for (int kb = 0; kb < KB; ++kb, ++g) {
+                for (int kb = ks * KB / KS; kb < (ks + 1) * KB / KS; ++kb, ++g) {
                     const int s = (int)(g % C::STAGES);
                     if (g >= C::STAGES && !tc::bar_wait(&empty[s], (unsigned)(((g / C::STAGES) - 1) & 1), &abort_, a.status, PF_STATUS_WAIT))
                         break;
@@ -406,7 +462,8 @@ __global__ void __launch_bounds__(192, 1) k_pf_gemm(const __grid_constant__ CUte
                     break;
                 tc::fence_after_sync();
                 bool ok = true;
-                for (int kb = 0; kb < KB; ++kb, ++g) {
+                const int ks = (int)(tile % KS), kb0 = ks * KB / KS;
+                for (int kb = kb0; kb < (ks + 1) * KB / KS; ++kb, ++g) {
                     const int s = (int)(g % C::STAGES);
                     if (!tc::bar_wait(&full[s], (unsigned)((g / C::STAGES) & 1), &abort_, a.status, PF_STATUS_WAIT)) {
                         ok = false;
@@ -417,7 +474,7 @@ __global__ void __launch_bounds__(192, 1) k_pf_gemm(const __grid_constant__ CUte
                     const uint32_t b0 = a0 + C::NA * PF_TILE_BYTES;
 #pragma unroll
                     for (int k = 0; k < PF_BK / 16; ++k) {
-                        const uint32_t acc = (kb > 0 || k > 0) ? 1u : 0u;
+                        const uint32_t acc = (kb > kb0 || k > 0) ? 1u : 0u;
                         tc::mma_bf16(dcol, tc::desc_k_sw128(a0 + k * 32), tc::desc_k_sw128(b0 + k * 32), idesc, acc);
                         if (MODE == 0)
                             tc::mma_bf16(dcol + PF_BN, tc::desc_k_sw128(a0 + PF_TILE_BYTES + k * 32),
@@ -442,7 +499,8 @@ __global__ void __launch_bounds__(192, 1) k_pf_gemm(const __grid_constant__ CUte
             if (!tc::bar_wait(&acc_full[ab], (unsigned)((i >> 1) & 1), &abort_, a.status, PF_STATUS_WAIT)) break;
             tc::fence_after_sync();
             int e, nt, mt;
-            locate(tile, e, nt, mt);
+            const int ks = (int)(tile % KS);
+            locate(tile / KS, e, nt, mt);
             const int seg = a.off[e], n_rows = a.off[e + 1] - seg;
             const int f = mt * PF_BM + 32 * qd + lane;  // this thread's feature row
             const bool fok = f < a.Mrows;
@@ -465,7 +523,7 @@ __global__ void __launch_bounds__(192, 1) k_pf_gemm(const __grid_constant__ CUte
                                 f32_to_bf16_rn(act_fn(a.act, d[j] + bg, u[j] + bu, a.alpha, a.limit));
                     }
                 } else {
-                    float *ybase = a.seg_y ? a.seg_y[e] : a.y_out + (size_t)seg * a.Mrows;
+                    float *ybase = a.seg_y ? a.seg_y[e] : a.y_out + ks * a.split_stride + (size_t)seg * a.Mrows;
 #pragma unroll
                     for (int j = 0; j < 16; ++j) {
                         const int n = nt * PF_BN + c0 + j;
@@ -960,25 +1018,39 @@ struct pf_gemm4_args {
     int RB, KB;         // row blocks and 64-column blocks of one matrix
 };
 
-template <int MODE, int WT>
+// BN: rows (tokens) per tile. 128 for prefill; 32 for decode-sized batches (a few rows per
+// expert), where the issue of the small MMAs bounds the kernel: a stage's MMAs are split between
+// ISS = 4 issuing threads, each into its own accumulator (gate-up: issuer i takes matrix i / 2,
+// K steps 2 (i % 2) and 2 (i % 2) + 1; down: K step i), the epilogue adding them in a fixed order.
+//
+// Stages: RS raw stages (the B tile and the stage's 4-bit chunks, filled by the producer's
+// copies) and TS f16 tile stages (written by the decoder warps). With RS == TS (both variants)
+// stage s is one unit: the MMAs' one commit per issuer releases both, and the decoders wait for
+// that release before rewriting the tile.
+template <int MODE, int WT, int BN = PF_BN>
 struct pf4_cfg {
     static constexpr int NA = MODE == 0 ? 2 : 1;
+    static constexpr int ISS = BN < PF_BN ? 4 : 1;
     static constexpr int CB = tc4_chunk<WT>();
-    static constexpr int STAGE_RAW = ((NA * CB + 1023) / 1024) * 1024;
-    static constexpr int STAGE = (NA + 1) * PF_TILE_BYTES + STAGE_RAW;  // bf16 A tiles, B tile, 4-bit chunks
-    static constexpr int STAGES = MODE == 0 ? 3 : 5;
-    static constexpr int SMEM = STAGES * STAGE + 1024;
-    static constexpr int ACC_COLS = NA * PF_BN;
+    static constexpr int B_BYTES = BN * PF_BK * 2;
+    static constexpr int RSTAGE = ((B_BYTES + NA * CB + 1023) / 1024) * 1024;  // B tile, then 4-bit chunks
+    static constexpr int TSTAGE = NA * PF_TILE_BYTES;                          // f16 A tiles
+    static constexpr int TS = BN == PF_BN ? (MODE == 0 ? 3 : 5) : (MODE == 0 ? 4 : 8);
+    static constexpr int RS = TS;
+    static constexpr int SMEM = TS * TSTAGE + RS * RSTAGE + 1024;
+    static constexpr int ACC_COLS = (NA > ISS ? NA : ISS) * BN;
     static constexpr int TMEM_COLS = 2 * ACC_COLS;
     static constexpr int DEC_WARPS = 8;
-    static constexpr int THREADS = (6 + DEC_WARPS) * 32;
+    static constexpr int ISS_WARP1 = 6 + DEC_WARPS;  // issuers 1 .. ISS - 1 (issuer 0: warp 1)
+    static constexpr int THREADS = (6 + DEC_WARPS + ISS - 1) * 32;
 };
 
-// Decode one thread's half row (32 columns: one scale block) of a staged chunk into the f16 A
-// tile in the 128-byte swizzle layout (row `row`, 16-byte unit u at (u ^ (row & 7)) * 16).
+// Decode a quarter row (16 columns: half a scale block) of a staged chunk into the f16 A tile in
+// the 128-byte swizzle layout (row `row`, 16-byte unit u at (u ^ (row & 7)) * 16).
 template <int WT>
-__device__ __forceinline__ void tc4_decode_half(const uint8_t *chunk, uint8_t *tile, int row, int half) {
-    const uint4 w = *reinterpret_cast<const uint4 *>(chunk + row * 32 + half * 16);
+__device__ __forceinline__ void tc4_decode_quarter(const uint8_t *chunk, uint8_t *tile, int row, int qtr) {
+    const uint2 w = *reinterpret_cast<const uint2 *>(chunk + row * 32 + qtr * 8);
+    const int half = qtr >> 1;
     __half2 s2;
     if constexpr (WT == 39) {
         // 2^(e - 127) (e = 0: a zero block), exact in f16 for the exponents the load accepts
@@ -987,9 +1059,9 @@ __device__ __forceinline__ void tc4_decode_half(const uint8_t *chunk, uint8_t *t
         const __half d = __ushort_as_half(*reinterpret_cast<const uint16_t *>(chunk + TC4_NIB + row * 4 + half * 2));
         s2 = __halves2half2(d, d);
     }
-    const uint32_t words[4] = {w.x, w.y, w.z, w.w};
+    const uint32_t words[2] = {w.x, w.y};
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {  // 8 columns: bytes 4i .. 4i+3 of the half row
+    for (int i = 0; i < 2; ++i) {  // 8 columns: bytes 4i .. 4i+3 of the quarter row
         uint32_t pr[4];
         decode4<WT>(words[i], pr);  // pr[j]: (column 2j, 2j + 1) of these 8, true values
         uint32_t o[4];
@@ -998,7 +1070,7 @@ __device__ __forceinline__ void tc4_decode_half(const uint8_t *chunk, uint8_t *t
             const __half2 h = __hmul2(*reinterpret_cast<const __half2 *>(&pr[j]), s2);
             o[j] = *reinterpret_cast<const uint32_t *>(&h);
         }
-        const int u = half * 4 + i;
+        const int u = qtr * 2 + i;
         *reinterpret_cast<uint4 *>(tile + row * 128 + ((u ^ (row & 7)) * 16)) = make_uint4(o[0], o[1], o[2], o[3]);
     }
 }
@@ -1008,30 +1080,31 @@ __device__ __forceinline__ void tc4_decode_half(const uint8_t *chunk, uint8_t *t
 // producer's copies complete on full[s]; the decoders wait for it, write the tiles, fence them to
 // the async proxy and arrive on dec[s] (one arrival per decoder warp); the MMA issuer waits for
 // both.
-template <int MODE, int WT>
-__global__ void __launch_bounds__(pf4_cfg<MODE, WT>::THREADS, 1)
+template <int MODE, int WT, int BN = PF_BN>
+__global__ void __launch_bounds__(pf4_cfg<MODE, WT, BN>::THREADS, 1)
     k_pf_gemm4(const __grid_constant__ CUtensorMap xmap, pf_gemm4_args a4) {
-    using C = pf4_cfg<MODE, WT>;
+    using C = pf4_cfg<MODE, WT, BN>;
     const pf_gemm_args &a = a4.g;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
-    __shared__ __align__(8) uint64_t full[C::STAGES], dec[C::STAGES], empty[C::STAGES], acc_full[2], acc_empty[2], done;
+    static_assert(C::RS == C::TS, "one commit per stage releases the raw and the tile stage together");
+    __shared__ __align__(8) uint64_t full[C::RS], empty[C::RS], dec[C::TS], acc_full[2], acc_empty[2], done[C::ISS];
     __shared__ uint32_t tmem_slot;
     __shared__ volatile int abort_;
     __shared__ int s_toff[1025];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     for (int i = threadIdx.x; i <= a.E; i += blockDim.x) s_toff[i] = a.toff[i];
     if (threadIdx.x == 0) {
-        for (int s = 0; s < C::STAGES; ++s) {
+        for (int s = 0; s < C::RS; ++s) {
             tc::bar_init(&full[s], 1);
-            tc::bar_init(&dec[s], C::DEC_WARPS);
-            tc::bar_init(&empty[s], 1);
+            tc::bar_init(&empty[s], C::ISS);  // one commit per issuer
         }
+        for (int s = 0; s < C::TS; ++s) tc::bar_init(&dec[s], C::DEC_WARPS);
         for (int b = 0; b < 2; ++b) {
-            tc::bar_init(&acc_full[b], 1);
+            tc::bar_init(&acc_full[b], C::ISS);
             tc::bar_init(&acc_empty[b], 4);
         }
-        tc::bar_init(&done, 1);
+        for (int i = 0; i < C::ISS; ++i) tc::bar_init(&done[i], 1);
         abort_ = 0;
         tc::bar_init_fence();
     }
@@ -1054,9 +1127,9 @@ __global__ void __launch_bounds__(pf4_cfg<MODE, WT>::THREADS, 1)
         e = lo;
         nt = ntg - s_toff[e];
     };
-    auto stage_a = [&](int s) { return smem + (size_t)s * C::STAGE; };                 // bf16 A tiles
-    auto stage_b = [&](int s) { return stage_a(s) + C::NA * PF_TILE_BYTES; };           // B tile
-    auto stage_raw = [&](int s) { return stage_a(s) + (C::NA + 1) * PF_TILE_BYTES; };   // 4-bit chunks
+    auto stage_a = [&](int t) { return smem + (size_t)t * C::TSTAGE; };                       // f16 A tiles
+    auto stage_b = [&](int s) { return smem + (size_t)C::TS * C::TSTAGE + (size_t)s * C::RSTAGE; };  // B tile
+    auto stage_raw = [&](int s) { return stage_b(s) + C::B_BYTES; };                            // 4-bit chunks
 
     if (warp == 0) {
         long g = 0;
@@ -1065,13 +1138,13 @@ __global__ void __launch_bounds__(pf4_cfg<MODE, WT>::THREADS, 1)
                 int e, nt, mt;
                 locate(tile, e, nt, mt);
                 const int we = a.seg_w ? a.seg_w[e] : e;
-                const int rowB = a.off[e] + nt * PF_BN;
+                const int rowB = a.off[e] + nt * BN;
                 for (int kb = 0; kb < KB; ++kb, ++g) {
-                    const int s = (int)(g % C::STAGES);
-                    if (g >= C::STAGES &&
-                        !tc::bar_wait(&empty[s], (unsigned)(((g / C::STAGES) - 1) & 1), &abort_, a.status, PF_STATUS_WAIT))
+                    const int s = (int)(g % C::RS);
+                    if (g >= C::RS &&
+                        !tc::bar_wait(&empty[s], (unsigned)(((g / C::RS) - 1) & 1), &abort_, a.status, PF_STATUS_WAIT))
                         break;
-                    tc::bar_expect_tx(&full[s], C::NA * C::CB + PF_TILE_BYTES);
+                    tc::bar_expect_tx(&full[s], C::NA * C::CB + C::B_BYTES);
                     for (int m = 0; m < C::NA; ++m) {
                         const uint8_t *src = a4.w4 + ((((size_t)we * C::NA + m) * a4.RB + mt) * a4.KB + kb) * C::CB;
                         bulk_g2s(stage_raw(s) + m * C::CB, src, (unsigned)C::CB, &full[s]);
@@ -1080,13 +1153,14 @@ __global__ void __launch_bounds__(pf4_cfg<MODE, WT>::THREADS, 1)
                 }
             }
             if (abort_)
-                for (long j = std::max(0L, g - C::STAGES); j < g; ++j)
-                    tc::bar_drain(&full[j % C::STAGES], (unsigned)((j / C::STAGES) & 1));
+                for (long j = std::max(0L, g - C::RS); j < g; ++j)
+                    tc::bar_drain(&full[j % C::RS], (unsigned)((j / C::RS) & 1));
         }
         __syncwarp();
-    } else if (warp == 1) {
+    } else if (warp == 1 || (C::ISS > 1 && warp >= C::ISS_WARP1)) {
+        const int iss = warp == 1 ? 0 : 1 + warp - C::ISS_WARP1;
         if (lane == 0) {
-            constexpr uint32_t idesc = tc::idesc_f16_f32(PF_BM, PF_BN);  // A and B both f16
+            constexpr uint32_t idesc = tc::idesc_f16_f32(PF_BM, BN);  // A and B both f16
             long g = 0, i = 0;
             for (long tile = blockIdx.x; tile < total && !abort_; tile += gridDim.x, ++i) {
                 const int ab = (int)(i & 1);
@@ -1096,30 +1170,44 @@ __global__ void __launch_bounds__(pf4_cfg<MODE, WT>::THREADS, 1)
                 tc::fence_after_sync();
                 bool ok = true;
                 for (int kb = 0; kb < KB; ++kb, ++g) {
-                    const int s = (int)(g % C::STAGES);
-                    const unsigned ph = (unsigned)((g / C::STAGES) & 1);
-                    if (!tc::bar_wait(&full[s], ph, &abort_, a.status, PF_STATUS_WAIT) ||
-                        !tc::bar_wait(&dec[s], ph, &abort_, a.status, PF_STATUS_WAIT)) {
+                    const int s = (int)(g % C::RS), ts = (int)(g % C::TS);
+                    if (!tc::bar_wait(&full[s], (unsigned)((g / C::RS) & 1), &abort_, a.status, PF_STATUS_WAIT) ||
+                        !tc::bar_wait(&dec[ts], (unsigned)((g / C::TS) & 1), &abort_, a.status, PF_STATUS_WAIT)) {
                         ok = false;
                         break;
                     }
                     tc::fence_after_sync();
-                    const uint32_t a0 = tc::sa(stage_a(s)), b0 = tc::sa(stage_b(s));
+                    const uint32_t a0 = tc::sa(stage_a(ts)), b0 = tc::sa(stage_b(s));
+                    if constexpr (C::ISS == 1) {
 #pragma unroll
-                    for (int k = 0; k < PF_BK / 16; ++k) {
-                        const uint32_t acc = (kb > 0 || k > 0) ? 1u : 0u;
-                        tc::mma_bf16(dcol, tc::desc_k_sw128(a0 + k * 32), tc::desc_k_sw128(b0 + k * 32), idesc, acc);
-                        if (MODE == 0)
-                            tc::mma_bf16(dcol + PF_BN, tc::desc_k_sw128(a0 + PF_TILE_BYTES + k * 32),
-                                         tc::desc_k_sw128(b0 + k * 32), idesc, acc);
+                        for (int k = 0; k < PF_BK / 16; ++k) {
+                            const uint32_t acc = (kb > 0 || k > 0) ? 1u : 0u;
+                            tc::mma_bf16(dcol, tc::desc_k_sw128(a0 + k * 32), tc::desc_k_sw128(b0 + k * 32), idesc, acc);
+                            if (MODE == 0)
+                                tc::mma_bf16(dcol + BN, tc::desc_k_sw128(a0 + PF_TILE_BYTES + k * 32),
+                                             tc::desc_k_sw128(b0 + k * 32), idesc, acc);
+                        }
+                    } else if constexpr (MODE == 0) {
+                        // issuer iss: matrix iss / 2 (gate or up), K steps 2 (iss % 2), 2 (iss % 2) + 1
+                        const uint32_t am = a0 + (uint32_t)((iss >> 1) * PF_TILE_BYTES);
+#pragma unroll
+                        for (int k = 0; k < 2; ++k) {
+                            const int kk = 2 * (iss & 1) + k;
+                            tc::mma_bf16(dcol + iss * BN, tc::desc_k_sw128(am + kk * 32), tc::desc_k_sw128(b0 + kk * 32),
+                                         idesc, (kb > 0 || k > 0) ? 1u : 0u);
+                        }
+                    } else {
+                        // issuer iss: K step iss into accumulator iss
+                        tc::mma_bf16(dcol + iss * BN, tc::desc_k_sw128(a0 + iss * 32), tc::desc_k_sw128(b0 + iss * 32),
+                                     idesc, kb > 0 ? 1u : 0u);
                     }
-                    tc::mma_commit(&empty[s]);
+                    tc::mma_commit(&empty[s]);  // releases the raw stage and the tile stage
                 }
                 if (!ok) break;
                 tc::mma_commit(&acc_full[ab]);
             }
-            tc::mma_commit(&done);
-            tc::bar_drain(&done, 0);
+            tc::mma_commit(&done[iss]);
+            tc::bar_drain(&done[iss], 0);
         }
         __syncwarp();
     } else if (warp < 6) {
@@ -1140,15 +1228,35 @@ __global__ void __launch_bounds__(pf4_cfg<MODE, WT>::THREADS, 1)
             const int wblk = a.seg_w ? a.seg_w[e] : e;
             const float bg = (a.bias && fok) ? a.bias[(size_t)wblk * a.Mrows + f] : 0.f;
             const float bu = (MODE == 0 && a.bias && fok) ? a.bias[(size_t)(a.n_blocks + wblk) * a.Mrows + f] : 0.f;
-            for (int c0 = 0; c0 < PF_BN; c0 += 16) {
+            for (int c0 = 0; c0 < BN; c0 += 16) {
                 float d[16];
                 tc::tmem_ld16(acc_base + c0, d);
+                if (MODE == 1 && C::ISS == 4) {  // the other issuers' K steps, in order
+                    float d2[16];
+#pragma unroll
+                    for (int i = 1; i < 4; ++i) {
+                        tc::tmem_ld16(acc_base + i * BN + c0, d2);
+#pragma unroll
+                        for (int j = 0; j < 16; ++j) d[j] += d2[j];
+                    }
+                }
                 if (MODE == 0) {
                     float u[16];
-                    tc::tmem_ld16(acc_base + PF_BN + c0, u);
+                    if constexpr (C::ISS == 4) {  // gate = acc 0 + acc 1, up = acc 2 + acc 3
+                        float d2[16];
+                        tc::tmem_ld16(acc_base + BN + c0, d2);
+#pragma unroll
+                        for (int j = 0; j < 16; ++j) d[j] += d2[j];
+                        tc::tmem_ld16(acc_base + 2 * BN + c0, u);
+                        tc::tmem_ld16(acc_base + 3 * BN + c0, d2);
+#pragma unroll
+                        for (int j = 0; j < 16; ++j) u[j] += d2[j];
+                    } else {
+                        tc::tmem_ld16(acc_base + BN + c0, u);
+                    }
 #pragma unroll
                     for (int j = 0; j < 16; ++j) {
-                        const int n = nt * PF_BN + c0 + j;
+                        const int n = nt * BN + c0 + j;
                         if (fok && n < n_rows)
                             a.act_out[(size_t)(seg + n) * a.Mrows + f] =
                                 __half_as_ushort(__float2half_rn(act_fn(a.act, d[j] + bg, u[j] + bu, a.alpha, a.limit)));
@@ -1157,7 +1265,7 @@ __global__ void __launch_bounds__(pf4_cfg<MODE, WT>::THREADS, 1)
                     float *ybase = a.seg_y ? a.seg_y[e] : a.y_out + (size_t)seg * a.Mrows;
 #pragma unroll
                     for (int j = 0; j < 16; ++j) {
-                        const int n = nt * PF_BN + c0 + j;
+                        const int n = nt * BN + c0 + j;
                         if (fok && n < n_rows) ybase[(size_t)n * a.Mrows + f] = d[j] + bg;
                     }
                 }
@@ -1168,23 +1276,28 @@ __global__ void __launch_bounds__(pf4_cfg<MODE, WT>::THREADS, 1)
             if (lane == 0) tc::bar_arrive(&acc_empty[ab]);
         }
     } else {
-        // decoder warps: thread t takes row t / 2, half t % 2 of every staged chunk
-        const int t = threadIdx.x - 6 * 32, row = t >> 1, half = t & 1;
+        // decoder warps: quarter rows (16 columns) t, t + 32 DEC_WARPS, ... of the stage's chunks
+        const int t = threadIdx.x - 6 * 32;
         long g = 0;
         for (long tile = blockIdx.x; tile < total && !abort_; tile += gridDim.x) {
             bool ok = true;
             for (int kb = 0; kb < KB; ++kb, ++g) {
-                const int s = (int)(g % C::STAGES);
-                if (!tc::bar_wait(&full[s], (unsigned)((g / C::STAGES) & 1), &abort_, a.status, PF_STATUS_WAIT)) {
+                const int s = (int)(g % C::RS), ts = (int)(g % C::TS);
+                // the tile stage is free once the MMAs of its previous use have completed
+                if (!tc::bar_wait(&full[s], (unsigned)((g / C::RS) & 1), &abort_, a.status, PF_STATUS_WAIT) ||
+                    (g >= C::TS &&
+                     !tc::bar_wait(&empty[ts], (unsigned)(((g / C::TS) - 1) & 1), &abort_, a.status, PF_STATUS_WAIT))) {
                     ok = false;
                     break;
                 }
 #pragma unroll
-                for (int m = 0; m < C::NA; ++m)
-                    tc4_decode_half<WT>(stage_raw(s) + m * C::CB, stage_a(s) + m * PF_TILE_BYTES, row, half);
+                for (int q = t; q < C::NA * 512; q += C::DEC_WARPS * 32) {
+                    const int m = q >> 9, row = (q & 511) >> 2;
+                    tc4_decode_quarter<WT>(stage_raw(s) + m * C::CB, stage_a(ts) + m * PF_TILE_BYTES, row, q & 3);
+                }
                 fence_proxy_async();  // the generic-proxy tile writes, visible to the MMA's reads
                 __syncwarp();
-                if (lane == 0) tc::bar_arrive(&dec[s]);
+                if (lane == 0) tc::bar_arrive(&dec[ts]);
             }
             if (!ok) break;
         }
@@ -1216,8 +1329,6 @@ encode_tiled_fn encoder() {
     return fn;
 }
 
-// A bf16 row-major [rows][cols] matrix read as 128-row x 64-column boxes, 128-byte swizzle
-// (the UMMA K-major canonical layout); rows past the end read as zeros.
 // An E4M3 row-major [rows][cols] matrix read as box_rows-row x 128-byte boxes, 128-byte swizzle;
 // rows and columns past the end read as zeros.
 bool make_map8(CUtensorMap *map, const void *base, long rows, int cols, int box_rows) {
@@ -1232,12 +1343,14 @@ bool make_map8(CUtensorMap *map, const void *base, long rows, int cols, int box_
                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-bool make_map(CUtensorMap *map, const void *base, long rows, int cols) {
+// A bf16 (or f16) row-major [rows][cols] matrix read as box_rows-row x 64-column boxes, 128-byte
+// swizzle (the UMMA K-major canonical layout); rows past the end read as zeros.
+bool make_map(CUtensorMap *map, const void *base, long rows, int cols, int box_rows = PF_BM) {
     encode_tiled_fn enc = encoder();
     if (!enc) return false;
     const cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
     const cuuint64_t strides[1] = {(cuuint64_t)cols * 2};
-    const cuuint32_t box[2] = {PF_BK, PF_BM};
+    const cuuint32_t box[2] = {PF_BK, (cuuint32_t)box_rows};
     const cuuint32_t es[2] = {1, 1};
     return enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void *>(base), dims, strides, box, es,
                CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -1250,11 +1363,13 @@ namespace moearc {
 
 // For other translation units (the batched decoder): the 128 x 64 bf16 K-major tensor map, and a
 // dense GEMM on the same kernel, out[n][m] = sum_k W[m][k] x[n][k] (f32), as one segment of
-// n rows: seg_off = {0, n} and seg_toff = {0, ceil(n / 128)} in device memory.
+// n rows: seg_off = {0, n} and seg_toff = {0, ceil(n / 128)} in device memory. With ksplit > 1
+// the K blocks are split into ksplit runs and run j's partial sums go to out + j * split_stride
+// (the caller adds them, in order).
 bool tc_make_map_bf16(CUtensorMap *map, const void *base, long rows, int cols) { return make_map(map, base, rows, cols); }
 
 int tc_dense_gemm(moearc_ctx *c, const CUtensorMap &w, int M, int K, const CUtensorMap &x, const int *seg_off,
-                  const int *seg_toff, float *out, int *status) {
+                  const int *seg_toff, float *out, int *status, int ksplit, size_t split_stride) {
     static std::atomic<bool> ready[MOEARC_MAX_DEVICES];
     if (once_per_device(ready, [] { return set_smem(k_pf_gemm<1>, pf_cfg<1>::SMEM); }) != cudaSuccess) return ERR;
     if (K % PF_BK) return ERR_ARG;
@@ -1266,7 +1381,10 @@ int tc_dense_gemm(moearc_ctx *c, const CUtensorMap &w, int M, int K, const CUten
     g.toff = seg_toff;
     g.y_out = out;
     g.status = status;
-    const int grid = std::min(c->sm_count, (M + PF_BM - 1) / PF_BM * 8);  // tiles are few: n is small
+    if (ksplit > K / PF_BK) return ERR_ARG;
+    g.ksplit = ksplit;
+    g.split_stride = split_stride;
+    const int grid = std::min(c->sm_count, (M + PF_BM - 1) / PF_BM * std::max(8, ksplit));  // n is small
     k_pf_gemm<1><<<grid, 192, pf_cfg<1>::SMEM, c->stream>>>(w, x, g);
     return cudaGetLastError() == cudaSuccess ? OK : ERR;
 }
@@ -1287,6 +1405,7 @@ struct moearc_x_prefill {
     bool order_identity = true;
     uint16_t *xp, *actb;
     CUtensorMap map_xp, map_act;
+    CUtensorMap map_xp32, map_act32;  // the same with 32-row boxes (the 4-bit form's decode-sized tiles)
     // expert weights, allocated by the first load of each form: the bf16 expansion
     // ([E][2][I][H] and [E][H][I]) or the 4-bit chunks (tc4 layout); the last load picks the form
     void *w16 = nullptr;
@@ -1384,7 +1503,8 @@ bool ensure_4bit(moearc_x_prefill *p) {
 }
 
 // The grouped GEMM of one matrix set (MODE 0 gate-up, 1 down) on whichever weight form is loaded.
-int launch_gemm(moearc_x_prefill *p, int mode, const pf_gemm_args &g_in, const CUtensorMap &xmap) {
+// bn: rows per tile, PF_BN or (4-bit form only) PF4_BN_SMALL, as the tile offsets were counted.
+int launch_gemm(moearc_x_prefill *p, int mode, const pf_gemm_args &g_in, const CUtensorMap &xmap, int bn = PF_BN) {
     moearc_ctx *c = p->c;
     cudaStream_t st = c->stream;
     pf_gemm_args g = g_in;
@@ -1398,6 +1518,18 @@ int launch_gemm(moearc_x_prefill *p, int mode, const pf_gemm_args &g_in, const C
     pf_gemm4_args a4{g, mode == 0 ? p->w4gu : p->w4dn, 0, 0};
     a4.RB = mode == 0 ? (p->I + 127) / 128 : (p->H + 127) / 128;
     a4.KB = mode == 0 ? p->H / 64 : p->I / 64;
+    if (bn == PF4_BN_SMALL) {
+        constexpr int S = PF4_BN_SMALL;
+        if (p->wtype == T_MXFP4) {
+            if (mode == 0) k_pf_gemm4<0, 39, S><<<c->sm_count, pf4_cfg<0, 39, S>::THREADS, pf4_cfg<0, 39, S>::SMEM, st>>>(xmap, a4);
+            else k_pf_gemm4<1, 39, S><<<c->sm_count, pf4_cfg<1, 39, S>::THREADS, pf4_cfg<1, 39, S>::SMEM, st>>>(xmap, a4);
+        } else {
+            if (mode == 0) k_pf_gemm4<0, 2, S><<<c->sm_count, pf4_cfg<0, 2, S>::THREADS, pf4_cfg<0, 2, S>::SMEM, st>>>(xmap, a4);
+            else k_pf_gemm4<1, 2, S><<<c->sm_count, pf4_cfg<1, 2, S>::THREADS, pf4_cfg<1, 2, S>::SMEM, st>>>(xmap, a4);
+        }
+        return cudaGetLastError() == cudaSuccess ? OK : ERR;
+    }
+    if (bn != PF_BN) return ERR_ARG;
     if (p->wtype == T_MXFP4) {
         if (mode == 0) k_pf_gemm4<0, 39><<<c->sm_count, pf4_cfg<0, 39>::THREADS, pf4_cfg<0, 39>::SMEM, st>>>(xmap, a4);
         else k_pf_gemm4<1, 39><<<c->sm_count, pf4_cfg<1, 39>::THREADS, pf4_cfg<1, 39>::SMEM, st>>>(xmap, a4);
@@ -1475,8 +1607,15 @@ moearc_x_prefill *moearc_x_prefill_create(moearc_ctx *c, const moearc_x_moe_desc
     p->dst_base = reinterpret_cast<int *>(b + o_ptrs + sizeof(void *) * 2048);
     p->xp = reinterpret_cast<uint16_t *>(b + o_xp);
     p->actb = reinterpret_cast<uint16_t *>(b + o_act);
+    constexpr int S = PF4_BN_SMALL;
     const bool ok = make_map(&p->map_xp, p->xp, (long)rows, p->H) &&
                     make_map(&p->map_act, p->actb, (long)rows, p->I) &&
+                    make_map(&p->map_xp32, p->xp, (long)rows, p->H, S) &&
+                    make_map(&p->map_act32, p->actb, (long)rows, p->I, S) &&
+                    set_smem(k_pf_gemm4<0, 39, S>, pf4_cfg<0, 39, S>::SMEM) == cudaSuccess &&
+                    set_smem(k_pf_gemm4<1, 39, S>, pf4_cfg<1, 39, S>::SMEM) == cudaSuccess &&
+                    set_smem(k_pf_gemm4<0, 2, S>, pf4_cfg<0, 2, S>::SMEM) == cudaSuccess &&
+                    set_smem(k_pf_gemm4<1, 2, S>, pf4_cfg<1, 2, S>::SMEM) == cudaSuccess &&
                     set_smem(k_pf_gemm4<0, 39>, pf4_cfg<0, 39>::SMEM) == cudaSuccess &&
                     set_smem(k_pf_gemm4<1, 39>, pf4_cfg<1, 39>::SMEM) == cudaSuccess &&
                     set_smem(k_pf_gemm4<0, 2>, pf4_cfg<0, 2>::SMEM) == cudaSuccess &&
@@ -1674,11 +1813,13 @@ int prefill_forward(moearc_x_prefill *p, const uint16_t *x, unsigned n_tokens, c
     if (cudaMemsetAsync(p->cnt, 0, sizeof(int) * (p->E + 1), st) != cudaSuccess) return ERR;
     mark(0);
     pf_route_args ra{x, x32, router_w, router_b, T, p->H, p->E, p->K, p->gating, p->logits, p->idx, p->wts, p->cnt, p->epos};
-    k_pf_logits<<<(T + PF_LOGIT_TOK - 1) / PF_LOGIT_TOK, 256, PF_LOGIT_TOK * p->H * 4, st>>>(ra);
+    k_pf_logits<<<logit_grid(T, p->E), 256, PF_LOGIT_TOK * p->H * 4, st>>>(ra);
     mark(1);
     k_pf_topk<<<(T + 7) / 8, 256, 0, st>>>(ra);
     mark(2);
-    k_pf_scan<<<1, 1024, 0, st>>>(p->cnt, p->E, p->off, p->toff, p->cursor, p->mode8 ? PF8_BN : PF_BN);
+    // the 4-bit form takes 32-row tiles when the rows per expert are few (decode-sized batches)
+    const int bn = p->mode8 ? PF8_BN : (p->mode4 && (long)T * p->K <= (long)PF4_SMALL_ROWS * p->E) ? PF4_BN_SMALL : PF_BN;
+    k_pf_scan<<<1, 1024, 0, st>>>(p->cnt, p->E, p->off, p->toff, p->cursor, bn);
     mark(3);
     const long pairs = (long)T * p->K;
     if (p->mode8) {
@@ -1735,11 +1876,12 @@ int prefill_forward(moearc_x_prefill *p, const uint16_t *x, unsigned n_tokens, c
     g.Mrows = p->I;
     g.K = p->H;
     if (!p->w16 && !p->w4) return ERR_ARG;  // no weights loaded
-    if (launch_gemm(p, 0, g, p->map_xp) != OK) return ERR;
+    const bool small = bn == PF4_BN_SMALL;
+    if (launch_gemm(p, 0, g, small ? p->map_xp32 : p->map_xp, bn) != OK) return ERR;
     mark(5);
     g.Mrows = p->H;
     g.K = p->I;
-    if (launch_gemm(p, 1, g, p->map_act) != OK) return ERR;
+    if (launch_gemm(p, 1, g, small ? p->map_act32 : p->map_act, bn) != OK) return ERR;
     mark(6);
     const long n = (long)T * p->H;
     k_pf_combine<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(p->y, p->perm, p->wts, residual, out, T, p->K, p->H);
@@ -1756,6 +1898,8 @@ int prefill_forward_x32(moearc_x_prefill *p, const uint16_t *x, const float *x32
                         const float *router_w, const float *router_b, const float *residual, float *out) {
     return prefill_forward(p, x, n_tokens, router_w, router_b, residual, out, nullptr, x32);
 }
+int prefill_route_x32(moearc_x_prefill *p, const uint16_t *x, const float *x32, unsigned n_tokens,
+                      const float *router_w, const float *router_b);
 }  // namespace moearc
 
 extern "C" {
@@ -1788,8 +1932,15 @@ int moearc_x_prefill_profile(moearc_x_prefill *p, const uint16_t *x, unsigned n_
 // expert range travel to the rank that owns it before moearc_x_prefill_experts.
 int moearc_x_prefill_route(moearc_x_prefill *p, const uint16_t *x, unsigned n_tokens, const float *router_w,
                            const float *router_b) {
+    return prefill_route_x32(p, x, nullptr, n_tokens, router_w, router_b);
+}
+}  // extern "C"
+
+namespace moearc {
+// moearc_x_prefill_route with the router logits taken from x32 (f32 [T][H]) when it is given.
+int prefill_route_x32(moearc_x_prefill *p, const uint16_t *x, const float *x32, unsigned n_tokens,
+                      const float *router_w, const float *router_b) {
     if (p && p->mode8) return ERR_ARG;  // the expert-parallel steps take the bf16 and 4-bit forms
-    const float *x32 = nullptr;
     if (!p || !x || !router_w) return ERR;
     if (n_tokens == 0) return OK;
     if ((int)n_tokens > p->T_max) return ERR_ARG;
@@ -1798,7 +1949,7 @@ int moearc_x_prefill_route(moearc_x_prefill *p, const uint16_t *x, unsigned n_to
     const int T = (int)n_tokens;
     if (cudaMemsetAsync(p->cnt, 0, sizeof(int) * (p->E + 1), st) != cudaSuccess) return ERR;
     pf_route_args ra{x, x32, router_w, router_b, T, p->H, p->E, p->K, p->gating, p->logits, p->idx, p->wts, p->cnt, p->epos};
-    k_pf_logits<<<(T + PF_LOGIT_TOK - 1) / PF_LOGIT_TOK, 256, PF_LOGIT_TOK * p->H * 4, st>>>(ra);
+    k_pf_logits<<<logit_grid(T, p->E), 256, PF_LOGIT_TOK * p->H * 4, st>>>(ra);
     k_pf_topk<<<(T + 7) / 8, 256, 0, st>>>(ra);
     k_pf_scan<<<1, 1024, 0, st>>>(p->cnt, p->E, p->off, p->toff, p->cursor);
     const long pairs = (long)T * p->K;
@@ -1806,6 +1957,40 @@ int moearc_x_prefill_route(moearc_x_prefill *p, const uint16_t *x, unsigned n_to
                                                               p->perm, p->xp, p->mode4 ? 1 : 0, nullptr, nullptr, 0);
     return cudaGetLastError() == cudaSuccess ? OK : ERR;
 }
+
+// The expert FFN of the 4-bit form over segments described in device memory, for a caller whose
+// row counts never reach the host (the batched decoder's expert-parallel step, inside a captured
+// graph): segment i is rows off[i] .. off[i+1] of rows (f16 [n_rows][n_embd]) for weight slot
+// seg_w[i], toff its 32-row tile offsets (a segment with no tiles is skipped: gaps between the
+// segments). act (f16 [n_rows][n_ff]) and y (f32 [n_rows][n_embd]) are indexed like rows.
+int prefill_experts_dev(moearc_x_prefill *p, const uint16_t *rows, long n_rows, const int *off, const int *toff,
+                        const int *seg_w, int n_seg, uint16_t *act, float *y) {
+    if (!p || !rows || !off || !toff || !seg_w || !act || !y) return ERR;
+    if (!p->mode4 || n_seg < 1 || n_seg > 1024) return ERR_ARG;
+    CUtensorMap map_rows, map_act;
+    if (!make_map(&map_rows, rows, n_rows, p->H, PF4_BN_SMALL) || !make_map(&map_act, act, n_rows, p->I, PF4_BN_SMALL))
+        return ERR_ARG;
+    pf_gemm_args g{};
+    g.E = n_seg;
+    g.off = off;
+    g.toff = toff;
+    g.seg_w = seg_w;
+    g.act = p->act;
+    g.alpha = p->alpha;
+    g.limit = p->limit;
+    g.act_out = act;
+    g.y_out = y;
+    g.status = p->status;
+    g.Mrows = p->I;
+    g.K = p->H;
+    if (launch_gemm(p, 0, g, map_rows, PF4_BN_SMALL) != OK) return ERR;
+    g.Mrows = p->H;
+    g.K = p->I;
+    return launch_gemm(p, 1, g, map_act, PF4_BN_SMALL);
+}
+}  // namespace moearc
+
+extern "C" {
 
 // The expert FFN over rows given in segments: segment s holds seg_counts[s] consecutive rows of
 // rows_in (bf16 [n_rows][n_embd]) for expert seg_expert[s], an index into the experts last
@@ -1879,7 +2064,7 @@ int moearc_x_prefill_route_begin(moearc_x_prefill *p, const uint16_t *x, unsigne
     const int T = (int)n_tokens;
     const float *x32 = nullptr;
     pf_route_args ra{x, x32, router_w, router_b, T, p->H, p->E, p->K, p->gating, p->logits, p->idx, p->wts, p->cnt, p->epos};
-    k_pf_logits<<<(T + PF_LOGIT_TOK - 1) / PF_LOGIT_TOK, 256, PF_LOGIT_TOK * p->H * 4, st>>>(ra);
+    k_pf_logits<<<logit_grid(T, p->E), 256, PF_LOGIT_TOK * p->H * 4, st>>>(ra);
     k_pf_topk<<<(T + 7) / 8, 256, 0, st>>>(ra);
     return cudaGetLastError() == cudaSuccess ? OK : ERR;
 }

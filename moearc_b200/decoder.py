@@ -276,10 +276,16 @@ class BatchDecoder:
     """n_batch independent sequences decoding one token each per step (moearc_x_batch_decoder_*):
     the batched serving case (configs[4]: 64 streams of a Qwen3-MoE-shaped model)."""
 
-    def __init__(self, ctx: Context, cfg: DecoderConfig, n_batch: int):
+    def __init__(self, ctx: Context, cfg: DecoderConfig, n_batch: int, ep: tuple | None = None):
+        """ep = (comm, rank, n_ranks): expert parallelism over an NCCL communicator (a handle from
+        moearc_b200.ep.nccl_comm); n_batch is then this rank's streams."""
         self.ctx, self.cfg, self.n_batch = ctx, cfg, n_batch
         self._c = cfg.to_c()
-        self.h = ctx.lib.moearc_x_batch_decoder_create(ctx.raw, C.byref(self._c), n_batch)
+        if ep is None:
+            self.h = ctx.lib.moearc_x_batch_decoder_create(ctx.raw, C.byref(self._c), n_batch)
+        else:
+            comm, rank, world = ep
+            self.h = ctx.lib.moearc_x_batch_decoder_create_ep(ctx.raw, C.byref(self._c), n_batch, comm, rank, world)
         if not self.h:
             raise BadArgument("moearc_x_batch_decoder_create refused the configuration or ran out of memory")
         self.in_ptr = ctx.lib.moearc_x_batch_decoder_input(self.h)

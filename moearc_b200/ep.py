@@ -277,6 +277,23 @@ def nccl_unique_id(lib) -> bytes:
     return bytes(buf)
 
 
+def nccl_comm(ctx, rank: int, world: int, unique_id: bytes) -> int:
+    """The library's NCCL communicator of `world` ranks (moearc_x_ep_comm_init) from a unique id
+    every rank shares; release it with nccl_comm_destroy."""
+    import ctypes as C
+
+    p = C.c_void_p()
+    idb = (C.c_char * 128).from_buffer_copy(unique_id)
+    if ctx.lib.moearc_x_ep_comm_init(ctx.raw, C.byref(p), world, idb, rank) != 0:
+        raise RuntimeError("ncclCommInitRank failed")
+    return p.value
+
+
+def nccl_comm_destroy(ctx, comm: int) -> None:
+    if ctx.lib.moearc_x_ep_comm_destroy(comm) != 0:
+        raise RuntimeError("ncclCommDestroy failed")
+
+
 class NcclExpertParallelPrefill:
     """Expert parallelism through the library's C ABI (moearc_x_ep_*): the count all-gather, the
     row exchange and the result return run inside the library on an NCCL communicator, on the

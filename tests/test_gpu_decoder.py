@@ -481,10 +481,12 @@ def test_residency_cache_fetches_exactly_what_the_host_replay_predicts(ctx, sour
     assert sum(got) < steps * 2 * k  # the cache kept something
 
 
+@pytest.mark.parametrize("layout", [0, 1])  # experts at 4 bits (f16 tiles), or the bf16 expansion
 @pytest.mark.parametrize("etype,qk", [(O.MXFP4, 0), (O.Q4_0, 1)])  # Q4_0 with QK-norm: the qwen3moe form
-def test_batch_decoder_matches_single_stream_decoders(ctx, etype, qk):
+def test_batch_decoder_matches_single_stream_decoders(ctx, etype, qk, layout):
     """Three sequences decoded together (moearc_x_batch_decoder: tcgen05 GEMMs for the
-    projections and the experts on bf16 activations, one batched attention launch) against the
+    projections and the experts on bf16 activations — the experts read at 4 bits and expanded to
+    f16 tiles in shared memory, or as their bf16 expansion — one batched attention launch) against the
     oracle's decode step run per sequence with its own KV pools, and against three single-stream
     decoders of the same configuration fed the same tokens: every sequence's output agrees
     within the reference's bf16-activation bound, max |a - b| <= 1e-2 max |b| (bf16 rounding of
@@ -495,7 +497,7 @@ def test_batch_decoder_matches_single_stream_decoders(ctx, etype, qk):
     kw = dict(n_layer=2, n_embd=256, n_head=8, n_head_kv=2, head_dim=64, n_expert=8, n_expert_used=2, n_ff=128,
               expert_type=etype, n_swa=0, has_sinks=0, n_ctx=96, seed=0xBA7C, has_qk_norm=qk)
     B = 3
-    bd = BatchDecoder(ctx, DecoderConfig(**kw), B)
+    bd = BatchDecoder(ctx, DecoderConfig(**kw, expert_layout=layout), B)
     bd.set_pos(0)
     singles = [Decoder(ctx, DecoderConfig(**kw)) for _ in range(B)]
     for d in singles:
@@ -534,7 +536,7 @@ def test_batch_decoder_matches_single_stream_decoders(ctx, etype, qk):
             worst = max(worst, float(np.max(np.abs(got[b] - want)) / np.max(np.abs(want))))
             worst_or = max(worst_or, float(np.max(np.abs(got[b] - ow)) / np.max(np.abs(ow))))
     assert bd.status() == 0
-    print(f"batch decoder etype={etype} qk_norm={qk}: 3 streams x 40 tokens, max |a-b| / max|b| = {worst_or:.3e} "
+    print(f"batch decoder etype={etype} qk_norm={qk} layout={layout}: 3 streams x 40 tokens, max |a-b| / max|b| = {worst_or:.3e} "
           f"against the oracle, {worst:.3e} against single-stream decoders (tolerance 1e-2); "
           f"near-tie routing flips (stream: token, block, margin): {diverged}")
     assert len(diverged) <= 1
