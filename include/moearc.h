@@ -452,6 +452,12 @@ int moearc_x_decoder_fill_kv(moearc_x_decoder *d, unsigned int depth, unsigned l
 /* Decode one token at the current position, enqueued on the context's stream; the first call
  * captures the step as a CUDA graph (unless disabled) and later calls replay it. */
 int moearc_x_decoder_step(moearc_x_decoder *d);
+/* One token from host memory to host memory (the reference's decode loop takes a host embedding
+ * row and returns host results, moe.rs:1862-1870, 2429-2442): x and y are n_embd f32 in any host
+ * memory. The call copies x to pinned staging, launches the step with its two copies as one
+ * graph (unless graphs are disabled), waits for it and writes the step's output to y. The first
+ * call allocates the pinned staging and captures that graph. */
+int moearc_x_decoder_step_host(moearc_x_decoder *d, const float *x, float *y);
 int moearc_x_decoder_use_graph(moearc_x_decoder *d, int on);
 /* Reads and clears the device status words of the decoder's kernels: 0, or nonzero when a
  * bounded wait gave up (the step's output is then invalid). No reference counterpart: the

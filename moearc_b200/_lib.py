@@ -142,6 +142,7 @@ SIGNATURES: dict[str, tuple] = {
     "moearc_x_decoder_set_pos": (I, [P, U]),
     "moearc_x_decoder_fill_kv": (I, [P, U, C.c_ulonglong]),
     "moearc_x_decoder_step": (I, [P]),
+    "moearc_x_decoder_step_host": (I, [P, P, P]),
     "moearc_x_decoder_use_graph": (I, [P, I]),
     "moearc_x_decoder_kernel_spans": (I, [P, I]),
     "moearc_x_decoder_host_experts": (I, [P, I, F, U, I]),

@@ -128,6 +128,11 @@ struct moearc_x_decoder {
     unsigned long long *fetched = nullptr;  // experts the residency caches fetched
     cudaGraph_t graph = nullptr;
     cudaGraphExec_t exec = nullptr;
+    // moearc_x_decoder_step_host: pinned staging of one input and one output row, and the step
+    // captured with its two copies (host -> in, out -> host) as one graph
+    float *pin_in = nullptr, *pin_out = nullptr;
+    cudaGraph_t graph_io = nullptr;
+    cudaGraphExec_t exec_io = nullptr;
     bool use_graph = true;
     // the whole step as one persistent kernel (step.cuh) when the shape allows it; the chain
     // of per-block kernels otherwise (offloaded experts, head_dim 128, ...) or on request
@@ -200,8 +205,12 @@ struct moearc_x_decoder {
     void drop_graph() {
         if (exec) cudaGraphExecDestroy(exec);
         if (graph) cudaGraphDestroy(graph);
+        if (exec_io) cudaGraphExecDestroy(exec_io);
+        if (graph_io) cudaGraphDestroy(graph_io);
         exec = nullptr;
         graph = nullptr;
+        exec_io = nullptr;
+        graph_io = nullptr;
     }
 
     void *alloc(size_t bytes) {
@@ -825,6 +834,65 @@ int moearc_x_decoder_step(moearc_x_decoder *d) {
         rc = cudaGraphLaunch(d->exec, c->stream) == cudaSuccess ? OK : ERR;
     }
     if (rc == OK) d->pos += 1;
+    return rc;
+}
+
+// One step from host memory to host memory in one call (the reference's decode loop hands the
+// engine a host embedding row and reads host results back, moe.rs:1862-1870, 2429-2442): the
+// row goes to pinned staging, then one graph launch runs the host -> device copy, the step and
+// the device -> host copy of the output, and the call waits for it. Replacing three enqueues
+// and a wait by one launch and a wait keeps the GPU's idle time between synchronous steps to
+// the launch latency of one graph.
+int moearc_x_decoder_step_host(moearc_x_decoder *d, const float *x, float *y) {
+    if (!d || !x || !y) return ERR;
+    if ((unsigned)d->pos >= d->cfg.n_ctx) return ERR_ARG;
+    moearc_ctx *c = d->c;
+    const size_t bytes = sizeof(float) * d->cfg.n_embd;
+    if (!d->pin_in) {
+        void *pi = nullptr, *po = nullptr;
+        if (cudaMallocHost(&pi, bytes) != cudaSuccess || cudaMallocHost(&po, bytes) != cudaSuccess) {
+            cudaGetLastError();
+            if (pi) cudaFreeHost(pi);
+            return ERR;
+        }
+        d->host_allocs.push_back(pi);
+        d->host_allocs.push_back(po);
+        d->pin_in = static_cast<float *>(pi);
+        d->pin_out = static_cast<float *>(po);
+    }
+    // the previous call waited for its graph, so the staging rows are free
+    std::memcpy(d->pin_in, x, bytes);
+    auto enqueue = [&]() -> int {
+        if (cudaMemcpyAsync(d->in, d->pin_in, bytes, cudaMemcpyHostToDevice, c->stream) != cudaSuccess) return ERR;
+        const int r = enqueue_step(d);
+        if (r) return r;
+        return cudaMemcpyAsync(d->pin_out, d->out, bytes, cudaMemcpyDeviceToHost, c->stream) == cudaSuccess ? OK : ERR;
+    };
+    int rc = OK;
+    if (!d->use_graph) {
+        rc = enqueue();
+    } else {
+        if (!d->exec_io) {
+            if (cudaStreamBeginCapture(c->stream, cudaStreamCaptureModeThreadLocal) != cudaSuccess) return ERR;
+            rc = enqueue();
+            cudaGraph_t g = nullptr;
+            const cudaError_t e = cudaStreamEndCapture(c->stream, &g);
+            if (rc || e != cudaSuccess) {
+                if (g) cudaGraphDestroy(g);
+                cudaGetLastError();
+                return rc ? rc : ERR;
+            }
+            d->graph_io = g;
+            if (cudaGraphInstantiate(&d->exec_io, g, 0) != cudaSuccess) {
+                cudaGetLastError();
+                return ERR;
+            }
+        }
+        rc = cudaGraphLaunch(d->exec_io, c->stream) == cudaSuccess ? OK : ERR;
+    }
+    if (rc == OK) d->pos += 1;
+    if (cudaStreamSynchronize(c->stream) != cudaSuccess) return ERR;
+    if (rc == OK) std::memcpy(y, d->pin_out, bytes);
     return rc;
 }
 

@@ -217,6 +217,19 @@ class Decoder:
         """Enqueue one decode step (the caller synchronises when it needs the output)."""
         self.ctx._finish(self.ctx.lib.moearc_x_decoder_step(self.h), "decoder step")
 
+    def step_host(self, x: np.ndarray, out: np.ndarray | None = None) -> np.ndarray:
+        """Decode one token from a host row to a host row in one call: the input copy, the step
+        and the output copy run as one graph launch, and the call returns when the output has
+        arrived (moearc_x_decoder_step_host)."""
+        x = np.ascontiguousarray(x, np.float32)
+        assert x.size == self.cfg.n_embd
+        if out is None:
+            out = np.empty(self.cfg.n_embd, np.float32)
+        assert out.dtype == np.float32 and out.size == self.cfg.n_embd and out.flags.c_contiguous
+        self.ctx._finish(self.ctx.lib.moearc_x_decoder_step_host(self.h, x.ctypes.data, out.ctypes.data),
+                         "decoder step (host buffers)")
+        return out
+
     def set_input(self, x: np.ndarray) -> None:
         x = np.ascontiguousarray(x, np.float32)
         assert x.size == self.cfg.n_embd

@@ -578,3 +578,26 @@ def test_a_grid_barrier_that_runs_out_reports_it_and_the_next_step_is_exact(ctx)
     assert dec.status() == 0
     assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
     dec.close()
+
+
+@pytest.mark.parametrize("graph", [True, False])
+def test_one_call_host_step_gives_the_bits_of_the_enqueued_step(ctx, graph):
+    """moearc_x_decoder_step_host (host row in, host row out, the copies inside the step's graph)
+    against a twin decoder driven by input copy, step and output copy as separate calls: the
+    same bits at every position, past the 40-key window, and the positions advance alike."""
+    kw = dict(n_layer=2, n_embd=256, n_head=8, n_head_kv=2, head_dim=64, n_expert=8, n_expert_used=2,
+              n_ff=128, n_swa=40, swa_pattern=2, n_ctx=64, seed=0x5EED)
+    dec, twin = Decoder(ctx, DecoderConfig(**kw)), Decoder(ctx, DecoderConfig(**kw))
+    dec.use_graph(graph)
+    twin.use_graph(graph)
+    out = np.empty(kw["n_embd"], np.float32)
+    for pos in range(48):
+        x = O.synth_normal_f32(0x7100 + pos, kw["n_embd"], 1.0)
+        got = dec.step_host(x, out)
+        twin.set_input(x)
+        twin.step()
+        assert np.array_equal(got.view(np.uint32), twin.output().view(np.uint32)), pos
+    assert dec.pos == twin.pos == 48
+    assert dec.status() == 0 and twin.status() == 0
+    dec.close()
+    twin.close()
