@@ -131,6 +131,7 @@ struct moearc_x_decoder {
     // moearc_x_decoder_step_host: pinned staging of one input and one output row, and the step
     // captured with its two copies (host -> in, out -> host) as one graph
     float *pin_in = nullptr, *pin_out = nullptr;
+    float *pin_in_dev = nullptr, *pin_out_dev = nullptr;  // their device mappings
     cudaGraph_t graph_io = nullptr;
     cudaGraphExec_t exec_io = nullptr;
     bool use_graph = true;
@@ -843,6 +844,13 @@ int moearc_x_decoder_step(moearc_x_decoder *d) {
 // the device -> host copy of the output, and the call waits for it. Replacing three enqueues
 // and a wait by one launch and a wait keeps the GPU's idle time between synchronous steps to
 // the launch latency of one graph.
+// Copies one row between pinned host memory (read or written by the kernel over PCIe through its
+// device mapping) and device memory; a kernel node beside the step's kernels in place of a copy
+// engine node, whose hand-over to and from the compute engine costs more than the row's PCIe time.
+__global__ void k_row_copy(float4 *__restrict__ dst, const float4 *__restrict__ src, int n4) {
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += gridDim.x * blockDim.x) dst[i] = src[i];
+}
+
 int moearc_x_decoder_step_host(moearc_x_decoder *d, const float *x, float *y) {
     if (!d || !x || !y) return ERR;
     if ((unsigned)d->pos >= d->cfg.n_ctx) return ERR_ARG;
@@ -859,13 +867,36 @@ int moearc_x_decoder_step_host(moearc_x_decoder *d, const float *x, float *y) {
         d->host_allocs.push_back(po);
         d->pin_in = static_cast<float *>(pi);
         d->pin_out = static_cast<float *>(po);
+        void *di = nullptr, *dout = nullptr;
+        if (cudaHostGetDevicePointer(&di, pi, 0) != cudaSuccess || cudaHostGetDevicePointer(&dout, po, 0) != cudaSuccess) {
+            cudaGetLastError();
+            d->pin_in = d->pin_out = nullptr;
+            return ERR;
+        }
+        d->pin_in_dev = static_cast<float *>(di);
+        d->pin_out_dev = static_cast<float *>(dout);
     }
     // the previous call waited for its graph, so the staging rows are free
     std::memcpy(d->pin_in, x, bytes);
+    // rows of whole float4s (n_embd is a multiple of 64) copied by kernels; a copy engine otherwise
+    const bool rows4 = d->cfg.n_embd % 4 == 0;
+    const int n4 = (int)(d->cfg.n_embd / 4);
+    const unsigned nb = (unsigned)((n4 + 255) / 256);
     auto enqueue = [&]() -> int {
-        if (cudaMemcpyAsync(d->in, d->pin_in, bytes, cudaMemcpyHostToDevice, c->stream) != cudaSuccess) return ERR;
+        if (rows4) {
+            k_row_copy<<<nb, 256, 0, c->stream>>>(reinterpret_cast<float4 *>(d->in),
+                                                   reinterpret_cast<const float4 *>(d->pin_in_dev), n4);
+            if (cudaPeekAtLastError() != cudaSuccess) return ERR;
+        } else if (cudaMemcpyAsync(d->in, d->pin_in, bytes, cudaMemcpyHostToDevice, c->stream) != cudaSuccess) {
+            return ERR;
+        }
         const int r = enqueue_step(d);
         if (r) return r;
+        if (rows4) {
+            k_row_copy<<<nb, 256, 0, c->stream>>>(reinterpret_cast<float4 *>(d->pin_out_dev),
+                                                   reinterpret_cast<const float4 *>(d->out), n4);
+            return cudaPeekAtLastError() == cudaSuccess ? OK : ERR;
+        }
         return cudaMemcpyAsync(d->pin_out, d->out, bytes, cudaMemcpyDeviceToHost, c->stream) == cudaSuccess ? OK : ERR;
     };
     int rc = OK;
