@@ -361,6 +361,9 @@ def gpu_run(args, cfg, rank: int, world: int, dist) -> dict:
     xs_host = (np.ctypeslib.as_array(C.cast(pool, C.POINTER(C.c_float)), (n_pool, H)) if n_pool else
                np.ctypeslib.as_array(C.cast(host_in, C.POINTER(C.c_float)), (1, H)))
     y_host = np.empty(H, np.float32)
+    # warm-up: the first call pins its staging rows and captures the graph with the copies
+    for i in range(min(args.warmup, 3)):
+        dec.step_host(xs_host[i % len(xs_host)], y_host)
     e2e_s = 0.0
     t1 = time.perf_counter()
     for i in range(args.steps):
